@@ -1,0 +1,184 @@
+/*
+ * kernelo_b200.h -- C ABI of the B200 (sm_100a) KernelForge hot path.
+ *
+ * Every entry point takes raw device pointers, int64 sizes and ELEMENT strides,
+ * a dtype code, an optional config struct and a cudaStream_t passed as void*.
+ * Nothing here allocates or frees device memory, synchronises, or keeps state
+ * beyond per-device caches (SM count, the tensor-map encoder) and one device
+ * status word per GPU. Kernels are launched asynchronously on `stream`.
+ *
+ * Each entry point replaces the launch site of one reference wrapper; the
+ * citations are file:line in the KernelForge sources (package `kernelforge`):
+ *
+ *   kf_gemm             kernels/matmul.py:132-155        matmul(a, b, config=)
+ *   kf_linear_bias_act  kernels/fused_linear.py:112-157  fused_linear_gelu(x, w, bias, config=)
+ *   kf_gemv             kernels/matmul.py:132-155 at M in {1,4,16}
+ *                       (the decode-shape GEMM; the reference has no dedicated kernel)
+ *   kf_softmax_rows     kernels/softmax.py:70-104        softmax(x, config=)
+ *   kf_rmsnorm_rows     kernels/rmsnorm.py:81-127        rmsnorm(x, gamma, eps=, config=)
+ *                       and csrc/rmsnorm.cu:19-57        (the hand-written CUDA baseline)
+ *   kf_query_gemm_config  tuning/search.py:299-394      shared-memory / feasibility model
+ *
+ * Status codes are returned by value; kf_last_error() gives the message of the
+ * most recent failure on the calling thread.
+ */
+#ifndef KERNELO_B200_H
+#define KERNELO_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KF_ABI_VERSION 1
+
+/* Exported from the shared library (it is built with -fvisibility=hidden). */
+#if defined(__GNUC__)
+#define KF_API __attribute__((visibility("default")))
+#else
+#define KF_API
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+enum kf_status {
+  KF_OK = 0,
+  KF_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad dtype code      */
+  KF_ERR_INVALID_CONFIG = 2,   /* config cannot run on this device / these shapes  */
+  KF_ERR_UNALIGNED = 3,        /* strides or pointers unusable by the chosen kernel */
+  KF_ERR_LAUNCH = 4,           /* the CUDA runtime rejected the launch              */
+  KF_ERR_TIMEOUT = 5,          /* a bounded device-side wait gave up (status word)  */
+  KF_ERR_UNSUPPORTED = 6,      /* dtype/shape combination has no kernel             */
+  KF_ERR_WORKSPACE = 7,        /* workspace missing or too small                    */
+  KF_ERR_NO_DEVICE = 8         /* no usable sm_100 device                           */
+};
+
+/* ---- dtype codes (kernelforge/dtypes.py:13-17) -------------------------- */
+enum kf_dtype { KF_FP16 = 0, KF_BF16 = 1, KF_FP32 = 2 };
+
+/* ---- GEMM epilogues (kernels/fused_linear.py:94-104) -------------------- */
+enum kf_epilogue {
+  KF_EPI_NONE = 0,           /* C = A.B                                   */
+  KF_EPI_BIAS = 1,           /* C = A.B + bias[n]                         */
+  KF_EPI_BIAS_GELU_TANH = 2, /* C = gelu_tanh(A.B + bias[n]) (reference)  */
+  KF_EPI_BIAS_GELU_ERF = 3   /* C = gelu_erf(A.B + bias[n])  (exact form) */
+};
+
+/* ---- GEMM kernels -------------------------------------------------------- */
+enum kf_gemm_kernel {
+  KF_GEMM_AUTO = 0,    /* library default for the shape                     */
+  KF_GEMM_TCGEN05 = 1, /* TMA + tcgen05.mma + TMEM, persistent, fp16/bf16    */
+  KF_GEMM_SIMT = 2     /* CUDA-core FFMA, any strides, fp16/bf16/fp32        */
+};
+
+/* Tunable GEMM parameters. Replaces KernelConfig's BLOCK_M/BLOCK_N/BLOCK_K/
+ * GROUP_M/num_stages keys (kernels/matmul.py:118-120) with their sm_100a
+ * meaning. Zero in any field selects the library default. */
+typedef struct kf_gemm_config {
+  int32_t kernel;    /* enum kf_gemm_kernel                                         */
+  int32_t block_m;   /* tcgen05: 128 (MMA M); SIMT: 64 or 128                        */
+  int32_t block_n;   /* tcgen05: multiple of 16 in [16,256]; SIMT: 64 or 128         */
+  int32_t block_k;   /* tcgen05: 64 or 128; SIMT: 8 or 16                            */
+  int32_t stages;    /* tcgen05 shared-memory ring depth                             */
+  int32_t group_m;   /* grouped (L2-aware) raster width, in M tiles                  */
+  int32_t stream_k;  /* tcgen05: 0 = library choice, 1 = split K over the persistent
+                        grid (stream-K), 2 = whole tiles only                          */
+  int32_t swap_ab;   /* tcgen05: 0 = library choice, 1 = compute C^T = B^T.A^T
+                        (skinny M), 2 = never swap                                     */
+  int32_t cluster_m; /* reserved, must be 0 or 1                                     */
+  int32_t cluster_n; /* reserved, must be 0 or 1                                     */
+  int32_t num_ctas;  /* persistent grid size; 0 = one CTA per SM                     */
+  int32_t reserved[5];
+} kf_gemm_config;
+
+/* Row-kernel parameters (softmax / RMSNorm). Replaces BLOCK_SIZE /
+ * ROWS_PER_PROGRAM / num_warps (kernels/softmax.py:61-67). */
+typedef struct kf_rows_config {
+  int32_t num_warps;        /* warps per CTA, 1..32                                   */
+  int32_t rows_per_cta;     /* rows handled by one CTA (or cluster), in sequence      */
+  int32_t cluster;          /* CTAs sharing one row through distributed shared memory */
+  int32_t reserved[5];
+} kf_rows_config;
+
+/* ---- library information -------------------------------------------------- */
+KF_API int32_t kf_abi_version(void);
+KF_API const char* kf_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+KF_API const char* kf_last_error(void);
+/* Number of SMs of `device` (cached), or a negative status. */
+KF_API int32_t kf_sm_count(int32_t device);
+
+/* Reads and clears the device status word of `device` (synchronises that device).
+ * *out receives KF_OK or KF_ERR_TIMEOUT with the kernel site in the high bits. */
+KF_API int32_t kf_device_status(int32_t device, int32_t* out);
+
+/* ---- GEMM: C[M,N] = A[M,K] . B[K,N] --------------------------------------- *
+ * Strides are in elements: A(m,k) = a[m*sa_m + k*sa_k], B(k,n) = b[k*sb_k + n*sb_n],
+ * C(m,n) = c[m*sc_m + n*sc_n]. Accumulation is fp32; C has the operand dtype.
+ * `workspace` is needed only by stream-K configs; kf_gemm_workspace_bytes()
+ * gives its size (256-byte aligned). Layout: 64 KiB of per-tile arrival
+ * counters, then fp32 partial tiles. The counters must be zero before the first
+ * use; every call leaves them zero again, so one zeroed buffer can serve any
+ * sequence of calls on one stream (calls that overlap on the GPU race). */
+KF_API int32_t kf_gemm(int32_t dtype, const void* a, int64_t sa_m, int64_t sa_k, const void* b,
+                int64_t sb_k, int64_t sb_n, void* c, int64_t sc_m, int64_t sc_n, int64_t M,
+                int64_t N, int64_t K, const kf_gemm_config* cfg, void* workspace,
+                int64_t workspace_bytes, void* stream);
+
+/* Y = act(X . W + bias). W(k,n) = w[k*sw_k + n*sw_n]: both the reference's (K,N)
+ * layout and nn.Linear's [N,K] layout (sw_k = 1) are accepted without copies. */
+KF_API int32_t kf_linear_bias_act(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
+                           const void* w, int64_t sw_k, int64_t sw_n, const void* bias,
+                           void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
+                           int32_t epilogue, const kf_gemm_config* cfg, void* workspace,
+                           int64_t workspace_bytes, void* stream);
+
+/* Decode-shape GEMM Y[M,N] = X[M,K] . W^T for small M (1..256) with W stored
+ * [N,K] (sw_n = row stride, sw_k = 1) or [K,N] (sw_k = row stride, sw_n = 1).
+ * Memory-bound: streams W once with TMA, splits K across all SMs (stream-K);
+ * needs kf_gemv_workspace_bytes() of workspace. */
+KF_API int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w,
+                int64_t sw_n, int64_t sw_k, void* y, int64_t sy_m, int64_t sy_n, int64_t M,
+                int64_t N, int64_t K, const kf_gemm_config* cfg, void* workspace,
+                int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes a kf_gemm / kf_linear_bias_act (resp. kf_gemv) call with
+ * these strides, sizes and config needs on `device` (0 when none; negative
+ * status on error). Operand pointers are assumed 16-byte aligned. */
+KF_API int64_t kf_gemm_workspace_bytes(int32_t device, int32_t dtype, int64_t sa_m, int64_t sa_k,
+                                int64_t sb_k, int64_t sb_n, int64_t M, int64_t N, int64_t K,
+                                const kf_gemm_config* cfg);
+KF_API int64_t kf_gemv_workspace_bytes(int32_t device, int32_t dtype, int64_t sx_m, int64_t sx_k,
+                                int64_t sw_n, int64_t sw_k, int64_t M, int64_t N, int64_t K,
+                                const kf_gemm_config* cfg);
+
+/* Feasibility model used by the tuner's filters (tuning/search.py:299-394).
+ * Fills the shared memory (bytes) and TMEM columns a tcgen05 config needs;
+ * returns KF_OK or KF_ERR_INVALID_CONFIG. Needs no GPU. */
+KF_API int32_t kf_query_gemm_config(int32_t dtype, const kf_gemm_config* cfg, int64_t* smem_bytes,
+                             int32_t* tmem_cols);
+
+/* ---- row kernels ----------------------------------------------------------- *
+ * y[r, :] = softmax(x[r, :]) over `cols`; fp32 math, output in the input dtype.
+ * Row strides in elements; the last dimension must be contiguous. */
+KF_API int32_t kf_softmax_rows(int32_t dtype, const void* x, int64_t sx_row, void* y, int64_t sy_row,
+                        int64_t rows, int64_t cols, const kf_rows_config* cfg, void* stream);
+
+/* y[r, :] = x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * gamma; fp32 reduction,
+ * one rounding at the end (kernels/rmsnorm.py:130-143). */
+KF_API int32_t kf_rmsnorm_rows(int32_t dtype, const void* x, int64_t sx_row, const void* gamma,
+                        void* y, int64_t sy_row, int64_t rows, int64_t cols, float eps,
+                        const kf_rows_config* cfg, void* stream);
+
+/* ---- failure-detection self test ------------------------------------------- *
+ * Launches one CTA that waits on an mbarrier nothing will ever complete, with
+ * a limit of `timeout_us` microseconds, then records KF_ERR_TIMEOUT in the
+ * device status word and returns. Exercises the bounded-wait path without
+ * hanging or faulting the GPU. */
+KF_API int32_t kf_selftest_bounded_wait(int32_t timeout_us, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KERNELO_B200_H */

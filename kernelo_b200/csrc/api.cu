@@ -1,0 +1,396 @@
+// extern "C" entry points of libkernelo_b200: argument checks, config
+// resolution, dispatch to the tcgen05 / SIMT / row kernels, per-device caches
+// and the device status word that bounded waits report timeouts into.
+#include <array>
+#include <mutex>
+#include <string>
+
+#include "kf_common.cuh"
+#include "kf_internal.h"
+
+// One status word per device context. Kernels whose bounded waits give up
+// write KF_ERR_TIMEOUT | (site << 8) here; kf_device_status() reads and clears it.
+__device__ int kf_status_word;
+
+namespace kf {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_dev_mutex;
+std::array<DeviceInfo, 64> g_devices;
+std::array<bool, 64> g_device_ready{};
+
+__global__ void selftest_wait_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  // Nothing ever arrives on `bar`: the wait must give up on its own.
+  if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, nullptr, status, SITE_SELFTEST, limit_ns);
+}
+
+bool valid_dtype(int d) { return d == KF_FP16 || d == KF_BF16 || d == KF_FP32; }
+
+kf_gemm_config zero_config() {
+  kf_gemm_config c{};
+  return c;
+}
+}  // namespace
+
+int set_error(int code, const std::string& message) {
+  g_last_error = message;
+  return code;
+}
+
+int cuda_error(cudaError_t err, const char* where) {
+  const std::string msg = std::string(where) + ": " + cudaGetErrorString(err);
+  switch (err) {
+    case cudaErrorLaunchOutOfResources:
+    case cudaErrorInvalidConfiguration:
+    case cudaErrorInvalidClusterSize:
+      return set_error(KF_ERR_INVALID_CONFIG, msg);
+    case cudaErrorNoDevice:
+    case cudaErrorInsufficientDriver:
+    case cudaErrorNoKernelImageForDevice:
+      return set_error(KF_ERR_NO_DEVICE, msg);
+    default:
+      return set_error(KF_ERR_LAUNCH, msg);
+  }
+}
+
+int current_device(int* device) {
+  cudaError_t err = cudaGetDevice(device);
+  if (err != cudaSuccess) return cuda_error(err, "cudaGetDevice");
+  return KF_OK;
+}
+
+int device_info(int device, DeviceInfo** out) {
+  if (device < 0 || device >= static_cast<int>(g_devices.size()))
+    return set_error(KF_ERR_INVALID_ARGUMENT, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (!g_device_ready[device]) {
+    int prev = 0;
+    cudaError_t err = cudaGetDevice(&prev);
+    if (err != cudaSuccess) return cuda_error(err, "cudaGetDevice");
+    if (prev != device) {
+      err = cudaSetDevice(device);
+      if (err != cudaSuccess) return cuda_error(err, "cudaSetDevice");
+    }
+    DeviceInfo info;
+    cudaDeviceProp prop;
+    err = cudaGetDeviceProperties(&prop, device);
+    if (err == cudaSuccess) {
+      info.sm_count = prop.multiProcessorCount;
+      info.max_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+      info.major = prop.major;
+      info.minor = prop.minor;
+      void* addr = nullptr;
+      err = cudaGetSymbolAddress(&addr, kf_status_word);
+      info.status = static_cast<int*>(addr);
+    }
+    if (prev != device) cudaSetDevice(prev);
+    if (err != cudaSuccess) return cuda_error(err, "device_info");
+    if (info.major != 10)
+      return set_error(KF_ERR_NO_DEVICE, "libkernelo_b200 is built for sm_100a; device " +
+                                             std::to_string(device) + " is sm_" +
+                                             std::to_string(info.major) +
+                                             std::to_string(info.minor));
+    g_devices[device] = info;
+    g_device_ready[device] = true;
+  }
+  *out = &g_devices[device];
+  return KF_OK;
+}
+
+kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user, int sm_count) {
+  kf_gemm_config c = user ? *user : zero_config();
+  const bool tc_ok = tcgen05_operands_ok(g, nullptr);
+  if (c.kernel == KF_GEMM_AUTO) c.kernel = tc_ok ? KF_GEMM_TCGEN05 : KF_GEMM_SIMT;
+  if (c.kernel == KF_GEMM_SIMT) {
+    if (c.block_m == 0 && c.block_n == 0 && c.block_k == 0) {
+      const bool small = g.M * g.N < 128LL * 128 * sm_count;
+      c.block_m = small ? 64 : 128;
+      c.block_n = small ? 64 : 128;
+      c.block_k = small ? 16 : 8;
+    }
+    return c;
+  }
+  // tcgen05 defaults.
+  if (c.swap_ab == 0) c.swap_ab = (g.M <= 64 && g.N > g.M) ? 1 : 2;
+  const bool swap = c.swap_ab == 1;
+  const int64_t m = swap ? g.N : g.M;
+  const int64_t n = swap ? g.M : g.N;
+  // B' is MN-major when its N' index has unit stride.
+  const int64_t sb_c = swap ? g.sa_m : g.sb_n;
+  const int64_t sb_k = swap ? g.sa_k : g.sb_k;
+  const bool b_mn = !(sb_k == 1) && sb_c == 1;
+  if (c.block_m == 0) c.block_m = 128;
+  if (c.block_n == 0) {
+    const int quantum = b_mn ? 64 : 16;
+    int64_t bn = n <= 256 ? ((n + quantum - 1) / quantum) * quantum : 256;
+    if (bn < quantum) bn = quantum;
+    if (bn > 256) bn = 256;
+    c.block_n = static_cast<int32_t>(bn);
+  }
+  if (c.block_k == 0) c.block_k = 64;
+  if (c.stages == 0) {
+    const int64_t per_stage = static_cast<int64_t>(128 + c.block_n) * c.block_k * 2;
+    int64_t s = (232448 - 1024 - 256) / per_stage;
+    if (s > 12) s = 12;
+    if (s < 2) s = 2;
+    c.stages = static_cast<int32_t>(s);
+  }
+  if (c.group_m == 0) c.group_m = 8;
+  if (c.stream_k == 0) {
+    const int64_t tiles = ((m + 127) / 128) * ((n + c.block_n - 1) / c.block_n);
+    const int64_t kb = (g.K + c.block_k - 1) / c.block_k;
+    c.stream_k = (tiles < sm_count && kb >= 4) ? 1 : 2;
+  }
+  return c;
+}
+
+}  // namespace kf
+
+using namespace kf;
+
+namespace {
+
+int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
+  if (!valid_dtype(g.dtype)) return set_error(KF_ERR_INVALID_ARGUMENT, "unknown dtype code");
+  if (g.M < 0 || g.N < 0 || g.K < 0) return set_error(KF_ERR_INVALID_ARGUMENT, "negative size");
+  if (g.M == 0 || g.N == 0) return KF_OK;
+  if (g.c == nullptr || (g.K > 0 && (g.a == nullptr || g.b == nullptr)))
+    return set_error(KF_ERR_INVALID_ARGUMENT, "null operand pointer");
+  if (g.epilogue != KF_EPI_NONE && g.bias == nullptr)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "epilogue needs a bias pointer");
+  if (g.epilogue < KF_EPI_NONE || g.epilogue > KF_EPI_BIAS_GELU_ERF)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "unknown epilogue code");
+  int device = 0;
+  int rc = current_device(&device);
+  if (rc != KF_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = device_info(device, &dev);
+  if (rc != KF_OK) return rc;
+  const kf_gemm_config cfg = resolve_gemm_config(g, user, dev->sm_count);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cfg.kernel == KF_GEMM_TCGEN05) return launch_gemm_tcgen05(g, cfg, *dev, s);
+  if (cfg.kernel == KF_GEMM_SIMT) return launch_gemm_simt(g, cfg, s);
+  return set_error(KF_ERR_INVALID_CONFIG, "unknown GEMM kernel code");
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t kf_abi_version(void) { return KF_ABI_VERSION; }
+
+const char* kf_version(void) { return "kernelo_b200 0.1.0 (sm_100a)"; }
+
+const char* kf_last_error(void) { return g_last_error.c_str(); }
+
+int32_t kf_sm_count(int32_t device) {
+  DeviceInfo* dev = nullptr;
+  const int rc = device_info(device, &dev);
+  if (rc != KF_OK) return -rc;
+  return dev->sm_count;
+}
+
+int32_t kf_device_status(int32_t device, int32_t* out) {
+  if (out == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null out pointer");
+  DeviceInfo* dev = nullptr;
+  int rc = device_info(device, &dev);
+  if (rc != KF_OK) return rc;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  int value = 0;
+  cudaError_t err = cudaDeviceSynchronize();
+  if (err == cudaSuccess) err = cudaMemcpyFromSymbol(&value, kf_status_word, sizeof(int));
+  const int zero = 0;
+  if (err == cudaSuccess) err = cudaMemcpyToSymbol(kf_status_word, &zero, sizeof(int));
+  cudaSetDevice(prev);
+  if (err != cudaSuccess) return cuda_error(err, "kf_device_status");
+  *out = value;
+  return KF_OK;
+}
+
+int32_t kf_gemm(int32_t dtype, const void* a, int64_t sa_m, int64_t sa_k, const void* b,
+                int64_t sb_k, int64_t sb_n, void* c, int64_t sc_m, int64_t sc_n, int64_t M,
+                int64_t N, int64_t K, const kf_gemm_config* cfg, void* workspace,
+                int64_t workspace_bytes, void* stream) {
+  GemmArgs g;
+  g.dtype = dtype;
+  g.a = a;
+  g.sa_m = sa_m;
+  g.sa_k = sa_k;
+  g.b = b;
+  g.sb_k = sb_k;
+  g.sb_n = sb_n;
+  g.c = c;
+  g.sc_m = sc_m;
+  g.sc_n = sc_n;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.workspace = workspace;
+  g.workspace_bytes = workspace_bytes;
+  return gemm_common(g, cfg, stream);
+}
+
+int32_t kf_linear_bias_act(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
+                           const void* w, int64_t sw_k, int64_t sw_n, const void* bias, void* y,
+                           int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
+                           int32_t epilogue, const kf_gemm_config* cfg, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
+  GemmArgs g;
+  g.dtype = dtype;
+  g.a = x;
+  g.sa_m = sx_m;
+  g.sa_k = sx_k;
+  g.b = w;
+  g.sb_k = sw_k;
+  g.sb_n = sw_n;
+  g.c = y;
+  g.sc_m = sy_m;
+  g.sc_n = sy_n;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.bias = bias;
+  g.epilogue = epilogue;
+  g.workspace = workspace;
+  g.workspace_bytes = workspace_bytes;
+  return gemm_common(g, cfg, stream);
+}
+
+int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w,
+                int64_t sw_n, int64_t sw_k, void* y, int64_t sy_m, int64_t sy_n, int64_t M,
+                int64_t N, int64_t K, const kf_gemm_config* cfg, void* workspace,
+                int64_t workspace_bytes, void* stream) {
+  if (M > 256) return set_error(KF_ERR_UNSUPPORTED, "kf_gemv takes M <= 256; use kf_gemm");
+  kf_gemm_config c = cfg ? *cfg : zero_config();
+  if (c.kernel == KF_GEMM_AUTO || c.kernel == KF_GEMM_TCGEN05) {
+    if (c.swap_ab == 0) c.swap_ab = 1;
+    if (c.stream_k == 0) c.stream_k = 1;
+  }
+  return kf_gemm(dtype, x, sx_m, sx_k, w, sw_k, sw_n, y, sy_m, sy_n, M, N, K, &c, workspace,
+                 workspace_bytes, stream);
+}
+
+int64_t kf_gemm_workspace_bytes(int32_t device, int32_t dtype, int64_t sa_m, int64_t sa_k,
+                                int64_t sb_k, int64_t sb_n, int64_t M, int64_t N, int64_t K,
+                                const kf_gemm_config* cfg) {
+  DeviceInfo* dev = nullptr;
+  const int rc = device_info(device, &dev);
+  if (rc != KF_OK) return -rc;
+  GemmArgs g;
+  g.dtype = dtype;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.sa_m = sa_m;
+  g.sa_k = sa_k;
+  g.sb_k = sb_k;
+  g.sb_n = sb_n;
+  // Any 16-byte-aligned stand-in: only strides and sizes decide the config.
+  g.a = g.b = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  const kf_gemm_config c = resolve_gemm_config(g, cfg, dev->sm_count);
+  if (c.kernel != KF_GEMM_TCGEN05) return 0;
+  return gemm_tcgen05_workspace_bytes(g, c, *dev);
+}
+
+int64_t kf_gemv_workspace_bytes(int32_t device, int32_t dtype, int64_t sx_m, int64_t sx_k,
+                                int64_t sw_n, int64_t sw_k, int64_t M, int64_t N, int64_t K,
+                                const kf_gemm_config* cfg) {
+  kf_gemm_config c = cfg ? *cfg : zero_config();
+  if (c.kernel == KF_GEMM_AUTO || c.kernel == KF_GEMM_TCGEN05) {
+    if (c.swap_ab == 0) c.swap_ab = 1;
+    if (c.stream_k == 0) c.stream_k = 1;
+  }
+  return kf_gemm_workspace_bytes(device, dtype, sx_m, sx_k, sw_k, sw_n, M, N, K, &c);
+}
+
+int32_t kf_query_gemm_config(int32_t dtype, const kf_gemm_config* cfg, int64_t* smem_bytes,
+                             int32_t* tmem_cols) {
+  if (cfg == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null config");
+  if (cfg->kernel == KF_GEMM_SIMT) {
+    if (smem_bytes) *smem_bytes = 2LL * cfg->block_k * (cfg->block_m + cfg->block_n) * 4;
+    if (tmem_cols) *tmem_cols = 0;
+    return KF_OK;
+  }
+  return query_tcgen05_config(dtype, *cfg, smem_bytes, tmem_cols);
+}
+
+int32_t kf_softmax_rows(int32_t dtype, const void* x, int64_t sx_row, void* y, int64_t sy_row,
+                        int64_t rows, int64_t cols, const kf_rows_config* cfg, void* stream) {
+  if (!valid_dtype(dtype)) return set_error(KF_ERR_INVALID_ARGUMENT, "unknown dtype code");
+  if (rows < 0 || cols < 0) return set_error(KF_ERR_INVALID_ARGUMENT, "negative size");
+  if (rows == 0 || cols == 0) return KF_OK;
+  if (x == nullptr || y == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null pointer");
+  int device = 0;
+  int rc = current_device(&device);
+  if (rc != KF_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = device_info(device, &dev);
+  if (rc != KF_OK) return rc;
+  RowsArgs a;
+  a.dtype = dtype;
+  a.op = 0;
+  a.x = x;
+  a.sx = sx_row;
+  a.y = y;
+  a.sy = sy_row;
+  a.rows = rows;
+  a.cols = cols;
+  const kf_rows_config c = resolve_rows_config(a, cfg);
+  return launch_rows(a, c, *dev, static_cast<cudaStream_t>(stream));
+}
+
+int32_t kf_rmsnorm_rows(int32_t dtype, const void* x, int64_t sx_row, const void* gamma,
+                        void* y, int64_t sy_row, int64_t rows, int64_t cols, float eps,
+                        const kf_rows_config* cfg, void* stream) {
+  if (!valid_dtype(dtype)) return set_error(KF_ERR_INVALID_ARGUMENT, "unknown dtype code");
+  if (rows < 0 || cols < 0) return set_error(KF_ERR_INVALID_ARGUMENT, "negative size");
+  if (rows == 0 || cols == 0) return KF_OK;
+  if (x == nullptr || y == nullptr || gamma == nullptr)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "null pointer");
+  int device = 0;
+  int rc = current_device(&device);
+  if (rc != KF_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = device_info(device, &dev);
+  if (rc != KF_OK) return rc;
+  RowsArgs a;
+  a.dtype = dtype;
+  a.op = 1;
+  a.x = x;
+  a.sx = sx_row;
+  a.gamma = gamma;
+  a.y = y;
+  a.sy = sy_row;
+  a.rows = rows;
+  a.cols = cols;
+  a.eps = eps;
+  const kf_rows_config c = resolve_rows_config(a, cfg);
+  return launch_rows(a, c, *dev, static_cast<cudaStream_t>(stream));
+}
+
+int32_t kf_selftest_bounded_wait(int32_t timeout_us, void* stream) {
+  if (timeout_us <= 0 || timeout_us > 5000000)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "timeout_us must be in (0, 5e6]");
+  int device = 0;
+  int rc = current_device(&device);
+  if (rc != KF_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = device_info(device, &dev);
+  if (rc != KF_OK) return rc;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      dev->status, static_cast<unsigned long long>(timeout_us) * 1000ull);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_error(err, "launch(selftest)");
+  return KF_OK;
+}
+
+}  // extern "C"

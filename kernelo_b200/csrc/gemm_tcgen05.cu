@@ -1,0 +1,708 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[M,N] = epilogue(A[M,K] . B[K,N])       fp16/bf16 in, fp32 accumulate
+//
+// One CTA per SM, 6 warps:
+//   warp 0      TMA producer: 2-D tiled bulk loads of A and B k-blocks into a
+//               `stages`-deep ring of 128-byte-swizzled shared-memory tiles,
+//               completion tracked by full/empty mbarrier pairs.
+//   warp 1      allocates TMEM, then one lane issues tcgen05.mma (M=128, N=BN,
+//               K=16 per instruction) into a double-buffered fp32 accumulator
+//               in TMEM and releases ring slots with tcgen05.commit.
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (each warp owns one
+//               32-lane TMEM quadrant = 32 rows), add bias, apply GELU, round
+//               to the output dtype and store -- while the MMA warp already
+//               accumulates the next tile into the other TMEM buffer.
+//
+// Operands may be K-major or MN-major in global memory (row-major (K,N) B,
+// nn.Linear's [N,K] weight and transposed views all map to a TMA tensor map
+// without a copy); the MMA reads either layout through its smem descriptors.
+//
+// Work is a list of segments (tile, k-block range). Data-parallel mode gives
+// every CTA whole tiles in a grouped (GROUP_M) raster. Stream-K mode splits the
+// flattened (tile, k-block) iteration space evenly over the grid; a tile split
+// between CTAs is finished by whichever contributor arrives last, which sums the
+// fp32 partials in a fixed order (so results are deterministic) and runs the
+// epilogue. Nobody waits for another CTA, so the scheme cannot deadlock.
+//
+// Reference: kernelforge/kernels/matmul.py:54-113 (blocked GEMM with grouped
+// ordering) and kernelforge/kernels/fused_linear.py:49-104 (bias + GELU in the
+// epilogue). The algorithm (tile, accumulate in fp32, fused epilogue) is the
+// same; the mechanics are Blackwell's.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kf_common.cuh"
+#include "kf_internal.h"
+
+namespace kf {
+namespace {
+
+constexpr int BM = 128;
+constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARP0 = 2;
+constexpr int NUM_EPI_THREADS = 128;
+constexpr int MAX_STAGES = 16;
+constexpr int MIN_SMEM_PER_CTA = 120 * 1024;  // > half an SM: one CTA per SM
+constexpr uint64_t DRAIN_LIMIT_NS = 100000000ull;
+// Stream-K workspace layout: [tile arrival counters | 2 partial tiles per CTA].
+constexpr int64_t SK_MAX_TILES = 16384;
+constexpr int64_t SK_COUNTER_BYTES = SK_MAX_TILES * 4;
+
+struct TcParams {
+  int M, N, K;  // as the kernel sees them (after an optional A/B swap)
+  int bn, bk, stages, group_m;
+  int a_mn, b_mn;
+  int tiles_m, tiles_n, kb_per_tile;
+  long long total_iters;
+  int stream_k;
+  void* c;
+  long long sc_r, sc_c;
+  const void* bias;
+  int bias_on_rows;
+  float* partials;
+  int* counters;
+  int* status;
+  uint32_t idesc;
+  uint32_t a_stage_bytes, b_stage_bytes;
+  uint32_t tmem_cols;
+};
+
+struct Segment {
+  int tile;
+  int kb0, kb1;
+};
+
+struct Cursor {
+  long long next, end, begin;
+};
+
+__device__ __forceinline__ void cursor_init(const TcParams& p, Cursor& c) {
+  if (p.stream_k) {
+    const long long g = gridDim.x;
+    c.begin = (p.total_iters * blockIdx.x) / g;
+    c.end = (p.total_iters * (blockIdx.x + 1)) / g;
+    c.next = c.begin;
+  } else {
+    c.begin = 0;
+    c.end = static_cast<long long>(p.tiles_m) * p.tiles_n;
+    c.next = blockIdx.x;
+  }
+}
+
+__device__ __forceinline__ bool cursor_next(const TcParams& p, Cursor& c, Segment& s) {
+  if (c.next >= c.end) return false;
+  if (p.stream_k) {
+    const long long tile = c.next / p.kb_per_tile;
+    const long long tile_start = tile * p.kb_per_tile;
+    long long stop = c.end - tile_start;
+    if (stop > p.kb_per_tile) stop = p.kb_per_tile;
+    s.tile = static_cast<int>(tile);
+    s.kb0 = static_cast<int>(c.next - tile_start);
+    s.kb1 = static_cast<int>(stop);
+    c.next = tile_start + stop;
+  } else {
+    s.tile = static_cast<int>(c.next);
+    s.kb0 = 0;
+    s.kb1 = p.kb_per_tile;
+    c.next += gridDim.x;
+  }
+  return true;
+}
+
+// Grouped raster: GROUP_M consecutive M tiles share each N column, so the CTAs
+// resident at one time touch a compact block of C and its A/B panels stay in L2.
+__device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& m_blk, int& n_blk) {
+  const int per_group = p.group_m * p.tiles_n;
+  const int gid = tile / per_group;
+  const int first_m = gid * p.group_m;
+  int rows = p.tiles_m - first_m;
+  if (rows > p.group_m) rows = p.group_m;
+  const int r = tile - gid * per_group;
+  m_blk = first_m + r % rows;
+  n_blk = r / rows;
+}
+
+// Stream-K: the CTA whose iteration range contains iteration x.
+__device__ __forceinline__ long long owner_of(long long x, long long total, long long grid) {
+  return ((x + 1) * grid + total - 1) / total - 1;
+}
+
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NUM_EPI_THREADS) : "memory");
+}
+
+// Epilogue for 16 accumulator columns of one row: bias, activation, rounding, store.
+template <typename T, int EPI>
+__device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0, const float* acc) {
+  if (row >= p.M) return;
+  float v[16];
+  const T* bias = static_cast<const T*>(p.bias);
+  const float row_bias = (EPI != KF_EPI_NONE && p.bias_on_rows) ? to_f32(bias[row]) : 0.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float b = row_bias;
+    if (EPI != KF_EPI_NONE && !p.bias_on_rows) {
+      const int col = col0 + j;
+      b = col < p.N ? to_f32(bias[col]) : 0.0f;
+    }
+    v[j] = apply_epilogue<EPI>(acc[j], b);
+  }
+  T* out = static_cast<T*>(p.c) + static_cast<long long>(row) * p.sc_r +
+           static_cast<long long>(col0) * p.sc_c;
+  const bool vec_ok = p.sc_c == 1 && col0 + 16 <= p.N &&
+                      (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && sizeof(T) == 2;
+  if (vec_ok) {
+    uint32_t packed[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      T lo = from_f32<T>(v[2 * j]);
+      T hi = from_f32<T>(v[2 * j + 1]);
+      packed[j] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) |
+                  (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out);
+    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (col0 + j < p.N) out[static_cast<long long>(j) * p.sc_c] = from_f32<T>(v[j]);
+    }
+  }
+}
+
+template <typename T, int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
+                   const __grid_constant__ CUtensorMap tm_b, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int S = p.stages;
+  uint8_t* a_ring = smem;
+  uint8_t* b_ring = smem + static_cast<size_t>(S) * p.a_stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b_ring + static_cast<size_t>(S) * p.b_stage_bytes);
+  // bars: full[S] | empty[S] | tmem_full[2] | tmem_empty[2] | drain
+  uint32_t* misc = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  // misc[0] TMEM base address, misc[1] abort flag, misc[2] "last contributor" flag
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(&misc[1]);
+  volatile uint32_t* last_flag = &misc[2];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = smem_u32(bars + S);
+  const uint32_t tfull0 = smem_u32(bars + 2 * S);
+  const uint32_t tempty0 = smem_u32(bars + 2 * S + 2);
+  const uint32_t drain_bar = smem_u32(bars + 2 * S + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, NUM_EPI_THREADS);
+    }
+    mbar_init(drain_bar, 1);
+    misc[1] = 0;
+    misc[2] = 0;
+    mbar_init_fence();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&misc[0]), p.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = misc[0];
+
+  Cursor cur;
+  cursor_init(p, cur);
+  Segment seg;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      const uint32_t tx_bytes = p.a_stage_bytes + p.b_stage_bytes;
+      while (ok && cursor_next(p, cur, seg)) {
+        int m_blk, n_blk;
+        tile_coords(p, seg.tile, m_blk, n_blk);
+        const int m0 = m_blk * BM;
+        const int n0 = n_blk * p.bn;
+        for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag, p.status, SITE_TMA_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + 8 * stage;
+          mbar_arrive_expect_tx(fb, tx_bytes);
+          const int k0 = kb * p.bk;
+          const uint32_t a_dst = smem_u32(a_ring + static_cast<size_t>(stage) * p.a_stage_bytes);
+          const uint32_t b_dst = smem_u32(b_ring + static_cast<size_t>(stage) * p.b_stage_bytes);
+          if (!p.a_mn) {
+            for (int j = 0; j < p.bk / 64; ++j)
+              tma_load_2d(a_dst + j * (BM * 128), &tm_a, fb, k0 + 64 * j, m0);
+          } else {
+            for (int i = 0; i < BM / 64; ++i)
+              tma_load_2d(a_dst + i * (p.bk * 128), &tm_a, fb, m0 + 64 * i, k0);
+          }
+          if (!p.b_mn) {
+            for (int j = 0; j < p.bk / 64; ++j)
+              tma_load_2d(b_dst + j * (p.bn * 128), &tm_b, fb, k0 + 64 * j, n0);
+          } else {
+            for (int i = 0; i < p.bn / 64; ++i)
+              tma_load_2d(b_dst + i * (p.bk * 128), &tm_b, fb, n0 + 64 * i, k0);
+          }
+          ++issued;
+          if (++stage == static_cast<uint32_t>(S)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Aborting: let every bulk copy already issued land before the CTA's
+        // shared memory goes away.
+        for (int s = 0; s < S && s < issued; ++s) {
+          const long long armed = (issued - s + S - 1) / S;
+          mbar_wait(full0 + 8 * s, static_cast<uint32_t>((armed - 1) & 1), nullptr, p.status,
+                    SITE_DRAIN, DRAIN_LIMIT_NS);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      while (ok && cursor_next(p, cur, seg)) {
+        if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, abort_flag, p.status,
+                       SITE_MMA_TMEM_EMPTY)) {
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(p.bn);
+        for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
+          if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, p.status, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(a_ring + static_cast<size_t>(stage) * p.a_stage_bytes);
+          const uint32_t b_base = smem_u32(b_ring + static_cast<size_t>(stage) * p.b_stage_bytes);
+          for (int kk = 0; kk < p.bk / 16; ++kk) {
+            // K-major: 64-element-wide swizzle atoms along K; K=16 is a 32-byte
+            // step inside the atom. MN-major: 16 K-rows of 128 bytes per step.
+            const uint64_t a_desc =
+                p.a_mn ? smem_desc_sw128(a_base + kk * 2048, p.bk * 128, 1024)
+                       : smem_desc_sw128(a_base + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t b_desc =
+                p.b_mn ? smem_desc_sw128(b_base + kk * 2048, p.bk * 128, 1024)
+                       : smem_desc_sw128(b_base + (kk >> 2) * (p.bn * 128) + (kk & 3) * 32, 16,
+                                         1024);
+            tc_mma_f16(d_tmem, a_desc, b_desc, p.idesc, (kb > seg.kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(empty0 + 8 * stage);  // ring slot reusable once these MMAs finish
+          if (++stage == static_cast<uint32_t>(S)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(tfull0 + 8 * acc);  // accumulator complete
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA issued must complete before TMEM is released.
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, nullptr, p.status, SITE_DRAIN, DRAIN_LIMIT_NS);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // the TMEM lane quadrant this warp may read
+    const int row_in_tile = quad * 32 + lane;
+    const int ethread = threadIdx.x - EPI_WARP0 * 32;
+    uint32_t acc = 0, acc_phase = 0;
+    while (cursor_next(p, cur, seg)) {
+      if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, p.status, SITE_EPI_TMEM_FULL)) break;
+      tc_fence_after();
+      int m_blk, n_blk;
+      tile_coords(p, seg.tile, m_blk, n_blk);
+      const int row = m_blk * BM + row_in_tile;
+      const int col_base = n_blk * p.bn;
+      const uint32_t t_acc =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * static_cast<uint32_t>(p.bn);
+      const bool whole_tile = seg.kb0 == 0 && seg.kb1 == p.kb_per_tile;
+      if (whole_tile) {
+        for (int c = 0; c < p.bn; c += 16) {
+          uint32_t r[16];
+          __syncwarp();  // tcgen05.ld is .sync.aligned
+          tmem_ld_16(t_acc + c, r);
+          tmem_ld_wait();
+          store_chunk<T, EPI>(p, row, col_base + c, reinterpret_cast<const float*>(r));
+        }
+      } else {
+        // Stream-K fix-up for a tile shared between CTAs.
+        const long long grid = gridDim.x;
+        const long long t_start = static_cast<long long>(seg.tile) * p.kb_per_tile;
+        const long long c_first = owner_of(t_start, p.total_iters, grid);
+        const long long c_last = owner_of(t_start + p.kb_per_tile - 1, p.total_iters, grid);
+        const long long me = blockIdx.x;
+        const size_t slot_elems = static_cast<size_t>(p.bn) * BM;
+        const long long my_slot = 2 * me + (cur.begin >= t_start ? 0 : 1);
+        float* mine = p.partials + static_cast<size_t>(my_slot) * slot_elems;
+        for (int c = 0; c < p.bn; c += 16) {
+          uint32_t r[16];
+          __syncwarp();
+          tmem_ld_16(t_acc + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            __stcg(mine + static_cast<size_t>(c + j) * BM + row_in_tile, __uint_as_float(r[j]));
+        }
+        __threadfence();
+        epi_bar_sync();
+        if (ethread == 0) {
+          const int arrived = atomicAdd(&p.counters[seg.tile], 1);
+          *last_flag = (arrived == static_cast<int>(c_last - c_first)) ? 1u : 0u;
+        }
+        epi_bar_sync();
+        if (*last_flag) {
+          __threadfence();
+          for (int c = 0; c < p.bn; c += 16) {
+            uint32_t r[16];
+            __syncwarp();
+            tmem_ld_16(t_acc + c, r);
+            tmem_ld_wait();
+            float sum[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
+            for (long long cc = c_first; cc <= c_last; ++cc) {
+              if (cc == me) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sum[j] += __uint_as_float(r[j]);
+              } else {
+                const long long cc_begin = (p.total_iters * cc) / grid;
+                const long long slot = 2 * cc + (cc_begin >= t_start ? 0 : 1);
+                const float* part = p.partials + static_cast<size_t>(slot) * slot_elems;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  sum[j] += __ldcg(part + static_cast<size_t>(c + j) * BM + row_in_tile);
+              }
+            }
+            store_chunk<T, EPI>(p, row, col_base + c, sum);
+          }
+          if (ethread == 0) p.counters[seg.tile] = 0;  // leave the workspace clean
+        }
+        epi_bar_sync();
+      }
+      tc_fence_before();
+      mbar_arrive(tempty0 + 8 * acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();  // tcgen05.dealloc is .sync.aligned: the whole warp, converged
+    tc_fence_after();
+    tmem_dealloc(tmem_base, p.tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------- host side
+
+uint32_t tmem_cols_for(int bn) {
+  uint32_t need = static_cast<uint32_t>(2 * bn);
+  uint32_t cols = 32;
+  while (cols < need) cols <<= 1;
+  return cols;
+}
+
+int64_t smem_bytes_for(int bn, int bk, int stages) {
+  const int64_t ring = static_cast<int64_t>(stages) * (BM + bn) * bk * 2;
+  return 1024 + ring + 8 * (2 * stages + 5) + 16;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* sym = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(sym);
+    }
+  });
+  return fn;
+}
+
+// A 2-D view [outer][inner] with `outer_stride` elements between rows.
+int encode_map(CUtensorMap* map, int dtype, const void* ptr, uint64_t inner, uint64_t outer,
+               int64_t outer_stride, uint32_t box_inner, uint32_t box_outer) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return set_error(KF_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  int64_t stride_bytes = outer_stride * 2;
+  if (outer <= 1) stride_bytes = ((static_cast<int64_t>(inner) * 2 + 15) / 16) * 16;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem_strides[2] = {1, 1};
+  const CUtensorMapDataType t =
+      dtype == KF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, t, 2, const_cast<void*>(ptr), dims, strides, box, elem_strides,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return set_error(KF_ERR_UNALIGNED,
+                     "cuTensorMapEncodeTiled rejected the operand (error " + std::to_string(r) +
+                         ", inner=" + std::to_string(inner) + ", outer=" + std::to_string(outer) +
+                         ", stride_bytes=" + std::to_string(stride_bytes) + ")");
+  }
+  return KF_OK;
+}
+
+// The kernel's view of the problem after an optional swap of A and B.
+struct View {
+  const void* a;
+  int64_t sa_r, sa_k;  // A'(r, k)
+  const void* b;
+  int64_t sb_k, sb_c;  // B'(k, c)
+  int64_t sc_r, sc_c;  // C'(r, c)
+  int64_t M, N;
+  bool bias_on_rows;
+};
+
+View make_view(const GemmArgs& g, bool swap) {
+  View v;
+  if (!swap) {
+    v = View{g.a, g.sa_m, g.sa_k, g.b, g.sb_k, g.sb_n, g.sc_m, g.sc_n, g.M, g.N, false};
+  } else {
+    // C^T = B^T A^T: A'(n, k) = B(k, n), B'(k, m) = A(m, k), C'(n, m) = C(m, n).
+    v = View{g.b, g.sb_n, g.sb_k, g.a, g.sa_k, g.sa_m, g.sc_n, g.sc_m, g.N, g.M, true};
+  }
+  return v;
+}
+
+// Operand majorness for TMA: 0 = K-major, 1 = MN-major, -1 = not describable.
+int operand_major(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int64_t k) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return -1;
+  if (k < 8) return -1;
+  if (s_k == 1 && (mn == 1 || (s_mn % 8 == 0 && s_mn >= k))) return 0;
+  if (s_mn == 1 && s_k % 8 == 0 && s_k >= mn) return 1;
+  return -1;
+}
+
+template <typename T, int EPI>
+void* kernel_ptr() {
+  return reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI>);
+}
+
+void* pick_kernel(int dtype, int epi) {
+  if (dtype == KF_FP16) {
+    switch (epi) {
+      case KF_EPI_NONE: return kernel_ptr<__half, KF_EPI_NONE>();
+      case KF_EPI_BIAS: return kernel_ptr<__half, KF_EPI_BIAS>();
+      case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__half, KF_EPI_BIAS_GELU_TANH>();
+      default: return kernel_ptr<__half, KF_EPI_BIAS_GELU_ERF>();
+    }
+  }
+  switch (epi) {
+    case KF_EPI_NONE: return kernel_ptr<__nv_bfloat16, KF_EPI_NONE>();
+    case KF_EPI_BIAS: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS>();
+    case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_TANH>();
+    default: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_ERF>();
+  }
+}
+
+int validate_config(const kf_gemm_config& cfg, int b_mn, std::string* why) {
+  if (cfg.block_m != BM) {
+    *why = "tcgen05 path supports BLOCK_M=128 (one-CTA MMA M); got " + std::to_string(cfg.block_m);
+    return KF_ERR_INVALID_CONFIG;
+  }
+  if (cfg.block_n < 16 || cfg.block_n > 256 || cfg.block_n % 16 != 0) {
+    *why = "BLOCK_N must be a multiple of 16 in [16, 256]; got " + std::to_string(cfg.block_n);
+    return KF_ERR_INVALID_CONFIG;
+  }
+  if (b_mn == 1 && cfg.block_n % 64 != 0) {
+    *why = "an MN-major B operand needs BLOCK_N to be a multiple of 64";
+    return KF_ERR_INVALID_CONFIG;
+  }
+  if (cfg.block_k != 64 && cfg.block_k != 128) {
+    *why = "BLOCK_K must be 64 or 128 (whole 128-byte swizzle atoms); got " +
+           std::to_string(cfg.block_k);
+    return KF_ERR_INVALID_CONFIG;
+  }
+  if (cfg.stages < 2 || cfg.stages > MAX_STAGES) {
+    *why = "stages must be in [2, 16]; got " + std::to_string(cfg.stages);
+    return KF_ERR_INVALID_CONFIG;
+  }
+  if (cfg.cluster_m > 1 || cfg.cluster_n > 1) {
+    *why = "thread-block clusters are not implemented by this build";
+    return KF_ERR_INVALID_CONFIG;
+  }
+  if (cfg.group_m < 1) {
+    *why = "GROUP_M must be positive";
+    return KF_ERR_INVALID_CONFIG;
+  }
+  return KF_OK;
+}
+
+}  // namespace
+
+bool tcgen05_operands_ok(const GemmArgs& g, std::string* why) {
+  if (g.dtype != KF_FP16 && g.dtype != KF_BF16) {
+    if (why) *why = "tcgen05 kind::f16 path takes fp16/bf16 only";
+    return false;
+  }
+  if (operand_major(g.a, g.sa_m, g.sa_k, g.M, g.K) < 0 ||
+      operand_major(g.b, g.sb_n, g.sb_k, g.N, g.K) < 0) {
+    if (why)
+      *why =
+          "operand strides/pointers are not TMA-describable (16-byte aligned base and row "
+          "stride, K >= 8)";
+    return false;
+  }
+  return true;
+}
+
+int query_tcgen05_config(int dtype, const kf_gemm_config& cfg, int64_t* smem_bytes,
+                         int32_t* tmem_cols) {
+  std::string why;
+  if (dtype != KF_FP16 && dtype != KF_BF16)
+    return set_error(KF_ERR_INVALID_CONFIG, "tcgen05 path takes fp16/bf16 only");
+  int rc = validate_config(cfg, 0, &why);
+  if (rc != KF_OK) return set_error(rc, why);
+  const int64_t smem = smem_bytes_for(cfg.block_n, cfg.block_k, cfg.stages);
+  if (smem_bytes) *smem_bytes = smem;
+  if (tmem_cols) *tmem_cols = static_cast<int32_t>(tmem_cols_for(cfg.block_n));
+  if (smem > 232448)
+    return set_error(KF_ERR_INVALID_CONFIG,
+                     "shared memory " + std::to_string(smem) + " B exceeds 227 KiB per CTA");
+  return KF_OK;
+}
+
+int64_t gemm_tcgen05_workspace_bytes(const GemmArgs& g, const kf_gemm_config& cfg,
+                                     const DeviceInfo& dev) {
+  if (cfg.stream_k != 1) return 0;
+  const bool swap = cfg.swap_ab == 1;
+  const int64_t m = swap ? g.N : g.M;
+  const int64_t n = swap ? g.M : g.N;
+  (void)m;
+  (void)n;
+  const int grid = cfg.num_ctas > 0 ? cfg.num_ctas : dev.sm_count;
+  return SK_COUNTER_BYTES + 2LL * grid * cfg.block_n * BM * 4;
+}
+
+int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const DeviceInfo& dev,
+                        cudaStream_t stream) {
+  std::string why;
+  if (!tcgen05_operands_ok(g, &why)) return set_error(KF_ERR_UNALIGNED, why);
+  const bool swap = cfg.swap_ab == 1;
+  const View v = make_view(g, swap);
+  const int a_major = operand_major(v.a, v.sa_r, v.sa_k, v.M, g.K);
+  const int b_major = operand_major(v.b, v.sb_c, v.sb_k, v.N, g.K);
+  if (a_major < 0 || b_major < 0) return set_error(KF_ERR_UNALIGNED, "operands not TMA-describable");
+  int rc = validate_config(cfg, b_major, &why);
+  if (rc != KF_OK) return set_error(rc, why);
+  if (v.M > INT32_MAX || v.N > INT32_MAX || g.K > INT32_MAX)
+    return set_error(KF_ERR_UNSUPPORTED, "dimensions above 2^31 are not supported");
+
+  const int bn = cfg.block_n, bk = cfg.block_k, S = cfg.stages;
+  const int64_t smem = smem_bytes_for(bn, bk, S);
+  if (smem > dev.max_smem_optin)
+    return set_error(KF_ERR_INVALID_CONFIG, "shared memory " + std::to_string(smem) +
+                                                " B exceeds the device limit of " +
+                                                std::to_string(dev.max_smem_optin));
+  const int64_t smem_request = smem < MIN_SMEM_PER_CTA ? MIN_SMEM_PER_CTA : smem;
+
+  CUtensorMap tm_a, tm_b;
+  rc = a_major == 0 ? encode_map(&tm_a, g.dtype, v.a, g.K, v.M, v.sa_r, 64, BM)
+                    : encode_map(&tm_a, g.dtype, v.a, v.M, g.K, v.sa_k, 64, bk);
+  if (rc != KF_OK) return rc;
+  rc = b_major == 0 ? encode_map(&tm_b, g.dtype, v.b, g.K, v.N, v.sb_c, 64, bn)
+                    : encode_map(&tm_b, g.dtype, v.b, v.N, g.K, v.sb_k, 64, bk);
+  if (rc != KF_OK) return rc;
+
+  TcParams p{};
+  p.M = static_cast<int>(v.M);
+  p.N = static_cast<int>(v.N);
+  p.K = static_cast<int>(g.K);
+  p.bn = bn;
+  p.bk = bk;
+  p.stages = S;
+  p.group_m = cfg.group_m;
+  p.a_mn = a_major;
+  p.b_mn = b_major;
+  p.tiles_m = static_cast<int>(ceil_div(v.M, BM));
+  p.tiles_n = static_cast<int>(ceil_div(v.N, bn));
+  p.kb_per_tile = static_cast<int>(ceil_div(g.K, bk));
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  p.total_iters = tiles * p.kb_per_tile;
+  p.stream_k = cfg.stream_k == 1 ? 1 : 0;
+  p.c = g.c;
+  p.sc_r = v.sc_r;
+  p.sc_c = v.sc_c;
+  p.bias = g.bias;
+  p.bias_on_rows = v.bias_on_rows ? 1 : 0;
+  p.status = dev.status;
+  p.idesc = instr_desc_f16(g.dtype == KF_BF16 ? 1u : 0u, static_cast<uint32_t>(a_major),
+                           static_cast<uint32_t>(b_major), BM, static_cast<uint32_t>(bn));
+  p.a_stage_bytes = static_cast<uint32_t>(BM * bk * 2);
+  p.b_stage_bytes = static_cast<uint32_t>(bn * bk * 2);
+  p.tmem_cols = tmem_cols_for(bn);
+
+  int grid = cfg.num_ctas > 0 ? cfg.num_ctas : dev.sm_count;
+  if (p.stream_k) {
+    if (grid > p.total_iters) grid = static_cast<int>(p.total_iters);
+    const int64_t need = gemm_tcgen05_workspace_bytes(g, cfg, dev);
+    if (g.workspace == nullptr || g.workspace_bytes < need)
+      return set_error(KF_ERR_WORKSPACE, "stream-K needs " + std::to_string(need) +
+                                             " bytes of zero-initialised workspace");
+    if ((reinterpret_cast<uintptr_t>(g.workspace) & 255u) != 0)
+      return set_error(KF_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    if (tiles > SK_MAX_TILES)
+      return set_error(KF_ERR_INVALID_CONFIG, "stream-K takes at most " +
+                                                  std::to_string(SK_MAX_TILES) +
+                                                  " output tiles; use whole tiles");
+    // Counters first, at a fixed offset: every call finds them where the last
+    // call left them (at zero), whatever its tile or grid size.
+    p.counters = static_cast<int*>(g.workspace);
+    p.partials = reinterpret_cast<float*>(static_cast<char*>(g.workspace) + SK_COUNTER_BYTES);
+  } else {
+    if (grid > tiles) grid = static_cast<int>(tiles);
+  }
+  if (grid < 1) grid = 1;
+
+  void* fn = pick_kernel(g.dtype, g.epilogue);
+  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem_request));
+  if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(tcgen05 gemm)");
+  void* args[] = {&tm_a, &tm_b, &p};
+  err = cudaLaunchKernel(fn, dim3(grid), dim3(NUM_THREADS), args,
+                         static_cast<size_t>(smem_request), stream);
+  if (err != cudaSuccess) return cuda_error(err, "launch(tcgen05 gemm)");
+  return KF_OK;
+}
+
+}  // namespace kf

@@ -1,0 +1,80 @@
+// Host-side declarations shared by the translation units of libkernelo_b200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "kernelo_b200.h"
+
+namespace kf {
+
+// Records the message returned by kf_last_error() and passes the code through.
+int set_error(int code, const std::string& message);
+int cuda_error(cudaError_t err, const char* where);
+
+// Per-device facts, cached on first use.
+struct DeviceInfo {
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  int major = 0;
+  int minor = 0;
+  int* status = nullptr;  // device address of this device's status word
+};
+int device_info(int device, DeviceInfo** out);
+int current_device(int* device);
+
+// One GEMM problem as the C ABI received it (element strides).
+struct GemmArgs {
+  int dtype = KF_FP16;
+  const void* a = nullptr;
+  int64_t sa_m = 0, sa_k = 0;
+  const void* b = nullptr;
+  int64_t sb_k = 0, sb_n = 0;
+  void* c = nullptr;
+  int64_t sc_m = 0, sc_n = 0;
+  int64_t M = 0, N = 0, K = 0;
+  const void* bias = nullptr;
+  int epilogue = KF_EPI_NONE;
+  void* workspace = nullptr;
+  int64_t workspace_bytes = 0;
+};
+
+// Fills zero fields of `cfg` with the library default for this problem.
+kf_gemm_config resolve_gemm_config(const GemmArgs& args, const kf_gemm_config* user,
+                                   int sm_count);
+
+// tcgen05 path. Returns KF_ERR_UNALIGNED when the operands cannot be described
+// by TMA tensor maps, KF_ERR_INVALID_CONFIG for configs the kernel cannot run.
+int launch_gemm_tcgen05(const GemmArgs& args, const kf_gemm_config& cfg, const DeviceInfo& dev,
+                        cudaStream_t stream);
+int64_t gemm_tcgen05_workspace_bytes(const GemmArgs& args, const kf_gemm_config& cfg,
+                                     const DeviceInfo& dev);
+int query_tcgen05_config(int dtype, const kf_gemm_config& cfg, int64_t* smem_bytes,
+                         int32_t* tmem_cols);
+// Whether the operands can take the tcgen05 path (TMA strides/alignment).
+bool tcgen05_operands_ok(const GemmArgs& args, std::string* why);
+
+// CUDA-core path: any strides, fp16/bf16/fp32.
+int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream_t stream);
+
+// Row kernels.
+struct RowsArgs {
+  int dtype = KF_FP16;
+  int op = 0;  // 0 softmax, 1 rmsnorm
+  const void* x = nullptr;
+  int64_t sx = 0;
+  const void* gamma = nullptr;
+  void* y = nullptr;
+  int64_t sy = 0;
+  int64_t rows = 0, cols = 0;
+  float eps = 0.0f;
+};
+kf_rows_config resolve_rows_config(const RowsArgs& args, const kf_rows_config* user);
+int launch_rows(const RowsArgs& args, const kf_rows_config& cfg, const DeviceInfo& dev,
+                cudaStream_t stream);
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace kf

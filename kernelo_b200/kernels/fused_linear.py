@@ -1,0 +1,162 @@
+"""Fused linear + bias + GELU on sm_100a (``kernelforge/kernels/fused_linear.py:1-216``).
+
+``y = gelu(x @ w + bias)`` in one kernel: the GEMM accumulates in TMEM and the
+epilogue warps add the bias, apply GELU and round to the output dtype before
+the single store, so the M x N intermediate is never written (1 launch, M*N
+output traffic, against 3 launches and 5*M*N unfused).
+
+``w`` is ``(K, N)`` as in the reference (``torch.matmul`` orientation); an
+``nn.Linear`` weight ``[N, K]`` is passed as ``weight.t()`` and read through
+its strides with no copy -- that K-major layout is the fast one for tcgen05.
+
+GELU forms: ``approximate="tanh"`` is the reference's (``linear_gelu_reference``
+= ``F.gelu(..., approximate="tanh")``, fused_linear.py:160-162);
+``approximate="none"`` (alias ``"erf"``) is the exact x * Phi(x) form the
+baseline workload specifies. Both call CUDA's own ``tanhf`` / ``erff``.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+import torch
+import torch.nn.functional as F
+
+from kernelo_b200.benchmark import metrics
+from kernelo_b200.kernels import gemm_common as gc
+from kernelo_b200.kernels.base import Operator, seeded_generator
+from kernelo_b200.runtime import native
+from kernelo_b200.tuning.config import KernelConfig, Problem
+from kernelo_b200.tuning.search import FusedLinearErfSearchSpace, FusedLinearSearchSpace
+
+_EPILOGUES = {
+    "tanh": native.KF_EPI_BIAS_GELU_TANH,
+    "none": native.KF_EPI_BIAS_GELU_ERF,
+    "erf": native.KF_EPI_BIAS_GELU_ERF,
+}
+
+
+def _torch_approximate(approximate: str) -> str:
+    if approximate not in _EPILOGUES:
+        raise ValueError(f"approximate must be 'tanh', 'none' or 'erf', got {approximate!r}")
+    return "tanh" if approximate == "tanh" else "none"
+
+
+def fused_linear_gelu(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    bias: torch.Tensor,
+    *,
+    config: KernelConfig | None = None,
+    approximate: str = "tanh",
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``gelu(x @ w + bias)`` in one launch; ``w`` is (K, N), any strides.
+
+    ``out`` may be a preallocated (M, N) tensor or view (e.g. a column slice
+    of a larger buffer); otherwise a contiguous output is allocated.
+    """
+    if x.ndim != 2 or w.ndim != 2:
+        raise ValueError(f"expected 2D x and w, got {tuple(x.shape)} and {tuple(w.shape)}")
+    if x.shape[1] != w.shape[0]:
+        raise ValueError(f"shape mismatch: {tuple(x.shape)} @ {tuple(w.shape)}")
+    if tuple(bias.shape) != (w.shape[1],):
+        raise ValueError(f"bias must have shape ({w.shape[1]},), got {tuple(bias.shape)}")
+    if not (x.dtype == w.dtype == bias.dtype):
+        raise ValueError(f"dtype mismatch: {x.dtype}, {w.dtype}, {bias.dtype}")
+    if not (x.device == w.device == bias.device) or x.device.type != "cuda":
+        raise ValueError("x, w and bias must be CUDA tensors on one device")
+    epilogue = _EPILOGUES.get(approximate)
+    if epilogue is None:
+        raise ValueError(f"approximate must be 'tanh', 'none' or 'erf', got {approximate!r}")
+    m, n = x.shape[0], w.shape[1]
+    if out is None:
+        out = torch.empty((m, n), device=x.device, dtype=x.dtype)
+    elif tuple(out.shape) != (m, n) or out.dtype != x.dtype:
+        raise ValueError(f"out must be a ({m}, {n}) {x.dtype} tensor")
+    if m and n:
+        native.gemm(x, w, out, bias=bias, epilogue=epilogue,
+                    launch=native.GemmLaunch.from_config(config))
+    return out
+
+
+def linear_gelu_reference(
+    x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, approximate: str = "tanh"
+) -> torch.Tensor:
+    """The unfused sequence a model would run: matmul, bias add, GELU."""
+    return F.gelu(torch.matmul(x, w) + bias, approximate=_torch_approximate(approximate))
+
+
+def default_config(m: int, n: int, k: int, dtype: torch.dtype, *, operation: str = "fused_linear",
+                   sm_count: int = 148) -> KernelConfig:
+    """Library default for x [M,K] and an nn.Linear weight [N,K] passed as ``weight.t()``."""
+    return gc.default_gemm_config(operation, m, n, k, dtype, b_layout="nk", sm_count=sm_count)
+
+
+class FusedLinearOperator(Operator):
+    """``gelu(x @ w + b)`` with the reference's tanh GELU."""
+
+    name = "fused_linear"
+    approximate = "tanh"
+    config_order = ("KERNEL", "BLOCK_M", "BLOCK_N", "BLOCK_K", "GROUP_M", "num_stages", "STREAM_K",
+                    "SWAP_AB", "CLUSTER_M", "CLUSTER_N")
+
+    def __init__(self, *, distribution: str = "baseline") -> None:
+        if distribution not in ("baseline", "reference"):
+            raise ValueError("distribution must be 'baseline' or 'reference'")
+        self.distribution = distribution
+
+    def search_space(self):
+        return FusedLinearSearchSpace()
+
+    def make_inputs(self, problem: Problem, device: torch.device, *, seed: int = 0):
+        """x ~ N(0,1) [M,K]; W ~ N(0,1/K) stored [N,K] and passed as W.t();
+        bias ~ N(0, 0.1) (variance 0.1, the baseline workload) or N(0, 1)
+        (``distribution="reference"``, fused_linear.py:183)."""
+        d = problem.dims_dict
+        gen = seeded_generator(seed)
+        x = torch.randn(d["M"], d["K"], generator=gen).to(problem.dtype)
+        weight = (torch.randn(d["N"], d["K"], generator=gen) * d["K"] ** -0.5).to(problem.dtype)
+        std = 0.1**0.5 if self.distribution == "baseline" else 1.0
+        bias = (torch.randn(d["N"], generator=gen) * std).to(problem.dtype)
+        return x.to(device), weight.to(device).t(), bias.to(device)
+
+    def reference(self, *inputs: torch.Tensor) -> torch.Tensor:
+        x, w, bias = inputs
+        return linear_gelu_reference(x, w, bias, self.approximate)
+
+    def run(self, config: KernelConfig, *inputs: torch.Tensor) -> torch.Tensor:
+        x, w, bias = inputs
+        return fused_linear_gelu(x, w, bias, config=config, approximate=self.approximate)
+
+    def default_config(self, problem: Problem) -> KernelConfig:
+        d = problem.dims_dict
+        return default_config(d["M"], d["N"], d["K"], problem.dtype, operation=self.name)
+
+    def flops(self, problem: Problem) -> int:
+        d = problem.dims_dict
+        return metrics.matmul_flops(d["M"], d["N"], d["K"])
+
+    def bytes_moved(self, problem: Problem) -> int:
+        d = problem.dims_dict
+        return metrics.fused_linear_bytes(d["M"], d["N"], d["K"], problem.itemsize, fused=True)
+
+    def baselines(self, problem: Problem, inputs) -> dict[str, Callable[[], torch.Tensor]]:
+        x, w, bias = inputs
+        default = self.default_config(problem)
+        return {
+            "torch_eager": lambda: linear_gelu_reference(x, w, bias, self.approximate),
+            "kernelforge_default": lambda: fused_linear_gelu(
+                x, w, bias, config=default, approximate=self.approximate
+            ),
+        }
+
+
+class FusedLinearErfOperator(FusedLinearOperator):
+    """The baseline workload's variant: exact erf GELU."""
+
+    name = "fused_linear_erf"
+    approximate = "none"
+
+    def search_space(self):
+        return FusedLinearErfSearchSpace()

@@ -1,0 +1,129 @@
+"""Shared host logic of the GEMM-shaped operators (matmul, fused_linear, gemv).
+
+Mirrors, in Python, the two decisions the native library makes per call so
+that configs can be stated explicitly (cached, ranked, filtered):
+
+* whether an operand can be described by a TMA tensor map (16-byte aligned
+  base, unit stride along K or along M/N, the other stride a multiple of 16
+  bytes) -- otherwise only the SIMT kernel can take the problem;
+* the default tcgen05 tile for a shape: 128-row MMA tiles, BLOCK_N up to 256,
+  A/B swapped for skinny M (the weight becomes the 128-row operand), stream-K
+  when whole tiles would leave SMs idle.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from kernelo_b200.tuning.config import KernelConfig
+
+KERNEL_TCGEN05 = 1
+KERNEL_SIMT = 2
+
+SM100_SMEM_PER_BLOCK = 232_448
+TC_BLOCK_M = 128
+#: Bytes the kernel adds to its operand ring: alignment slack and barriers.
+TC_SMEM_OVERHEAD = 1024 + 8 * 37 + 16
+
+
+def tc_smem_bytes(block_n: int, block_k: int, stages: int, itemsize: int = 2) -> int:
+    """Shared memory of one tcgen05 CTA: the A/B ring plus barriers."""
+    return stages * (TC_BLOCK_M + block_n) * block_k * itemsize + 1024 + 8 * (2 * stages + 5) + 16
+
+
+def tc_tmem_columns(block_n: int) -> int:
+    """TMEM columns: a double-buffered fp32 accumulator, rounded to a power of two >= 32."""
+    cols = 32
+    while cols < 2 * block_n:
+        cols *= 2
+    return cols
+
+
+def operand_major(t: torch.Tensor, mn_dim: int, k_dim: int) -> int:
+    """0 = K-major, 1 = MN-major, -1 = no TMA description (mirrors gemm_tcgen05.cu)."""
+    if t.dtype not in (torch.float16, torch.bfloat16):
+        return -1
+    if t.data_ptr() % 16 != 0:
+        return -1
+    mn, k = t.shape[mn_dim], t.shape[k_dim]
+    s_mn, s_k = t.stride(mn_dim), t.stride(k_dim)
+    if k < 8:
+        return -1
+    if s_k == 1 and (mn == 1 or (s_mn % 8 == 0 and s_mn >= k)):
+        return 0
+    if s_mn == 1 and s_k % 8 == 0 and s_k >= mn:
+        return 1
+    return -1
+
+
+def shape_allows_tcgen05(m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str) -> str | None:
+    """Why contiguous operands of this shape cannot take the tcgen05 path, or None.
+
+    ``b_layout`` is ``"kn"`` for a row-major (K, N) B (matmul) and ``"nk"`` for
+    an nn.Linear-style [N, K] weight.
+    """
+    if dtype not in (torch.float16, torch.bfloat16):
+        return "tcgen05 kind::f16 takes fp16/bf16 operands only"
+    if k < 8:
+        return f"TMA alignment: K={k} is below one 16-byte vector"
+    if m > 1 and k % 8 != 0:
+        return f"TMA alignment: A row stride K={k} is not a multiple of 16 bytes"
+    if b_layout == "kn" and n > 1 and n % 8 != 0:
+        return f"TMA alignment: B row stride N={n} is not a multiple of 16 bytes"
+    if b_layout == "nk" and n > 1 and k % 8 != 0:
+        return f"TMA alignment: W row stride K={k} is not a multiple of 16 bytes"
+    return None
+
+
+def default_swap(m: int, n: int) -> bool:
+    return m <= 64 and n > m
+
+
+def default_tcgen05_config(
+    operation: str, m: int, n: int, k: int, *, b_layout: str, sm_count: int = 148
+) -> KernelConfig:
+    """The tcgen05 config the library would choose for contiguous operands."""
+    swap = default_swap(m, n)
+    m_k, n_k = (n, m) if swap else (m, n)
+    # B' (the kernel's second operand) is MN-major for matmul's row-major B
+    # unless swapped (then B' is A, which is K-major).
+    b_mn = (b_layout == "kn") and not swap
+    quantum = 64 if b_mn else 16
+    if n_k <= 256:
+        block_n = max(quantum, -(-n_k // quantum) * quantum)
+    else:
+        block_n = 256
+    block_k = 64
+    per_stage = (TC_BLOCK_M + block_n) * block_k * 2
+    stages = max(2, min(12, (SM100_SMEM_PER_BLOCK - 1024 - 256) // per_stage))
+    tiles = -(-m_k // TC_BLOCK_M) * -(-n_k // block_n)
+    k_blocks = -(-k // block_k)
+    stream_k = 1 if (tiles < sm_count and k_blocks >= 4) else 2
+    return KernelConfig(
+        operation,
+        KERNEL=KERNEL_TCGEN05,
+        BLOCK_M=TC_BLOCK_M,
+        BLOCK_N=block_n,
+        BLOCK_K=block_k,
+        GROUP_M=8,
+        num_stages=stages,
+        STREAM_K=stream_k,
+        SWAP_AB=1 if swap else 2,
+        CLUSTER_M=1,
+        CLUSTER_N=1,
+    )
+
+
+def default_simt_config(operation: str, m: int, n: int, *, sm_count: int = 148) -> KernelConfig:
+    small = m * n < 128 * 128 * sm_count
+    if small:
+        return KernelConfig(operation, KERNEL=KERNEL_SIMT, BLOCK_M=64, BLOCK_N=64, BLOCK_K=16)
+    return KernelConfig(operation, KERNEL=KERNEL_SIMT, BLOCK_M=128, BLOCK_N=128, BLOCK_K=8)
+
+
+def default_gemm_config(
+    operation: str, m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str, sm_count: int = 148
+) -> KernelConfig:
+    if shape_allows_tcgen05(m, n, k, dtype, b_layout=b_layout) is None:
+        return default_tcgen05_config(operation, m, n, k, b_layout=b_layout, sm_count=sm_count)
+    return default_simt_config(operation, m, n, sm_count=sm_count)

@@ -1,0 +1,116 @@
+"""Decode-shape GEMM ``Y[M,N] = X[M,K] @ W^T`` for M in 1..256.
+
+The reference has no dedicated kernel: single-token decoding calls its blocked
+GEMM with M=1 (``kernelforge/kernels/matmul.py:132`` with BLOCK_M=16, one tile
+row), and README.md:666-670 lists split-K as future work. This shape moves
+90 MB of weight for 90 MFLOP (1 FLOP/byte), so it is bound by HBM, not by the
+tensor cores. The sm_100a kernel is the tcgen05 GEMM with A and B swapped --
+the weight W [N,K] becomes the 128-row MMA operand, the few activation rows
+the N=16 side -- streamed through a deep TMA ring, with K split evenly over
+every SM (stream-K) so that all 148 SMs pull weight bytes at once. Partial
+sums go to a workspace; the last CTA to finish a tile reduces them in a fixed
+order.
+
+W may be stored [N,K] (``w_layout="nk"``, nn.Linear, the baseline layout) or
+[K,N] (``"kn"``, the reference's ``matmul(x, w)`` orientation).
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+import torch
+
+from kernelo_b200.benchmark import metrics
+from kernelo_b200.kernels import gemm_common as gc
+from kernelo_b200.kernels.base import Operator, seeded_generator
+from kernelo_b200.runtime import native
+from kernelo_b200.testing import exact_fp32_matmul
+from kernelo_b200.tuning.config import KernelConfig, Problem
+from kernelo_b200.tuning.search import GemvSearchSpace
+
+MAX_ROWS = 256
+
+
+def gemv(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    *,
+    w_layout: str = "nk",
+    config: KernelConfig | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``x @ w.T`` (``"nk"``) or ``x @ w`` (``"kn"``) for a handful of rows."""
+    if x.ndim != 2 or w.ndim != 2:
+        raise ValueError(f"expected 2D x and w, got {tuple(x.shape)} and {tuple(w.shape)}")
+    if w_layout not in ("nk", "kn"):
+        raise ValueError(f"w_layout must be 'nk' or 'kn', got {w_layout!r}")
+    k = x.shape[1]
+    k_w = w.shape[1] if w_layout == "nk" else w.shape[0]
+    n = w.shape[0] if w_layout == "nk" else w.shape[1]
+    if k != k_w:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} against w {tuple(w.shape)} ({w_layout})")
+    if x.dtype != w.dtype:
+        raise ValueError(f"dtype mismatch: {x.dtype} vs {w.dtype}")
+    if x.device != w.device or x.device.type != "cuda":
+        raise ValueError("x and w must be CUDA tensors on one device")
+    m = x.shape[0]
+    if m > MAX_ROWS:
+        raise ValueError(f"gemv takes at most {MAX_ROWS} rows, got {m}; use matmul")
+    if out is None:
+        out = torch.empty((m, n), device=x.device, dtype=x.dtype)
+    if m and n:
+        native.gemv(x, w, out, w_layout=w_layout, launch=native.GemmLaunch.from_config(config))
+    return out
+
+
+def default_config(m: int, n: int, k: int, dtype: torch.dtype, *, sm_count: int = 148) -> KernelConfig:
+    if gc.shape_allows_tcgen05(m, n, k, dtype, b_layout="nk") is not None:
+        return gc.default_simt_config("gemv", m, n, sm_count=sm_count)
+    cfg = gc.default_tcgen05_config("gemv", m, n, k, b_layout="nk", sm_count=sm_count)
+    # Always swap and split K: the weight streams through every SM.
+    return cfg.replace(SWAP_AB=1, STREAM_K=1)
+
+
+class GemvOperator(Operator):
+    name = "gemv"
+    config_order = ("KERNEL", "BLOCK_M", "BLOCK_N", "BLOCK_K", "num_stages", "STREAM_K", "SWAP_AB")
+
+    def search_space(self) -> GemvSearchSpace:
+        return GemvSearchSpace()
+
+    def make_inputs(self, problem: Problem, device: torch.device, *, seed: int = 0):
+        """X ~ N(0,1) [M,K]; W ~ N(0,1/K) stored [N,K]."""
+        d = problem.dims_dict
+        gen = seeded_generator(seed)
+        x = torch.randn(d["M"], d["K"], generator=gen).to(problem.dtype)
+        w = (torch.randn(d["N"], d["K"], generator=gen) * d["K"] ** -0.5).to(problem.dtype)
+        return x.to(device), w.to(device)
+
+    def reference(self, *inputs: torch.Tensor) -> torch.Tensor:
+        x, w = inputs
+        with exact_fp32_matmul():
+            return torch.matmul(x, w.t())
+
+    def run(self, config: KernelConfig, *inputs: torch.Tensor) -> torch.Tensor:
+        x, w = inputs
+        return gemv(x, w, config=config)
+
+    def default_config(self, problem: Problem) -> KernelConfig:
+        d = problem.dims_dict
+        return default_config(d["M"], d["N"], d["K"], problem.dtype)
+
+    def flops(self, problem: Problem) -> int:
+        d = problem.dims_dict
+        return metrics.matmul_flops(d["M"], d["N"], d["K"])
+
+    def bytes_moved(self, problem: Problem) -> int:
+        d = problem.dims_dict
+        return metrics.gemv_bytes(d["M"], d["N"], d["K"], problem.itemsize)
+
+    def is_memory_bound(self) -> bool:
+        return True
+
+    def baselines(self, problem: Problem, inputs) -> dict[str, Callable[[], torch.Tensor]]:
+        x, w = inputs
+        return {"torch_eager": lambda: torch.matmul(x, w.t())}
