@@ -1,0 +1,431 @@
+"""Headline benchmark: fused linear + bias + exact-erf GELU, 4096 x 11008 x 4096 bf16.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+One step = ``Y = gelu(X @ W^T + b)`` over the whole workload (X [4096,4096],
+W [11008,4096] stored nn.Linear-style, b [11008]; X ~ N(0,1), W ~ N(0,1/4096),
+b ~ N(0,0.1); synthetic, seeded). With N GPUs (torchrun, one process per GPU,
+NCCL) the weight is column-sharded by N and the output slices are exchanged
+with one all-gather per step (strong scaling: the total work is fixed).
+
+Printed (rank 0, one JSON line): whole-job TFLOP/s over K timed steps (device
+time, CUDA events, max over ranks, barrier + synchronize on both sides), the
+end-to-end figure through the public API with host<->device copies, the
+dominant kernel's roofline against the measured peak, SM clocks sampled during
+the timed region, the reference's CPU path timed on this host's cores, and the
+memory-bound rows (RMSNorm, softmax, decode GEMV) as secondary lines.
+
+``--impl reference`` times the reference's own CPU implementation of the path
+(the oracle's restatement of ``linear_gelu_reference``, torch on host cores,
+fp32) on a bounded sample of the same workload, and prints the same line with
+``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+M, N, K = 4096, 11008, 4096
+FLOP = 2 * M * N * K
+METRIC = "fused_linear_gelu TFLOP/s (4096x11008x4096 bf16, erf GELU)"
+UNIT = "TFLOP/s"
+WORKLOAD = "fused_linear bias+erf-GELU M=4096 N=11008 K=4096 bf16, W [N,K]"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks() -> tuple[dict, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+def profile_traffic(kernel: str) -> float | None:
+    """Per-launch DRAM bytes recorded from an ncu capture (profiles/<kernel>.txt)."""
+    path = REPO / "profiles" / f"{kernel}.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+        else:
+            self.out = ""
+
+    def summary(self) -> dict:
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        max_mhz = rows[0][1]
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in loaded for i, flag in enumerate(r[3]) if flag.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max_mhz, "reasons": reasons,
+                "samples": len(loaded), "power_w_max": max(r[2] for r in rows)}
+
+
+# ------------------------------------------------------------------ helpers
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if gpus != world:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs(device, rank: int, world: int):
+    """X replicated on every rank; each rank builds only its W/b slice."""
+    from kernelo_b200.distributed import shard_chunk
+
+    gen = torch.Generator(device=device).manual_seed(1234)
+    x = torch.randn(M, K, device=device, generator=gen, dtype=torch.float32).to(torch.bfloat16)
+    chunk = shard_chunk(N, world) if world > 1 else N
+    wgen = torch.Generator(device=device).manual_seed(99 + rank)
+    w = (torch.randn(chunk, K, device=device, generator=wgen) * K ** -0.5).to(torch.bfloat16)
+    b = (torch.randn(chunk, device=device, generator=wgen) * math.sqrt(0.1)).to(torch.bfloat16)
+    if world > 1:  # zero the padding rows of the last shard
+        valid = max(0, min(chunk, N - rank * chunk))
+        w[valid:] = 0
+        b[valid:] = 0
+    return x, w, b, chunk
+
+
+def cpu_baseline(rows: int = 512, budget_s: float = 10.0) -> dict:
+    """The reference's CPU path (oracle restatement, torch on host cores, fp32)
+    on a bounded sample: ``rows`` rows of X against the full W."""
+    from oracle.cpu_reference import torch_cpu
+
+    gen = torch.Generator().manual_seed(7)
+    x = torch.randn(rows, K, generator=gen).bfloat16()
+    w = (torch.randn(N, K, generator=gen) * K ** -0.5).bfloat16()
+    b = (torch.randn(N, generator=gen) * math.sqrt(0.1)).bfloat16()
+    wt = w.t()
+    torch_cpu.linear_gelu(x[:8], wt, b, "none")  # warm the BLAS
+    flop = 2 * rows * N * K
+    calls, start = 0, time.perf_counter()
+    while True:
+        torch_cpu.linear_gelu(x, wt, b, "none")
+        calls += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= budget_s or calls >= 50:
+            break
+    return {"value": flop * calls / elapsed / 1e12, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{calls} calls of {rows}x{N}x{K} (fp32 math on bf16 operands) in {elapsed:.1f} s",
+            "host_cpus": os.cpu_count()}
+
+
+# ------------------------------------------------------------------ secondary rows
+def secondary_lines(pk: dict, flush: torch.Tensor) -> list[dict]:
+    """Memory-bound rows at their baseline sizes, N=1: GB/s and fraction of HBM peak."""
+    from kernelo_b200.benchmark.metrics import gemv_bytes, rmsnorm_bytes, softmax_bytes
+    from kernelo_b200.kernels.gemv import gemv
+    from kernelo_b200.kernels.rmsnorm import rmsnorm
+    from kernelo_b200.kernels.softmax import softmax
+
+    dev = torch.device("cuda")
+    out = []
+
+    def time_ms(fn, iters=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for s, e in ev:
+            flush.zero_()
+            s.record()
+            fn()
+            e.record()
+        torch.cuda.synchronize()
+        return statistics.median(s.elapsed_time(e) for s, e in ev)
+
+    g = torch.Generator(device=dev).manual_seed(5)
+    for cols in (4096, 8192):
+        x = torch.randn(16384, cols, device=dev, generator=g).bfloat16()
+        gamma = (torch.randn(cols, device=dev, generator=g) * 0.1 + 1).bfloat16()
+        ms = time_ms(lambda: rmsnorm(x, gamma, eps=1e-6))
+        gbs = rmsnorm_bytes(16384, cols, 2) / ms / 1e6
+        out.append({"metric": f"rmsnorm 16384x{cols} bf16", "value": round(gbs, 1), "unit": "GB/s",
+                    "frac": round(gbs / pk["hbm_gbs"], 3)})
+        del x
+    for cols, dt in ((1000, torch.float16), (4096, torch.float16), (4097, torch.float16), (32000, torch.float32)):
+        x = (torch.randn(32768, cols, device=dev, generator=g) * 4).to(dt)
+        ms = time_ms(lambda: softmax(x), iters=10)
+        gbs = softmax_bytes(32768, cols, x.element_size()) / ms / 1e6
+        out.append({"metric": f"softmax 32768x{cols} {str(dt)[6:]}", "value": round(gbs, 1), "unit": "GB/s",
+                    "frac": round(gbs / pk["hbm_gbs"], 3)})
+        del x
+    w = (torch.randn(N, K, device=dev, generator=g) * K ** -0.5).half()
+    for m in (1, 4, 16):
+        xx = torch.randn(m, K, device=dev, generator=g).half()
+        ms = time_ms(lambda: gemv(xx, w), iters=50)
+        gbs = gemv_bytes(m, N, K, 2) / ms / 1e6
+        out.append({"metric": f"gemv M={m} N={N} K={K} fp16", "value": round(gbs, 1), "unit": "GB/s",
+                    "frac": round(gbs / pk["hbm_gbs"], 3)})
+    return out
+
+
+# ------------------------------------------------------------------ arms
+def run_reference(args, world: int, rank: int) -> int:
+    if rank != 0:
+        return 0
+    rows = 256
+    from oracle.cpu_reference import torch_cpu
+
+    gen = torch.Generator().manual_seed(7)
+    x = torch.randn(rows, K, generator=gen).bfloat16()
+    w = (torch.randn(N, K, generator=gen) * K ** -0.5).bfloat16().t()
+    b = (torch.randn(N, generator=gen) * math.sqrt(0.1)).bfloat16()
+    for _ in range(max(args.warmup, 1)):
+        torch_cpu.linear_gelu(x, w, b, "none")
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        torch_cpu.linear_gelu(x, w, b, "none")
+    elapsed = time.perf_counter() - start
+    value = 2 * rows * N * K * args.steps / elapsed / 1e12
+    sample = f"each step {rows}x{N}x{K} rows of the workload (torch fp32 on host cores)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_rows": rows, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_native(args, world: int, rank: int, local: int) -> int:
+    from kernelo_b200.distributed import ShardedFusedLinear
+    from kernelo_b200.kernels.fused_linear import fused_linear_gelu
+    from kernelo_b200.runtime import native
+
+    dev = torch.device("cuda", local)
+    pk, pk_kind = peaks()
+    x, w, b, chunk = make_inputs(dev, rank, world)
+    if world > 1:
+        layer = ShardedFusedLinear(None, None, out_features=N, shard_weight=w, shard_bias=b, approximate="none")
+
+        def step():
+            return layer(x)
+
+        def kernel_only():
+            return layer.local(x, out=layer._gather_buf[rank] if layer._gather_buf is not None else None)
+    else:
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+
+        def step():
+            return fused_linear_gelu(x, w.t(), b, approximate="none", out=y)
+
+        kernel_only = step
+
+    # correctness gate on a sample before timing (never inside the timed region)
+    out = step()
+    torch.cuda.synchronize()
+    rows = torch.arange(0, M, 97, device=dev)[:32]
+    full_w = w if world == 1 else None
+    if full_w is not None:
+        ref = torch.nn.functional.gelu(x[rows].float() @ full_w.float().t() + b.float(), approximate="none")
+        err = float((out[rows].float() - ref).abs().max() / ref.abs().max())
+        if not err < 2e-2:
+            raise SystemExit(f"fused linear failed the bf16 gate before timing: err={err:.3e}")
+    if native.device_status(local) != 0:
+        raise SystemExit("device status word set before timing")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_total = max_over_ranks(start.elapsed_time(end), world)
+    ms_step = ms_total / args.steps
+    value = FLOP * args.steps / (ms_total * 1e-3) / 1e12
+
+    # dominant kernel alone: average launch duration over a burst, same stream
+    kiters = max(10, min(200, args.steps))
+    torch.cuda.synchronize()
+    ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ks.record(stream)
+    for _ in range(kiters):
+        kernel_only()
+    ke.record(stream)
+    torch.cuda.synchronize()
+    kernel_ms = max_over_ranks(ks.elapsed_time(ke) / kiters, world)
+    achieved = FLOP / world / (kernel_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} burst bf16",
+                "traffic": profile_traffic("tc_gemm_fused_linear_erf_bf16"), "kernel": "tc_gemm_kernel<bf16,erf>",
+                "kernel_ms": round(kernel_ms, 4)}
+
+    # end to end through the public API: pinned host X in, Y back to pinned host
+    e2e_steps = max(3, min(20, args.steps))
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        if world > 1:
+            yy = layer(x_dev)
+        else:
+            yy = fused_linear_gelu(x_dev, w.t(), b, approximate="none", out=y)
+        y_host.copy_(yy, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(es.elapsed_time(ee), world)
+    e2e_value = FLOP * e2e_steps / (e2e_ms * 1e-3) / 1e12
+
+    secondary = []
+    baseline = None
+    if rank == 0 and world == 1 and not args.no_secondary:
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.int8, device=dev)
+        secondary = secondary_lines(pk, flush)
+        del flush
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        baseline = cpu_baseline()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) X, N(0,1/4096) W, N(0,0.1) b; random init)",
+            "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "gelu": "erf",
+                       "parallelism": f"N-sharded columns x{world} + NCCL all_gather" if world > 1 else "single GPU",
+                       "l2": "inputs exceed L2 (X 32 MiB + W 86 MiB + Y 86 MiB > 126 MiB), no flush"},
+            "roofline": roofline,
+            "clocks": clocks.summary(),
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": x.numel() * 2,
+                    "d2h_bytes_per_step": M * N * 2, "steps": e2e_steps},
+            "gpu_launches": args.steps,
+            "cpu_baseline": baseline,
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=("native", "reference"), default="native")
+    p.add_argument("--no-secondary", action="store_true", help="skip the memory-bound rows")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    args = p.parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference(args, world, rank)
+    world, rank, local = dist_setup(args.gpus)
+    return run_native(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -320,7 +320,9 @@ int32_t kf_query_gemm_config(int32_t dtype, const kf_gemm_config* cfg, int64_t* 
     if (tmem_cols) *tmem_cols = 0;
     return KF_OK;
   }
-  return query_tcgen05_config(dtype, *cfg, smem_bytes, tmem_cols);
+  kf_gemm_config c = *cfg;
+  if (c.group_m == 0) c.group_m = 8;  // zero selects the default, as at launch
+  return query_tcgen05_config(dtype, c, smem_bytes, tmem_cols);
 }
 
 int32_t kf_softmax_rows(int32_t dtype, const void* x, int64_t sx_row, void* y, int64_t sy_row,

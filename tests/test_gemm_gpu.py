@@ -1,0 +1,295 @@
+"""GEMM, fused linear and decode GEMV on the B200, against the CPU oracle.
+
+Mirrors the reference's GEMM test strategy (tests/test_matmul.py,
+tests/test_fused_linear.py): awkward shapes (primes, one-off-a-tile, single
+rows/columns) in every dtype, several tile configs per shape, every budgeted
+candidate, non-contiguous views, fp32 held to the fp32 gate, and the fusion's
+launch count -- plus the sm_100a specifics: both weight layouts, swapped
+skinny shapes, stream-K workspace reuse and determinism, and the baseline's
+full sizes checked on sampled rows.
+"""
+
+from __future__ import annotations
+
+import random
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from kernelo_b200.benchmark import workloads
+from kernelo_b200.kernels import gemm_common as gc
+from kernelo_b200.kernels.fused_linear import FusedLinearErfOperator, fused_linear_gelu
+from kernelo_b200.kernels.gemv import gemv
+from kernelo_b200.kernels.matmul import matmul
+from kernelo_b200.runtime import native
+from kernelo_b200.runtime.env import device_caps
+from kernelo_b200.tuning.config import KernelConfig, Problem
+from kernelo_b200.tuning.search import FusedLinearSearchSpace, MatmulSearchSpace
+from oracle import cpu_reference as ref
+from tests.conftest import golden_names, load_golden
+from tests.parity import gate, host, sample_rows
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+SHAPES = [tuple(p.dims_dict.values()) for p in workloads.problems("matmul", "correctness")]
+
+
+def operands(m, k, n, dtype, device, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=gen).to(dtype).to(device)
+    b = torch.randn(k, n, generator=gen).to(dtype).to(device)
+    return a, b
+
+
+def tc(op="matmul", **kw):
+    base = dict(KERNEL=1, BLOCK_M=128, BLOCK_N=128, BLOCK_K=64, GROUP_M=8, num_stages=4, STREAM_K=2, SWAP_AB=2)
+    base.update(kw)
+    return KernelConfig(op, **base)
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_matmul_default_config_awkward_shapes(shape, dtype, device):
+    m, n, k = shape
+    a, b = operands(m, k, n, dtype, device)
+    gate(ref.matmul_ref(host(a), host(b)), matmul(a, b), dtype, context=f"{shape} {dtype}")
+
+
+@pytest.mark.parametrize(
+    "config",
+    [
+        tc(BLOCK_N=64),
+        tc(BLOCK_N=128, BLOCK_K=128, num_stages=3),
+        tc(BLOCK_N=256, num_stages=3),
+        tc(BLOCK_N=128, STREAM_K=1),
+        KernelConfig("matmul", KERNEL=2, BLOCK_M=128, BLOCK_N=128, BLOCK_K=8),
+        KernelConfig("matmul", KERNEL=2, BLOCK_M=64, BLOCK_N=64, BLOCK_K=16),
+    ],
+)
+@pytest.mark.parametrize("shape", [(127, 192, 64), (257, 256, 512), (1, 128, 4096), (300, 64, 1024)])
+def test_matmul_tile_configs_mask_boundaries(config, shape, device):
+    m, n, k = shape
+    a, b = operands(m, k, n, torch.float16, device)
+    gate(ref.matmul_ref(host(a), host(b)), matmul(a, b, config=config), torch.float16,
+         context=f"{shape} {config}")
+
+
+@pytest.mark.parametrize("seed", range(16))
+def test_matmul_randomised_shapes_and_candidates(seed, device):
+    rng = random.Random(seed)
+    m, n, k = (rng.randint(1, 600) for _ in range(3))
+    if rng.random() < 0.5:  # half the draws on TMA-friendly multiples of 8
+        n, k = 8 * max(1, n // 8), 8 * max(1, k // 8)
+    dtype = rng.choice(DTYPES)
+    problem = Problem.create("matmul", dtype, M=m, N=n, K=k)
+    chosen = rng.choice(MatmulSearchSpace().candidates(problem, device_caps(device)))
+    a, b = operands(m, k, n, dtype, device, seed=seed)
+    gate(ref.matmul_ref(host(a), host(b)), matmul(a, b, config=chosen), dtype,
+         context=f"{m}x{n}x{k} {dtype} {chosen}")
+
+
+def test_every_budgeted_matmul_candidate_agrees(device):
+    problem = Problem.create("matmul", "fp16", M=257, N=512, K=320)
+    a, b = operands(257, 320, 512, torch.float16, device)
+    expected = ref.matmul_ref(host(a), host(b))
+    cands = MatmulSearchSpace().candidates(problem, device_caps(device))
+    assert any(c["KERNEL"] == gc.KERNEL_TCGEN05 for c in cands)
+    for c in cands:
+        gate(expected, matmul(a, b, config=c), torch.float16, context=repr(c))
+
+
+def test_non_contiguous_views_need_no_copy(device):
+    gen = torch.Generator().manual_seed(0)
+    for dtype in (torch.float16, torch.bfloat16):
+        a = torch.randn(128, 96, generator=gen).to(dtype).to(device).t()   # [96,128], M-major
+        b = torch.randn(192, 128, generator=gen).to(dtype).to(device).t()  # [128,192], K-major
+        assert not a.is_contiguous() and not b.is_contiguous()
+        gate(ref.matmul_ref(host(a), host(b)), matmul(a, b), dtype)
+        sliced = torch.randn(64, 256, generator=gen).to(dtype).to(device)[:, 64:192]  # row stride 256
+        bb = torch.randn(128, 80, generator=gen).to(dtype).to(device)
+        gate(ref.matmul_ref(host(sliced), host(bb)), matmul(sliced, bb), dtype)
+
+
+def test_fp32_is_ieee_not_tf32(device):
+    a, b = operands(512, 1024, 256, torch.float32, device)
+    result = gate(ref.matmul_ref(host(a), host(b)), matmul(a, b), torch.float32)
+    assert result.error < 1e-5
+
+
+def test_k_zero_and_empty_outputs(device):
+    a = torch.randn(5, 0, device=device, dtype=torch.float16)
+    b = torch.randn(0, 7, device=device, dtype=torch.float16)
+    assert torch.count_nonzero(matmul(a, b)) == 0
+    assert matmul(torch.randn(0, 8, device=device).half(), torch.randn(8, 3, device=device).half()).shape == (0, 3)
+
+
+def test_matmul_validation(device):
+    a = torch.randn(4, 8, device=device, dtype=torch.float16)
+    with pytest.raises(ValueError, match="shape mismatch"):
+        matmul(a, torch.randn(9, 4, device=device, dtype=torch.float16))
+    with pytest.raises(ValueError, match="dtype mismatch"):
+        matmul(a, torch.randn(8, 4, device=device, dtype=torch.float32))
+    with pytest.raises(ValueError, match="2D"):
+        matmul(a, torch.randn(8, device=device, dtype=torch.float16))
+
+
+def test_infeasible_config_raises_out_of_resources(device):
+    a, b = operands(64, 72, 64, torch.float16, device)  # K=72 is fine, N=64 is fine
+    with pytest.raises(native.OutOfResources):
+        matmul(a, b, config=tc(BLOCK_N=256, BLOCK_K=64, num_stages=8))  # 384 KiB of smem
+    c, d = operands(64, 509, 64, torch.float16, device)  # K=509: no TMA description
+    with pytest.raises(native.OutOfResources):
+        matmul(c, d, config=tc())
+
+
+# ------------------------------------------------------------------ fused linear
+def linear_inputs(m, k, n, dtype, device, seed=0, layout="nk"):
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=gen).to(dtype).to(device)
+    w = (torch.randn(n, k, generator=gen) * k ** -0.5).to(dtype).to(device)
+    b = (torch.randn(n, generator=gen) * 0.316).to(dtype).to(device)
+    return x, (w.t() if layout == "nk" else w.t().contiguous()), b
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("approximate", ["tanh", "none"])
+def test_fused_linear_matches_unfused_sequence(shape, dtype, approximate, device):
+    m, n, k = shape
+    x, w, b = linear_inputs(m, k, n, dtype, device)
+    expected = ref.linear_gelu_ref(host(x), host(w), host(b), approximate)
+    gate(expected, fused_linear_gelu(x, w, b, approximate=approximate), dtype, context=f"{shape} {dtype}")
+
+
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("m", [1, 16, 100, 513])
+def test_fused_linear_weight_layouts_and_skinny_swap(layout, m, device):
+    x, w, b = linear_inputs(m, 512, 1000, torch.bfloat16, device, layout=layout)
+    gate(ref.linear_gelu_ref(host(x), host(w), host(b), "none"),
+         fused_linear_gelu(x, w, b, approximate="none"), torch.bfloat16, context=f"{layout} m={m}")
+
+
+def test_gelu_over_its_whole_range(device):
+    """tests/test_fused_linear.py:96-122 through an identity weight (fp32 -> SIMT path)."""
+    g = load_golden("fused_linear_gelu_range_fp32")
+    x, w, b = (torch.from_numpy(a).to(device) for a in g["inputs"])
+    out = fused_linear_gelu(x, w, b, approximate="tanh")
+    assert torch.isfinite(out).all()
+    gate(g["ref_torch"], out, torch.float32, threshold=1e-4)
+    gate(ref.gelu_tanh(host(x)), out, torch.float32, threshold=1e-4)
+    # and the erf form, through bf16 tcgen05 with the identity scaled into range
+    xs = torch.linspace(-8, 8, 1024, device=device).reshape(1, -1).bfloat16()
+    eye = torch.eye(1024, device=device).bfloat16()
+    gate(ref.gelu_erf(host(xs)), fused_linear_gelu(xs, eye, torch.zeros(1024, device=device).bfloat16(),
+                                                   approximate="none"), torch.bfloat16)
+
+
+def test_bias_precedes_activation(device):
+    g = load_golden("fused_linear_bias_order_fp32")
+    x, w, b = (torch.from_numpy(a).to(device) for a in g["inputs"])
+    gate(g["ref_torch"], fused_linear_gelu(x, w, b), torch.float32)
+    xb, wb, bb = x.bfloat16(), torch.zeros(32, 64, device=device).bfloat16(), b.bfloat16()
+    gate(ref.gelu_tanh(host(bb))[None, :].repeat(8, 0), fused_linear_gelu(xb, wb, bb), torch.bfloat16)
+
+
+def test_every_budgeted_fused_candidate_agrees(device):
+    problem = Problem.create("fused_linear", "fp16", M=257, N=512, K=192)
+    x, w, b = linear_inputs(257, 192, 512, torch.float16, device)
+    expected = ref.linear_gelu_ref(host(x), host(w), host(b), "tanh")
+    for c in FusedLinearSearchSpace().candidates(problem, device_caps(device)):
+        gate(expected, fused_linear_gelu(x, w, b, config=c), torch.float16, context=repr(c))
+
+
+def test_fusion_is_one_launch(device):
+    from kernelo_b200.profiling import profile_kernels
+
+    x, w, b = linear_inputs(1024, 1024, 1024, torch.float16, device)
+    fused = profile_kernels(lambda: fused_linear_gelu(x, w, b), label="fused", warmup=3, iterations=5)
+    unfused = profile_kernels(lambda: F.gelu(x @ w + b, approximate="tanh"), label="unfused",
+                              warmup=3, iterations=5)
+    assert fused.launches_per_iteration == pytest.approx(1.0, abs=0.01)
+    assert unfused.launches_per_iteration >= 2.0
+
+
+def test_fused_linear_validation(device):
+    x = torch.zeros(4, 8, device=device, dtype=torch.float16)
+    w = torch.zeros(8, 16, device=device, dtype=torch.float16)
+    bias = torch.zeros(16, device=device, dtype=torch.float16)
+    with pytest.raises(ValueError, match="bias must have shape"):
+        fused_linear_gelu(x, w, torch.zeros(8, device=device, dtype=torch.float16))
+    with pytest.raises(ValueError, match="shape mismatch"):
+        fused_linear_gelu(x, torch.zeros(9, 16, device=device, dtype=torch.float16), bias)
+    with pytest.raises(ValueError, match="dtype mismatch"):
+        fused_linear_gelu(x, w.float(), bias)
+    with pytest.raises(ValueError, match="approximate"):
+        fused_linear_gelu(x, w, bias, approximate="sigmoid")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_baseline_fused_linear_full_size_sampled_rows(dtype, device):
+    """4096 x 11008 x 4096, erf GELU, the headline workload: rows checked on a sample."""
+    op = FusedLinearErfOperator()
+    problem = Problem.create("fused_linear_erf", dtype, M=4096, N=11008, K=4096)
+    x, w, b = op.make_inputs(problem, device, seed=0)
+    out = op.run(op.default_config(problem), x, w, b)
+    rows = sample_rows(4096, 48)
+    expected = ref.linear_gelu_ref(host(x[rows]), host(w), host(b), "none")
+    gate(expected, out[rows], dtype)
+    assert torch.isfinite(out).all()
+
+
+# ------------------------------------------------------------------ golden fixtures
+@pytest.mark.parametrize("name", [n for n in golden_names() if n.startswith(("matmul", "fused_linear_"))
+                                  and "range" not in n and "bias_order" not in n])
+def test_golden_gemm_fixtures(name, device):
+    g = load_golden(name)
+    dtype = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32}[g["meta"]["dtype"]]
+    ins = [torch.from_numpy(a).to(dtype).to(device) for a in g["inputs"]]
+    out = matmul(*ins) if g["meta"]["op"] == "matmul" else fused_linear_gelu(*ins, approximate="tanh")
+    gate(g["ref_torch"], out, dtype, context=name)
+    if g["ref_kernel"] is not None:
+        gate(g["ref_kernel"], out, dtype, context=name + " vs reference kernel")
+
+
+# ------------------------------------------------------------------ decode GEMV
+@pytest.mark.parametrize("m", [1, 4, 16])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+def test_gemv_baseline_shapes(m, dtype, layout, device):
+    gen = torch.Generator().manual_seed(m)
+    x = torch.randn(m, 4096, generator=gen).to(dtype).to(device)
+    w_nk = (torch.randn(11008, 4096, generator=gen) * 4096 ** -0.5).to(dtype).to(device)
+    w = w_nk if layout == "nk" else w_nk.t().contiguous()
+    out = gemv(x, w, w_layout=layout)
+    gate(ref.gemv_ref(host(x), host(w_nk)), out, dtype, context=f"M={m} {layout}")
+
+
+def test_gemv_stream_k_is_deterministic_and_reuses_its_workspace(device):
+    """Calls with different tile/grid layouts share one pooled workspace; the
+    arrival counters must come back to zero after each, and the fixed-order
+    reduction must give bitwise-identical results on repeat."""
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(16, 4096, generator=gen).half().to(device)
+    w = (torch.randn(11008, 4096, generator=gen) * 0.02).half().to(device)
+    expected = ref.gemv_ref(host(x), host(w))
+    first = gemv(x, w)
+    for cfg in (
+        KernelConfig("gemv", KERNEL=1, BLOCK_M=128, BLOCK_N=16, BLOCK_K=128, num_stages=6, STREAM_K=1, SWAP_AB=1),
+        KernelConfig("gemv", KERNEL=1, BLOCK_M=128, BLOCK_N=32, BLOCK_K=64, num_stages=8, STREAM_K=1, SWAP_AB=1,
+                     NUM_CTAS=37),
+        None,
+    ):
+        gate(expected, gemv(x, w, config=cfg), torch.float16, context=str(cfg))
+    assert torch.equal(first, gemv(x, w))
+    assert native.device_status(device.index) == 0
+
+
+def test_gemv_validation(device):
+    x = torch.randn(300, 64, device=device, dtype=torch.float16)
+    with pytest.raises(ValueError, match="at most"):
+        gemv(x, torch.randn(128, 64, device=device, dtype=torch.float16))
+    with pytest.raises(ValueError, match="shape mismatch"):
+        gemv(x[:4], torch.randn(128, 65, device=device, dtype=torch.float16))

@@ -1,0 +1,169 @@
+"""Softmax and RMSNorm on the B200 against the CPU oracle.
+
+Follows tests/test_softmax_and_vector_add.py and tests/test_rmsnorm.py of the
+reference: awkward widths in every dtype, overflow logits, constant rows, zero
+rows, the fp32-reduction teeth test, indivisible rows per program, every
+candidate -- plus the widths the reference kernels refuse (4097 with unaligned
+rows, 32000 through a thread-block cluster) and the baseline sizes.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from kernelo_b200.benchmark import workloads
+from kernelo_b200.kernels.rmsnorm import RMSNormOperator, rmsnorm
+from kernelo_b200.kernels.softmax import SoftmaxOperator, softmax
+from kernelo_b200.runtime.env import device_caps
+from kernelo_b200.tuning.config import KernelConfig, Problem
+from kernelo_b200.tuning.search import RMSNormSearchSpace, SoftmaxSearchSpace
+from oracle import cpu_reference as ref
+from tests.conftest import golden_names, load_golden
+from tests.parity import gate, host, sample_rows
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+ROW_SHAPES = [tuple(p.dims_dict.values()) for p in workloads.problems("softmax", "correctness")] + [
+    (8, 4097), (4, 32000), (2, 65536), (3, 1000)]
+
+
+def rand(rows, cols, dtype, device, scale=1.0, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    return (torch.randn(rows, cols, generator=gen) * scale).to(dtype).to(device)
+
+
+@pytest.mark.parametrize("shape", ROW_SHAPES)
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_softmax_shapes(shape, dtype, device):
+    x = rand(*shape, dtype, device, scale=4.0)
+    gate(ref.softmax_ref(host(x)), softmax(x), dtype, context=f"{shape}")
+
+
+@pytest.mark.parametrize("shape", ROW_SHAPES)
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("eps", [1e-5, 1e-6])
+def test_rmsnorm_shapes(shape, dtype, eps, device):
+    x = rand(*shape, dtype, device)
+    gamma = (rand(1, shape[1], torch.float32, device, seed=1)[0] * 0.1 + 1).to(dtype)
+    gate(ref.rmsnorm_ref(host(x), host(gamma), eps), rmsnorm(x, gamma, eps=eps), dtype, context=f"{shape}")
+
+
+def test_softmax_logits_that_overflow_fp16(device):
+    x = torch.full((4, 512), 60.0, device=device, dtype=torch.float16)
+    x[:, 0] = 80.0
+    out = softmax(x)
+    assert torch.isfinite(out).all()
+    gate(ref.softmax_ref(host(x)), out, torch.float16)
+    assert torch.allclose(out.float().sum(-1), torch.ones(4, device=device), atol=1e-2)
+
+
+def test_softmax_constant_row_is_uniform(device):
+    out = softmax(torch.full((2, 128), -3.5, device=device))
+    assert torch.allclose(out, torch.full_like(out, 1 / 128), atol=1e-6)
+
+
+def test_rmsnorm_zero_row_is_finite(device):
+    out = rmsnorm(torch.zeros(4, 256, device=device, dtype=torch.float16),
+                  torch.ones(256, device=device, dtype=torch.float16))
+    assert torch.isfinite(out).all() and torch.count_nonzero(out) == 0
+
+
+def test_wide_fp16_rows_need_the_fp32_reduction(device):
+    x = rand(64, 8192, torch.float16, device)
+    gamma = (rand(1, 8192, torch.float32, device, seed=1)[0] * 0.1 + 1).half()
+    result = gate(ref.rmsnorm_ref(host(x), host(gamma)), rmsnorm(x, gamma), torch.float16)
+    naive_sum = x.pow(2).sum(-1, keepdim=True, dtype=torch.float16)
+    naive = (x * torch.rsqrt(naive_sum.float() / 8192 + 1e-5) * gamma).half()
+    from kernelo_b200.testing import verify
+
+    assert verify(torch.from_numpy(ref.rmsnorm_ref(host(x), host(gamma))), naive.cpu().double(),
+                  dtype=torch.float16).error > result.error
+
+
+@pytest.mark.parametrize("rows_per_program", [1, 2, 4, 8])
+@pytest.mark.parametrize("rows", [1, 3, 7, 17, 129])
+def test_rows_per_program_with_indivisible_rows(rows_per_program, rows, device):
+    x = rand(rows, 513, torch.float16, device)
+    gamma = torch.ones(513, device=device, dtype=torch.float16)
+    cfg = KernelConfig("rmsnorm", BLOCK_SIZE=1024, ROWS_PER_PROGRAM=rows_per_program, num_warps=2, CLUSTER=1)
+    gate(ref.rmsnorm_ref(host(x), host(gamma)), rmsnorm(x, gamma, config=cfg), torch.float16)
+    cfg = KernelConfig("softmax", BLOCK_SIZE=1024, ROWS_PER_PROGRAM=rows_per_program, num_warps=2, CLUSTER=2)
+    gate(ref.softmax_ref(host(x)), softmax(x, config=cfg), torch.float16)
+
+
+def test_every_candidate_agrees(device):
+    for space, fn, name in ((SoftmaxSearchSpace(), softmax, "softmax"), (RMSNormSearchSpace(), None, "rmsnorm")):
+        problem = Problem.create(name, "fp16", rows=333, cols=2048)
+        x = rand(333, 2048, torch.float16, device)
+        gamma = torch.ones(2048, device=device, dtype=torch.float16)
+        expected = ref.softmax_ref(host(x)) if name == "softmax" else ref.rmsnorm_ref(host(x), host(gamma))
+        for c in space.candidates(problem, device_caps(device)):
+            out = softmax(x, config=c) if name == "softmax" else rmsnorm(x, gamma, config=c)
+            gate(expected, out, torch.float16, context=repr(c))
+
+
+def test_row_strided_input(device):
+    base = rand(64, 1536, torch.bfloat16, device)
+    x = base[:, 256:1280]  # row stride 1536, last dim contiguous
+    gate(ref.softmax_ref(host(x)), softmax(x), torch.bfloat16)
+    gamma = torch.ones(1024, device=device, dtype=torch.bfloat16)
+    gate(ref.rmsnorm_ref(host(x), host(gamma)), rmsnorm(x, gamma), torch.bfloat16)
+
+
+def test_validation(device):
+    with pytest.raises(ValueError, match="2D"):
+        softmax(torch.zeros(2, 3, 4, device=device, dtype=torch.float16))
+    with pytest.raises(ValueError, match="contiguous"):
+        softmax(torch.zeros(8, 8, device=device).t())
+    with pytest.raises(ValueError, match="gamma must have shape"):
+        rmsnorm(torch.zeros(4, 128, device=device), torch.ones(64, device=device))
+    cfg = KernelConfig("rmsnorm", BLOCK_SIZE=256, ROWS_PER_PROGRAM=1, num_warps=4, CLUSTER=1)
+    with pytest.raises(ValueError, match="cannot hold a row"):
+        rmsnorm(torch.zeros(8, 1024, device=device), torch.ones(1024, device=device), config=cfg)
+    with pytest.raises(ValueError, match="single-pass limit"):
+        softmax(torch.zeros(1, 300_000, device=device, dtype=torch.float16))
+
+
+@pytest.mark.parametrize("name", [n for n in golden_names() if n.startswith(("softmax", "rmsnorm"))])
+def test_golden_row_fixtures(name, device):
+    g = load_golden(name)
+    meta = g["meta"]
+    dtype = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32}[meta["dtype"]]
+    ins = [torch.from_numpy(a).to(dtype).to(device) for a in g["inputs"]]
+    out = softmax(ins[0]) if meta["op"] == "softmax" else rmsnorm(*ins, eps=meta["eps"])
+    gate(g["ref_torch"], out, dtype, context=name)
+    if g["ref_kernel"] is not None:
+        gate(g["ref_kernel"], out, dtype, context=name + " vs reference kernel")
+
+
+# ---------------------------------------------------------------- baseline sizes
+@pytest.mark.parametrize("cols,dtype", [(1000, torch.float16), (4096, torch.bfloat16), (4097, torch.float16),
+                                        (32000, torch.float32)])
+def test_softmax_baseline_sizes(cols, dtype, device):
+    """[32768, C] with x ~ N(0, 4^2): sampled rows against the oracle, every row sums to 1."""
+    op = SoftmaxOperator()
+    problem = Problem.create("softmax", dtype, rows=32768, cols=cols)
+    (x,) = op.make_inputs(problem, device)
+    out = softmax(x)
+    rows = sample_rows(32768, 32)
+    gate(ref.softmax_ref(host(x[rows])), out[rows], dtype)
+    sums = out.float().sum(-1)
+    tol = {torch.float32: 1e-4, torch.bfloat16: 0.05, torch.float16: 0.01}[dtype]
+    assert float((sums - 1).abs().max()) < tol
+
+
+@pytest.mark.parametrize("cols", [4096, 8192])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_rmsnorm_baseline_sizes(cols, dtype, device):
+    op = RMSNormOperator(eps=1e-6)
+    problem = Problem.create("rmsnorm", dtype, rows=16384, cols=cols)
+    x, gamma = op.make_inputs(problem, device)
+    out = op.run(op.default_config(problem), x, gamma)
+    rows = sample_rows(16384, 32)
+    gate(ref.rmsnorm_ref(host(x[rows]), host(gamma), 1e-6), out[rows], dtype)
+    # Normalised rows have unit RMS before gamma: undo gamma and check.
+    rms = (out.float() / gamma.float()).pow(2).mean(-1).sqrt()
+    assert float((rms - 1).abs().max()) < (0.02 if dtype == torch.bfloat16 else 0.005)

@@ -1,0 +1,155 @@
+"""sm_100a search spaces: every filter rule named and checked against the
+configuration it exists to reject, on device capabilities passed in as values
+(no GPU needed). The reference's rules (tuning/search.py:259-503) are
+regenerated for Blackwell: tcgen05 tiles, TMEM columns, 227 KiB shared memory,
+TMA alignment, swizzle atoms and thread-block clusters.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from kernelo_b200.kernels import gemm_common as gc
+from kernelo_b200.tuning.config import KernelConfig, Problem
+from kernelo_b200.tuning.search import (
+    DEFAULT_MAX_CANDIDATES,
+    FusedLinearErfSearchSpace,
+    GemvSearchSpace,
+    MatmulSearchSpace,
+    RMSNormSearchSpace,
+    SoftmaxSearchSpace,
+    next_power_of_2,
+    search_space,
+)
+
+GEMM = Problem.create("matmul", "fp16", M=2048, N=4096, K=4096)
+FUSED = Problem.create("fused_linear_erf", "bf16", M=4096, N=11008, K=4096)
+
+
+def tc(op="matmul", **kw):
+    base = dict(KERNEL=1, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64, GROUP_M=8, num_stages=4, STREAM_K=0,
+                SWAP_AB=2, CLUSTER_M=1, CLUSTER_N=1)
+    base.update(kw)
+    return KernelConfig(op, **base)
+
+
+@pytest.mark.parametrize("n,expected", [(1, 1), (3, 4), (127, 128), (128, 128), (4097, 8192)])
+def test_next_power_of_2(n, expected):
+    assert next_power_of_2(n) == expected
+
+
+def test_grid_size_and_budget(b200_caps):
+    result = MatmulSearchSpace().generate(GEMM, b200_caps)
+    assert result.generated == 3 * 5 * 3 * 3 * 4 + 3  # tcgen05 grid + SIMT tiles
+    assert 0 < result.feasible < result.generated
+    assert len(result.candidates) <= DEFAULT_MAX_CANDIDATES
+    assert len(set(result.candidates)) == len(result.candidates)
+    assert MatmulSearchSpace().candidates(GEMM, b200_caps) == MatmulSearchSpace().candidates(GEMM, b200_caps)
+    assert len(MatmulSearchSpace().candidates(GEMM, b200_caps, max_candidates=5)) == 5
+
+
+def test_flagship_shape_prefers_big_tcgen05_tiles(b200_caps):
+    best = FusedLinearErfSearchSpace().candidates(FUSED, b200_caps)[0]
+    assert best["KERNEL"] == gc.KERNEL_TCGEN05 and best["BLOCK_N"] == 256 and best["BLOCK_M"] == 128
+
+
+@pytest.mark.parametrize(
+    "config,rule",
+    [
+        (tc(BLOCK_N=256, BLOCK_K=64, num_stages=6), "shared memory"),
+        (tc(BLOCK_K=32), "swizzle atom"),
+        (tc(BLOCK_M=256), "not implemented"),
+        (tc(CLUSTER_M=2), "not implemented"),
+        (tc(BLOCK_N=16), "MN-major B"),  # matmul's B is row-major (K, N)
+        (tc(BLOCK_N=256, num_stages=6, BLOCK_K=128), "shared memory"),
+    ],
+)
+def test_each_rule_rejects_its_config(config, rule, b200_caps):
+    reason = MatmulSearchSpace().reject_reason(config, GEMM, b200_caps)
+    assert reason is not None and reason.startswith(rule), reason
+
+
+def test_tmem_budget_is_a_device_property(b200_caps, a100_caps):
+    """A double-buffered 256-column accumulator fits B200's 512 TMEM columns;
+    a device without TMEM rejects every tcgen05 tile."""
+    space = FusedLinearErfSearchSpace()
+    assert space.reject_reason(tc("fused_linear_erf"), FUSED, b200_caps) is None
+    reason = space.reject_reason(tc("fused_linear_erf"), FUSED, a100_caps)
+    assert reason is not None and ("TMEM" in reason or "shared memory" in reason)
+
+
+def test_fp32_and_unaligned_shapes_fall_back_to_simt(b200_caps):
+    for problem in (
+        Problem.create("matmul", "fp32", M=4099, N=4099, K=4099),
+        Problem.create("matmul", "fp16", M=4099, N=4099, K=4099),
+        Problem.create("matmul", "bf16", M=1021, N=2053, K=509),
+    ):
+        cands = MatmulSearchSpace().candidates(problem, b200_caps)
+        assert cands and all(c["KERNEL"] == gc.KERNEL_SIMT for c in cands)
+        reasons = {r for _, r in MatmulSearchSpace().generate(problem, b200_caps).rejected}
+        assert any(r.startswith(("tcgen05 kind", "TMA alignment")) for r in reasons)
+
+
+@pytest.mark.parametrize("m", [1, 4, 16])
+def test_decode_shapes_swap_and_keep_the_smallest_tile(m, b200_caps):
+    problem = Problem.create("gemv", "fp16", M=m, N=11008, K=4096)
+    cands = GemvSearchSpace().candidates(problem, b200_caps)
+    tcs = [c for c in cands if c["KERNEL"] == gc.KERNEL_TCGEN05]
+    assert tcs and all(c["SWAP_AB"] == 1 and c["BLOCK_N"] == 16 for c in tcs)
+
+
+def test_pipeline_fill_rule(b200_caps):
+    shallow = Problem.create("matmul", "fp16", M=2048, N=2048, K=128)
+    reason = MatmulSearchSpace().reject_reason(tc(num_stages=4, BLOCK_N=128), shallow, b200_caps)
+    assert reason is not None and reason.startswith("pipeline cannot fill")
+
+
+def test_underutilisation_prune(b200_caps):
+    problem = Problem.create("matmul", "fp16", M=1024, N=4096, K=1024)
+    result = MatmulSearchSpace().generate(problem, b200_caps)
+    space = MatmulSearchSpace()
+    assert all(space.num_programs(c, problem) >= b200_caps.sm_count // 2 for c in result.candidates)
+    tiny = Problem.create("matmul", "fp16", M=64, N=64, K=256)
+    r = space.generate(tiny, b200_caps)
+    assert r.after_prune == r.feasible and r.candidates
+
+
+def test_explain_names_rules_and_device(b200_caps):
+    text = MatmulSearchSpace().explain(GEMM, b200_caps)
+    assert "NVIDIA B200" in text and "grid points" in text and "rejections by rule" in text
+
+
+def test_row_space_shape_and_rules(b200_caps):
+    problem = Problem.create("rmsnorm", "fp16", rows=16384, cols=4096)
+    cands = RMSNormSearchSpace().candidates(problem, b200_caps)
+    assert cands and {k for c in cands for k in c} == {"BLOCK_SIZE", "ROWS_PER_PROGRAM", "num_warps", "CLUSTER"}
+    assert {c["BLOCK_SIZE"] for c in cands} == {4096}
+    wide = Problem.create("softmax", "fp32", rows=32768, cols=32000)
+    space = SoftmaxSearchSpace()
+    one_cta = KernelConfig("softmax", BLOCK_SIZE=32768, ROWS_PER_PROGRAM=1, num_warps=4, CLUSTER=1)
+    assert space.reject_reason(one_cta, wide, b200_caps).startswith("register pressure")
+    assert any(c["CLUSTER"] > 1 for c in space.candidates(wide, b200_caps))
+    too_wide = Problem.create("softmax", "fp16", rows=2, cols=300_000)
+    assert all(r.startswith("row of") for _, r in space.generate(too_wide, b200_caps).rejected)
+
+
+def test_default_configs_are_feasible(b200_caps):
+    from kernelo_b200.kernels import get_operator
+
+    for op_name, problem in (
+        ("matmul", GEMM),
+        ("fused_linear_erf", FUSED),
+        ("gemv", Problem.create("gemv", "fp16", M=1, N=11008, K=4096)),
+        ("softmax", Problem.create("softmax", "fp32", rows=32768, cols=32000)),
+        ("rmsnorm", Problem.create("rmsnorm", "bf16", rows=16384, cols=8192)),
+    ):
+        op = get_operator(op_name)
+        cfg = op.default_config(problem)
+        assert op.search_space().reject_reason(cfg, problem, b200_caps) is None, (op_name, cfg)
+
+
+def test_unknown_space_is_an_error():
+    with pytest.raises(ValueError):
+        search_space("vector_add")
+    assert isinstance(search_space("gemv"), GemvSearchSpace)
