@@ -142,6 +142,25 @@ KF_API int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
                 int64_t N, int64_t K, const kf_gemm_config* cfg, void* workspace,
                 int64_t workspace_bytes, void* stream);
 
+/* kf_gemv for callers that cannot allocate device memory. No counterpart in
+ * the reference: it exists for callers such as a plugin inside a host
+ * application that owns all device memory and provides neither an allocator
+ * nor a workspace, or a latency-critical path that cannot pay for
+ * cudaMalloc/cudaFree (which may synchronise the device). Same arguments as
+ * kf_gemv minus the config and workspace: the stream-K scratch is a
+ * file-scope device array of KF_NOALLOC_SCRATCH_BYTES inside the library,
+ * present on every GPU that loads it until the process exits. Takes
+ * M <= KF_NOALLOC_MAX_ROWS and rejects larger M with KF_ERR_WORKSPACE. Calls
+ * no allocating routine. The first call on a device looks the array up
+ * (cudaGetSymbolAddress) and should come before any stream capture. Each call
+ * clears the array's counters on `stream`; all calls on a device share the
+ * array, so calls that overlap on the GPU race. */
+#define KF_NOALLOC_SCRATCH_BYTES (4 * 1024 * 1024)
+#define KF_NOALLOC_MAX_ROWS 16
+KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
+                               const void* w, int64_t sw_n, int64_t sw_k, void* y, int64_t sy_m,
+                               int64_t sy_n, int64_t M, int64_t N, int64_t K, void* stream);
+
 /* Workspace bytes a kf_gemm / kf_linear_bias_act (resp. kf_gemv) call with
  * these strides, sizes and config needs on `device` (0 when none; negative
  * status on error). Operand pointers are assumed 16-byte aligned. */

@@ -63,6 +63,7 @@ EXPORTED_SYMBOLS = (
     "kf_softmax_rows",
     "kf_rmsnorm_rows",
     "kf_selftest_bounded_wait",
+    "kf_gemv_noalloc",
 )
 
 
@@ -147,6 +148,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kf_softmax_rows": (_i32, [_i32, _vp, _i64, _vp, _i64, _i64, _i64, _RP, _vp]),
     "kf_rmsnorm_rows": (_i32, [_i32, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _f32, _RP, _vp]),
     "kf_selftest_bounded_wait": (_i32, [_i32, _vp]),
+    "kf_gemv_noalloc": (_i32, [_i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
+                               _vp]),
 }
 
 _lock = threading.Lock()
