@@ -6,24 +6,36 @@
 //   warp 0      TMA producer: 2-D tiled bulk loads of A and B k-blocks into a
 //               `stages`-deep ring of 128-byte-swizzled shared-memory tiles,
 //               completion tracked by full/empty mbarrier pairs.
-//   warp 1      allocates TMEM, then one lane issues tcgen05.mma (M=128, N=BN,
-//               K=16 per instruction) into a double-buffered fp32 accumulator
-//               in TMEM and releases ring slots with tcgen05.commit.
+//   warp 1      allocates TMEM, then one lane issues tcgen05.mma into a
+//               double-buffered fp32 accumulator in TMEM and releases ring
+//               slots with tcgen05.commit.
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (each warp owns one
 //               32-lane TMEM quadrant = 32 rows), add bias, apply GELU, round
 //               to the output dtype and store -- while the MMA warp already
 //               accumulates the next tile into the other TMEM buffer.
+//
+// Two tile shapes, chosen by the template parameter CG (CTAs per MMA):
+//   CG = 1   one SM computes a 128 x BN tile with M=128 MMAs.
+//   CG = 2   a thread-block cluster of two SMs computes a 256 x BN tile with
+//            the pair MMA (tcgen05.mma.cta_group::2, M=256): each CTA stages
+//            its own 128 rows of A and half (BN/2 rows) of B, so per SM the
+//            tensor core reads half the B bytes it would read for a 128 x BN
+//            tile -- the shared-memory bandwidth a 1-SM 128x256 tile runs out
+//            of. Both CTAs' TMA loads complete on the leader CTA's barrier,
+//            only the leader issues MMAs, and its commits arrive on both
+//            CTAs' barriers; each CTA's epilogue drains its own TMEM half.
 //
 // Operands may be K-major or MN-major in global memory (row-major (K,N) B,
 // nn.Linear's [N,K] weight and transposed views all map to a TMA tensor map
 // without a copy); the MMA reads either layout through its smem descriptors.
 //
 // Work is a list of segments (tile, k-block range). Data-parallel mode gives
-// every CTA whole tiles in a grouped (GROUP_M) raster. Stream-K mode splits the
-// flattened (tile, k-block) iteration space evenly over the grid; a tile split
-// between CTAs is finished by whichever contributor arrives last, which sums the
-// fp32 partials in a fixed order (so results are deterministic) and runs the
-// epilogue. Nobody waits for another CTA, so the scheme cannot deadlock.
+// every CTA (pair) whole tiles in a grouped (GROUP_M) raster. Stream-K mode
+// (CG = 1 only) splits the flattened (tile, k-block) iteration space evenly
+// over the grid; a tile split between CTAs is finished by whichever
+// contributor arrives last, which sums the fp32 partials in a fixed order (so
+// results are deterministic) and runs the epilogue. Nobody waits for another
+// CTA, so the scheme cannot deadlock.
 //
 // Reference: kernelforge/kernels/matmul.py:54-113 (blocked GEMM with grouped
 // ordering) and kernelforge/kernels/fused_linear.py:49-104 (bias + GELU in the
@@ -39,10 +51,14 @@
 namespace kf {
 namespace {
 
-constexpr int BM = 128;
-constexpr int NUM_THREADS = 192;
+constexpr int BM = 128;  // rows per CTA (the TMEM lane count)
+// Warp 0 TMA, warp 1 MMA, warps 2-9 epilogue: two epilogue warps per TMEM lane
+// quadrant, each draining half of the tile's columns, so the bias + GELU
+// epilogue keeps up with the pair MMA's mainloop.
 constexpr int EPI_WARP0 = 2;
-constexpr int NUM_EPI_THREADS = 128;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_EPI_THREADS = NUM_EPI_WARPS * 32;
+constexpr int NUM_THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
 constexpr int MAX_STAGES = 16;
 constexpr int MIN_SMEM_PER_CTA = 120 * 1024;  // > half an SM: one CTA per SM
 constexpr uint64_t DRAIN_LIMIT_NS = 100000000ull;
@@ -65,7 +81,7 @@ struct TcParams {
   int* counters;
   int* status;
   uint32_t idesc;
-  uint32_t a_stage_bytes, b_stage_bytes;
+  uint32_t a_stage_bytes, b_stage_bytes;  // per CTA
   uint32_t tmem_cols;
 };
 
@@ -78,20 +94,20 @@ struct Cursor {
   long long next, end, begin;
 };
 
-__device__ __forceinline__ void cursor_init(const TcParams& p, Cursor& c) {
+// `unit` is the CTA (CG = 1) or the CTA pair (CG = 2); `units` their number.
+__device__ __forceinline__ void cursor_init(const TcParams& p, Cursor& c, int unit, int units) {
   if (p.stream_k) {
-    const long long g = gridDim.x;
-    c.begin = (p.total_iters * blockIdx.x) / g;
-    c.end = (p.total_iters * (blockIdx.x + 1)) / g;
+    c.begin = (p.total_iters * unit) / units;
+    c.end = (p.total_iters * (unit + 1)) / units;
     c.next = c.begin;
   } else {
     c.begin = 0;
     c.end = static_cast<long long>(p.tiles_m) * p.tiles_n;
-    c.next = blockIdx.x;
+    c.next = unit;
   }
 }
 
-__device__ __forceinline__ bool cursor_next(const TcParams& p, Cursor& c, Segment& s) {
+__device__ __forceinline__ bool cursor_next(const TcParams& p, Cursor& c, Segment& s, int units) {
   if (c.next >= c.end) return false;
   if (p.stream_k) {
     const long long tile = c.next / p.kb_per_tile;
@@ -106,7 +122,7 @@ __device__ __forceinline__ bool cursor_next(const TcParams& p, Cursor& c, Segmen
     s.tile = static_cast<int>(c.next);
     s.kb0 = 0;
     s.kb1 = p.kb_per_tile;
-    c.next += gridDim.x;
+    c.next += units;
   }
   return true;
 }
@@ -134,20 +150,58 @@ __device__ __forceinline__ void epi_bar_sync() {
 }
 
 // Epilogue for 16 accumulator columns of one row: bias, activation, rounding, store.
+// Two fp32 values rounded to one packed pair of 16-bit values.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  uint32_t out;
+  if constexpr (DType<T>::code == KF_BF16) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    memcpy(&out, &v, 4);
+  } else {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    memcpy(&out, &v, 4);
+  }
+  return out;
+}
+
+// Bias for 16 consecutive columns starting at col0 (zero past N).
+template <typename T>
+__device__ __forceinline__ void load_bias16(const T* bias, int col0, int n, float (&b)[16]) {
+  if (col0 + 16 <= n && (reinterpret_cast<uintptr_t>(bias + col0) & 15u) == 0) {
+    const uint4* src = reinterpret_cast<const uint4*>(bias + col0);
+    const uint4 lo = __ldg(src), hi = __ldg(src + 1);
+    const T* e0 = reinterpret_cast<const T*>(&lo);
+    const T* e1 = reinterpret_cast<const T*>(&hi);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      b[j] = to_f32(e0[j]);
+      b[8 + j] = to_f32(e1[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) b[j] = col0 + j < n ? to_f32(__ldg(bias + col0 + j)) : 0.0f;
+  }
+}
+
 template <typename T, int EPI>
 __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0, const float* acc) {
   if (row >= p.M) return;
   float v[16];
   const T* bias = static_cast<const T*>(p.bias);
-  const float row_bias = (EPI != KF_EPI_NONE && p.bias_on_rows) ? to_f32(bias[row]) : 0.0f;
+  if constexpr (EPI != KF_EPI_NONE) {
+    float b[16];
+    if (p.bias_on_rows) {
+      const float rb = to_f32(bias[row]);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    float b = row_bias;
-    if (EPI != KF_EPI_NONE && !p.bias_on_rows) {
-      const int col = col0 + j;
-      b = col < p.N ? to_f32(bias[col]) : 0.0f;
+      for (int j = 0; j < 16; ++j) b[j] = rb;
+    } else {
+      load_bias16<T>(bias, col0, p.N, b);
     }
-    v[j] = apply_epilogue<EPI>(acc[j], b);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = apply_epilogue<EPI>(acc[j], b[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = acc[j];
   }
   T* out = static_cast<T*>(p.c) + static_cast<long long>(row) * p.sc_r +
            static_cast<long long>(col0) * p.sc_c;
@@ -156,12 +210,7 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0
   if (vec_ok) {
     uint32_t packed[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      T lo = from_f32<T>(v[2 * j]);
-      T hi = from_f32<T>(v[2 * j + 1]);
-      packed[j] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) |
-                  (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
-    }
+    for (int j = 0; j < 8; ++j) packed[j] = pack2<T>(v[2 * j], v[2 * j + 1]);
     uint4* dst = reinterpret_cast<uint4*>(out);
     dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
@@ -173,7 +222,7 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0
   }
 }
 
-template <typename T, int EPI>
+template <typename T, int EPI, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                    const __grid_constant__ CUtensorMap tm_b, const TcParams p) {
@@ -197,6 +246,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tfull0 = smem_u32(bars + 2 * S);
   const uint32_t tempty0 = smem_u32(bars + 2 * S + 2);
   const uint32_t drain_bar = smem_u32(bars + 2 * S + 4);
+  const uint32_t crank = CG == 2 ? cluster_ctarank() : 0u;
+  const bool leader = crank == 0;
+  const int unit = static_cast<int>(blockIdx.x) / CG;
+  const int units = static_cast<int>(gridDim.x) / CG;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -205,7 +258,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull0 + 8 * a, 1);
-      mbar_init(tempty0 + 8 * a, NUM_EPI_THREADS);
+      // one arrival per epilogue warp of every CTA of the MMA group
+      mbar_init(tempty0 + 8 * a, NUM_EPI_WARPS * CG);
     }
     mbar_init(drain_bar, 1);
     misc[1] = 0;
@@ -217,16 +271,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tm_b);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&misc[0]), p.tmem_cols);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(smem_u32(&misc[0]), p.tmem_cols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(&misc[0]), p.tmem_cols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) {
+    cluster_sync_all();  // the peer's TMA may target the leader's barriers from here on
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = misc[0];
 
   Cursor cur;
-  cursor_init(p, cur);
+  cursor_init(p, cur, unit, units);
   Segment seg;
 
   if (warp == 0) {
@@ -235,35 +298,55 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t stage = 0, phase = 0;
       long long issued = 0;
       bool ok = true;
-      const uint32_t tx_bytes = p.a_stage_bytes + p.b_stage_bytes;
-      while (ok && cursor_next(p, cur, seg)) {
+      const uint32_t tx_bytes = (p.a_stage_bytes + p.b_stage_bytes) * CG;
+      const int b_rows = p.bn / CG;  // B rows this CTA stages
+      while (ok && cursor_next(p, cur, seg, units)) {
         int m_blk, n_blk;
         tile_coords(p, seg.tile, m_blk, n_blk);
-        const int m0 = m_blk * BM;
-        const int n0 = n_blk * p.bn;
+        const int m0 = m_blk * (BM * CG) + BM * static_cast<int>(crank);
+        const int n0 = n_blk * p.bn + b_rows * static_cast<int>(crank);
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag, p.status, SITE_TMA_EMPTY)) {
             ok = false;
             break;
           }
           const uint32_t fb = full0 + 8 * stage;
-          mbar_arrive_expect_tx(fb, tx_bytes);
           const int k0 = kb * p.bk;
           const uint32_t a_dst = smem_u32(a_ring + static_cast<size_t>(stage) * p.a_stage_bytes);
           const uint32_t b_dst = smem_u32(b_ring + static_cast<size_t>(stage) * p.b_stage_bytes);
-          if (!p.a_mn) {
-            for (int j = 0; j < p.bk / 64; ++j)
-              tma_load_2d(a_dst + j * (BM * 128), &tm_a, fb, k0 + 64 * j, m0);
+          if constexpr (CG == 2) {
+            if (leader) mbar_arrive_expect_tx(fb, tx_bytes);
+            const uint32_t lb = mapa_shared(fb, 0);  // both CTAs count on the leader's barrier
+            if (!p.a_mn) {
+              for (int j = 0; j < p.bk / 64; ++j)
+                tma_load_2d_pair(a_dst + j * (BM * 128), &tm_a, lb, k0 + 64 * j, m0);
+            } else {
+              for (int i = 0; i < BM / 64; ++i)
+                tma_load_2d_pair(a_dst + i * (p.bk * 128), &tm_a, lb, m0 + 64 * i, k0);
+            }
+            if (!p.b_mn) {
+              for (int j = 0; j < p.bk / 64; ++j)
+                tma_load_2d_pair(b_dst + j * (b_rows * 128), &tm_b, lb, k0 + 64 * j, n0);
+            } else {
+              for (int i = 0; i < b_rows / 64; ++i)
+                tma_load_2d_pair(b_dst + i * (p.bk * 128), &tm_b, lb, n0 + 64 * i, k0);
+            }
           } else {
-            for (int i = 0; i < BM / 64; ++i)
-              tma_load_2d(a_dst + i * (p.bk * 128), &tm_a, fb, m0 + 64 * i, k0);
-          }
-          if (!p.b_mn) {
-            for (int j = 0; j < p.bk / 64; ++j)
-              tma_load_2d(b_dst + j * (p.bn * 128), &tm_b, fb, k0 + 64 * j, n0);
-          } else {
-            for (int i = 0; i < p.bn / 64; ++i)
-              tma_load_2d(b_dst + i * (p.bk * 128), &tm_b, fb, n0 + 64 * i, k0);
+            mbar_arrive_expect_tx(fb, tx_bytes);
+            if (!p.a_mn) {
+              for (int j = 0; j < p.bk / 64; ++j)
+                tma_load_2d(a_dst + j * (BM * 128), &tm_a, fb, k0 + 64 * j, m0);
+            } else {
+              for (int i = 0; i < BM / 64; ++i)
+                tma_load_2d(a_dst + i * (p.bk * 128), &tm_a, fb, m0 + 64 * i, k0);
+            }
+            if (!p.b_mn) {
+              for (int j = 0; j < p.bk / 64; ++j)
+                tma_load_2d(b_dst + j * (b_rows * 128), &tm_b, fb, k0 + 64 * j, n0);
+            } else {
+              for (int i = 0; i < b_rows / 64; ++i)
+                tma_load_2d(b_dst + i * (p.bk * 128), &tm_b, fb, n0 + 64 * i, k0);
+            }
           }
           ++issued;
           if (++stage == static_cast<uint32_t>(S)) {
@@ -272,9 +355,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
-      if (!ok) {
+      if (!ok && leader) {
         // Aborting: let every bulk copy already issued land before the CTA's
-        // shared memory goes away.
+        // shared memory goes away. (A pair's copies all count on the leader's
+        // barriers; the follower is held by the final cluster barrier.)
         for (int s = 0; s < S && s < issued; ++s) {
           const long long armed = (issued - s + S - 1) / S;
           mbar_wait(full0 + 8 * s, static_cast<uint32_t>((armed - 1) & 1), nullptr, p.status,
@@ -284,10 +368,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
-      while (ok && cursor_next(p, cur, seg)) {
+      const int b_rows = p.bn / CG;
+      // Start-address steps in 16-byte units. K-major operands: a K=16 slice is
+      // 32 bytes inside a 128-byte swizzle row, and the next 64-element K atom
+      // starts `rows * 128` bytes on. MN-major operands: a K=16 slice is 16
+      // K-rows of 128 bytes, and one 64-deep atom is 4 slices.
+      const uint32_t a_k_step = p.a_mn ? 2048 / 16 : 32 / 16;
+      const uint32_t b_k_step = p.b_mn ? 2048 / 16 : 32 / 16;
+      const uint32_t a_atom_step = p.a_mn ? 4 * 2048 / 16 : (BM * 128) / 16;
+      const uint32_t b_atom_step = p.b_mn ? 4 * 2048 / 16 : static_cast<uint32_t>(b_rows * 128) / 16;
+      const uint32_t a_lbo = p.a_mn ? static_cast<uint32_t>(p.bk * 128) : 16u;
+      const uint32_t b_lbo = p.b_mn ? static_cast<uint32_t>(p.bk * 128) : 16u;
+      while (ok && cursor_next(p, cur, seg, units)) {
         if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, abort_flag, p.status,
                        SITE_MMA_TMEM_EMPTY)) {
           break;
@@ -302,33 +397,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           const uint32_t a_base = smem_u32(a_ring + static_cast<size_t>(stage) * p.a_stage_bytes);
           const uint32_t b_base = smem_u32(b_ring + static_cast<size_t>(stage) * p.b_stage_bytes);
-          for (int kk = 0; kk < p.bk / 16; ++kk) {
-            // K-major: 64-element-wide swizzle atoms along K; K=16 is a 32-byte
-            // step inside the atom. MN-major: 16 K-rows of 128 bytes per step.
-            const uint64_t a_desc =
-                p.a_mn ? smem_desc_sw128(a_base + kk * 2048, p.bk * 128, 1024)
-                       : smem_desc_sw128(a_base + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-            const uint64_t b_desc =
-                p.b_mn ? smem_desc_sw128(b_base + kk * 2048, p.bk * 128, 1024)
-                       : smem_desc_sw128(b_base + (kk >> 2) * (p.bn * 128) + (kk & 3) * 32, 16,
-                                         1024);
-            tc_mma_f16(d_tmem, a_desc, b_desc, p.idesc, (kb > seg.kb0 || kk > 0) ? 1u : 0u);
+          const uint64_t a_desc0 = smem_desc_sw128(a_base, a_lbo, 1024);
+          const uint64_t b_desc0 = smem_desc_sw128(b_base, b_lbo, 1024);
+          // The descriptors of one k-block differ only in their start address
+          // (bits 0-13, 16-byte units): step by constants, issue unrolled.
+          for (int atom = 0; atom < p.bk / 64; ++atom) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(atom * a_atom_step + kk * a_k_step);
+              const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(atom * b_atom_step + kk * b_k_step);
+              const uint32_t accumulate = (kb > seg.kb0 || atom > 0 || kk > 0) ? 1u : 0u;
+              if constexpr (CG == 2) {
+                tc_mma_f16_pair(d_tmem, a_desc, b_desc, p.idesc, accumulate);
+              } else {
+                tc_mma_f16(d_tmem, a_desc, b_desc, p.idesc, accumulate);
+              }
+            }
           }
-          tc_commit(empty0 + 8 * stage);  // ring slot reusable once these MMAs finish
+          // ring slot reusable (in every CTA of the group) once these MMAs finish
+          if constexpr (CG == 2) {
+            tc_commit_pair_to(empty0 + 8 * stage, 0x3);
+          } else {
+            tc_commit(empty0 + 8 * stage);
+          }
           if (++stage == static_cast<uint32_t>(S)) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(tfull0 + 8 * acc);  // accumulator complete
+        // accumulator complete: wake the epilogue of every CTA of the group
+        if constexpr (CG == 2) {
+          tc_commit_pair_to(tfull0 + 8 * acc, 0x3);
+        } else {
+          tc_commit(tfull0 + 8 * acc);
+        }
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       // Every MMA issued must complete before TMEM is released.
-      tc_commit(drain_bar);
+      if constexpr (CG == 2) {
+        tc_commit_pair(drain_bar);
+      } else {
+        tc_commit(drain_bar);
+      }
       mbar_wait(drain_bar, 0, nullptr, p.status, SITE_DRAIN, DRAIN_LIMIT_NS);
     }
   } else {
@@ -336,36 +450,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quad = warp & 3;  // the TMEM lane quadrant this warp may read
     const int row_in_tile = quad * 32 + lane;
     const int ethread = threadIdx.x - EPI_WARP0 * 32;
+    // Two warps share each quadrant: the first takes the first half of the
+    // tile's 16-column chunks, the second the rest.
+    const int half = (warp - EPI_WARP0) / 4;
+    const int chunks = p.bn / 16;
+    const int chunk_split = (chunks + 1) / 2;
+    const int c_begin = half == 0 ? 0 : chunk_split * 16;
+    const int c_end = half == 0 ? chunk_split * 16 : p.bn;
+    // The MMA leader's tmem_empty barriers (this CTA's own when CG = 1).
+    const uint32_t tempty_leader = CG == 2 ? mapa_shared(tempty0, 0) : tempty0;
     uint32_t acc = 0, acc_phase = 0;
-    while (cursor_next(p, cur, seg)) {
+    while (cursor_next(p, cur, seg, units)) {
       if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, p.status, SITE_EPI_TMEM_FULL)) break;
       tc_fence_after();
       int m_blk, n_blk;
       tile_coords(p, seg.tile, m_blk, n_blk);
-      const int row = m_blk * BM + row_in_tile;
+      const int row = m_blk * (BM * CG) + BM * static_cast<int>(crank) + row_in_tile;
       const int col_base = n_blk * p.bn;
       const uint32_t t_acc =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * static_cast<uint32_t>(p.bn);
       const bool whole_tile = seg.kb0 == 0 && seg.kb1 == p.kb_per_tile;
       if (whole_tile) {
-        for (int c = 0; c < p.bn; c += 16) {
-          uint32_t r[16];
+        // Two 16-column TMEM loads in flight per wait.
+        for (int c = c_begin; c < c_end; c += 32) {
+          uint32_t r0[16], r1[16];
+          const bool two = c + 16 < c_end;
           __syncwarp();  // tcgen05.ld is .sync.aligned
-          tmem_ld_16(t_acc + c, r);
+          tmem_ld_16(t_acc + c, r0);
+          if (two) tmem_ld_16(t_acc + c + 16, r1);
           tmem_ld_wait();
-          store_chunk<T, EPI>(p, row, col_base + c, reinterpret_cast<const float*>(r));
+          store_chunk<T, EPI>(p, row, col_base + c, reinterpret_cast<const float*>(r0));
+          if (two) store_chunk<T, EPI>(p, row, col_base + c + 16, reinterpret_cast<const float*>(r1));
         }
       } else {
-        // Stream-K fix-up for a tile shared between CTAs.
-        const long long grid = gridDim.x;
+        // Stream-K fix-up for a tile shared between CTAs (CG = 1 only).
+        const long long grid = units;
         const long long t_start = static_cast<long long>(seg.tile) * p.kb_per_tile;
         const long long c_first = owner_of(t_start, p.total_iters, grid);
         const long long c_last = owner_of(t_start + p.kb_per_tile - 1, p.total_iters, grid);
-        const long long me = blockIdx.x;
+        const long long me = unit;
         const size_t slot_elems = static_cast<size_t>(p.bn) * BM;
         const long long my_slot = 2 * me + (cur.begin >= t_start ? 0 : 1);
         float* mine = p.partials + static_cast<size_t>(my_slot) * slot_elems;
-        for (int c = 0; c < p.bn; c += 16) {
+        for (int c = c_begin; c < c_end; c += 16) {
           uint32_t r[16];
           __syncwarp();
           tmem_ld_16(t_acc + c, r);
@@ -383,7 +510,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         epi_bar_sync();
         if (*last_flag) {
           __threadfence();
-          for (int c = 0; c < p.bn; c += 16) {
+          for (int c = c_begin; c < c_end; c += 16) {
             uint32_t r[16];
             __syncwarp();
             tmem_ld_16(t_acc + c, r);
@@ -411,7 +538,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         epi_bar_sync();
       }
       tc_fence_before();
-      mbar_arrive(tempty0 + 8 * acc);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CG == 2) {
+          mbar_arrive_cluster(tempty_leader + 8 * acc);
+        } else {
+          mbar_arrive(tempty0 + 8 * acc);
+        }
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -420,11 +554,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();  // lanes 1-31 of warps 0 and 1 arrive here before their lane 0
+  if constexpr (CG == 2) {
+    cluster_sync_all();  // both CTAs done: no MMA, TMEM read or remote arrive in flight
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     __syncwarp();  // tcgen05.dealloc is .sync.aligned: the whole warp, converged
     tc_fence_after();
-    tmem_dealloc(tmem_base, p.tmem_cols);
+    if constexpr (CG == 2) {
+      tmem_dealloc_pair(tmem_base, p.tmem_cols);
+    } else {
+      tmem_dealloc(tmem_base, p.tmem_cols);
+    }
   }
 }
 
@@ -437,8 +580,9 @@ uint32_t tmem_cols_for(int bn) {
   return cols;
 }
 
-int64_t smem_bytes_for(int bn, int bk, int stages) {
-  const int64_t ring = static_cast<int64_t>(stages) * (BM + bn) * bk * 2;
+// Shared memory of one CTA: A rows (128) and this CTA's B rows per stage.
+int64_t smem_bytes_for(int bn, int bk, int stages, int cg) {
+  const int64_t ring = static_cast<int64_t>(stages) * (BM + bn / cg) * bk * 2;
   return 1024 + ring + 8 * (2 * stages + 5) + 16;
 }
 
@@ -514,38 +658,44 @@ int operand_major(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int64_
 }
 
 template <typename T, int EPI>
-void* kernel_ptr() {
-  return reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI>);
+void* kernel_ptr(int cg) {
+  return cg == 2 ? reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI, 2>)
+                 : reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI, 1>);
 }
 
-void* pick_kernel(int dtype, int epi) {
+void* pick_kernel(int dtype, int epi, int cg) {
   if (dtype == KF_FP16) {
     switch (epi) {
-      case KF_EPI_NONE: return kernel_ptr<__half, KF_EPI_NONE>();
-      case KF_EPI_BIAS: return kernel_ptr<__half, KF_EPI_BIAS>();
-      case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__half, KF_EPI_BIAS_GELU_TANH>();
-      default: return kernel_ptr<__half, KF_EPI_BIAS_GELU_ERF>();
+      case KF_EPI_NONE: return kernel_ptr<__half, KF_EPI_NONE>(cg);
+      case KF_EPI_BIAS: return kernel_ptr<__half, KF_EPI_BIAS>(cg);
+      case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__half, KF_EPI_BIAS_GELU_TANH>(cg);
+      default: return kernel_ptr<__half, KF_EPI_BIAS_GELU_ERF>(cg);
     }
   }
   switch (epi) {
-    case KF_EPI_NONE: return kernel_ptr<__nv_bfloat16, KF_EPI_NONE>();
-    case KF_EPI_BIAS: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS>();
-    case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_TANH>();
-    default: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_ERF>();
+    case KF_EPI_NONE: return kernel_ptr<__nv_bfloat16, KF_EPI_NONE>(cg);
+    case KF_EPI_BIAS: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS>(cg);
+    case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_TANH>(cg);
+    default: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_ERF>(cg);
   }
 }
 
+int cta_group_of(const kf_gemm_config& cfg) { return cfg.block_m == 2 * BM ? 2 : 1; }
+
 int validate_config(const kf_gemm_config& cfg, int b_mn, std::string* why) {
-  if (cfg.block_m != BM) {
-    *why = "tcgen05 path supports BLOCK_M=128 (one-CTA MMA M); got " + std::to_string(cfg.block_m);
+  if (cfg.block_m != BM && cfg.block_m != 2 * BM) {
+    *why = "tcgen05 path supports BLOCK_M=128 (one SM) or 256 (an SM pair); got " +
+           std::to_string(cfg.block_m);
     return KF_ERR_INVALID_CONFIG;
   }
-  if (cfg.block_n < 16 || cfg.block_n > 256 || cfg.block_n % 16 != 0) {
-    *why = "BLOCK_N must be a multiple of 16 in [16, 256]; got " + std::to_string(cfg.block_n);
+  const int cg = cta_group_of(cfg);
+  if (cfg.block_n < 16 || cfg.block_n > 256 || cfg.block_n % (16 * cg) != 0) {
+    *why = "BLOCK_N must be a multiple of " + std::to_string(16 * cg) + " in [16, 256]; got " +
+           std::to_string(cfg.block_n);
     return KF_ERR_INVALID_CONFIG;
   }
-  if (b_mn == 1 && cfg.block_n % 64 != 0) {
-    *why = "an MN-major B operand needs BLOCK_N to be a multiple of 64";
+  if (b_mn == 1 && (cfg.block_n / cg) % 64 != 0) {
+    *why = "an MN-major B operand needs each CTA's BLOCK_N share to be a multiple of 64";
     return KF_ERR_INVALID_CONFIG;
   }
   if (cfg.block_k != 64 && cfg.block_k != 128) {
@@ -557,8 +707,12 @@ int validate_config(const kf_gemm_config& cfg, int b_mn, std::string* why) {
     *why = "stages must be in [2, 16]; got " + std::to_string(cfg.stages);
     return KF_ERR_INVALID_CONFIG;
   }
-  if (cfg.cluster_m > 1 || cfg.cluster_n > 1) {
-    *why = "thread-block clusters are not implemented by this build";
+  if (cfg.cluster_n > 1 || (cg == 1 && cfg.cluster_m > 1) || (cg == 2 && cfg.cluster_m > 2)) {
+    *why = "clusters beyond the SM pair of a BLOCK_M=256 tile are not implemented";
+    return KF_ERR_INVALID_CONFIG;
+  }
+  if (cg == 2 && cfg.stream_k == 1) {
+    *why = "stream-K is implemented for one-SM (BLOCK_M=128) tiles only";
     return KF_ERR_INVALID_CONFIG;
   }
   if (cfg.group_m < 1) {
@@ -593,7 +747,7 @@ int query_tcgen05_config(int dtype, const kf_gemm_config& cfg, int64_t* smem_byt
     return set_error(KF_ERR_INVALID_CONFIG, "tcgen05 path takes fp16/bf16 only");
   int rc = validate_config(cfg, 0, &why);
   if (rc != KF_OK) return set_error(rc, why);
-  const int64_t smem = smem_bytes_for(cfg.block_n, cfg.block_k, cfg.stages);
+  const int64_t smem = smem_bytes_for(cfg.block_n, cfg.block_k, cfg.stages, cta_group_of(cfg));
   if (smem_bytes) *smem_bytes = smem;
   if (tmem_cols) *tmem_cols = static_cast<int32_t>(tmem_cols_for(cfg.block_n));
   if (smem > 232448)
@@ -604,12 +758,8 @@ int query_tcgen05_config(int dtype, const kf_gemm_config& cfg, int64_t* smem_byt
 
 int64_t gemm_tcgen05_workspace_bytes(const GemmArgs& g, const kf_gemm_config& cfg,
                                      const DeviceInfo& dev) {
+  (void)g;
   if (cfg.stream_k != 1) return 0;
-  const bool swap = cfg.swap_ab == 1;
-  const int64_t m = swap ? g.N : g.M;
-  const int64_t n = swap ? g.M : g.N;
-  (void)m;
-  (void)n;
   const int grid = cfg.num_ctas > 0 ? cfg.num_ctas : dev.sm_count;
   return SK_COUNTER_BYTES + 2LL * grid * cfg.block_n * BM * 4;
 }
@@ -628,8 +778,10 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   if (v.M > INT32_MAX || v.N > INT32_MAX || g.K > INT32_MAX)
     return set_error(KF_ERR_UNSUPPORTED, "dimensions above 2^31 are not supported");
 
+  const int cg = cta_group_of(cfg);
   const int bn = cfg.block_n, bk = cfg.block_k, S = cfg.stages;
-  const int64_t smem = smem_bytes_for(bn, bk, S);
+  const int b_rows = bn / cg;
+  const int64_t smem = smem_bytes_for(bn, bk, S, cg);
   if (smem > dev.max_smem_optin)
     return set_error(KF_ERR_INVALID_CONFIG, "shared memory " + std::to_string(smem) +
                                                 " B exceeds the device limit of " +
@@ -640,7 +792,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   rc = a_major == 0 ? encode_map(&tm_a, g.dtype, v.a, g.K, v.M, v.sa_r, 64, BM)
                     : encode_map(&tm_a, g.dtype, v.a, v.M, g.K, v.sa_k, 64, bk);
   if (rc != KF_OK) return rc;
-  rc = b_major == 0 ? encode_map(&tm_b, g.dtype, v.b, g.K, v.N, v.sb_c, 64, bn)
+  rc = b_major == 0 ? encode_map(&tm_b, g.dtype, v.b, g.K, v.N, v.sb_c, 64, b_rows)
                     : encode_map(&tm_b, g.dtype, v.b, v.N, g.K, v.sb_k, 64, bk);
   if (rc != KF_OK) return rc;
 
@@ -654,7 +806,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   p.group_m = cfg.group_m;
   p.a_mn = a_major;
   p.b_mn = b_major;
-  p.tiles_m = static_cast<int>(ceil_div(v.M, BM));
+  p.tiles_m = static_cast<int>(ceil_div(v.M, BM * cg));
   p.tiles_n = static_cast<int>(ceil_div(v.N, bn));
   p.kb_per_tile = static_cast<int>(ceil_div(g.K, bk));
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
@@ -667,14 +819,42 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   p.bias_on_rows = v.bias_on_rows ? 1 : 0;
   p.status = dev.status;
   p.idesc = instr_desc_f16(g.dtype == KF_BF16 ? 1u : 0u, static_cast<uint32_t>(a_major),
-                           static_cast<uint32_t>(b_major), BM, static_cast<uint32_t>(bn));
+                           static_cast<uint32_t>(b_major), BM * cg, static_cast<uint32_t>(bn));
   p.a_stage_bytes = static_cast<uint32_t>(BM * bk * 2);
-  p.b_stage_bytes = static_cast<uint32_t>(bn * bk * 2);
+  p.b_stage_bytes = static_cast<uint32_t>(b_rows * bk * 2);
   p.tmem_cols = tmem_cols_for(bn);
 
-  int grid = cfg.num_ctas > 0 ? cfg.num_ctas : dev.sm_count;
+  void* fn = pick_kernel(g.dtype, g.epilogue, cg);
+  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem_request));
+  if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(tcgen05 gemm)");
+
+  cudaLaunchConfig_t lc{};
+  lc.blockDim = dim3(NUM_THREADS);
+  lc.dynamicSmemBytes = static_cast<size_t>(smem_request);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  lc.attrs = attr;
+  lc.numAttrs = 0;
+
+  int units = cfg.num_ctas > 0 ? cfg.num_ctas / cg : dev.sm_count / cg;
+  if (cg == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.numAttrs = 1;
+    if (cfg.num_ctas <= 0) {
+      // Persistent pairs: as many as can be resident at once (pairs must share a GPC).
+      lc.gridDim = dim3(static_cast<unsigned>(2 * units));
+      int clusters = 0;
+      err = cudaOccupancyMaxActiveClusters(&clusters, fn, &lc);
+      if (err != cudaSuccess) return cuda_error(err, "cudaOccupancyMaxActiveClusters");
+      if (clusters > 0 && clusters < units) units = clusters;
+    }
+  }
   if (p.stream_k) {
-    if (grid > p.total_iters) grid = static_cast<int>(p.total_iters);
+    if (units > p.total_iters) units = static_cast<int>(p.total_iters);
     const int64_t need = gemm_tcgen05_workspace_bytes(g, cfg, dev);
     if (g.workspace == nullptr || g.workspace_bytes < need)
       return set_error(KF_ERR_WORKSPACE, "stream-K needs " + std::to_string(need) +
@@ -690,17 +870,13 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
     p.counters = static_cast<int*>(g.workspace);
     p.partials = reinterpret_cast<float*>(static_cast<char*>(g.workspace) + SK_COUNTER_BYTES);
   } else {
-    if (grid > tiles) grid = static_cast<int>(tiles);
+    if (units > tiles) units = static_cast<int>(tiles);
   }
-  if (grid < 1) grid = 1;
+  if (units < 1) units = 1;
+  lc.gridDim = dim3(static_cast<unsigned>(units * cg));
 
-  void* fn = pick_kernel(g.dtype, g.epilogue);
-  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_request));
-  if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(tcgen05 gemm)");
   void* args[] = {&tm_a, &tm_b, &p};
-  err = cudaLaunchKernel(fn, dim3(grid), dim3(NUM_THREADS), args,
-                         static_cast<size_t>(smem_request), stream);
+  err = cudaLaunchKernelExC(&lc, fn, args);
   if (err != cudaSuccess) return cuda_error(err, "launch(tcgen05 gemm)");
   return KF_OK;
 }

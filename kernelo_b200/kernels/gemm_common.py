@@ -26,9 +26,19 @@ TC_BLOCK_M = 128
 TC_SMEM_OVERHEAD = 1024 + 8 * 37 + 16
 
 
-def tc_smem_bytes(block_n: int, block_k: int, stages: int, itemsize: int = 2) -> int:
-    """Shared memory of one tcgen05 CTA: the A/B ring plus barriers."""
-    return stages * (TC_BLOCK_M + block_n) * block_k * itemsize + 1024 + 8 * (2 * stages + 5) + 16
+def tc_smem_bytes(block_n: int, block_k: int, stages: int, itemsize: int = 2, cta_group: int = 1) -> int:
+    """Shared memory of one tcgen05 CTA: the A/B ring plus barriers.
+
+    Each CTA stages 128 rows of A and its share of B: all BLOCK_N rows for a
+    one-SM tile, half of them for a 256-row SM-pair tile.
+    """
+    ring = stages * (TC_BLOCK_M + block_n // cta_group) * block_k * itemsize
+    return ring + 1024 + 8 * (2 * stages + 5) + 16
+
+
+def cta_group(block_m: int) -> int:
+    """SMs per MMA: BLOCK_M=256 tiles run on an SM pair (tcgen05 cta_group::2)."""
+    return 2 if block_m == 2 * TC_BLOCK_M else 1
 
 
 def tc_tmem_columns(block_n: int) -> int:
@@ -88,28 +98,30 @@ def default_tcgen05_config(
     # B' (the kernel's second operand) is MN-major for matmul's row-major B
     # unless swapped (then B' is A, which is K-major).
     b_mn = (b_layout == "kn") and not swap
-    quantum = 64 if b_mn else 16
+    pair_tiles = -(-m_k // 256) * -(-n_k // 256)
+    cg = 2 if (m_k >= 256 and n_k >= 128 and pair_tiles >= sm_count // 2) else 1
+    quantum = (64 if b_mn else 16) * cg
     if n_k <= 256:
         block_n = max(quantum, -(-n_k // quantum) * quantum)
     else:
         block_n = 256
-    block_k = 64
-    per_stage = (TC_BLOCK_M + block_n) * block_k * 2
+    block_k = 128 if (cg == 2 and k >= 512) else 64
+    per_stage = (TC_BLOCK_M + block_n // cg) * block_k * 2
     stages = max(2, min(12, (SM100_SMEM_PER_BLOCK - 1024 - 256) // per_stage))
     tiles = -(-m_k // TC_BLOCK_M) * -(-n_k // block_n)
     k_blocks = -(-k // block_k)
-    stream_k = 1 if (tiles < sm_count and k_blocks >= 4) else 2
+    stream_k = 1 if (cg == 1 and tiles < sm_count and k_blocks >= 4) else 2
     return KernelConfig(
         operation,
         KERNEL=KERNEL_TCGEN05,
-        BLOCK_M=TC_BLOCK_M,
+        BLOCK_M=TC_BLOCK_M * cg,
         BLOCK_N=block_n,
         BLOCK_K=block_k,
         GROUP_M=8,
         num_stages=stages,
         STREAM_K=stream_k,
         SWAP_AB=1 if swap else 2,
-        CLUSTER_M=1,
+        CLUSTER_M=cg,
         CLUSTER_N=1,
     )
 

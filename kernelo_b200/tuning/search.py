@@ -232,11 +232,13 @@ class _Sm100GemmSpace(SearchSpace):
         if config["KERNEL"] == gc.KERNEL_SIMT:
             return 2 * config["BLOCK_K"] * (config["BLOCK_M"] + config["BLOCK_N"]) * 4
         return gc.tc_smem_bytes(config["BLOCK_N"], config["BLOCK_K"], config["num_stages"],
-                                itemsize(problem.dtype))
+                                itemsize(problem.dtype), gc.cta_group(config["BLOCK_M"]))
 
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
+        """CTAs with work: tiles, times two for SM-pair tiles."""
         m_k, n_k = self.kernel_view(config, problem)
-        return ceil_div(m_k, config["BLOCK_M"]) * ceil_div(n_k, config["BLOCK_N"])
+        tiles = ceil_div(m_k, config["BLOCK_M"]) * ceil_div(n_k, config["BLOCK_N"])
+        return tiles * (gc.cta_group(config["BLOCK_M"]) if config["KERNEL"] == gc.KERNEL_TCGEN05 else 1)
 
     def reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
         m, n, k = self.dims(problem)
@@ -246,10 +248,19 @@ class _Sm100GemmSpace(SearchSpace):
         if why is not None:
             return why
         bm, bn, bk, stages = config["BLOCK_M"], config["BLOCK_N"], config["BLOCK_K"], config["num_stages"]
-        if bm != gc.TC_BLOCK_M:
-            return f"not implemented: BLOCK_M={bm} (this build issues one-CTA M=128 MMAs)"
-        if (config["CLUSTER_M"], config["CLUSTER_N"]) != (1, 1):
-            return f"not implemented: thread-block cluster {config['CLUSTER_M']}x{config['CLUSTER_N']}"
+        cluster = (config["CLUSTER_M"], config["CLUSTER_N"])
+        if bm == 64:
+            return "not implemented: BLOCK_M=64 (M=64 MMAs use a different TMEM layout)"
+        cg = gc.cta_group(bm)
+        if cg == 2 and cluster != (2, 1):
+            if cluster == (1, 1):
+                return "SM pair: BLOCK_M=256 runs on a 2x1 cluster (CLUSTER_M=2)"
+            return f"not implemented: cluster {cluster[0]}x{cluster[1]} beyond the SM pair"
+        if cg == 1 and cluster != (1, 1):
+            return (f"not implemented: cluster {cluster[0]}x{cluster[1]} without the pair MMA "
+                    "(sharing tiles would need TMA multicast)")
+        if bn % (16 * cg) != 0:
+            return f"SM pair: BLOCK_N={bn} does not split into two 16-column halves"
         if bk * itemsize(problem.dtype) < 128:
             return f"swizzle atom: BLOCK_K={bk} is less than one 128-byte swizzle row"
         smem = self.shared_memory_bytes(config, problem)
@@ -262,12 +273,14 @@ class _Sm100GemmSpace(SearchSpace):
         if tmem > caps.tmem_columns_per_sm:
             return f"TMEM: {tmem} accumulator columns exceed {caps.tmem_columns_per_sm} per SM"
         swapped = config["SWAP_AB"] == 1
-        if self.b_layout == "kn" and not swapped and bn % 64 != 0:
-            return f"MN-major B: BLOCK_N={bn} is not a multiple of 64-column TMA boxes"
+        if self.b_layout == "kn" and not swapped and (bn // cg) % 64 != 0:
+            return f"MN-major B: BLOCK_N={bn} gives each CTA a share that is not 64-column TMA boxes"
         m_k, n_k = self.kernel_view(config, problem)
         smallest = min(v for v in self.BLOCK_N if self.b_layout != "kn" or swapped or v % 64 == 0)
         if bn > 2 * n_k and bn > smallest:
             return f"tile overshoot: BLOCK_N={bn} for N={n_k}"
+        if cg == 2 and m_k <= gc.TC_BLOCK_M:
+            return f"tile overshoot: BLOCK_M={bm} for M={m_k}"
         k_iters = ceil_div(k, bk)
         if stages > 2 and k_iters < stages:
             return f"pipeline cannot fill: {k_iters} K iterations for num_stages={stages}"

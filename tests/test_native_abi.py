@@ -63,7 +63,10 @@ def test_library_is_built_for_sm100a_only():
         (dict(kernel=1, block_m=128, block_n=256, block_k=64, stages=4), True),
         (dict(kernel=1, block_m=128, block_n=16, block_k=128, stages=6), True),
         (dict(kernel=1, block_m=128, block_n=256, block_k=64, stages=6), False),  # smem
-        (dict(kernel=1, block_m=256, block_n=256, block_k=64, stages=2), False),  # not built
+        (dict(kernel=1, block_m=256, block_n=256, block_k=64, stages=6, cluster_m=2), True),  # SM pair
+        (dict(kernel=1, block_m=256, block_n=256, block_k=64, stages=8, cluster_m=2), False),  # smem
+        (dict(kernel=1, block_m=256, block_n=48, block_k=64, stages=2, cluster_m=2), False),  # halves
+        (dict(kernel=1, block_m=64, block_n=64, block_k=64, stages=2), False),    # not built
         (dict(kernel=1, block_m=128, block_n=24, block_k=64, stages=2), False),   # N % 16
         (dict(kernel=1, block_m=128, block_n=64, block_k=32, stages=2), False),   # half atom
         (dict(kernel=1, block_m=128, block_n=64, block_k=64, stages=2, cluster_m=2), False),
@@ -75,7 +78,8 @@ def test_query_gemm_config_without_a_gpu(cfg, ok):
     if ok:
         from kernelo_b200.kernels import gemm_common as gc
 
-        assert smem == gc.tc_smem_bytes(cfg["block_n"], cfg["block_k"], cfg["stages"])
+        assert smem == gc.tc_smem_bytes(cfg["block_n"], cfg["block_k"], cfg["stages"],
+                                        cta_group=gc.cta_group(cfg["block_m"]))
         assert tmem == gc.tc_tmem_columns(cfg["block_n"])
     else:
         assert message

@@ -49,9 +49,19 @@ def test_grid_size_and_budget(b200_caps):
     assert len(MatmulSearchSpace().candidates(GEMM, b200_caps, max_candidates=5)) == 5
 
 
-def test_flagship_shape_prefers_big_tcgen05_tiles(b200_caps):
+def test_flagship_shape_prefers_sm_pair_tiles(b200_caps):
     best = FusedLinearErfSearchSpace().candidates(FUSED, b200_caps)[0]
-    assert best["KERNEL"] == gc.KERNEL_TCGEN05 and best["BLOCK_N"] == 256 and best["BLOCK_M"] == 128
+    assert best["KERNEL"] == gc.KERNEL_TCGEN05 and best["BLOCK_N"] == 256 and best["BLOCK_M"] == 256
+    assert (best["CLUSTER_M"], best["CLUSTER_N"]) == (2, 1)
+
+
+def test_sm_pair_tiles_are_feasible_and_sized_per_cta(b200_caps):
+    space = MatmulSearchSpace()
+    pair = tc(BLOCK_M=256, CLUSTER_M=2, BLOCK_N=256, num_stages=6)
+    assert space.reject_reason(pair, GEMM, b200_caps) is None
+    # each CTA stages 128 rows of A and half of B: 6 x (128 + 128) x 64 x 2 bytes
+    assert space.shared_memory_bytes(pair, GEMM) == 6 * 256 * 64 * 2 + 1024 + 8 * 17 + 16
+    assert space.num_programs(pair, GEMM) == 2 * (2048 // 256) * (4096 // 256)
 
 
 @pytest.mark.parametrize(
@@ -59,8 +69,11 @@ def test_flagship_shape_prefers_big_tcgen05_tiles(b200_caps):
     [
         (tc(BLOCK_N=256, BLOCK_K=64, num_stages=6), "shared memory"),
         (tc(BLOCK_K=32), "swizzle atom"),
-        (tc(BLOCK_M=256), "not implemented"),
+        (tc(BLOCK_M=256), "SM pair"),
+        (tc(BLOCK_M=64), "not implemented"),
         (tc(CLUSTER_M=2), "not implemented"),
+        (tc(BLOCK_M=256, CLUSTER_M=2, CLUSTER_N=2), "not implemented"),
+        (tc(BLOCK_M=256, CLUSTER_M=2, BLOCK_N=192), "MN-major B"),
         (tc(BLOCK_N=16), "MN-major B"),  # matmul's B is row-major (K, N)
         (tc(BLOCK_N=256, num_stages=6, BLOCK_K=128), "shared memory"),
     ],
