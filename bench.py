@@ -194,7 +194,7 @@ def cpu_baseline(rows: int = 512, budget_s: float = 10.0) -> dict:
 
 
 # ------------------------------------------------------------------ secondary rows
-def secondary_lines(pk: dict, flush: torch.Tensor) -> list[dict]:
+def secondary_lines(pk: dict, flush) -> list[dict]:
     """Memory-bound rows at their baseline sizes, N=1: GB/s and fraction of HBM peak."""
     from kernelo_b200.benchmark.metrics import gemv_bytes, rmsnorm_bytes, softmax_bytes
     from kernelo_b200.kernels.gemv import gemv
@@ -210,7 +210,7 @@ def secondary_lines(pk: dict, flush: torch.Tensor) -> list[dict]:
         torch.cuda.synchronize()
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
         for s, e in ev:
-            flush.zero_()
+            flush()
             s.record()
             fn()
             e.record()
@@ -378,7 +378,9 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     secondary = []
     baseline = None
     if rank == 0 and world == 1 and not args.no_secondary:
-        flush = torch.empty(256 * 1024 * 1024, dtype=torch.int8, device=dev)
+        from kernelo_b200.benchmark.runner import L2Flush
+
+        flush = L2Flush(dev)
         secondary = secondary_lines(pk, flush)
         del flush
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

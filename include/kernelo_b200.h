@@ -76,8 +76,10 @@ enum kf_gemm_kernel {
  * meaning. Zero in any field selects the library default. */
 typedef struct kf_gemm_config {
   int32_t kernel;    /* enum kf_gemm_kernel                                         */
-  int32_t block_m;   /* tcgen05: 128 (MMA M); SIMT: 64 or 128                        */
-  int32_t block_n;   /* tcgen05: multiple of 16 in [16,256]; SIMT: 64 or 128         */
+  int32_t block_m;   /* tcgen05: 128 (one SM) or 256 (an SM pair, cta_group::2);
+                        SIMT: 64 or 128                                              */
+  int32_t block_n;   /* tcgen05: multiple of 16 (32 for pairs) in [16,256];
+                        SIMT: 64 or 128                                              */
   int32_t block_k;   /* tcgen05: 64 or 128; SIMT: 8 or 16                            */
   int32_t stages;    /* tcgen05 shared-memory ring depth                             */
   int32_t group_m;   /* grouped (L2-aware) raster width, in M tiles                  */
@@ -85,7 +87,7 @@ typedef struct kf_gemm_config {
                         grid (stream-K), 2 = whole tiles only                          */
   int32_t swap_ab;   /* tcgen05: 0 = library choice, 1 = compute C^T = B^T.A^T
                         (skinny M), 2 = never swap                                     */
-  int32_t cluster_m; /* reserved, must be 0 or 1                                     */
+  int32_t cluster_m; /* 1, or 2 with block_m 256 (the SM pair is a 2x1 cluster)      */
   int32_t cluster_n; /* reserved, must be 0 or 1                                     */
   int32_t num_ctas;  /* persistent grid size; 0 = one CTA per SM                     */
   int32_t reserved[5];
@@ -94,11 +96,22 @@ typedef struct kf_gemm_config {
 /* Row-kernel parameters (softmax / RMSNorm). Replaces BLOCK_SIZE /
  * ROWS_PER_PROGRAM / num_warps (kernels/softmax.py:61-67). */
 typedef struct kf_rows_config {
-  int32_t num_warps;        /* warps per CTA, 1..32                                   */
-  int32_t rows_per_cta;     /* rows handled by one CTA (or cluster), in sequence      */
-  int32_t cluster;          /* CTAs sharing one row through distributed shared memory */
-  int32_t reserved[5];
+  int32_t num_warps;        /* warps per row: per CTA (register kernel, 1..32) or per
+                               row group (streaming kernel, 1..16)                   */
+  int32_t rows_per_cta;     /* register kernel: rows one CTA (or cluster) handles     */
+  int32_t cluster;          /* register kernel: CTAs sharing one row through DSMEM    */
+  int32_t kernel;           /* KF_ROWS_AUTO, KF_ROWS_REGISTER or KF_ROWS_STREAM       */
+  int32_t row_groups;       /* streaming kernel: row groups per CTA (0 = 16 / num_warps) */
+  int32_t stages;           /* streaming kernel: shared-memory row slots per row group
+                               (0 = as many as fit, at most 8)                        */
+  int32_t reserved[2];
 } kf_rows_config;
+
+/* Row kernels. REGISTER: one row per CTA (or per cluster of up to 8 CTAs for
+ * wide rows), loaded straight into registers. STREAM: persistent CTAs (one or
+ * two per SM) of row groups; each group keeps its next rows in flight as bulk
+ * copies into shared-memory slots while it reduces and writes earlier ones. */
+enum kf_rows_kernel { KF_ROWS_AUTO = 0, KF_ROWS_REGISTER = 1, KF_ROWS_STREAM = 2 };
 
 /* ---- library information -------------------------------------------------- */
 KF_API int32_t kf_abi_version(void);

@@ -355,7 +355,7 @@ int32_t kf_softmax_rows(int32_t dtype, const void* x, int64_t sx_row, void* y, i
   a.sy = sy_row;
   a.rows = rows;
   a.cols = cols;
-  const kf_rows_config c = resolve_rows_config(a, cfg);
+  const kf_rows_config c = resolve_rows_config(a, cfg, *dev);
   return launch_rows(a, c, *dev, static_cast<cudaStream_t>(stream));
 }
 
@@ -384,7 +384,7 @@ int32_t kf_rmsnorm_rows(int32_t dtype, const void* x, int64_t sx_row, const void
   a.rows = rows;
   a.cols = cols;
   a.eps = eps;
-  const kf_rows_config c = resolve_rows_config(a, cfg);
+  const kf_rows_config c = resolve_rows_config(a, cfg, *dev);
   return launch_rows(a, c, *dev, static_cast<cudaStream_t>(stream));
 }
 

@@ -71,9 +71,17 @@ struct RowsArgs {
   int64_t rows = 0, cols = 0;
   float eps = 0.0f;
 };
-kf_rows_config resolve_rows_config(const RowsArgs& args, const kf_rows_config* user);
+// Fills zero fields of `cfg`: kernel choice (streaming for many rows whose
+// x/y phases allow it), then that kernel's warps / cluster.
+kf_rows_config resolve_rows_config(const RowsArgs& args, const kf_rows_config* user,
+                                   const DeviceInfo& dev);
 int launch_rows(const RowsArgs& args, const kf_rows_config& cfg, const DeviceInfo& dev,
                 cudaStream_t stream);
+// Streaming kernel (rows_stream.cu).
+bool rows_stream_supported(const RowsArgs& args, int max_smem_optin, std::string* why);
+int stream_default_warps(int64_t cols, int elem);
+int launch_rows_stream(const RowsArgs& args, const kf_rows_config& cfg, const DeviceInfo& dev,
+                       cudaStream_t stream);
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 

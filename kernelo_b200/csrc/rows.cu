@@ -10,8 +10,10 @@
 //
 // Rows whose start is not 16-byte aligned (e.g. 4097 fp16 columns) are split
 // into a scalar head, a vector body and a scalar tail, so every access stays
-// inside the row. Softmax reduces (max, sum of exp) pairs in one pass with the
-// online rescaling rule sum = sum_a * exp(max_a - max) + sum_b * exp(max_b - max).
+// inside the row. Softmax reduces (max, sum of exp) pairs in one pass: each
+// thread sums exp(x - m_thread); a warp takes the maximum M first and rescales
+// each lane's sum by exp(m_lane - M); warps and cluster CTAs combine the same
+// way. The per-element arithmetic lives in rows_math.cuh.
 //
 // Reference semantics: kernelforge/kernels/softmax.py:31-58 (max-shifted exp,
 // fp32 math, output rounded once) and kernelforge/kernels/rmsnorm.py:41-72,
@@ -21,6 +23,7 @@
 
 #include "kf_common.cuh"
 #include "kf_internal.h"
+#include "rows_math.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -29,8 +32,6 @@ namespace {
 
 constexpr int OP_SOFTMAX = 0;
 constexpr int OP_RMSNORM = 1;
-// log2(e): exp(x) = 2^(x log2 e), so exponentials go through CUDA's exp2f.
-constexpr float kLog2e = 1.4426950408889634f;
 
 struct RowsParams {
   const void* x;
@@ -90,16 +91,32 @@ constexpr int max_threads_for() {
   return NV <= 4 ? 1024 : (NV <= 8 ? 512 : 256);
 }
 
-struct MaxSum {
-  float m, s;
-};
+template <typename T, int VE>
+__device__ __forceinline__ uint4 as_u4(const Vec<T, VE>& v) {
+  static_assert(sizeof(Vec<T, VE>) == 16, "16-byte vectors only");
+  return *reinterpret_cast<const uint4*>(&v);
+}
 
-__device__ __forceinline__ MaxSum combine(MaxSum a, MaxSum b) {
-  const float m = fmaxf(a.m, b.m);
-  // An empty partial has m = -inf and s = 0; the guards keep -inf - -inf out.
-  const float sa = a.m == m ? a.s : a.s * expf(a.m - m);
-  const float sb = b.m == m ? b.s : b.s * expf(b.m - m);
-  return {m, sa + sb};
+// The VE elements of one loaded vector as fp32.
+template <typename T, int VE>
+__device__ __forceinline__ void vec_floats(const Vec<T, VE>& v, float* f) {
+  if constexpr (VE > 1) {
+    to_floats<T>(as_u4(v), f);
+  } else {
+    f[0] = to_f32(v.e[0]);
+  }
+}
+
+template <typename T, int VE>
+__device__ __forceinline__ Vec<T, VE> vec_from_floats(const float* f) {
+  Vec<T, VE> o;
+  if constexpr (VE > 1) {
+    const uint4 u = from_floats<T>(f);
+    memcpy(&o, &u, 16);
+  } else {
+    o.e[0] = from_f32<T>(f[0]);
+  }
+  return o;
 }
 
 template <typename T, int VE, int NV, int OP>
@@ -115,6 +132,9 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
   const int nwarps = (nthreads + 31) >> 5;
   const int g = static_cast<int>(crank) * nthreads + tid;  // thread index within the row
   const int G = static_cast<int>(csize) * nthreads;        // threads per row
+  // Softmax keeps exp(x - m_thread) in registers when that fits; wider rows
+  // evaluate it again in the output pass (same value either way).
+  constexpr bool KEEP_EV = OP == OP_SOFTMAX && NV * VE <= 32;
 
   __shared__ float2 warp_part[2][32];
   __shared__ float2 cta_part[2];  // read by the other CTAs of the cluster
@@ -130,7 +150,7 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
 
     int head = 0;
     if (VE > 1) {
-      const uintptr_t addr = reinterpret_cast<uintptr_t>(xr);
+      const uint32_t addr = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(xr));
       head = static_cast<int>(((16u - (addr & 15u)) & 15u) / sizeof(T));
       if (head > p.cols) head = p.cols;
     }
@@ -151,119 +171,106 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
     const float xh = has_head ? to_f32(xr[g]) : 0.0f;
     const float xt = has_tail ? to_f32(xr[tail_idx]) : 0.0f;
 
-    // ---- per-thread partial statistic
+    // ---- per-thread partial, reduced over the warp
     float2 part;
-    float ev[OP == OP_SOFTMAX ? NV * VE : 1];  // softmax: exp(x - m_local) per element
-    float eh = 0.0f, et = 0.0f, m_local = 0.0f;
+    float ev[KEEP_EV ? NV * VE : 1];
+    float eh = 0.0f, et = 0.0f, m_thr = -INFINITY;
     if constexpr (OP == OP_SOFTMAX) {
-      float m = -INFINITY;
+      if constexpr (VE > 1) {
+        uint4 mv = RowVec<T>::lowest();
 #pragma unroll
-      for (int j = 0; j < NV; ++j) {
-        if (g + j * G < nvec) {
+        for (int j = 0; j < NV; ++j)
+          if (g + j * G < nvec) mv = vmax<T>(mv, as_u4(raw[j]));
+        m_thr = hmax<T>(mv);
+      } else {
 #pragma unroll
-          for (int e = 0; e < VE; ++e) m = fmaxf(m, to_f32(raw[j].e[e]));
-        }
+        for (int j = 0; j < NV; ++j)
+          if (g + j * G < nvec) m_thr = fmaxf(m_thr, to_f32(raw[j].e[0]));
       }
-      if (has_head) m = fmaxf(m, xh);
-      if (has_tail) m = fmaxf(m, xt);
-      // One exponential per element, relative to this thread's own maximum;
-      // the values stay in registers and are rescaled by exp(m - M) / S once
-      // the row's maximum M and sum S are known.
+      if (has_head) m_thr = fmaxf(m_thr, xh);
+      if (has_tail) m_thr = fmaxf(m_thr, xt);
       float s = 0.0f;
-      if (m != -INFINITY) {
+      if (m_thr != -INFINITY) {
+        const float mb = m_thr * kRowLog2e;
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
           if (g + j * G < nvec) {
+            float f[VE];
+            vec_floats(raw[j], f);
 #pragma unroll
             for (int e = 0; e < VE; ++e) {
-              const float t = exp2f((to_f32(raw[j].e[e]) - m) * kLog2e);
-              ev[j * VE + e] = t;
+              const float t = ex2_approx(fmaf(f[e], kRowLog2e, -mb));
+              if constexpr (KEEP_EV) ev[j * VE + e] = t;
               s += t;
             }
           }
         }
-        if (has_head) {
-          eh = exp2f((xh - m) * kLog2e);
-          s += eh;
-        }
-        if (has_tail) {
-          et = exp2f((xt - m) * kLog2e);
-          s += et;
-        }
+        if (has_head) s += (eh = ex2_approx(fmaf(xh, kRowLog2e, -mb)));
+        if (has_tail) s += (et = ex2_approx(fmaf(xt, kRowLog2e, -mb)));
       }
-      m_local = m;
-      part = make_float2(m, s);
+      part = warp_max_sum(m_thr, s);
     } else {
       float ss = 0.0f;
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
         if (g + j * G < nvec) {
+          float f[VE];
+          vec_floats(raw[j], f);
 #pragma unroll
-          for (int e = 0; e < VE; ++e) {
-            const float f = to_f32(raw[j].e[e]);
-            ss = fmaf(f, f, ss);
-          }
+          for (int e = 0; e < VE; ++e) ss = fmaf(f[e], f[e], ss);
         }
       }
       if (has_head) ss = fmaf(xh, xh, ss);
       if (has_tail) ss = fmaf(xt, xt, ss);
-      part = make_float2(ss, 0.0f);
+      part = make_float2(warp_sum(ss), 0.0f);
     }
 
-    // ---- reduce: warp -> CTA -> cluster
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float a = __shfl_xor_sync(0xffffffffu, part.x, off);
-      const float b = __shfl_xor_sync(0xffffffffu, part.y, off);
+    // ---- across warps, then across the cluster: lane-parallel combines
+    float2 tot = part;
+    if (nwarps > 1) {
+      if (lane == 0) warp_part[par][warp] = part;
+      __syncthreads();
+      const float2 o = lane < nwarps ? warp_part[par][lane] : make_float2(-INFINITY, 0.0f);
       if constexpr (OP == OP_SOFTMAX) {
-        const MaxSum r = combine({part.x, part.y}, {a, b});
-        part = make_float2(r.m, r.s);
+        tot = warp_max_sum(o.x, o.y);
       } else {
-        part.x += a;
-      }
-    }
-    if (lane == 0) warp_part[par][warp] = part;
-    __syncthreads();
-    float2 tot = warp_part[par][0];
-    for (int w = 1; w < nwarps; ++w) {
-      const float2 o = warp_part[par][w];
-      if constexpr (OP == OP_SOFTMAX) {
-        const MaxSum r = combine({tot.x, tot.y}, {o.x, o.y});
-        tot = make_float2(r.m, r.s);
-      } else {
-        tot.x += o.x;
+        tot = make_float2(warp_sum(lane < nwarps ? o.x : 0.0f), 0.0f);
       }
     }
     if (csize > 1) {
       if (tid == 0) cta_part[par] = tot;
       cluster.sync();
-      float2 all = *cluster.map_shared_rank(&cta_part[par], 0);
-      for (unsigned r = 1; r < csize; ++r) {
-        const float2 o = *cluster.map_shared_rank(&cta_part[par], r);
-        if constexpr (OP == OP_SOFTMAX) {
-          const MaxSum c = combine({all.x, all.y}, {o.x, o.y});
-          all = make_float2(c.m, c.s);
-        } else {
-          all.x += o.x;
-        }
+      const float2 o = lane < static_cast<int>(csize)
+                           ? *cluster.map_shared_rank(&cta_part[par], static_cast<unsigned>(lane))
+                           : make_float2(-INFINITY, 0.0f);
+      if constexpr (OP == OP_SOFTMAX) {
+        tot = warp_max_sum(o.x, o.y);
+      } else {
+        tot = make_float2(warp_sum(lane < static_cast<int>(csize) ? o.x : 0.0f), 0.0f);
       }
-      tot = all;
     }
 
     // ---- normalise and store
     V* yv = reinterpret_cast<V*>(yr + head);
     if constexpr (OP == OP_SOFTMAX) {
-      // exp(x - M) / S = exp(x - m_local) * (exp(m_local - M) / S)
+      // exp(x - M) / S = exp(x - m_thr) * (exp(m_thr - M) / S)
       const float factor =
-          m_local == -INFINITY ? 0.0f : exp2f((m_local - tot.x) * kLog2e) / tot.y;
+          m_thr == -INFINITY ? 0.0f : ex2_approx((m_thr - tot.x) * kRowLog2e) / tot.y;
+      const float mb = m_thr * kRowLog2e;
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
         const int v = g + j * G;
         if (v < nvec) {
-          V o;
+          float o[VE];
+          if constexpr (KEEP_EV) {
 #pragma unroll
-          for (int e = 0; e < VE; ++e) o.e[e] = from_f32<T>(ev[j * VE + e] * factor);
-          store_stream(yv + v, o);
+            for (int e = 0; e < VE; ++e) o[e] = ev[j * VE + e] * factor;
+          } else {
+            vec_floats(raw[j], o);
+#pragma unroll
+            for (int e = 0; e < VE; ++e) o[e] = ex2_approx(fmaf(o[e], kRowLog2e, -mb)) * factor;
+          }
+          store_stream(yv + v, vec_from_floats<T, VE>(o));
         }
       }
       if (has_head) yr[g] = from_f32<T>(eh * factor);
@@ -276,18 +283,17 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
       for (int j = 0; j < NV; ++j) {
         const int v = g + j * G;
         if (v < nvec) {
-          V gv;
+          float f[VE], gf[VE];
+          vec_floats(raw[j], f);
           if (gamma_vec) {
-            gv = load_cached(reinterpret_cast<const V*>(gb) + v);
+            vec_floats(load_cached(reinterpret_cast<const V*>(gb) + v), gf);
           } else {
 #pragma unroll
-            for (int e = 0; e < VE; ++e) gv.e[e] = gb[v * VE + e];
+            for (int e = 0; e < VE; ++e) gf[e] = to_f32(gb[v * VE + e]);
           }
-          V o;
 #pragma unroll
-          for (int e = 0; e < VE; ++e)
-            o.e[e] = from_f32<T>(to_f32(raw[j].e[e]) * scale * to_f32(gv.e[e]));
-          store_stream(yv + v, o);
+          for (int e = 0; e < VE; ++e) f[e] = f[e] * scale * gf[e];
+          store_stream(yv + v, vec_from_floats<T, VE>(f));
         }
       }
       if (has_head) yr[g] = from_f32<T>(xh * scale * to_f32(gamma[g]));
@@ -374,10 +380,37 @@ int launch_typed(const RowsArgs& a, const kf_rows_config& cfg, cudaStream_t stre
 
 }  // namespace
 
-kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user) {
+kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user,
+                                   const DeviceInfo& dev) {
   kf_rows_config c{};
   if (user) c = *user;
   const int elem = a.dtype == KF_FP32 ? 4 : 2;
+  if (c.kernel == KF_ROWS_AUTO) {
+    // A field only one kernel has selects that kernel. Otherwise a softmax
+    // with enough rows for every SM to stream several of them goes to the
+    // persistent streaming kernel, which keeps loads in flight while rows are
+    // reduced; the rest go to the register kernel, which can spread one row
+    // over a cluster of SMs.
+    const bool register_fields = c.rows_per_cta > 0 || c.cluster > 0 || c.num_warps > 16;
+    const bool stream_fields = c.row_groups > 0 || c.stages > 0;
+    if (register_fields != stream_fields) {
+      c.kernel = register_fields ? KF_ROWS_REGISTER : KF_ROWS_STREAM;
+    } else {
+      // Measured on B200: the streaming kernel wins for softmax at every
+      // baseline width; RMSNorm's lighter arithmetic runs as fast or faster
+      // in the register kernel.
+      const int warps = c.num_warps > 0 ? c.num_warps : stream_default_warps(a.cols, elem);
+      const long long per_thread = ceil_div(a.cols * elem / 16, 32LL * warps);
+      c.kernel = (a.op == 0 && a.rows >= 2LL * dev.sm_count && per_thread <= 16 &&
+                  rows_stream_supported(a, dev.max_smem_optin, nullptr))
+                     ? KF_ROWS_STREAM
+                     : KF_ROWS_REGISTER;
+    }
+  }
+  if (c.kernel == KF_ROWS_STREAM) {
+    if (c.num_warps <= 0) c.num_warps = stream_default_warps(a.cols, elem);
+    return c;
+  }
   const long long nvec = (a.cols * elem + 15) / 16;
   if (c.cluster <= 0) {
     // One CTA holds up to 1024 threads x 4 vectors (64 KiB) of the row in registers.
@@ -409,7 +442,9 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
 
 int launch_rows(const RowsArgs& a, const kf_rows_config& cfg, const DeviceInfo& dev,
                 cudaStream_t stream) {
-  (void)dev;
+  if (cfg.kernel == KF_ROWS_STREAM) return launch_rows_stream(a, cfg, dev, stream);
+  if (cfg.kernel != KF_ROWS_REGISTER)
+    return set_error(KF_ERR_INVALID_CONFIG, "kernel must be KF_ROWS_AUTO, _REGISTER or _STREAM");
   if (cfg.num_warps < 1 || cfg.num_warps > 32)
     return set_error(KF_ERR_INVALID_CONFIG, "num_warps must be in [1, 32]");
   if (cfg.cluster < 1 || cfg.cluster > 8 || (cfg.cluster & (cfg.cluster - 1)) != 0)

@@ -4,9 +4,11 @@
 (an fp16 running sum over 8192 columns stops resolving its terms) and eps
 inside the square root (an all-zero row stays finite); the rescale and the
 gamma multiply happen in fp32 and the result is rounded once, as in
-``rmsnorm_reference``. The native kernel reads each row once into registers
-with 128-bit loads, reduces with warp shuffles, and writes it once; gamma is
-read through the read-only cache. ``eps`` defaults to the reference's 1e-5;
+``rmsnorm_reference``. The native kernels read each row once into registers,
+reduce with warp shuffles, and write it once with 128-bit stores: for many
+rows a persistent kernel streams rows through a shared-memory ring with bulk
+copies and keeps gamma in shared memory; otherwise one CTA (or a cluster) per
+row loads it with 128-bit loads. ``eps`` defaults to the reference's 1e-5;
 the baseline workload passes 1e-6.
 """
 
@@ -27,8 +29,9 @@ DEFAULT_EPS = 1e-5
 BASELINE_EPS = 1e-6
 
 
-def default_config(n_cols: int, dtype: torch.dtype = torch.float16) -> KernelConfig:
-    return default_rows_config("rmsnorm", n_cols, dtype)
+def default_config(n_cols: int, dtype: torch.dtype = torch.float16, n_rows: int | None = None) -> KernelConfig:
+    """The library's choice for contiguous rows (``n_rows`` unknown: the register kernel)."""
+    return default_rows_config("rmsnorm", n_cols, dtype, rows=n_rows)
 
 
 def rmsnorm(
@@ -48,7 +51,8 @@ def rmsnorm(
         raise ValueError(f"dtype mismatch: {x.dtype} vs {gamma.dtype}")
     if gamma.device != x.device:
         raise ValueError("x and gamma must be on one device")
-    cfg = config or default_config(n_cols, x.dtype)
+    cfg = config or default_rows_config("rmsnorm", n_cols, x.dtype, rows=n_rows, x=x,
+                                        sm_count=native.sm_count(x.device.index))
     check_block(cfg, n_cols, "hidden size")
     out = torch.empty((n_rows, n_cols), device=x.device, dtype=x.dtype)
     if n_rows and n_cols:
@@ -65,7 +69,8 @@ def rmsnorm_reference(x: torch.Tensor, gamma: torch.Tensor, *, eps: float = DEFA
 
 class RMSNormOperator(Operator):
     name = "rmsnorm"
-    config_order = ("BLOCK_SIZE", "ROWS_PER_PROGRAM", "num_warps", "CLUSTER")
+    config_order = ("ROW_KERNEL", "BLOCK_SIZE", "ROWS_PER_PROGRAM", "num_warps", "CLUSTER", "ROW_GROUPS",
+                    "num_stages")
 
     def __init__(self, *, eps: float = DEFAULT_EPS) -> None:
         self.eps = eps
@@ -90,7 +95,7 @@ class RMSNormOperator(Operator):
         return rmsnorm(x, gamma, eps=self.eps, config=config)
 
     def default_config(self, problem: Problem) -> KernelConfig:
-        return default_config(problem.dims_dict["cols"], problem.dtype)
+        return default_config(problem.dims_dict["cols"], problem.dtype, problem.dims_dict["rows"])
 
     def flops(self, problem: Problem) -> int:
         d = problem.dims_dict

@@ -1,8 +1,17 @@
 """Shared host logic of the row kernels (softmax, RMSNorm).
 
 ``default_rows_config`` mirrors ``resolve_rows_config`` in ``csrc/rows.cu``:
-about four 16-byte vectors per thread, one CTA per row until a row exceeds
-4096 vectors (64 KiB), then a power-of-two cluster of CTAs shares it.
+
+* a softmax over many rows (at least two per SM) whose input and output rows
+  sit at the same 16-byte phase goes to the persistent streaming kernel
+  (``ROW_KERNEL=2``, ``csrc/rows_stream.cu``): row groups of ``num_warps`` warps
+  (the fewest, as a power of two, that hold a row at up to 16 vectors a
+  thread) each keeping their next rows in flight as bulk copies into
+  shared-memory slots;
+* otherwise -- and for RMSNorm, whose lighter arithmetic measured as fast or
+  faster there -- the register kernel (``ROW_KERNEL=1``, ``csrc/rows.cu``): about four
+  16-byte vectors per thread, one CTA per row until a row exceeds 4096 vectors
+  (64 KiB), then a power-of-two cluster of CTAs shares it.
 """
 
 from __future__ import annotations
@@ -16,8 +25,66 @@ from kernelo_b200.tuning.search import _RowReductionSpace, ceil_div, next_power_
 MAX_BLOCK_SIZE = _RowReductionSpace.MAX_BLOCK_SIZE
 VECTORS_PER_CTA = 4096
 
+ROW_KERNEL_REGISTER = 1
+ROW_KERNEL_STREAM = 2
+#: Warps of one streaming CTA, shared by its row groups.
+STREAM_CONSUMER_WARPS = 16
+#: Shared memory of one sm_100 CTA, and what the streaming kernel keeps besides its slots.
+SM100_SMEM_PER_BLOCK = 232_448
+STREAM_FIXED_SMEM = 128 + 8 * 16 * 16 + 16
+#: 16-byte vectors a streaming thread may hold.
+STREAM_MAX_VECTORS = 16
 
-def default_rows_config(operation: str, cols: int, dtype: torch.dtype) -> KernelConfig:
+
+def stream_default_warps(cols: int, dtype: torch.dtype) -> int:
+    nvec = cols * itemsize(dtype) // 16
+    warps = min(STREAM_CONSUMER_WARPS, max(1, ceil_div(nvec, 32 * STREAM_MAX_VECTORS)))
+    return next_power_of_2(warps)
+
+
+def stream_vectors_per_thread(cols: int, dtype: torch.dtype, warps: int) -> int:
+    return max(1, ceil_div(cols * itemsize(dtype) // 16, 32 * warps))
+
+
+def stream_fits(cols: int, dtype: torch.dtype) -> bool:
+    """Whether one row fits a shared-memory slot and 16 vectors per thread at 16 warps."""
+    slot = ceil_div(cols * itemsize(dtype) // 16 * 16, 128) * 128
+    if STREAM_FIXED_SMEM + slot + 8 > SM100_SMEM_PER_BLOCK:
+        return False
+    return stream_vectors_per_thread(cols, dtype, STREAM_CONSUMER_WARPS) <= STREAM_MAX_VECTORS
+
+
+def same_phase(x: torch.Tensor | None, cols: int) -> bool:
+    """x rows at the 16-byte phase of a fresh contiguous output (mirrors rows_stream.cu)."""
+    if x is None:
+        return True
+    size = x.element_size()
+    return x.data_ptr() % 16 == 0 and (x.stride(0) * size) % 16 == (cols * size) % 16
+
+
+def default_rows_config(
+    operation: str,
+    cols: int,
+    dtype: torch.dtype,
+    *,
+    rows: int | None = None,
+    x: torch.Tensor | None = None,
+    sm_count: int = 148,
+) -> KernelConfig:
+    block = next_power_of_2(max(cols, 1))
+    if (
+        operation == "softmax"
+        and rows is not None
+        and rows >= 2 * sm_count
+        and stream_fits(cols, dtype)
+        and same_phase(x, cols)
+    ):
+        return KernelConfig(
+            operation,
+            BLOCK_SIZE=block,
+            ROW_KERNEL=ROW_KERNEL_STREAM,
+            num_warps=stream_default_warps(cols, dtype),
+        )
     nvec = ceil_div(cols * itemsize(dtype), 16)
     cluster = 1
     if nvec > VECTORS_PER_CTA:
@@ -27,7 +94,8 @@ def default_rows_config(operation: str, cols: int, dtype: torch.dtype) -> Kernel
     warps = max(1, min(32, ceil_div(threads, 32)))
     return KernelConfig(
         operation,
-        BLOCK_SIZE=next_power_of_2(max(cols, 1)),
+        BLOCK_SIZE=block,
+        ROW_KERNEL=ROW_KERNEL_REGISTER,
         ROWS_PER_PROGRAM=1,
         num_warps=warps,
         CLUSTER=cluster,

@@ -2,10 +2,13 @@
 
 ``y_i = exp(x_i - max x) / sum_j exp(x_j - max x)`` with fp32 arithmetic and one
 rounding to the input dtype. The row maximum is subtracted for the reason the
-reference gives: fp16 ``exp`` overflows above x ~ 11. The native kernel reads
-each row once into registers (one CTA, or a cluster of CTAs for rows wider
-than 64 KiB), reduces the (max, sum of exp) pair in a single pass with the
-online rescaling rule, and writes the row once. Unlike the reference's Triton
+reference gives: fp16 ``exp`` overflows above x ~ 11. Both native kernels read
+each row once into registers, reduce the (max, sum of exp) pair in a single
+pass with the online rescaling rule, and write the row once: for many rows a
+persistent kernel streams rows through a shared-memory ring with bulk copies
+(one CTA per SM, loads of later rows in flight while earlier ones reduce);
+otherwise one CTA, or a cluster of CTAs for rows wider than 64 KiB, takes a
+row straight from global memory. Unlike the reference's Triton
 kernel (capped at 16384 columns) it takes rows up to 131072 columns, which
 covers the baseline's 32000-column vocabulary softmax.
 """
@@ -24,14 +27,16 @@ from kernelo_b200.tuning.config import KernelConfig, Problem
 from kernelo_b200.tuning.search import SoftmaxSearchSpace
 
 
-def default_config(n_cols: int, dtype: torch.dtype = torch.float16) -> KernelConfig:
-    return default_rows_config("softmax", n_cols, dtype)
+def default_config(n_cols: int, dtype: torch.dtype = torch.float16, n_rows: int | None = None) -> KernelConfig:
+    """The library's choice for contiguous rows (``n_rows`` unknown: the register kernel)."""
+    return default_rows_config("softmax", n_cols, dtype, rows=n_rows)
 
 
 def softmax(x: torch.Tensor, *, config: KernelConfig | None = None) -> torch.Tensor:
     check_row_input(x)
     n_rows, n_cols = x.shape
-    cfg = config or default_config(n_cols, x.dtype)
+    cfg = config or default_rows_config("softmax", n_cols, x.dtype, rows=n_rows, x=x,
+                                        sm_count=native.sm_count(x.device.index))
     check_block(cfg, n_cols, "row width")
     out = torch.empty((n_rows, n_cols), device=x.device, dtype=x.dtype)
     if n_rows and n_cols:
@@ -41,7 +46,8 @@ def softmax(x: torch.Tensor, *, config: KernelConfig | None = None) -> torch.Ten
 
 class SoftmaxOperator(Operator):
     name = "softmax"
-    config_order = ("BLOCK_SIZE", "ROWS_PER_PROGRAM", "num_warps", "CLUSTER")
+    config_order = ("ROW_KERNEL", "BLOCK_SIZE", "ROWS_PER_PROGRAM", "num_warps", "CLUSTER", "ROW_GROUPS",
+                    "num_stages")
 
     def __init__(self, *, distribution: str = "baseline") -> None:
         if distribution not in ("baseline", "reference"):
@@ -68,7 +74,7 @@ class SoftmaxOperator(Operator):
         return softmax(x, config=config)
 
     def default_config(self, problem: Problem) -> KernelConfig:
-        return default_config(problem.dims_dict["cols"], problem.dtype)
+        return default_config(problem.dims_dict["cols"], problem.dtype, problem.dims_dict["rows"])
 
     def flops(self, problem: Problem) -> int:
         d = problem.dims_dict

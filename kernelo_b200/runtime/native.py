@@ -122,7 +122,10 @@ class KfRowsConfig(ctypes.Structure):
         ("num_warps", ctypes.c_int32),
         ("rows_per_cta", ctypes.c_int32),
         ("cluster", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 5),
+        ("kernel", ctypes.c_int32),
+        ("row_groups", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 2),
     ]
 
 
@@ -281,6 +284,9 @@ def rows_struct(config) -> KfRowsConfig:
         s.num_warps = config.get("num_warps", 0)
         s.rows_per_cta = config.get("ROWS_PER_PROGRAM", 0)
         s.cluster = config.get("CLUSTER", 0)
+        s.kernel = config.get("ROW_KERNEL", 0)
+        s.row_groups = config.get("ROW_GROUPS", 0)
+        s.stages = config.get("num_stages", 0)
     return s
 
 

@@ -4,8 +4,10 @@ A :class:`KernelConfig` is an immutable, hashable mapping of integer tuning
 parameters owned by one operation; each operator's search space defines its
 keys. On sm_100a the GEMM keys are ``KERNEL`` (1 = tcgen05, 2 = SIMT),
 ``BLOCK_M/BLOCK_N/BLOCK_K``, ``GROUP_M``, ``num_stages``, ``STREAM_K``,
-``SWAP_AB`` and ``CLUSTER_M/CLUSTER_N``; the row kernels use ``BLOCK_SIZE``,
-``ROWS_PER_PROGRAM``, ``num_warps`` and ``CLUSTER``. All keys travel to the
+``SWAP_AB`` and ``CLUSTER_M/CLUSTER_N``; the row kernels use ``ROW_KERNEL``
+(1 = register, 2 = streaming), ``BLOCK_SIZE``, ``num_warps``, and
+``ROWS_PER_PROGRAM``/``CLUSTER`` (register kernel) or ``ROW_GROUPS``/``num_stages``
+(streaming kernel). All keys travel to the
 C ABI; ``meta``/``launch`` keep the reference's split for callers that use it.
 
 A :class:`Problem` is one workload: an operation name, named dimensions in

@@ -322,11 +322,17 @@ class GemvSearchSpace(_Sm100GemmSpace):
 
 # ------------------------------------------------------------------------ rows
 class _RowReductionSpace(SearchSpace):
-    """Register-resident row kernels: threads per CTA, rows per CTA, CTAs per row."""
+    """Row kernels. The register kernel (``ROW_KERNEL=1``): threads per CTA, rows
+    per CTA, CTAs per row. The persistent streaming kernel (``ROW_KERNEL=2``):
+    warps per row group, one CTA per SM with 16 consumer warps."""
 
     NUM_WARPS = (1, 2, 4, 8, 16, 32)
     ROWS_PER_PROGRAM = (1, 2, 4)
     CLUSTER = (1, 2, 4, 8)
+    STREAM_WARPS = (1, 2, 4, 8, 16)
+    STREAM_CONSUMER_WARPS = 16
+    #: Shared memory the streaming kernel keeps besides its row slots.
+    STREAM_FIXED_SMEM = 128 + 8 * 16 * 16 + 16
     #: 16-byte vectors one thread may hold (the largest kernel instantiation).
     MAX_VECTORS_PER_THREAD = 16
     #: Widest row accepted: 8 CTAs x 512 threads x 8 vectors x 4 fp32 values.
@@ -339,29 +345,60 @@ class _RowReductionSpace(SearchSpace):
 
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
         block = next_power_of_2(problem.dims_dict["cols"])
+        for warps in self.STREAM_WARPS:
+            yield KernelConfig(self.operation, BLOCK_SIZE=block, ROW_KERNEL=2, num_warps=warps)
         for cluster, warps, rows in product(self.CLUSTER, self.NUM_WARPS, self.ROWS_PER_PROGRAM):
             yield KernelConfig(
                 self.operation,
                 BLOCK_SIZE=block,
+                ROW_KERNEL=1,
                 ROWS_PER_PROGRAM=rows,
                 num_warps=warps,
                 CLUSTER=cluster,
             )
 
+    @staticmethod
+    def is_stream(config: KernelConfig) -> bool:
+        return config.get("ROW_KERNEL", 1) == 2
+
     def vectors_per_row(self, problem: Problem) -> int:
         return ceil_div(problem.dims_dict["cols"] * problem.itemsize, 16)
 
     def vectors_per_thread(self, config: KernelConfig, problem: Problem) -> int:
+        if self.is_stream(config):  # interior vectors only; head/tail are scalar
+            whole = problem.dims_dict["cols"] * problem.itemsize // 16
+            return max(1, ceil_div(whole, config["num_warps"] * 32))
         threads = config["num_warps"] * 32 * config.get("CLUSTER", 1)
         return ceil_div(self.vectors_per_row(problem), threads)
 
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
+        if self.is_stream(config):
+            return problem.dims_dict["rows"]
         return ceil_div(problem.dims_dict["rows"], config["ROWS_PER_PROGRAM"]) * config.get("CLUSTER", 1)
+
+    def stream_reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
+        cols, rows = problem.dims_dict["cols"], problem.dims_dict["rows"]
+        warps = config["num_warps"]
+        if warps > self.STREAM_CONSUMER_WARPS:
+            return f"streaming kernel: {warps} warps per row exceed its {self.STREAM_CONSUMER_WARPS} consumer warps"
+        slot = ceil_div(cols * problem.itemsize // 16 * 16, 128) * 128
+        if self.STREAM_FIXED_SMEM + slot + 8 > caps.max_shared_memory_per_block:
+            return f"streaming kernel: a row of {slot} bytes does not fit one shared-memory slot"
+        nv = self.vectors_per_thread(config, problem)
+        if nv > self.MAX_VECTORS_PER_THREAD:
+            return f"register pressure: {nv} vectors per thread"
+        if warps > 1 and warps * 32 >= 2 * self.vectors_per_row(problem):
+            return f"idle threads: {warps * 32} threads for {self.vectors_per_row(problem)} vectors"
+        if rows < caps.sm_count:
+            return f"streaming kernel: {rows} rows leave persistent CTAs of {caps.sm_count} SMs idle"
+        return None
 
     def reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
         cols, rows = problem.dims_dict["cols"], problem.dims_dict["rows"]
         if config["BLOCK_SIZE"] > self.MAX_BLOCK_SIZE:
             return f"row of {cols} exceeds the single-pass limit"
+        if self.is_stream(config):
+            return self.stream_reject_reason(config, problem, caps)
         cluster = config.get("CLUSTER", 1)
         if cluster > caps.max_cluster_size:
             return f"cluster of {cluster} exceeds the portable limit of {caps.max_cluster_size}"
@@ -379,11 +416,17 @@ class _RowReductionSpace(SearchSpace):
         return None
 
     def priority(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> tuple[float, ...]:
-        """Memory-bound: fill the machine first, keep about four 16-byte loads in
-        flight per thread, prefer no cluster, then fewer rows per program."""
+        """Memory-bound: for a softmax with at least two rows per SM the
+        streaming kernel first (as the library default), then fill the machine,
+        keep about four 16-byte loads in flight per thread, prefer no cluster,
+        then fewer rows per program."""
+        rows = problem.dims_dict["rows"]
+        stream_first = self.operation == "softmax" and rows >= 2 * caps.sm_count
+        kernel_rank = 0 if self.is_stream(config) == stream_first else 1
         programs = min(self.num_programs(config, problem), caps.sm_count)
         nv = self.vectors_per_thread(config, problem)
-        return (-programs, abs(math.log2(nv) - 2), config.get("CLUSTER", 1), config["ROWS_PER_PROGRAM"])
+        return (kernel_rank, -programs, abs(math.log2(nv) - 2), config.get("CLUSTER", 1),
+                config.get("ROWS_PER_PROGRAM", 1))
 
 
 class SoftmaxSearchSpace(_RowReductionSpace):

@@ -167,3 +167,94 @@ def test_rmsnorm_baseline_sizes(cols, dtype, device):
     # Normalised rows have unit RMS before gamma: undo gamma and check.
     rms = (out.float() / gamma.float()).pow(2).mean(-1).sqrt()
     assert float((rms - 1).abs().max()) < (0.02 if dtype == torch.bfloat16 else 0.005)
+
+
+# ---------------------------------------------------------------- streaming kernel
+def stream_cfg(op, cols, **kw):
+    return KernelConfig(op, BLOCK_SIZE=max(1, 1 << (cols - 1).bit_length()), ROW_KERNEL=2, **kw)
+
+
+STREAM_COLS = (1, 3, 8, 9, 127, 1000, 2048, 4097, 8192, 16000, 32000)
+
+
+@pytest.mark.parametrize("cols", STREAM_COLS)
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_stream_kernel_widths(cols, dtype, device):
+    """Explicit streaming kernel at its default warps: widths below one vector,
+    unaligned (4097) rows with scalar head/tail, up to 64-128 KiB rows."""
+    from kernelo_b200.kernels.rows_common import stream_default_warps
+
+    rows = 2 * 148 + 5
+    x = rand(rows, cols, dtype, device, scale=4.0)
+    warps = stream_default_warps(cols, dtype)
+    gate(ref.softmax_ref(host(x)), softmax(x, config=stream_cfg("softmax", cols, num_warps=warps)), dtype,
+         context=f"softmax {cols}")
+    gamma = (rand(1, cols, torch.float32, device, seed=1)[0] * 0.1 + 1).to(dtype)
+    x1 = rand(rows, cols, dtype, device)
+    gate(ref.rmsnorm_ref(host(x1), host(gamma), 1e-6),
+         rmsnorm(x1, gamma, eps=1e-6, config=stream_cfg("rmsnorm", cols, num_warps=warps)), dtype,
+         context=f"rmsnorm {cols}")
+
+
+@pytest.mark.parametrize("warps", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("row_groups,stages", [(0, 0), (1, 0), (3, 0), (0, 1), (0, 2), (2, 5)])
+def test_stream_kernel_launch_shapes(warps, row_groups, stages, device):
+    """Every warps x row-group x ring-depth combination, including one slot
+    shared by all groups (stages=1) and more groups than slots."""
+    if row_groups * warps > 16:
+        pytest.skip("more than 16 consumer warps")
+    x = rand(1000, 2048, torch.float16, device, scale=4.0)
+    gamma = (rand(1, 2048, torch.float32, device, seed=1)[0] * 0.1 + 1).half()
+    kw = dict(num_warps=warps, ROW_GROUPS=row_groups, num_stages=stages)
+    gate(ref.softmax_ref(host(x)), softmax(x, config=stream_cfg("softmax", 2048, **kw)), torch.float16)
+    gate(ref.rmsnorm_ref(host(x), host(gamma)), rmsnorm(x, gamma, config=stream_cfg("rmsnorm", 2048, **kw)),
+         torch.float16)
+
+
+def test_stream_kernel_sixteen_vectors_per_thread(device):
+    """The 16-vector instantiation (rows of 128 KiB fp32 / 64 KiB 16-bit at 16 warps)."""
+    for dtype, cols in ((torch.float32, 32000), (torch.bfloat16, 64000)):
+        x = rand(300, cols, dtype, device, scale=4.0)
+        gate(ref.softmax_ref(host(x)), softmax(x, config=stream_cfg("softmax", cols, num_warps=16)), dtype,
+             context=f"{dtype} {cols}")
+
+
+def test_stream_kernel_strided_rows(device):
+    base = rand(600, 1536, torch.bfloat16, device, scale=4.0)
+    x = base[:, 8:1008]  # row stride 1536, 16-byte-aligned start: same phase as the output
+    out = softmax(x, config=stream_cfg("softmax", 1000, num_warps=1))
+    gate(ref.softmax_ref(host(x)), out, torch.bfloat16)
+    gamma = torch.ones(1000, device=device, dtype=torch.bfloat16)
+    gate(ref.rmsnorm_ref(host(x), host(gamma)), rmsnorm(x, gamma, config=stream_cfg("rmsnorm", 1000, num_warps=1)),
+         torch.bfloat16)
+    # A start off the 16-byte grid puts x and a fresh output at different
+    # phases: the default picks the register kernel, an explicit stream config
+    # is refused.
+    odd = base[:, 3:1003]
+    gate(ref.softmax_ref(host(odd)), softmax(odd), torch.bfloat16)
+    from kernelo_b200.runtime.native import OutOfResources
+
+    with pytest.raises(OutOfResources, match="phase"):
+        softmax(odd, config=stream_cfg("softmax", 1000, num_warps=1))
+
+
+def test_stream_kernel_is_the_default_for_many_rows(device):
+    from kernelo_b200.kernels.rows_common import default_rows_config
+
+    x = rand(4096, 4096, torch.float16, device)
+    assert default_rows_config("softmax", 4096, torch.float16, rows=4096, x=x)["ROW_KERNEL"] == 2
+    assert default_rows_config("softmax", 4096, torch.float16, rows=64, x=x[:64])["ROW_KERNEL"] == 1
+    assert default_rows_config("softmax", 32000, torch.float32, rows=32768)["ROW_KERNEL"] == 2
+    assert default_rows_config("rmsnorm", 4096, torch.float16, rows=16384, x=x)["ROW_KERNEL"] == 1
+
+
+def test_stream_kernel_rejects_bad_configs(device):
+    from kernelo_b200.runtime.native import OutOfResources
+
+    x = rand(400, 4096, torch.float32, device)
+    with pytest.raises(OutOfResources, match="register pressure"):
+        softmax(x, config=stream_cfg("softmax", 4096, num_warps=1))  # 32 vectors per thread
+    with pytest.raises(OutOfResources, match="16 warps"):
+        softmax(x, config=stream_cfg("softmax", 4096, num_warps=8, ROW_GROUPS=3))
+    with pytest.raises(OutOfResources, match="row slots"):
+        softmax(x, config=stream_cfg("softmax", 4096, num_warps=8, num_stages=40))

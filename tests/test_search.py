@@ -136,13 +136,36 @@ def test_explain_names_rules_and_device(b200_caps):
 def test_row_space_shape_and_rules(b200_caps):
     problem = Problem.create("rmsnorm", "fp16", rows=16384, cols=4096)
     cands = RMSNormSearchSpace().candidates(problem, b200_caps)
-    assert cands and {k for c in cands for k in c} == {"BLOCK_SIZE", "ROWS_PER_PROGRAM", "num_warps", "CLUSTER"}
+    register = [c for c in cands if c["ROW_KERNEL"] == 1]
+    stream = [c for c in cands if c["ROW_KERNEL"] == 2]
+    assert register and {k for c in register for k in c} == {
+        "ROW_KERNEL", "BLOCK_SIZE", "ROWS_PER_PROGRAM", "num_warps", "CLUSTER"}
+    assert stream and {k for c in stream for k in c} == {"ROW_KERNEL", "BLOCK_SIZE", "num_warps"}
+    assert sorted(c["num_warps"] for c in stream) == [1, 2, 4, 8, 16]
+    assert cands[0]["ROW_KERNEL"] == 1, "RMSNorm: the register kernel (library default) ranks first"
+    soft = Problem.create("softmax", "fp16", rows=16384, cols=4096)
+    assert SoftmaxSearchSpace().candidates(soft, b200_caps)[0]["ROW_KERNEL"] == 2
     assert {c["BLOCK_SIZE"] for c in cands} == {4096}
     wide = Problem.create("softmax", "fp32", rows=32768, cols=32000)
     space = SoftmaxSearchSpace()
     one_cta = KernelConfig("softmax", BLOCK_SIZE=32768, ROWS_PER_PROGRAM=1, num_warps=4, CLUSTER=1)
     assert space.reject_reason(one_cta, wide, b200_caps).startswith("register pressure")
-    assert any(c["CLUSTER"] > 1 for c in space.candidates(wide, b200_caps))
+    assert any(c.get("CLUSTER", 1) > 1 for c in space.candidates(wide, b200_caps))
+    # 8000 vectors: 16 streaming warps hold 16 each; 8 would need 32
+    st16 = KernelConfig("softmax", BLOCK_SIZE=32768, ROW_KERNEL=2, num_warps=16)
+    st8 = KernelConfig("softmax", BLOCK_SIZE=32768, ROW_KERNEL=2, num_warps=8)
+    assert space.reject_reason(st16, wide, b200_caps) is None
+    assert space.reject_reason(st8, wide, b200_caps).startswith("register pressure")
+    few = Problem.create("softmax", "fp16", rows=64, cols=4096)
+    st4 = KernelConfig("softmax", BLOCK_SIZE=4096, ROW_KERNEL=2, num_warps=4)
+    assert "rows leave persistent CTAs" in space.reject_reason(st4, few, b200_caps)
+    assert space.candidates(few, b200_caps)[0]["ROW_KERNEL"] == 1
+    narrow = Problem.create("softmax", "fp16", rows=32768, cols=1000)  # 125 vectors
+    st8 = KernelConfig("softmax", BLOCK_SIZE=1024, ROW_KERNEL=2, num_warps=8)
+    assert space.reject_reason(st8, narrow, b200_caps).startswith("idle threads")
+    huge = Problem.create("softmax", "fp32", rows=4096, cols=65536)  # 256 KiB rows
+    st = KernelConfig("softmax", BLOCK_SIZE=65536, ROW_KERNEL=2, num_warps=16)
+    assert "shared-memory slot" in space.reject_reason(st, huge, b200_caps)
     too_wide = Problem.create("softmax", "fp16", rows=2, cols=300_000)
     assert all(r.startswith("row of") for _, r in space.generate(too_wide, b200_caps).rejected)
 
