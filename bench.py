@@ -195,8 +195,16 @@ def cpu_baseline(rows: int = 512, budget_s: float = 10.0) -> dict:
 
 # ------------------------------------------------------------------ secondary rows
 def secondary_lines(pk: dict, flush) -> list[dict]:
-    """Memory-bound rows at their baseline sizes, N=1: GB/s and fraction of HBM peak."""
+    """Memory-bound rows at their baseline sizes, N=1: GB/s and fraction of HBM peak.
+
+    ``value`` is device time per launch from a CUDA graph of back-to-back
+    launches that cycle through input sets together larger than twice the L2
+    (no launch finds its inputs cached, no host overhead or event gap inside);
+    ``single_launch`` is one launch between two events after an L2 flush (clean
+    lines), which adds the ~6 us launch-and-event floor.
+    """
     from kernelo_b200.benchmark.metrics import gemv_bytes, rmsnorm_bytes, softmax_bytes
+    from kernelo_b200.benchmark.runner import graph_time_per_launch, rotation_sets
     from kernelo_b200.kernels.gemv import gemv
     from kernelo_b200.kernels.rmsnorm import rmsnorm
     from kernelo_b200.kernels.softmax import softmax
@@ -204,7 +212,7 @@ def secondary_lines(pk: dict, flush) -> list[dict]:
     dev = torch.device("cuda")
     out = []
 
-    def time_ms(fn, iters=20):
+    def single_ms(fn, iters=10):
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
@@ -217,29 +225,39 @@ def secondary_lines(pk: dict, flush) -> list[dict]:
         torch.cuda.synchronize()
         return statistics.median(s.elapsed_time(e) for s, e in ev)
 
+    def line(metric, nbytes, calls, sets):
+        ms = graph_time_per_launch(calls)
+        one = single_ms(calls[0])
+        gbs = nbytes / ms / 1e6
+        return {"metric": metric, "value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 3),
+                "us_per_launch": round(ms * 1e3, 2), "single_launch_gbs": round(nbytes / one / 1e6, 1),
+                "timing": f"CUDA graph of {len(calls)} launches over {sets} rotating input sets (> 2x L2)"}
+
     g = torch.Generator(device=dev).manual_seed(5)
     for cols in (4096, 8192):
-        x = torch.randn(16384, cols, device=dev, generator=g).bfloat16()
+        nbytes = rmsnorm_bytes(16384, cols, 2)
+        sets = rotation_sets(nbytes, dev)
+        xs = [torch.randn(16384, cols, device=dev, generator=g).bfloat16() for _ in range(sets)]
         gamma = (torch.randn(cols, device=dev, generator=g) * 0.1 + 1).bfloat16()
-        ms = time_ms(lambda: rmsnorm(x, gamma, eps=1e-6))
-        gbs = rmsnorm_bytes(16384, cols, 2) / ms / 1e6
-        out.append({"metric": f"rmsnorm 16384x{cols} bf16", "value": round(gbs, 1), "unit": "GB/s",
-                    "frac": round(gbs / pk["hbm_gbs"], 3)})
-        del x
+        calls = [lambda x=x: rmsnorm(x, gamma, eps=1e-6) for x in xs] * 2
+        out.append(line(f"rmsnorm 16384x{cols} bf16", nbytes, calls, sets))
+        del xs, calls
     for cols, dt in ((1000, torch.float16), (4096, torch.float16), (4097, torch.float16), (32000, torch.float32)):
-        x = (torch.randn(32768, cols, device=dev, generator=g) * 4).to(dt)
-        ms = time_ms(lambda: softmax(x), iters=10)
-        gbs = softmax_bytes(32768, cols, x.element_size()) / ms / 1e6
-        out.append({"metric": f"softmax 32768x{cols} {str(dt)[6:]}", "value": round(gbs, 1), "unit": "GB/s",
-                    "frac": round(gbs / pk["hbm_gbs"], 3)})
-        del x
-    w = (torch.randn(N, K, device=dev, generator=g) * K ** -0.5).half()
+        item = torch.empty(0, dtype=dt).element_size()
+        nbytes = softmax_bytes(32768, cols, item)
+        sets = rotation_sets(nbytes, dev)
+        xs = [(torch.randn(32768, cols, device=dev, generator=g) * 4).to(dt) for _ in range(sets)]
+        calls = [lambda x=x: softmax(x) for x in xs] * (2 if nbytes < (1 << 30) else 1)
+        out.append(line(f"softmax 32768x{cols} {str(dt)[6:]}", nbytes, calls, sets))
+        del xs, calls
+    wbytes = N * K * 2
+    sets = rotation_sets(wbytes, dev)
+    ws = [(torch.randn(N, K, device=dev, generator=g) * K ** -0.5).half() for _ in range(sets)]
     for m in (1, 4, 16):
         xx = torch.randn(m, K, device=dev, generator=g).half()
-        ms = time_ms(lambda: gemv(xx, w), iters=50)
-        gbs = gemv_bytes(m, N, K, 2) / ms / 1e6
-        out.append({"metric": f"gemv M={m} N={N} K={K} fp16", "value": round(gbs, 1), "unit": "GB/s",
-                    "frac": round(gbs / pk["hbm_gbs"], 3)})
+        calls = [lambda w=w: gemv(xx, w) for w in ws] * 4
+        out.append(line(f"gemv M={m} N={N} K={K} fp16", gemv_bytes(m, N, K, 2), calls, sets))
+    del ws
     return out
 
 
@@ -285,19 +303,28 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     x, w, b, chunk = make_inputs(dev, rank, world)
     if world > 1:
         layer = ShardedFusedLinear(None, None, out_features=N, shard_weight=w, shard_bias=b, approximate="none")
+        gathered = torch.empty(world, M, chunk, device=dev, dtype=torch.bfloat16)
+        mine = gathered[rank]
 
-        def step():
-            return layer(x)
+        # layer(x) in two parts, so the timed loop can bracket the kernel alone
+        def launch_kernel():
+            layer.local(x, out=mine)
 
-        def kernel_only():
-            return layer.local(x, out=layer._gather_buf[rank] if layer._gather_buf is not None else None)
+        def finish_step():
+            dist.all_gather_into_tensor(gathered.view(-1), mine.reshape(-1))
+            return gathered.permute(1, 0, 2).reshape(M, world * chunk)[:, :N]
     else:
         y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
 
-        def step():
-            return fused_linear_gelu(x, w.t(), b, approximate="none", out=y)
+        def launch_kernel():
+            fused_linear_gelu(x, w.t(), b, approximate="none", out=y)
 
-        kernel_only = step
+        def finish_step():
+            return y
+
+    def step():
+        launch_kernel()
+        return finish_step()
 
     # correctness gate on a sample before timing (never inside the timed region)
     out = step()
@@ -319,12 +346,17 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     stream = torch.cuda.current_stream(dev)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    # every launch of the dominant kernel bracketed on its own stream, inside the timed region
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
         barrier(world)
         start.record(stream)
-        for _ in range(args.steps):
-            step()
+        for ks, ke in kev:
+            ks.record(stream)
+            launch_kernel()
+            ke.record(stream)
+            finish_step()
         end.record(stream)
         torch.cuda.synchronize()
         barrier(world)
@@ -332,19 +364,16 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     ms_step = ms_total / args.steps
     value = FLOP * args.steps / (ms_total * 1e-3) / 1e12
 
-    # dominant kernel alone: average launch duration over a burst, same stream
-    kiters = max(10, min(200, args.steps))
-    torch.cuda.synchronize()
-    ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ks.record(stream)
-    for _ in range(kiters):
-        kernel_only()
-    ke.record(stream)
-    torch.cuda.synchronize()
-    kernel_ms = max_over_ranks(ks.elapsed_time(ke) / kiters, world)
+    # the dominant kernel's average launch duration over the timed region
+    kernel_ms = max_over_ranks(sum(ks.elapsed_time(ke) for ks, ke in kev) / len(kev), world)
     achieved = FLOP / world / (kernel_ms * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} burst bf16",
+    # A thousand back-to-back launches run at the power cap: the sustained GEMM
+    # figure is the denominator; the burst figure is reported beside it.
+    peak = pk.get("bf16_tflops_sustained") or pk["bf16_tflops"]
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4),
+                "peak_kind": f"{pk_kind} {'sustained' if pk.get('bf16_tflops_sustained') else 'burst'} bf16",
+                "frac_of_burst": round(achieved / pk["bf16_tflops"], 4),
                 "traffic": profile_traffic("tc_gemm_fused_linear_erf_bf16"), "kernel": "tc_gemm_kernel<bf16,erf>",
                 "kernel_ms": round(kernel_ms, 4)}
 

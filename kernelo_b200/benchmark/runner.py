@@ -198,3 +198,42 @@ def cross_check_median_ms(
         fn()
     timer = tbench.Timer(stmt="fn()", globals={"fn": fn})
     return float(timer.blocked_autorange(min_run_time=min_run_time).median) * 1e3
+
+
+def rotation_sets(bytes_per_set: int, device: torch.device | str | None = None, *, minimum: int = 2) -> int:
+    """Input sets to cycle through so that the sets together exceed twice the L2."""
+    gpu = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    l2 = device_caps(gpu).l2_cache_bytes
+    return max(minimum, -(-2 * l2 // max(1, bytes_per_set)) + 1)
+
+
+def graph_time_per_launch(calls: list[Callable[[], object]], *, replays: int = 5) -> float:
+    """Median device milliseconds per launch of ``calls`` replayed as one CUDA graph.
+
+    ``calls`` should cycle through input sets whose total exceeds the L2 (see
+    :func:`rotation_sets`), so that no launch finds its inputs cached. The
+    graph replays the launches back to back: host overhead and the per-event
+    launch gap (about 6 us on B200) stay out of the per-launch figure.
+    """
+    if not calls:
+        raise ValueError("no calls to time")
+    for call in calls:  # allocations, kernel attributes, workspaces
+        call()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for call in calls:
+            call()
+    graph.replay()
+    torch.cuda.synchronize()
+    samples = []
+    for _ in range(replays):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        end.record()
+        end.synchronize()
+        samples.append(start.elapsed_time(end) / len(calls))
+    del graph
+    samples.sort()
+    return samples[len(samples) // 2]

@@ -280,6 +280,27 @@ int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const 
                 int64_t workspace_bytes, void* stream) {
   if (M > 256) return set_error(KF_ERR_UNSUPPORTED, "kf_gemv takes M <= 256; use kf_gemm");
   kf_gemm_config c = cfg ? *cfg : zero_config();
+  if ((c.kernel == KF_GEMM_AUTO && M <= GEMV_ROWS_AUTO_MAX_M) || c.kernel == KF_GEMM_WARP_ROWS) {
+    // Few rows with K-contiguous weight rows: stream the rows warp by warp on
+    // CUDA cores (measured on B200: 128-row TMA tiles of a row-major weight
+    // read it well below the rate a contiguous row stream reaches).
+    if (!valid_dtype(dtype)) return set_error(KF_ERR_INVALID_ARGUMENT, "unknown dtype code");
+    if (M < 0 || N < 0 || K < 0) return set_error(KF_ERR_INVALID_ARGUMENT, "negative size");
+    if (M == 0 || N == 0) return KF_OK;
+    if (x == nullptr || w == nullptr || y == nullptr)
+      return set_error(KF_ERR_INVALID_ARGUMENT, "null pointer");
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc != KF_OK) return rc;
+    DeviceInfo* dev = nullptr;
+    rc = device_info(device, &dev);
+    if (rc != KF_OK) return rc;
+    std::string why;
+    if (gemv_rows_supported(dtype, w, sw_n, sw_k, M, N, K, dev->max_smem_optin, &why))
+      return launch_gemv_rows(dtype, x, sx_m, sx_k, w, sw_n, y, sy_m, sy_n, M, N, K, c, *dev,
+                              static_cast<cudaStream_t>(stream));
+    if (c.kernel == KF_GEMM_WARP_ROWS) return set_error(KF_ERR_UNALIGNED, "warp-per-row GEMV: " + why);
+  }
   if (c.kernel == KF_GEMM_AUTO || c.kernel == KF_GEMM_TCGEN05) {
     if (c.swap_ab == 0) c.swap_ab = 1;
     if (c.stream_k == 0) c.stream_k = 1;
@@ -314,6 +335,9 @@ int64_t kf_gemv_workspace_bytes(int32_t device, int32_t dtype, int64_t sx_m, int
                                 int64_t sw_n, int64_t sw_k, int64_t M, int64_t N, int64_t K,
                                 const kf_gemm_config* cfg) {
   kf_gemm_config c = cfg ? *cfg : zero_config();
+  // The warp-per-row kernel needs none; AUTO reports the stream-K size, since
+  // a weight pointer off the 16-byte grid sends the call there.
+  if (c.kernel == KF_GEMM_WARP_ROWS) return 0;
   if (c.kernel == KF_GEMM_AUTO || c.kernel == KF_GEMM_TCGEN05) {
     if (c.swap_ab == 0) c.swap_ab = 1;
     if (c.stream_k == 0) c.stream_k = 1;
@@ -324,6 +348,11 @@ int64_t kf_gemv_workspace_bytes(int32_t device, int32_t dtype, int64_t sx_m, int
 int32_t kf_query_gemm_config(int32_t dtype, const kf_gemm_config* cfg, int64_t* smem_bytes,
                              int32_t* tmem_cols) {
   if (cfg == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null config");
+  if (cfg->kernel == KF_GEMM_WARP_ROWS) {  // x's shared memory depends on M and K
+    if (smem_bytes) *smem_bytes = 0;
+    if (tmem_cols) *tmem_cols = 0;
+    return KF_OK;
+  }
   if (cfg->kernel == KF_GEMM_SIMT) {
     if (smem_bytes) *smem_bytes = 2LL * cfg->block_k * (cfg->block_m + cfg->block_n) * 4;
     if (tmem_cols) *tmem_cols = 0;

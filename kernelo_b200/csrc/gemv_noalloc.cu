@@ -73,7 +73,10 @@ extern "C" KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t 
   int rc = kf::current_device(&device);
   if (rc != KF_OK) return rc;
   if (device >= kMaxDevices) return kf::set_error(KF_ERR_INVALID_ARGUMENT, "device index out of range");
-  const int64_t need = kf_gemv_workspace_bytes(device, dtype, sx_m, sx_k, sw_n, sw_k, M, N, K, nullptr);
+  // Always the stream-K tcgen05 GEMV: the kernel whose scratch this entry point holds.
+  kf_gemm_config cfg{};
+  cfg.kernel = KF_GEMM_TCGEN05;
+  const int64_t need = kf_gemv_workspace_bytes(device, dtype, sx_m, sx_k, sw_n, sw_k, M, N, K, &cfg);
   if (need < 0) return static_cast<int32_t>(-need);
   if (need > KF_NOALLOC_SCRATCH_BYTES)
     return kf::set_error(KF_ERR_WORKSPACE, "this GEMV needs " + std::to_string(need) +
@@ -89,6 +92,6 @@ extern "C" KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t 
     const cudaError_t err = cudaMemsetAsync(scratch, 0, kCounterBytes, s);
     if (err != cudaSuccess) return kf::cuda_error(err, "cudaMemsetAsync(no-alloc counters)");
   }
-  return kf_gemv(dtype, x, sx_m, sx_k, w, sw_n, sw_k, y, sy_m, sy_n, M, N, K, nullptr, scratch,
+  return kf_gemv(dtype, x, sx_m, sx_k, w, sw_n, sw_k, y, sy_m, sy_n, M, N, K, &cfg, scratch,
                  KF_NOALLOC_SCRATCH_BYTES, stream);
 }

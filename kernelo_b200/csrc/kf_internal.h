@@ -59,6 +59,19 @@ bool tcgen05_operands_ok(const GemmArgs& args, std::string* why);
 // CUDA-core path: any strides, fp16/bf16/fp32.
 int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream_t stream);
 
+// Warp-per-row decode GEMV (gemv_rows.cu): y[M, N] = x[M, K] . w[N, K]^T for
+// M <= GEMV_ROWS_MAX_M with K-contiguous, 16-byte-aligned weight rows.
+constexpr int GEMV_ROWS_MAX_M = 4;
+// kf_gemv picks it by itself up to this many rows (measured on B200: at M=4
+// the tcgen05 GEMV streams the weight faster).
+constexpr int GEMV_ROWS_AUTO_MAX_M = 2;
+bool gemv_rows_supported(int dtype, const void* w, int64_t sw_n, int64_t sw_k, int64_t M,
+                         int64_t N, int64_t K, int max_smem_optin, std::string* why);
+int launch_gemv_rows(int dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w,
+                     int64_t sw_n, void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N,
+                     int64_t K, const kf_gemm_config& cfg, const DeviceInfo& dev,
+                     cudaStream_t stream);
+
 // Row kernels.
 struct RowsArgs {
   int dtype = KF_FP16;

@@ -19,6 +19,22 @@ from kernelo_b200.tuning.config import KernelConfig
 
 KERNEL_TCGEN05 = 1
 KERNEL_SIMT = 2
+#: kf_gemv only: warps streaming K-contiguous weight rows, M <= 4 (csrc/gemv_rows.cu).
+KERNEL_WARP_ROWS = 3
+WARP_ROWS_MAX_M = 4
+#: The library default up to this M (measured on B200: at M=4 the tcgen05 GEMV is faster).
+WARP_ROWS_AUTO_MAX_M = 2
+
+
+def warp_rows_rows(m: int) -> int:
+    """Rows of x the warp-per-row GEMV is compiled for: M rounded up to 1, 2 or 4."""
+    return 1 if m <= 1 else 2 if m <= 2 else 4
+
+
+def warp_rows_smem_bytes(m: int, k: int, itemsize: int = 2) -> int:
+    """x staged as fp32: whole 16-byte weight vectors plus one vector of tail."""
+    ve = 16 // itemsize
+    return warp_rows_rows(m) * (k // ve * ve + ve) * 4
 
 SM100_SMEM_PER_BLOCK = 232_448
 TC_BLOCK_M = 128

@@ -11,6 +11,14 @@ every SM (stream-K) so that all 148 SMs pull weight bytes at once. Partial
 sums go to a workspace; the last CTA to finish a tile reduces them in a fixed
 order.
 
+For M <= 2 with a K-contiguous [N,K] weight the default is the warp-per-row
+kernel (``KERNEL=3``, ``csrc/gemv_rows.cu``): each warp streams one or two
+whole weight rows with contiguous 512-byte loads and accumulates with packed
+fp32x2 FMAs against x held in shared memory. Measured on B200, the 128-row TMA tiles of
+the tcgen05 path read a row-major weight at well under the rate of a
+contiguous row stream; from M=4 on the x reads of the CUDA-core kernel cost
+more than that (it still takes M <= 4 when asked for with ``KERNEL=3``).
+
 W may be stored [N,K] (``w_layout="nk"``, nn.Linear, the baseline layout) or
 [K,N] (``"kn"``, the reference's ``matmul(x, w)`` orientation).
 """
@@ -22,6 +30,7 @@ from collections.abc import Callable
 import torch
 
 from kernelo_b200.benchmark import metrics
+from kernelo_b200.dtypes import itemsize
 from kernelo_b200.kernels import gemm_common as gc
 from kernelo_b200.kernels.base import Operator, seeded_generator
 from kernelo_b200.runtime import native
@@ -65,6 +74,9 @@ def gemv(
 
 
 def default_config(m: int, n: int, k: int, dtype: torch.dtype, *, sm_count: int = 148) -> KernelConfig:
+    """The library's choice for contiguous [M,K] x and [N,K] w (mirrors kf_gemv)."""
+    if 1 <= m <= gc.WARP_ROWS_AUTO_MAX_M and gc.warp_rows_smem_bytes(m, k, itemsize(dtype)) <= gc.SM100_SMEM_PER_BLOCK:
+        return KernelConfig("gemv", KERNEL=gc.KERNEL_WARP_ROWS)
     if gc.shape_allows_tcgen05(m, n, k, dtype, b_layout="nk") is not None:
         return gc.default_simt_config("gemv", m, n, sm_count=sm_count)
     cfg = gc.default_tcgen05_config("gemv", m, n, k, b_layout="nk", sm_count=sm_count)

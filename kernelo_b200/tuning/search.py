@@ -316,8 +316,42 @@ class FusedLinearErfSearchSpace(_Sm100GemmSpace):
 
 
 class GemvSearchSpace(_Sm100GemmSpace):
+    """The GEMM grid plus the warp-per-row CUDA-core GEMV (``KERNEL=3``)."""
+
     operation = "gemv"
     b_layout = "nk"
+
+    def grid(self, problem: Problem) -> Iterator[KernelConfig]:
+        yield KernelConfig(self.operation, KERNEL=gc.KERNEL_WARP_ROWS)
+        yield from super().grid(problem)
+
+    def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
+        if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
+            m, _, k = self.dims(problem)
+            return gc.warp_rows_smem_bytes(m, k, itemsize(problem.dtype))
+        return super().shared_memory_bytes(config, problem)
+
+    def num_programs(self, config: KernelConfig, problem: Problem) -> int:
+        if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
+            return ceil_div(self.dims(problem)[1], 16)  # 16 warps per CTA, a row or two each
+        return super().num_programs(config, problem)
+
+    def reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
+        if config["KERNEL"] != gc.KERNEL_WARP_ROWS:
+            return super().reject_reason(config, problem, caps)
+        m, _, _ = self.dims(problem)
+        if m > gc.WARP_ROWS_MAX_M:
+            return f"warp-per-row GEMV takes at most {gc.WARP_ROWS_MAX_M} rows of x, got M={m}"
+        smem = self.shared_memory_bytes(config, problem)
+        if smem > caps.max_shared_memory_per_block:
+            return f"shared memory: x as fp32 needs {smem // 1024} KiB"
+        return None
+
+    def priority(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> tuple[float, ...]:
+        """The warp-per-row kernel first where it is the library default (M <= 2)."""
+        if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
+            return (-1,) if self.dims(problem)[0] <= gc.WARP_ROWS_AUTO_MAX_M else (2,)
+        return super().priority(config, problem, caps)
 
 
 # ------------------------------------------------------------------------ rows

@@ -293,3 +293,50 @@ def test_gemv_validation(device):
         gemv(x, torch.randn(128, 64, device=device, dtype=torch.float16))
     with pytest.raises(ValueError, match="shape mismatch"):
         gemv(x[:4], torch.randn(128, 65, device=device, dtype=torch.float16))
+
+
+# ------------------------------------------------------------------ warp-per-row GEMV
+WARP_ROWS = KernelConfig("gemv", KERNEL=3)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_gemv_warp_rows(m, dtype, device):
+    """Every compiled row count (1, 2, 4) with unused rows masked; N = 2051 is
+    odd (a two-row tile with one row) and leaves the last CTA's warps idle."""
+    gen = torch.Generator().manual_seed(10 + m)
+    x = torch.randn(m, 1024, generator=gen).to(dtype).to(device)
+    w = (torch.randn(2051, 1024, generator=gen) * 1024 ** -0.5).to(dtype).to(device)
+    gate(ref.gemv_ref(host(x), host(w)), gemv(x, w, config=WARP_ROWS), dtype, context=f"M={m}")
+
+
+def test_gemv_warp_rows_tails_and_strides(device):
+    """K = 4093 (a 5-element scalar tail after 511 vectors) on weight rows that
+    stay 16-byte aligned (row stride 4096), x strided along K, y transposed."""
+    gen = torch.Generator().manual_seed(21)
+    base = (torch.randn(777, 4096, generator=gen) * 0.02).half().to(device)
+    w = base[:, :4093]
+    xb = torch.randn(3, 2 * 4093, generator=gen).half().to(device)
+    x = xb[:, ::2]
+    out = torch.empty(777, 3, device=device, dtype=torch.float16).t()
+    gemv(x, w, config=WARP_ROWS, out=out)
+    gate(ref.gemv_ref(host(x), host(w)), out, torch.float16)
+
+
+def test_gemv_warp_rows_refuses_unaligned_weight_rows(device):
+    from kernelo_b200.runtime.native import OutOfResources
+
+    x = torch.randn(2, 4097, device=device, dtype=torch.float16)
+    w = torch.randn(64, 4097, device=device, dtype=torch.float16)  # rows 8194 bytes apart
+    with pytest.raises(OutOfResources, match="16-byte"):
+        gemv(x, w, config=WARP_ROWS)
+    gate(ref.gemv_ref(host(x), host(w)), gemv(x, w), torch.float16)  # the default falls back
+
+
+def test_gemv_default_kernel_choice():
+    from kernelo_b200.kernels.gemv import default_config
+
+    assert default_config(1, 11008, 4096, torch.float16)["KERNEL"] == 3
+    assert default_config(2, 11008, 4096, torch.bfloat16)["KERNEL"] == 3
+    assert default_config(4, 11008, 4096, torch.float16)["KERNEL"] == 1
+    assert default_config(16, 11008, 4096, torch.float16)["KERNEL"] == 1

@@ -189,3 +189,20 @@ def test_unknown_space_is_an_error():
     with pytest.raises(ValueError):
         search_space("vector_add")
     assert isinstance(search_space("gemv"), GemvSearchSpace)
+
+
+def test_gemv_warp_rows_candidate(b200_caps):
+    space = GemvSearchSpace()
+    one = Problem.create("gemv", "fp16", M=1, N=11008, K=4096)
+    cands = space.candidates(one, b200_caps)
+    assert cands[0]["KERNEL"] == gc.KERNEL_WARP_ROWS, "M=1: the warp-per-row kernel is the default"
+    four = Problem.create("gemv", "fp16", M=4, N=11008, K=4096)
+    cands4 = space.candidates(four, b200_caps)
+    assert cands4[0]["KERNEL"] == gc.KERNEL_TCGEN05 and any(c["KERNEL"] == 3 for c in cands4)
+    wide = Problem.create("gemv", "fp16", M=16, N=11008, K=4096)
+    warp_rows = KernelConfig("gemv", KERNEL=gc.KERNEL_WARP_ROWS)
+    assert space.reject_reason(warp_rows, wide, b200_caps).startswith("warp-per-row GEMV takes at most 4")
+    # x staged as fp32: 4 rows x 16384 columns = 256 KiB of shared memory
+    long_k = Problem.create("gemv", "fp16", M=4, N=1024, K=16384)
+    assert space.reject_reason(warp_rows, long_k, b200_caps).startswith("shared memory")
+    assert gc.warp_rows_smem_bytes(1, 4096, 2) == 1 * (4096 + 8) * 4
