@@ -80,6 +80,83 @@ def fused_linear_gelu(
     return out
 
 
+_copy_streams: dict[int, tuple[torch.cuda.Stream, torch.cuda.Stream]] = {}
+
+
+def _streams(device: torch.device) -> tuple[torch.cuda.Stream, torch.cuda.Stream]:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _copy_streams:
+        _copy_streams[idx] = (torch.cuda.Stream(idx), torch.cuda.Stream(idx))
+    return _copy_streams[idx]
+
+
+def fused_linear_gelu_host(
+    x_host: torch.Tensor,
+    w: torch.Tensor,
+    bias: torch.Tensor,
+    *,
+    approximate: str = "tanh",
+    out: torch.Tensor | None = None,
+    chunks: int = 8,
+    config: KernelConfig | None = None,
+) -> torch.Tensor:
+    """``gelu(x @ w + bias)`` for activations in pinned host memory, result in
+    pinned host memory; ``w`` and ``bias`` are resident on the GPU.
+
+    The rows move in ``chunks`` pieces on two copy streams: chunk i+1 goes to
+    the device while chunk i runs through the fused kernel and chunk i-1
+    comes back, so a call costs about the larger of the two transfer
+    directions instead of their sum plus the kernel. Everything is ordered
+    after the work already queued on the current stream, and the current
+    stream waits for the last copy, so synchronising it makes ``out`` valid.
+    Each chunk is one launch of the same kernel as :func:`fused_linear_gelu`.
+    """
+    if x_host.ndim != 2 or w.ndim != 2:
+        raise ValueError(f"expected 2D x and w, got {tuple(x_host.shape)} and {tuple(w.shape)}")
+    if x_host.device.type != "cpu" or not x_host.is_pinned():
+        raise ValueError("x_host must be a pinned (page-locked) CPU tensor; see Tensor.pin_memory()")
+    if x_host.shape[1] != w.shape[0]:
+        raise ValueError(f"shape mismatch: {tuple(x_host.shape)} @ {tuple(w.shape)}")
+    if x_host.dtype != w.dtype:
+        raise ValueError(f"dtype mismatch: {x_host.dtype}, {w.dtype}, {bias.dtype}")
+    if chunks < 1:
+        raise ValueError(f"chunks must be positive, got {chunks}")
+    m, n = x_host.shape[0], w.shape[1]
+    if out is None:
+        out = torch.empty((m, n), dtype=x_host.dtype, pin_memory=True)
+    elif tuple(out.shape) != (m, n) or out.dtype != x_host.dtype or not out.is_pinned() or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous pinned ({m}, {n}) {x_host.dtype} CPU tensor")
+    if not x_host.is_contiguous():
+        raise ValueError("x_host must be contiguous")
+    if m == 0 or n == 0:
+        return out
+    dev = w.device
+    compute = torch.cuda.current_stream(dev)
+    s_in, s_out = _streams(dev)
+    x_dev = torch.empty((m, x_host.shape[1]), device=dev, dtype=x_host.dtype)
+    y_dev = torch.empty((m, n), device=dev, dtype=x_host.dtype)
+    rows = -(-m // chunks)
+    rows = -(-rows // 128) * 128  # whole 128-row MMA tiles per chunk
+    s_in.wait_stream(compute)
+    s_out.wait_stream(compute)
+    for r0 in range(0, m, rows):
+        r1 = min(m, r0 + rows)
+        with torch.cuda.stream(s_in):
+            x_dev[r0:r1].copy_(x_host[r0:r1], non_blocking=True)
+        loaded = s_in.record_event()
+        compute.wait_event(loaded)
+        fused_linear_gelu(x_dev[r0:r1], w, bias, config=config, approximate=approximate, out=y_dev[r0:r1])
+        done = compute.record_event()
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            out[r0:r1].copy_(y_dev[r0:r1], non_blocking=True)
+    # x_dev / y_dev belong to the compute stream's pool: joining the copy
+    # streams back orders their release after the last copy.
+    compute.wait_stream(s_in)
+    compute.wait_stream(s_out)
+    return out
+
+
 def linear_gelu_reference(
     x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, approximate: str = "tanh"
 ) -> torch.Tensor:

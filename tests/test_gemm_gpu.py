@@ -340,3 +340,31 @@ def test_gemv_default_kernel_choice():
     assert default_config(2, 11008, 4096, torch.bfloat16)["KERNEL"] == 3
     assert default_config(4, 11008, 4096, torch.float16)["KERNEL"] == 1
     assert default_config(16, 11008, 4096, torch.float16)["KERNEL"] == 1
+
+
+# ------------------------------------------------------------------ host-buffer fused linear
+@pytest.mark.parametrize("m", [1, 300, 1024, 1500])
+def test_fused_linear_host_matches_the_oracle(m, device):
+    """Row chunks (a partial last chunk, a single chunk, M=1) against the oracle."""
+    from kernelo_b200.kernels.fused_linear import fused_linear_gelu_host
+
+    gen = torch.Generator().manual_seed(m)
+    x = torch.randn(m, 512, generator=gen).bfloat16()
+    w = (torch.randn(768, 512, generator=gen) * 512 ** -0.5).bfloat16().to(device)
+    b = (torch.randn(768, generator=gen) * 0.3).bfloat16().to(device)
+    out = torch.empty(m, 768, dtype=torch.bfloat16, pin_memory=True)
+    got = fused_linear_gelu_host(x.pin_memory(), w.t(), b, approximate="none", out=out, chunks=3)
+    torch.cuda.current_stream().synchronize()
+    assert got is out
+    gate(ref.linear_gelu_ref(host(x), host(w.t()), host(b), "none"), got, torch.bfloat16, context=f"M={m}")
+
+
+def test_fused_linear_host_validation(device):
+    from kernelo_b200.kernels.fused_linear import fused_linear_gelu_host
+
+    w = torch.randn(64, 32, device=device, dtype=torch.bfloat16)
+    b = torch.randn(32, device=device, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="pinned"):
+        fused_linear_gelu_host(torch.randn(8, 64).bfloat16(), w, b)
+    with pytest.raises(ValueError, match="out must be"):
+        fused_linear_gelu_host(torch.randn(8, 64).bfloat16().pin_memory(), w, b, out=torch.empty(8, 32).bfloat16())
