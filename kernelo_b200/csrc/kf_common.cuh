@@ -291,12 +291,64 @@ __host__ __device__ constexpr uint32_t instr_desc_f16(uint32_t fmt, uint32_t a_m
 // GELU, written from its definition: exact form x * Phi(x) with
 // Phi(x) = (1 + erf(x / sqrt(2))) / 2, and the tanh approximation
 // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))). CUDA's erff/tanhf are called.
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+// Hardware approximations (PTX ISA: relative error about 2^-22 / 2^-23;
+// subnormal results flush to zero).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
+// The same without flushing: subnormal results are kept, which GELU's far
+// negative tail needs (a bf16 output still resolves values near 1e-38).
+__device__ __forceinline__ float ex2_sub(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Exact GELU, x * Phi(x), Phi(x) = erfc(-x / sqrt 2) / 2.
+// erfc comes from the Chebyshev fit of W. H. Press et al., Numerical Recipes,
+// 2nd ed., section 6.2 ("erfcc"): for z >= 0, with t = 1 / (1 + z/2),
+//   erfc(z) = t * exp(-z^2 + P(t)),  P a degree-9 polynomial,
+// with fractional error below 1.2e-7 over the whole range -- so Phi keeps its
+// relative accuracy in the negative tail, where GELU is tiny. With the
+// hardware reciprocal and exponential the result stays within about 2e-7
+// relative (plus 2^-24 times |z^2| from rounding the exponent), far below
+// half an ulp of an fp16 or bf16 output. For x >= 0, Phi = 1 - erfc(z) / 2.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float z = fabsf(x) * 0.70710678118654752440f;
+  const float t = rcp_ftz(fmaf(0.5f, z, 1.0f));
+  float p = fmaf(t, 0.17087277f, -0.82215223f);
+  p = fmaf(t, p, 1.48851587f);
+  p = fmaf(t, p, -1.13520398f);
+  p = fmaf(t, p, 0.27886807f);
+  p = fmaf(t, p, -0.18628806f);
+  p = fmaf(t, p, 0.09678418f);
+  p = fmaf(t, p, 0.37409196f);
+  p = fmaf(t, p, 1.00002368f);
+  p = fmaf(t, p, -1.26551223f);
+  const float half_erfc = 0.5f * t * ex2_sub(fmaf(-z, z, p) * 1.4426950408889634f);
+  return x * (x >= 0.0f ? 1.0f - half_erfc : half_erfc);
+}
+
+// tanh GELU, 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715 x^3),
+// through the identity 1 + tanh(u) = 2 / (1 + exp(-2u)). With e = exp(-2|u|)
+// in (0, 1]:
+//   gelu = x / (1 + e)      for u >= 0,
+//   gelu = x e / (1 + e)    for u < 0,
+// which never overflows and keeps relative accuracy at both ends (no
+// 1 + tanh cancellation for u << 0). The constants define the function
+// (kernelforge/kernels/fused_linear.py).
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float inner = 0.79788456080286535588f * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(inner));
+  const float u = 0.79788456080286535588f * fmaf(0.044715f * x, x * x, x);
+  const float e = ex2_sub(fabsf(u) * (-2.0f * 1.4426950408889634f));
+  const float r = rcp_ftz(1.0f + e);
+  return x * (u >= 0.0f ? r : e * r);
 }
 
 template <int EPI>

@@ -199,14 +199,14 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
             vec_floats(raw[j], f);
 #pragma unroll
             for (int e = 0; e < VE; ++e) {
-              const float t = ex2_approx(fmaf(f[e], kRowLog2e, -mb));
+              const float t = ex2_ftz(fmaf(f[e], kRowLog2e, -mb));
               if constexpr (KEEP_EV) ev[j * VE + e] = t;
               s += t;
             }
           }
         }
-        if (has_head) s += (eh = ex2_approx(fmaf(xh, kRowLog2e, -mb)));
-        if (has_tail) s += (et = ex2_approx(fmaf(xt, kRowLog2e, -mb)));
+        if (has_head) s += (eh = ex2_ftz(fmaf(xh, kRowLog2e, -mb)));
+        if (has_tail) s += (et = ex2_ftz(fmaf(xt, kRowLog2e, -mb)));
       }
       part = warp_max_sum(m_thr, s);
     } else {
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
     if constexpr (OP == OP_SOFTMAX) {
       // exp(x - M) / S = exp(x - m_thr) * (exp(m_thr - M) / S)
       const float factor =
-          m_thr == -INFINITY ? 0.0f : ex2_approx((m_thr - tot.x) * kRowLog2e) / tot.y;
+          m_thr == -INFINITY ? 0.0f : ex2_ftz((m_thr - tot.x) * kRowLog2e) / tot.y;
       const float mb = m_thr * kRowLog2e;
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
           } else {
             vec_floats(raw[j], o);
 #pragma unroll
-            for (int e = 0; e < VE; ++e) o[e] = ex2_approx(fmaf(o[e], kRowLog2e, -mb)) * factor;
+            for (int e = 0; e < VE; ++e) o[e] = ex2_ftz(fmaf(o[e], kRowLog2e, -mb)) * factor;
           }
           store_stream(yv + v, vec_from_floats<T, VE>(o));
         }

@@ -16,15 +16,12 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "kf_common.cuh"  // ex2_ftz
+
 namespace kf {
 
 constexpr float kRowLog2e = 1.4426950408889634f;
 
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 template <typename P>
 __device__ __forceinline__ P bitcast_pair(uint32_t u) {
@@ -146,7 +143,7 @@ __device__ __forceinline__ float2 warp_max_sum(float m, float s) {
   float M = m;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float t = m == -INFINITY ? 0.0f : s * ex2_approx((m - M) * kRowLog2e);
+  float t = m == -INFINITY ? 0.0f : s * ex2_ftz((m - M) * kRowLog2e);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
   return make_float2(M, t);

@@ -270,14 +270,14 @@ __global__ void __launch_bounds__(STREAM_THREADS, stream_min_blocks<NV>())
             to_floats<T>(raw[j], f);
 #pragma unroll
             for (int k = 0; k < VE; ++k) {
-              const float t = ex2_approx(fmaf(f[k], kRowLog2e, -mb));
+              const float t = ex2_ftz(fmaf(f[k], kRowLog2e, -mb));
               if constexpr (KEEP_EV) ev[j * VE + k] = t;
               s += t;
             }
           }
         }
-        if (has_head) s += (eh = ex2_approx(fmaf(xh, kRowLog2e, -mb)));
-        if (has_tail) s += (et = ex2_approx(fmaf(xt, kRowLog2e, -mb)));
+        if (has_head) s += (eh = ex2_ftz(fmaf(xh, kRowLog2e, -mb)));
+        if (has_tail) s += (et = ex2_ftz(fmaf(xt, kRowLog2e, -mb)));
       }
       part = warp_max_sum(m_thr, s);
     } else {
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, stream_min_blocks<NV>())
     if constexpr (OP == OP_SOFTMAX) {
       // exp(x - M) / S = exp(x - m_thr) * (exp(m_thr - M) / S)
       const float factor =
-          m_thr == -INFINITY ? 0.0f : ex2_approx((m_thr - part.x) * kRowLog2e) / part.y;
+          m_thr == -INFINITY ? 0.0f : ex2_ftz((m_thr - part.x) * kRowLog2e) / part.y;
       const float mb = m_thr * kRowLog2e;
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, stream_min_blocks<NV>())
           } else {
             to_floats<T>(raw[j], o);
 #pragma unroll
-            for (int k = 0; k < VE; ++k) o[k] = ex2_approx(fmaf(o[k], kRowLog2e, -mb)) * factor;
+            for (int k = 0; k < VE; ++k) o[k] = ex2_ftz(fmaf(o[k], kRowLog2e, -mb)) * factor;
           }
           __stcs(yv + v, from_floats<T>(o));
         }

@@ -368,3 +368,32 @@ def test_fused_linear_host_validation(device):
         fused_linear_gelu_host(torch.randn(8, 64).bfloat16(), w, b)
     with pytest.raises(ValueError, match="out must be"):
         fused_linear_gelu_host(torch.randn(8, 64).bfloat16().pin_memory(), w, b, out=torch.empty(8, 32).bfloat16())
+
+
+# ------------------------------------------------------------------ epilogue GELU accuracy
+@pytest.mark.parametrize("approximate", ["none", "tanh"])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_epilogue_gelu_within_one_ulp_of_torch(approximate, dtype, device):
+    """x = 0 makes the fused output gelu(bias): sweep bias over [-12, 12]
+    (negative tail included) and compare each element with GELU evaluated in
+    float64 and rounded to the output dtype -- at most one unit in the last
+    place apart. The float64 reference avoids the cancellation of 1 + erf and
+    1 + tanh in the negative tail (torch's fp32 GELU loses its relative
+    accuracy there): 0.5 x erfc(-x / sqrt 2), and x / (1 + exp(-2u))."""
+    n = 11008
+    bias = torch.linspace(-12, 12, n, device=device).to(dtype)
+    x = torch.zeros(128, 64, device=device, dtype=dtype)
+    w = torch.randn(n, 64, device=device, dtype=dtype)
+    out = fused_linear_gelu(x, w.t(), bias, approximate=approximate)[0].float()
+    xd = bias.double()
+    if approximate == "tanh":
+        u = (2 / torch.pi) ** 0.5 * (xd + 0.044715 * xd ** 3)
+        ref64 = xd / (1 + torch.exp(-2 * u))
+    else:
+        ref64 = 0.5 * xd * torch.special.erfc(-xd / 2 ** 0.5)
+    ref = ref64.to(dtype).float()
+    mant = 10 if dtype == torch.float16 else 7
+    tiny = 2.0 ** (-14 if dtype == torch.float16 else -126)
+    ulp = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(tiny))) - mant)
+    worst = float(((out - ref).abs() / ulp).max())
+    assert worst <= 1.0, f"{worst:.2f} ulp"
