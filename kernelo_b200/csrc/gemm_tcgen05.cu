@@ -198,7 +198,11 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0
       load_bias16<T>(bias, col0, p.N, b);
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = apply_epilogue<EPI>(acc[j], b[j]);
+    for (int j = 0; j < 16; j += 2) {
+      const float2 r = apply_epilogue2<EPI>(make_float2(acc[j], acc[j + 1]), make_float2(b[j], b[j + 1]));
+      v[j] = r.x;
+      v[j + 1] = r.y;
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = acc[j];

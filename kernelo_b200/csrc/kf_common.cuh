@@ -351,6 +351,89 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return x * (u >= 0.0f ? r : e * r);
 }
 
+// ---- packed fp32x2 arithmetic (sm_100: one instruction for two lanes)
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return make_float2(a, b);
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_splat(float a) { return f2_pack(a, a); }
+
+// gelu_erf on two values: the same operations and roundings as gelu_erf,
+// with the polynomial and the scalings done pairwise.
+__device__ __forceinline__ float2 gelu_erf2(float2 x) {
+  const float z0 = fabsf(x.x) * 0.70710678118654752440f;
+  const float z1 = fabsf(x.y) * 0.70710678118654752440f;
+  const float2 d = f2_unpack(f2_fma(f2_splat(0.5f), f2_pack(z0, z1), f2_splat(1.0f)));
+  const uint64_t t = f2_pack(rcp_ftz(d.x), rcp_ftz(d.y));
+  uint64_t p = f2_fma(t, f2_splat(0.17087277f), f2_splat(-0.82215223f));
+  p = f2_fma(t, p, f2_splat(1.48851587f));
+  p = f2_fma(t, p, f2_splat(-1.13520398f));
+  p = f2_fma(t, p, f2_splat(0.27886807f));
+  p = f2_fma(t, p, f2_splat(-0.18628806f));
+  p = f2_fma(t, p, f2_splat(0.09678418f));
+  p = f2_fma(t, p, f2_splat(0.37409196f));
+  p = f2_fma(t, p, f2_splat(1.00002368f));
+  p = f2_fma(t, p, f2_splat(-1.26551223f));
+  const float2 pf = f2_unpack(p);
+  const uint64_t e = f2_pack(ex2_sub(fmaf(-z0, z0, pf.x) * 1.4426950408889634f),
+                             ex2_sub(fmaf(-z1, z1, pf.y) * 1.4426950408889634f));
+  const float2 he = f2_unpack(f2_mul(f2_mul(f2_splat(0.5f), t), e));
+  const float phi0 = x.x >= 0.0f ? 1.0f - he.x : he.x;
+  const float phi1 = x.y >= 0.0f ? 1.0f - he.y : he.y;
+  return f2_unpack(f2_mul(f2_pack(x.x, x.y), f2_pack(phi0, phi1)));
+}
+
+// gelu_tanh on two values, pairwise where the arithmetic allows.
+__device__ __forceinline__ float2 gelu_tanh2(float2 x) {
+  const uint64_t xv = f2_pack(x.x, x.y);
+  const uint64_t x2 = f2_mul(xv, xv);
+  const uint64_t inner = f2_fma(f2_mul(f2_splat(0.044715f), xv), x2, xv);
+  const float2 u = f2_unpack(f2_mul(f2_splat(0.79788456080286535588f), inner));
+  const float e0 = ex2_sub(fabsf(u.x) * (-2.0f * 1.4426950408889634f));
+  const float e1 = ex2_sub(fabsf(u.y) * (-2.0f * 1.4426950408889634f));
+  const float2 den = f2_unpack(f2_add(f2_pack(e0, e1), f2_splat(1.0f)));
+  const float r0 = rcp_ftz(den.x), r1 = rcp_ftz(den.y);
+  return f2_unpack(f2_mul(xv, f2_pack(u.x >= 0.0f ? r0 : e0 * r0, u.y >= 0.0f ? r1 : e1 * r1)));
+}
+
+// The epilogue on two adjacent outputs.
+template <int EPI>
+__device__ __forceinline__ float2 apply_epilogue2(float2 acc, float2 bias) {
+  if constexpr (EPI == KF_EPI_NONE) {
+    return acc;
+  } else {
+    const float2 v = f2_unpack(f2_add(f2_pack(acc.x, acc.y), f2_pack(bias.x, bias.y)));
+    if constexpr (EPI == KF_EPI_BIAS) {
+      return v;
+    } else if constexpr (EPI == KF_EPI_BIAS_GELU_TANH) {
+      return gelu_tanh2(v);
+    } else {
+      return gelu_erf2(v);
+    }
+  }
+}
+
 template <int EPI>
 __device__ __forceinline__ float apply_epilogue(float acc, float bias) {
   if constexpr (EPI == KF_EPI_NONE) {

@@ -127,13 +127,16 @@ def default_tcgen05_config(
     tiles = -(-m_k // TC_BLOCK_M) * -(-n_k // block_n)
     k_blocks = -(-k // block_k)
     stream_k = 1 if (cg == 1 and tiles < sm_count and k_blocks >= 4) else 2
+    # A panels of one raster group within ~48 MB of L2 (mirrors api.cu)
+    tile_rows = TC_BLOCK_M * cg
+    group_m = max(1, min(-(-m_k // tile_rows), (48 << 20) // max(1, tile_rows * k * 2)))
     return KernelConfig(
         operation,
         KERNEL=KERNEL_TCGEN05,
         BLOCK_M=TC_BLOCK_M * cg,
         BLOCK_N=block_n,
         BLOCK_K=block_k,
-        GROUP_M=8,
+        GROUP_M=group_m,
         num_stages=stages,
         STREAM_K=stream_k,
         SWAP_AB=1 if swap else 2,

@@ -189,7 +189,8 @@ class _Sm100GemmSpace(SearchSpace):
     BLOCK_K = (32, 64, 128)
     NUM_STAGES = (2, 4, 6)
     CLUSTERS = ((1, 1), (2, 1), (1, 2), (2, 2))
-    GROUP_M = 8
+    #: L2 the A panels of one raster group may take (the library default's rule).
+    GROUP_L2_BYTES = 48 << 20
     #: (BLOCK_M, BLOCK_N, BLOCK_K) of the CUDA-core kernel's instantiations.
     SIMT_TILES = ((128, 128, 8), (64, 64, 16), (128, 64, 16))
     #: How B is laid out for this operator's canonical inputs.
@@ -198,6 +199,14 @@ class _Sm100GemmSpace(SearchSpace):
     def dims(self, problem: Problem) -> tuple[int, int, int]:
         d = problem.dims_dict
         return d["M"], d["N"], d["K"]
+
+    def group_m(self, block_m: int, problem: Problem) -> int:
+        """Raster group width: as many M tiles as keep their A panels within
+        GROUP_L2_BYTES of L2 (so each group streams B once)."""
+        m, n, k = self.dims(problem)
+        m_k = n if gc.default_swap(m, n) else m
+        rows = max(block_m, gc.TC_BLOCK_M)
+        return max(1, min(ceil_div(m_k, rows), self.GROUP_L2_BYTES // max(1, rows * k * problem.itemsize)))
 
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
         m, n, _ = self.dims(problem)
@@ -211,7 +220,7 @@ class _Sm100GemmSpace(SearchSpace):
                 BLOCK_M=bm,
                 BLOCK_N=bn,
                 BLOCK_K=bk,
-                GROUP_M=self.GROUP_M,
+                GROUP_M=self.group_m(bm, problem),
                 num_stages=stages,
                 STREAM_K=0,
                 SWAP_AB=swap,
