@@ -86,7 +86,11 @@ typedef struct kf_gemm_config {
   int32_t stages;    /* tcgen05 shared-memory ring depth                             */
   int32_t group_m;   /* grouped (L2-aware) raster width, in M tiles                  */
   int32_t stream_k;  /* tcgen05: 0 = library choice, 1 = split K over the persistent
-                        grid (stream-K), 2 = whole tiles only                          */
+                        grid (stream-K), 2 = whole tiles only, 3 = split tail:
+                        whole tiles for the full waves, the last partial wave as
+                        half-width tiles (no workspace). A library choice that
+                        needs workspace the call did not pass falls back to
+                        whole tiles.                                               */
   int32_t swap_ab;   /* tcgen05: 0 = library choice, 1 = compute C^T = B^T.A^T
                         (skinny M), 2 = never swap                                     */
   int32_t cluster_m; /* 1, or 2 with block_m 256 (the SM pair is a 2x1 cluster)      */

@@ -164,9 +164,14 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
     c.group_m = static_cast<int32_t>(gm);
   }
   if (c.stream_k == 0) {
-    const int64_t tiles = ((m + 127) / 128) * ((n + c.block_n - 1) / c.block_n);
+    // Fewer one-SM tiles than SMs: all stream-K. Otherwise the split tail:
+    // whole tiles for the full waves, the last partial wave as half-width
+    // tiles (at 4096x11008x4096: 688 pair tiles on 74 pairs leave 22 for the
+    // last wave; a stream-K tail measured slower there, its fix-up epilogues
+    // all falling at the end).
+    const int64_t tiles = ((m + 128LL * cg - 1) / (128LL * cg)) * ((n + c.block_n - 1) / c.block_n);
     const int64_t kb = (g.K + c.block_k - 1) / c.block_k;
-    c.stream_k = (cg == 1 && tiles < sm_count && kb >= 4) ? 1 : 2;
+    c.stream_k = kb < 4 ? 2 : (cg == 1 && tiles < sm_count) ? 1 : 3;
   }
   if (cg == 2 && c.cluster_m == 0) c.cluster_m = 2;
   return c;
@@ -194,8 +199,16 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
   DeviceInfo* dev = nullptr;
   rc = device_info(device, &dev);
   if (rc != KF_OK) return rc;
-  const kf_gemm_config cfg = resolve_gemm_config(g, user, dev->sm_count);
+  kf_gemm_config cfg = resolve_gemm_config(g, user, dev->sm_count);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cfg.kernel == KF_GEMM_TCGEN05 && (user == nullptr || user->stream_k == 0)) {
+    const int64_t need = gemm_tcgen05_workspace_bytes(g, cfg, *dev);
+    if (need > 0 && (g.workspace == nullptr || g.workspace_bytes < need)) {
+      // The library's own stream-K choice never makes a call without (enough)
+      // workspace fail: it runs whole tiles instead. An explicit request errors.
+      cfg.stream_k = 2;
+    }
+  }
   if (cfg.kernel == KF_GEMM_TCGEN05) return launch_gemm_tcgen05(g, cfg, *dev, s);
   if (cfg.kernel == KF_GEMM_SIMT) return launch_gemm_simt(g, cfg, s);
   return set_error(KF_ERR_INVALID_CONFIG, "unknown GEMM kernel code");

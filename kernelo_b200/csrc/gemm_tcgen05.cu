@@ -72,7 +72,16 @@ struct TcParams {
   int a_mn, b_mn;
   int tiles_m, tiles_n, kb_per_tile;
   long long total_iters;
-  int stream_k;
+  // Schedule: tiles [0, dp_tiles) go whole to unit t % units. Then either
+  // (split tail) the remaining tiles are cut into two half-width tiles each,
+  // dealt out the same way -- the last partial wave takes half as long, with
+  // no K split and no fix-up -- or (stream-K) the k-block iterations
+  // [sk_base, sk_base + sk_iters) of the remaining tiles are split evenly over
+  // the units with a fixed-order fix-up.
+  long long dp_tiles, sk_base, sk_iters;
+  int tail_halves;  // half-width tiles after the whole ones (split tail)
+  int stream_k;     // sk_iters > 0
+  uint32_t idesc_half;
   void* c;
   long long sc_r, sc_c;
   const void* bias;
@@ -88,42 +97,55 @@ struct TcParams {
 struct Segment {
   int tile;
   int kb0, kb1;
+  int half;  // -1: a whole tile; 0 / 1: the first / second half-width tile of it
 };
 
 struct Cursor {
-  long long next, end, begin;
+  long long dp_next;          // next whole tile
+  long long next, end, begin;  // stream-K iteration range [begin, end)
 };
+
+// First k-block iteration of a unit's stream-K range.
+__device__ __forceinline__ long long sk_begin_of(const TcParams& p, long long unit, long long units) {
+  return p.sk_base + (p.sk_iters * unit) / units;
+}
 
 // `unit` is the CTA (CG = 1) or the CTA pair (CG = 2); `units` their number.
 __device__ __forceinline__ void cursor_init(const TcParams& p, Cursor& c, int unit, int units) {
-  if (p.stream_k) {
-    c.begin = (p.total_iters * unit) / units;
-    c.end = (p.total_iters * (unit + 1)) / units;
-    c.next = c.begin;
-  } else {
-    c.begin = 0;
-    c.end = static_cast<long long>(p.tiles_m) * p.tiles_n;
-    c.next = unit;
-  }
+  c.dp_next = unit;
+  c.begin = sk_begin_of(p, unit, units);
+  c.end = sk_begin_of(p, unit + 1, units);
+  c.next = c.begin;
 }
 
 __device__ __forceinline__ bool cursor_next(const TcParams& p, Cursor& c, Segment& s, int units) {
-  if (c.next >= c.end) return false;
-  if (p.stream_k) {
-    const long long tile = c.next / p.kb_per_tile;
-    const long long tile_start = tile * p.kb_per_tile;
-    long long stop = c.end - tile_start;
-    if (stop > p.kb_per_tile) stop = p.kb_per_tile;
-    s.tile = static_cast<int>(tile);
-    s.kb0 = static_cast<int>(c.next - tile_start);
-    s.kb1 = static_cast<int>(stop);
-    c.next = tile_start + stop;
-  } else {
-    s.tile = static_cast<int>(c.next);
+  if (c.dp_next < p.dp_tiles) {
+    s.tile = static_cast<int>(c.dp_next);
     s.kb0 = 0;
     s.kb1 = p.kb_per_tile;
-    c.next += units;
+    s.half = -1;
+    c.dp_next += units;
+    return true;
   }
+  if (c.dp_next < p.dp_tiles + p.tail_halves) {
+    const long long j = c.dp_next - p.dp_tiles;
+    s.tile = static_cast<int>(p.dp_tiles + j / 2);
+    s.half = static_cast<int>(j & 1);
+    s.kb0 = 0;
+    s.kb1 = p.kb_per_tile;
+    c.dp_next += units;
+    return true;
+  }
+  s.half = -1;
+  if (c.next >= c.end) return false;
+  const long long tile = c.next / p.kb_per_tile;
+  const long long tile_start = tile * p.kb_per_tile;
+  long long stop = c.end - tile_start;
+  if (stop > p.kb_per_tile) stop = p.kb_per_tile;
+  s.tile = static_cast<int>(tile);
+  s.kb0 = static_cast<int>(c.next - tile_start);
+  s.kb1 = static_cast<int>(stop);
+  c.next = tile_start + stop;
   return true;
 }
 
@@ -229,7 +251,8 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0
 template <typename T, int EPI, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
-                   const __grid_constant__ CUtensorMap tm_b, const TcParams p) {
+                   const __grid_constant__ CUtensorMap tm_b,
+                   const __grid_constant__ CUtensorMap tm_b_half, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -273,6 +296,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
+    if (p.tail_halves) tma_prefetch_desc(&tm_b_half);
   }
   if (warp == 1) {
     if constexpr (CG == 2) {
@@ -302,13 +326,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t stage = 0, phase = 0;
       long long issued = 0;
       bool ok = true;
-      const uint32_t tx_bytes = (p.a_stage_bytes + p.b_stage_bytes) * CG;
-      const int b_rows = p.bn / CG;  // B rows this CTA stages
       while (ok && cursor_next(p, cur, seg, units)) {
         int m_blk, n_blk;
         tile_coords(p, seg.tile, m_blk, n_blk);
+        // A half-width tile stages half the B rows, through the half-height map.
+        const bool half = seg.half >= 0;
+        const int seg_bn = half ? p.bn / 2 : p.bn;
+        const int b_rows = seg_bn / CG;  // B rows this CTA stages
+        const CUtensorMap* map_b = half ? &tm_b_half : &tm_b;
+        const uint32_t tx_bytes =
+            (p.a_stage_bytes + static_cast<uint32_t>(b_rows * p.bk * 2)) * CG;
         const int m0 = m_blk * (BM * CG) + BM * static_cast<int>(crank);
-        const int n0 = n_blk * p.bn + b_rows * static_cast<int>(crank);
+        const int n0 = n_blk * p.bn + (half ? seg.half * seg_bn : 0) + b_rows * static_cast<int>(crank);
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag, p.status, SITE_TMA_EMPTY)) {
             ok = false;
@@ -330,10 +359,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (!p.b_mn) {
               for (int j = 0; j < p.bk / 64; ++j)
-                tma_load_2d_pair(b_dst + j * (b_rows * 128), &tm_b, lb, k0 + 64 * j, n0);
+                tma_load_2d_pair(b_dst + j * (b_rows * 128), map_b, lb, k0 + 64 * j, n0);
             } else {
               for (int i = 0; i < b_rows / 64; ++i)
-                tma_load_2d_pair(b_dst + i * (p.bk * 128), &tm_b, lb, n0 + 64 * i, k0);
+                tma_load_2d_pair(b_dst + i * (p.bk * 128), map_b, lb, n0 + 64 * i, k0);
             }
           } else {
             mbar_arrive_expect_tx(fb, tx_bytes);
@@ -346,10 +375,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (!p.b_mn) {
               for (int j = 0; j < p.bk / 64; ++j)
-                tma_load_2d(b_dst + j * (b_rows * 128), &tm_b, fb, k0 + 64 * j, n0);
+                tma_load_2d(b_dst + j * (b_rows * 128), map_b, fb, k0 + 64 * j, n0);
             } else {
               for (int i = 0; i < b_rows / 64; ++i)
-                tma_load_2d(b_dst + i * (p.bk * 128), &tm_b, fb, n0 + 64 * i, k0);
+                tma_load_2d(b_dst + i * (p.bk * 128), map_b, fb, n0 + 64 * i, k0);
             }
           }
           ++issued;
@@ -375,7 +404,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0 && leader) {
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
-      const int b_rows = p.bn / CG;
       // Start-address steps in 16-byte units. K-major operands: a K=16 slice is
       // 32 bytes inside a 128-byte swizzle row, and the next 64-element K atom
       // starts `rows * 128` bytes on. MN-major operands: a K=16 slice is 16
@@ -383,7 +411,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t a_k_step = p.a_mn ? 2048 / 16 : 32 / 16;
       const uint32_t b_k_step = p.b_mn ? 2048 / 16 : 32 / 16;
       const uint32_t a_atom_step = p.a_mn ? 4 * 2048 / 16 : (BM * 128) / 16;
-      const uint32_t b_atom_step = p.b_mn ? 4 * 2048 / 16 : static_cast<uint32_t>(b_rows * 128) / 16;
       const uint32_t a_lbo = p.a_mn ? static_cast<uint32_t>(p.bk * 128) : 16u;
       const uint32_t b_lbo = p.b_mn ? static_cast<uint32_t>(p.bk * 128) : 16u;
       while (ok && cursor_next(p, cur, seg, units)) {
@@ -392,6 +419,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
+        // A half-width tile: half the B rows per K atom and an N/2 instruction.
+        const int b_rows = (seg.half >= 0 ? p.bn / 2 : p.bn) / CG;
+        const uint32_t b_atom_step =
+            p.b_mn ? 4 * 2048 / 16 : static_cast<uint32_t>(b_rows * 128) / 16;
+        const uint32_t idesc = seg.half >= 0 ? p.idesc_half : p.idesc;
         const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(p.bn);
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
           if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, p.status, SITE_MMA_FULL)) {
@@ -412,9 +444,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(atom * b_atom_step + kk * b_k_step);
               const uint32_t accumulate = (kb > seg.kb0 || atom > 0 || kk > 0) ? 1u : 0u;
               if constexpr (CG == 2) {
-                tc_mma_f16_pair(d_tmem, a_desc, b_desc, p.idesc, accumulate);
+                tc_mma_f16_pair(d_tmem, a_desc, b_desc, idesc, accumulate);
               } else {
-                tc_mma_f16(d_tmem, a_desc, b_desc, p.idesc, accumulate);
+                tc_mma_f16(d_tmem, a_desc, b_desc, idesc, accumulate);
               }
             }
           }
@@ -457,10 +489,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // Two warps share each quadrant: the first takes the first half of the
     // tile's 16-column chunks, the second the rest.
     const int half = (warp - EPI_WARP0) / 4;
-    const int chunks = p.bn / 16;
-    const int chunk_split = (chunks + 1) / 2;
-    const int c_begin = half == 0 ? 0 : chunk_split * 16;
-    const int c_end = half == 0 ? chunk_split * 16 : p.bn;
     // The MMA leader's tmem_empty barriers (this CTA's own when CG = 1).
     const uint32_t tempty_leader = CG == 2 ? mapa_shared(tempty0, 0) : tempty0;
     uint32_t acc = 0, acc_phase = 0;
@@ -469,8 +497,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       int m_blk, n_blk;
       tile_coords(p, seg.tile, m_blk, n_blk);
+      const int seg_bn = seg.half >= 0 ? p.bn / 2 : p.bn;
+      const int chunks = seg_bn / 16;
+      const int chunk_split = (chunks + 1) / 2;
+      const int c_begin = half == 0 ? 0 : chunk_split * 16;
+      const int c_end = half == 0 ? chunk_split * 16 : seg_bn;
       const int row = m_blk * (BM * CG) + BM * static_cast<int>(crank) + row_in_tile;
-      const int col_base = n_blk * p.bn;
+      const int col_base = n_blk * p.bn + (seg.half >= 0 ? seg.half * seg_bn : 0);
       const uint32_t t_acc =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * static_cast<uint32_t>(p.bn);
       const bool whole_tile = seg.kb0 == 0 && seg.kb1 == p.kb_per_tile;
@@ -487,57 +520,91 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (two) store_chunk<T, EPI>(p, row, col_base + c + 16, reinterpret_cast<const float*>(r1));
         }
       } else {
-        // Stream-K fix-up for a tile shared between CTAs (CG = 1 only).
+        // Stream-K fix-up for a tile shared between units. Each CTA fixes up
+        // its own 128 rows: its own counter and its own partial slots (a
+        // unit's first and last segment), so the two CTAs of a pair proceed
+        // independently.
         const long long grid = units;
         const long long t_start = static_cast<long long>(seg.tile) * p.kb_per_tile;
-        const long long c_first = owner_of(t_start, p.total_iters, grid);
-        const long long c_last = owner_of(t_start + p.kb_per_tile - 1, p.total_iters, grid);
+        const long long rel = t_start - p.sk_base;
+        const long long c_first = owner_of(rel, p.sk_iters, grid);
+        const long long c_last = owner_of(rel + p.kb_per_tile - 1, p.sk_iters, grid);
         const long long me = unit;
         const size_t slot_elems = static_cast<size_t>(p.bn) * BM;
-        const long long my_slot = 2 * me + (cur.begin >= t_start ? 0 : 1);
+        const long long my_slot = 2 * (me * CG + crank) + (cur.begin >= t_start ? 0 : 1);
         float* mine = p.partials + static_cast<size_t>(my_slot) * slot_elems;
+        int* counter = p.counters + static_cast<size_t>(seg.tile) * CG + crank;
+        // Partial tiles are laid out [16-column chunk][row][16]: a lane's 16
+        // columns are 64 contiguous bytes and a warp's stores cover 2 KB.
         for (int c = c_begin; c < c_end; c += 16) {
           uint32_t r[16];
           __syncwarp();
           tmem_ld_16(t_acc + c, r);
           tmem_ld_wait();
+          float4* dst = reinterpret_cast<float4*>(mine + (static_cast<size_t>(c / 16) * BM + row_in_tile) * 16);
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            __stcg(mine + static_cast<size_t>(c + j) * BM + row_in_tile, __uint_as_float(r[j]));
+          for (int q = 0; q < 4; ++q)
+            __stcg(dst + q, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
         }
         __threadfence();
         epi_bar_sync();
         if (ethread == 0) {
-          const int arrived = atomicAdd(&p.counters[seg.tile], 1);
+          const int arrived = atomicAdd(counter, 1);
           *last_flag = (arrived == static_cast<int>(c_last - c_first)) ? 1u : 0u;
         }
         epi_bar_sync();
         if (*last_flag) {
           __threadfence();
+          // The contributors' partials of a chunk are loaded FIX_BATCH at a
+          // time, all loads in flight together (one L2 round trip per batch,
+          // not per contributor), then summed in contributor order -- the
+          // same fixed order, so the result stays deterministic.
+          constexpr int FIX_BATCH = 2;
           for (int c = c_begin; c < c_end; c += 16) {
             uint32_t r[16];
             __syncwarp();
             tmem_ld_16(t_acc + c, r);
-            tmem_ld_wait();
             float sum[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
-            for (long long cc = c_first; cc <= c_last; ++cc) {
-              if (cc == me) {
+            for (long long cc0 = c_first; cc0 <= c_last; cc0 += FIX_BATCH) {
+              float4 v[FIX_BATCH][4];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) sum[j] += __uint_as_float(r[j]);
-              } else {
-                const long long cc_begin = (p.total_iters * cc) / grid;
-                const long long slot = 2 * cc + (cc_begin >= t_start ? 0 : 1);
-                const float* part = p.partials + static_cast<size_t>(slot) * slot_elems;
+              for (int bi = 0; bi < FIX_BATCH; ++bi) {
+                const long long cc = cc0 + bi;
+                if (cc <= c_last && cc != me) {
+                  const long long cc_begin = sk_begin_of(p, cc, grid);
+                  const long long slot = 2 * (cc * CG + crank) + (cc_begin >= t_start ? 0 : 1);
+                  const float4* part = reinterpret_cast<const float4*>(
+                      p.partials + static_cast<size_t>(slot) * slot_elems +
+                      (static_cast<size_t>(c / 16) * BM + row_in_tile) * 16);
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                  sum[j] += __ldcg(part + static_cast<size_t>(c + j) * BM + row_in_tile);
+                  for (int q = 0; q < 4; ++q) v[bi][q] = __ldcg(part + q);
+                }
+              }
+              if (cc0 == c_first) tmem_ld_wait();
+#pragma unroll
+              for (int bi = 0; bi < FIX_BATCH; ++bi) {
+                const long long cc = cc0 + bi;
+                if (cc > c_last) break;
+                if (cc == me) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) sum[j] += __uint_as_float(r[j]);
+                } else {
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    sum[4 * q] += v[bi][q].x;
+                    sum[4 * q + 1] += v[bi][q].y;
+                    sum[4 * q + 2] += v[bi][q].z;
+                    sum[4 * q + 3] += v[bi][q].w;
+                  }
+                }
               }
             }
             store_chunk<T, EPI>(p, row, col_base + c, sum);
           }
-          if (ethread == 0) p.counters[seg.tile] = 0;  // leave the workspace clean
+          if (ethread == 0) *counter = 0;  // leave the workspace clean
         }
         epi_bar_sync();
       }
@@ -715,8 +782,8 @@ int validate_config(const kf_gemm_config& cfg, int b_mn, std::string* why) {
     *why = "clusters beyond the SM pair of a BLOCK_M=256 tile are not implemented";
     return KF_ERR_INVALID_CONFIG;
   }
-  if (cg == 2 && cfg.stream_k == 1) {
-    *why = "stream-K is implemented for one-SM (BLOCK_M=128) tiles only";
+  if (cfg.stream_k < 0 || cfg.stream_k > 3) {
+    *why = "stream_k must be 0 (library choice), 1 (all), 2 (off) or 3 (split tail)";
     return KF_ERR_INVALID_CONFIG;
   }
   if (cfg.group_m < 1) {
@@ -764,6 +831,7 @@ int64_t gemm_tcgen05_workspace_bytes(const GemmArgs& g, const kf_gemm_config& cf
                                      const DeviceInfo& dev) {
   (void)g;
   if (cfg.stream_k != 1) return 0;
+  // counters, then two fp32 partial tiles (128 rows x BLOCK_N) per CTA
   const int grid = cfg.num_ctas > 0 ? cfg.num_ctas : dev.sm_count;
   return SK_COUNTER_BYTES + 2LL * grid * cfg.block_n * BM * 4;
 }
@@ -792,13 +860,22 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
                                                 std::to_string(dev.max_smem_optin));
   const int64_t smem_request = smem < MIN_SMEM_PER_CTA ? MIN_SMEM_PER_CTA : smem;
 
-  CUtensorMap tm_a, tm_b;
+  CUtensorMap tm_a, tm_b, tm_b_half;
   rc = a_major == 0 ? encode_map(&tm_a, g.dtype, v.a, g.K, v.M, v.sa_r, 64, BM)
                     : encode_map(&tm_a, g.dtype, v.a, v.M, g.K, v.sa_k, 64, bk);
   if (rc != KF_OK) return rc;
   rc = b_major == 0 ? encode_map(&tm_b, g.dtype, v.b, g.K, v.N, v.sb_c, 64, b_rows)
                     : encode_map(&tm_b, g.dtype, v.b, v.N, g.K, v.sb_k, 64, bk);
   if (rc != KF_OK) return rc;
+  // Half-width tail tiles: an N/2 MMA needs N/2 a multiple of 16 per CTA pair
+  // share, and MN-major B boxes stay 64 columns wide.
+  const bool split_ok = cfg.stream_k == 3 && (bn / 2) % (16 * cg) == 0 &&
+                        (b_major == 0 || (b_rows / 2) % 64 == 0);
+  tm_b_half = tm_b;
+  if (split_ok && b_major == 0) {
+    rc = encode_map(&tm_b_half, g.dtype, v.b, g.K, v.N, v.sb_c, 64, b_rows / 2);
+    if (rc != KF_OK) return rc;
+  }
 
   TcParams p{};
   p.M = static_cast<int>(v.M);
@@ -815,7 +892,6 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   p.kb_per_tile = static_cast<int>(ceil_div(g.K, bk));
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   p.total_iters = tiles * p.kb_per_tile;
-  p.stream_k = cfg.stream_k == 1 ? 1 : 0;
   p.c = g.c;
   p.sc_r = v.sc_r;
   p.sc_c = v.sc_c;
@@ -824,6 +900,9 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   p.status = dev.status;
   p.idesc = instr_desc_f16(g.dtype == KF_BF16 ? 1u : 0u, static_cast<uint32_t>(a_major),
                            static_cast<uint32_t>(b_major), BM * cg, static_cast<uint32_t>(bn));
+  p.idesc_half = instr_desc_f16(g.dtype == KF_BF16 ? 1u : 0u, static_cast<uint32_t>(a_major),
+                                static_cast<uint32_t>(b_major), BM * cg,
+                                static_cast<uint32_t>(bn / 2));
   p.a_stage_bytes = static_cast<uint32_t>(BM * bk * 2);
   p.b_stage_bytes = static_cast<uint32_t>(b_rows * bk * 2);
   p.tmem_cols = tmem_cols_for(bn);
@@ -857,17 +936,35 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
       if (clusters > 0 && clusters < units) units = clusters;
     }
   }
+  // The schedule: whole tiles; all stream-K; or (split tail) whole tiles for
+  // the full waves and the last partial wave as half-width tiles, which pays
+  // when the halves still fit one round (2 x remainder <= units).
+  long long dp = tiles;
+  p.tail_halves = 0;
+  if (cfg.stream_k == 1) {
+    dp = 0;
+  } else if (split_ok) {
+    const long long rem = tiles % units;
+    if (rem != 0 && 2 * rem <= units && tiles > units) {
+      dp = tiles - rem;
+      p.tail_halves = static_cast<int>(2 * rem);
+    }
+  }
+  p.dp_tiles = dp;
+  p.sk_base = dp * p.kb_per_tile;
+  p.sk_iters = cfg.stream_k == 1 ? tiles * p.kb_per_tile : 0;
+  p.stream_k = p.sk_iters > 0 ? 1 : 0;
   if (p.stream_k) {
-    if (units > p.total_iters) units = static_cast<int>(p.total_iters);
+    if (dp == 0 && units > p.sk_iters) units = static_cast<int>(p.sk_iters);
     const int64_t need = gemm_tcgen05_workspace_bytes(g, cfg, dev);
     if (g.workspace == nullptr || g.workspace_bytes < need)
       return set_error(KF_ERR_WORKSPACE, "stream-K needs " + std::to_string(need) +
                                              " bytes of zero-initialised workspace");
     if ((reinterpret_cast<uintptr_t>(g.workspace) & 255u) != 0)
       return set_error(KF_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-    if (tiles > SK_MAX_TILES)
+    if (tiles * cg > SK_MAX_TILES)
       return set_error(KF_ERR_INVALID_CONFIG, "stream-K takes at most " +
-                                                  std::to_string(SK_MAX_TILES) +
+                                                  std::to_string(SK_MAX_TILES / cg) +
                                                   " output tiles; use whole tiles");
     // Counters first, at a fixed offset: every call finds them where the last
     // call left them (at zero), whatever its tile or grid size.
@@ -879,7 +976,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   if (units < 1) units = 1;
   lc.gridDim = dim3(static_cast<unsigned>(units * cg));
 
-  void* args[] = {&tm_a, &tm_b, &p};
+  void* args[] = {&tm_a, &tm_b, &tm_b_half, &p};
   err = cudaLaunchKernelExC(&lc, fn, args);
   if (err != cudaSuccess) return cuda_error(err, "launch(tcgen05 gemm)");
   return KF_OK;

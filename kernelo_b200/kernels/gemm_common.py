@@ -6,9 +6,11 @@ that configs can be stated explicitly (cached, ranked, filtered):
 * whether an operand can be described by a TMA tensor map (16-byte aligned
   base, unit stride along K or along M/N, the other stride a multiple of 16
   bytes) -- otherwise only the SIMT kernel can take the problem;
-* the default tcgen05 tile for a shape: 128-row MMA tiles, BLOCK_N up to 256,
-  A/B swapped for skinny M (the weight becomes the 128-row operand), stream-K
-  when whole tiles would leave SMs idle.
+* the default tcgen05 tile for a shape: 256-row SM-pair tiles when they fill
+  the machine (else 128-row), BLOCK_N up to 256, A/B swapped for skinny M (the
+  weight becomes the 128-row operand), all stream-K when whole tiles would
+  leave SMs idle, else the split tail (whole tiles, the last partial wave as
+  half-width tiles).
 """
 
 from __future__ import annotations
@@ -124,9 +126,10 @@ def default_tcgen05_config(
     block_k = 128 if (cg == 2 and k >= 512) else 64
     per_stage = (TC_BLOCK_M + block_n // cg) * block_k * 2
     stages = max(2, min(12, (SM100_SMEM_PER_BLOCK - 1024 - 256) // per_stage))
-    tiles = -(-m_k // TC_BLOCK_M) * -(-n_k // block_n)
+    tiles = -(-m_k // (TC_BLOCK_M * cg)) * -(-n_k // block_n)
     k_blocks = -(-k // block_k)
-    stream_k = 1 if (cg == 1 and tiles < sm_count and k_blocks >= 4) else 2
+    # all stream-K below one wave of one-SM tiles, else the split tail (mirrors api.cu)
+    stream_k = 2 if k_blocks < 4 else (1 if (cg == 1 and tiles < sm_count) else 3)
     # A panels of one raster group within ~48 MB of L2 (mirrors api.cu)
     tile_rows = TC_BLOCK_M * cg
     group_m = max(1, min(-(-m_k // tile_rows), (48 << 20) // max(1, tile_rows * k * 2)))

@@ -397,3 +397,92 @@ def test_epilogue_gelu_within_one_ulp_of_torch(approximate, dtype, device):
     ulp = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(tiny))) - mant)
     worst = float(((out - ref).abs() / ulp).max())
     assert worst <= 1.0, f"{worst:.2f} ulp"
+
+
+# ------------------------------------------------------------------ split tail / pair stream-K
+def _pair(**kw):
+    base = dict(KERNEL=1, BLOCK_M=256, BLOCK_N=256, BLOCK_K=128, num_stages=3, GROUP_M=16, SWAP_AB=2,
+                CLUSTER_M=2)
+    base.update(kw)
+    return KernelConfig("fused_linear_erf", **base)
+
+
+def _one_sm(**kw):
+    base = dict(KERNEL=1, BLOCK_M=128, BLOCK_N=128, BLOCK_K=64, num_stages=6, GROUP_M=8, SWAP_AB=2)
+    base.update(kw)
+    return KernelConfig("fused_linear_erf", **base)
+
+
+@pytest.mark.parametrize("shape,cfg", [
+    ((4096, 11008, 1024), _pair(STREAM_K=3)),             # 688 pair tiles: 9 waves + 22 tiles as 44 halves
+    ((4096, 11008, 1024), _pair(STREAM_K=1)),             # all stream-K on SM pairs
+    ((2048, 2816, 2048), _pair(STREAM_K=3, NUM_CTAS=60)),  # 88 tiles on 30 pairs: remainder too large to split
+    ((1024, 1024, 4096), _pair(STREAM_K=1)),
+    ((1500, 3000, 1000), _pair(STREAM_K=3, BLOCK_N=128, BLOCK_K=64, num_stages=6)),  # ragged edges
+    ((2560, 2048, 512), _one_sm(STREAM_K=3)),             # 320 one-SM tiles: 2 waves + 24 as 48 halves
+    ((2500, 1990, 512), _one_sm(STREAM_K=3)),             # the same with ragged M and N
+])
+def test_split_tail_and_pair_stream_k(shape, cfg, device):
+    """Whole tiles for the full waves and the last partial wave as half-width
+    tiles, or stream-K with the fix-up done per CTA of an SM pair: sampled
+    rows against the oracle, bitwise-identical repeats, agreement with whole
+    tiles, and a clean device status."""
+    m, n, k = shape
+    gen = torch.Generator().manual_seed(m + n + k)
+    x = torch.randn(m, k, generator=gen).bfloat16().to(device)
+    w = (torch.randn(n, k, generator=gen) * k ** -0.5).bfloat16().to(device)
+    b = (torch.randn(n, generator=gen) * 0.3).bfloat16().to(device)
+    out = fused_linear_gelu(x, w.t(), b, approximate="none", config=cfg)
+    rows = sample_rows(m, 48)
+    gate(ref.linear_gelu_ref(host(x[rows]), host(w.t()), host(b), "none"), out[rows], torch.bfloat16,
+         context=f"{shape} {cfg}")
+    assert torch.equal(out, fused_linear_gelu(x, w.t(), b, approximate="none", config=cfg))
+    whole = fused_linear_gelu(x, w.t(), b, approximate="none", config=cfg.replace(STREAM_K=2))
+    if cfg["STREAM_K"] == 3:  # same K order per output: bitwise the same as whole tiles
+        assert torch.equal(out, whole)
+    else:
+        gate(host(whole[rows].float()), out[rows], torch.bfloat16, context="against whole tiles")
+    assert native.device_status(device.index) == 0
+
+
+def test_split_tail_with_an_mn_major_b(device):
+    """matmul's row-major (K, N) B is MN-major: the half-width tiles keep
+    64-column TMA boxes."""
+    gen = torch.Generator().manual_seed(9)
+    a = torch.randn(4096, 1024, generator=gen).half().to(device)
+    bm = (torch.randn(1024, 11008, generator=gen) * 1024 ** -0.5).half().to(device)
+    cfg = KernelConfig("matmul", KERNEL=1, BLOCK_M=256, BLOCK_N=256, BLOCK_K=128, num_stages=3, GROUP_M=16,
+                       SWAP_AB=2, CLUSTER_M=2, STREAM_K=3)
+    out = matmul(a, bm, config=cfg)
+    rows = sample_rows(4096, 32)
+    gate(ref.matmul_ref(host(a[rows]), host(bm)), out[rows], torch.float16)
+    assert torch.equal(out, matmul(a, bm, config=cfg.replace(STREAM_K=2)))
+
+
+def test_auto_stream_k_without_workspace_runs_whole_tiles(device):
+    """A C-ABI caller that passes no workspace still gets a result under the
+    library's own config: its stream-K choice falls back to whole tiles. An
+    explicit stream-K request without workspace is refused."""
+    import ctypes
+
+    lib = native.load()
+    m, n, k = 4096, 11008, 1024
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(m, k, generator=gen).bfloat16().to(device)
+    w = (torch.randn(n, k, generator=gen) * k ** -0.5).bfloat16().to(device)
+    b = (torch.randn(n, generator=gen) * 0.3).bfloat16().to(device)
+    y = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+    wt = w.t()
+    stream = torch.cuda.current_stream(device).cuda_stream
+
+    def call(cfg):
+        return lib.kf_linear_bias_act(native.native_code(torch.bfloat16), x.data_ptr(), x.stride(0), x.stride(1),
+                                      wt.data_ptr(), wt.stride(0), wt.stride(1), b.data_ptr(), y.data_ptr(),
+                                      y.stride(0), y.stride(1), m, n, k, native.KF_EPI_BIAS_GELU_ERF,
+                                      cfg, None, 0, stream)
+
+    assert call(None) == native.KF_OK
+    rows = sample_rows(m, 32)
+    gate(ref.linear_gelu_ref(host(x[rows]), host(wt), host(b), "none"), y[rows], torch.bfloat16)
+    explicit = native.GemmLaunch.from_config(_pair(STREAM_K=1)).struct()
+    assert call(ctypes.byref(explicit)) == native.KF_ERR_WORKSPACE
