@@ -31,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -71,55 +72,90 @@ def profile_traffic(kernel: str) -> float | None:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clock, power and clock-event reasons sampled every 10 ms through NVML
+    (read-only queries) on a background thread during the timed region;
+    nvidia-smi polling when NVML is not importable."""
 
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int) -> None:
-        self.gpu_index = gpu_index
-        self.proc = None
+    def __init__(self, device_index: int, period_s: float = 0.01) -> None:
+        self.device_index = device_index
+        self.period_s = period_s
+        self.rows: list[tuple[float, float, float, int]] = []  # (sm MHz, max MHz, watts, reason bits)
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
+        self._smi_out = ""
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.device_index).uuid)
+        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+
+    def _loop(self, nvml, handle) -> None:
+        max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+        while True:
+            try:
+                mhz = float(nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM))
+                watts = nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                bits = int(nvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+                self.rows.append((mhz, max_mhz, watts, bits))
+            except Exception:  # noqa: BLE001 - a failed read is a missing sample
+                pass
+            if self._stop.wait(self.period_s):
+                return
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.gpu_index)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            nvml, handle = self._nvml_handle()
+            self._thread = threading.Thread(target=self._loop, args=(nvml, handle), daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001 - NVML unavailable: poll nvidia-smi instead
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                     "-i", str(self.device_index)],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                self._proc = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self._smi_out, _ = self._proc.communicate(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out = ""
-        else:
-            self.out = ""
+                self._proc.kill()
+            for line in (self._smi_out or "").splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    flags = [f.lower() == "active" for f in parts[5:9]]
+                    bits = sum(b for (_, b), on in zip(self.REASONS[:4], flags) if on)
+                    self.rows.append((float(parts[1]), float(parts[2]), float(parts[3]), bits))
+                except ValueError:
+                    continue
 
     def summary(self) -> dict:
-        rows = []
-        for line in (self.out or "").splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
-            except ValueError:
-                continue
+        rows = list(self.rows)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        max_mhz = rows[0][1]
         loaded = [r for r in rows if r[2] > 200.0] or rows
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({names[i] for r in loaded for i, flag in enumerate(r[3]) if flag.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max_mhz, "reasons": reasons,
-                "samples": len(loaded), "power_w_max": max(r[2] for r in rows)}
+        reasons = sorted({name for r in loaded for name, bit in self.REASONS if r[3] & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": rows[0][1], "reasons": reasons,
+                "samples": len(loaded), "power_w_max": max(r[2] for r in rows),
+                "source": "nvml" if self._thread is not None else "nvidia-smi"}
 
 
 # ------------------------------------------------------------------ helpers
@@ -174,6 +210,7 @@ def cpu_baseline(rows: int = 512, budget_s: float = 10.0) -> dict:
     on a bounded sample: ``rows`` rows of X against the full W."""
     from oracle.cpu_reference import torch_cpu
 
+    torch.set_num_threads(os.cpu_count() or 1)
     gen = torch.Generator().manual_seed(7)
     x = torch.randn(rows, K, generator=gen).bfloat16()
     w = (torch.randn(N, K, generator=gen) * K ** -0.5).bfloat16()
@@ -265,6 +302,9 @@ def secondary_lines(pk: dict, flush) -> list[dict]:
 def run_reference(args, world: int, rank: int) -> int:
     if rank != 0:
         return 0
+    # Every host thread the box has: torchrun sets OMP_NUM_THREADS=1 for its
+    # workers, which would time the reference's CPU path on one core.
+    torch.set_num_threads(os.cpu_count() or 1)
     rows = 256
     from oracle.cpu_reference import torch_cpu
 
@@ -302,17 +342,19 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     pk, pk_kind = peaks()
     x, w, b, chunk = make_inputs(dev, rank, world)
     if world > 1:
-        layer = ShardedFusedLinear(None, None, out_features=N, shard_weight=w, shard_bias=b, approximate="none")
-        gathered = torch.empty(world, M, chunk, device=dev, dtype=torch.bfloat16)
-        mine = gathered[rank]
+        layer = ShardedFusedLinear(None, None, out_features=N, shard_weight=w, shard_bias=b, approximate="none",
+                                   gather="fused")
+        written: list[torch.Tensor] = []
 
-        # layer(x) in two parts, so the timed loop can bracket the kernel alone
+        # layer(x) in two parts, so the timed loop can bracket the kernel alone:
+        # the GEMM whose epilogue also stores every output tile into the peers'
+        # copies of Y over NVLink, then the bounded cross-GPU barrier
         def launch_kernel():
-            layer.local(x, out=mine)
+            written[:] = [layer.fused_kernel(x)]
 
         def finish_step():
-            dist.all_gather_into_tensor(gathered.view(-1), mine.reshape(-1))
-            return gathered.permute(1, 0, 2).reshape(M, world * chunk)[:, :N]
+            layer.fused_publish(x)
+            return written[0][:, :N]
     else:
         y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
 
@@ -330,13 +372,21 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     out = step()
     torch.cuda.synchronize()
     rows = torch.arange(0, M, 97, device=dev)[:32]
-    full_w = w if world == 1 else None
-    if full_w is not None:
-        ref = torch.nn.functional.gelu(x[rows].float() @ full_w.float().t() + b.float(), approximate="none")
+    if world == 1:
+        ref = torch.nn.functional.gelu(x[rows].float() @ w.float().t() + b.float(), approximate="none")
         err = float((out[rows].float() - ref).abs().max() / ref.abs().max())
         if not err < 2e-2:
             raise SystemExit(f"fused linear failed the bf16 gate before timing: err={err:.3e}")
-    if native.device_status(local) != 0:
+    else:
+        # every rank's tiles must have arrived: the same layer gathered by NCCL
+        nccl = ShardedFusedLinear(None, None, out_features=N, shard_weight=w, shard_bias=b, approximate="none",
+                                  gather="nccl")
+        differs = float(not torch.equal(out, nccl(x)))
+        torch.cuda.synchronize()
+        del nccl
+        if max_over_ranks(differs, world) > 0:  # every rank takes the same exit
+            raise SystemExit("the fused all-gather differs from the NCCL all-gather before timing")
+    if max_over_ranks(float(native.device_status(local) != 0), world) > 0:
         raise SystemExit("device status word set before timing")
 
     for _ in range(args.warmup):
@@ -360,6 +410,8 @@ def run_native(args, world: int, rank: int, local: int) -> int:
         end.record(stream)
         torch.cuda.synchronize()
         barrier(world)
+    if max_over_ranks(float(native.device_status(local) != 0), world) > 0:
+        raise SystemExit(f"device status word {native.device_status(local):#x} after the timed loop")
     ms_total = max_over_ranks(start.elapsed_time(end), world)
     ms_step = ms_total / args.steps
     value = FLOP * args.steps / (ms_total * 1e-3) / 1e12
@@ -381,12 +433,11 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     e2e_steps = max(3, min(20, args.steps))
     x_host = x.cpu().pin_memory()
     y_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty_like(x)
 
     def e2e_step():
         if world > 1:
-            x_dev.copy_(x_host, non_blocking=True)
-            y_host.copy_(layer(x_dev), non_blocking=True)
+            # each rank moves 1/world of X in and of Y out over its own PCIe link
+            layer.forward_host(x_host, y_host, chunks=4)
         else:
             # the host-buffer entry point: row chunks overlap H2D, the kernel and D2H
             fused_linear_gelu_host(x_host, w.t(), b, approximate="none", out=y_host)
@@ -422,7 +473,8 @@ def run_native(args, world: int, rank: int, local: int) -> int:
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) X, N(0,1/4096) W, N(0,0.1) b; random init)",
             "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "gelu": "erf",
-                       "parallelism": f"N-sharded columns x{world} + NCCL all_gather" if world > 1 else "single GPU",
+                       "parallelism": (f"N-sharded columns x{world}, all-gather fused into the GEMM epilogue "
+                                       "(NVLink peer stores) + bounded peer barrier") if world > 1 else "single GPU",
                        "l2": "inputs exceed L2 (X 32 MiB + W 86 MiB + Y 86 MiB > 126 MiB), no flush"},
             "roofline": roofline,
             "clocks": clocks.summary(),
@@ -430,13 +482,16 @@ def run_native(args, world: int, rank: int, local: int) -> int:
                     "d2h_bytes_per_step": M * N * 2, "steps": e2e_steps,
                     "api": ("fused_linear_gelu_host (pinned X in, pinned Y out, 8 row chunks overlapping "
                             "copies and kernel)" if world == 1 else
-                            "ShardedFusedLinear with pinned X copied in and Y copied out")},
-            "gpu_launches": args.steps,
+                            "ShardedFusedLinear.forward_host: each rank copies 1/N of X's rows in and 1/N of "
+                            "Y's rows out (bytes summed over ranks), X all-gathered over NVLink, 4 row chunks "
+                            "pipelined")},
+            "gpu_launches": args.steps * (2 if world > 1 else 1),
             "cpu_baseline": baseline,
             "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        layer.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -113,6 +113,9 @@ typedef struct kf_rows_config {
   int32_t reserved[2];
 } kf_rows_config;
 
+/* Peers an all-gathering call can write to: an 8-GPU node. */
+#define KF_MAX_PEERS 7
+
 /* Row kernels. REGISTER: one row per CTA (or per cluster of up to 8 CTAs for
  * wide rows), loaded straight into registers. STREAM: persistent CTAs (one or
  * two per SM) of row groups; each group keeps its next rows in flight as bulk
@@ -207,6 +210,47 @@ KF_API int32_t kf_softmax_rows(int32_t dtype, const void* x, int64_t sx_row, voi
 KF_API int32_t kf_rmsnorm_rows(int32_t dtype, const void* x, int64_t sx_row, const void* gamma,
                         void* y, int64_t sy_row, int64_t rows, int64_t cols, float eps,
                         const kf_rows_config* cfg, void* stream);
+
+/* ---- fused linear + all-gather over NVLink ---------------------------------- *
+ * kf_linear_bias_act, and every output tile is also stored into the n_peers
+ * buffers y_peers[i]: device pointers (peer-mapped, e.g. symmetric memory) to
+ * the element that corresponds to y[0,0] in each peer's copy of Y, which has
+ * y's strides. A rank of a column-sharded linear passes its column block of
+ * its own Y as y and the same block of every peer's Y as y_peers: when every
+ * rank's call has finished and kf_peer_barrier has run, every rank holds all
+ * of Y with no collective and no copy. The epilogue ends with a system-scope
+ * fence. tcgen05 path only (n_peers <= KF_MAX_PEERS). No reference
+ * counterpart: the reference is single-GPU; this replaces the NCCL
+ * all_gather of the sharded fused linear. */
+KF_API int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
+                                            const void* w, int64_t sw_k, int64_t sw_n,
+                                            const void* bias, void* y, int64_t sy_m, int64_t sy_n,
+                                            int64_t M, int64_t N, int64_t K, int32_t epilogue,
+                                            void* const* y_peers, int32_t n_peers,
+                                            const kf_gemm_config* cfg, void* workspace,
+                                            int64_t workspace_bytes, void* stream);
+
+/* Cross-GPU barrier on the stream: writes `epoch` into slot `rank` of every
+ * peer's signal array (release, system scope) and waits -- at most
+ * timeout_us microseconds -- until every peer's slot in the local array holds
+ * `epoch` (acquire, system scope). local_signals / peer_signals[i] are
+ * peer-mapped arrays of `world` uint32 (zero-initialised; epochs increase
+ * from 1). A timeout records KF_ERR_TIMEOUT in the device status word (read
+ * with kf_device_status) and the kernel returns: it never waits without
+ * limit. peer_signals lists the OTHER ranks in rank order. */
+KF_API int32_t kf_peer_barrier(uint32_t* local_signals, uint32_t* const* peer_signals,
+                               int32_t rank, int32_t world, uint32_t epoch, int32_t timeout_us,
+                               void* stream);
+
+/* Peer mapping for the all-gather buffers, by CUDA IPC (no multicast object).
+ * kf_ipc_handle: the IPC handle (KF_IPC_HANDLE_BYTES bytes) of the allocation
+ * holding `ptr`, and ptr's byte offset in it. kf_ipc_open: map a handle from
+ * another process on this device; the peer's pointer is *base_out + offset.
+ * kf_ipc_close: unmap (pass the base kf_ipc_open returned). */
+#define KF_IPC_HANDLE_BYTES 64
+KF_API int32_t kf_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+KF_API int32_t kf_ipc_open(const void* handle, void** base_out);
+KF_API int32_t kf_ipc_close(void* base);
 
 /* ---- failure-detection self test ------------------------------------------- *
  * Launches one CTA that waits on an mbarrier nothing will ever complete, with

@@ -145,7 +145,8 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
   if (c.block_k == 0) c.block_k = (cg == 2 && g.K >= 512) ? 128 : 64;
   if (c.stages == 0) {
     const int64_t per_stage = static_cast<int64_t>(128 + c.block_n / cg) * c.block_k * 2;
-    int64_t s = (232448 - 1024 - 256) / per_stage;
+    // (the all-gather epilogue's output stage comes out of the same 227 KiB)
+    int64_t s = (232448 - 1024 - 256 - (g.n_peers > 0 ? GEMM_PEER_STAGE_BYTES + 16 : 0)) / per_stage;
     if (s > 12) s = 12;
     if (s < 2) s = 2;
     c.stages = static_cast<int32_t>(s);
@@ -210,7 +211,11 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
     }
   }
   if (cfg.kernel == KF_GEMM_TCGEN05) return launch_gemm_tcgen05(g, cfg, *dev, s);
-  if (cfg.kernel == KF_GEMM_SIMT) return launch_gemm_simt(g, cfg, s);
+  if (cfg.kernel == KF_GEMM_SIMT) {
+    if (g.n_peers > 0)
+      return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 path only");
+    return launch_gemm_simt(g, cfg, s);
+  }
   return set_error(KF_ERR_INVALID_CONFIG, "unknown GEMM kernel code");
 }
 
@@ -297,6 +302,58 @@ int32_t kf_linear_bias_act(int32_t dtype, const void* x, int64_t sx_m, int64_t s
   g.workspace = workspace;
   g.workspace_bytes = workspace_bytes;
   return gemm_common(g, cfg, stream);
+}
+
+int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
+                                     const void* w, int64_t sw_k, int64_t sw_n, const void* bias,
+                                     void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N,
+                                     int64_t K, int32_t epilogue, void* const* y_peers,
+                                     int32_t n_peers, const kf_gemm_config* cfg, void* workspace,
+                                     int64_t workspace_bytes, void* stream) {
+  if (n_peers < 0 || n_peers > KF_MAX_PEERS)
+    return set_error(KF_ERR_INVALID_ARGUMENT,
+                     "n_peers must be in [0, " + std::to_string(KF_MAX_PEERS) + "]");
+  if (n_peers > 0 && y_peers == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null y_peers");
+  if (cfg != nullptr && cfg->kernel == KF_GEMM_SIMT && n_peers > 0)
+    return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 path only");
+  GemmArgs g;
+  g.dtype = dtype;
+  g.a = x;
+  g.sa_m = sx_m;
+  g.sa_k = sx_k;
+  g.b = w;
+  g.sb_k = sw_k;
+  g.sb_n = sw_n;
+  g.c = y;
+  g.sc_m = sy_m;
+  g.sc_n = sy_n;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.bias = bias;
+  g.epilogue = epilogue;
+  g.workspace = workspace;
+  g.workspace_bytes = workspace_bytes;
+  g.n_peers = n_peers;
+  for (int i = 0; i < n_peers; ++i) {
+    if (y_peers[i] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer output pointer");
+    g.peers[i] = y_peers[i];
+  }
+  if (n_peers > 0 && !tcgen05_operands_ok(g, nullptr))
+    return set_error(KF_ERR_UNALIGNED, "the all-gather epilogue needs TMA-describable operands");
+  return gemm_common(g, cfg, stream);
+}
+
+int32_t kf_peer_barrier(uint32_t* local_signals, uint32_t* const* peer_signals, int32_t rank,
+                        int32_t world, uint32_t epoch, int32_t timeout_us, void* stream) {
+  int device = 0;
+  int rc = current_device(&device);
+  if (rc != KF_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = device_info(device, &dev);
+  if (rc != KF_OK) return rc;
+  return launch_peer_barrier(local_signals, peer_signals, rank, world, epoch, timeout_us, *dev,
+                             static_cast<cudaStream_t>(stream));
 }
 
 int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w,

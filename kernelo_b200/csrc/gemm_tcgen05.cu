@@ -88,6 +88,10 @@ struct TcParams {
   int bias_on_rows;
   float* partials;
   int* counters;
+  // Peer copies of C, written with the same offsets (all-gather epilogue).
+  void* peers[KF_MAX_PEERS];
+  int n_peers;
+  int peer_stage;  // whole 64-column chunks go through the shared-memory stage
   int* status;
   uint32_t idesc;
   uint32_t a_stage_bytes, b_stage_bytes;  // per CTA
@@ -205,10 +209,11 @@ __device__ __forceinline__ void load_bias16(const T* bias, int col0, int n, floa
   }
 }
 
+// Bias and activation for one lane's 16 accumulators (row `row`, columns
+// col0 .. col0 + 15).
 template <typename T, int EPI>
-__device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0, const float* acc) {
-  if (row >= p.M) return;
-  float v[16];
+__device__ __forceinline__ void epilogue16(const TcParams& p, int row, int col0, const float* acc,
+                                           float (&v)[16]) {
   const T* bias = static_cast<const T*>(p.bias);
   if constexpr (EPI != KF_EPI_NONE) {
     float b[16];
@@ -229,26 +234,96 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = acc[j];
   }
-  T* out = static_cast<T*>(p.c) + static_cast<long long>(row) * p.sc_r +
-           static_cast<long long>(col0) * p.sc_c;
+}
+
+template <typename T, int EPI, bool PEERS>
+__device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0, const float* acc) {
+  if (row >= p.M) return;
+  float v[16];
+  epilogue16<T, EPI>(p, row, col0, acc, v);
+  const long long off = static_cast<long long>(row) * p.sc_r + static_cast<long long>(col0) * p.sc_c;
+  T* out = static_cast<T*>(p.c) + off;
   const bool vec_ok = p.sc_c == 1 && col0 + 16 <= p.N &&
                       (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && sizeof(T) == 2;
   if (vec_ok) {
     uint32_t packed[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) packed[j] = pack2<T>(v[2 * j], v[2 * j + 1]);
+    const uint4 q0 = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    const uint4 q1 = make_uint4(packed[4], packed[5], packed[6], packed[7]);
     uint4* dst = reinterpret_cast<uint4*>(out);
-    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    dst[0] = q0;
+    dst[1] = q1;
+    // The same 32 bytes into every peer's copy (NVLink stores; the peers'
+    // buffers share this layout, so their 16-byte alignment matches).
+    if constexpr (PEERS) {
+      for (int i = 0; i < p.n_peers; ++i) {
+        uint4* pd = reinterpret_cast<uint4*>(static_cast<T*>(p.peers[i]) + off);
+        pd[0] = q0;
+        pd[1] = q1;
+      }
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      if (col0 + j < p.N) out[static_cast<long long>(j) * p.sc_c] = from_f32<T>(v[j]);
+      if (col0 + j < p.N) {
+        const T val = from_f32<T>(v[j]);
+        out[static_cast<long long>(j) * p.sc_c] = val;
+        if constexpr (PEERS) {
+          for (int i = 0; i < p.n_peers; ++i)
+            (static_cast<T*>(p.peers[i]) + off)[static_cast<long long>(j) * p.sc_c] = val;
+        }
+      }
     }
   }
 }
 
-template <typename T, int EPI, int CG>
+// All-gather epilogue for 64 columns of a warp's 32 rows. Stores straight
+// from the TMEM lane layout (one row per lane) would send each row's bytes as
+// a separate 16-byte write over NVLink. Instead the warp stages its 32 x 64
+// block in shared memory (16-byte segments XOR-swizzled by row, so both the
+// row-per-lane writes and the segment-per-lane reads are conflict-free) and
+// reads it back so that every store instruction covers 4 rows x 128
+// contiguous bytes, sent to this GPU's C and to every peer's copy.
+// Requires: 2-byte T, unit column stride, 16-byte aligned row starts in C and
+// in every peer copy, and col0 + 64 <= N (the caller checks).
+// Stage 16 columns (segments 2q and 2q + 1 of the lane's row).
+template <typename T, int EPI>
+__device__ __forceinline__ void stage16(const TcParams& p, int row, int lane, int col0, int q,
+                                        const uint32_t (&r)[16], uint4* stage) {
+  static_assert(sizeof(T) == 2, "the staged epilogue packs 2-byte elements");
+  float v[16];
+  epilogue16<T, EPI>(p, row, col0 + 16 * q, reinterpret_cast<const float*>(r), v);
+  uint32_t packed[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) packed[j] = pack2<T>(v[2 * j], v[2 * j + 1]);
+  stage[lane * 8 + ((2 * q) ^ (lane & 7))] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  stage[lane * 8 + ((2 * q + 1) ^ (lane & 7))] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+}
+
+// Write the staged 32 x 64 block (see stage16) to C and every peer copy.
+template <typename T>
+__device__ __forceinline__ void flush_stage64(const TcParams& p, int row_base, int lane, int col0,
+                                              const uint4* stage) {
+  __syncwarp();
+  const int seg = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r_local = 4 * i + (lane >> 3);
+    const uint4 val = stage[r_local * 8 + (seg ^ (r_local & 7))];
+    const int grow = row_base + r_local;
+    if (grow < p.M) {
+      const long long off = static_cast<long long>(grow) * p.sc_r + col0 + 8 * seg;
+      *reinterpret_cast<uint4*>(static_cast<T*>(p.c) + off) = val;
+      for (int k = 0; k < p.n_peers; ++k) *reinterpret_cast<uint4*>(static_cast<T*>(p.peers[k]) + off) = val;
+    }
+  }
+  __syncwarp();  // the stage is free for the next chunk
+}
+
+// PEERS: the all-gathering variant (every output tile also stored into the
+// peers' copies of C); the plain GEMM is compiled without any of that code.
+template <typename T, int EPI, int CG, bool PEERS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                    const __grid_constant__ CUtensorMap tm_b,
@@ -265,6 +340,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // misc[0] TMEM base address, misc[1] abort flag, misc[2] "last contributor" flag
   volatile int* abort_flag = reinterpret_cast<volatile int*>(&misc[1]);
   volatile uint32_t* last_flag = &misc[2];
+  // The all-gather epilogue's per-warp stages (allocated only when peer_stage).
+  uint4* peer_stage = reinterpret_cast<uint4*>((reinterpret_cast<uintptr_t>(misc + 4) + 15) &
+                                               ~static_cast<uintptr_t>(15));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -508,16 +586,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * static_cast<uint32_t>(p.bn);
       const bool whole_tile = seg.kb0 == 0 && seg.kb1 == p.kb_per_tile;
       if (whole_tile) {
+        int c = c_begin;
+        if (PEERS && p.peer_stage) {
+          uint4* stage = peer_stage + (warp - EPI_WARP0) * (32 * 8);
+          const int row_base = row - lane;
+          for (; c + 64 <= c_end && col_base + c + 64 <= p.N; c += 64) {
+#pragma unroll
+            for (int q = 0; q < 4; q += 2) {  // two 16-column TMEM loads in flight per wait
+              uint32_t r0[16], r1[16];
+              __syncwarp();
+              tmem_ld_16(t_acc + c + 16 * q, r0);
+              tmem_ld_16(t_acc + c + 16 * q + 16, r1);
+              tmem_ld_wait();
+              stage16<T, EPI>(p, row, lane, col_base + c, q, r0, stage);
+              stage16<T, EPI>(p, row, lane, col_base + c, q + 1, r1, stage);
+            }
+            flush_stage64<T>(p, row_base, lane, col_base + c, stage);
+          }
+        }
         // Two 16-column TMEM loads in flight per wait.
-        for (int c = c_begin; c < c_end; c += 32) {
+        for (; c < c_end; c += 32) {
           uint32_t r0[16], r1[16];
           const bool two = c + 16 < c_end;
           __syncwarp();  // tcgen05.ld is .sync.aligned
           tmem_ld_16(t_acc + c, r0);
           if (two) tmem_ld_16(t_acc + c + 16, r1);
           tmem_ld_wait();
-          store_chunk<T, EPI>(p, row, col_base + c, reinterpret_cast<const float*>(r0));
-          if (two) store_chunk<T, EPI>(p, row, col_base + c + 16, reinterpret_cast<const float*>(r1));
+          store_chunk<T, EPI, PEERS>(p, row, col_base + c, reinterpret_cast<const float*>(r0));
+          if (two) store_chunk<T, EPI, PEERS>(p, row, col_base + c + 16, reinterpret_cast<const float*>(r1));
         }
       } else {
         // Stream-K fix-up for a tile shared between units. Each CTA fixes up
@@ -602,7 +698,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
               }
             }
-            store_chunk<T, EPI>(p, row, col_base + c, sum);
+            store_chunk<T, EPI, PEERS>(p, row, col_base + c, sum);
           }
           if (ethread == 0) *counter = 0;  // leave the workspace clean
         }
@@ -624,6 +720,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
 
+  // Stores into peers' memory are made visible system-wide before the kernel
+  // ends, so that a barrier kernel that follows on the stream can publish them.
+  if (PEERS && warp >= EPI_WARP0) __threadfence_system();
   tc_fence_before();
   __syncwarp();  // lanes 1-31 of warps 0 and 1 arrive here before their lane 0
   if constexpr (CG == 2) {
@@ -652,9 +751,9 @@ uint32_t tmem_cols_for(int bn) {
 }
 
 // Shared memory of one CTA: A rows (128) and this CTA's B rows per stage.
-int64_t smem_bytes_for(int bn, int bk, int stages, int cg) {
+int64_t smem_bytes_for(int bn, int bk, int stages, int cg, bool peer_stage = false) {
   const int64_t ring = static_cast<int64_t>(stages) * (BM + bn / cg) * bk * 2;
-  return 1024 + ring + 8 * (2 * stages + 5) + 16;
+  return 1024 + ring + 8 * (2 * stages + 5) + 16 + (peer_stage ? 16 + GEMM_PEER_STAGE_BYTES : 0);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -729,25 +828,28 @@ int operand_major(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int64_
 }
 
 template <typename T, int EPI>
-void* kernel_ptr(int cg) {
-  return cg == 2 ? reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI, 2>)
-                 : reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI, 1>);
+void* kernel_ptr(int cg, bool peers) {
+  if (peers)
+    return cg == 2 ? reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI, 2, true>)
+                   : reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI, 1, true>);
+  return cg == 2 ? reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI, 2, false>)
+                 : reinterpret_cast<void*>(&tc_gemm_kernel<T, EPI, 1, false>);
 }
 
-void* pick_kernel(int dtype, int epi, int cg) {
+void* pick_kernel(int dtype, int epi, int cg, bool peers) {
   if (dtype == KF_FP16) {
     switch (epi) {
-      case KF_EPI_NONE: return kernel_ptr<__half, KF_EPI_NONE>(cg);
-      case KF_EPI_BIAS: return kernel_ptr<__half, KF_EPI_BIAS>(cg);
-      case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__half, KF_EPI_BIAS_GELU_TANH>(cg);
-      default: return kernel_ptr<__half, KF_EPI_BIAS_GELU_ERF>(cg);
+      case KF_EPI_NONE: return kernel_ptr<__half, KF_EPI_NONE>(cg, peers);
+      case KF_EPI_BIAS: return kernel_ptr<__half, KF_EPI_BIAS>(cg, peers);
+      case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__half, KF_EPI_BIAS_GELU_TANH>(cg, peers);
+      default: return kernel_ptr<__half, KF_EPI_BIAS_GELU_ERF>(cg, peers);
     }
   }
   switch (epi) {
-    case KF_EPI_NONE: return kernel_ptr<__nv_bfloat16, KF_EPI_NONE>(cg);
-    case KF_EPI_BIAS: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS>(cg);
-    case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_TANH>(cg);
-    default: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_ERF>(cg);
+    case KF_EPI_NONE: return kernel_ptr<__nv_bfloat16, KF_EPI_NONE>(cg, peers);
+    case KF_EPI_BIAS: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS>(cg, peers);
+    case KF_EPI_BIAS_GELU_TANH: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_TANH>(cg, peers);
+    default: return kernel_ptr<__nv_bfloat16, KF_EPI_BIAS_GELU_ERF>(cg, peers);
   }
 }
 
@@ -853,7 +955,13 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   const int cg = cta_group_of(cfg);
   const int bn = cfg.block_n, bk = cfg.block_k, S = cfg.stages;
   const int b_rows = bn / cg;
-  const int64_t smem = smem_bytes_for(bn, bk, S, cg);
+  // The staged all-gather epilogue needs unit column stride and 16-byte
+  // aligned rows in C and in every peer copy.
+  bool peer_stage = g.n_peers > 0 && v.sc_c == 1 && (v.sc_r * 2) % 16 == 0 &&
+                    (reinterpret_cast<uintptr_t>(g.c) & 15u) == 0;
+  for (int i = 0; i < g.n_peers; ++i)
+    peer_stage = peer_stage && (reinterpret_cast<uintptr_t>(g.peers[i]) & 15u) == 0;
+  const int64_t smem = smem_bytes_for(bn, bk, S, cg, peer_stage);
   if (smem > dev.max_smem_optin)
     return set_error(KF_ERR_INVALID_CONFIG, "shared memory " + std::to_string(smem) +
                                                 " B exceeds the device limit of " +
@@ -897,6 +1005,9 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   p.sc_c = v.sc_c;
   p.bias = g.bias;
   p.bias_on_rows = v.bias_on_rows ? 1 : 0;
+  p.n_peers = g.n_peers;
+  for (int i = 0; i < g.n_peers; ++i) p.peers[i] = g.peers[i];
+  p.peer_stage = peer_stage ? 1 : 0;
   p.status = dev.status;
   p.idesc = instr_desc_f16(g.dtype == KF_BF16 ? 1u : 0u, static_cast<uint32_t>(a_major),
                            static_cast<uint32_t>(b_major), BM * cg, static_cast<uint32_t>(bn));
@@ -907,7 +1018,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   p.b_stage_bytes = static_cast<uint32_t>(b_rows * bk * 2);
   p.tmem_cols = tmem_cols_for(bn);
 
-  void* fn = pick_kernel(g.dtype, g.epilogue, cg);
+  void* fn = pick_kernel(g.dtype, g.epilogue, cg, g.n_peers > 0);
   cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem_request));
   if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(tcgen05 gemm)");

@@ -48,6 +48,7 @@ enum WaitSite : int {
   SITE_EPI_TMEM_FULL = 4,
   SITE_DRAIN = 5,
   SITE_SELFTEST = 6,
+  SITE_PEER_BARRIER = 7,
 };
 
 __device__ __forceinline__ void record_status(int* status, int code, int site) {

@@ -39,6 +39,11 @@ struct GemmArgs {
   int epilogue = KF_EPI_NONE;
   void* workspace = nullptr;
   int64_t workspace_bytes = 0;
+  // Peer copies of C (device pointers to the same element (0, 0) in other
+  // GPUs' buffers of the same layout): the epilogue stores every output tile
+  // into each of them as well (the all-gather of a column-sharded linear).
+  void* peers[KF_MAX_PEERS] = {};
+  int n_peers = 0;
 };
 
 // Fills zero fields of `cfg` with the library default for this problem.
@@ -61,6 +66,10 @@ int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream
 
 // Warp-per-row decode GEMV (gemv_rows.cu): y[M, N] = x[M, K] . w[N, K]^T for
 // M <= GEMV_ROWS_MAX_M with K-contiguous, 16-byte-aligned weight rows.
+// Shared memory the all-gathering GEMM epilogue stages its output in: per
+// epilogue warp, 32 rows x 64 columns of 2-byte elements.
+constexpr int GEMM_PEER_STAGE_BYTES = 8 * 32 * 64 * 2;
+
 constexpr int GEMV_ROWS_MAX_M = 4;
 // kf_gemv picks it by itself up to this many rows (measured on B200: at M=4
 // the tcgen05 GEMV streams the weight faster).
@@ -71,6 +80,10 @@ int launch_gemv_rows(int dtype, const void* x, int64_t sx_m, int64_t sx_k, const
                      int64_t sw_n, void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N,
                      int64_t K, const kf_gemm_config& cfg, const DeviceInfo& dev,
                      cudaStream_t stream);
+
+// Cross-GPU barrier over peer-mapped signal words (peer_sync.cu).
+int launch_peer_barrier(uint32_t* local, uint32_t* const* peers, int rank, int world,
+                        uint32_t epoch, int timeout_us, const DeviceInfo& dev, cudaStream_t stream);
 
 // Row kernels.
 struct RowsArgs {

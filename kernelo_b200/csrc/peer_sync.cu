@@ -1,0 +1,159 @@
+// Cross-GPU barrier over peer-mapped signal words (sm_100a), for the
+// all-gathering fused linear: after every rank's GEMM has stored its output
+// tiles into all peers' copies of Y, this publishes "my stores are done" and
+// waits for the same from every peer.
+//
+// One warp: lane t < world - 1 owns peer t. It writes `epoch` into the slot
+// of this rank in that peer's signal array with a release store at system
+// scope, then polls this rank's own slot for that peer with acquire loads at
+// system scope until it reads `epoch` or a later one. The GEMM that precedes
+// this kernel on the stream ended with a system-scope fence, so a peer that
+// observes the signal also observes the data. Every wait is bounded by
+// %globaltimer: on timeout the kernel records
+// KF_ERR_TIMEOUT | SITE_PEER_BARRIER << 8 in the device status word and
+// returns, leaving the context usable.
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "kf_common.cuh"
+#include "kf_internal.h"
+
+namespace kf {
+namespace {
+
+struct PeerBarrierParams {
+  uint32_t* local;                    // this rank's signal array [world]
+  uint32_t* peers[KF_MAX_PEERS];      // the other ranks' arrays, in rank order
+  int peer_rank[KF_MAX_PEERS];        // their ranks
+  int rank, n_peers;
+  uint32_t epoch;
+  unsigned long long timeout_ns;
+  int* status;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool reached(uint32_t v, uint32_t epoch) {
+  return static_cast<int32_t>(v - epoch) >= 0;
+}
+
+__global__ void peer_barrier_kernel(const PeerBarrierParams p) {
+  const int t = threadIdx.x;
+  if (t >= p.n_peers) return;
+  __threadfence_system();
+  st_release_sys(p.peers[t] + p.rank, p.epoch);
+  // A peer that saw this rank's signal may run ahead and write epoch + 1
+  // before this poll reads epoch, so "reached" is a wrap-safe v >= epoch.
+  const uint32_t* mine = p.local + p.peer_rank[t];
+  if (reached(ld_acquire_sys(mine), p.epoch)) return;
+  const unsigned long long start = global_timer_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    if (reached(ld_acquire_sys(mine), p.epoch)) return;
+    if ((spin & 63u) == 0 && global_timer_ns() - start > p.timeout_ns) {
+      record_status(p.status, KF_ERR_TIMEOUT, SITE_PEER_BARRIER);
+      return;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_peer_barrier(uint32_t* local, uint32_t* const* peers, int rank, int world,
+                        uint32_t epoch, int timeout_us, const DeviceInfo& dev, cudaStream_t stream) {
+  if (world < 1 || world > KF_MAX_PEERS + 1)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "world must be in [1, 8]");
+  if (rank < 0 || rank >= world) return set_error(KF_ERR_INVALID_ARGUMENT, "rank out of range");
+  if (timeout_us <= 0 || timeout_us > 60000000)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "timeout_us must be in (0, 6e7]");
+  if (epoch == 0) return set_error(KF_ERR_INVALID_ARGUMENT, "epochs start at 1 (0 is the initial value)");
+  if (world == 1) return KF_OK;
+  if (local == nullptr || peers == nullptr)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "null signal pointer");
+  PeerBarrierParams p{};
+  p.local = local;
+  p.rank = rank;
+  p.n_peers = world - 1;
+  for (int i = 0, r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    if (peers[i] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer signal pointer");
+    p.peers[i] = peers[i];
+    p.peer_rank[i] = r;
+    ++i;
+  }
+  p.epoch = epoch;
+  p.timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
+  p.status = dev.status;
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(p);
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_error(err, "launch(peer barrier)");
+  return KF_OK;
+}
+
+// ------------------------------------------------------------------ IPC mapping
+// Peer copies of a buffer are mapped with CUDA IPC handles (no multicast
+// object is ever created). A handle names a whole allocation, so the exporter
+// also reports where its pointer sits inside it (allocators sub-allocate).
+
+namespace {
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* sym = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &sym, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(sym);
+  });
+  return fn;
+}
+}  // namespace
+
+}  // namespace kf
+
+using namespace kf;
+
+int32_t kf_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "null pointer");
+  AddressRangeFn range = address_range_fn();
+  if (range == nullptr) return set_error(KF_ERR_NO_DEVICE, "cuMemGetAddressRange is not available");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "pointer is not device memory of this process");
+  cudaIpcMemHandle_t h;
+  const cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (err != cudaSuccess) return cuda_error(err, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == KF_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return KF_OK;
+}
+
+int32_t kf_ipc_open(const void* handle, void** base_out) {
+  if (handle == nullptr || base_out == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t err = cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return cuda_error(err, "cudaIpcOpenMemHandle");
+  return KF_OK;
+}
+
+int32_t kf_ipc_close(void* base) {
+  if (base == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null pointer");
+  const cudaError_t err = cudaIpcCloseMemHandle(base);
+  if (err != cudaSuccess) return cuda_error(err, "cudaIpcCloseMemHandle");
+  return KF_OK;
+}

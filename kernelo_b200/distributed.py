@@ -3,11 +3,16 @@
 Three shardings, each where the work splits naturally:
 
 * :class:`ShardedFusedLinear` -- the fused linear is column-sharded by N: rank r
-  holds rows [r*chunk, (r+1)*chunk) of the [N, K] weight and of the bias,
+  holds rows [r*chunk, (r+1)*chunk) of the [N, K] weight and of the bias and
   computes its [M, chunk] slice of ``gelu(x @ W^T + b)`` with the native
-  kernel, and the slices are exchanged with one NCCL ``all_gather_into_tensor``
-  over NVLink. N is padded to ``world * chunk`` with zero weight rows (their
-  columns are dropped), since the collective needs equal chunks.
+  kernel. With ``gather="fused"`` (``"auto"``, the default, on CUDA) the kernel's epilogue
+  stores every output tile into all ranks' copies of Y over NVLink (peer
+  pointers, mapped by CUDA IPC, into double-buffered copies) and a bounded cross-GPU
+  barrier kernel publishes completion: no collective, no copy, and the
+  transfer overlaps the math tile by tile. ``gather="nccl"`` (and ``"auto"``
+  off CUDA) exchanges the slices with one ``all_gather_into_tensor`` of the
+  group's backend and permutes them into [M, N]. N is padded to ``world * chunk`` with zero weight rows (their
+  columns are dropped).
 * :func:`row_range` -- softmax / RMSNorm rows split evenly; no exchange.
 * :func:`distributed_tune` -- the tuner's budgeted candidates dealt round-robin
   to one worker per GPU; outcomes are gathered on rank 0, which alone writes
@@ -15,7 +20,7 @@ Three shardings, each where the work splits naturally:
   (timings from different GPUs are never ranked against each other).
 
 The reference has no multi-GPU code; this module is new. No TMA multicast is
-used anywhere (the collective is NCCL's).
+used anywhere: the fused gather is plain stores to peer memory.
 """
 
 from __future__ import annotations
@@ -70,11 +75,20 @@ class ShardedFusedLinear:
         approximate: str = "none",
         group=None,
         config=None,
+        gather: str = "auto",
+        barrier_timeout_us: int = 2_000_000,
     ) -> None:
+        if gather not in ("auto", "fused", "nccl"):
+            raise ValueError("gather must be 'auto', 'fused' or 'nccl'")
         self.group = group
         self.world, self.rank = world_info(group)
         self.approximate = approximate
         self.config = config
+        self.gather = gather
+        self.barrier_timeout_us = barrier_timeout_us
+        self._symm: dict[int, _PeerOutput] = {}
+        self._host: dict = {}  # forward_host state per M: X staging, peer output, copy streams
+        self._host_out: dict[int, torch.Tensor] = {}
         if shard_weight is not None:
             if out_features is None or shard_bias is None:
                 raise ValueError("shard_weight needs out_features and shard_bias")
@@ -107,6 +121,8 @@ class ShardedFusedLinear:
         m = x.shape[0]
         if self.world == 1:
             return self.local(x)[:, : self.n]
+        if self.gather == "fused" or (self.gather == "auto" and x.is_cuda):
+            return self.fused_step(x)
         if self._gather_buf is None or self._gather_buf.shape != (self.world, m, self.chunk):
             self._gather_buf = torch.empty(self.world, m, self.chunk, device=x.device, dtype=x.dtype)
         mine = self._gather_buf[self.rank]
@@ -114,6 +130,205 @@ class ShardedFusedLinear:
         dist.all_gather_into_tensor(self._gather_buf.view(-1), mine.reshape(-1), group=self.group)
         full = self._gather_buf.permute(1, 0, 2).reshape(m, self.world * self.chunk)
         return full[:, : self.n]
+
+
+    # ---------------------------------------------------------------- fused all-gather
+    def fused_kernel(self, x: torch.Tensor) -> torch.Tensor:
+        """Launch this rank's GEMM whose epilogue also writes every peer's Y;
+        returns the buffer it wrote (valid on all ranks after :meth:`fused_publish`)."""
+        from kernelo_b200.kernels.fused_linear import _EPILOGUES
+        from kernelo_b200.runtime import native
+
+        m = x.shape[0]
+        sym = self._symm.get(m)
+        if sym is None:
+            sym = self._symm[m] = _PeerOutput(m, self.world * self.chunk, x.dtype, x.device, self.group)
+        buf, peers = sym.next_buffer(self.rank * self.chunk)
+        mine = buf[:, self.rank * self.chunk:(self.rank + 1) * self.chunk]
+        native.linear_bias_act_allgather(x, self.w.t(), mine, peers, bias=self.b,
+                                         epilogue=_EPILOGUES[self.approximate],
+                                         launch=native.GemmLaunch.from_config(self.config))
+        return buf
+
+    def fused_publish(self, x: torch.Tensor) -> None:
+        """Enqueue the bounded cross-GPU barrier that completes the gather."""
+        self._symm[x.shape[0]].barrier(self.rank, self.world, self.barrier_timeout_us)
+
+    def forward_host(self, x_host: torch.Tensor, out: torch.Tensor, *, chunks: int = 4) -> torch.Tensor:
+        """The layer from host memory to host memory, the PCIe traffic split
+        over the ranks: each rank copies 1/world of X's rows in (its own PCIe
+        link), X is all-gathered over NVLink, every rank computes its column
+        shard for all rows with the all-gathering kernel, and each rank copies
+        its 1/world of Y's rows (all N columns) back out. Row chunks pipeline
+        the copies, the gather and the kernels.
+
+        ``x_host`` [M, K] and ``out`` [M, N] are pinned host tensors; on return
+        (after synchronizing this rank's current stream) this rank's rows of
+        ``out`` hold the result -- rank r owns rows [a + r*q, a + (r+1)*q) of
+        every chunk [a, a + world*q). Collective: every rank calls it with the
+        same shapes. CUDA only (the all-gathering kernel).
+        """
+        from kernelo_b200.kernels.fused_linear import _EPILOGUES
+        from kernelo_b200.runtime import native
+
+        if not (x_host.is_pinned() and out.is_pinned()):
+            raise ValueError("forward_host needs pinned host tensors")
+        m, k = x_host.shape
+        if out.shape != (m, self.n):
+            raise ValueError(f"out must be [{m}, {self.n}]")
+        dev = self.w.device
+        world, rank = self.world, self.rank
+        chunks = max(1, min(chunks, m // max(1, world)))
+        q = -(-m // (world * chunks))  # rows per rank per chunk
+        step = q * world
+        key = ("host", m)
+        state = self._host.get(key)
+        if state is None:
+            x_dev = torch.empty(step * chunks, k, device=dev, dtype=x_host.dtype)
+            sym = _PeerOutput(m, world * self.chunk, x_host.dtype, dev, self.group) if world > 1 else None
+            state = self._host[key] = (x_dev, sym, torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        x_dev, sym, h2d, d2h = state
+        compute = torch.cuda.current_stream(dev)
+        if sym is not None:
+            buf = sym.bufs[sym.parity]
+            parity = sym.parity
+            sym.parity ^= 1
+        else:
+            buf = self._host_out.get(m)
+            if buf is None:
+                buf = self._host_out[m] = torch.empty(m, self.chunk, device=dev, dtype=x_host.dtype)
+        launch = native.GemmLaunch.from_config(self.config)
+        h2d.wait_stream(compute)  # x_dev is free once the previous call's kernels ran
+        elt = buf.element_size()
+        for c in range(chunks):
+            a = c * step
+            if a >= m:
+                break
+            b = min(m, a + step)
+            mine0 = min(b, a + rank * q)
+            mine1 = min(b, a + (rank + 1) * q)
+            with torch.cuda.stream(h2d):
+                if mine1 > mine0:
+                    x_dev[mine0:mine1].copy_(x_host[mine0:mine1], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(h2d)
+            compute.wait_event(ready)
+            if world > 1:
+                dist.all_gather_into_tensor(x_dev[a:a + step], x_dev[a + rank * q:a + (rank + 1) * q],
+                                            group=self.group)
+                cols = slice(rank * self.chunk, (rank + 1) * self.chunk)
+                peers = [sym.peer_ptrs[parity][j] + (a * buf.shape[1] + rank * self.chunk) * elt
+                         for j in range(world) if j != rank]
+                native.linear_bias_act_allgather(x_dev[a:b], self.w.t(), buf[a:b, cols], peers, bias=self.b,
+                                                 epilogue=_EPILOGUES[self.approximate], launch=launch)
+                sym.barrier(rank, world, self.barrier_timeout_us)
+                rows_out = buf[mine0:mine1, : self.n]
+            else:
+                fused_linear_gelu(x_dev[a:b], self.w.t(), self.b, approximate=self.approximate,
+                                  config=self.config, out=buf[a:b])
+                rows_out = buf[mine0:mine1, : self.n]
+            done = torch.cuda.Event()
+            done.record(compute)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done)
+                if mine1 > mine0:
+                    out[mine0:mine1].copy_(rows_out, non_blocking=True)
+        # later barrier signals (which let peers overwrite this buffer) follow
+        # this call's reads of it
+        compute.wait_stream(d2h)
+        return out
+
+    def close(self) -> None:
+        """Unmap the peers' output buffers. Collective: call on every rank, after
+        the last use of a fused result; the process group stays usable."""
+        for sym in self._symm.values():
+            sym.close()
+        for _, sym, _, _ in self._host.values():
+            if sym is not None:
+                sym.close()
+        self._symm.clear()
+        self._host.clear()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
+    def fused_step(self, x: torch.Tensor) -> torch.Tensor:
+        """``gelu(x @ W^T + b)`` as a full [M, N] view of the peer-mapped output.
+
+        Two buffers alternate between calls, so the result stays valid until
+        the call after next; consume it (on this stream) before then."""
+        buf = self.fused_kernel(x)
+        self.fused_publish(x)
+        return buf[:, : self.n]
+
+
+class _PeerOutput:
+    """Two copies of Y [M, n_total] and a signal array on every rank, each
+    mapped into every other rank by CUDA IPC handles (exchanged over the
+    process group's store); no NVLink multicast object is created.
+
+    Double buffering: call i writes buffer i % 2 on every rank. A rank cannot
+    start call i + 2 (and overwrite a peer's buffer i % 2) before that peer has
+    signalled the barrier of call i + 1, which it enqueues after whatever it
+    did with the result of call i.
+    """
+
+    def __init__(self, m: int, n_total: int, dtype: torch.dtype, device: torch.device, group) -> None:
+        from kernelo_b200.runtime import native
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.bufs = [torch.empty((m, n_total), dtype=dtype, device=device) for _ in range(2)]
+        self.signals = torch.zeros((self.world,), dtype=torch.int32, device=device)
+        torch.cuda.synchronize(device)
+        mine = [native.ipc_handle(t) for t in (*self.bufs, self.signals)]
+        everyone: list = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self._opened: list[int] = []
+        bases: dict[tuple[int, int], int] = {}
+        self.peer_ptrs: list[list[int]] = [[0] * self.world for _ in range(3)]
+        for j in range(self.world):
+            for i, (handle, offset) in enumerate(everyone[j]):
+                if j == self.rank:
+                    addr = (self.bufs + [self.signals])[i].data_ptr()
+                else:
+                    key = (j, handle)
+                    if key not in bases:
+                        bases[key] = native.ipc_open(handle)
+                        self._opened.append(bases[key])
+                    addr = bases[key] + offset
+                self.peer_ptrs[i][j] = addr
+        dist.barrier(group=group)  # every rank's signal array is zero before any peer signals
+        self.parity = 0
+        self.epoch = 0
+
+    def next_buffer(self, col_offset: int) -> tuple[torch.Tensor, list[int]]:
+        """The buffer of this call and the peers' addresses of element (0, col_offset)."""
+        i = self.parity
+        self.parity ^= 1
+        buf = self.bufs[i]
+        off = col_offset * buf.element_size()
+        return buf, [self.peer_ptrs[i][j] + off for j in range(self.world) if j != self.rank]
+
+    def signal_ptrs(self) -> tuple[int, list[int]]:
+        return self.signals.data_ptr(), [self.peer_ptrs[2][j] for j in range(self.world) if j != self.rank]
+
+    def barrier(self, rank: int, world: int, timeout_us: int) -> None:
+        from kernelo_b200.runtime import native
+
+        self.epoch += 1
+        local, peers = self.signal_ptrs()
+        native.peer_barrier(local, peers, rank, world, self.epoch, timeout_us=timeout_us,
+                            device=self.signals.device)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (all ranks should be done with them)."""
+        from kernelo_b200.runtime import native
+
+        torch.cuda.synchronize(self.signals.device)
+        for base in self._opened:
+            native.ipc_close(base)
+        self._opened = []
 
 
 def distributed_tune(tuner, operator, problem, *, device=None, group=None, finalists: int = 3):

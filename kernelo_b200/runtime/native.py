@@ -64,6 +64,11 @@ EXPORTED_SYMBOLS = (
     "kf_rmsnorm_rows",
     "kf_selftest_bounded_wait",
     "kf_gemv_noalloc",
+    "kf_linear_bias_act_allgather",
+    "kf_peer_barrier",
+    "kf_ipc_handle",
+    "kf_ipc_open",
+    "kf_ipc_close",
 )
 
 
@@ -153,6 +158,13 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kf_selftest_bounded_wait": (_i32, [_i32, _vp]),
     "kf_gemv_noalloc": (_i32, [_i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
                                _vp]),
+    "kf_linear_bias_act_allgather": (_i32, [_i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64,
+                                            _i64, _i64, _i64, _i32, ctypes.POINTER(_vp), _i32, _GP, _vp, _i64,
+                                            _vp]),
+    "kf_peer_barrier": (_i32, [_vp, ctypes.POINTER(_vp), _i32, _i32, ctypes.c_uint32, _i32, _vp]),
+    "kf_ipc_handle": (_i32, [_vp, _vp, ctypes.POINTER(_i64)]),
+    "kf_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "kf_ipc_close": (_i32, [_vp]),
 }
 
 _lock = threading.Lock()
@@ -365,6 +377,67 @@ def gemm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, *, bias: torch.Tenso
                                         c.stride(0), c.stride(1), m, n, k, epilogue,
                                         ctypes.byref(cfg), ws_ptr, max(ws_bytes, 0), stream)
         check(status, "kf_linear_bias_act")
+
+
+def linear_bias_act_allgather(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, peers: list[int], *,
+                              bias: torch.Tensor, epilogue: int, launch: GemmLaunch | None = None) -> None:
+    """``c = epilogue(a @ b + bias)``, every output tile also stored at the same
+    offsets from each address in ``peers`` (peer-mapped copies of c's buffer)."""
+    lib = load()
+    launch = launch or GemmLaunch()
+    cfg = launch.struct()
+    dev = c.device
+    stream = current_stream_handle(dev)
+    code = native_code(a.dtype)
+    m, k = a.shape
+    n = b.shape[1]
+    ws_bytes = lib.kf_gemm_workspace_bytes(dev.index or 0, code, a.stride(0), a.stride(1),
+                                           b.stride(0), b.stride(1), m, n, k, ctypes.byref(cfg))
+    if ws_bytes < 0:
+        check(int(-ws_bytes), "kf_gemm_workspace_bytes")
+    ws = workspaces.get(dev, stream, ws_bytes)
+    arr = (_vp * max(1, len(peers)))(*[ctypes.c_void_p(int(p)) for p in peers])
+    status = lib.kf_linear_bias_act_allgather(code, a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(),
+                                              b.stride(0), b.stride(1), _ptr(bias), c.data_ptr(), c.stride(0),
+                                              c.stride(1), m, n, k, epilogue, arr, len(peers),
+                                              ctypes.byref(cfg), _ptr(ws), max(ws_bytes, 0), stream)
+    check(status, "kf_linear_bias_act_allgather")
+
+
+def peer_barrier(local_signals: int, peer_signals: list[int], rank: int, world: int, epoch: int,
+                 *, timeout_us: int = 2_000_000, device: torch.device | None = None) -> None:
+    """Enqueue the bounded cross-GPU barrier (kf_peer_barrier) on the current stream."""
+    lib = load()
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    arr = (_vp * max(1, len(peer_signals)))(*[ctypes.c_void_p(int(p)) for p in peer_signals])
+    status = lib.kf_peer_barrier(ctypes.c_void_p(int(local_signals)), arr, rank, world, epoch, timeout_us,
+                                 current_stream_handle(dev))
+    check(status, "kf_peer_barrier")
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """(CUDA IPC handle of the allocation holding t, t's byte offset in it)."""
+    lib = load()
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = ctypes.c_int64(0)
+    check(lib.kf_ipc_handle(ctypes.c_void_p(t.data_ptr()), buf, ctypes.byref(off)), "kf_ipc_handle")
+    return buf.raw, off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map another process's allocation on the current device; returns its base address."""
+    lib = load()
+    base = ctypes.c_void_p(0)
+    check(lib.kf_ipc_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(base)),
+          "kf_ipc_open")
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    check(load().kf_ipc_close(ctypes.c_void_p(base)), "kf_ipc_close")
 
 
 def gemv(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, *, w_layout: str = "nk",

@@ -1,0 +1,120 @@
+"""The column-sharded fused linear on two B200s: the all-gather done by the
+GEMM epilogue (stores into peers' IPC-mapped copies of Y) against the
+NCCL gather and the oracle, the host-to-host entry point with its PCIe
+traffic split over the ranks, and the bounded cross-GPU barrier timing out
+cleanly when a peer never signals. Spawns two ranks; skipped with fewer
+than two GPUs."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, results) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from kernelo_b200.distributed import ShardedFusedLinear
+        from kernelo_b200.runtime import native
+
+        m, n, k = 1024, 3000, 512
+        gen = torch.Generator().manual_seed(11)
+        x = torch.randn(m, k, generator=gen).bfloat16().to(dev)
+        w = (torch.randn(n, k, generator=gen) * k ** -0.5).bfloat16().to(dev)
+        b = (torch.randn(n, generator=gen) * 0.3).bfloat16().to(dev)
+        fused = ShardedFusedLinear(w, b, approximate="none", gather="fused")
+        nccl = ShardedFusedLinear(w, b, approximate="none", gather="nccl")
+        outs = []
+        for step in range(3):  # both buffers, then the first again
+            xs = x if step != 1 else (x * 0.5)
+            y = fused(xs).clone()
+            y_ref = nccl(xs).clone()
+            outs.append(bool(torch.equal(y, y_ref)))
+        torch.cuda.synchronize()
+        from kernelo_b200.testing import verify
+
+        # host to host, PCIe traffic split over the ranks: this rank's rows only
+        y_full = nccl(x).clone()
+        x_host = x.cpu().pin_memory()
+        y_host = torch.zeros(m, n, dtype=torch.bfloat16).pin_memory()
+        host_ok = []
+        for _ in range(3):  # both peer buffers, then the first again
+            y_host.zero_()
+            fused.forward_host(x_host, y_host, chunks=3)
+            torch.cuda.synchronize()
+            q = -(-m // (world * 3))
+            rows = torch.cat([torch.arange(a + rank * q, min(m, a + (rank + 1) * q))
+                              for a in range(0, m, q * world)])
+            # row chunks are scheduled differently (smaller M): the bf16 gate, not bit equality
+            got, exp = y_host[rows].float(), y_full.cpu()[rows].float()
+            host_ok.append((verify(exp.double(), got.double(), dtype=torch.bfloat16).passed,
+                            float((got - exp).abs().max())))
+        status = native.device_status(rank)
+        # the first output against the oracle on rank 0 (sampled rows)
+        err = None
+        if rank == 0:
+            from oracle import cpu_reference as ref
+
+            rows = torch.arange(0, m, 37)
+            got = fused(x)[rows].float().cpu().double()
+            torch.cuda.synchronize()
+            exp = ref.linear_gelu_ref(x[rows].float().cpu().double().numpy(),
+                                      w.t().float().cpu().double().numpy(),
+                                      b.float().cpu().double().numpy(), "none")
+            err = verify(torch.from_numpy(exp), got, dtype=torch.bfloat16).passed
+        else:
+            fused(x)
+            torch.cuda.synchronize()
+        dist.barrier()
+        # a barrier nobody answers: rank 0 waits 100 ms for an epoch rank 1 never writes
+        timed_out = None
+        if rank == 0:
+            sym = next(iter(fused._symm.values()))
+            local, peers = sym.signal_ptrs()
+            native.peer_barrier(local, peers, 0, 2, 0x7FFFFFF0, timeout_us=100_000, device=dev)
+            torch.cuda.synchronize()
+            word = native.device_status(0)
+            timed_out = (word & 0xFF) == native.KF_ERR_TIMEOUT and (word >> 8) == 7
+        dist.barrier()
+        fused.close()
+        results[rank] = {"equal": outs, "host": host_ok, "status": status, "oracle": err,
+                         "timed_out": timed_out}
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_all_gather_on_two_gpus():
+    import torch.multiprocessing as mp
+
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.spawn(_worker, args=(2, _free_port(), results), nprocs=2, join=True)
+    for rank in (0, 1):
+        r = results[rank]
+        assert all(r["equal"]), f"rank {rank}: fused gather differs from the NCCL gather {r['equal']}"
+        assert all(ok for ok, _ in r["host"]), f"rank {rank}: forward_host rows differ {r['host']}"
+        assert r["status"] == 0, f"rank {rank}: device status {r['status']:#x}"
+    assert results[0]["oracle"], "rank 0: the gathered output fails the bf16 gate"
+    assert results[0]["timed_out"], "the unanswered barrier did not record a timeout"
