@@ -49,6 +49,10 @@ WORKLOAD = "fused_linear bias+erf-GELU M=4096 N=11008 K=4096 bf16, W [N,K]"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+# NVLink 5 peer copy, per direction per GPU, measured on this pool's B200s.
+NVLINK_GBS = 770.0
+
+
 def peaks() -> tuple[dict, str]:
     path = REPO / "MEASURED_PEAKS.json"
     if path.exists():
@@ -418,16 +422,38 @@ def run_native(args, world: int, rank: int, local: int) -> int:
 
     # the dominant kernel's average launch duration over the timed region
     kernel_ms = max_over_ranks(sum(ks.elapsed_time(ke) for ks, ke in kev) / len(kev), world)
-    achieved = FLOP / world / (kernel_ms * 1e-3) / 1e12
+    flop_rank = 2 * M * chunk * K  # this rank's column shard (padded to the shard width)
+    achieved = flop_rank / (kernel_ms * 1e-3) / 1e12
     # A thousand back-to-back launches run at the power cap: the sustained GEMM
     # figure is the denominator; the burst figure is reported beside it.
     peak = pk.get("bf16_tflops_sustained") or pk["bf16_tflops"]
-    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4),
-                "peak_kind": f"{pk_kind} {'sustained' if pk.get('bf16_tflops_sustained') else 'burst'} bf16",
-                "frac_of_burst": round(achieved / pk["bf16_tflops"], 4),
-                "traffic": profile_traffic("tc_gemm_fused_linear_erf_bf16"), "kernel": "tc_gemm_kernel<bf16,erf>",
-                "kernel_ms": round(kernel_ms, 4)}
+    peak_kind = f"{pk_kind} {'sustained' if pk.get('bf16_tflops_sustained') else 'burst'} bf16"
+    if world == 1:
+        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                    "frac_of_burst": round(achieved / pk["bf16_tflops"], 4),
+                    "traffic": profile_traffic("tc_gemm_fused_linear_erf_bf16"),
+                    "kernel": "tc_gemm_kernel<bf16,erf>", "kernel_ms": round(kernel_ms, 4)}
+    else:
+        # GEMM + all-gather in one kernel: the target is the slower of the
+        # shard's FLOPs at the GEMM peak and the bytes each rank must send
+        # over NVLink (its shard to every peer) at the measured peer-copy rate.
+        link_bytes = M * chunk * 2 * (world - 1)
+        t_tensor = flop_rank / (peak * 1e12)
+        t_link = link_bytes / (NVLINK_GBS * 1e9)
+        link_gbs = link_bytes / (kernel_ms * 1e-3) / 1e9
+        target_ms = max(t_tensor, t_link) * 1e3
+        nvlink_bound = t_link > t_tensor
+        roofline = {"bound": "nvlink" if nvlink_bound else "tensor",
+                    "achieved": round(link_gbs if nvlink_bound else achieved, 1),
+                    "peak": NVLINK_GBS if nvlink_bound else peak,
+                    "unit": "GB/s" if nvlink_bound else "TFLOP/s",
+                    "frac": round(target_ms / kernel_ms, 4), "target_ms": round(target_ms, 4),
+                    "tensor_tflops": round(achieved, 1), "tensor_peak": peak, "tensor_peak_kind": peak_kind,
+                    "nvlink_gbs": round(link_gbs, 1), "nvlink_bytes_per_rank": link_bytes,
+                    "nvlink_peak_kind": "measured peer copy per direction on this pool",
+                    "traffic": None, "kernel": "tc_gemm_kernel<bf16,erf,all-gather>",
+                    "kernel_ms": round(kernel_ms, 4)}
 
     # end to end through the public API: pinned host X in, Y back to pinned host
     e2e_steps = max(3, min(20, args.steps))

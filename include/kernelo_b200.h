@@ -96,7 +96,10 @@ typedef struct kf_gemm_config {
   int32_t cluster_m; /* 1, or 2 with block_m 256 (the SM pair is a 2x1 cluster)      */
   int32_t cluster_n; /* reserved, must be 0 or 1                                     */
   int32_t num_ctas;  /* persistent grid size; 0 = one CTA per SM                     */
-  int32_t reserved[5];
+  int32_t epi_store; /* all-gather epilogue (kf_linear_bias_act_allgather): 0 = library
+                        choice, 1 = stores from the threads (rows staged through
+                        shared memory), 2 = TMA tensor stores of the staged blocks    */
+  int32_t reserved[4];
 } kf_gemm_config;
 
 /* Row-kernel parameters (softmax / RMSNorm). Replaces BLOCK_SIZE /

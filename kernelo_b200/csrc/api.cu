@@ -146,7 +146,7 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
   if (c.stages == 0) {
     const int64_t per_stage = static_cast<int64_t>(128 + c.block_n / cg) * c.block_k * 2;
     // (the all-gather epilogue's output stage comes out of the same 227 KiB)
-    int64_t s = (232448 - 1024 - 256 - (g.n_peers > 0 ? GEMM_PEER_STAGE_BYTES + 16 : 0)) / per_stage;
+    int64_t s = (232448 - 1024 - 256 - (g.n_peers > 0 ? GEMM_PEER_STAGE_SMEM : 0)) / per_stage;
     if (s > 12) s = 12;
     if (s < 2) s = 2;
     c.stages = static_cast<int32_t>(s);

@@ -91,7 +91,9 @@ struct TcParams {
   // Peer copies of C, written with the same offsets (all-gather epilogue).
   void* peers[KF_MAX_PEERS];
   int n_peers;
-  int peer_stage;  // whole 64-column chunks go through the shared-memory stage
+  // Whole 64-column chunks go through the shared-memory stage: 1 = written
+  // out by the warp's stores, 2 = by TMA tensor stores (one per destination).
+  int peer_stage;
   int* status;
   uint32_t idesc;
   uint32_t a_stage_bytes, b_stage_bytes;  // per CTA
@@ -315,10 +317,45 @@ __device__ __forceinline__ void flush_stage64(const TcParams& p, int row_base, i
     if (grow < p.M) {
       const long long off = static_cast<long long>(grow) * p.sc_r + col0 + 8 * seg;
       *reinterpret_cast<uint4*>(static_cast<T*>(p.c) + off) = val;
-      for (int k = 0; k < p.n_peers; ++k) *reinterpret_cast<uint4*>(static_cast<T*>(p.peers[k]) + off) = val;
+      // Each CTA starts with a different peer, so that every GPU receives
+      // from all the others at once rather than all of them in turn.
+      int k = static_cast<int>(blockIdx.x % static_cast<unsigned>(p.n_peers));
+      for (int kk = 0; kk < p.n_peers; ++kk) {
+        *reinterpret_cast<uint4*>(static_cast<T*>(p.peers[k]) + off) = val;
+        if (++k == p.n_peers) k = 0;
+      }
     }
   }
   __syncwarp();  // the stage is free for the next chunk
+}
+
+// Tensor maps of C and of the peers' copies for the TMA-store epilogue
+// (box: 64 columns x 32 rows, 128-byte swizzle); the plain GEMM takes a
+// 4-byte placeholder instead.
+template <bool PEERS>
+struct OutMaps {
+  CUtensorMap m[KF_MAX_PEERS + 1];
+};
+template <>
+struct OutMaps<false> {
+  int unused;
+};
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The staged block has been read out of shared memory by every earlier store.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Every earlier bulk store has completed (its writes are performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // PEERS: the all-gathering variant (every output tile also stored into the
@@ -327,7 +364,8 @@ template <typename T, int EPI, int CG, bool PEERS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                    const __grid_constant__ CUtensorMap tm_b,
-                   const __grid_constant__ CUtensorMap tm_b_half, const TcParams p) {
+                   const __grid_constant__ CUtensorMap tm_b_half, const TcParams p,
+                   const __grid_constant__ OutMaps<PEERS> out_maps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -341,8 +379,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(&misc[1]);
   volatile uint32_t* last_flag = &misc[2];
   // The all-gather epilogue's per-warp stages (allocated only when peer_stage).
-  uint4* peer_stage = reinterpret_cast<uint4*>((reinterpret_cast<uintptr_t>(misc + 4) + 15) &
-                                               ~static_cast<uintptr_t>(15));
+  uint4* peer_stage = reinterpret_cast<uint4*>((reinterpret_cast<uintptr_t>(misc + 4) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -587,21 +625,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool whole_tile = seg.kb0 == 0 && seg.kb1 == p.kb_per_tile;
       if (whole_tile) {
         int c = c_begin;
-        if (PEERS && p.peer_stage) {
-          uint4* stage = peer_stage + (warp - EPI_WARP0) * (32 * 8);
-          const int row_base = row - lane;
-          for (; c + 64 <= c_end && col_base + c + 64 <= p.N; c += 64) {
-#pragma unroll
-            for (int q = 0; q < 4; q += 2) {  // two 16-column TMEM loads in flight per wait
-              uint32_t r0[16], r1[16];
-              __syncwarp();
-              tmem_ld_16(t_acc + c + 16 * q, r0);
-              tmem_ld_16(t_acc + c + 16 * q + 16, r1);
-              tmem_ld_wait();
-              stage16<T, EPI>(p, row, lane, col_base + c, q, r0, stage);
-              stage16<T, EPI>(p, row, lane, col_base + c, q + 1, r1, stage);
+        if constexpr (PEERS) {
+          if (p.peer_stage) {
+            uint4* stage = peer_stage + (warp - EPI_WARP0) * (32 * 8);
+            const int row_base = row - lane;
+            const bool tma = p.peer_stage == 2;
+            // TMA stores clip at the tensor's edge, so a ragged last chunk
+            // still goes through the stage; thread stores need whole chunks.
+            const int n_limit = tma ? p.N : p.N - 63;
+            for (; c + 64 <= c_end && col_base + c < n_limit; c += 64) {
+              if (tma) {
+                if (lane == 0) bulk_wait_read_all();  // the previous chunk has left the stage
+                __syncwarp();
+              }
+  #pragma unroll
+              for (int q = 0; q < 4; q += 2) {  // two 16-column TMEM loads in flight per wait
+                uint32_t r0[16], r1[16];
+                __syncwarp();
+                tmem_ld_16(t_acc + c + 16 * q, r0);
+                tmem_ld_16(t_acc + c + 16 * q + 16, r1);
+                tmem_ld_wait();
+                stage16<T, EPI>(p, row, lane, col_base + c, q, r0, stage);
+                stage16<T, EPI>(p, row, lane, col_base + c, q + 1, r1, stage);
+              }
+              if (tma) {
+                fence_async_shared();  // the stage writes are visible to the TMA unit
+                __syncwarp();
+                if (lane == 0 && row_base < p.M) {  // (no store starts past the last row)
+                  const uint32_t src = smem_u32(stage);
+                  tma_store_2d(&out_maps.m[0], src, col_base + c, row_base);
+                  // peers from a different one per CTA (see flush_stage64)
+                  int k = static_cast<int>(blockIdx.x % static_cast<unsigned>(p.n_peers));
+                  for (int kk = 0; kk < p.n_peers; ++kk) {
+                    tma_store_2d(&out_maps.m[1 + k], src, col_base + c, row_base);
+                    if (++k == p.n_peers) k = 0;
+                  }
+                  bulk_commit_group();
+                }
+              } else {
+                flush_stage64<T>(p, row_base, lane, col_base + c, stage);
+              }
             }
-            flush_stage64<T>(p, row_base, lane, col_base + c, stage);
           }
         }
         // Two 16-column TMEM loads in flight per wait.
@@ -722,7 +786,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   // Stores into peers' memory are made visible system-wide before the kernel
   // ends, so that a barrier kernel that follows on the stream can publish them.
-  if (PEERS && warp >= EPI_WARP0) __threadfence_system();
+  if (PEERS && warp >= EPI_WARP0) {
+    if (p.peer_stage == 2 && lane == 0) bulk_wait_all();  // this warp's TMA stores are done
+    __syncwarp();
+    __threadfence_system();
+  }
   tc_fence_before();
   __syncwarp();  // lanes 1-31 of warps 0 and 1 arrive here before their lane 0
   if constexpr (CG == 2) {
@@ -753,7 +821,7 @@ uint32_t tmem_cols_for(int bn) {
 // Shared memory of one CTA: A rows (128) and this CTA's B rows per stage.
 int64_t smem_bytes_for(int bn, int bk, int stages, int cg, bool peer_stage = false) {
   const int64_t ring = static_cast<int64_t>(stages) * (BM + bn / cg) * bk * 2;
-  return 1024 + ring + 8 * (2 * stages + 5) + 16 + (peer_stage ? 16 + GEMM_PEER_STAGE_BYTES : 0);
+  return 1024 + ring + 8 * (2 * stages + 5) + 16 + (peer_stage ? GEMM_PEER_STAGE_SMEM : 0);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -878,6 +946,10 @@ int validate_config(const kf_gemm_config& cfg, int b_mn, std::string* why) {
   }
   if (cfg.stages < 2 || cfg.stages > MAX_STAGES) {
     *why = "stages must be in [2, 16]; got " + std::to_string(cfg.stages);
+    return KF_ERR_INVALID_CONFIG;
+  }
+  if (cfg.epi_store < 0 || cfg.epi_store > 2) {
+    *why = "epi_store must be 0 (library choice), 1 (thread stores) or 2 (TMA stores)";
     return KF_ERR_INVALID_CONFIG;
   }
   if (cfg.cluster_n > 1 || (cg == 1 && cfg.cluster_m > 1) || (cg == 2 && cfg.cluster_m > 2)) {
@@ -1007,7 +1079,20 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   p.bias_on_rows = v.bias_on_rows ? 1 : 0;
   p.n_peers = g.n_peers;
   for (int i = 0; i < g.n_peers; ++i) p.peers[i] = g.peers[i];
-  p.peer_stage = peer_stage ? 1 : 0;
+  OutMaps<true> out_maps{};
+  p.peer_stage = 0;
+  if (peer_stage) {
+    // TMA stores (library choice) unless the config asks for thread stores.
+    p.peer_stage = cfg.epi_store == 1 ? 1 : 2;
+    if (p.peer_stage == 2) {
+      rc = encode_map(&out_maps.m[0], g.dtype, g.c, static_cast<uint64_t>(v.N), static_cast<uint64_t>(v.M),
+                      v.sc_r, 64, 32);
+      for (int i = 0; rc == KF_OK && i < g.n_peers; ++i)
+        rc = encode_map(&out_maps.m[1 + i], g.dtype, g.peers[i], static_cast<uint64_t>(v.N),
+                        static_cast<uint64_t>(v.M), v.sc_r, 64, 32);
+      if (rc != KF_OK) return rc;
+    }
+  }
   p.status = dev.status;
   p.idesc = instr_desc_f16(g.dtype == KF_BF16 ? 1u : 0u, static_cast<uint32_t>(a_major),
                            static_cast<uint32_t>(b_major), BM * cg, static_cast<uint32_t>(bn));
@@ -1087,7 +1172,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   if (units < 1) units = 1;
   lc.gridDim = dim3(static_cast<unsigned>(units * cg));
 
-  void* args[] = {&tm_a, &tm_b, &tm_b_half, &p};
+  void* args[] = {&tm_a, &tm_b, &tm_b_half, &p, &out_maps};
   err = cudaLaunchKernelExC(&lc, fn, args);
   if (err != cudaSuccess) return cuda_error(err, "launch(tcgen05 gemm)");
   return KF_OK;

@@ -67,8 +67,10 @@ int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream
 // Warp-per-row decode GEMV (gemv_rows.cu): y[M, N] = x[M, K] . w[N, K]^T for
 // M <= GEMV_ROWS_MAX_M with K-contiguous, 16-byte-aligned weight rows.
 // Shared memory the all-gathering GEMM epilogue stages its output in: per
-// epilogue warp, 32 rows x 64 columns of 2-byte elements.
+// epilogue warp, 32 rows x 64 columns of 2-byte elements, 1024-byte aligned
+// (the 128-byte swizzle of a TMA box repeats every 8 rows).
 constexpr int GEMM_PEER_STAGE_BYTES = 8 * 32 * 64 * 2;
+constexpr int GEMM_PEER_STAGE_SMEM = GEMM_PEER_STAGE_BYTES + 1024;
 
 constexpr int GEMV_ROWS_MAX_M = 4;
 // kf_gemv picks it by itself up to this many rows (measured on B200: at M=4

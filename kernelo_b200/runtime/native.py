@@ -118,7 +118,8 @@ class KfGemmConfig(ctypes.Structure):
         ("cluster_m", ctypes.c_int32),
         ("cluster_n", ctypes.c_int32),
         ("num_ctas", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 5),
+        ("epi_store", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 4),
     ]
 
 
@@ -251,6 +252,7 @@ class GemmLaunch:
     cluster_m: int = 0
     cluster_n: int = 0
     num_ctas: int = 0
+    epi_store: int = 0
 
     @classmethod
     def from_config(cls, config) -> GemmLaunch:
@@ -269,6 +271,7 @@ class GemmLaunch:
             cluster_m=get("CLUSTER_M", 0),
             cluster_n=get("CLUSTER_N", 0),
             num_ctas=get("NUM_CTAS", 0),
+            epi_store=get("EPI_STORE", 0),
         )
 
     def struct(self) -> KfGemmConfig:
@@ -285,6 +288,7 @@ class GemmLaunch:
             "cluster_m",
             "cluster_n",
             "num_ctas",
+            "epi_store",
         ):
             setattr(s, name, getattr(self, name))
         return s

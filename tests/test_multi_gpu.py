@@ -43,14 +43,16 @@ def _worker(rank: int, world: int, port: int, results) -> None:
         x = torch.randn(m, k, generator=gen).bfloat16().to(dev)
         w = (torch.randn(n, k, generator=gen) * k ** -0.5).bfloat16().to(dev)
         b = (torch.randn(n, generator=gen) * 0.3).bfloat16().to(dev)
-        fused = ShardedFusedLinear(w, b, approximate="none", gather="fused")
+        fused = ShardedFusedLinear(w, b, approximate="none", gather="fused")  # TMA-store epilogue
+        threads = ShardedFusedLinear(w, b, approximate="none", gather="fused", config={"EPI_STORE": 1})
         nccl = ShardedFusedLinear(w, b, approximate="none", gather="nccl")
         outs = []
         for step in range(3):  # both buffers, then the first again
             xs = x if step != 1 else (x * 0.5)
             y = fused(xs).clone()
+            y_threads = threads(xs).clone()
             y_ref = nccl(xs).clone()
-            outs.append(bool(torch.equal(y, y_ref)))
+            outs.append(bool(torch.equal(y, y_ref)) and bool(torch.equal(y_threads, y_ref)))
         torch.cuda.synchronize()
         from kernelo_b200.testing import verify
 
@@ -98,6 +100,7 @@ def _worker(rank: int, world: int, port: int, results) -> None:
             timed_out = (word & 0xFF) == native.KF_ERR_TIMEOUT and (word >> 8) == 7
         dist.barrier()
         fused.close()
+        threads.close()
         results[rank] = {"equal": outs, "host": host_ok, "status": status, "oracle": err,
                          "timed_out": timed_out}
     finally:
