@@ -1,0 +1,223 @@
+// Decode-shape GEMV with 16-row weight tiles: y[m, n] = sum_k x[m, k] w[n, k]
+// for M <= 16 and a weight whose rows are K-contiguous (nn.Linear's [N, K]).
+//
+// The product is ~M FLOP per weight byte, so the kernel's job is to stream W
+// from HBM at full rate; the arithmetic must only stay out of the way. One CTA
+// takes one 16-row tile of W and splits its K extent over its S warps. Lane
+// (g, t) (g = lane / 4, t = lane % 4) loads 16-byte vectors of weight rows g
+// and g + 8 at vector positions t, t + 4, t + 8, ... of its warp's K slice, so
+// each quad of lanes reads 64 contiguous bytes of a row and every row is read
+// front to back. Those registers are the A fragments of `mma.sync.m16n8k16`
+// as loaded: the K order inside an MMA is free as long as A and B agree, and a
+// lane's B fragment is x[g (+8)][the same eight K positions], a 16-byte load
+// from L1/L2 (x is a few KB). So there is no conversion, no shared-memory
+// staging of x and no prologue: the first weight loads go out at once. Each
+// 16-byte vector pair feeds two MMAs per 8 rows of x; products accumulate in
+// fp32. The S partial tiles are summed through shared memory and rounded
+// once into y.
+//
+// The tensor-core instruction here is the warp-level mma.sync, not tcgen05:
+// at M <= 16 the contraction is under 1 % of the time, and what decides the
+// speed is the weight stream. tcgen05 operands come from shared memory as TMA
+// boxes of 128 rows x 128 bytes, which measured 3.5 TB/s on this shape; rows
+// streamed contiguously by warps measured 4.8 TB/s (same W, same M).
+//
+// Replaces the reference's matmul launch at decode shapes
+// (kernelforge/kernels/matmul.py:132-155 with M in {1, 4, 16}); fp32
+// accumulation and one output rounding as in the reference's matmul.
+#include "kf_common.cuh"
+#include "kf_internal.h"
+
+namespace kf {
+namespace {
+
+struct GemvMmaParams {
+  const void* x;
+  long long sx_m;  // x rows are K-contiguous
+  const void* w;
+  long long sw_n;
+  void* y;
+  long long sy_m, sy_n;
+  int M, N, K;
+};
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  if constexpr (DType<T>::code == KF_BF16) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+// NT: 8-row groups of x (1 for M <= 8, 2 for M <= 16); S: warps per CTA (K
+// slices); U: vector pairs per lane in flight.
+// At least five CTAs per SM: a tile's CTA lasts about the whole kernel, so
+// all of them (688 for N = 11008) must be resident at once.
+template <typename T, int NT, int S, int U>
+__global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams p) {
+  __shared__ float4 part[S > 1 ? S - 1 : 1][32][NT];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int n0 = blockIdx.x * 16;
+  const int nvec = p.K / 8;  // 16-byte vectors per row (K % 8 == 0)
+  // This warp's K slice, in whole quads of vectors.
+  const int quads = (nvec + 3) / 4;
+  const int q0 = static_cast<int>(static_cast<long long>(quads) * warp / S);
+  const int q1 = static_cast<int>(static_cast<long long>(quads) * (warp + 1) / S);
+  const int ra = min(n0 + g, p.N - 1), rb = min(n0 + g + 8, p.N - 1);  // clamped rows are not stored
+  const uint4* wa = reinterpret_cast<const uint4*>(static_cast<const T*>(p.w) + ra * p.sw_n);
+  const uint4* wb = reinterpret_cast<const uint4*>(static_cast<const T*>(p.w) + rb * p.sw_n);
+  const uint4* xr[NT];
+  bool xon[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int m = g + 8 * nt;
+    xon[nt] = m < p.M;
+    xr[nt] = reinterpret_cast<const uint4*>(static_cast<const T*>(p.x) + (xon[nt] ? m : 0) * p.sx_m);
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[nt][i] = 0.0f;
+
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  for (int q = q0; q < q1; q += U) {
+    // The weight loads of the batch go out first (HBM); x is read per vector
+    // just before its MMAs (L1 hits), which keeps its registers short-lived.
+    uint4 va[U], vb[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int v = 4 * (q + u) + t;
+      const bool ok = q + u < q1 && v < nvec;
+      va[u] = ok ? __ldcs(wa + v) : zero;
+      vb[u] = ok ? __ldcs(wb + v) : zero;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int v = 4 * (q + u) + t;
+      const bool ok = q + u < q1 && v < nvec;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint4 vx = (ok && xon[nt]) ? __ldg(xr[nt] + v) : zero;
+        // elements 0-3 of the vector, then 4-7: logical k {2t, 2t+1, 2t+8, 2t+9}
+        mma16816<T>(acc[nt], va[u].x, vb[u].x, va[u].y, vb[u].y, vx.x, vx.y);
+        mma16816<T>(acc[nt], va[u].z, vb[u].z, va[u].w, vb[u].w, vx.z, vx.w);
+      }
+    }
+  }
+
+  if constexpr (S > 1) {
+    if (warp > 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        part[warp - 1][lane][nt] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    }
+    __syncthreads();
+    if (warp > 0) return;
+#pragma unroll
+    for (int s = 0; s < S - 1; ++s)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const float4 o = part[s][lane][nt];
+        acc[nt][0] += o.x;
+        acc[nt][1] += o.y;
+        acc[nt][2] += o.z;
+        acc[nt][3] += o.w;
+      }
+  }
+  // D fragment: acc[nt][0..1] = rows n0+g, x rows 8nt+2t, +1; [2..3] = rows n0+g+8.
+  T* y = static_cast<T*>(p.y);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = 8 * nt + 2 * t + (i & 1);
+      const int n = n0 + g + (i >> 1) * 8;
+      if (m < p.M && n < p.N) y[m * p.sy_m + static_cast<long long>(n) * p.sy_n] = from_f32<T>(acc[nt][i]);
+    }
+  }
+}
+
+template <typename T, int NT, int S, int U>
+int launch_shape(const GemvMmaParams& p, cudaStream_t stream) {
+  const unsigned tiles = static_cast<unsigned>((p.N + 15) / 16);
+  gemv_mma_kernel<T, NT, S, U><<<tiles, 32 * S, 0, stream>>>(p);
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_error(err, "launch(gemv mma)");
+  return KF_OK;
+}
+
+// Launch shapes (S warps per tile, U vector pairs in flight per lane): config
+// block_m selects S and stages selects U; zero picks the default, measured
+// on B200 at N = 11008, K = 4096: (8, 2) up to 8 rows of x (17.0 us at M=1,
+// 17.9 at M=4), (6, 4) above (19.6 us at M=16; 8 warps of 4 pairs spill).
+template <typename T, int NT>
+int launch_nt(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t stream) {
+  const int s = cfg.block_m != 0 ? cfg.block_m : (NT == 1 ? 8 : 6);
+  const int u = cfg.stages != 0 ? cfg.stages : (NT == 1 ? 2 : 4);
+  if (s == 4 && u == 4) return launch_shape<T, NT, 4, 4>(p, stream);
+  if (s == 4 && u == 2) return launch_shape<T, NT, 4, 2>(p, stream);
+  if (s == 4 && u == 8) return launch_shape<T, NT, 4, 8>(p, stream);
+  if (s == 6 && u == 2) return launch_shape<T, NT, 6, 2>(p, stream);
+  if (s == 6 && u == 4) return launch_shape<T, NT, 6, 4>(p, stream);
+  if (s == 8 && u == 2) return launch_shape<T, NT, 8, 2>(p, stream);
+  if (s == 8 && u == 4) return launch_shape<T, NT, 8, 4>(p, stream);
+  return set_error(KF_ERR_INVALID_CONFIG, "tile GEMV: no compiled shape with " + std::to_string(s) +
+                                              " warps per tile and " + std::to_string(u) +
+                                              " vector pairs in flight");
+}
+
+template <typename T>
+int launch_typed(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t stream) {
+  return p.M <= 8 ? launch_nt<T, 1>(p, cfg, stream) : launch_nt<T, 2>(p, cfg, stream);
+}
+
+}  // namespace
+
+bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w, int64_t sw_n,
+                        int64_t sw_k, int64_t M, int64_t N, int64_t K, std::string* why) {
+  auto no = [&](const char* msg) {
+    if (why) *why = msg;
+    return false;
+  };
+  if (dtype != KF_FP16 && dtype != KF_BF16) return no("the tile GEMV takes fp16 or bf16");
+  if (M < 1 || M > GEMV_MMA_MAX_M) return no("the tile GEMV takes 1..16 rows of x");
+  if (N > INT32_MAX || K > INT32_MAX) return no("dimensions above 2^31");
+  if (K % 8 != 0) return no("K must be a multiple of 8 (whole 16-byte vectors)");
+  if (sw_k != 1 || sx_k != 1) return no("weight and x rows must be K-contiguous");
+  if ((reinterpret_cast<uintptr_t>(w) & 15u) != 0 || ((sw_n * 2) & 15) != 0)
+    return no("weight rows must start on 16-byte boundaries");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (M > 1 && ((sx_m * 2) & 15) != 0))
+    return no("x rows must start on 16-byte boundaries");
+  return true;
+}
+
+int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
+                    int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
+                    const kf_gemm_config& cfg, cudaStream_t stream) {
+  GemvMmaParams p{};
+  p.x = x;
+  p.sx_m = sx_m;
+  p.w = w;
+  p.sw_n = sw_n;
+  p.y = y;
+  p.sy_m = sy_m;
+  p.sy_n = sy_n;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  if (N == 0 || M == 0) return KF_OK;
+  if (dtype == KF_BF16) return launch_typed<__nv_bfloat16>(p, cfg, stream);
+  return launch_typed<__half>(p, cfg, stream);
+}
+
+}  // namespace kf

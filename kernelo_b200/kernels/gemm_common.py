@@ -23,6 +23,28 @@ KERNEL_TCGEN05 = 1
 KERNEL_SIMT = 2
 #: kf_gemv only: warps streaming K-contiguous weight rows, M <= 4 (csrc/gemv_rows.cu).
 KERNEL_WARP_ROWS = 3
+#: kf_gemv's 16-row weight tiles on mma.sync (fp16/bf16, M <= 16, K % 8 == 0);
+#: BLOCK_M = warps per tile (K slices), num_stages = vector pairs in flight.
+KERNEL_TILE_ROWS = 4
+TILE_ROWS_MAX_M = 16
+#: (warps per tile, vector pairs in flight) compiled in gemv_mma.cu
+TILE_ROWS_SHAPES = ((8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8))
+
+
+def tile_rows_default(m: int) -> tuple[int, int]:
+    """The kernel's default shape (mirrors gemv_mma.cu)."""
+    return (8, 2) if m <= 8 else (6, 4)
+
+
+def tile_rows_reject(m: int, k: int, dtype: torch.dtype) -> str | None:
+    """Why the tile GEMV cannot take this contiguous problem (None: it can)."""
+    if dtype not in (torch.float16, torch.bfloat16):
+        return "the tile GEMV takes fp16 or bf16"
+    if not 1 <= m <= TILE_ROWS_MAX_M:
+        return f"the tile GEMV takes 1..{TILE_ROWS_MAX_M} rows of x, got M={m}"
+    if k % 8 != 0:
+        return "the tile GEMV needs K % 8 == 0 (whole 16-byte vectors)"
+    return None
 WARP_ROWS_MAX_M = 4
 #: The library default up to this M (measured on B200: at M=4 the tcgen05 GEMV is faster).
 WARP_ROWS_AUTO_MAX_M = 2

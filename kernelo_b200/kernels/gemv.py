@@ -75,6 +75,9 @@ def gemv(
 
 def default_config(m: int, n: int, k: int, dtype: torch.dtype, *, sm_count: int = 148) -> KernelConfig:
     """The library's choice for contiguous [M,K] x and [N,K] w (mirrors kf_gemv)."""
+    if gc.tile_rows_reject(m, k, dtype) is None:
+        warps, pairs = gc.tile_rows_default(m)
+        return KernelConfig("gemv", KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
     if 1 <= m <= gc.WARP_ROWS_AUTO_MAX_M and gc.warp_rows_smem_bytes(m, k, itemsize(dtype)) <= gc.SM100_SMEM_PER_BLOCK:
         return KernelConfig("gemv", KERNEL=gc.KERNEL_WARP_ROWS)
     if gc.shape_allows_tcgen05(m, n, k, dtype, b_layout="nk") is not None:

@@ -325,27 +325,39 @@ class FusedLinearErfSearchSpace(_Sm100GemmSpace):
 
 
 class GemvSearchSpace(_Sm100GemmSpace):
-    """The GEMM grid plus the warp-per-row CUDA-core GEMV (``KERNEL=3``)."""
+    """The GEMM grid plus the decode kernels: 16-row weight tiles on mma.sync
+    (``KERNEL=4``; BLOCK_M warps per tile, num_stages vector pairs in flight)
+    and the warp-per-row CUDA-core GEMV (``KERNEL=3``)."""
 
     operation = "gemv"
     b_layout = "nk"
 
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
+        for warps, pairs in gc.TILE_ROWS_SHAPES:
+            yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
         yield KernelConfig(self.operation, KERNEL=gc.KERNEL_WARP_ROWS)
         yield from super().grid(problem)
 
     def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
+        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
+            m = self.dims(problem)[0]
+            return (config["BLOCK_M"] - 1) * 32 * (1 if m <= 8 else 2) * 16  # the K-slice partials
         if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
             m, _, k = self.dims(problem)
             return gc.warp_rows_smem_bytes(m, k, itemsize(problem.dtype))
         return super().shared_memory_bytes(config, problem)
 
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
+        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
+            return ceil_div(self.dims(problem)[1], 16)  # one CTA per 16 weight rows
         if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
             return ceil_div(self.dims(problem)[1], 16)  # 16 warps per CTA, a row or two each
         return super().num_programs(config, problem)
 
     def reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
+        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
+            m, _, k = self.dims(problem)
+            return gc.tile_rows_reject(m, k, problem.dtype)
         if config["KERNEL"] != gc.KERNEL_WARP_ROWS:
             return super().reject_reason(config, problem, caps)
         m, _, _ = self.dims(problem)
@@ -357,7 +369,12 @@ class GemvSearchSpace(_Sm100GemmSpace):
         return None
 
     def priority(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> tuple[float, ...]:
-        """The warp-per-row kernel first where it is the library default (M <= 2)."""
+        """The tile kernel's default shape first, then its other shapes, then the
+        warp-per-row kernel (first where it is the library default, M <= 2, and
+        the tile kernel cannot run)."""
+        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
+            default = (config["BLOCK_M"], config["num_stages"]) == gc.tile_rows_default(self.dims(problem)[0])
+            return (-3,) if default else (-2,)
         if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
             return (-1,) if self.dims(problem)[0] <= gc.WARP_ROWS_AUTO_MAX_M else (2,)
         return super().priority(config, problem, caps)

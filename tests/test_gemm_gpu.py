@@ -336,10 +336,72 @@ def test_gemv_warp_rows_refuses_unaligned_weight_rows(device):
 def test_gemv_default_kernel_choice():
     from kernelo_b200.kernels.gemv import default_config
 
-    assert default_config(1, 11008, 4096, torch.float16)["KERNEL"] == 3
-    assert default_config(2, 11008, 4096, torch.bfloat16)["KERNEL"] == 3
-    assert default_config(4, 11008, 4096, torch.float16)["KERNEL"] == 1
-    assert default_config(16, 11008, 4096, torch.float16)["KERNEL"] == 1
+    for m in (1, 2, 4, 16):
+        assert default_config(m, 11008, 4096, torch.float16)["KERNEL"] == 4
+    assert default_config(1, 11008, 4096, torch.float32)["KERNEL"] == 3
+    assert default_config(2, 11008, 4099, torch.bfloat16)["KERNEL"] == 3  # K % 8 != 0
+    assert default_config(17, 11008, 4096, torch.float16)["KERNEL"] == 1
+
+
+# ------------------------------------------------------------------ 16-row tile GEMV (mma.sync)
+def tile_cfg(warps=0, pairs=0):
+    return KernelConfig("gemv", KERNEL=4, BLOCK_M=warps, num_stages=pairs)
+
+
+@pytest.mark.parametrize("m", [1, 3, 4, 8, 9, 16])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_gemv_tile_rows(m, dtype, device):
+    """Both x-row groupings (M <= 8, M <= 16) with unused rows masked; N = 1000
+    ends in a half tile; K = 1032 is 129 vectors, so the K slices are uneven
+    and the last quad of vectors is partial."""
+    gen = torch.Generator().manual_seed(40 + m)
+    x = torch.randn(m, 1032, generator=gen).to(dtype).to(device)
+    w = (torch.randn(1000, 1032, generator=gen) * 1032 ** -0.5).to(dtype).to(device)
+    expected = ref.gemv_ref(host(x), host(w))
+    gate(expected, gemv(x, w, config=tile_cfg()), dtype, context=f"M={m} default shape")
+    gate(expected, gemv(x, w), dtype, context=f"M={m} library choice")
+
+
+@pytest.mark.parametrize("shape", [(8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8)])
+@pytest.mark.parametrize("m", [4, 16])
+def test_gemv_tile_rows_every_shape(shape, m, device):
+    gen = torch.Generator().manual_seed(7 * shape[0] + shape[1])
+    x = torch.randn(m, 4096, generator=gen).half().to(device)
+    w = (torch.randn(11008, 4096, generator=gen) * 4096 ** -0.5).half().to(device)
+    gate(ref.gemv_ref(host(x), host(w)), gemv(x, w, config=tile_cfg(*shape)), torch.float16,
+         context=f"shape {shape} M={m}")
+
+
+def test_gemv_tile_rows_edges_and_strides(device):
+    """K of one and two vectors, fewer weight rows than a tile, padded weight and
+    x rows (16-byte aligned), y written transposed."""
+    gen = torch.Generator().manual_seed(77)
+    for n, k in ((5, 8), (16, 16), (17, 24), (33, 264)):
+        x = torch.randn(3, k, generator=gen).bfloat16().to(device)
+        w = torch.randn(n, k, generator=gen).bfloat16().to(device)
+        gate(ref.gemv_ref(host(x), host(w)), gemv(x, w, config=tile_cfg()), torch.bfloat16, context=f"{n}x{k}")
+    wb = (torch.randn(300, 1040, generator=gen) * 0.03).half().to(device)
+    w = wb[:, :1032]
+    xb = torch.randn(12, 1096, generator=gen).half().to(device)
+    x = xb[:, :1032]
+    out = torch.empty(300, 12, device=device, dtype=torch.float16).t()
+    gemv(x, w, config=tile_cfg(), out=out)
+    gate(ref.gemv_ref(host(x), host(w)), out, torch.float16)
+    assert native.device_status(device.index) == 0
+
+
+def test_gemv_tile_rows_refusals(device):
+    from kernelo_b200.runtime.native import OutOfResources
+
+    x = torch.randn(2, 4099, device=device, dtype=torch.float16)
+    w = torch.randn(64, 4099, device=device, dtype=torch.float16)
+    with pytest.raises(OutOfResources, match="multiple of 8"):
+        gemv(x, w, config=tile_cfg())
+    gate(ref.gemv_ref(host(x), host(w)), gemv(x, w), torch.float16)  # the library choice falls back
+    with pytest.raises(OutOfResources, match="fp16 or bf16"):
+        gemv(x[:, :4096].float(), w[:, :4096].float(), config=tile_cfg())
+    with pytest.raises((OutOfResources, ValueError)):
+        gemv(x[:, :4096], w[:, :4096], config=tile_cfg(5, 3))  # no such compiled shape
 
 
 # ------------------------------------------------------------------ host-buffer fused linear

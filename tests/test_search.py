@@ -191,14 +191,34 @@ def test_unknown_space_is_an_error():
     assert isinstance(search_space("gemv"), GemvSearchSpace)
 
 
+def test_gemv_tile_rows_candidates(b200_caps):
+    """The 16-row tile kernel leads for 16-bit x up to 16 rows, its default
+    shape first; fp32, M > 16 and K % 8 != 0 reject it."""
+    space = GemvSearchSpace()
+    for m, default in ((1, (8, 2)), (4, (8, 2)), (16, (6, 4))):
+        p = Problem.create("gemv", "bf16", M=m, N=11008, K=4096)
+        cands = space.candidates(p, b200_caps)
+        assert cands[0]["KERNEL"] == gc.KERNEL_TILE_ROWS
+        assert (cands[0]["BLOCK_M"], cands[0]["num_stages"]) == default
+        tiles = [c for c in cands if c["KERNEL"] == gc.KERNEL_TILE_ROWS]
+        assert len(tiles) == len(gc.TILE_ROWS_SHAPES)
+        assert space.num_programs(tiles[0], p) == 688
+    tile = KernelConfig("gemv", KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=8, num_stages=2)
+    assert space.reject_reason(tile, Problem.create("gemv", "fp32", M=1, N=64, K=64), b200_caps).startswith(
+        "the tile GEMV takes fp16 or bf16")
+    assert "1..16 rows" in space.reject_reason(tile, Problem.create("gemv", "fp16", M=17, N=64, K=64), b200_caps)
+    assert "K % 8" in space.reject_reason(tile, Problem.create("gemv", "fp16", M=2, N=64, K=4099), b200_caps)
+
+
 def test_gemv_warp_rows_candidate(b200_caps):
     space = GemvSearchSpace()
-    one = Problem.create("gemv", "fp16", M=1, N=11008, K=4096)
+    # fp32 x: the tile kernel is out, the warp-per-row kernel is the default at M <= 2
+    one = Problem.create("gemv", "fp32", M=1, N=11008, K=4096)
     cands = space.candidates(one, b200_caps)
-    assert cands[0]["KERNEL"] == gc.KERNEL_WARP_ROWS, "M=1: the warp-per-row kernel is the default"
+    assert cands[0]["KERNEL"] == gc.KERNEL_WARP_ROWS, "M=1 fp32: the warp-per-row kernel is the default"
     four = Problem.create("gemv", "fp16", M=4, N=11008, K=4096)
     cands4 = space.candidates(four, b200_caps)
-    assert cands4[0]["KERNEL"] == gc.KERNEL_TCGEN05 and any(c["KERNEL"] == 3 for c in cands4)
+    assert any(c["KERNEL"] == 3 for c in cands4)
     wide = Problem.create("gemv", "fp16", M=16, N=11008, K=4096)
     warp_rows = KernelConfig("gemv", KERNEL=gc.KERNEL_WARP_ROWS)
     assert space.reject_reason(warp_rows, wide, b200_caps).startswith("warp-per-row GEMV takes at most 4")
