@@ -80,6 +80,10 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
                     int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
                     const kf_gemm_config& cfg, cudaStream_t stream);
 
+// Softmax kernel choice by row width in 16-byte vectors (rows.cu).
+constexpr long long SOFTMAX_STREAM_MAX_VECTORS = 128;     // up to 2 KB: streaming kernel
+constexpr long long SOFTMAX_REGISTER_MAX_VECTORS = 4096;  // up to 64 KB: register kernel
+
 constexpr int GEMV_ROWS_MAX_M = 4;
 // kf_gemv picks it by itself up to this many rows (measured on B200: at M=4
 // the tcgen05 GEMV streams the weight faster).

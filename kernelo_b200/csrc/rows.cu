@@ -396,15 +396,23 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
     if (register_fields != stream_fields) {
       c.kernel = register_fields ? KF_ROWS_REGISTER : KF_ROWS_STREAM;
     } else {
-      // Measured on B200: the streaming kernel wins for softmax at every
-      // baseline width; RMSNorm's lighter arithmetic runs as fast or faster
-      // in the register kernel.
+      // Measured on B200 (graph-timed, inputs beyond L2): softmax rows of up
+      // to 2 KB stream (32768 x 1000 fp16: 0.78 of the copy bandwidth against
+      // 0.70 in registers); rows up to 64 KB sit in registers at about eight
+      // vectors per thread (2048 / 4096 / 8192 fp16 columns: 0.95 / 0.99 /
+      // 0.98, against 0.80 / 0.80 / 0.87 streamed); wider rows stream again.
+      // RMSNorm's lighter arithmetic runs as fast in the register kernel.
+      const long long nvec_row = ceil_div(a.cols * elem, 16LL);
       const int warps = c.num_warps > 0 ? c.num_warps : stream_default_warps(a.cols, elem);
-      const long long per_thread = ceil_div(a.cols * elem / 16, 32LL * warps);
-      c.kernel = (a.op == 0 && a.rows >= 2LL * dev.sm_count && per_thread <= 16 &&
-                  rows_stream_supported(a, dev.max_smem_optin, nullptr))
-                     ? KF_ROWS_STREAM
-                     : KF_ROWS_REGISTER;
+      const long long per_thread = ceil_div(nvec_row, 32LL * warps);
+      const bool stream_ok = a.op == 0 && a.rows >= 2LL * dev.sm_count && per_thread <= 16 &&
+                             rows_stream_supported(a, dev.max_smem_optin, nullptr);
+      const bool narrow = nvec_row <= SOFTMAX_STREAM_MAX_VECTORS;
+      const bool in_registers = nvec_row <= SOFTMAX_REGISTER_MAX_VECTORS;
+      c.kernel = stream_ok && (narrow || !in_registers) ? KF_ROWS_STREAM : KF_ROWS_REGISTER;
+      // Two slots per row group leave room for two CTAs per SM, which beats
+      // deeper slots on narrow rows (25.8 against 27.6 us at 1000 columns).
+      if (c.kernel == KF_ROWS_STREAM && narrow && c.stages <= 0) c.stages = 2;
     }
   }
   if (c.kernel == KF_ROWS_STREAM) {
@@ -412,6 +420,15 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
     return c;
   }
   const long long nvec = (a.cols * elem + 15) / 16;
+  if (a.op == 0 && c.num_warps <= 0 && c.cluster <= 0 && nvec <= SOFTMAX_REGISTER_MAX_VECTORS) {
+    // Softmax in registers: about eight 16-byte vectors per thread (a power
+    // of two of warps, at most 16 vectors each), one CTA per row.
+    long long w = 1;
+    while (2 * w * 256 <= nvec) w *= 2;
+    while (ceil_div(nvec, 32 * w) > 16) w *= 2;
+    c.num_warps = static_cast<int>(w);
+    c.cluster = 1;
+  }
   if (c.cluster <= 0) {
     // One CTA holds up to 1024 threads x 4 vectors (64 KiB) of the row in registers.
     c.cluster = 1;

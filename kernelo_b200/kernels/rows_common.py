@@ -3,14 +3,16 @@
 ``default_rows_config`` mirrors ``resolve_rows_config`` in ``csrc/rows.cu``:
 
 * a softmax over many rows (at least two per SM) whose input and output rows
-  sit at the same 16-byte phase goes to the persistent streaming kernel
-  (``ROW_KERNEL=2``, ``csrc/rows_stream.cu``): row groups of ``num_warps`` warps
-  (the fewest, as a power of two, that hold a row at up to 16 vectors a
-  thread) each keeping their next rows in flight as bulk copies into
-  shared-memory slots;
-* otherwise -- and for RMSNorm, whose lighter arithmetic measured as fast or
-  faster there -- the register kernel (``ROW_KERNEL=1``, ``csrc/rows.cu``): about four
-  16-byte vectors per thread, one CTA per row until a row exceeds 4096 vectors
+  sit at the same 16-byte phase, with rows of up to 2 KB or beyond 64 KB, goes
+  to the persistent streaming kernel (``ROW_KERNEL=2``,
+  ``csrc/rows_stream.cu``): row groups of ``num_warps`` warps (the fewest, as a
+  power of two, that hold a row at up to 16 vectors a thread) each keeping
+  their next rows in flight as bulk copies into shared-memory slots (two slots
+  per group for the narrow rows);
+* other softmax rows of up to 64 KB go to the register kernel (``ROW_KERNEL=1``,
+  ``csrc/rows.cu``) at about eight 16-byte vectors per thread, one CTA per row;
+* RMSNorm, and whatever else is left, to the register kernel at about four
+  vectors per thread, one CTA per row until a row exceeds 4096 vectors
   (64 KiB), then a power-of-two cluster of CTAs shares it.
 """
 
@@ -62,6 +64,11 @@ def same_phase(x: torch.Tensor | None, cols: int) -> bool:
     return x.data_ptr() % 16 == 0 and (x.stride(0) * size) % 16 == (cols * size) % 16
 
 
+#: Softmax kernel choice by row width in 16-byte vectors (mirrors kf_internal.h).
+SOFTMAX_STREAM_MAX_VECTORS = 128
+SOFTMAX_REGISTER_MAX_VECTORS = 4096
+
+
 def default_rows_config(
     operation: str,
     cols: int,
@@ -71,21 +78,44 @@ def default_rows_config(
     x: torch.Tensor | None = None,
     sm_count: int = 148,
 ) -> KernelConfig:
+    """The library's choice (mirrors resolve_rows_config in rows.cu): softmax
+    rows up to 2 KB stream, rows up to 64 KB sit in registers at about eight
+    16-byte vectors per thread, wider rows stream again (when there are enough
+    rows for every SM and the streaming kernel takes the layout); RMSNorm uses
+    the register kernel at about four vectors per thread."""
     block = next_power_of_2(max(cols, 1))
-    if (
-        operation == "softmax"
-        and rows is not None
-        and rows >= 2 * sm_count
-        and stream_fits(cols, dtype)
-        and same_phase(x, cols)
-    ):
-        return KernelConfig(
-            operation,
-            BLOCK_SIZE=block,
-            ROW_KERNEL=ROW_KERNEL_STREAM,
-            num_warps=stream_default_warps(cols, dtype),
-        )
     nvec = ceil_div(cols * itemsize(dtype), 16)
+    if operation == "softmax":
+        narrow = nvec <= SOFTMAX_STREAM_MAX_VECTORS
+        in_registers = nvec <= SOFTMAX_REGISTER_MAX_VECTORS
+        if (
+            (narrow or not in_registers)
+            and rows is not None
+            and rows >= 2 * sm_count
+            and stream_fits(cols, dtype)
+            and same_phase(x, cols)
+        ):
+            cfg = KernelConfig(
+                operation,
+                BLOCK_SIZE=block,
+                ROW_KERNEL=ROW_KERNEL_STREAM,
+                num_warps=stream_default_warps(cols, dtype),
+            )
+            return cfg.replace(num_stages=2) if narrow else cfg
+        if in_registers:
+            warps = 1
+            while 2 * warps * 256 <= nvec:
+                warps *= 2
+            while ceil_div(nvec, 32 * warps) > 16:
+                warps *= 2
+            return KernelConfig(
+                operation,
+                BLOCK_SIZE=block,
+                ROW_KERNEL=ROW_KERNEL_REGISTER,
+                ROWS_PER_PROGRAM=1,
+                num_warps=warps,
+                CLUSTER=1,
+            )
     cluster = 1
     if nvec > VECTORS_PER_CTA:
         cluster = next_power_of_2(min(8, ceil_div(nvec, VECTORS_PER_CTA)))

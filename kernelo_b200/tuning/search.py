@@ -407,6 +407,8 @@ class _RowReductionSpace(SearchSpace):
         block = next_power_of_2(problem.dims_dict["cols"])
         for warps in self.STREAM_WARPS:
             yield KernelConfig(self.operation, BLOCK_SIZE=block, ROW_KERNEL=2, num_warps=warps)
+            # two slots per row group: room for two CTAs per SM
+            yield KernelConfig(self.operation, BLOCK_SIZE=block, ROW_KERNEL=2, num_warps=warps, num_stages=2)
         for cluster, warps, rows in product(self.CLUSTER, self.NUM_WARPS, self.ROWS_PER_PROGRAM):
             yield KernelConfig(
                 self.operation,
@@ -444,6 +446,12 @@ class _RowReductionSpace(SearchSpace):
         slot = ceil_div(cols * problem.itemsize // 16 * 16, 128) * 128
         if self.STREAM_FIXED_SMEM + slot + 8 > caps.max_shared_memory_per_block:
             return f"streaming kernel: a row of {slot} bytes does not fit one shared-memory slot"
+        stages = config.get("num_stages", 0)
+        if stages:
+            groups = self.STREAM_CONSUMER_WARPS // warps
+            need = self.STREAM_FIXED_SMEM + groups * stages * (slot + 8)
+            if need > caps.max_shared_memory_per_block:
+                return f"streaming kernel: {stages} row slots per group of {slot} bytes exceed shared memory"
         nv = self.vectors_per_thread(config, problem)
         if nv > self.MAX_VECTORS_PER_THREAD:
             return f"register pressure: {nv} vectors per thread"
@@ -476,17 +484,23 @@ class _RowReductionSpace(SearchSpace):
         return None
 
     def priority(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> tuple[float, ...]:
-        """Memory-bound: for a softmax with at least two rows per SM the
-        streaming kernel first (as the library default), then fill the machine,
-        keep about four 16-byte loads in flight per thread, prefer no cluster,
-        then fewer rows per program."""
-        rows = problem.dims_dict["rows"]
-        stream_first = self.operation == "softmax" and rows >= 2 * caps.sm_count
+        """Memory-bound: the library default first, then its kernel (streaming
+        or register), then fill the machine, keep about as many 16-byte loads
+        in flight per thread as the default does (eight for a softmax in
+        registers, else four), prefer no cluster, then fewer rows per program."""
+        from kernelo_b200.kernels.rows_common import default_rows_config
+
+        d = problem.dims_dict
+        default = default_rows_config(self.operation, d["cols"], problem.dtype, rows=d["rows"],
+                                      sm_count=caps.sm_count)
+        is_default = dict(config) == dict(default)
+        stream_first = self.is_stream(default)
         kernel_rank = 0 if self.is_stream(config) == stream_first else 1
         programs = min(self.num_programs(config, problem), caps.sm_count)
         nv = self.vectors_per_thread(config, problem)
-        return (kernel_rank, -programs, abs(math.log2(nv) - 2), config.get("CLUSTER", 1),
-                config.get("ROWS_PER_PROGRAM", 1))
+        target = 3 if (self.operation == "softmax" and not stream_first) else 2
+        return (0 if is_default else 1, kernel_rank, -programs, abs(math.log2(nv) - target),
+                config.get("CLUSTER", 1), config.get("ROWS_PER_PROGRAM", 1))
 
 
 class SoftmaxSearchSpace(_RowReductionSpace):

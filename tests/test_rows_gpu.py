@@ -238,12 +238,23 @@ def test_stream_kernel_strided_rows(device):
         softmax(odd, config=stream_cfg("softmax", 1000, num_warps=1))
 
 
-def test_stream_kernel_is_the_default_for_many_rows(device):
+def test_softmax_default_kernel_by_row_width(device):
+    """Many rows: rows up to 2 KB stream (two slots per group), rows up to
+    64 KB sit in registers at ~8 vectors per thread, wider rows stream; few
+    rows, or x off the output's 16-byte phase, stay in registers. Each default
+    also runs and passes the gate."""
     from kernelo_b200.kernels.rows_common import default_rows_config
 
     x = rand(4096, 4096, torch.float16, device)
-    assert default_rows_config("softmax", 4096, torch.float16, rows=4096, x=x)["ROW_KERNEL"] == 2
-    assert default_rows_config("softmax", 4096, torch.float16, rows=64, x=x[:64])["ROW_KERNEL"] == 1
+    narrow = rand(4096, 1000, torch.float16, device)
+    cfg = default_rows_config("softmax", 1000, torch.float16, rows=4096, x=narrow)
+    assert (cfg["ROW_KERNEL"], cfg["num_warps"], cfg["num_stages"]) == (2, 1, 2)
+    gate(ref.softmax_ref(host(narrow)), softmax(narrow), torch.float16)
+    cfg = default_rows_config("softmax", 4096, torch.float16, rows=4096, x=x)
+    assert (cfg["ROW_KERNEL"], cfg["num_warps"]) == (1, 2)
+    gate(ref.softmax_ref(host(x)), softmax(x), torch.float16)
+    assert default_rows_config("softmax", 8192, torch.float16, rows=4096)["num_warps"] == 4
+    assert default_rows_config("softmax", 1000, torch.float16, rows=64, x=narrow[:64])["ROW_KERNEL"] == 1
     assert default_rows_config("softmax", 32000, torch.float32, rows=32768)["ROW_KERNEL"] == 2
     assert default_rows_config("rmsnorm", 4096, torch.float16, rows=16384, x=x)["ROW_KERNEL"] == 1
 

@@ -135,16 +135,21 @@ def test_explain_names_rules_and_device(b200_caps):
 
 def test_row_space_shape_and_rules(b200_caps):
     problem = Problem.create("rmsnorm", "fp16", rows=16384, cols=4096)
-    cands = RMSNormSearchSpace().candidates(problem, b200_caps)
+    cands = RMSNormSearchSpace().candidates(problem, b200_caps, max_candidates=1000)
     register = [c for c in cands if c["ROW_KERNEL"] == 1]
     stream = [c for c in cands if c["ROW_KERNEL"] == 2]
     assert register and {k for c in register for k in c} == {
         "ROW_KERNEL", "BLOCK_SIZE", "ROWS_PER_PROGRAM", "num_warps", "CLUSTER"}
-    assert stream and {k for c in stream for k in c} == {"ROW_KERNEL", "BLOCK_SIZE", "num_warps"}
-    assert sorted(c["num_warps"] for c in stream) == [1, 2, 4, 8, 16]
+    assert stream and {k for c in stream for k in c} == {"ROW_KERNEL", "BLOCK_SIZE", "num_warps", "num_stages"}
+    assert sorted({c["num_warps"] for c in stream}) == [1, 2, 4, 8, 16]
     assert cands[0]["ROW_KERNEL"] == 1, "RMSNorm: the register kernel (library default) ranks first"
+    # softmax: 8 KB rows in registers at ~8 vectors per thread (2 warps), 2 KB rows streamed
     soft = Problem.create("softmax", "fp16", rows=16384, cols=4096)
-    assert SoftmaxSearchSpace().candidates(soft, b200_caps)[0]["ROW_KERNEL"] == 2
+    first = SoftmaxSearchSpace().candidates(soft, b200_caps)[0]
+    assert (first["ROW_KERNEL"], first["num_warps"], first["CLUSTER"]) == (1, 2, 1)
+    soft_narrow = Problem.create("softmax", "fp16", rows=32768, cols=1000)
+    first = SoftmaxSearchSpace().candidates(soft_narrow, b200_caps)[0]
+    assert (first["ROW_KERNEL"], first["num_warps"], first.get("num_stages")) == (2, 1, 2)
     assert {c["BLOCK_SIZE"] for c in cands} == {4096}
     wide = Problem.create("softmax", "fp32", rows=32768, cols=32000)
     space = SoftmaxSearchSpace()
