@@ -19,6 +19,8 @@
 //    array's device address is looked up with cudaGetSymbolAddress once per
 //    device, by the first call made while that device is current; make that
 //    first call before any stream capture begins.
+//  - fp16/bf16 operands with K-contiguous rows (and K % 8 == 0) go to the
+//    16-row tile GEMV, which uses no scratch; only the others touch the array.
 //  - All calls on a device share the one array. Each call clears the arrival
 //    counters (cudaMemsetAsync on the caller's stream) before its kernel, and
 //    the partial tiles are always written before they are read. Calls that
@@ -73,7 +75,14 @@ extern "C" KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t 
   int rc = kf::current_device(&device);
   if (rc != KF_OK) return rc;
   if (device >= kMaxDevices) return kf::set_error(KF_ERR_INVALID_ARGUMENT, "device index out of range");
-  // Always the stream-K tcgen05 GEMV: the kernel whose scratch this entry point holds.
+  // K-contiguous 16-bit operands take the 16-row tile kernel, which needs no
+  // scratch at all (and so cannot race with an overlapping call); the rest
+  // take the stream-K tcgen05 GEMV, the kernel whose scratch this entry point
+  // holds.
+  if (x != nullptr && w != nullptr && y != nullptr &&
+      kf::gemv_mma_supported(dtype, x, sx_m, sx_k, w, sw_n, sw_k, M, N, K, nullptr))
+    return kf::launch_gemv_mma(dtype, x, sx_m, w, sw_n, y, sy_m, sy_n, M, N, K, kf_gemm_config{},
+                               static_cast<cudaStream_t>(stream));
   kf_gemm_config cfg{};
   cfg.kernel = KF_GEMM_TCGEN05;
   const int64_t need = kf_gemv_workspace_bytes(device, dtype, sx_m, sx_k, sw_n, sw_k, M, N, K, &cfg);
