@@ -91,6 +91,13 @@ _ROWS: dict[str, tuple[tuple[int, int], ...]] = {
     "baseline_rmsnorm": ((16384, 4096), (16384, 8192)),
 }
 
+#: Decode shapes (M rows of x, N, K) for the GEMV's smoke and sweep suites.
+_GEMV: dict[str, tuple[tuple[int, int, int], ...]] = {
+    "smoke": ((1, 4096, 4096), (4, 4096, 4096)),
+    "sweep": ((1, 4096, 4096), (1, 11008, 4096), (4, 11008, 4096), (16, 11008, 4096), (16, 4096, 11008),
+              (64, 11008, 4096)),
+}
+
 SUITES: tuple[str, ...] = ("smoke", "sweep", "transformer", "correctness", "baseline", "sweep_sm100")
 
 
@@ -101,7 +108,9 @@ def problems(operation: str, suite: str = "sweep", dtype: str | torch.dtype = "f
     if operation in ("matmul", "fused_linear", "gemv"):
         shapes = _MATMUL[suite]
         if operation == "gemv":
-            shapes = tuple(s for s in shapes if s[0] <= 256)
+            # The GEMM suites' smoke and sweep shapes are all prefill-sized:
+            # the decode GEMV gets decode shapes of its own there.
+            shapes = _GEMV.get(suite) or tuple(s for s in shapes if s[0] <= 256)
         return [Problem.create(operation, dtype, M=m, N=n, K=k) for m, n, k in shapes]
     if operation in ("softmax", "rmsnorm"):
         key = suite
