@@ -194,6 +194,23 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
     return set_error(KF_ERR_INVALID_ARGUMENT, "epilogue needs a bias pointer");
   if (g.epilogue < KF_EPI_NONE || g.epilogue > KF_EPI_BIAS_GELU_ERF)
     return set_error(KF_ERR_INVALID_ARGUMENT, "unknown epilogue code");
+  // Up to 16 rows of x against a K-contiguous 16-bit B (an nn.Linear weight
+  // [N, K] passed as its transpose): the 16-row tile kernel, epilogue
+  // included (the decode-shape fused linear). It reads the weight at 0.8 of
+  // the copy bandwidth against ~0.55 for 128-row TMA tiles.
+  const bool tile_auto = (user == nullptr || user->kernel == KF_GEMM_AUTO) && g.n_peers == 0 &&
+                         g.M <= GEMV_MMA_MAX_M &&
+                         gemv_mma_supported(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_n, g.sb_k, g.M, g.N,
+                                            g.K, nullptr);
+  if (tile_auto || (user != nullptr && user->kernel == KF_GEMM_TILE_ROWS)) {
+    std::string why;
+    if (g.n_peers > 0) return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 path only");
+    if (!gemv_mma_supported(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_n, g.sb_k, g.M, g.N, g.K, &why))
+      return set_error(KF_ERR_UNALIGNED, "tile GEMV: " + why);
+    return launch_gemv_mma(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K,
+                           user ? *user : zero_config(), static_cast<cudaStream_t>(stream), g.epilogue,
+                           g.bias);
+  }
   int device = 0;
   int rc = current_device(&device);
   if (rc != KF_OK) return rc;

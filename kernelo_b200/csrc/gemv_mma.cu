@@ -1,5 +1,7 @@
-// Decode-shape GEMV with 16-row weight tiles: y[m, n] = sum_k x[m, k] w[n, k]
-// for M <= 16 and a weight whose rows are K-contiguous (nn.Linear's [N, K]).
+// Decode-shape GEMV with 16-row weight tiles: y[m, n] = epi(sum_k x[m, k] w[n, k])
+// for M <= 16 and a weight whose rows are K-contiguous (nn.Linear's [N, K]);
+// epi is none, + bias[n], or + bias[n] then GELU (the fused linear at decode
+// shapes).
 //
 // The product is ~M FLOP per weight byte, so the kernel's job is to stream W
 // from HBM at full rate; the arithmetic must only stay out of the way. One CTA
@@ -38,6 +40,7 @@ struct GemvMmaParams {
   long long sw_n;
   void* y;
   long long sy_m, sy_n;
+  const void* bias;  // [N], for the bias / GELU epilogues
   int M, N, K;
 };
 
@@ -61,7 +64,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 // slices); U: vector pairs per lane in flight.
 // At least five CTAs per SM: a tile's CTA lasts about the whole kernel, so
 // all of them (688 for N = 11008) must be resident at once.
-template <typename T, int NT, int S, int U>
+template <typename T, int NT, int S, int U, int EPI>
 __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams p) {
   __shared__ float4 part[S > 1 ? S - 1 : 1][32][NT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,22 +138,32 @@ __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams
       }
   }
   // D fragment: acc[nt][0..1] = rows n0+g, x rows 8nt+2t, +1; [2..3] = rows n0+g+8.
+  // The fused linear's epilogue (bias[n], then GELU) runs here, before the
+  // one rounding, as in the GEMM.
   T* y = static_cast<T*>(p.y);
+  float bias[2] = {0.0f, 0.0f};
+  if constexpr (EPI != KF_EPI_NONE) {
+    const T* b = static_cast<const T*>(p.bias);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) bias[h] = to_f32(b[min(n0 + g + 8 * h, p.N - 1)]);
+  }
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int m = 8 * nt + 2 * t + (i & 1);
       const int n = n0 + g + (i >> 1) * 8;
-      if (m < p.M && n < p.N) y[m * p.sy_m + static_cast<long long>(n) * p.sy_n] = from_f32<T>(acc[nt][i]);
+      if (m < p.M && n < p.N)
+        y[m * p.sy_m + static_cast<long long>(n) * p.sy_n] =
+            from_f32<T>(apply_epilogue<EPI>(acc[nt][i], bias[i >> 1]));
     }
   }
 }
 
-template <typename T, int NT, int S, int U>
+template <typename T, int NT, int S, int U, int EPI>
 int launch_shape(const GemvMmaParams& p, cudaStream_t stream) {
   const unsigned tiles = static_cast<unsigned>((p.N + 15) / 16);
-  gemv_mma_kernel<T, NT, S, U><<<tiles, 32 * S, 0, stream>>>(p);
+  gemv_mma_kernel<T, NT, S, U, EPI><<<tiles, 32 * S, 0, stream>>>(p);
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_error(err, "launch(gemv mma)");
   return KF_OK;
@@ -160,25 +173,36 @@ int launch_shape(const GemvMmaParams& p, cudaStream_t stream) {
 // block_m selects S and stages selects U; zero picks the default, measured
 // on B200 at N = 11008, K = 4096: (8, 2) up to 8 rows of x (17.0 us at M=1,
 // 17.9 at M=4), (6, 4) above (19.6 us at M=16; 8 warps of 4 pairs spill).
-template <typename T, int NT>
+template <typename T, int NT, int EPI>
 int launch_nt(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t stream) {
   const int s = cfg.block_m != 0 ? cfg.block_m : (NT == 1 ? 8 : 6);
   const int u = cfg.stages != 0 ? cfg.stages : (NT == 1 ? 2 : 4);
-  if (s == 4 && u == 4) return launch_shape<T, NT, 4, 4>(p, stream);
-  if (s == 4 && u == 2) return launch_shape<T, NT, 4, 2>(p, stream);
-  if (s == 4 && u == 8) return launch_shape<T, NT, 4, 8>(p, stream);
-  if (s == 6 && u == 2) return launch_shape<T, NT, 6, 2>(p, stream);
-  if (s == 6 && u == 4) return launch_shape<T, NT, 6, 4>(p, stream);
-  if (s == 8 && u == 2) return launch_shape<T, NT, 8, 2>(p, stream);
-  if (s == 8 && u == 4) return launch_shape<T, NT, 8, 4>(p, stream);
+  if (s == 4 && u == 4) return launch_shape<T, NT, 4, 4, EPI>(p, stream);
+  if (s == 4 && u == 2) return launch_shape<T, NT, 4, 2, EPI>(p, stream);
+  if (s == 4 && u == 8) return launch_shape<T, NT, 4, 8, EPI>(p, stream);
+  if (s == 6 && u == 2) return launch_shape<T, NT, 6, 2, EPI>(p, stream);
+  if (s == 6 && u == 4) return launch_shape<T, NT, 6, 4, EPI>(p, stream);
+  if (s == 8 && u == 2) return launch_shape<T, NT, 8, 2, EPI>(p, stream);
+  if (s == 8 && u == 4) return launch_shape<T, NT, 8, 4, EPI>(p, stream);
   return set_error(KF_ERR_INVALID_CONFIG, "tile GEMV: no compiled shape with " + std::to_string(s) +
                                               " warps per tile and " + std::to_string(u) +
                                               " vector pairs in flight");
 }
 
+template <typename T, int EPI>
+int launch_epi(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t stream) {
+  return p.M <= 8 ? launch_nt<T, 1, EPI>(p, cfg, stream) : launch_nt<T, 2, EPI>(p, cfg, stream);
+}
+
 template <typename T>
-int launch_typed(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t stream) {
-  return p.M <= 8 ? launch_nt<T, 1>(p, cfg, stream) : launch_nt<T, 2>(p, cfg, stream);
+int launch_typed(const GemvMmaParams& p, const kf_gemm_config& cfg, int epilogue, cudaStream_t stream) {
+  switch (epilogue) {
+    case KF_EPI_NONE: return launch_epi<T, KF_EPI_NONE>(p, cfg, stream);
+    case KF_EPI_BIAS: return launch_epi<T, KF_EPI_BIAS>(p, cfg, stream);
+    case KF_EPI_BIAS_GELU_TANH: return launch_epi<T, KF_EPI_BIAS_GELU_TANH>(p, cfg, stream);
+    case KF_EPI_BIAS_GELU_ERF: return launch_epi<T, KF_EPI_BIAS_GELU_ERF>(p, cfg, stream);
+  }
+  return set_error(KF_ERR_INVALID_ARGUMENT, "unknown epilogue code");
 }
 
 }  // namespace
@@ -203,7 +227,9 @@ bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, co
 
 int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
                     int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
-                    const kf_gemm_config& cfg, cudaStream_t stream) {
+                    const kf_gemm_config& cfg, cudaStream_t stream, int epilogue, const void* bias) {
+  if (epilogue != KF_EPI_NONE && bias == nullptr)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "epilogue needs a bias pointer");
   GemvMmaParams p{};
   p.x = x;
   p.sx_m = sx_m;
@@ -215,9 +241,10 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
+  p.bias = bias;
   if (N == 0 || M == 0) return KF_OK;
-  if (dtype == KF_BF16) return launch_typed<__nv_bfloat16>(p, cfg, stream);
-  return launch_typed<__half>(p, cfg, stream);
+  if (dtype == KF_BF16) return launch_typed<__nv_bfloat16>(p, cfg, epilogue, stream);
+  return launch_typed<__half>(p, cfg, epilogue, stream);
 }
 
 }  // namespace kf

@@ -78,7 +78,8 @@ bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, co
                         int64_t sw_k, int64_t M, int64_t N, int64_t K, std::string* why);
 int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
                     int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
-                    const kf_gemm_config& cfg, cudaStream_t stream);
+                    const kf_gemm_config& cfg, cudaStream_t stream, int epilogue = KF_EPI_NONE,
+                    const void* bias = nullptr);
 
 // Softmax kernel choice by row width in 16-byte vectors (rows.cu).
 constexpr long long SOFTMAX_STREAM_MAX_VECTORS = 128;     // up to 2 KB: streaming kernel

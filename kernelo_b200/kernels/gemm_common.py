@@ -180,6 +180,12 @@ def default_simt_config(operation: str, m: int, n: int, *, sm_count: int = 148) 
 def default_gemm_config(
     operation: str, m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str, sm_count: int = 148
 ) -> KernelConfig:
+    """The library's choice for contiguous operands (mirrors gemm_common in api.cu): the 16-row
+    tile kernel for up to 16 rows of x against a K-contiguous B, else tcgen05 tiles where TMA
+    can describe the operands, else the CUDA-core kernel."""
+    if b_layout == "nk" and tile_rows_reject(m, k, dtype) is None:
+        warps, pairs = tile_rows_default(m)
+        return KernelConfig(operation, KERNEL=KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
     if shape_allows_tcgen05(m, n, k, dtype, b_layout=b_layout) is None:
         return default_tcgen05_config(operation, m, n, k, b_layout=b_layout, sm_count=sm_count)
     return default_simt_config(operation, m, n, sm_count=sm_count)

@@ -62,12 +62,18 @@ def profile_kernels(fn: Callable[[], object], *, label: str, warmup: int = 5,
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    from torch.profiler import ProfilerActivity, profile
+    from torch.profiler import ProfilerActivity, profile, schedule
 
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        for _ in range(iterations):
+    # One traced-but-discarded warm-up step first: a profiler session started
+    # after an earlier one in the same process can miss the first launch it
+    # sees, which would read as a fused call making fewer than one launch.
+    with profile(activities=[ProfilerActivity.CUDA],
+                 schedule=schedule(wait=0, warmup=1, active=iterations, repeat=1)) as prof:
+        for step in range(iterations + 1):
             fn()
-        torch.cuda.synchronize()
+            if step == iterations:
+                torch.cuda.synchronize()
+            prof.step()
     names: Counter[str] = Counter()
     times: Counter[str] = Counter()
     for evt in prof.events():

@@ -210,6 +210,11 @@ class _Sm100GemmSpace(SearchSpace):
 
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
         m, n, _ = self.dims(problem)
+        if self.b_layout == "nk":
+            # decode shapes: 16-row weight tiles on mma.sync (BLOCK_M warps per tile,
+            # num_stages vector pairs in flight)
+            for warps, pairs in gc.TILE_ROWS_SHAPES:
+                yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
         swap = 1 if gc.default_swap(m, n) else 2
         for bm, bn, bk, stages, (cm, cn) in product(
             self.BLOCK_M, self.BLOCK_N, self.BLOCK_K, self.NUM_STAGES, self.CLUSTERS
@@ -238,6 +243,9 @@ class _Sm100GemmSpace(SearchSpace):
         return m, n
 
     def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
+        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
+            m = self.dims(problem)[0]
+            return (config["BLOCK_M"] - 1) * 32 * (1 if m <= 8 else 2) * 16  # the K-slice partials
         if config["KERNEL"] == gc.KERNEL_SIMT:
             return 2 * config["BLOCK_K"] * (config["BLOCK_M"] + config["BLOCK_N"]) * 4
         return gc.tc_smem_bytes(config["BLOCK_N"], config["BLOCK_K"], config["num_stages"],
@@ -245,12 +253,16 @@ class _Sm100GemmSpace(SearchSpace):
 
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
         """CTAs with work: tiles, times two for SM-pair tiles."""
+        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
+            return ceil_div(self.dims(problem)[1], 16)  # one CTA per 16 weight rows
         m_k, n_k = self.kernel_view(config, problem)
         tiles = ceil_div(m_k, config["BLOCK_M"]) * ceil_div(n_k, config["BLOCK_N"])
         return tiles * (gc.cta_group(config["BLOCK_M"]) if config["KERNEL"] == gc.KERNEL_TCGEN05 else 1)
 
     def reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
         m, n, k = self.dims(problem)
+        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
+            return gc.tile_rows_reject(m, k, problem.dtype)
         if config["KERNEL"] == gc.KERNEL_SIMT:
             return None  # the fallback always runs
         why = gc.shape_allows_tcgen05(m, n, k, problem.dtype, b_layout=self.b_layout)
@@ -296,9 +308,13 @@ class _Sm100GemmSpace(SearchSpace):
         return None
 
     def priority(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> tuple[float, ...]:
-        """tcgen05 before SIMT; then parallelism up to one wave; then reuse
+        """The tile kernel first where it runs (its default shape first); then
+        tcgen05 before SIMT; then parallelism up to one wave; then reuse
         BM*BN/(BM+BN) (operand bytes per MMA); then least padding; then the
         deeper ring."""
+        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
+            default = (config["BLOCK_M"], config["num_stages"]) == gc.tile_rows_default(self.dims(problem)[0])
+            return (-3,) if default else (-2,)
         kernel_rank = 0 if config["KERNEL"] == gc.KERNEL_TCGEN05 else 1
         m_k, n_k = self.kernel_view(config, problem)
         bm, bn = config["BLOCK_M"], config["BLOCK_N"]
@@ -333,31 +349,21 @@ class GemvSearchSpace(_Sm100GemmSpace):
     b_layout = "nk"
 
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
-        for warps, pairs in gc.TILE_ROWS_SHAPES:
-            yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
         yield KernelConfig(self.operation, KERNEL=gc.KERNEL_WARP_ROWS)
         yield from super().grid(problem)
 
     def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
-        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
-            m = self.dims(problem)[0]
-            return (config["BLOCK_M"] - 1) * 32 * (1 if m <= 8 else 2) * 16  # the K-slice partials
         if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
             m, _, k = self.dims(problem)
             return gc.warp_rows_smem_bytes(m, k, itemsize(problem.dtype))
         return super().shared_memory_bytes(config, problem)
 
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
-        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
-            return ceil_div(self.dims(problem)[1], 16)  # one CTA per 16 weight rows
         if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
             return ceil_div(self.dims(problem)[1], 16)  # 16 warps per CTA, a row or two each
         return super().num_programs(config, problem)
 
     def reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
-        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
-            m, _, k = self.dims(problem)
-            return gc.tile_rows_reject(m, k, problem.dtype)
         if config["KERNEL"] != gc.KERNEL_WARP_ROWS:
             return super().reject_reason(config, problem, caps)
         m, _, _ = self.dims(problem)
@@ -369,12 +375,9 @@ class GemvSearchSpace(_Sm100GemmSpace):
         return None
 
     def priority(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> tuple[float, ...]:
-        """The tile kernel's default shape first, then its other shapes, then the
+        """The tile kernel's shapes as for every K-contiguous GEMM, then the
         warp-per-row kernel (first where it is the library default, M <= 2, and
         the tile kernel cannot run)."""
-        if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
-            default = (config["BLOCK_M"], config["num_stages"]) == gc.tile_rows_default(self.dims(problem)[0])
-            return (-3,) if default else (-2,)
         if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
             return (-1,) if self.dims(problem)[0] <= gc.WARP_ROWS_AUTO_MAX_M else (2,)
         return super().priority(config, problem, caps)

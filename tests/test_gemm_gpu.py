@@ -390,6 +390,39 @@ def test_gemv_tile_rows_edges_and_strides(device):
     assert native.device_status(device.index) == 0
 
 
+@pytest.mark.parametrize("m", [1, 4, 9, 16])
+@pytest.mark.parametrize("approximate", ["tanh", "none"])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_fused_linear_decode_shapes_on_tile_rows(m, approximate, dtype, device):
+    """The fused linear at decode shapes (an nn.Linear weight passed as W.t()):
+    the library routes it to the 16-row tile kernel with the bias + GELU
+    epilogue; the explicit tile config and the tcgen05 path agree with the
+    oracle too."""
+    from kernelo_b200.kernels.fused_linear import default_config
+
+    gen = torch.Generator().manual_seed(60 + m)
+    x = torch.randn(m, 4096, generator=gen).to(dtype).to(device)
+    w_nk = (torch.randn(11008, 4096, generator=gen) * 4096 ** -0.5).to(dtype).to(device)
+    b = (torch.randn(11008, generator=gen) * 0.3).to(dtype).to(device)
+    expected = ref.linear_gelu_ref(host(x), host(w_nk.t()), host(b), approximate)
+    cfg = default_config(m, 11008, 4096, dtype)
+    assert cfg["KERNEL"] == 4
+    for config in (None, cfg, KernelConfig("fused_linear", KERNEL=1)):
+        out = fused_linear_gelu(x, w_nk.t(), b, approximate=approximate, config=config)
+        gate(expected, out, dtype, context=f"M={m} {approximate} {config}")
+
+
+def test_tile_rows_bias_only_epilogue_and_plain_matmul(device):
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(3, 1032, generator=gen).half().to(device)
+    w_nk = (torch.randn(1000, 1032, generator=gen) * 0.03).half().to(device)
+    b = torch.randn(1000, generator=gen).half().to(device)
+    y = torch.empty(3, 1000, device=device, dtype=torch.float16)
+    native.gemm(x, w_nk.t(), y, bias=b, epilogue=native.KF_EPI_BIAS, launch=native.GemmLaunch())
+    gate(ref.matmul_ref(host(x), host(w_nk.t())) + host(b), y, torch.float16, context="bias only")
+    gate(ref.matmul_ref(host(x), host(w_nk.t())), matmul(x, w_nk.t()), torch.float16, context="matmul M=3")
+
+
 def test_gemv_tile_rows_refusals(device):
     from kernelo_b200.runtime.native import OutOfResources
 

@@ -215,6 +215,21 @@ def test_gemv_tile_rows_candidates(b200_caps):
     assert "K % 8" in space.reject_reason(tile, Problem.create("gemv", "fp16", M=2, N=64, K=4099), b200_caps)
 
 
+def test_fused_linear_decode_shapes_take_tile_rows(b200_caps):
+    from kernelo_b200.tuning.search import FusedLinearErfSearchSpace, MatmulSearchSpace
+
+    for m, expected in ((1, 4), (16, 4), (17, 1), (4096, 1)):
+        cfg = gc.default_gemm_config("fused_linear_erf", m, 11008, 4096, torch.bfloat16, b_layout="nk")
+        assert cfg["KERNEL"] == expected, (m, cfg)
+    decode = Problem.create("fused_linear_erf", "bf16", M=4, N=11008, K=4096)
+    first = FusedLinearErfSearchSpace().candidates(decode, b200_caps)[0]
+    assert (first["KERNEL"], first["BLOCK_M"], first["num_stages"]) == (4, 8, 2)
+    # a row-major (K, N) B is not K-contiguous: no tile candidates for matmul
+    mm = Problem.create("matmul", "fp16", M=4, N=4096, K=4096)
+    assert all(c["KERNEL"] != 4 for c in MatmulSearchSpace().candidates(mm, b200_caps))
+    assert gc.default_gemm_config("matmul", 4, 4096, 4096, torch.float16, b_layout="kn")["KERNEL"] == 1
+
+
 def test_gemv_warp_rows_candidate(b200_caps):
     space = GemvSearchSpace()
     # fp32 x: the tile kernel is out, the warp-per-row kernel is the default at M <= 2
