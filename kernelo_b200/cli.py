@@ -153,9 +153,11 @@ def command_tune(args: argparse.Namespace) -> int:
     print()
     db = _open_db(args)
     try:
+        if args.resume and db is None:
+            raise ValueError("--resume reads the results database; drop --no-db")
         result = Tuner(warmup=args.warmup, iterations=args.iterations, max_candidates=args.max_candidates,
                        measure_baselines=not args.no_baselines, flush_l2=not args.no_flush_l2, db=db,
-                       cache=_open_cache(args), log=print).tune(operator, problem)
+                       cache=_open_cache(args), log=print, resume=args.resume).tune(operator, problem)
     finally:
         if db is not None:
             db.close()
@@ -414,6 +416,8 @@ def build_parser() -> argparse.ArgumentParser:
     tune.add_argument("--no-baselines", action="store_true", help="skip comparison baselines")
     tune.add_argument("--explain", action="store_true",
                       help="print the candidate-generation breakdown and exit without tuning")
+    tune.add_argument("--resume", action="store_true",
+                      help="reuse candidates the database already holds for this problem and device")
 
     bench = sub.add_parser("benchmark", help="run a named workload suite")
     bench.add_argument("operation", choices=OPERATIONS)

@@ -237,6 +237,17 @@ class ResultsDB:
         ).fetchone()
         return row is not None
 
+    def latest_result(self, problem: Problem, config: KernelConfig, *, device_key: str,
+                      label: str = "kernelforge") -> dict | None:
+        """The newest row for (problem, config, label) measured on ``device_key``,
+        or None: what a resumed sweep reuses instead of measuring again."""
+        row = self._conn.execute(
+            _JOINED + " WHERE p.operation=? AND p.shape_key=? AND p.dtype=? AND c.digest=? AND r.label=? "
+            "AND run.device_key=? ORDER BY r.result_id DESC LIMIT 1",
+            (problem.operation, problem.shape_key, problem.dtype_name, config.digest, label, device_key),
+        ).fetchone()
+        return None if row is None else dict(row)
+
     # reads ------------------------------------------------------------------
     def rows(self, *, operation: str | None = None, dtype: str | None = None) -> list[dict]:
         where, params = [], []

@@ -123,6 +123,22 @@ class TuningResult:
         return counts
 
 
+def _outcome_from_row(config: KernelConfig, row: dict) -> CandidateOutcome:
+    """A stored measurement as a candidate outcome (times are kept in us)."""
+    timing = None
+    if row["median_us"] is not None:
+        ms = {k: (row[f"{k}_us"] or 0.0) / 1e3 for k in ("median", "mean", "std", "min", "max", "p95", "p99")}
+        timing = TimingResult(ms["median"], ms["mean"], ms["std"], ms["min"], ms["max"], ms["p95"], ms["p99"],
+                              int(row["warmup"] or 0), int(row["iterations"] or 0), row["timer"] or "",
+                              bool(row["flushed_l2"]))
+    verification = None
+    if row["correct"] is not None:
+        verification = VerificationResult(bool(row["correct"]), row["rel_error"] or 0.0, 0.0, 0, 0, 0.0,
+                                          "" if row["correct"] else row["error"])
+    return CandidateOutcome(config=config, status=row["status"], verification=verification, timing=timing,
+                            error=row["error"] or "")
+
+
 def _device_status_check(device: torch.device) -> None:
     if device.type != "cuda":
         return
@@ -147,6 +163,7 @@ class Tuner:
         cache: ConfigCache | None = None,
         log: Callable[[str], None] | None = None,
         candidate_filter: Callable[[int, KernelConfig], bool] | None = None,
+        resume: bool = False,
     ) -> None:
         self.warmup = warmup
         self.iterations = iterations
@@ -159,6 +176,12 @@ class Tuner:
         self._log = log
         #: (index, config) -> keep? Used to shard one candidate list over workers.
         self.candidate_filter = candidate_filter
+        #: Reuse the outcome of every candidate the database already holds for
+        #: this problem and device, so an interrupted sweep continues where it
+        #: stopped (needs ``db``).
+        self.resume = resume
+        if resume and db is None:
+            raise ValueError("resume needs a results database")
 
     def log(self, message: str) -> None:
         if self._log is not None:
@@ -177,13 +200,24 @@ class Tuner:
             candidates = [c for i, c in enumerate(candidates) if self.candidate_filter(i, c)]
         inputs = operator.make_inputs(problem, target, seed=self.seed)
 
+        reused: dict[KernelConfig, CandidateOutcome] = {}
+        if self.resume:
+            for c in candidates:
+                row = self.db.latest_result(problem, c, device_key=env.device_key)
+                if row is not None:
+                    reused[c] = _outcome_from_row(c, row)
+            if reused:
+                self.log(f"Resuming: {len(reused)} of {len(candidates)} candidates already measured")
+        fresh = [c for c in candidates if c not in reused]
+
         with exact_fp32_matmul():
             reference = operator.reference(*inputs)
-            self.log(f"Verifying candidates... ({len(candidates)} to check)")
-            verified = [self._verify_candidate(operator, c, inputs, reference, problem) for c in candidates]
-            self.log(f"{sum(o.ok for o in verified)} / {len(candidates)} configurations passed correctness")
+            self.log(f"Verifying candidates... ({len(fresh)} to check)")
+            verified = [self._verify_candidate(operator, c, inputs, reference, problem) for c in fresh]
+            self.log(f"{sum(o.ok for o in verified)} / {len(fresh)} configurations passed correctness")
             self.log("Benchmarking...")
-            timed = [self._time_candidate(operator, o, inputs, target) for o in verified]
+            measured = {o.config: self._time_candidate(operator, o, inputs, target) for o in verified}
+            timed = [reused[c] if c in reused else measured[c] for c in candidates]
             baselines = (
                 self._measure_baselines(operator, problem, inputs, reference, target)
                 if self.measure_baselines
@@ -203,7 +237,7 @@ class Tuner:
             memory_bound=operator.is_memory_bound(),
             rejections=cset.rejected,
         )
-        self._persist(result, env)
+        self._persist(result, env, skip=set(reused))
         return result
 
     # stages -------------------------------------------------------------------
@@ -256,7 +290,7 @@ class Tuner:
                 self.log(f"  baseline {label} unavailable: {_classify(exc)[1]}")
         return out
 
-    def _persist(self, result: TuningResult, env: Environment) -> None:
+    def _persist(self, result: TuningResult, env: Environment, *, skip: set[KernelConfig] = frozenset()) -> None:
         best = result.best
         if self.cache is not None and best is not None:
             self.cache.put(
@@ -274,6 +308,8 @@ class Tuner:
         run_id = self.db.start_run(env, notes="tune", version=__version__)
         rows = []
         for o in result.outcomes:
+            if o.config in skip:  # reused from an earlier run: its row is already there
+                continue
             ms = o.timing.median_ms if o.timing else None
             rows.append(
                 Measurement(

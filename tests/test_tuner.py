@@ -142,6 +142,34 @@ def test_persistence(tmp_path):
     db.close()
 
 
+def test_resumed_sweep_reuses_stored_outcomes(tmp_path):
+    """A second tune with resume=True measures nothing already in the database
+    (same problem, same device) and ranks the stored outcomes the same way."""
+    db = ResultsDB(tmp_path / "r.db")
+    first = Tuner(warmup=1, iterations=2, flush_l2=False, measure_baselines=False, db=db).tune(
+        _FakeOperator(), PROBLEM, device="cpu")
+    rows_after_first = db.counts()["results"]
+    calls = []
+
+    class _Counting(_FakeOperator):
+        def run(self, config, x):
+            calls.append(config)
+            return super().run(config, x)
+
+    lines: list[str] = []
+    second = Tuner(warmup=1, iterations=2, flush_l2=False, measure_baselines=False, db=db, resume=True,
+                   log=lines.append).tune(_Counting(), PROBLEM, device="cpu")
+    assert calls == [], "a resumed sweep re-ran stored candidates"
+    assert any(line.startswith("Resuming:") for line in lines)
+    assert [o.status for o in second.outcomes] == [o.status for o in first.outcomes]
+    assert second.best_config == first.best_config
+    assert abs(second.best.median_ms - first.best.median_ms) < 1e-9
+    assert db.counts()["results"] == rows_after_first  # nothing recorded twice
+    with pytest.raises(ValueError, match="resume needs"):
+        Tuner(resume=True)
+    db.close()
+
+
 def test_budget_filter_and_log():
     lines = []
     result = Tuner(warmup=1, iterations=2, max_candidates=2, measure_baselines=False, log=lines.append).tune(
