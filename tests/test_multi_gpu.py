@@ -101,8 +101,23 @@ def _worker(rank: int, world: int, port: int, results) -> None:
         dist.barrier()
         fused.close()
         threads.close()
+        # a second shape: fp16, tanh GELU, M not a multiple of the 256-row pair
+        # tile, N not a multiple of 16 per rank, decode-sized M through the tile
+        # kernel's NCCL path and the all-gathering GEMM's fused path
+        g2 = torch.Generator().manual_seed(5)
+        w2 = (torch.randn(1000, 256, generator=g2) * 0.0625).half().to(dev)
+        b2 = (torch.randn(1000, generator=g2) * 0.3).half().to(dev)
+        f2 = ShardedFusedLinear(w2, b2, approximate="tanh", gather="fused")
+        n2 = ShardedFusedLinear(w2, b2, approximate="tanh", gather="nccl")
+        second = []
+        for m2 in (777, 300):
+            x2 = torch.randn(m2, 256, generator=g2).half().to(dev)
+            second.append(bool(torch.equal(f2(x2).clone(), n2(x2).clone())))
+        torch.cuda.synchronize()
+        f2.close()
+        status2 = native.device_status(rank)
         results[rank] = {"equal": outs, "host": host_ok, "status": status, "oracle": err,
-                         "timed_out": timed_out}
+                         "timed_out": timed_out, "second": second, "status2": status2}
     finally:
         dist.destroy_process_group()
 
@@ -119,5 +134,7 @@ def test_fused_all_gather_on_two_gpus():
         assert all(r["equal"]), f"rank {rank}: fused gather differs from the NCCL gather {r['equal']}"
         assert all(ok for ok, _ in r["host"]), f"rank {rank}: forward_host rows differ {r['host']}"
         assert r["status"] == 0, f"rank {rank}: device status {r['status']:#x}"
+        assert all(r["second"]), f"rank {rank}: fp16/tanh ragged shapes differ {r['second']}"
+        assert r["status2"] == 0, f"rank {rank}: device status {r['status2']:#x} after the second shape"
     assert results[0]["oracle"], "rank 0: the gathered output fails the bf16 gate"
     assert results[0]["timed_out"], "the unanswered barrier did not record a timeout"
