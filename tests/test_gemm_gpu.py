@@ -581,3 +581,45 @@ def test_auto_stream_k_without_workspace_runs_whole_tiles(device):
     gate(ref.linear_gelu_ref(host(x[rows]), host(wt), host(b), "none"), y[rows], torch.bfloat16)
     explicit = native.GemmLaunch.from_config(_pair(STREAM_K=1)).struct()
     assert call(ctypes.byref(explicit)) == native.KF_ERR_WORKSPACE
+
+
+# ------------------------------------------------------------------ every output written
+@pytest.mark.parametrize("case", [
+    # (M, N, K, config) through each schedule and kernel: split tail, whole tiles,
+    # stream-K on SM pairs and on single SMs, the tile GEMV route, the CUDA-core kernel
+    (4096, 11008, 512, None),
+    (1000, 3000, 256, KernelConfig("fused_linear", KERNEL=1, STREAM_K=2)),
+    (777, 1500, 1024, KernelConfig("fused_linear", KERNEL=1, BLOCK_M=256, STREAM_K=1, CLUSTER_M=2)),
+    (300, 700, 384, KernelConfig("fused_linear", KERNEL=1, BLOCK_M=128, STREAM_K=1)),
+    (9, 1000, 1032, None),
+    (65, 130, 72, KernelConfig("fused_linear", KERNEL=2)),
+])
+def test_fused_linear_writes_every_output(case, device):
+    """The output starts as NaN: a tile the kernel skipped would fail the gate's
+    non-finite check (the race-detection plan in place of compute-sanitizer)."""
+    m, n, k, config = case
+    gen = torch.Generator().manual_seed(m + n)
+    x = torch.randn(m, k, generator=gen).bfloat16().to(device)
+    w_nk = (torch.randn(n, k, generator=gen) * k ** -0.5).bfloat16().to(device)
+    b = (torch.randn(n, generator=gen) * 0.3).bfloat16().to(device)
+    out = torch.full((m, n), float("nan"), device=device, dtype=torch.bfloat16)
+    fused_linear_gelu(x, w_nk.t(), b, approximate="none", config=config, out=out)
+    assert torch.isfinite(out).all(), f"{case}: unwritten outputs"
+    rows = torch.arange(0, m, max(1, m // 64))
+    gate(ref.linear_gelu_ref(host(x[rows.to(device)]), host(w_nk.t()), host(b), "none"), out[rows.to(device)],
+         torch.bfloat16, context=str(case))
+    assert native.device_status(device.index) == 0
+
+
+@pytest.mark.parametrize("m", [1, 3, 16])
+@pytest.mark.parametrize("kernel", [1, 3, 4])
+def test_gemv_writes_every_output(m, kernel, device):
+    if kernel == 3 and m > 4:
+        pytest.skip("the warp-per-row kernel takes M <= 4")
+    gen = torch.Generator().manual_seed(m * 10 + kernel)
+    x = torch.randn(m, 4096, generator=gen).half().to(device)
+    w = (torch.randn(5003, 4096, generator=gen) * 4096 ** -0.5).half().to(device)
+    out = torch.full((m, 5003), float("nan"), device=device, dtype=torch.float16)
+    gemv(x, w, config=KernelConfig("gemv", KERNEL=kernel), out=out)
+    assert torch.isfinite(out).all()
+    gate(ref.gemv_ref(host(x), host(w)), out, torch.float16, context=f"kernel {kernel} M={m}")

@@ -269,3 +269,30 @@ def test_stream_kernel_rejects_bad_configs(device):
         softmax(x, config=stream_cfg("softmax", 4096, num_warps=8, ROW_GROUPS=3))
     with pytest.raises(OutOfResources, match="row slots"):
         softmax(x, config=stream_cfg("softmax", 4096, num_warps=8, num_stages=40))
+
+
+@pytest.mark.parametrize("cols", [1, 7, 1000, 4096, 4097, 32000])
+@pytest.mark.parametrize("kernel", [1, 2])
+def test_row_kernels_write_every_output(cols, kernel, device):
+    """Outputs start as NaN, so a row or a tail the kernel skipped fails the
+    finiteness check; both kernels, narrow to 128 KiB rows, unaligned widths."""
+    from kernelo_b200.kernels.rows_common import stream_fits
+    from kernelo_b200.runtime import native
+    from kernelo_b200.tuning.config import KernelConfig
+
+    dtype = torch.float32 if cols == 32000 else torch.float16
+    rows = 300 if kernel == 2 else 37
+    if kernel == 2 and not stream_fits(cols, dtype):
+        pytest.skip("row does not fit a streaming slot")
+    x = rand(rows, cols, dtype, device)
+    gamma = rand(1, cols, dtype, device)[0]
+    block = max(1, 1 << (cols - 1).bit_length())
+    cfg = KernelConfig("softmax", BLOCK_SIZE=block, ROW_KERNEL=kernel)
+    y = torch.full_like(x, float("nan"))
+    native.softmax_rows(x, y, cfg)
+    assert torch.isfinite(y).all()
+    gate(ref.softmax_ref(host(x)), y, dtype)
+    y = torch.full_like(x, float("nan"))
+    native.rmsnorm_rows(x, gamma, y, 1e-5, KernelConfig("rmsnorm", BLOCK_SIZE=block, ROW_KERNEL=kernel))
+    assert torch.isfinite(y).all()
+    gate(ref.rmsnorm_ref(host(x), host(gamma)), y, dtype)
