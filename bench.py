@@ -463,7 +463,7 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     def e2e_step():
         if world > 1:
             # each rank moves 1/world of X in and of Y out over its own PCIe link
-            layer.forward_host(x_host, y_host, chunks=4)
+            layer.forward_host(x_host, y_host)
         else:
             # the host-buffer entry point: row chunks overlap H2D, the kernel and D2H
             fused_linear_gelu_host(x_host, w.t(), b, approximate="none", out=y_host)
@@ -509,8 +509,8 @@ def run_native(args, world: int, rank: int, local: int) -> int:
                     "api": ("fused_linear_gelu_host (pinned X in, pinned Y out, 8 row chunks overlapping "
                             "copies and kernel)" if world == 1 else
                             "ShardedFusedLinear.forward_host: each rank copies 1/N of X's rows in and 1/N of "
-                            "Y's rows out (bytes summed over ranks), X all-gathered over NVLink, 4 row chunks "
-                            "pipelined")},
+                            f"Y's rows out (bytes summed over ranks), X all-gathered over NVLink, "
+                            f"{max(1, 8 // world)} row chunk(s) pipelined")},
             "gpu_launches": args.steps * (2 if world > 1 else 1),
             "cpu_baseline": baseline,
             "secondary": secondary,
