@@ -207,8 +207,10 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
     if (g.n_peers > 0) return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 path only");
     if (!gemv_mma_supported(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_n, g.sb_k, g.M, g.N, g.K, &why))
       return set_error(KF_ERR_UNALIGNED, "tile GEMV: " + why);
+    // The library's own choice ignores the other config fields (they describe
+    // tcgen05 tiles when the kernel was left to the library).
     return launch_gemv_mma(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K,
-                           user ? *user : zero_config(), static_cast<cudaStream_t>(stream), g.epilogue,
+                           tile_auto ? zero_config() : *user, static_cast<cudaStream_t>(stream), g.epilogue,
                            g.bias);
   }
   int device = 0;
