@@ -171,6 +171,10 @@ def dist_setup(gpus: int):
         raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        # NCCL carries only the timing reductions and the gate here; without
+        # NVLS no buffer is ever bound to an NVLink multicast object, so a rank
+        # that fails cannot take its peers' GPUs down with it.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
