@@ -4,9 +4,10 @@
 
 One step = ``Y = gelu(X @ W^T + b)`` over the whole workload (X [4096,4096],
 W [11008,4096] stored nn.Linear-style, b [11008]; X ~ N(0,1), W ~ N(0,1/4096),
-b ~ N(0,0.1); synthetic, seeded). With N GPUs (torchrun, one process per GPU,
-NCCL) the weight is column-sharded by N and the output slices are exchanged
-with one all-gather per step (strong scaling: the total work is fixed).
+b ~ N(0,0.1); synthetic, seeded). With N GPUs (torchrun, one process per GPU)
+the weight is column-sharded by N and the GEMM's epilogue stores every output
+tile into all ranks' copies of Y over NVLink, followed by a bounded peer
+barrier (strong scaling: the total work is fixed).
 
 Printed (rank 0, one JSON line): whole-job TFLOP/s over K timed steps (device
 time, CUDA events, max over ranks, barrier + synchronize on both sides), the
