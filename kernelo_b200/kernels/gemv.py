@@ -4,20 +4,20 @@ The reference has no dedicated kernel: single-token decoding calls its blocked
 GEMM with M=1 (``kernelforge/kernels/matmul.py:132`` with BLOCK_M=16, one tile
 row), and README.md:666-670 lists split-K as future work. This shape moves
 90 MB of weight for 90 MFLOP (1 FLOP/byte), so it is bound by HBM, not by the
-tensor cores. The sm_100a kernel is the tcgen05 GEMM with A and B swapped --
-the weight W [N,K] becomes the 128-row MMA operand, the few activation rows
-the N=16 side -- streamed through a deep TMA ring, with K split evenly over
-every SM (stream-K) so that all 148 SMs pull weight bytes at once. Partial
-sums go to a workspace; the last CTA to finish a tile reduces them in a fixed
-order.
+tensor cores. Three sm_100a kernels, chosen by the library:
 
-For M <= 2 with a K-contiguous [N,K] weight the default is the warp-per-row
-kernel (``KERNEL=3``, ``csrc/gemv_rows.cu``): each warp streams one or two
-whole weight rows with contiguous 512-byte loads and accumulates with packed
-fp32x2 FMAs against x held in shared memory. Measured on B200, the 128-row TMA tiles of
-the tcgen05 path read a row-major weight at well under the rate of a
-contiguous row stream; from M=4 on the x reads of the CUDA-core kernel cost
-more than that (it still takes M <= 4 when asked for with ``KERNEL=3``).
+* fp16/bf16 x with up to 16 rows and a K-contiguous [N,K] weight (K % 8 == 0):
+  the 16-row tile kernel (``KERNEL=4``, ``csrc/gemv_mma.cu``). One CTA per 16
+  weight rows, K split over its warps; lanes stream the rows with contiguous
+  loads straight into ``mma.sync`` fragments (0.84 / 0.80 / 0.76 of the copy
+  bandwidth at M = 1 / 4 / 16 on B200).
+* fp32 x with M <= 2: the warp-per-row CUDA-core kernel (``KERNEL=3``,
+  ``csrc/gemv_rows.cu``), packed fp32x2 FMAs against x held in shared memory;
+  it takes M <= 4 when asked for.
+* otherwise (a [K,N] weight, unaligned rows, M > 16): the tcgen05 GEMM with A
+  and B swapped -- the weight becomes the 128-row MMA operand -- and K split
+  evenly over every SM (stream-K); the last CTA to finish a tile sums the
+  partials in a fixed order.
 
 W may be stored [N,K] (``w_layout="nk"``, nn.Linear, the baseline layout) or
 [K,N] (``"kn"``, the reference's ``matmul(x, w)`` orientation).
