@@ -187,7 +187,7 @@ class _Sm100GemmSpace(SearchSpace):
     BLOCK_M = (64, 128, 256)
     BLOCK_N = (16, 64, 128, 192, 256)
     BLOCK_K = (32, 64, 128)
-    NUM_STAGES = (2, 4, 6)
+    NUM_STAGES = (2, 3, 4, 6)
     CLUSTERS = ((1, 1), (2, 1), (1, 2), (2, 2))
     #: L2 the A panels of one raster group may take (the library default's rule).
     GROUP_L2_BYTES = 48 << 20
@@ -208,7 +208,20 @@ class _Sm100GemmSpace(SearchSpace):
         rows = max(block_m, gc.TC_BLOCK_M)
         return max(1, min(ceil_div(m_k, rows), self.GROUP_L2_BYTES // max(1, rows * k * problem.itemsize)))
 
+    def library_default(self, problem: Problem) -> KernelConfig:
+        """The config the library picks on its own: always a candidate, so that
+        tuning never ends worse than not tuning."""
+        m, n, k = self.dims(problem)
+        return gc.default_gemm_config(self.operation, m, n, k, problem.dtype, b_layout=self.b_layout)
+
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
+        default = self.library_default(problem)
+        yield default
+        for config in self._grid(problem):
+            if config != default:
+                yield config
+
+    def _grid(self, problem: Problem) -> Iterator[KernelConfig]:
         m, n, _ = self.dims(problem)
         if self.b_layout == "nk":
             # decode shapes: 16-row weight tiles on mma.sync (BLOCK_M warps per tile,
@@ -312,6 +325,8 @@ class _Sm100GemmSpace(SearchSpace):
         tcgen05 before SIMT; then parallelism up to one wave; then reuse
         BM*BN/(BM+BN) (operand bytes per MMA); then least padding; then the
         deeper ring."""
+        if config == self.library_default(problem):
+            return (-10,)
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             default = (config["BLOCK_M"], config["num_stages"]) == gc.tile_rows_default(self.dims(problem)[0])
             return (-3,) if default else (-2,)
@@ -348,9 +363,15 @@ class GemvSearchSpace(_Sm100GemmSpace):
     operation = "gemv"
     b_layout = "nk"
 
-    def grid(self, problem: Problem) -> Iterator[KernelConfig]:
+    def library_default(self, problem: Problem) -> KernelConfig:
+        from kernelo_b200.kernels.gemv import default_config
+
+        m, n, k = self.dims(problem)
+        return default_config(m, n, k, problem.dtype)
+
+    def _grid(self, problem: Problem) -> Iterator[KernelConfig]:
         yield KernelConfig(self.operation, KERNEL=gc.KERNEL_WARP_ROWS)
-        yield from super().grid(problem)
+        yield from super()._grid(problem)
 
     def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
         if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
@@ -378,7 +399,7 @@ class GemvSearchSpace(_Sm100GemmSpace):
         """The tile kernel's shapes as for every K-contiguous GEMM, then the
         warp-per-row kernel (first where it is the library default, M <= 2, and
         the tile kernel cannot run)."""
-        if config["KERNEL"] == gc.KERNEL_WARP_ROWS:
+        if config["KERNEL"] == gc.KERNEL_WARP_ROWS and config != self.library_default(problem):
             return (-1,) if self.dims(problem)[0] <= gc.WARP_ROWS_AUTO_MAX_M else (2,)
         return super().priority(config, problem, caps)
 

@@ -41,7 +41,9 @@ def test_next_power_of_2(n, expected):
 
 def test_grid_size_and_budget(b200_caps):
     result = MatmulSearchSpace().generate(GEMM, b200_caps)
-    assert result.generated == 3 * 5 * 3 * 3 * 4 + 3  # tcgen05 grid + SIMT tiles
+    assert result.generated == 1 + 3 * 5 * 3 * 4 * 4 + 3  # library default + tcgen05 grid + SIMT tiles
+    default = MatmulSearchSpace().library_default(GEMM)
+    assert result.candidates[0] == default, "the library default is always measured, first"
     assert 0 < result.feasible < result.generated
     assert len(result.candidates) <= DEFAULT_MAX_CANDIDATES
     assert len(set(result.candidates)) == len(result.candidates)
