@@ -18,6 +18,10 @@
  *   kf_rmsnorm_rows     kernels/rmsnorm.py:81-127        rmsnorm(x, gamma, eps=, config=)
  *                       and csrc/rmsnorm.cu:19-57        (the hand-written CUDA baseline)
  *   kf_query_gemm_config  tuning/search.py:299-394      shared-memory / feasibility model
+ *   kf_gemv_noalloc     as kf_gemv, for callers that cannot hand over a workspace
+ *   kf_linear_bias_act_allgather, kf_peer_barrier, kf_ipc_handle / _open / _close
+ *                       the column-sharded fused linear over several GPUs (the
+ *                       reference is single-GPU: no counterpart)
  *
  * Status codes are returned by value; kf_last_error() gives the message of the
  * most recent failure on the calling thread.
