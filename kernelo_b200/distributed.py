@@ -176,6 +176,8 @@ class ShardedFusedLinear:
         from kernelo_b200.kernels.fused_linear import _EPILOGUES
         from kernelo_b200.runtime import native
 
+        if not self.w.is_cuda:
+            raise ValueError("forward_host runs the all-gathering kernel: the layer must be on a CUDA device")
         if not (x_host.is_pinned() and out.is_pinned()):
             raise ValueError("forward_host needs pinned host tensors")
         m, k = x_host.shape

@@ -30,6 +30,15 @@ def test_shard_chunk_and_row_range():
         kd.row_range(10, 2, 2)
 
 
+def test_forward_host_refuses_a_cpu_layer():
+    """The host-to-host path runs the all-gathering kernel: a CPU layer is an
+    error up front, not a failure deep inside torch."""
+    w = torch.zeros(32, 16)
+    layer = kd.ShardedFusedLinear(w, torch.zeros(32))
+    with pytest.raises(ValueError, match="CUDA device"):
+        layer.forward_host(torch.zeros(4, 16), torch.zeros(4, 32))
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
