@@ -54,6 +54,29 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 NVLINK_GBS = 770.0
 
 
+def allgather_roofline(flop_rank: float, link_bytes: int, kernel_ms: float, tensor_peak: float,
+                       tensor_peak_kind: str) -> dict:
+    """Roofline of the GEMM + all-gather kernel: the target time is the slower
+    of the shard's FLOPs at the GEMM peak and the bytes each rank must send over
+    NVLink (its shard to every peer) at the measured peer-copy rate; ``frac``
+    is target / measured, in the units of the binding resource."""
+    t_tensor = flop_rank / (tensor_peak * 1e12)
+    t_link = link_bytes / (NVLINK_GBS * 1e9)
+    tflops = flop_rank / (kernel_ms * 1e-3) / 1e12
+    link_gbs = link_bytes / (kernel_ms * 1e-3) / 1e9
+    target_ms = max(t_tensor, t_link) * 1e3
+    nvlink_bound = t_link > t_tensor
+    return {"bound": "nvlink" if nvlink_bound else "tensor",
+            "achieved": round(link_gbs if nvlink_bound else tflops, 1),
+            "peak": NVLINK_GBS if nvlink_bound else tensor_peak,
+            "unit": "GB/s" if nvlink_bound else "TFLOP/s",
+            "frac": round(target_ms / kernel_ms, 4), "target_ms": round(target_ms, 4),
+            "tensor_tflops": round(tflops, 1), "tensor_peak": tensor_peak, "tensor_peak_kind": tensor_peak_kind,
+            "nvlink_gbs": round(link_gbs, 1), "nvlink_bytes_per_rank": link_bytes,
+            "nvlink_peak_kind": "measured peer copy per direction on this pool",
+            "traffic": None, "kernel": "tc_gemm_kernel<bf16,erf,all-gather>", "kernel_ms": round(kernel_ms, 4)}
+
+
 def peaks() -> tuple[dict, str]:
     path = REPO / "MEASURED_PEAKS.json"
     if path.exists():
@@ -440,25 +463,7 @@ def run_native(args, world: int, rank: int, local: int) -> int:
                     "traffic": profile_traffic("tc_gemm_fused_linear_erf_bf16"),
                     "kernel": "tc_gemm_kernel<bf16,erf>", "kernel_ms": round(kernel_ms, 4)}
     else:
-        # GEMM + all-gather in one kernel: the target is the slower of the
-        # shard's FLOPs at the GEMM peak and the bytes each rank must send
-        # over NVLink (its shard to every peer) at the measured peer-copy rate.
-        link_bytes = M * chunk * 2 * (world - 1)
-        t_tensor = flop_rank / (peak * 1e12)
-        t_link = link_bytes / (NVLINK_GBS * 1e9)
-        link_gbs = link_bytes / (kernel_ms * 1e-3) / 1e9
-        target_ms = max(t_tensor, t_link) * 1e3
-        nvlink_bound = t_link > t_tensor
-        roofline = {"bound": "nvlink" if nvlink_bound else "tensor",
-                    "achieved": round(link_gbs if nvlink_bound else achieved, 1),
-                    "peak": NVLINK_GBS if nvlink_bound else peak,
-                    "unit": "GB/s" if nvlink_bound else "TFLOP/s",
-                    "frac": round(target_ms / kernel_ms, 4), "target_ms": round(target_ms, 4),
-                    "tensor_tflops": round(achieved, 1), "tensor_peak": peak, "tensor_peak_kind": peak_kind,
-                    "nvlink_gbs": round(link_gbs, 1), "nvlink_bytes_per_rank": link_bytes,
-                    "nvlink_peak_kind": "measured peer copy per direction on this pool",
-                    "traffic": None, "kernel": "tc_gemm_kernel<bf16,erf,all-gather>",
-                    "kernel_ms": round(kernel_ms, 4)}
+        roofline = allgather_roofline(flop_rank, M * chunk * 2 * (world - 1), kernel_ms, peak, peak_kind)
 
     # end to end through the public API: pinned host X in, Y back to pinned host
     e2e_steps = max(3, min(20, args.steps))
