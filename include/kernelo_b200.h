@@ -75,11 +75,13 @@ enum kf_gemm_kernel {
   KF_GEMM_SIMT = 2,    /* CUDA-core FFMA, any strides, fp16/bf16/fp32        */
   KF_GEMM_WARP_ROWS = 3, /* kf_gemv only: a warp per K-contiguous weight row,
                            M <= 4, packed fp32x2 FMA; num_ctas = grid size   */
-  KF_GEMM_TILE_ROWS = 4  /* kf_gemv only: a CTA per 16 K-contiguous weight rows,
+  KF_GEMM_TILE_ROWS = 4  /* a CTA per 16 K-contiguous weight rows (B's columns),
                            M <= 16, fp16/bf16, K % 8 == 0; the weight registers
                            feed mma.sync.m16n8k16 directly; block_m = warps
                            per tile (K slices), stages = 16-byte vector pairs
-                           per lane in flight                                */
+                           per lane in flight. kf_gemv, and kf_gemm /
+                           kf_linear_bias_act (epilogue included); AUTO picks
+                           it for such shapes                               */
 };
 
 /* Tunable GEMM parameters. Replaces KernelConfig's BLOCK_M/BLOCK_N/BLOCK_K/
