@@ -344,25 +344,56 @@ def distributed_tune(tuner, operator, problem, *, device=None, group=None, final
     """Tune with the candidate list dealt round-robin over the group's ranks.
 
     Every rank returns the merged :class:`TuningResult`; only rank 0 persists
-    it (the tuner's ``db``/``cache`` are ignored on other ranks). Rank 0 re-times
+    it (the tuner's ``db``/``cache`` are ignored on other ranks). With
+    ``resume`` on rank 0's tuner, candidates its database already holds for
+    this problem and device are not measured again on any rank. Rank 0 re-times
     its best ``finalists`` candidates locally before ranking, so the winner is
     chosen from measurements taken on one GPU.
     """
     world, rank = world_info(group)
     if world == 1:
         return tuner.tune(operator, problem, device=device)
-    db, cache = tuner.db, tuner.cache
+    db, cache, resume = tuner.db, tuner.cache, tuner.resume
+    # Resuming (rank 0's tuner decides, rank 0 being the database's only reader
+    # and writer): rank 0 looks up the candidates already measured on this
+    # device and tells every rank to skip them; their stored outcomes rejoin
+    # the merged list on rank 0.
+    reused: dict = {}
+    if resume and rank == 0:
+        from kernelo_b200.runtime.env import capture_environment, device_caps
+        from kernelo_b200.tuning.tuner import _outcome_from_row
+
+        target = torch.device(device) if device is not None else None
+        key = capture_environment(target).device_key
+        cset = operator.search_space().generate(problem, device_caps(target),
+                                                max_candidates=tuner.max_candidates)
+        for c in cset.candidates:
+            row = db.latest_result(problem, c, device_key=key)
+            if row is not None:
+                reused[c] = _outcome_from_row(c, row)
+    done = [sorted(c.digest for c in reused) if rank == 0 else None]
+    dist.broadcast_object_list(done, src=0, group=group)
+    skip = set(done[0])
     saved_filter = tuner.candidate_filter
     tuner.db = tuner.cache = None
-    tuner.candidate_filter = lambda i, c: i % world == rank
+    tuner.resume = False
+    fresh_index: dict = {}
+
+    def deal(i, c):  # round-robin over the candidates not measured yet
+        if c.digest in skip:
+            return False
+        j = fresh_index.setdefault(c.digest, len(fresh_index))
+        return j % world == rank
+
+    tuner.candidate_filter = deal
     try:
         local = tuner.tune(operator, problem, device=device)
     finally:
         tuner.candidate_filter = saved_filter
-        tuner.db, tuner.cache = db, cache
+        tuner.db, tuner.cache, tuner.resume = db, cache, resume
     gathered: list = [None] * world
     dist.all_gather_object(gathered, local.outcomes, group=group)
-    merged = [o for part in gathered for o in part]
+    merged = [o for part in gathered for o in part] + list(reused.values())
     result = replace(local, outcomes=tuple(merged))
     if rank == 0:
         correct = sorted((o for o in merged if o.ok and o.timing is not None), key=lambda o: o.median_ms)
@@ -371,7 +402,7 @@ def distributed_tune(tuner, operator, problem, *, device=None, group=None, final
             keep = {id(o) for o in correct[:finalists]}
             others = [o for o in merged if id(o) not in keep]
             result = replace(result, outcomes=tuple(retimed + others))
-        tuner._persist(result, result.environment)
+        tuner._persist(result, result.environment, skip=set(reused))
     # Every rank returns rank 0's ranking (the one measured on a single GPU).
     final = [result.outcomes if rank == 0 else None]
     dist.broadcast_object_list(final, src=0, group=group)

@@ -96,6 +96,36 @@ def _tune_worker(rank: int, world: int, port: int, tmpdir: str, out_q) -> None:
         dist.destroy_process_group()
 
 
+def _resume_worker(rank: int, world: int, port: int, tmpdir: str, out_q) -> None:
+    """Tune once, then again with resume=True: the second sweep measures nothing."""
+    _init(rank, world, port)
+    try:
+        from kernelo_b200.db import ResultsDB
+        from kernelo_b200.tuning.tuner import Tuner
+        from tests.test_tuner import PROBLEM, _FakeOperator
+
+        db = ResultsDB(os.path.join(tmpdir, "r.db")) if rank == 0 else None
+        first = kd.distributed_tune(Tuner(warmup=1, iterations=3, flush_l2=False, measure_baselines=False, db=db),
+                                    _FakeOperator(), PROBLEM, device="cpu", finalists=0)
+        calls = []
+
+        class _Counting(_FakeOperator):
+            def run(self, config, x):
+                calls.append(config)
+                return super().run(config, x)
+
+        # only rank 0 holds the database, so only its tuner asks to resume; it
+        # decides for every rank what is already done
+        tuner = Tuner(warmup=1, iterations=3, flush_l2=False, measure_baselines=False, db=db,
+                      resume=db is not None)
+        second = kd.distributed_tune(tuner, _Counting(), PROBLEM, device="cpu", finalists=0)
+        rows = db.counts()["results"] if db is not None else None
+        out_q.put((rank, len(calls), first.tested, second.tested,
+                   (first.best.config["MODE"], second.best.config["MODE"]), rows))
+    finally:
+        dist.destroy_process_group()
+
+
 def _run(target, *args):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -114,6 +144,15 @@ def test_sharded_fused_linear_gathers_columns_on_two_ranks():
     for rank, shape, err in _run(_sharded_linear_worker):
         assert shape == (6, 50)
         assert err < 1e-5
+
+
+def test_resumed_distributed_sweep_measures_nothing_twice(tmp_path):
+    results = _run(_resume_worker, str(tmp_path))
+    for rank, calls, first_tested, second_tested, (first_best, second_best), rows in results:
+        assert calls == 0, f"rank {rank} re-ran {calls} stored candidates"
+        assert second_tested == first_tested == 6
+        assert second_best == first_best, "the stored outcomes rank as they did when measured"
+    assert results[0][5] == 6  # rank 0's database: the first sweep's rows, none added
 
 
 def test_tuning_sweep_is_dealt_over_ranks_and_written_once(tmp_path):
