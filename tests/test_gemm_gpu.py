@@ -5,8 +5,10 @@ tests/test_fused_linear.py): awkward shapes (primes, one-off-a-tile, single
 rows/columns) in every dtype, several tile configs per shape, every budgeted
 candidate, non-contiguous views, fp32 held to the fp32 gate, and the fusion's
 launch count -- plus the sm_100a specifics: both weight layouts, swapped
-skinny shapes, stream-K workspace reuse and determinism, and the baseline's
-full sizes checked on sampled rows.
+skinny shapes, stream-K workspace reuse and determinism, the split tail, the
+GELU epilogues held to one ulp of float64, the decode kernels (16-row tiles,
+warp-per-row) and the decode-shape fused linear, outputs pre-filled with NaN
+so a skipped tile fails, and the baseline's full sizes checked on sampled rows.
 """
 
 from __future__ import annotations

@@ -4,7 +4,9 @@ Follows tests/test_softmax_and_vector_add.py and tests/test_rmsnorm.py of the
 reference: awkward widths in every dtype, overflow logits, constant rows, zero
 rows, the fp32-reduction teeth test, indivisible rows per program, every
 candidate -- plus the widths the reference kernels refuse (4097 with unaligned
-rows, 32000 through a thread-block cluster) and the baseline sizes.
+rows, 32000 through a thread-block cluster), the streaming kernel's launch
+shapes and refusals, the kernel chosen per row width, outputs pre-filled with
+NaN, and the baseline sizes.
 """
 
 from __future__ import annotations
