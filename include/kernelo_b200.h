@@ -76,7 +76,7 @@ enum kf_gemm_kernel {
   KF_GEMM_WARP_ROWS = 3, /* kf_gemv only: a warp per K-contiguous weight row,
                            M <= 4, packed fp32x2 FMA; num_ctas = grid size   */
   KF_GEMM_TILE_ROWS = 4  /* a CTA per 16 K-contiguous weight rows (B's columns),
-                           M <= 16, fp16/bf16, K % 8 == 0; the weight registers
+                           M <= 32, fp16/bf16, K % 8 == 0; the weight registers
                            feed mma.sync.m16n8k16 directly; block_m = warps
                            per tile (K slices), stages = 16-byte vector pairs
                            per lane in flight. kf_gemv, and kf_gemm /

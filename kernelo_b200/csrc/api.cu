@@ -194,7 +194,7 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
     return set_error(KF_ERR_INVALID_ARGUMENT, "epilogue needs a bias pointer");
   if (g.epilogue < KF_EPI_NONE || g.epilogue > KF_EPI_BIAS_GELU_ERF)
     return set_error(KF_ERR_INVALID_ARGUMENT, "unknown epilogue code");
-  // Up to 16 rows of x against a K-contiguous 16-bit B (an nn.Linear weight
+  // Up to 32 rows of x against a K-contiguous 16-bit B (an nn.Linear weight
   // [N, K] passed as its transpose): the 16-row tile kernel, epilogue
   // included (the decode-shape fused linear). It reads the weight at 0.8 of
   // the copy bandwidth against ~0.55 for 128-row TMA tiles.
@@ -381,7 +381,7 @@ int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const 
                 int64_t workspace_bytes, void* stream) {
   if (M > 256) return set_error(KF_ERR_UNSUPPORTED, "kf_gemv takes M <= 256; use kf_gemm");
   kf_gemm_config c = cfg ? *cfg : zero_config();
-  // Up to 16 rows of x with K-contiguous 16-bit weight rows: 16-row weight
+  // Up to 32 rows of x with K-contiguous 16-bit weight rows: 16-row weight
   // tiles streamed by warps straight into mma.sync fragments (measured on
   // B200 at 11008 x 4096: 0.80 of the copy bandwidth at M = 1 and 4, 0.71 at
   // M = 16, against 0.53 for 128-row TMA tiles).

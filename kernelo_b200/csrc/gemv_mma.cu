@@ -1,5 +1,5 @@
 // Decode-shape GEMV with 16-row weight tiles: y[m, n] = epi(sum_k x[m, k] w[n, k])
-// for M <= 16 and a weight whose rows are K-contiguous (nn.Linear's [N, K]);
+// for M <= 32 and a weight whose rows are K-contiguous (nn.Linear's [N, K]);
 // epi is none, + bias[n], or + bias[n] then GELU (the fused linear at decode
 // shapes).
 //
@@ -19,7 +19,7 @@
 // once into y.
 //
 // The tensor-core instruction here is the warp-level mma.sync, not tcgen05:
-// at M <= 16 the contraction is under 1 % of the time, and what decides the
+// at M <= 32 the contraction is a small part of the time, and what decides the
 // speed is the weight stream. tcgen05 operands come from shared memory as TMA
 // boxes of 128 rows x 128 bytes, which measured 3.5 TB/s on this shape; rows
 // streamed contiguously by warps measured 4.8 TB/s (same W, same M).
@@ -60,7 +60,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
   }
 }
 
-// NT: 8-row groups of x (1 for M <= 8, 2 for M <= 16); S: warps per CTA (K
+// NT: 8-row groups of x (1 for M <= 8, 2 for M <= 16, 4 for M <= 32); S: warps per CTA (K
 // slices); U: vector pairs per lane in flight.
 // At least five CTAs per SM: a tile's CTA lasts about the whole kernel, so
 // all of them (688 for N = 11008) must be resident at once.
@@ -172,10 +172,12 @@ int launch_shape(const GemvMmaParams& p, cudaStream_t stream) {
 // Launch shapes (S warps per tile, U vector pairs in flight per lane): config
 // block_m selects S and stages selects U; zero picks the default, measured
 // on B200 at N = 11008, K = 4096: (8, 2) up to 8 rows of x (17.0 us at M=1,
-// 17.9 at M=4), (6, 4) above (19.6 us at M=16; 8 warps of 4 pairs spill).
+// 17.9 at M=4), (6, 4) up to 16 (19.6 us at M=16; 8 warps of 4 pairs spill),
+// (4, 4) up to 32 (23.1 / 24.0 us at M = 24 / 32 against 27.1 / 27.4 for the
+// tcgen05 GEMV; 6 warps spill there).
 template <typename T, int NT, int EPI>
 int launch_nt(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t stream) {
-  const int s = cfg.block_m != 0 ? cfg.block_m : (NT == 1 ? 8 : 6);
+  const int s = cfg.block_m != 0 ? cfg.block_m : (NT == 1 ? 8 : NT == 2 ? 6 : 4);
   const int u = cfg.stages != 0 ? cfg.stages : (NT == 1 ? 2 : 4);
   if (s == 4 && u == 4) return launch_shape<T, NT, 4, 4, EPI>(p, stream);
   if (s == 4 && u == 2) return launch_shape<T, NT, 4, 2, EPI>(p, stream);
@@ -191,7 +193,9 @@ int launch_nt(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t st
 
 template <typename T, int EPI>
 int launch_epi(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t stream) {
-  return p.M <= 8 ? launch_nt<T, 1, EPI>(p, cfg, stream) : launch_nt<T, 2, EPI>(p, cfg, stream);
+  if (p.M <= 8) return launch_nt<T, 1, EPI>(p, cfg, stream);
+  if (p.M <= 16) return launch_nt<T, 2, EPI>(p, cfg, stream);
+  return launch_nt<T, 4, EPI>(p, cfg, stream);
 }
 
 template <typename T>
@@ -214,7 +218,7 @@ bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, co
     return false;
   };
   if (dtype != KF_FP16 && dtype != KF_BF16) return no("the tile GEMV takes fp16 or bf16");
-  if (M < 1 || M > GEMV_MMA_MAX_M) return no("the tile GEMV takes 1..16 rows of x");
+  if (M < 1 || M > GEMV_MMA_MAX_M) return no("the tile GEMV takes 1..32 rows of x");
   if (N > INT32_MAX || K > INT32_MAX) return no("dimensions above 2^31");
   if (K % 8 != 0) return no("K must be a multiple of 8 (whole 16-byte vectors)");
   if (sw_k != 1 || sx_k != 1) return no("weight and x rows must be K-contiguous");

@@ -72,8 +72,8 @@ int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream
 constexpr int GEMM_PEER_STAGE_BYTES = 8 * 32 * 64 * 2;
 constexpr int GEMM_PEER_STAGE_SMEM = GEMM_PEER_STAGE_BYTES + 1024;
 
-// 16-row tile decode GEMV (gemv_mma.cu): M <= 16, fp16/bf16.
-constexpr int GEMV_MMA_MAX_M = 16;
+// 16-row tile decode GEMV (gemv_mma.cu): M <= 32, fp16/bf16.
+constexpr int GEMV_MMA_MAX_M = 32;
 bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w, int64_t sw_n,
                         int64_t sw_k, int64_t M, int64_t N, int64_t K, std::string* why);
 int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,

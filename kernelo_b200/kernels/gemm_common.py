@@ -23,17 +23,22 @@ KERNEL_TCGEN05 = 1
 KERNEL_SIMT = 2
 #: kf_gemv only: warps streaming K-contiguous weight rows, M <= 4 (csrc/gemv_rows.cu).
 KERNEL_WARP_ROWS = 3
-#: kf_gemv's 16-row weight tiles on mma.sync (fp16/bf16, M <= 16, K % 8 == 0);
+#: kf_gemv's 16-row weight tiles on mma.sync (fp16/bf16, M <= 32, K % 8 == 0);
 #: BLOCK_M = warps per tile (K slices), num_stages = vector pairs in flight.
 KERNEL_TILE_ROWS = 4
-TILE_ROWS_MAX_M = 16
+TILE_ROWS_MAX_M = 32
 #: (warps per tile, vector pairs in flight) compiled in gemv_mma.cu
 TILE_ROWS_SHAPES = ((8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8))
 
 
+def tile_rows_groups(m: int) -> int:
+    """8-row groups of x the kernel is compiled for (mirrors gemv_mma.cu)."""
+    return 1 if m <= 8 else (2 if m <= 16 else 4)
+
+
 def tile_rows_default(m: int) -> tuple[int, int]:
     """The kernel's default shape (mirrors gemv_mma.cu)."""
-    return (8, 2) if m <= 8 else (6, 4)
+    return {1: (8, 2), 2: (6, 4), 4: (4, 4)}[tile_rows_groups(m)]
 
 
 def tile_rows_reject(m: int, k: int, dtype: torch.dtype) -> str | None:
@@ -181,7 +186,7 @@ def default_gemm_config(
     operation: str, m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str, sm_count: int = 148
 ) -> KernelConfig:
     """The library's choice for contiguous operands (mirrors gemm_common in api.cu): the 16-row
-    tile kernel for up to 16 rows of x against a K-contiguous B, else tcgen05 tiles where TMA
+    tile kernel for up to 32 rows of x against a K-contiguous B, else tcgen05 tiles where TMA
     can describe the operands, else the CUDA-core kernel."""
     if b_layout == "nk" and tile_rows_reject(m, k, dtype) is None:
         warps, pairs = tile_rows_default(m)

@@ -6,15 +6,16 @@ row), and README.md:666-670 lists split-K as future work. This shape moves
 90 MB of weight for 90 MFLOP (1 FLOP/byte), so it is bound by HBM, not by the
 tensor cores. Three sm_100a kernels, chosen by the library:
 
-* fp16/bf16 x with up to 16 rows and a K-contiguous [N,K] weight (K % 8 == 0):
+* fp16/bf16 x with up to 32 rows and a K-contiguous [N,K] weight (K % 8 == 0):
   the 16-row tile kernel (``KERNEL=4``, ``csrc/gemv_mma.cu``). One CTA per 16
   weight rows, K split over its warps; lanes stream the rows with contiguous
   loads straight into ``mma.sync`` fragments (0.84 / 0.80 / 0.76 of the copy
-  bandwidth at M = 1 / 4 / 16 on B200).
+  bandwidth at M = 1 / 4 / 16 on B200; at M = 32 24 us against 27 us for the
+  tcgen05 GEMV).
 * fp32 x with M <= 2: the warp-per-row CUDA-core kernel (``KERNEL=3``,
   ``csrc/gemv_rows.cu``), packed fp32x2 FMAs against x held in shared memory;
   it takes M <= 4 when asked for.
-* otherwise (a [K,N] weight, unaligned rows, M > 16): the tcgen05 GEMM with A
+* otherwise (a [K,N] weight, unaligned rows, M > 32): the tcgen05 GEMM with A
   and B swapped -- the weight becomes the 128-row MMA operand -- and K split
   evenly over every SM (stream-K); the last CTA to finish a tile sums the
   partials in a fixed order.

@@ -258,7 +258,7 @@ class _Sm100GemmSpace(SearchSpace):
     def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             m = self.dims(problem)[0]
-            return (config["BLOCK_M"] - 1) * 32 * (1 if m <= 8 else 2) * 16  # the K-slice partials
+            return (config["BLOCK_M"] - 1) * 32 * gc.tile_rows_groups(m) * 16  # the K-slice partials
         if config["KERNEL"] == gc.KERNEL_SIMT:
             return 2 * config["BLOCK_K"] * (config["BLOCK_M"] + config["BLOCK_N"]) * 4
         return gc.tc_smem_bytes(config["BLOCK_N"], config["BLOCK_K"], config["num_stages"],

@@ -342,7 +342,8 @@ def test_gemv_default_kernel_choice():
         assert default_config(m, 11008, 4096, torch.float16)["KERNEL"] == 4
     assert default_config(1, 11008, 4096, torch.float32)["KERNEL"] == 3
     assert default_config(2, 11008, 4099, torch.bfloat16)["KERNEL"] == 3  # K % 8 != 0
-    assert default_config(17, 11008, 4096, torch.float16)["KERNEL"] == 1
+    assert default_config(32, 11008, 4096, torch.float16)["KERNEL"] == 4
+    assert default_config(33, 11008, 4096, torch.float16)["KERNEL"] == 1
 
 
 # ------------------------------------------------------------------ 16-row tile GEMV (mma.sync)
@@ -350,7 +351,7 @@ def tile_cfg(warps=0, pairs=0):
     return KernelConfig("gemv", KERNEL=4, BLOCK_M=warps, num_stages=pairs)
 
 
-@pytest.mark.parametrize("m", [1, 3, 4, 8, 9, 16])
+@pytest.mark.parametrize("m", [1, 3, 4, 8, 9, 16, 17, 24, 32])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_gemv_tile_rows(m, dtype, device):
     """Both x-row groupings (M <= 8, M <= 16) with unused rows masked; N = 1000
@@ -365,7 +366,7 @@ def test_gemv_tile_rows(m, dtype, device):
 
 
 @pytest.mark.parametrize("shape", [(8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8)])
-@pytest.mark.parametrize("m", [4, 16])
+@pytest.mark.parametrize("m", [4, 16, 32])
 def test_gemv_tile_rows_every_shape(shape, m, device):
     gen = torch.Generator().manual_seed(7 * shape[0] + shape[1])
     x = torch.randn(m, 4096, generator=gen).half().to(device)

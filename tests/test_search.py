@@ -213,14 +213,14 @@ def test_gemv_tile_rows_candidates(b200_caps):
     tile = KernelConfig("gemv", KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=8, num_stages=2)
     assert space.reject_reason(tile, Problem.create("gemv", "fp32", M=1, N=64, K=64), b200_caps).startswith(
         "the tile GEMV takes fp16 or bf16")
-    assert "1..16 rows" in space.reject_reason(tile, Problem.create("gemv", "fp16", M=17, N=64, K=64), b200_caps)
+    assert "1..32 rows" in space.reject_reason(tile, Problem.create("gemv", "fp16", M=33, N=64, K=64), b200_caps)
     assert "K % 8" in space.reject_reason(tile, Problem.create("gemv", "fp16", M=2, N=64, K=4099), b200_caps)
 
 
 def test_fused_linear_decode_shapes_take_tile_rows(b200_caps):
     from kernelo_b200.tuning.search import FusedLinearErfSearchSpace, MatmulSearchSpace
 
-    for m, expected in ((1, 4), (16, 4), (17, 1), (4096, 1)):
+    for m, expected in ((1, 4), (16, 4), (32, 4), (33, 1), (4096, 1)):
         cfg = gc.default_gemm_config("fused_linear_erf", m, 11008, 4096, torch.bfloat16, b_layout="nk")
         assert cfg["KERNEL"] == expected, (m, cfg)
     decode = Problem.create("fused_linear_erf", "bf16", M=4, N=11008, K=4096)
