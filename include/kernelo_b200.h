@@ -233,9 +233,11 @@ KF_API int32_t kf_rmsnorm_rows(int32_t dtype, const void* x, int64_t sx_row, con
  * its own Y as y and the same block of every peer's Y as y_peers: when every
  * rank's call has finished and kf_peer_barrier has run, every rank holds all
  * of Y with no collective and no copy. The epilogue ends with a system-scope
- * fence. tcgen05 path only (n_peers <= KF_MAX_PEERS). No reference
- * counterpart: the reference is single-GPU; this replaces the NCCL
- * all_gather of the sharded fused linear. */
+ * fence. Runs on the tcgen05 GEMM, or at M <= 32 with a K-contiguous 16-bit
+ * weight on the 16-row tile GEMV (the decode-shape layer; epilogue KF_EPI_NONE
+ * with a null bias gives the plain sharded GEMV); n_peers <= KF_MAX_PEERS.
+ * No reference counterpart: the reference is single-GPU; this replaces the
+ * NCCL all_gather of the column-sharded fused linear and decode GEMV. */
 KF_API int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
                                             const void* w, int64_t sw_k, int64_t sw_n,
                                             const void* bias, void* y, int64_t sy_m, int64_t sy_n,

@@ -195,24 +195,26 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
   if (g.epilogue < KF_EPI_NONE || g.epilogue > KF_EPI_BIAS_GELU_ERF)
     return set_error(KF_ERR_INVALID_ARGUMENT, "unknown epilogue code");
   // Up to 32 rows of x against a K-contiguous 16-bit B (an nn.Linear weight
-  // [N, K] passed as its transpose): the 16-row tile kernel, epilogue
-  // included (the decode-shape fused linear). It reads the weight at 0.8 of
-  // the copy bandwidth against ~0.55 for 128-row TMA tiles.
-  const bool tile_auto = (user == nullptr || user->kernel == KF_GEMM_AUTO) && g.n_peers == 0 &&
-                         g.M <= GEMV_MMA_MAX_M &&
+  // [N, K] passed as its transpose): the 16-row tile kernel, epilogue and
+  // peer stores included (the decode-shape fused linear and its all-gather).
+  // It reads the weight at 0.8 of the copy bandwidth against ~0.55 for
+  // 128-row TMA tiles.
+  const bool tile_auto = (user == nullptr || user->kernel == KF_GEMM_AUTO) && g.M <= GEMV_MMA_MAX_M &&
                          gemv_mma_supported(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_n, g.sb_k, g.M, g.N,
                                             g.K, nullptr);
   if (tile_auto || (user != nullptr && user->kernel == KF_GEMM_TILE_ROWS)) {
     std::string why;
-    if (g.n_peers > 0) return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 path only");
     if (!gemv_mma_supported(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_n, g.sb_k, g.M, g.N, g.K, &why))
       return set_error(KF_ERR_UNALIGNED, "tile GEMV: " + why);
     // The library's own choice ignores the other config fields (they describe
     // tcgen05 tiles when the kernel was left to the library).
     return launch_gemv_mma(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K,
                            tile_auto ? zero_config() : *user, static_cast<cudaStream_t>(stream), g.epilogue,
-                           g.bias);
+                           g.bias, g.peers, g.n_peers);
   }
+  if (g.n_peers > 0 && !tcgen05_operands_ok(g, nullptr))
+    return set_error(KF_ERR_UNALIGNED,
+                     "the all-gather epilogue needs TMA-describable operands (or the tile GEMV's, M <= 32)");
   int device = 0;
   int rc = current_device(&device);
   if (rc != KF_OK) return rc;
@@ -232,7 +234,7 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
   if (cfg.kernel == KF_GEMM_TCGEN05) return launch_gemm_tcgen05(g, cfg, *dev, s);
   if (cfg.kernel == KF_GEMM_SIMT) {
     if (g.n_peers > 0)
-      return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 path only");
+      return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 and tile GEMV paths only");
     return launch_gemm_simt(g, cfg, s);
   }
   return set_error(KF_ERR_INVALID_CONFIG, "unknown GEMM kernel code");
@@ -334,7 +336,7 @@ int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_t sx_m,
                      "n_peers must be in [0, " + std::to_string(KF_MAX_PEERS) + "]");
   if (n_peers > 0 && y_peers == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null y_peers");
   if (cfg != nullptr && cfg->kernel == KF_GEMM_SIMT && n_peers > 0)
-    return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 path only");
+    return set_error(KF_ERR_UNSUPPORTED, "the all-gather epilogue is on the tcgen05 and tile GEMV paths only");
   GemmArgs g;
   g.dtype = dtype;
   g.a = x;
@@ -358,8 +360,6 @@ int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_t sx_m,
     if (y_peers[i] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer output pointer");
     g.peers[i] = y_peers[i];
   }
-  if (n_peers > 0 && !tcgen05_operands_ok(g, nullptr))
-    return set_error(KF_ERR_UNALIGNED, "the all-gather epilogue needs TMA-describable operands");
   return gemm_common(g, cfg, stream);
 }
 

@@ -24,6 +24,11 @@
 // boxes of 128 rows x 128 bytes, which measured 3.5 TB/s on this shape; rows
 // streamed contiguously by warps measured 4.8 TB/s (same W, same M).
 //
+// With peer pointers the kernel is also the column-sharded decode layer's
+// all-gather: each output element goes to this rank's y and, at the same
+// offset, to every peer's copy (at M = 16 and 8 ranks, 44 KB per peer), so
+// no collective follows the GEMV -- only the bounded peer barrier.
+//
 // Replaces the reference's matmul launch at decode shapes
 // (kernelforge/kernels/matmul.py:132-155 with M in {1, 4, 16}); fp32
 // accumulation and one output rounding as in the reference's matmul.
@@ -42,6 +47,10 @@ struct GemvMmaParams {
   long long sy_m, sy_n;
   const void* bias;  // [N], for the bias / GELU epilogues
   int M, N, K;
+  // Peer copies of y (same strides; the element that corresponds to y[0, 0]):
+  // every output element is stored there too -- the decode-shape all-gather.
+  int n_peers;
+  void* peers[KF_MAX_PEERS];
 };
 
 template <typename T>
@@ -153,11 +162,21 @@ __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams
     for (int i = 0; i < 4; ++i) {
       const int m = 8 * nt + 2 * t + (i & 1);
       const int n = n0 + g + (i >> 1) * 8;
-      if (m < p.M && n < p.N)
-        y[m * p.sy_m + static_cast<long long>(n) * p.sy_n] =
-            from_f32<T>(apply_epilogue<EPI>(acc[nt][i], bias[i >> 1]));
+      if (m < p.M && n < p.N) {
+        const long long off = m * p.sy_m + static_cast<long long>(n) * p.sy_n;
+        const T v = from_f32<T>(apply_epilogue<EPI>(acc[nt][i], bias[i >> 1]));
+        y[off] = v;
+        // Peer stores: the same element into every other rank's copy of y over
+        // NVLink. Eight lanes of a quad column write 16 contiguous bytes.
+#pragma unroll
+        for (int j = 0; j < KF_MAX_PEERS; ++j)
+          if (j < p.n_peers) static_cast<T*>(p.peers[j])[off] = v;
+      }
     }
   }
+  // The peer barrier that follows on the stream publishes these stores with a
+  // system-scope release; this fence orders them before the kernel ends.
+  if (p.n_peers > 0) __threadfence_system();
 }
 
 template <typename T, int NT, int S, int U, int EPI>
@@ -231,9 +250,12 @@ bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, co
 
 int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
                     int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
-                    const kf_gemm_config& cfg, cudaStream_t stream, int epilogue, const void* bias) {
+                    const kf_gemm_config& cfg, cudaStream_t stream, int epilogue, const void* bias,
+                    void* const* peers, int n_peers) {
   if (epilogue != KF_EPI_NONE && bias == nullptr)
     return set_error(KF_ERR_INVALID_ARGUMENT, "epilogue needs a bias pointer");
+  if (n_peers < 0 || n_peers > KF_MAX_PEERS || (n_peers > 0 && peers == nullptr))
+    return set_error(KF_ERR_INVALID_ARGUMENT, "tile GEMV: bad peer list");
   GemvMmaParams p{};
   p.x = x;
   p.sx_m = sx_m;
@@ -246,6 +268,11 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
   p.bias = bias;
+  p.n_peers = n_peers;
+  for (int j = 0; j < n_peers; ++j) {
+    if (peers[j] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer output pointer");
+    p.peers[j] = peers[j];
+  }
   if (N == 0 || M == 0) return KF_OK;
   if (dtype == KF_BF16) return launch_typed<__nv_bfloat16>(p, cfg, epilogue, stream);
   return launch_typed<__half>(p, cfg, epilogue, stream);

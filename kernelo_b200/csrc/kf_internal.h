@@ -72,14 +72,16 @@ int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream
 constexpr int GEMM_PEER_STAGE_BYTES = 8 * 32 * 64 * 2;
 constexpr int GEMM_PEER_STAGE_SMEM = GEMM_PEER_STAGE_BYTES + 1024;
 
-// 16-row tile decode GEMV (gemv_mma.cu): M <= 32, fp16/bf16.
+// 16-row tile decode GEMV (gemv_mma.cu): M <= 32, fp16/bf16. With n_peers > 0
+// every output element is also stored at the same offset from each peers[i]
+// (the decode-shape all-gather; the caller's barrier publishes it).
 constexpr int GEMV_MMA_MAX_M = 32;
 bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w, int64_t sw_n,
                         int64_t sw_k, int64_t M, int64_t N, int64_t K, std::string* why);
 int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
                     int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
                     const kf_gemm_config& cfg, cudaStream_t stream, int epilogue = KF_EPI_NONE,
-                    const void* bias = nullptr);
+                    const void* bias = nullptr, void* const* peers = nullptr, int n_peers = 0);
 
 // Softmax kernel choice by row width in 16-byte vectors (rows.cu).
 constexpr long long SOFTMAX_STREAM_MAX_VECTORS = 128;     // up to 2 KB: streaming kernel

@@ -13,6 +13,11 @@ Three shardings, each where the work splits naturally:
   off CUDA) exchanges the slices with one ``all_gather_into_tensor`` of the
   group's backend and permutes them into [M, N]. N is padded to ``world * chunk`` with zero weight rows (their
   columns are dropped).
+* :class:`ShardedGemv` -- the decode GEMV ``x @ W^T`` sharded the same way:
+  each rank streams 1/world of the weight (the HBM-bound part) through the
+  16-row tile kernel, whose stores also write every peer's copy of Y; the
+  bounded barrier publishes it. The gathered Y is at most a few hundred KB,
+  so the exchange costs about the barrier's latency.
 * :func:`row_range` -- softmax / RMSNorm rows split evenly; no exchange.
 * :func:`distributed_tune` -- the tuner's budgeted candidates dealt round-robin
   to one worker per GPU; outcomes are gathered on rank 0, which alone writes
@@ -30,7 +35,9 @@ from dataclasses import replace
 import torch
 import torch.distributed as dist
 
-from kernelo_b200.kernels.fused_linear import fused_linear_gelu
+from kernelo_b200.kernels.fused_linear import _EPILOGUES, fused_linear_gelu
+from kernelo_b200.kernels.gemv import MAX_ROWS as MAX_GEMV_ROWS
+from kernelo_b200.kernels.gemv import gemv
 
 
 def world_info(group=None) -> tuple[int, int]:
@@ -64,6 +71,8 @@ class ShardedFusedLinear:
     a rank-local slice of ``chunk`` rows.
     """
 
+    _plain = False  # ShardedGemv: x @ W^T with no bias and no activation
+
     def __init__(
         self,
         weight: torch.Tensor | None,
@@ -80,6 +89,8 @@ class ShardedFusedLinear:
     ) -> None:
         if gather not in ("auto", "fused", "nccl"):
             raise ValueError("gather must be 'auto', 'fused' or 'nccl'")
+        if not self._plain and approximate not in _EPILOGUES:
+            raise ValueError(f"approximate must be 'tanh', 'none' or 'erf', got {approximate!r}")
         self.group = group
         self.world, self.rank = world_info(group)
         self.approximate = approximate
@@ -90,14 +101,14 @@ class ShardedFusedLinear:
         self._host: dict = {}  # forward_host state per M: X staging, peer output, copy streams
         self._host_out: dict[int, torch.Tensor] = {}
         if shard_weight is not None:
-            if out_features is None or shard_bias is None:
+            if out_features is None or (shard_bias is None and not self._plain):
                 raise ValueError("shard_weight needs out_features and shard_bias")
             self.n = out_features
             self.chunk = shard_weight.shape[0]
             self.w = shard_weight
             self.b = shard_bias
         else:
-            if weight is None or bias is None:
+            if weight is None or (bias is None and not self._plain):
                 raise ValueError("pass weight and bias, or shard_weight and shard_bias")
             self.n = weight.shape[0]
             self.chunk = shard_chunk(self.n, self.world)
@@ -105,12 +116,18 @@ class ShardedFusedLinear:
             stop = min(self.n, start + self.chunk)
             k = weight.shape[1]
             w = torch.zeros(self.chunk, k, device=weight.device, dtype=weight.dtype)
-            b = torch.zeros(self.chunk, device=bias.device, dtype=bias.dtype)
+            b = None if bias is None else torch.zeros(self.chunk, device=bias.device, dtype=bias.dtype)
             if stop > start:
                 w[: stop - start].copy_(weight[start:stop])
-                b[: stop - start].copy_(bias[start:stop])
+                if b is not None:
+                    b[: stop - start].copy_(bias[start:stop])
             self.w, self.b = w, b
         self._gather_buf: torch.Tensor | None = None
+
+    def _epilogue(self) -> int:
+        from kernelo_b200.runtime import native
+
+        return native.KF_EPI_NONE if self._plain else _EPILOGUES[self.approximate]
 
     def local(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's [M, chunk] slice of the output."""
@@ -136,7 +153,6 @@ class ShardedFusedLinear:
     def fused_kernel(self, x: torch.Tensor) -> torch.Tensor:
         """Launch this rank's GEMM whose epilogue also writes every peer's Y;
         returns the buffer it wrote (valid on all ranks after :meth:`fused_publish`)."""
-        from kernelo_b200.kernels.fused_linear import _EPILOGUES
         from kernelo_b200.runtime import native
 
         m = x.shape[0]
@@ -145,8 +161,7 @@ class ShardedFusedLinear:
             sym = self._symm[m] = _PeerOutput(m, self.world * self.chunk, x.dtype, x.device, self.group)
         buf, peers = sym.next_buffer(self.rank * self.chunk)
         mine = buf[:, self.rank * self.chunk:(self.rank + 1) * self.chunk]
-        native.linear_bias_act_allgather(x, self.w.t(), mine, peers, bias=self.b,
-                                         epilogue=_EPILOGUES[self.approximate],
+        native.linear_bias_act_allgather(x, self.w.t(), mine, peers, bias=self.b, epilogue=self._epilogue(),
                                          launch=native.GemmLaunch.from_config(self.config))
         return buf
 
@@ -173,7 +188,6 @@ class ShardedFusedLinear:
         every chunk [a, a + world*q). Collective: every rank calls it with the
         same shapes. CUDA only (the all-gathering kernel).
         """
-        from kernelo_b200.kernels.fused_linear import _EPILOGUES
         from kernelo_b200.runtime import native
 
         if not self.w.is_cuda:
@@ -229,12 +243,11 @@ class ShardedFusedLinear:
                 peers = [sym.peer_ptrs[parity][j] + (a * buf.shape[1] + rank * self.chunk) * elt
                          for j in range(world) if j != rank]
                 native.linear_bias_act_allgather(x_dev[a:b], self.w.t(), buf[a:b, cols], peers, bias=self.b,
-                                                 epilogue=_EPILOGUES[self.approximate], launch=launch)
+                                                 epilogue=self._epilogue(), launch=launch)
                 sym.barrier(rank, world, self.barrier_timeout_us)
                 rows_out = buf[mine0:mine1, : self.n]
             else:
-                fused_linear_gelu(x_dev[a:b], self.w.t(), self.b, approximate=self.approximate,
-                                  config=self.config, out=buf[a:b])
+                self.local(x_dev[a:b], out=buf[a:b])
                 rows_out = buf[mine0:mine1, : self.n]
             done = torch.cuda.Event()
             done.record(compute)
@@ -268,6 +281,51 @@ class ShardedFusedLinear:
         buf = self.fused_kernel(x)
         self.fused_publish(x)
         return buf[:, : self.n]
+
+
+class ShardedGemv(ShardedFusedLinear):
+    """Decode GEMV ``x @ W^T`` (no bias, no activation) with W [N, K]
+    column-sharded over the process group.
+
+    Each rank reads only its ``chunk`` rows of the weight -- 1/world of the
+    HBM traffic that bounds the single-GPU GEMV -- through the 16-row tile
+    kernel for up to 32 rows of x (the tcgen05 GEMM above that, up to the
+    GEMV operator's 256 rows).
+    With ``gather="fused"`` (``"auto"`` on CUDA) that kernel's stores also
+    write every peer's copy of Y and the bounded barrier publishes it; at
+    M = 16, N = 11008 the whole gathered Y is 352 KB. ``gather="nccl"`` runs
+    :func:`kernelo_b200.kernels.gemv.gemv` locally and all-gathers the slices.
+    ``forward_host`` and ``close`` behave as for the fused linear.
+
+    The reference has no dedicated GEMV and no multi-GPU code: single-GPU
+    decode is its ``matmul`` at M in {1, 4, 16}
+    (kernelforge/kernels/matmul.py:132-155).
+    """
+
+    _plain = True
+
+    def __init__(
+        self,
+        weight: torch.Tensor | None,
+        *,
+        out_features: int | None = None,
+        shard_weight: torch.Tensor | None = None,
+        group=None,
+        config=None,
+        gather: str = "auto",
+        barrier_timeout_us: int = 2_000_000,
+    ) -> None:
+        super().__init__(weight, None, out_features=out_features, shard_weight=shard_weight, group=group,
+                         config=config, gather=gather, barrier_timeout_us=barrier_timeout_us)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if x.shape[0] > MAX_GEMV_ROWS:
+            raise ValueError(f"gemv takes at most {MAX_GEMV_ROWS} rows, got {x.shape[0]}; use matmul")
+        return super().__call__(x)
+
+    def local(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's [M, chunk] slice of ``x @ W^T``."""
+        return gemv(x, self.w, config=self.config, out=out)
 
 
 class _PeerOutput:

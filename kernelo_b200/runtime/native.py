@@ -384,9 +384,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, *, bias: torch.Tenso
 
 
 def linear_bias_act_allgather(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, peers: list[int], *,
-                              bias: torch.Tensor, epilogue: int, launch: GemmLaunch | None = None) -> None:
+                              bias: torch.Tensor | None, epilogue: int, launch: GemmLaunch | None = None) -> None:
     """``c = epilogue(a @ b + bias)``, every output tile also stored at the same
-    offsets from each address in ``peers`` (peer-mapped copies of c's buffer)."""
+    offsets from each address in ``peers`` (peer-mapped copies of c's buffer).
+    ``bias`` may be None with ``KF_EPI_NONE`` (the plain sharded GEMM/GEMV)."""
     lib = load()
     launch = launch or GemmLaunch()
     cfg = launch.struct()

@@ -1,8 +1,9 @@
 """Multi-process host logic on CPU: two gloo ranks.
 
 Covers the parts of ``kernelo_b200.distributed`` that need no GPU: the shard
-arithmetic, the row split, the sharded fused linear's gather/permute path
-(with the native kernel replaced by a CPU stand-in in the child processes),
+arithmetic, the row split, the sharded fused linear's and decode GEMV's
+gather/permute paths (with the native kernel replaced by a CPU stand-in in
+the child processes),
 and the tuner sweep dealt over ranks with rank 0 as the single writer --
 including a rank whose candidates all fail.
 """
@@ -79,6 +80,38 @@ def _sharded_linear_worker(rank: int, world: int, port: int, out_q) -> None:
         dist.destroy_process_group()
 
 
+def _sharded_gemv_worker(rank: int, world: int, port: int, out_q) -> None:
+    _init(rank, world, port)
+    try:
+        import kernelo_b200.distributed as mod
+
+        # CPU stand-in for the native GEMV: same signature, exact math.
+        def fake_gemv(x, w, *, config=None, out=None):
+            y = (x.double() @ w.double().t()).to(x.dtype)
+            if out is None:
+                return y
+            out.copy_(y)
+            return out
+
+        mod.gemv = fake_gemv
+        gen = torch.Generator().manual_seed(1)
+        w = torch.randn(50, 32, generator=gen)  # N=50: padded to 2 x 64
+        layer = mod.ShardedGemv(w, gather="nccl")
+        errs = []
+        for m in (1, 4, 16):
+            x = torch.randn(m, 32, generator=gen)
+            y = layer(x)
+            errs.append((tuple(y.shape), float((y - x @ w.t()).abs().max())))
+        refused = False
+        try:
+            layer(torch.zeros(257, 32))
+        except ValueError:
+            refused = True
+        out_q.put((rank, layer.b is None, errs, refused))
+    finally:
+        dist.destroy_process_group()
+
+
 def _tune_worker(rank: int, world: int, port: int, tmpdir: str, out_q) -> None:
     _init(rank, world, port)
     try:
@@ -144,6 +177,17 @@ def test_sharded_fused_linear_gathers_columns_on_two_ranks():
     for rank, shape, err in _run(_sharded_linear_worker):
         assert shape == (6, 50)
         assert err < 1e-5
+
+
+def test_sharded_gemv_gathers_columns_on_two_ranks():
+    """The decode GEMV sharded by weight rows: no bias anywhere, each rank's
+    slice gathered into [M, N] (N padded to the shard grid, padding dropped),
+    and more rows than the GEMV operator takes refused up front."""
+    for rank, no_bias, errs, refused in _run(_sharded_gemv_worker):
+        assert no_bias and refused
+        for (shape, err), m in zip(errs, (1, 4, 16)):
+            assert shape == (m, 50)
+            assert err < 1e-5
 
 
 def test_resumed_distributed_sweep_measures_nothing_twice(tmp_path):

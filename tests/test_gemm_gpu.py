@@ -440,6 +440,36 @@ def test_gemv_tile_rows_refusals(device):
         gemv(x[:, :4096], w[:, :4096], config=tile_cfg(5, 3))  # no such compiled shape
 
 
+@pytest.mark.parametrize("m", [1, 4, 16, 32, 300])
+@pytest.mark.parametrize("epilogue", ["none", "erf"])
+def test_allgather_peer_stores_on_one_gpu(m, epilogue, device):
+    """The all-gathering entry point with "peer" copies that are other buffers
+    on this GPU (a peer address is any device pointer): every copy holds the
+    block bit for bit, and it equals the plain call's output. M <= 32 runs the
+    tile GEMV's peer stores (the decode-shape gather), M = 300 the tcgen05
+    epilogue's TMA stores. Y is [M, 2 * 1000] per copy; this call owns columns
+    [1000, 2000) of each."""
+    gen = torch.Generator().manual_seed(70 + m)
+    x = torch.randn(m, 1024, generator=gen).half().to(device)
+    w_nk = (torch.randn(1000, 1024, generator=gen) * 0.03).half().to(device)
+    b = torch.randn(1000, generator=gen).half().to(device) if epilogue == "erf" else None
+    code = native.KF_EPI_BIAS_GELU_ERF if epilogue == "erf" else native.KF_EPI_NONE
+    copies = [torch.full((m, 2000), float("nan"), device=device, dtype=torch.float16) for _ in range(3)]
+    peers = [c[:, 1000:].data_ptr() for c in copies[1:]]
+    native.linear_bias_act_allgather(x, w_nk.t(), copies[0][:, 1000:], peers, bias=b, epilogue=code)
+    plain = torch.empty(m, 1000, device=device, dtype=torch.float16)
+    native.gemm(x, w_nk.t(), plain, bias=b, epilogue=code, launch=native.GemmLaunch())
+    torch.cuda.synchronize()
+    for i, c in enumerate(copies):
+        assert torch.equal(c[:, 1000:], plain), f"copy {i} differs from the plain call at M={m}"
+        assert torch.isnan(c[:, :1000]).all(), f"copy {i}: columns outside the block were written"
+    expected = ref.matmul_ref(host(x), host(w_nk.t()))
+    if b is not None:
+        expected = ref.linear_gelu_ref(host(x), host(w_nk.t()), host(b), "none")
+    gate(expected, plain, torch.float16, context=f"M={m} {epilogue}")
+    assert native.device_status(device.index or 0) == 0
+
+
 # ------------------------------------------------------------------ host-buffer fused linear
 @pytest.mark.parametrize("m", [1, 300, 1024, 1500])
 def test_fused_linear_host_matches_the_oracle(m, device):

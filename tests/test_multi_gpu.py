@@ -1,9 +1,10 @@
 """The column-sharded fused linear on two B200s: the all-gather done by the
 GEMM epilogue (stores into peers' IPC-mapped copies of Y) against the
 NCCL gather and the oracle, the host-to-host entry point with its PCIe
-traffic split over the ranks, and the bounded cross-GPU barrier timing out
-cleanly when a peer never signals. Spawns two ranks; skipped with fewer
-than two GPUs."""
+traffic split over the ranks, the bounded cross-GPU barrier timing out
+cleanly when a peer never signals, and the decode shapes (the sharded GEMV
+and the fused linear at M <= 32), whose gather is the tile GEMV's own
+stores. Spawns two ranks; skipped with fewer than two GPUs."""
 
 from __future__ import annotations
 
@@ -116,8 +117,40 @@ def _worker(rank: int, world: int, port: int, results) -> None:
         torch.cuda.synchronize()
         f2.close()
         status2 = native.device_status(rank)
+        # decode shapes: the 16-row tile kernel does the gather with its own
+        # stores -- the plain sharded GEMV (N = 11008 split as 2 x 5504) and the
+        # fused linear at M = 4 -- against the NCCL gather (bit-equal: the same
+        # kernel computes the local slice) and the fp64 oracle
+        from kernelo_b200.distributed import ShardedGemv
+        from oracle import cpu_reference as ref
+
+        g3 = torch.Generator().manual_seed(7)
+        w3 = (torch.randn(11008, 1024, generator=g3) * 1024 ** -0.5).half().to(dev)
+        b3 = (torch.randn(11008, generator=g3) * 0.1).half().to(dev)
+        decode = []
+        layers = [(ShardedGemv(w3, gather="fused"), ShardedGemv(w3, gather="nccl"), None),
+                  (ShardedFusedLinear(w3, b3, approximate="none", gather="fused"),
+                   ShardedFusedLinear(w3, b3, approximate="none", gather="nccl"), b3)]
+        for f3, n3, bias3 in layers:
+            for m3 in (1, 4, 16, 32):
+                for _ in range(2):  # both peer buffers
+                    x3 = torch.randn(m3, 1024, generator=g3).half().to(dev)
+                    y3 = f3(x3).clone()
+                    same = bool(torch.equal(y3, n3(x3)))
+                    xs3 = x3.double().cpu().numpy()
+                    ws3 = w3.t().double().cpu().numpy()
+                    if bias3 is None:
+                        exp3 = torch.from_numpy(ref.matmul_ref(xs3, ws3))
+                    else:
+                        exp3 = torch.from_numpy(ref.linear_gelu_ref(xs3, ws3, bias3.double().cpu().numpy(), "none"))
+                    ok = verify(exp3, y3.double().cpu(), dtype=torch.float16).passed
+                    decode.append((m3, bias3 is not None, same, ok))
+            torch.cuda.synchronize()
+            f3.close()
+        status3 = native.device_status(rank)
         results[rank] = {"equal": outs, "host": host_ok, "status": status, "oracle": err,
-                         "timed_out": timed_out, "second": second, "status2": status2}
+                         "timed_out": timed_out, "second": second, "status2": status2,
+                         "decode": decode, "status3": status3}
     finally:
         dist.destroy_process_group()
 
@@ -136,5 +169,8 @@ def test_fused_all_gather_on_two_gpus():
         assert r["status"] == 0, f"rank {rank}: device status {r['status']:#x}"
         assert all(r["second"]), f"rank {rank}: fp16/tanh ragged shapes differ {r['second']}"
         assert r["status2"] == 0, f"rank {rank}: device status {r['status2']:#x} after the second shape"
+        bad = [d for d in r["decode"] if not (d[2] and d[3])]
+        assert not bad, f"rank {rank}: decode-shape gather (M, fused linear, equal to NCCL, gate) {bad}"
+        assert r["status3"] == 0, f"rank {rank}: device status {r['status3']:#x} after the decode shapes"
     assert results[0]["oracle"], "rank 0: the gathered output fails the bf16 gate"
     assert results[0]["timed_out"], "the unanswered barrier did not record a timeout"
