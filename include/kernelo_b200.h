@@ -19,7 +19,7 @@
  *                       and csrc/rmsnorm.cu:19-57        (the hand-written CUDA baseline)
  *   kf_query_gemm_config  tuning/search.py:299-394      shared-memory / feasibility model
  *   kf_gemv_noalloc     as kf_gemv, for callers that cannot hand over a workspace
- *   kf_linear_bias_act_allgather, kf_peer_barrier, kf_ipc_handle / _open / _close
+ *   kf_linear_bias_act_allgather, kf_peer_barrier(_counted), kf_ipc_handle / _open / _close
  *                       the column-sharded fused linear over several GPUs (the
  *                       reference is single-GPU: no counterpart)
  *
@@ -257,6 +257,16 @@ KF_API int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_
 KF_API int32_t kf_peer_barrier(uint32_t* local_signals, uint32_t* const* peer_signals,
                                int32_t rank, int32_t world, uint32_t epoch, int32_t timeout_us,
                                void* stream);
+
+/* kf_peer_barrier with the epoch kept on the device: epoch_counter is a
+ * uint32 in this rank's memory (zero-initialised, used by nothing else); each
+ * barrier takes *epoch_counter + 1 as its epoch and stores it back. Every rank
+ * runs the same sequence of barriers, so the counters agree, and the call can
+ * be captured once in a CUDA graph and replayed: each replay advances the
+ * epoch. Do not mix it with kf_peer_barrier on the same signal arrays. */
+KF_API int32_t kf_peer_barrier_counted(uint32_t* local_signals, uint32_t* const* peer_signals,
+                                       int32_t rank, int32_t world, uint32_t* epoch_counter,
+                                       int32_t timeout_us, void* stream);
 
 /* Peer mapping for the all-gather buffers, by CUDA IPC (no multicast object).
  * kf_ipc_handle: the IPC handle (KF_IPC_HANDLE_BYTES bytes) of the allocation

@@ -375,6 +375,19 @@ int32_t kf_peer_barrier(uint32_t* local_signals, uint32_t* const* peer_signals, 
                              static_cast<cudaStream_t>(stream));
 }
 
+int32_t kf_peer_barrier_counted(uint32_t* local_signals, uint32_t* const* peer_signals, int32_t rank,
+                                int32_t world, uint32_t* epoch_counter, int32_t timeout_us, void* stream) {
+  if (epoch_counter == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null epoch counter");
+  int device = 0;
+  int rc = current_device(&device);
+  if (rc != KF_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = device_info(device, &dev);
+  if (rc != KF_OK) return rc;
+  return launch_peer_barrier(local_signals, peer_signals, rank, world, 0, timeout_us, *dev,
+                             static_cast<cudaStream_t>(stream), epoch_counter);
+}
+
 int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w,
                 int64_t sw_n, int64_t sw_k, void* y, int64_t sy_m, int64_t sy_n, int64_t M,
                 int64_t N, int64_t K, const kf_gemm_config* cfg, void* workspace,

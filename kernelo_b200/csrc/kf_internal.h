@@ -99,8 +99,10 @@ int launch_gemv_rows(int dtype, const void* x, int64_t sx_m, int64_t sx_k, const
                      cudaStream_t stream);
 
 // Cross-GPU barrier over peer-mapped signal words (peer_sync.cu).
+// counter != nullptr: the epoch is *counter + 1, advanced on the device (epoch unused).
 int launch_peer_barrier(uint32_t* local, uint32_t* const* peers, int rank, int world,
-                        uint32_t epoch, int timeout_us, const DeviceInfo& dev, cudaStream_t stream);
+                        uint32_t epoch, int timeout_us, const DeviceInfo& dev, cudaStream_t stream,
+                        uint32_t* counter = nullptr);
 
 // Row kernels.
 struct RowsArgs {

@@ -12,6 +12,11 @@
 // %globaltimer: on timeout the kernel records
 // KF_ERR_TIMEOUT | SITE_PEER_BARRIER << 8 in the device status word and
 // returns, leaving the context usable.
+//
+// The counted form keeps the epoch in a device word of this rank: the kernel
+// takes *counter + 1 and stores it back, so a captured CUDA graph that holds
+// the barrier advances the epoch on every replay (a host-supplied epoch would
+// be frozen into the graph and let later replays pass unsynchronised).
 #include <cuda.h>
 
 #include <cstring>
@@ -29,6 +34,7 @@ struct PeerBarrierParams {
   int peer_rank[KF_MAX_PEERS];        // their ranks
   int rank, n_peers;
   uint32_t epoch;
+  uint32_t* counter;  // counted form: the epoch is *counter + 1 (this rank's memory)
   unsigned long long timeout_ns;
   int* status;
 };
@@ -48,16 +54,24 @@ __device__ __forceinline__ bool reached(uint32_t v, uint32_t epoch) {
 
 __global__ void peer_barrier_kernel(const PeerBarrierParams p) {
   const int t = threadIdx.x;
+  uint32_t epoch = p.epoch;
+  if (p.counter != nullptr) {
+    // Every lane reads the previous epoch before lane 0 advances it; the
+    // previous barrier on this stream wrote it (kernel boundary).
+    epoch = *p.counter + 1u;
+    __syncwarp();
+    if (t == 0) *p.counter = epoch;
+  }
   if (t >= p.n_peers) return;
   __threadfence_system();
-  st_release_sys(p.peers[t] + p.rank, p.epoch);
+  st_release_sys(p.peers[t] + p.rank, epoch);
   // A peer that saw this rank's signal may run ahead and write epoch + 1
   // before this poll reads epoch, so "reached" is a wrap-safe v >= epoch.
   const uint32_t* mine = p.local + p.peer_rank[t];
-  if (reached(ld_acquire_sys(mine), p.epoch)) return;
+  if (reached(ld_acquire_sys(mine), epoch)) return;
   const unsigned long long start = global_timer_ns();
   for (uint32_t spin = 1;; ++spin) {
-    if (reached(ld_acquire_sys(mine), p.epoch)) return;
+    if (reached(ld_acquire_sys(mine), epoch)) return;
     if ((spin & 63u) == 0 && global_timer_ns() - start > p.timeout_ns) {
       record_status(p.status, KF_ERR_TIMEOUT, SITE_PEER_BARRIER);
       return;
@@ -68,13 +82,15 @@ __global__ void peer_barrier_kernel(const PeerBarrierParams p) {
 }  // namespace
 
 int launch_peer_barrier(uint32_t* local, uint32_t* const* peers, int rank, int world,
-                        uint32_t epoch, int timeout_us, const DeviceInfo& dev, cudaStream_t stream) {
+                        uint32_t epoch, int timeout_us, const DeviceInfo& dev, cudaStream_t stream,
+                        uint32_t* counter) {
   if (world < 1 || world > KF_MAX_PEERS + 1)
     return set_error(KF_ERR_INVALID_ARGUMENT, "world must be in [1, 8]");
   if (rank < 0 || rank >= world) return set_error(KF_ERR_INVALID_ARGUMENT, "rank out of range");
   if (timeout_us <= 0 || timeout_us > 60000000)
     return set_error(KF_ERR_INVALID_ARGUMENT, "timeout_us must be in (0, 6e7]");
-  if (epoch == 0) return set_error(KF_ERR_INVALID_ARGUMENT, "epochs start at 1 (0 is the initial value)");
+  if (counter == nullptr && epoch == 0)
+    return set_error(KF_ERR_INVALID_ARGUMENT, "epochs start at 1 (0 is the initial value)");
   if (world == 1) return KF_OK;
   if (local == nullptr || peers == nullptr)
     return set_error(KF_ERR_INVALID_ARGUMENT, "null signal pointer");
@@ -90,6 +106,7 @@ int launch_peer_barrier(uint32_t* local, uint32_t* const* peers, int rank, int w
     ++i;
   }
   p.epoch = epoch;
+  p.counter = counter;
   p.timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
   p.status = dev.status;
   peer_barrier_kernel<<<1, 32, 0, stream>>>(p);

@@ -347,6 +347,8 @@ class _PeerOutput:
         self.rank = dist.get_rank(group)
         self.bufs = [torch.empty((m, n_total), dtype=dtype, device=device) for _ in range(2)]
         self.signals = torch.zeros((self.world,), dtype=torch.int32, device=device)
+        # this rank's barrier epoch, advanced on the device by each barrier
+        self.counter = torch.zeros((1,), dtype=torch.int32, device=device)
         torch.cuda.synchronize(device)
         mine = [native.ipc_handle(t) for t in (*self.bufs, self.signals)]
         everyone: list = [None] * self.world
@@ -367,7 +369,6 @@ class _PeerOutput:
                 self.peer_ptrs[i][j] = addr
         dist.barrier(group=group)  # every rank's signal array is zero before any peer signals
         self.parity = 0
-        self.epoch = 0
 
     def next_buffer(self, col_offset: int) -> tuple[torch.Tensor, list[int]]:
         """The buffer of this call and the peers' addresses of element (0, col_offset)."""
@@ -381,12 +382,13 @@ class _PeerOutput:
         return self.signals.data_ptr(), [self.peer_ptrs[2][j] for j in range(self.world) if j != self.rank]
 
     def barrier(self, rank: int, world: int, timeout_us: int) -> None:
+        """Enqueue the bounded barrier; its epoch lives on the device, so a
+        CUDA graph that captured it stays correct on every replay."""
         from kernelo_b200.runtime import native
 
-        self.epoch += 1
         local, peers = self.signal_ptrs()
-        native.peer_barrier(local, peers, rank, world, self.epoch, timeout_us=timeout_us,
-                            device=self.signals.device)
+        native.peer_barrier_counted(local, peers, rank, world, self.counter.data_ptr(), timeout_us=timeout_us,
+                                    device=self.signals.device)
 
     def close(self) -> None:
         """Unmap the peers' buffers (all ranks should be done with them)."""

@@ -66,6 +66,7 @@ EXPORTED_SYMBOLS = (
     "kf_gemv_noalloc",
     "kf_linear_bias_act_allgather",
     "kf_peer_barrier",
+    "kf_peer_barrier_counted",
     "kf_ipc_handle",
     "kf_ipc_open",
     "kf_ipc_close",
@@ -163,6 +164,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                             _i64, _i64, _i64, _i32, ctypes.POINTER(_vp), _i32, _GP, _vp, _i64,
                                             _vp]),
     "kf_peer_barrier": (_i32, [_vp, ctypes.POINTER(_vp), _i32, _i32, ctypes.c_uint32, _i32, _vp]),
+    "kf_peer_barrier_counted": (_i32, [_vp, ctypes.POINTER(_vp), _i32, _i32, _vp, _i32, _vp]),
     "kf_ipc_handle": (_i32, [_vp, _vp, ctypes.POINTER(_i64)]),
     "kf_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
     "kf_ipc_close": (_i32, [_vp]),
@@ -418,6 +420,20 @@ def peer_barrier(local_signals: int, peer_signals: list[int], rank: int, world: 
     status = lib.kf_peer_barrier(ctypes.c_void_p(int(local_signals)), arr, rank, world, epoch, timeout_us,
                                  current_stream_handle(dev))
     check(status, "kf_peer_barrier")
+
+
+def peer_barrier_counted(local_signals: int, peer_signals: list[int], rank: int, world: int, epoch_counter: int,
+                         *, timeout_us: int = 2_000_000, device: torch.device | None = None) -> None:
+    """Enqueue the bounded cross-GPU barrier whose epoch is a device counter
+    (kf_peer_barrier_counted): capturable in a CUDA graph, every replay
+    advances the epoch."""
+    lib = load()
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    arr = (_vp * max(1, len(peer_signals)))(*[ctypes.c_void_p(int(p)) for p in peer_signals])
+    status = lib.kf_peer_barrier_counted(ctypes.c_void_p(int(local_signals)), arr, rank, world,
+                                         ctypes.c_void_p(int(epoch_counter)), timeout_us,
+                                         current_stream_handle(dev))
+    check(status, "kf_peer_barrier_counted")
 
 
 IPC_HANDLE_BYTES = 64

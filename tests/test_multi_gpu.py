@@ -4,7 +4,7 @@ NCCL gather and the oracle, the host-to-host entry point with its PCIe
 traffic split over the ranks, the bounded cross-GPU barrier timing out
 cleanly when a peer never signals, and the decode shapes (the sharded GEMV
 and the fused linear at M <= 32), whose gather is the tile GEMV's own
-stores. Spawns two ranks; skipped with fewer than two GPUs."""
+stores, including a decode step captured in a CUDA graph and replayed. Spawns two ranks; skipped with fewer than two GPUs."""
 
 from __future__ import annotations
 
@@ -147,10 +147,35 @@ def _worker(rank: int, world: int, port: int, results) -> None:
                     decode.append((m3, bias3 is not None, same, ok))
             torch.cuda.synchronize()
             f3.close()
+        # the sharded decode step captured once in a CUDA graph (two calls: both
+        # peer buffers) and replayed on new inputs: the barrier's epoch lives on
+        # the device, so every replay synchronises the ranks again
+        gl, gn = ShardedGemv(w3, gather="fused"), ShardedGemv(w3, gather="nccl")
+        xg = torch.randn(16, 1024, generator=g3).half().to(dev)
+        gl(xg)
+        gl(xg)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ya = gl(xg)
+            yb = gl(xg * 2)
+        replayed = []
+        for _ in range(3):
+            torch.cuda.synchronize()
+            dist.barrier()  # both ranks have read the previous replay's outputs
+            torch.cuda.synchronize()
+            xg.copy_(torch.randn(16, 1024, generator=g3).half())
+            graph.replay()
+            got_a, got_b = ya.clone(), yb.clone()
+            replayed.append(bool(torch.equal(got_a, gn(xg))) and bool(torch.equal(got_b, gn(xg * 2))))
+        torch.cuda.synchronize()
+        dist.barrier()
+        del graph
+        gl.close()
         status3 = native.device_status(rank)
         results[rank] = {"equal": outs, "host": host_ok, "status": status, "oracle": err,
                          "timed_out": timed_out, "second": second, "status2": status2,
-                         "decode": decode, "status3": status3}
+                         "decode": decode, "status3": status3, "replayed": replayed}
     finally:
         dist.destroy_process_group()
 
@@ -172,5 +197,6 @@ def test_fused_all_gather_on_two_gpus():
         bad = [d for d in r["decode"] if not (d[2] and d[3])]
         assert not bad, f"rank {rank}: decode-shape gather (M, fused linear, equal to NCCL, gate) {bad}"
         assert r["status3"] == 0, f"rank {rank}: device status {r['status3']:#x} after the decode shapes"
+        assert all(r["replayed"]), f"rank {rank}: graph replays of the sharded decode step {r['replayed']}"
     assert results[0]["oracle"], "rank 0: the gathered output fails the bf16 gate"
     assert results[0]["timed_out"], "the unanswered barrier did not record a timeout"
