@@ -39,6 +39,49 @@ def test_a_recorded_timeout_surfaces_as_an_exception(device):
         native.raise_on_device_status(device.index)
 
 
+def test_counted_peer_barrier_advances_its_device_epoch(device):
+    """The graph-replayable barrier on one GPU, as rank 0 of 2 with a "peer"
+    signal array that is another local buffer. The peer's arrival is planted
+    in advance (this rank's slot for rank 1 already holds a later epoch), so
+    no launch waits on another: each barrier takes counter + 1 as its epoch,
+    stores it back and signals the peer with it, eagerly and on every replay
+    of a captured graph; a barrier whose peer never reaches the epoch gives
+    up after its limit with the barrier's site in the status word."""
+    local = torch.zeros(2, dtype=torch.int32, device=device)
+    peer = torch.zeros(2, dtype=torch.int32, device=device)
+    counter = torch.zeros(1, dtype=torch.int32, device=device)
+    local[1] = 100  # rank 1 "arrived" up to epoch 100
+
+    def barrier():
+        native.peer_barrier_counted(local.data_ptr(), [peer.data_ptr()], 0, 2, counter.data_ptr(),
+                                    timeout_us=1_000_000, device=device)
+
+    barrier()
+    barrier()
+    torch.cuda.synchronize(device)
+    assert counter.item() == 2 and peer.tolist() == [2, 0]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        barrier()
+        barrier()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    del graph
+    assert counter.item() == 8 and peer.tolist() == [8, 0]
+    assert native.device_status(device.index) == 0
+    # rank 1 stopped at epoch 100: the barrier of epoch 101 times out (20 ms)
+    counter.fill_(100)
+    native.peer_barrier_counted(local.data_ptr(), [peer.data_ptr()], 0, 2, counter.data_ptr(),
+                                timeout_us=20_000, device=device)
+    torch.cuda.synchronize(device)
+    value = native.device_status(device.index)
+    assert value & 0xFF == native.KF_ERR_TIMEOUT and value >> 8 == 7
+    assert counter.item() == 101 and peer[0].item() == 101
+    with pytest.raises(ValueError, match="null epoch counter"):
+        native.peer_barrier_counted(local.data_ptr(), [peer.data_ptr()], 0, 2, 0, device=device)
+
+
 def test_native_library_is_the_in_tree_build(device):
     import os
 
