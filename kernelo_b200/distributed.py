@@ -105,6 +105,8 @@ class ShardedFusedLinear:
                 raise ValueError("shard_weight needs out_features and shard_bias")
             self.n = out_features
             self.chunk = shard_weight.shape[0]
+            if self.world * self.chunk < self.n:
+                raise ValueError(f"{self.world} shards of {self.chunk} rows cannot hold {self.n} output features")
             self.w = shard_weight
             self.b = shard_bias
         else:

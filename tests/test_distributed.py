@@ -1,11 +1,10 @@
 """Multi-process host logic on CPU: two gloo ranks.
 
 Covers the parts of ``kernelo_b200.distributed`` that need no GPU: the shard
-arithmetic, the row split, the sharded fused linear's and decode GEMV's
-gather/permute paths (with the native kernel replaced by a CPU stand-in in
-the child processes),
-and the tuner sweep dealt over ranks with rank 0 as the single writer --
-including a rank whose candidates all fail.
+arithmetic and its validation, the row split, the sharded fused linear's and
+decode GEMV's gather/permute paths (with the native kernel replaced by a CPU
+stand-in in the child processes), and the tuner sweep dealt over ranks with
+rank 0 as the single writer -- including a rank whose candidates all fail.
 """
 
 from __future__ import annotations
@@ -38,6 +37,13 @@ def test_forward_host_refuses_a_cpu_layer():
     layer = kd.ShardedFusedLinear(w, torch.zeros(32))
     with pytest.raises(ValueError, match="CUDA device"):
         layer.forward_host(torch.zeros(4, 16), torch.zeros(4, 32))
+
+
+def test_shards_too_small_for_the_output_are_refused():
+    with pytest.raises(ValueError, match="cannot hold"):
+        kd.ShardedGemv(None, out_features=100, shard_weight=torch.zeros(64, 16))
+    layer = kd.ShardedGemv(None, out_features=64, shard_weight=torch.zeros(64, 16))
+    assert layer.b is None and layer.chunk == 64
 
 
 def _free_port() -> int:
