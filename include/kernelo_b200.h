@@ -171,8 +171,13 @@ KF_API int32_t kf_linear_bias_act(int32_t dtype, const void* x, int64_t sx_m, in
 
 /* Decode-shape GEMM Y[M,N] = X[M,K] . W^T for small M (1..256) with W stored
  * [N,K] (sw_n = row stride, sw_k = 1) or [K,N] (sw_k = row stride, sw_n = 1).
- * Memory-bound: streams W once with TMA, splits K across all SMs (stream-K);
- * needs kf_gemv_workspace_bytes() of workspace. */
+ * Memory-bound. The default config picks by layout: fp16/bf16 with
+ * K-contiguous W and x rows and M <= 32 run the 16-row tile kernel (W streamed
+ * by warps into mma.sync fragments, no workspace); fp32 at M <= 2 the
+ * warp-per-row kernel (no workspace); the rest the tcgen05 GEMV with A and B
+ * swapped and K split over all SMs (stream-K), which uses
+ * kf_gemv_workspace_bytes() of workspace when given one and whole tiles
+ * otherwise. Operands TMA cannot describe take the CUDA-core GEMM. */
 KF_API int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w,
                 int64_t sw_n, int64_t sw_k, void* y, int64_t sy_m, int64_t sy_n, int64_t M,
                 int64_t N, int64_t K, const kf_gemm_config* cfg, void* workspace,
@@ -183,14 +188,17 @@ KF_API int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
  * application that owns all device memory and provides neither an allocator
  * nor a workspace, or a latency-critical path that cannot pay for
  * cudaMalloc/cudaFree (which may synchronise the device). Same arguments as
- * kf_gemv minus the config and workspace: the stream-K scratch is a
- * file-scope device array of KF_NOALLOC_SCRATCH_BYTES inside the library,
- * present on every GPU that loads it until the process exits. Takes
- * M <= KF_NOALLOC_MAX_ROWS and rejects larger M with KF_ERR_WORKSPACE. Calls
- * no allocating routine. The first call on a device looks the array up
- * (cudaGetSymbolAddress) and should come before any stream capture. Each call
- * clears the array's counters on `stream`; all calls on a device share the
- * array, so calls that overlap on the GPU race. */
+ * kf_gemv minus the config and workspace, and the same kernel choice as
+ * kf_gemv's default config: the stream-K scratch is a file-scope device array
+ * of KF_NOALLOC_SCRATCH_BYTES inside the library, present on every GPU that
+ * loads it until the process exits. Takes M <= KF_NOALLOC_MAX_ROWS and
+ * rejects larger M, and any call whose stream-K scratch would not fit the
+ * array (x with unit stride along M, for example), with KF_ERR_WORKSPACE
+ * before launching anything. Calls no allocating routine. The first call on a
+ * device looks the array up (cudaGetSymbolAddress) and should come before any
+ * stream capture. Calls on the tile kernel never touch the array; the others
+ * clear its counters on `stream`. All calls on a device share the array, so
+ * such calls that overlap on the GPU race. */
 #define KF_NOALLOC_SCRATCH_BYTES (4 * 1024 * 1024)
 #define KF_NOALLOC_MAX_ROWS 16
 KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,

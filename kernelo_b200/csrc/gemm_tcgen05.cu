@@ -62,9 +62,8 @@ constexpr int NUM_THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
 constexpr int MAX_STAGES = 16;
 constexpr int MIN_SMEM_PER_CTA = 120 * 1024;  // > half an SM: one CTA per SM
 constexpr uint64_t DRAIN_LIMIT_NS = 100000000ull;
-// Stream-K workspace layout: [tile arrival counters | 2 partial tiles per CTA].
-constexpr int64_t SK_MAX_TILES = 16384;
-constexpr int64_t SK_COUNTER_BYTES = SK_MAX_TILES * 4;
+// Stream-K workspace layout: [tile arrival counters | 2 partial tiles per CTA];
+// SK_MAX_TILES and SK_COUNTER_BYTES live in kf_internal.h.
 
 struct TcParams {
   int M, N, K;  // as the kernel sees them (after an optional A/B swap)

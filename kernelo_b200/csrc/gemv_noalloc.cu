@@ -19,13 +19,18 @@
 //    array's device address is looked up with cudaGetSymbolAddress once per
 //    device, by the first call made while that device is current; make that
 //    first call before any stream capture begins.
-//  - fp16/bf16 operands with K-contiguous rows (and K % 8 == 0) go to the
-//    16-row tile GEMV, which uses no scratch; only the others touch the array.
-//  - All calls on a device share the one array. Each call clears the arrival
-//    counters (cudaMemsetAsync on the caller's stream) before its kernel, and
-//    the partial tiles are always written before they are read. Calls that
-//    overlap on the GPU (different streams, no ordering between them) race on
-//    the array and must not be issued.
+//  - It accepts what kf_gemv accepts at M <= 16 and picks the same kernels.
+//    fp16/bf16 operands with K-contiguous rows (and K % 8 == 0) go to the
+//    16-row tile GEMV, which uses no scratch and never touches the array.
+//    The rest may take the stream-K tcgen05 GEMV (the only kernel here that
+//    needs scratch) or a scratch-free CUDA-core kernel; a call whose
+//    stream-K scratch would exceed the array is rejected with
+//    KF_ERR_WORKSPACE before anything is launched.
+//  - All calls on a device share the one array. A call that may use it
+//    clears the arrival counters (cudaMemsetAsync on the caller's stream)
+//    before its kernel, and the partial tiles are always written before they
+//    are read. Such calls that overlap on the GPU (different streams, no
+//    ordering between them) race on the array and must not be issued.
 #include <mutex>
 #include <string>
 
@@ -39,7 +44,8 @@ namespace {
 static __device__ __align__(256) unsigned char kf_noalloc_scratch[KF_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-constexpr size_t kCounterBytes = 64 * 1024;  // stream-K counter region of a workspace
+static_assert(kf::SK_COUNTER_BYTES <= KF_NOALLOC_SCRATCH_BYTES,
+              "the stream-K counters must fit in the no-alloc scratch");
 
 std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
@@ -76,15 +82,15 @@ extern "C" KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t 
   if (rc != KF_OK) return rc;
   if (device >= kMaxDevices) return kf::set_error(KF_ERR_INVALID_ARGUMENT, "device index out of range");
   // K-contiguous 16-bit operands take the 16-row tile kernel, which needs no
-  // scratch at all (and so cannot race with an overlapping call); the rest
-  // take the stream-K tcgen05 GEMV, the kernel whose scratch this entry point
-  // holds.
+  // scratch at all (and so cannot race with an overlapping call). The rest go
+  // through kf_gemv's own choice (the default config): the stream-K tcgen05
+  // GEMV, the one kernel whose scratch this entry point holds, or a
+  // scratch-free CUDA-core kernel for operands TMA cannot describe.
   if (x != nullptr && w != nullptr && y != nullptr &&
       kf::gemv_mma_supported(dtype, x, sx_m, sx_k, w, sw_n, sw_k, M, N, K, nullptr))
     return kf::launch_gemv_mma(dtype, x, sx_m, w, sw_n, y, sy_m, sy_n, M, N, K, kf_gemm_config{},
                                static_cast<cudaStream_t>(stream));
-  kf_gemm_config cfg{};
-  cfg.kernel = KF_GEMM_TCGEN05;
+  kf_gemm_config cfg{};  // KF_GEMM_AUTO, as kf_gemv(..., cfg = NULL)
   const int64_t need = kf_gemv_workspace_bytes(device, dtype, sx_m, sx_k, sw_n, sw_k, M, N, K, &cfg);
   if (need < 0) return static_cast<int32_t>(-need);
   if (need > KF_NOALLOC_SCRATCH_BYTES)
@@ -98,7 +104,7 @@ extern "C" KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t 
   if (need > 0) {
     // The arrival counters must start at zero; the array keeps whatever the
     // previous call (or an aborted one) left.
-    const cudaError_t err = cudaMemsetAsync(scratch, 0, kCounterBytes, s);
+    const cudaError_t err = cudaMemsetAsync(scratch, 0, kf::SK_COUNTER_BYTES, s);
     if (err != cudaSuccess) return kf::cuda_error(err, "cudaMemsetAsync(no-alloc counters)");
   }
   return kf_gemv(dtype, x, sx_m, sx_k, w, sw_n, sw_k, y, sy_m, sy_n, M, N, K, &cfg, scratch,

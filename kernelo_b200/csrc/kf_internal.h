@@ -46,6 +46,11 @@ struct GemmArgs {
   int n_peers = 0;
 };
 
+// Stream-K workspace layout (tcgen05 GEMM): one int32 arrival counter per
+// output tile first, at a fixed offset, then the fp32 partial tiles.
+constexpr int64_t SK_MAX_TILES = 16384;
+constexpr int64_t SK_COUNTER_BYTES = SK_MAX_TILES * 4;
+
 // Fills zero fields of `cfg` with the library default for this problem.
 kf_gemm_config resolve_gemm_config(const GemmArgs& args, const kf_gemm_config* user,
                                    int sm_count);

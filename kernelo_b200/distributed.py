@@ -160,7 +160,8 @@ class ShardedFusedLinear:
         m = x.shape[0]
         sym = self._symm.get(m)
         if sym is None:
-            sym = self._symm[m] = _PeerOutput(m, self.world * self.chunk, x.dtype, x.device, self.group)
+            sym = self._symm[m] = _PeerOutput(m, self.world * self.chunk, x.dtype, x.device, self.group,
+                                              chunk=self.chunk)
         buf, peers = sym.next_buffer(self.rank * self.chunk)
         mine = buf[:, self.rank * self.chunk:(self.rank + 1) * self.chunk]
         native.linear_bias_act_allgather(x, self.w.t(), mine, peers, bias=self.b, epilogue=self._epilogue(),
@@ -210,7 +211,8 @@ class ShardedFusedLinear:
         state = self._host.get(key)
         if state is None:
             x_dev = torch.empty(step * chunks, k, device=dev, dtype=x_host.dtype)
-            sym = _PeerOutput(m, world * self.chunk, x_host.dtype, dev, self.group) if world > 1 else None
+            sym = (_PeerOutput(m, world * self.chunk, x_host.dtype, dev, self.group, chunk=self.chunk)
+                   if world > 1 else None)
             state = self._host[key] = (x_dev, sym, torch.cuda.Stream(dev), torch.cuda.Stream(dev))
         x_dev, sym, h2d, d2h = state
         compute = torch.cuda.current_stream(dev)
@@ -275,13 +277,27 @@ class ShardedFusedLinear:
         if self.world > 1:
             dist.barrier(group=self.group)
 
-    def fused_step(self, x: torch.Tensor) -> torch.Tensor:
+    def fused_step(self, x: torch.Tensor, *, check_status: bool = False) -> torch.Tensor:
         """``gelu(x @ W^T + b)`` as a full [M, N] view of the peer-mapped output.
 
         Two buffers alternate between calls, so the result stays valid until
-        the call after next; consume it (on this stream) before then."""
+        the call after next; consume it (on this stream) before then.
+
+        The barrier that publishes the result gives up after
+        ``barrier_timeout_us`` when a peer does not answer: it records
+        ``KF_ERR_TIMEOUT`` in the device status word and still advances its
+        epoch, so later calls run on without the guarantee that a peer has
+        consumed a buffer before it is overwritten, and their results cannot
+        be trusted. ``check_status=True`` synchronizes the stream after the
+        barrier and raises if the status word is set (a host round trip per
+        call); otherwise read :func:`kernelo_b200.runtime.native.device_status`
+        at a point of your choosing."""
         buf = self.fused_kernel(x)
         self.fused_publish(x)
+        if check_status:
+            from kernelo_b200.runtime import native
+
+            native.raise_on_device_status(x.device.index)
         return buf[:, : self.n]
 
 
@@ -330,6 +346,28 @@ class ShardedGemv(ShardedFusedLinear):
         return gemv(x, self.w, config=self.config, out=out)
 
 
+def check_peer_geometry(m: int, n_total: int, dtype: torch.dtype, chunk: int, group=None) -> None:
+    """Raise ``ValueError`` on every rank unless all ranks agree on the peer
+    output's geometry.
+
+    Each rank stores its tiles at columns ``[rank*chunk, (rank+1)*chunk)`` of
+    every peer's [m, n_total] buffer, computed from its own ``chunk``; a rank
+    whose shard (or M, or dtype) differs would write past the end of another
+    GPU's buffer. The check runs before any buffer is allocated, mapped or
+    written. Collective over ``group``.
+    """
+    world = dist.get_world_size(group)
+    mine = (int(m), int(n_total), str(dtype), torch.empty(0, dtype=dtype).element_size(), int(chunk))
+    everyone: list = [None] * world
+    dist.all_gather_object(everyone, mine, group=group)
+    if any(g != everyone[0] for g in everyone):
+        detail = ", ".join(f"rank {r}: m={g[0]} n_total={g[1]} dtype={g[2]} chunk={g[4]}"
+                           for r, g in enumerate(everyone))
+        raise ValueError(f"ranks disagree on the sharded output's geometry ({detail})")
+    if chunk * world != n_total:
+        raise ValueError(f"{world} shards of {chunk} columns do not tile {n_total} output columns")
+
+
 class _PeerOutput:
     """Two copies of Y [M, n_total] and a signal array on every rank, each
     mapped into every other rank by CUDA IPC handles (exchanged over the
@@ -341,12 +379,14 @@ class _PeerOutput:
     did with the result of call i.
     """
 
-    def __init__(self, m: int, n_total: int, dtype: torch.dtype, device: torch.device, group) -> None:
+    def __init__(self, m: int, n_total: int, dtype: torch.dtype, device: torch.device, group, *,
+                 chunk: int) -> None:
         from kernelo_b200.runtime import native
 
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        check_peer_geometry(m, n_total, dtype, chunk, group)
         self.bufs = [torch.empty((m, n_total), dtype=dtype, device=device) for _ in range(2)]
         self.signals = torch.zeros((self.world,), dtype=torch.int32, device=device)
         # this rank's barrier epoch, advanced on the device by each barrier

@@ -165,6 +165,24 @@ def _resume_worker(rank: int, world: int, port: int, tmpdir: str, out_q) -> None
         dist.destroy_process_group()
 
 
+def _mismatched_shard_worker(rank: int, world: int, port: int, out_q) -> None:
+    """Two ranks whose weight shards differ in size: the peer-mapped output
+    would be laid out differently on each, so both must refuse before any
+    buffer is allocated, mapped or written."""
+    _init(rank, world, port)
+    try:
+        chunk = 32 if rank == 0 else 48
+        layer = kd.ShardedFusedLinear(None, None, out_features=64, shard_weight=torch.zeros(chunk, 16),
+                                      shard_bias=torch.zeros(chunk), gather="fused")
+        try:
+            layer.fused_kernel(torch.zeros(4, 16))
+            out_q.put((rank, "no error"))
+        except ValueError as exc:
+            out_q.put((rank, str(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
 def _run(target, *args):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -219,3 +237,8 @@ def test_tuning_sweep_is_dealt_over_ranks_and_written_once(tmp_path):
     assert len(entries) == 1 and entries[0].config["MODE"] == 0
     db.close()
     del PROBLEM
+
+
+def test_ranks_with_different_shard_sizes_are_refused_before_any_peer_store():
+    for rank, message in _run(_mismatched_shard_worker):
+        assert "disagree" in message and "chunk=32" in message and "chunk=48" in message, (rank, message)
