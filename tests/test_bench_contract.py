@@ -45,11 +45,11 @@ def test_allgather_roofline_names_the_binding_resource(world):
     chunk = shard_chunk(n, world)
     flop = 2 * m * chunk * k
     link = m * chunk * 2 * (world - 1)
-    r = bench.allgather_roofline(flop, link, 0.2, 1340.9, "measured sustained bf16")
-    t_tensor, t_link = flop / 1340.9e12, link / (bench.NVLINK_GBS * 1e9)
+    r = bench.allgather_roofline(flop, link, 0.2, 1651.8, "measured burst bf16", 770.0)
+    t_tensor, t_link = flop / 1651.8e12, link / (770.0 * 1e9)
     assert r["bound"] == ("nvlink" if t_link > t_tensor else "tensor")
     assert r["frac"] == pytest.approx(max(t_tensor, t_link) * 1e3 / 0.2, abs=1e-4)
-    assert r["nvlink_bytes_per_rank"] == link and r["traffic"] is None
+    assert r["nvlink_bytes_per_rank"] == link and r["traffic"] is None and r["nvlink_peak"] == 770.0
     assert (world == 2) == (r["bound"] == "tensor")  # 4096 x 11008 x 4096: the link binds from 4 GPUs on
 
 
@@ -60,3 +60,15 @@ def test_clock_summary_names_throttle_reasons():
     assert summary["sm_mhz"] == 1490.0 and summary["sm_max_mhz"] == 1965.0 and summary["samples"] == 2
     assert summary["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
     assert bench.ClockSampler(0).summary()["samples"] == 0
+
+
+def test_tensor_peak_follows_the_run():
+    """Burst for a short region or one with no power cap; sustained only for a
+    seconds-long region under sw_power_cap."""
+    pk = {"bf16_tflops": 1651.8, "bf16_tflops_sustained": 1372.7}
+    assert bench.tensor_peak_for_run(pk, "measured", {"reasons": []}, 5.0)[0] == 1651.8
+    assert bench.tensor_peak_for_run(pk, "measured", {"reasons": ["sw_power_cap"]}, 0.0055)[0] == 1651.8
+    peak, kind = bench.tensor_peak_for_run(pk, "measured", {"reasons": ["sw_power_cap"]}, 2.5)
+    assert peak == 1372.7 and "sustained" in kind
+    assert bench.tensor_peak_for_run({"bf16_tflops": 1590.0}, "fallback", {"reasons": ["sw_power_cap"]}, 9.0)[0] \
+        == 1590.0

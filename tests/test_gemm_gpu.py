@@ -243,6 +243,40 @@ def test_baseline_fused_linear_full_size_sampled_rows(dtype, device):
     assert torch.isfinite(out).all()
 
 
+def test_config0_plain_gemm_full_size_sampled_rows(device):
+    """The plain GEMM at its baseline size, 2048 x 4096 x 4096 fp16 with
+    row-major (K, N) B, A and B ~ N(0, 1): sampled rows against the float64
+    oracle under the fp16 gate, every output finite."""
+    from kernelo_b200.kernels.matmul import MatmulOperator
+
+    op = MatmulOperator()
+    problem = Problem.create("matmul", "fp16", M=2048, N=4096, K=4096)
+    a, b = op.make_inputs(problem, device, seed=0)
+    out = op.run(op.default_config(problem), a, b)
+    rows = sample_rows(2048, 48)
+    gate(ref.matmul_ref(host(a[rows]), host(b)), out[rows], torch.float16, context="2048x4096x4096 fp16")
+    assert torch.isfinite(out).all()
+
+
+SWEEP_SHAPES = [tuple(p.dims_dict.values()) for p in workloads.problems("matmul", "sweep_sm100")]
+
+
+@pytest.mark.parametrize("shape", SWEEP_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: str(d)[6:])
+def test_tuner_sweep_shapes_every_dtype(shape, dtype, device):
+    """The tuner sweep's shapes (primes 4099^3 and 1021x2053x509 whose rows
+    TMA cannot describe, one-off-a-tile 129^3 and 257^3, the M=1 decode shape,
+    the plain-GEMM baseline) in fp16, bf16 and fp32 on the library default,
+    inputs N(0, 1): the oracle on up to 64 sampled rows, fp32 held to 1e-5
+    over accumulations up to 4099 long."""
+    m, n, k = shape
+    a, b = operands(m, k, n, dtype, device, seed=m + n + k)
+    out = matmul(a, b)
+    rows = sample_rows(m, 64)
+    gate(ref.matmul_ref(host(a[rows]), host(b)), out[rows], dtype, context=f"{shape} {dtype}")
+    assert torch.isfinite(out).all()
+
+
 # ------------------------------------------------------------------ golden fixtures
 @pytest.mark.parametrize("name", [n for n in golden_names() if n.startswith(("matmul", "fused_linear_"))
                                   and "range" not in n and "bias_order" not in n])

@@ -142,10 +142,11 @@ def test_golden_row_fixtures(name, device):
 
 
 # ---------------------------------------------------------------- baseline sizes
-@pytest.mark.parametrize("cols,dtype", [(1000, torch.float16), (4096, torch.bfloat16), (4097, torch.float16),
-                                        (32000, torch.float32)])
+@pytest.mark.parametrize("cols", [1000, 4096, 4097, 32000])
+@pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: str(d)[6:])
 def test_softmax_baseline_sizes(cols, dtype, device):
-    """[32768, C] with x ~ N(0, 4^2): sampled rows against the oracle, every row sums to 1."""
+    """[32768, C] with x ~ N(0, 4^2), every width and dtype of the baseline:
+    sampled rows against the oracle, every row sums to 1."""
     op = SoftmaxOperator()
     problem = Problem.create("softmax", dtype, rows=32768, cols=cols)
     (x,) = op.make_inputs(problem, device)
