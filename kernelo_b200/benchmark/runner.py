@@ -1,15 +1,21 @@
-"""CUDA-event timing harness (``kernelforge/benchmark/runner.py:123-207``).
+"""Timing harness: device time of one call, as a distribution.
 
-Each timed iteration is bracketed by a pair of CUDA events recorded on the
-current stream; the stream is synchronised once after the loop, so no
-per-iteration sync leaks into the samples. Before every iteration an
-L2-sized buffer is zeroed (enqueued before the start event, so outside the
-measured interval) to keep a previous iteration's operands from being served
-out of the 126 MB L2. Results are summarised as a distribution (median, p95,
-p99) and ranked on the median.
+The reference's ``benchmark`` (``kernelforge/benchmark/runner.py:123-207``)
+fixes the method this keeps: warm-up calls, then per-iteration CUDA events on
+the current stream with a single synchronisation after the loop (so no sync
+leaks into a sample), the L2 emptied before every timed iteration, and the
+samples summarised as median / p95 / p99 with the median used for ranking.
 
-Without a CUDA device the harness falls back to ``time.perf_counter`` and
-labels the result ``perf_counter`` so a CPU timing can never pass for a GPU one.
+Here a timer is a small strategy object -- :class:`_EventClock` on a CUDA
+device, :class:`_HostClock` without one -- that turns a callable into a list
+of per-iteration milliseconds; :func:`benchmark` picks one and
+:meth:`TimingResult.from_samples` summarises. A host-clock result is labelled
+``perf_counter`` so it can never pass for device time.
+
+Beyond the reference: the L2 is emptied by writing a buffer twice its size
+and then reading another (clean lines, no write-back debt for the timed
+kernel), and :func:`graph_time_per_launch` times back-to-back launches
+replayed as one CUDA graph over rotating input sets.
 """
 
 from __future__ import annotations
@@ -33,6 +39,8 @@ TIMER_RESOLUTION_MS = 0.002
 
 @dataclass(frozen=True)
 class TimingResult:
+    """Milliseconds per call: the summary statistics of one timing run."""
+
     median_ms: float
     mean_ms: float
     std_ms: float
@@ -46,28 +54,30 @@ class TimingResult:
     flushed_l2: bool
     samples_ms: tuple[float, ...] = field(default=(), repr=False)
 
+    @classmethod
+    def from_samples(cls, samples_ms, *, warmup: int, iterations: int, timer: str, flushed_l2: bool,
+                     keep_samples: bool = False) -> TimingResult:
+        values = np.sort(np.fromiter((float(v) for v in samples_ms), dtype=np.float64))
+        if values.size == 0:
+            raise ValueError("cannot summarize an empty set of timing samples")
+        median, p95, p99 = np.quantile(values, (0.5, 0.95, 0.99))
+        spread = float(np.std(values, ddof=1)) if values.size > 1 else 0.0
+        kept = tuple(float(v) for v in samples_ms) if keep_samples else ()
+        return cls(float(median), float(values.mean()), spread, float(values[0]), float(values[-1]),
+                   float(p95), float(p99), warmup, iterations, timer, flushed_l2, kept)
+
     @property
     def at_timer_resolution(self) -> bool:
         return self.timer == "cuda_event" and self.median_ms <= TIMER_RESOLUTION_MS
 
     @property
     def median_us(self) -> float:
-        return self.median_ms * 1e3
+        return 1e3 * self.median_ms
 
     def as_dict(self) -> dict[str, float | int | str | bool]:
-        return {
-            "median_ms": self.median_ms,
-            "mean_ms": self.mean_ms,
-            "std_ms": self.std_ms,
-            "min_ms": self.min_ms,
-            "max_ms": self.max_ms,
-            "p95_ms": self.p95_ms,
-            "p99_ms": self.p99_ms,
-            "warmup": self.warmup,
-            "iterations": self.iterations,
-            "timer": self.timer,
-            "flushed_l2": self.flushed_l2,
-        }
+        names = ("median_ms", "mean_ms", "std_ms", "min_ms", "max_ms", "p95_ms", "p99_ms", "warmup", "iterations",
+                 "timer", "flushed_l2")
+        return {name: getattr(self, name) for name in names}
 
 
 def summarize(
@@ -79,25 +89,9 @@ def summarize(
     flushed_l2: bool,
     keep_samples: bool = False,
 ) -> TimingResult:
-    """Distribution of per-iteration times (numpy's linear-interpolated percentiles)."""
-    arr = np.asarray(list(samples_ms), dtype=np.float64)
-    if arr.size == 0:
-        raise ValueError("cannot summarize an empty set of timing samples")
-    p95, p99 = np.percentile(arr, [95, 99])
-    return TimingResult(
-        median_ms=float(np.median(arr)),
-        mean_ms=float(arr.mean()),
-        std_ms=float(arr.std(ddof=1)) if arr.size > 1 else 0.0,
-        min_ms=float(arr.min()),
-        max_ms=float(arr.max()),
-        p95_ms=float(p95),
-        p99_ms=float(p99),
-        warmup=warmup,
-        iterations=iterations,
-        timer=timer,
-        flushed_l2=flushed_l2,
-        samples_ms=tuple(float(x) for x in arr) if keep_samples else (),
-    )
+    """Distribution of per-iteration times (linear-interpolated percentiles)."""
+    return TimingResult.from_samples(samples_ms, warmup=warmup, iterations=iterations, timer=timer,
+                                     flushed_l2=flushed_l2, keep_samples=keep_samples)
 
 
 def l2_flush_buffer(device: torch.device) -> torch.Tensor:
@@ -131,6 +125,47 @@ class L2Flush:
             sleep(self.guard_cycles)
 
 
+class _HostClock:
+    """Wall-clock timing for CPU callables (no device to synchronise)."""
+
+    name = "perf_counter"
+    flushes = False
+
+    def samples(self, fn: Callable[[], object], iterations: int) -> list[float]:
+        out = []
+        for _ in range(iterations):
+            t0 = time.perf_counter()
+            fn()
+            out.append(1e3 * (time.perf_counter() - t0))
+        return out
+
+
+class _EventClock:
+    """CUDA events around each call on the current stream; one sync at the end.
+    With ``flush``, the L2 is emptied before each start event (outside the
+    measured interval: the stream is in order)."""
+
+    name = "cuda_event"
+
+    def __init__(self, device: torch.device, flush: bool) -> None:
+        self.device = device
+        self.flushes = flush
+        self._flush = L2Flush(device) if flush else None
+
+    def samples(self, fn: Callable[[], object], iterations: int) -> list[float]:
+        torch.cuda.synchronize(self.device)
+        marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                 for _ in range(iterations)]
+        for begin, finish in marks:
+            if self._flush is not None:
+                self._flush()
+            begin.record()
+            fn()
+            finish.record()
+        torch.cuda.synchronize(self.device)
+        return [begin.elapsed_time(finish) for begin, finish in marks]
+
+
 def benchmark(
     fn: Callable[[], object],
     *,
@@ -146,58 +181,31 @@ def benchmark(
     if iterations < 1:
         raise ValueError(f"iterations must be at least 1, got {iterations}")
     target = torch.device(device) if device is not None else None
-    on_gpu = torch.cuda.is_available() and (target is None or target.type == "cuda")
-
+    if torch.cuda.is_available() and (target is None or target.type == "cuda"):
+        if target is None or target.index is None:
+            target = torch.device("cuda", torch.cuda.current_device())
+        clock: _HostClock | _EventClock = _EventClock(target, flush_l2)
+    else:
+        clock = _HostClock()
     for _ in range(warmup):
         fn()
-
-    if not on_gpu:
-        samples = []
-        for _ in range(iterations):
-            start = time.perf_counter()
-            fn()
-            samples.append((time.perf_counter() - start) * 1e3)
-        return summarize(
-            samples,
-            warmup=warmup,
-            iterations=iterations,
-            timer="perf_counter",
-            flushed_l2=False,
-            keep_samples=keep_samples,
-        )
-
-    gpu = target if target is not None else torch.device("cuda", torch.cuda.current_device())
-    torch.cuda.synchronize(gpu)
-    flush = L2Flush(gpu) if flush_l2 else None
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(iterations)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(iterations)]
-    for i in range(iterations):
-        if flush is not None:
-            flush()
-        starts[i].record()
-        fn()
-        ends[i].record()
-    torch.cuda.synchronize(gpu)
-    return summarize(
-        [s.elapsed_time(e) for s, e in zip(starts, ends)],
-        warmup=warmup,
-        iterations=iterations,
-        timer="cuda_event",
-        flushed_l2=flush_l2,
-        keep_samples=keep_samples,
-    )
+    samples = clock.samples(fn, iterations)
+    return TimingResult.from_samples(samples, warmup=warmup, iterations=iterations, timer=clock.name,
+                                     flushed_l2=clock.flushes, keep_samples=keep_samples)
 
 
 def cross_check_median_ms(
     fn: Callable[[], object], *, warmup: int = DEFAULT_WARMUP, min_run_time: float = 1.0
 ) -> float:
-    """Median latency from ``torch.utils.benchmark``: a second opinion on the loop above."""
-    import torch.utils.benchmark as tbench
+    """A second opinion on :func:`benchmark`: the median that
+    ``torch.utils.benchmark`` measures for ``fn`` (its own adaptive loop,
+    host-side timing around synchronised blocks), in milliseconds."""
+    from torch.utils.benchmark import Timer
 
     for _ in range(warmup):
         fn()
-    timer = tbench.Timer(stmt="fn()", globals={"fn": fn})
-    return float(timer.blocked_autorange(min_run_time=min_run_time).median) * 1e3
+    measurement = Timer(stmt="fn()", globals={"fn": fn}).blocked_autorange(min_run_time=min_run_time)
+    return 1e3 * float(measurement.median)
 
 
 def rotation_sets(bytes_per_set: int, device: torch.device | str | None = None, *, minimum: int = 2) -> int:

@@ -90,7 +90,7 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
 
 // Softmax kernel choice by row width in 16-byte vectors (rows.cu).
 constexpr long long SOFTMAX_STREAM_MAX_VECTORS = 128;     // up to 2 KB: streaming kernel
-constexpr long long SOFTMAX_REGISTER_MAX_VECTORS = 4096;  // up to 64 KB: register kernel
+constexpr long long SOFTMAX_REGISTER_MAX_VECTORS = 2048;  // up to 32 KB: register kernel
 
 constexpr int GEMV_ROWS_MAX_M = 4;
 // kf_gemv picks it by itself up to this many rows (measured on B200: at M=4

@@ -134,7 +134,9 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
   const int G = static_cast<int>(csize) * nthreads;        // threads per row
   // Softmax keeps exp(x - m_thread) in registers when that fits; wider rows
   // evaluate it again in the output pass (same value either way).
-  constexpr bool KEEP_EV = OP == OP_SOFTMAX && NV * VE <= 32;
+  // (at most 16 values: more pushed the fp32 rows past 64 registers and
+  // halved the resident warps, ncu: 4 CTAs of 128 threads per SM)
+  constexpr bool KEEP_EV = OP == OP_SOFTMAX && NV * VE <= 16;
 
   __shared__ float2 warp_part[2][32];
   __shared__ float2 cta_part[2];  // read by the other CTAs of the cluster
@@ -211,14 +213,18 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
       part = warp_max_sum(m_thr, s);
     } else {
       float ss = 0.0f;
+      if constexpr (VE > 1) {
+        // sm_100 mixed-precision FMA: the squares of 16-bit elements without
+        // converting them first (rows_math.cuh: sumsq_vec)
+        float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int j = 0; j < NV; ++j) {
-        if (g + j * G < nvec) {
-          float f[VE];
-          vec_floats(raw[j], f);
+        for (int j = 0; j < NV; ++j)
+          if (g + j * G < nvec) acc = sumsq_vec<T>(as_u4(raw[j]), acc);
+        ss = acc.x + acc.y;
+      } else {
 #pragma unroll
-          for (int e = 0; e < VE; ++e) ss = fmaf(f[e], f[e], ss);
-        }
+        for (int j = 0; j < NV; ++j)
+          if (g + j * G < nvec) ss = fmaf(to_f32(raw[j].e[0]), to_f32(raw[j].e[0]), ss);
       }
       if (has_head) ss = fmaf(xh, xh, ss);
       if (has_tail) ss = fmaf(xt, xt, ss);
@@ -283,21 +289,28 @@ __global__ void __launch_bounds__(max_threads_for<NV>()) rows_kernel(const RowsP
       for (int j = 0; j < NV; ++j) {
         const int v = g + j * G;
         if (v < nvec) {
+          if constexpr (VE > 1) {
+            if (gamma_vec) {
+              // x * gamma exact (mixed-precision FMA), times the scale, one rounding
+              const V gv = load_cached(reinterpret_cast<const V*>(gb) + v);
+              const uint4 o = scale_gamma_vec<T>(as_u4(raw[j]), as_u4(gv), scale);
+              V ov;
+              memcpy(&ov, &o, 16);
+              store_stream(yv + v, ov);
+              continue;
+            }
+          }
           float f[VE], gf[VE];
           vec_floats(raw[j], f);
-          if (gamma_vec) {
-            vec_floats(load_cached(reinterpret_cast<const V*>(gb) + v), gf);
-          } else {
 #pragma unroll
-            for (int e = 0; e < VE; ++e) gf[e] = to_f32(gb[v * VE + e]);
-          }
+          for (int e = 0; e < VE; ++e) gf[e] = to_f32(gb[v * VE + e]);
 #pragma unroll
-          for (int e = 0; e < VE; ++e) f[e] = f[e] * scale * gf[e];
+          for (int e = 0; e < VE; ++e) f[e] = f[e] * gf[e] * scale;
           store_stream(yv + v, vec_from_floats<T, VE>(f));
         }
       }
-      if (has_head) yr[g] = from_f32<T>(xh * scale * to_f32(gamma[g]));
-      if (has_tail) yr[tail_idx] = from_f32<T>(xt * scale * to_f32(gamma[tail_idx]));
+      if (has_head) yr[g] = from_f32<T>(xh * to_f32(gamma[g]) * scale);
+      if (has_tail) yr[tail_idx] = from_f32<T>(xt * to_f32(gamma[tail_idx]) * scale);
     }
   }
   // No CTA may leave while a peer could still read its cta_part.
@@ -398,9 +411,11 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
     } else {
       // Measured on B200 (graph-timed, inputs beyond L2): softmax rows of up
       // to 2 KB stream (32768 x 1000 fp16: 0.78 of the copy bandwidth against
-      // 0.70 in registers); rows up to 64 KB sit in registers at about eight
+      // 0.70 in registers); rows up to 32 KB sit in registers at about eight
       // vectors per thread (2048 / 4096 / 8192 fp16 columns: 0.95 / 0.99 /
-      // 0.98, against 0.80 / 0.80 / 0.87 streamed); wider rows stream again.
+      // 0.98, against 0.80 / 0.80 / 0.87 streamed); wider rows stream again
+      // (32000 fp16 columns: 0.99 streamed by 8-warp groups against 0.57 in
+      // registers at 16 vectors a thread).
       // RMSNorm's lighter arithmetic runs as fast in the register kernel.
       const long long nvec_row = ceil_div(a.cols * elem, 16LL);
       const int warps = c.num_warps > 0 ? c.num_warps : stream_default_warps(a.cols, elem);

@@ -16,7 +16,9 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
-#include "kf_common.cuh"  // ex2_ftz
+#include <type_traits>
+
+#include "kf_common.cuh"  // ex2_ftz, f2_*
 
 namespace kf {
 
@@ -133,6 +135,72 @@ __device__ __forceinline__ uint4 from_floats(const float* f) {
     using R = RowVec<T>;
     return make_uint4(R::from_f2(f[0], f[1]), R::from_f2(f[2], f[3]), R::from_f2(f[4], f[5]),
                       R::from_f2(f[6], f[7]));
+  }
+}
+
+// ---- RMSNorm on 16-byte vectors with sm_100's mixed-precision FMA.
+// `fma.rn.f32.{f16,bf16} d, a, b, c` multiplies two 16-bit values and adds an
+// fp32 value with one rounding to fp32. A product of two 16-bit values is
+// exact in fp32 (at most 22 significant bits), so x*x and x*gamma come out
+// exact without converting either operand first: the sum of squares keeps the
+// fp32 rounding of the reference's fp32 path (rmsnorm.py:130-143), and the
+// output x * gamma * scale is rounded in fp32 once before the final rounding
+// to T (the reference rounds (x*scale)*gamma twice in fp32).
+template <typename T>
+__device__ __forceinline__ float fma_mixed(uint16_t a, uint16_t b, float c) {
+  float d;
+  if constexpr (std::is_same_v<T, __half>) {
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  } else {
+    asm("fma.rn.f32.bf16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  }
+  return d;
+}
+
+// acc + sum of squares of the vector's elements, on two chains (even and odd
+// elements) so that consecutive FMAs do not wait on each other.
+template <typename T>
+__device__ __forceinline__ float2 sumsq_vec(uint4 v, float2 acc) {
+  if constexpr (sizeof(T) == 4) {
+    acc.x = fmaf(__uint_as_float(v.x), __uint_as_float(v.x), acc.x);
+    acc.y = fmaf(__uint_as_float(v.y), __uint_as_float(v.y), acc.y);
+    acc.x = fmaf(__uint_as_float(v.z), __uint_as_float(v.z), acc.x);
+    acc.y = fmaf(__uint_as_float(v.w), __uint_as_float(v.w), acc.y);
+  } else {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint16_t lo = static_cast<uint16_t>(w[i]), hi = static_cast<uint16_t>(w[i] >> 16);
+      acc.x = fma_mixed<T>(lo, lo, acc.x);
+      acc.y = fma_mixed<T>(hi, hi, acc.y);
+    }
+  }
+  return acc;
+}
+
+// The vector x * gamma * scale, rounded once to T.
+template <typename T>
+__device__ __forceinline__ uint4 scale_gamma_vec(uint4 x, uint4 g, float scale) {
+  const uint64_t s2 = f2_splat(scale);
+  const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, gw[4] = {g.x, g.y, g.z, g.w};
+  uint32_t out[4];
+  if constexpr (sizeof(T) == 4) {
+    // fp32 elements: x * gamma on pairs, then the scale
+    const uint64_t p0 = f2_mul(f2_pack(__uint_as_float(xw[0]), __uint_as_float(xw[1])),
+                               f2_pack(__uint_as_float(gw[0]), __uint_as_float(gw[1])));
+    const uint64_t p1 = f2_mul(f2_pack(__uint_as_float(xw[2]), __uint_as_float(xw[3])),
+                               f2_pack(__uint_as_float(gw[2]), __uint_as_float(gw[3])));
+    const float2 a = f2_unpack(f2_mul(p0, s2)), b = f2_unpack(f2_mul(p1, s2));
+    return make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x), __float_as_uint(b.y));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float plo = fma_mixed<T>(static_cast<uint16_t>(xw[i]), static_cast<uint16_t>(gw[i]), -0.0f);
+      const float phi = fma_mixed<T>(static_cast<uint16_t>(xw[i] >> 16), static_cast<uint16_t>(gw[i] >> 16), -0.0f);
+      const float2 y = f2_unpack(f2_mul(f2_pack(plo, phi), s2));
+      out[i] = RowVec<T>::from_f2(y.x, y.y);
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
   }
 }
 

@@ -1,11 +1,14 @@
-"""SQLite results store (``kernelforge/db.py:1-320``).
+"""SQLite results store.
 
 Every measurement row points at its problem, its config and its run, and the
 run carries the GPU, driver, CUDA, torch and native-library versions. The
-schema is the reference's (runs / problems / configs / results, configs stored
-as a JSON parameter set plus a content digest), so databases from the two
-implementations can be compared with the same queries. The ``triton_version``
-column of ``runs`` records the native library version here.
+schema text is the reference's (``kernelforge/db.py:35-99``: runs / problems /
+configs / results, configs stored as a JSON parameter set plus a content
+digest), so databases of the two implementations answer the same queries.
+The ``triton_version`` column of ``runs`` records the native library version
+here. The access layer is this project's own: interned problem and config
+rows, one transaction per write, and the best-per-label ranking done in SQL
+with a window function.
 """
 
 from __future__ import annotations
@@ -113,34 +116,65 @@ class Measurement:
     gbps: float | None = None
     error: str = ""
 
+    def columns(self) -> dict[str, Any]:
+        """The ``results`` columns this measurement fills (ids excluded).
+
+        Times are stored in microseconds; a measurement that never ran has
+        NULL timing and correctness columns."""
+        t, v = self.timing, self.verification
+        cols: dict[str, Any] = {"label": self.label, "status": self.status,
+                                "correct": None if v is None else int(v.passed),
+                                "rel_error": None if v is None else v.error,
+                                "tflops": self.tflops, "gbps": self.gbps, "error": self.error}
+        for stat in _TIMING_STATS:
+            cols[f"{stat}_us"] = None if t is None else 1e3 * getattr(t, f"{stat}_ms")
+        for name in ("warmup", "iterations", "timer"):
+            cols[name] = None if t is None else getattr(t, name)
+        cols["flushed_l2"] = None if t is None else int(t.flushed_l2)
+        return cols
+
+
+_TIMING_STATS = ("median", "mean", "std", "min", "max", "p95", "p99")
+_RUN_ENV_COLUMNS = ("timestamp", "hostname", "platform", "python_version", "torch_version", "triton_version",
+                    "cuda_version", "driver_version", "gpu_name", "gpu_arch", "gpu_memory_bytes", "sm_count",
+                    "device_key")
+
 
 def default_db_path() -> Path:
-    return Path(os.environ.get("KERNELFORGE_DB", str(DEFAULT_DB_PATH)))
-
-
-def _us(timing: Any, attr: str) -> float | None:
-    return None if timing is None else getattr(timing, attr) * 1e3
+    configured = os.environ.get("KERNELFORGE_DB")
+    return Path(configured) if configured else DEFAULT_DB_PATH
 
 
 class ResultsDB:
+    """The results store: one SQLite file in the reference's schema.
+
+    Problems and configs are interned (one row each, looked up by their
+    natural key and memoised per connection); every write is one transaction.
+    """
+
     def __init__(self, path: str | Path | None = None) -> None:
         self.path = Path(path) if path is not None else default_db_path()
         if str(self.path) != ":memory:":
             self.path.parent.mkdir(parents=True, exist_ok=True)
         self._conn = sqlite3.connect(str(self.path))
         self._conn.row_factory = sqlite3.Row
-        self._conn.execute("PRAGMA foreign_keys = ON")
-        self._conn.executescript(_SCHEMA)
-        version = int(self._conn.execute("PRAGMA user_version").fetchone()[0])
-        if version == 0:
-            self._conn.execute(f"PRAGMA user_version = {SCHEMA_VERSION}")
-        elif version != SCHEMA_VERSION:
+        self._ids: dict[tuple, int] = {}
+        try:
+            self._prepare()
+        except BaseException:
             self._conn.close()
-            raise RuntimeError(
-                f"{self.path} was written by schema version {version}, "
-                f"this build expects {SCHEMA_VERSION}"
-            )
-        self._conn.commit()
+            raise
+
+    def _prepare(self) -> None:
+        conn = self._conn
+        conn.execute("PRAGMA foreign_keys = ON")
+        found = conn.execute("PRAGMA user_version").fetchone()[0]
+        if found not in (0, SCHEMA_VERSION):
+            raise RuntimeError(f"{self.path} was written by schema version {found}, "
+                               f"this build expects {SCHEMA_VERSION}")
+        with conn:
+            conn.executescript(_SCHEMA)
+            conn.execute(f"PRAGMA user_version = {SCHEMA_VERSION}")
 
     def __enter__(self) -> ResultsDB:
         return self
@@ -151,134 +185,103 @@ class ResultsDB:
     def close(self) -> None:
         self._conn.close()
 
-    # writes -----------------------------------------------------------------
+    # ------------------------------------------------------------ writes
+    def _insert(self, table: str, values: dict[str, Any]) -> int:
+        names = ", ".join(values)
+        marks = ", ".join("?" for _ in values)
+        cursor = self._conn.execute(f"INSERT INTO {table} ({names}) VALUES ({marks})", tuple(values.values()))
+        return int(cursor.lastrowid)
+
+    def _intern(self, table: str, id_column: str, key: dict[str, Any], extra: dict[str, Any]) -> int:
+        """The id of the row of ``table`` with natural key ``key``, inserted if new."""
+        memo = (table, *key.values())
+        if memo in self._ids:
+            return self._ids[memo]
+        where = " AND ".join(f"{name} = ?" for name in key)
+        row = self._conn.execute(f"SELECT {id_column} FROM {table} WHERE {where}", tuple(key.values())).fetchone()
+        rowid = int(row[0]) if row is not None else self._insert(table, {**key, **extra})
+        self._ids[memo] = rowid
+        return rowid
+
     def start_run(self, env: Environment, *, notes: str = "", version: str = "") -> int:
-        cols = (
-            "timestamp, hostname, platform, python_version, torch_version, triton_version, "
-            "cuda_version, driver_version, gpu_name, gpu_arch, gpu_memory_bytes, sm_count, "
-            "device_key, kernelforge_version, notes"
-        )
-        values = (
-            env.timestamp, env.hostname, env.platform, env.python_version, env.torch_version,
-            env.triton_version, env.cuda_version, env.driver_version, env.gpu_name, env.gpu_arch,
-            env.gpu_memory_bytes, env.sm_count, env.device_key, version, notes,
-        )
-        cur = self._conn.execute(f"INSERT INTO runs ({cols}) VALUES ({','.join('?' * 15)})", values)
-        self._conn.commit()
-        return int(cur.lastrowid)
+        with self._conn:
+            return self._insert("runs", {**{name: getattr(env, name) for name in _RUN_ENV_COLUMNS},
+                                         "kernelforge_version": version, "notes": notes})
 
     def problem_id(self, problem: Problem) -> int:
-        key = (problem.operation, problem.shape_key, problem.dtype_name)
-        self._conn.execute(
-            "INSERT OR IGNORE INTO problems (operation, shape_key, dtype, dims_json) VALUES (?,?,?,?)",
-            (*key, json.dumps(problem.dims_dict, sort_keys=True)),
-        )
-        row = self._conn.execute(
-            "SELECT problem_id FROM problems WHERE operation=? AND shape_key=? AND dtype=?", key
-        ).fetchone()
-        return int(row[0])
+        return self._intern("problems", "problem_id",
+                            {"operation": problem.operation, "shape_key": problem.shape_key,
+                             "dtype": problem.dtype_name},
+                            {"dims_json": json.dumps(problem.dims_dict, sort_keys=True)})
 
     def config_id(self, config: KernelConfig) -> int:
-        self._conn.execute(
-            "INSERT OR IGNORE INTO configs (operation, digest, params_json) VALUES (?,?,?)",
-            (config.operation, config.digest, config.to_json()),
-        )
-        row = self._conn.execute(
-            "SELECT config_id FROM configs WHERE operation=? AND digest=?",
-            (config.operation, config.digest),
-        ).fetchone()
-        return int(row[0])
+        return self._intern("configs", "config_id", {"operation": config.operation, "digest": config.digest},
+                            {"params_json": config.to_json()})
+
+    def _record(self, run_id: int, problem: Problem, m: Measurement) -> int:
+        ids = {"run_id": run_id, "problem_id": self.problem_id(problem),
+               "config_id": None if m.config is None else self.config_id(m.config)}
+        return self._insert("results", {**ids, **m.columns()})
 
     def record(self, run_id: int, problem: Problem, m: Measurement) -> int:
-        t, v = m.timing, m.verification
-        values = (
-            run_id,
-            self.problem_id(problem),
-            None if m.config is None else self.config_id(m.config),
-            m.label,
-            m.status,
-            None if v is None else int(v.passed),
-            None if v is None else v.error,
-            _us(t, "median_ms"),
-            _us(t, "mean_ms"),
-            _us(t, "std_ms"),
-            _us(t, "min_ms"),
-            _us(t, "max_ms"),
-            _us(t, "p95_ms"),
-            _us(t, "p99_ms"),
-            None if t is None else t.warmup,
-            None if t is None else t.iterations,
-            None if t is None else t.timer,
-            None if t is None else int(t.flushed_l2),
-            m.tflops,
-            m.gbps,
-            m.error,
-        )
-        cur = self._conn.execute(
-            "INSERT INTO results (run_id, problem_id, config_id, label, status, correct, rel_error, "
-            "median_us, mean_us, std_us, min_us, max_us, p95_us, p99_us, warmup, iterations, timer, "
-            f"flushed_l2, tflops, gbps, error) VALUES ({','.join('?' * 21)})",
-            values,
-        )
-        self._conn.commit()
-        return int(cur.lastrowid)
+        with self._conn:
+            return self._record(run_id, problem, m)
 
     def record_many(self, run_id: int, problem: Problem, measurements: Iterable[Measurement]) -> None:
-        for m in measurements:
-            self.record(run_id, problem, m)
+        with self._conn:
+            for m in measurements:
+                self._record(run_id, problem, m)
+
+    # ------------------------------------------------------------ reads
+    def _select(self, filters: dict[str, Any], *, tail: str = "ORDER BY r.result_id") -> list[dict]:
+        where = " AND ".join(f"{column} = ?" for column in filters)
+        query = f"{_JOINED} {'WHERE ' + where if where else ''} {tail}"
+        return [dict(row) for row in self._conn.execute(query, tuple(filters.values()))]
+
+    def _lookup_filters(self, problem: Problem, config: KernelConfig, label: str) -> dict[str, Any]:
+        return {"p.operation": problem.operation, "p.shape_key": problem.shape_key, "p.dtype": problem.dtype_name,
+                "c.digest": config.digest, "r.label": label}
 
     def has_result(self, problem: Problem, config: KernelConfig, *, label: str = "kernelforge") -> bool:
         """Whether (problem, config) already has a row: lets a sweep resume."""
-        row = self._conn.execute(
-            "SELECT 1 FROM results r JOIN problems p ON p.problem_id = r.problem_id "
-            "JOIN configs c ON c.config_id = r.config_id WHERE p.operation=? AND p.shape_key=? "
-            "AND p.dtype=? AND c.digest=? AND r.label=? LIMIT 1",
-            (problem.operation, problem.shape_key, problem.dtype_name, config.digest, label),
-        ).fetchone()
-        return row is not None
+        return bool(self._select(self._lookup_filters(problem, config, label), tail="LIMIT 1"))
 
     def latest_result(self, problem: Problem, config: KernelConfig, *, device_key: str,
                       label: str = "kernelforge") -> dict | None:
         """The newest row for (problem, config, label) measured on ``device_key``,
         or None: what a resumed sweep reuses instead of measuring again."""
-        row = self._conn.execute(
-            _JOINED + " WHERE p.operation=? AND p.shape_key=? AND p.dtype=? AND c.digest=? AND r.label=? "
-            "AND run.device_key=? ORDER BY r.result_id DESC LIMIT 1",
-            (problem.operation, problem.shape_key, problem.dtype_name, config.digest, label, device_key),
-        ).fetchone()
-        return None if row is None else dict(row)
+        found = self._select({**self._lookup_filters(problem, config, label), "run.device_key": device_key},
+                             tail="ORDER BY r.result_id DESC LIMIT 1")
+        return found[0] if found else None
 
-    # reads ------------------------------------------------------------------
     def rows(self, *, operation: str | None = None, dtype: str | None = None) -> list[dict]:
-        where, params = [], []
-        if operation:
-            where.append("p.operation = ?")
-            params.append(operation)
-        if dtype:
-            where.append("p.dtype = ?")
-            params.append(dtype)
-        query = _JOINED + (" WHERE " + " AND ".join(where) if where else "") + " ORDER BY r.result_id"
-        return [dict(r) for r in self._conn.execute(query, params)]
+        filters = {column: value for column, value in (("p.operation", operation), ("p.dtype", dtype)) if value}
+        return self._select(filters)
 
     def best_per_label(self, *, operation: str | None = None) -> list[dict]:
-        """Fastest correct row per (operation, shape, dtype, label)."""
-        best: dict[tuple, dict] = {}
-        for row in self.rows(operation=operation):
-            if row["median_us"] is None or row["correct"] == 0:
-                continue
-            key = (row["operation"], row["shape_key"], row["dtype"], row["label"])
-            if key not in best or row["median_us"] < best[key]["median_us"]:
-                best[key] = row
-        return sorted(best.values(), key=lambda r: (r["operation"], r["dtype"], r["shape_key"], r["label"]))
+        """Fastest correct row per (operation, shape, dtype, label), ranked in SQL."""
+        where = "WHERE r.median_us IS NOT NULL AND (r.correct IS NULL OR r.correct != 0)"
+        args: tuple = ()
+        if operation:
+            where += " AND p.operation = ?"
+            args = (operation,)
+        query = (f"SELECT * FROM (SELECT j.*, ROW_NUMBER() OVER (PARTITION BY operation, shape_key, dtype, label "
+                 f"ORDER BY median_us, result_id) AS rank_in_label FROM ({_JOINED} {where}) AS j) "
+                 "WHERE rank_in_label = 1 ORDER BY operation, dtype, shape_key, label")
+        found = []
+        for row in self._conn.execute(query, args):
+            item = dict(row)
+            item.pop("rank_in_label")
+            found.append(item)
+        return found
 
     def runs(self) -> list[dict]:
-        return [dict(r) for r in self._conn.execute("SELECT * FROM runs ORDER BY run_id")]
+        return [dict(row) for row in self._conn.execute("SELECT * FROM runs ORDER BY run_id")]
 
     def counts(self) -> dict[str, int]:
-        return {
-            t: int(self._conn.execute(f"SELECT COUNT(*) FROM {t}").fetchone()[0])
-            for t in ("runs", "problems", "configs", "results")
-        }
+        tables = ("runs", "problems", "configs", "results")
+        query = " UNION ALL ".join(f"SELECT '{t}', COUNT(*) FROM {t}" for t in tables)
+        return {name: int(n) for name, n in self._conn.execute(query)}
 
     def operations(self) -> list[str]:
-        return [r[0] for r in self._conn.execute("SELECT DISTINCT operation FROM problems ORDER BY 1")]
+        return [row[0] for row in self._conn.execute("SELECT DISTINCT operation FROM problems ORDER BY operation")]

@@ -3,13 +3,13 @@
 ``default_rows_config`` mirrors ``resolve_rows_config`` in ``csrc/rows.cu``:
 
 * a softmax over many rows (at least two per SM) whose input and output rows
-  sit at the same 16-byte phase, with rows of up to 2 KB or beyond 64 KB, goes
+  sit at the same 16-byte phase, with rows of up to 2 KB or beyond 32 KB, goes
   to the persistent streaming kernel (``ROW_KERNEL=2``,
   ``csrc/rows_stream.cu``): row groups of ``num_warps`` warps (the fewest, as a
   power of two, that hold a row at up to 16 vectors a thread) each keeping
   their next rows in flight as bulk copies into shared-memory slots (two slots
   per group for the narrow rows);
-* other softmax rows of up to 64 KB go to the register kernel (``ROW_KERNEL=1``,
+* other softmax rows of up to 32 KB go to the register kernel (``ROW_KERNEL=1``,
   ``csrc/rows.cu``) at about eight 16-byte vectors per thread, one CTA per row;
 * RMSNorm, and whatever else is left, to the register kernel at about four
   vectors per thread, one CTA per row until a row exceeds 4096 vectors
@@ -66,7 +66,7 @@ def same_phase(x: torch.Tensor | None, cols: int) -> bool:
 
 #: Softmax kernel choice by row width in 16-byte vectors (mirrors kf_internal.h).
 SOFTMAX_STREAM_MAX_VECTORS = 128
-SOFTMAX_REGISTER_MAX_VECTORS = 4096
+SOFTMAX_REGISTER_MAX_VECTORS = 2048
 
 
 def default_rows_config(
@@ -79,7 +79,7 @@ def default_rows_config(
     sm_count: int = 148,
 ) -> KernelConfig:
     """The library's choice (mirrors resolve_rows_config in rows.cu): softmax
-    rows up to 2 KB stream, rows up to 64 KB sit in registers at about eight
+    rows up to 2 KB stream, rows up to 32 KB sit in registers at about eight
     16-byte vectors per thread, wider rows stream again (when there are enough
     rows for every SM and the streaming kernel takes the layout); RMSNorm uses
     the register kernel at about four vectors per thread."""

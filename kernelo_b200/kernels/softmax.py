@@ -5,7 +5,7 @@ rounding to the input dtype. The row maximum is subtracted for the reason the
 reference gives: fp16 ``exp`` overflows above x ~ 11. Both native kernels read
 each row once into registers, reduce the (max, sum of exp) pair in a single
 pass with the online rescaling rule, and write the row once. Rows of 2 to
-64 KB go to the register kernel (one CTA per row, about eight 16-byte vectors
+32 KB go to the register kernel (one CTA per row, about eight 16-byte vectors
 per thread, 0.95-0.99 of the copy bandwidth on B200); with many rows, narrower
 and wider rows go to a persistent kernel that streams rows through
 shared-memory slots with bulk copies (loads of later rows in flight while

@@ -1,22 +1,19 @@
-"""Nsight Compute counters for one launch (``kernelforge/profiling/nsight.py``).
+"""Hardware counters for one launch, through Nsight Compute.
 
-The latency harness says which configuration is faster; the counters say why
-(tensor-pipe and DRAM throughput against peak, occupancy, warp stalls). Sections
-are requested by name, as in the reference, and the raw page is parsed into
-{kernel: {metric: value}}.
+The reference profiles a kernel by re-running its CLI under ``ncu`` with named
+sections and parsing the raw CSV page (``kernelforge/profiling/nsight.py``);
+this module keeps that interface -- the section names a user passes
+(``throughput``, ``memory``, ...), :func:`build_command`, :func:`run` and
+:class:`NsightRun` -- and builds it around a :class:`Capture` description that
+knows the rules this pool imposes on a capture:
 
-Two rules are built in rather than left to the caller:
-
-* ``--clock-control none`` on every command. Without it ncu locks the GPU's
-  clocks for the capture, and a capture that is interrupted can leave them
-  locked for whoever uses the GPU next.
-* The target runs once without ncu first, and is profiled only if that run
-  exited 0: a program that faults must not be replayed under the profiler.
-
-Keep captures small (one launch of one kernel, inputs of a few GB at most):
-each captured launch is replayed once per hardware pass (a full set is ~40).
-No timeout is imposed on the ncu process, since killing ncu in the middle of
-a capture can leave the GPU unusable; a small capture ends by itself.
+* every command carries ``--clock-control none``: without it ncu locks the
+  GPU's clocks for the capture, and an interrupted capture can leave them
+  locked for the GPU's next user;
+* the target runs once without ncu first and is only profiled if that run
+  exited 0, so a program that faults is never replayed under the profiler;
+* a capture is one launch by default, and no timeout is put on ncu (killing it
+  mid-capture can leave the GPU unusable): keep the profiled case small.
 """
 
 from __future__ import annotations
@@ -41,9 +38,41 @@ SECTIONS: dict[str, str] = {
 
 DEFAULT_SECTIONS = ("launch", "occupancy", "throughput", "memory", "stalls")
 
+#: Non-metric columns of the raw page worth keeping beside the counters.
+_KEPT_COLUMNS = frozenset({"Grid Size", "Block Size", "Registers Per Thread"})
+
 
 def ncu_available() -> bool:
     return shutil.which("ncu") is not None
+
+
+@dataclass(frozen=True)
+class Capture:
+    """One ncu invocation: what to run, which sections, which launches."""
+
+    target: tuple[str, ...]
+    sections: tuple[str, ...] = DEFAULT_SECTIONS
+    kernel_filter: str | None = None
+    launch_count: int = 1
+    launch_skip: int = 0
+    report_path: Path | None = None
+
+    def __post_init__(self) -> None:
+        unknown = sorted(set(self.sections).difference(SECTIONS))
+        if unknown:
+            raise ValueError(f"unknown sections {unknown}; available: {sorted(SECTIONS)}")
+        if self.launch_count < 1:
+            raise ValueError("launch_count must be at least 1")
+
+    def argv(self) -> list[str]:
+        opts = ["--clock-control", "none", "--target-processes", "all"]
+        opts += [arg for name in self.sections for arg in ("--section", SECTIONS[name])]
+        if self.kernel_filter:
+            opts += ["--kernel-name", self.kernel_filter]
+        opts += ["--launch-count", str(self.launch_count), "--launch-skip", str(self.launch_skip)]
+        if self.report_path is not None:
+            opts += ["--export", str(self.report_path), "--force-overwrite"]
+        return ["ncu", *opts, "--csv", "--page", "raw", *self.target]
 
 
 @dataclass(frozen=True)
@@ -60,21 +89,22 @@ class NsightRun:
         return self.returncode == 0
 
     def render(self) -> str:
-        lines = [f"$ {' '.join(self.command)}"]
+        out = io.StringIO()
+        out.write("$ " + " ".join(self.command) + "\n")
         if not self.ok:
-            lines.append(f"exited {self.returncode}")
-            if self.stderr.strip():
-                lines.append(self.stderr.strip()[-2000:])
-            return "\n".join(lines)
-        for kernel, values in self.metrics.items():
-            lines.append(f"\n{kernel}")
-            width = max((len(k) for k in values), default=0)
-            lines.extend(f"  {k:<{width}}  {v}" for k, v in values.items())
+            out.write(f"exited {self.returncode}\n")
+            out.write(self.stderr.strip()[-2000:])
+            return out.getvalue().rstrip()
         if not self.metrics:
-            lines.append(self.stdout.strip())
+            out.write(self.stdout.strip() + "\n")
+        for kernel, counters in self.metrics.items():
+            out.write(f"\n{kernel}\n")
+            pad = max(map(len, counters), default=0)
+            for name in counters:
+                out.write(f"  {name.ljust(pad)}  {counters[name]}\n")
         if self.report_path is not None:
-            lines.append(f"\nreport: {self.report_path}")
-        return "\n".join(lines)
+            out.write(f"\nreport: {self.report_path}\n")
+        return out.getvalue().rstrip()
 
 
 def build_command(
@@ -87,21 +117,8 @@ def build_command(
     report_path: str | Path | None = None,
 ) -> list[str]:
     """The ncu command line that profiles ``target`` (clocks never locked)."""
-    unknown = sorted(set(sections) - set(SECTIONS))
-    if unknown:
-        raise ValueError(f"unknown sections {unknown}; available: {sorted(SECTIONS)}")
-    if launch_count < 1:
-        raise ValueError("launch_count must be at least 1")
-    command = ["ncu", "--clock-control", "none", "--target-processes", "all"]
-    for name in sections:
-        command += ["--section", SECTIONS[name]]
-    if kernel_filter:
-        command += ["--kernel-name", kernel_filter]
-    command += ["--launch-count", str(launch_count), "--launch-skip", str(launch_skip)]
-    if report_path is not None:
-        command += ["--export", str(report_path), "--force-overwrite"]
-    command += ["--csv", "--page", "raw"]
-    return command + list(target)
+    return Capture(tuple(target), tuple(sections), kernel_filter, launch_count, launch_skip,
+                   Path(report_path) if report_path is not None else None).argv()
 
 
 def self_command(argv: list[str]) -> list[str]:
@@ -110,31 +127,29 @@ def self_command(argv: list[str]) -> list[str]:
 
 
 def parse_raw_csv(stdout: str) -> dict[str, dict[str, str]]:
-    """``ncu --csv --page raw``: a header of metric names, a row of units, then
-    one row per profiled launch. Returns {kernel: {metric: "value unit"}};
-    empty if the text is not in that form (the caller keeps the raw text)."""
-    lines = [ln for ln in stdout.splitlines() if ln.startswith('"')]
+    """``ncu --csv --page raw`` text as {kernel: {metric: "value unit"}}.
+
+    The page is a header row of metric names, a row of units and one row per
+    profiled launch (ncu's own log lines, which do not start with a quote,
+    are skipped). A kernel seen twice gets ``#<launch>`` appended. Anything
+    not in that form parses to {} and the caller keeps the raw text."""
+    body = "\n".join(line for line in stdout.splitlines() if line.startswith('"'))
     try:
-        rows = list(csv.reader(io.StringIO("\n".join(lines))))
+        table = list(csv.reader(io.StringIO(body)))
     except csv.Error:
         return {}
-    if len(rows) < 3:
+    if len(table) < 3 or "Kernel Name" not in table[0]:
         return {}
-    header, units = rows[0], rows[1]
-    try:
-        name_col = header.index("Kernel Name")
-    except ValueError:
-        return {}
-    out: dict[str, dict[str, str]] = {}
-    for i, row in enumerate(rows[2:]):
+    header, units, launches = table[0], table[1], table[2:]
+    keep = [i for i, name in enumerate(header) if "__" in name or name in _KEPT_COLUMNS]
+    name_at = header.index("Kernel Name")
+    parsed: dict[str, dict[str, str]] = {}
+    for launch, row in enumerate(launches):
         if len(row) != len(header):
             continue
-        kernel = f"{row[name_col]} #{i}" if row[name_col] in out else row[name_col]
-        out[kernel] = {
-            h: f"{v} {u}".strip() for h, u, v in zip(header, units, row)
-            if "__" in h or h in ("Grid Size", "Block Size", "Registers Per Thread")
-        }
-    return out
+        kernel = row[name_at] if row[name_at] not in parsed else f"{row[name_at]} #{launch}"
+        parsed[kernel] = {header[i]: f"{row[i]} {units[i]}".strip() for i in keep}
+    return parsed
 
 
 def run(
@@ -149,18 +164,13 @@ def run(
     """Run ``target`` once plainly, then, if it exited 0, under Nsight Compute."""
     if not ncu_available():
         raise RuntimeError("ncu was not found on PATH; install NVIDIA Nsight Compute to collect counters")
+    capture = Capture(tuple(target), tuple(sections), kernel_filter, launch_count, launch_skip,
+                      Path(report_path) if report_path is not None else None)
     plain = subprocess.run(list(target), capture_output=True, text=True)
     if plain.returncode != 0:
         return NsightRun(tuple(target), plain.returncode, plain.stdout,
                          "not profiled: the plain run failed\n" + plain.stderr)
-    command = build_command(target, sections=sections, kernel_filter=kernel_filter,
-                            launch_count=launch_count, launch_skip=launch_skip, report_path=report_path)
-    result = subprocess.run(command, capture_output=True, text=True)
-    return NsightRun(
-        command=tuple(command),
-        returncode=result.returncode,
-        stdout=result.stdout,
-        stderr=result.stderr,
-        report_path=Path(report_path) if report_path else None,
-        metrics=parse_raw_csv(result.stdout) if result.returncode == 0 else {},
-    )
+    command = capture.argv()
+    done = subprocess.run(command, capture_output=True, text=True)
+    return NsightRun(tuple(command), done.returncode, done.stdout, done.stderr, capture.report_path,
+                     parse_raw_csv(done.stdout) if done.returncode == 0 else {})

@@ -1,34 +1,45 @@
-"""Tuned-configuration cache (``kernelforge/tuning/cache.py:1-159``).
+"""Tuned-configuration cache: the winner of each tuned problem, per device.
 
-A JSON file nested ``device -> operation -> dtype -> shape`` holding the winning
-config of each tuned problem, so a serving process reads a tuning instead of
-re-running it. The device part is the board name plus architecture: a file
-copied to other hardware misses rather than serving a foreign tuning. Writes
-go through a temporary file and ``os.replace`` so a crash never leaves a
-truncated cache. Location: ``$KERNELFORGE_CACHE``, else
-``$XDG_CACHE_HOME/kernelforge/configs.json``.
+The reference keeps its tuned configs in one JSON file nested
+``device -> operation -> dtype -> shape`` (``kernelforge/tuning/cache.py:97-129``)
+with a version number; that file layout is kept exactly, so a cache written by
+either implementation reads in the other.
+
+Inside, the store is a flat index keyed by the 4-tuple (device, operation,
+dtype, shape), which the file's nesting is only a serialisation of. Writes are
+merges: under an exclusive lock on the cache's directory, the file is re-read,
+only the keys this process changed are applied to it, and the result replaces
+the file through a temporary file and ``os.replace``. So several tuning
+processes (one per GPU, say) can put entries into one cache without losing
+each other's, and a crash never leaves a truncated file.
+
+The device part of a key is the board name plus architecture: a file copied to
+other hardware misses rather than serving a foreign tuning. Location:
+``$KERNELFORGE_CACHE``, else ``$XDG_CACHE_HOME/kernelforge/configs.json``.
 """
 
 from __future__ import annotations
 
+import contextlib
+import fcntl
 import json
 import os
 import tempfile
 from dataclasses import dataclass
 from pathlib import Path
-from typing import Any
 
 from kernelo_b200.tuning.config import KernelConfig, Problem
 
 CACHE_VERSION = 1
 
+Key = tuple[str, str, str, str]  # (device_key, operation, dtype, shape_key)
+
 
 def default_cache_path() -> Path:
-    explicit = os.environ.get("KERNELFORGE_CACHE")
-    if explicit:
-        return Path(explicit)
-    base = Path(os.environ.get("XDG_CACHE_HOME", str(Path.home() / ".cache")))
-    return base / "kernelforge" / "configs.json"
+    if os.environ.get("KERNELFORGE_CACHE"):
+        return Path(os.environ["KERNELFORGE_CACHE"])
+    root = os.environ.get("XDG_CACHE_HOME") or os.path.join(os.path.expanduser("~"), ".cache")
+    return Path(root, "kernelforge", "configs.json")
 
 
 @dataclass(frozen=True)
@@ -43,61 +54,92 @@ class CacheEntry:
     candidates_tested: int | None = None
 
     def describe(self) -> str:
-        params = ", ".join(f"{k}={v}" for k, v in self.config.as_dict().items())
-        latency = "unmeasured" if self.median_us is None else f"{self.median_us:.1f} us"
-        return (
-            f"{self.device_key}  {self.operation:<16} {self.dtype:<5} "
-            f"{self.shape_key:<22} {latency:>12}  {params}"
-        )
+        latency = f"{self.median_us:.1f} us" if self.median_us is not None else "unmeasured"
+        params = ", ".join(f"{name}={value}" for name, value in self.config.as_dict().items())
+        return (f"{self.device_key}  {self.operation:<16} {self.dtype:<5} {self.shape_key:<22} "
+                f"{latency:>12}  {params}")
+
+
+def _parse(path: Path, text: str) -> dict[Key, dict]:
+    """The file's nested document as a flat index (validated)."""
+    try:
+        doc = json.loads(text)
+    except json.JSONDecodeError as exc:
+        raise RuntimeError(f"cache file {path} is not valid JSON: {exc}") from exc
+    version = doc.get("version") if isinstance(doc, dict) else None
+    if version != CACHE_VERSION:
+        raise RuntimeError(f"cache file {path} has version {version}, expected {CACHE_VERSION}; "
+                           "run `kernelforge cache clear` to discard it")
+    index: dict[Key, dict] = {}
+    for device, by_op in doc.get("entries", {}).items():
+        for operation, by_dtype in by_op.items():
+            for dtype, by_shape in by_dtype.items():
+                for shape, record in by_shape.items():
+                    index[(device, operation, dtype, shape)] = record
+    return index
+
+
+def _document(index: dict[Key, dict]) -> dict:
+    """The flat index in the file's nested layout."""
+    entries: dict = {}
+    for (device, operation, dtype, shape), record in index.items():
+        entries.setdefault(device, {}).setdefault(operation, {}).setdefault(dtype, {})[shape] = record
+    return {"version": CACHE_VERSION, "entries": entries}
 
 
 class ConfigCache:
-    """Best-known configs in one JSON file."""
+    """Best-known configs in one JSON file (see the module docstring)."""
 
     def __init__(self, path: str | Path | None = None) -> None:
         self.path = Path(path) if path is not None else default_cache_path()
-        self._data = self._read()
+        self._index: dict[Key, dict] = self._load()
 
-    def _read(self) -> dict[str, Any]:
-        if not self.path.exists():
-            return {"version": CACHE_VERSION, "entries": {}}
+    # ------------------------------------------------------------ file access
+    def _load(self) -> dict[Key, dict]:
         try:
-            data = json.loads(self.path.read_text())
-        except json.JSONDecodeError as exc:
-            raise RuntimeError(f"cache file {self.path} is not valid JSON: {exc}") from exc
-        if data.get("version") != CACHE_VERSION:
-            raise RuntimeError(
-                f"cache file {self.path} has version {data.get('version')}, expected "
-                f"{CACHE_VERSION}; run `kernelforge cache clear` to discard it"
-            )
-        return data
+            text = self.path.read_text()
+        except FileNotFoundError:
+            return {}
+        return _parse(self.path, text)
 
-    def _write(self) -> None:
+    @contextlib.contextmanager
+    def _locked(self):
+        """Exclusive lock on the cache's directory for a read-merge-write."""
         self.path.parent.mkdir(parents=True, exist_ok=True)
-        fd, tmp_name = tempfile.mkstemp(dir=self.path.parent, suffix=".tmp")
+        fd = os.open(self.path.parent, os.O_RDONLY)
         try:
-            with os.fdopen(fd, "w") as fh:
-                json.dump(self._data, fh, indent=2, sort_keys=True)
-            os.replace(tmp_name, self.path)
-        except BaseException:
-            Path(tmp_name).unlink(missing_ok=True)
-            raise
+            fcntl.flock(fd, fcntl.LOCK_EX)
+            yield
+        finally:
+            fcntl.flock(fd, fcntl.LOCK_UN)
+            os.close(fd)
 
-    def _node(self, device_key: str, problem: Problem, *, create: bool) -> dict[str, Any] | None:
-        node: dict[str, Any] = self._data["entries"]
-        for key in (device_key, problem.operation, problem.dtype_name):
-            if key not in node:
-                if not create:
-                    return None
-                node[key] = {}
-            node = node[key]
-        return node
+    def _commit(self, changes: dict[Key, dict]) -> None:
+        """Apply ``changes`` to the file as it is now, atomically."""
+        with self._locked():
+            merged = self._load()
+            merged.update(changes)
+            fd, tmp = tempfile.mkstemp(dir=self.path.parent, prefix=".configs-", suffix=".tmp")
+            try:
+                with os.fdopen(fd, "w") as fh:
+                    json.dump(_document(merged), fh, indent=2, sort_keys=True)
+                    fh.flush()
+                    os.fsync(fh.fileno())
+                os.replace(tmp, self.path)
+            except BaseException:
+                with contextlib.suppress(FileNotFoundError):
+                    os.unlink(tmp)
+                raise
+        self._index = merged
+
+    # ------------------------------------------------------------ public API
+    @staticmethod
+    def _key(problem: Problem, device_key: str) -> Key:
+        return (device_key, problem.operation, problem.dtype_name, problem.shape_key)
 
     def get(self, problem: Problem, device_key: str) -> KernelConfig | None:
-        node = self._node(device_key, problem, create=False)
-        if node is None or problem.shape_key not in node:
-            return None
-        return KernelConfig(problem.operation, **node[problem.shape_key]["config"])
+        record = self._index.get(self._key(problem, device_key))
+        return None if record is None else KernelConfig(problem.operation, **record["config"])
 
     def put(
         self,
@@ -109,43 +151,26 @@ class ConfigCache:
         timestamp: str = "",
         candidates_tested: int | None = None,
     ) -> None:
-        node = self._node(device_key, problem, create=True)
-        assert node is not None
-        node[problem.shape_key] = {
-            "config": config.as_dict(),
-            "median_us": median_us,
-            "timestamp": timestamp,
-            "candidates_tested": candidates_tested,
-        }
-        self._write()
+        record = {"config": config.as_dict(), "median_us": median_us, "timestamp": timestamp,
+                  "candidates_tested": candidates_tested}
+        self._commit({self._key(problem, device_key): record})
 
     def entries(self) -> list[CacheEntry]:
-        found = []
-        for device_key, ops in self._data["entries"].items():
-            for operation, dtypes in ops.items():
-                for dtype, shapes in dtypes.items():
-                    for shape_key, payload in shapes.items():
-                        found.append(
-                            CacheEntry(
-                                device_key=device_key,
-                                operation=operation,
-                                dtype=dtype,
-                                shape_key=shape_key,
-                                config=KernelConfig(operation, **payload["config"]),
-                                median_us=payload.get("median_us"),
-                                timestamp=payload.get("timestamp", ""),
-                                candidates_tested=payload.get("candidates_tested"),
-                            )
-                        )
-        found.sort(key=lambda e: (e.device_key, e.operation, e.dtype, e.shape_key))
-        return found
+        rows = [
+            CacheEntry(device_key=device, operation=operation, dtype=dtype, shape_key=shape,
+                       config=KernelConfig(operation, **record["config"]), median_us=record.get("median_us"),
+                       timestamp=record.get("timestamp", ""), candidates_tested=record.get("candidates_tested"))
+            for (device, operation, dtype, shape), record in self._index.items()
+        ]
+        return sorted(rows, key=lambda e: (e.device_key, e.operation, e.dtype, e.shape_key))
 
     def clear(self) -> int:
-        count = len(self.entries())
-        self._data = {"version": CACHE_VERSION, "entries": {}}
-        if self.path.exists():
-            self.path.unlink()
-        return count
+        removed = len(self._index)
+        with self._locked():
+            with contextlib.suppress(FileNotFoundError):
+                self.path.unlink()
+        self._index = {}
+        return removed
 
     def __len__(self) -> int:
-        return len(self.entries())
+        return len(self._index)

@@ -1,20 +1,29 @@
-"""The tuner (``kernelforge/tuning/tuner.py:1-370``).
+"""The tuning pipeline: candidates -> gate -> timing -> ranking -> persistence.
 
-    problem -> candidates -> filters -> launch+verify -> benchmark -> rank -> persist
+The reference's ``Tuner.tune`` (``kernelforge/tuning/tuner.py:184-239``) fixes
+the contract this keeps: a candidate that fails the correctness gate is never
+ranked however fast it is; every candidate is gated before any is timed, so
+no first-launch cost lands in a measurement; one failing candidate never ends
+the sweep; failures are recorded with the statuses ``compile_error``,
+``runtime_error``, ``incorrect`` and ``out_of_memory``; the winner goes to the
+config cache and every outcome to the results database.
 
-Two guarantees carry over unchanged. A candidate that fails the correctness
-gate is never ranked, however fast (skipping work is fast). And every
-candidate is verified before any is timed, so no first-launch cost lands in a
-measurement. With native kernels there is no JIT compile: "compile" is the
-first launch, and a config the library cannot run surfaces as
-``OutOfResources`` -> ``compile_error``. After each verification the device
-status word is read, so a kernel whose bounded wait gave up is recorded as a
-``runtime_error`` instead of poisoning the rest of the sweep.
+The structure is this project's own. A :class:`_Sweep` holds one tuning
+run's state and walks it through explicit stages -- :meth:`~_Sweep.plan`
+(generate, filter, split off what a resumed run already measured),
+:meth:`~_Sweep.gate`, :meth:`~_Sweep.time`, :meth:`~_Sweep.compare` -- and
+:class:`Tuner` is the configuration plus persistence around it. With native
+kernels there is no JIT step: "compile" is the first launch, and a config
+the library refuses raises ``OutOfResources``, which classifies as
+``compile_error``. After every launch the device status word is read, so a
+kernel whose bounded wait gave up is a ``runtime_error`` of that candidate
+instead of a poisoned sweep.
 """
 
 from __future__ import annotations
 
 import time
+from collections import Counter
 from collections.abc import Callable
 from dataclasses import dataclass, field
 
@@ -37,16 +46,22 @@ STATUS_OOM = "out_of_memory"
 
 _MAX_ERROR_CHARS = 400
 
+#: Exception-class-name fragments and the status each maps to, first match
+#: wins. Names, not types: the native layer's ``OutOfResources`` and torch's
+#: ``OutOfMemoryError`` are matched the way the reference matches Triton's.
+_STATUS_BY_NAME: tuple[tuple[tuple[str, ...], str], ...] = (
+    (("OutOfMemory",), STATUS_OOM),
+    (("OutOfResources", "Compil", "Resource"), STATUS_COMPILE_ERROR),
+)
+
 
 def _classify(exc: BaseException) -> tuple[str, str]:
-    """Status and short message for an exception raised by a candidate."""
-    name = type(exc).__name__
+    """Status and a one-line message for an exception raised by a candidate."""
+    kind = type(exc).__name__
     text = " ".join(str(exc).split())[:_MAX_ERROR_CHARS]
-    if "OutOfMemory" in name:
-        return STATUS_OOM, text
-    if "OutOfResources" in name or "Compil" in name or "Resource" in name:
-        return STATUS_COMPILE_ERROR, f"{name}: {text}"
-    return STATUS_RUNTIME_ERROR, f"{name}: {text}"
+    status = next((s for fragments, s in _STATUS_BY_NAME if any(f in kind for f in fragments)),
+                  STATUS_RUNTIME_ERROR)
+    return status, text if status == STATUS_OOM else f"{kind}: {text}"
 
 
 @dataclass(frozen=True)
@@ -63,9 +78,9 @@ class CandidateOutcome:
 
     @property
     def median_ms(self) -> float:
-        if self.timing is None:
-            raise ValueError(f"candidate {self.config!r} has no timing ({self.status})")
-        return self.timing.median_ms
+        if self.timing is not None:
+            return self.timing.median_ms
+        raise ValueError(f"candidate {self.config!r} has no timing ({self.status})")
 
 
 @dataclass
@@ -88,21 +103,20 @@ class TuningResult:
 
     @property
     def correct(self) -> int:
-        return sum(o.ok for o in self.outcomes)
+        return sum(1 for o in self.outcomes if o.ok)
 
     def ranked(self) -> list[CandidateOutcome]:
-        """Correct candidates, fastest median first."""
-        return sorted((o for o in self.outcomes if o.ok and o.timing is not None), key=lambda o: o.median_ms)
+        """Correct, timed candidates, fastest median first (stable for ties)."""
+        timed = [o for o in self.outcomes if o.ok and o.timing is not None]
+        return sorted(timed, key=lambda o: o.timing.median_ms)
 
     @property
     def best(self) -> CandidateOutcome | None:
-        ranked = self.ranked()
-        return ranked[0] if ranked else None
+        return next(iter(self.ranked()), None)
 
     @property
     def best_config(self) -> KernelConfig | None:
-        best = self.best
-        return None if best is None else best.config
+        return self.best.config if self.best is not None else None
 
     def tflops(self, ms: float) -> float:
         return metrics.tflops(self.flops, ms)
@@ -111,40 +125,129 @@ class TuningResult:
         return metrics.gbps(self.bytes_moved, ms)
 
     def speedup_over(self, label: str) -> float | None:
-        best = self.best
-        if best is None or label not in self.baselines:
+        best, other = self.best, self.baselines.get(label)
+        if best is None or other is None:
             return None
-        return metrics.speedup(self.baselines[label].median_ms, best.median_ms)
+        return metrics.speedup(other.median_ms, best.median_ms)
 
     def status_counts(self) -> dict[str, int]:
-        counts: dict[str, int] = {}
-        for o in self.outcomes:
-            counts[o.status] = counts.get(o.status, 0) + 1
-        return counts
+        return dict(Counter(o.status for o in self.outcomes))
 
 
 def _outcome_from_row(config: KernelConfig, row: dict) -> CandidateOutcome:
-    """A stored measurement as a candidate outcome (times are kept in us)."""
+    """A stored ``results`` row (times in microseconds) as a candidate outcome."""
     timing = None
     if row["median_us"] is not None:
-        ms = {k: (row[f"{k}_us"] or 0.0) / 1e3 for k in ("median", "mean", "std", "min", "max", "p95", "p99")}
-        timing = TimingResult(ms["median"], ms["mean"], ms["std"], ms["min"], ms["max"], ms["p95"], ms["p99"],
-                              int(row["warmup"] or 0), int(row["iterations"] or 0), row["timer"] or "",
+        stats = [(row[f"{name}_us"] or 0.0) / 1e3 for name in ("median", "mean", "std", "min", "max", "p95", "p99")]
+        timing = TimingResult(*stats, int(row["warmup"] or 0), int(row["iterations"] or 0), row["timer"] or "",
                               bool(row["flushed_l2"]))
     verification = None
     if row["correct"] is not None:
-        verification = VerificationResult(bool(row["correct"]), row["rel_error"] or 0.0, 0.0, 0, 0, 0.0,
-                                          "" if row["correct"] else row["error"])
-    return CandidateOutcome(config=config, status=row["status"], verification=verification, timing=timing,
-                            error=row["error"] or "")
+        passed = bool(row["correct"])
+        verification = VerificationResult(passed, row["rel_error"] or 0.0, 0.0, 0, 0, 0.0,
+                                          "" if passed else row["error"])
+    return CandidateOutcome(config, row["status"], verification, timing, row["error"] or "")
 
 
-def _device_status_check(device: torch.device) -> None:
-    if device.type != "cuda":
-        return
-    from kernelo_b200.runtime import native
+def _check_device_status(device: torch.device) -> None:
+    """Raise if a kernel's bounded wait gave up since the last check."""
+    if device.type == "cuda":
+        from kernelo_b200.runtime import native
 
-    native.raise_on_device_status(device.index)
+        native.raise_on_device_status(device.index)
+
+
+def _time_gated(tuner: Tuner, operator: Operator, outcome: CandidateOutcome, inputs, device: torch.device
+                ) -> CandidateOutcome:
+    """Time a gated candidate with the tuner's settings (failures pass through)."""
+    if not outcome.ok:
+        return outcome
+    try:
+        timing = benchmark(lambda: operator.run(outcome.config, *inputs), warmup=tuner.warmup,
+                           iterations=tuner.iterations, device=device, flush_l2=tuner.flush_l2)
+        _check_device_status(device)
+    except Exception as exc:  # noqa: BLE001 - a failure is this candidate's outcome
+        status, message = _classify(exc)
+        return CandidateOutcome(outcome.config, status, outcome.verification, error=message)
+    return CandidateOutcome(outcome.config, STATUS_OK, outcome.verification, timing)
+
+
+class _Sweep:
+    """One tuning run's state, walked through the stages in order."""
+
+    def __init__(self, tuner: Tuner, operator: Operator, problem: Problem, device: torch.device) -> None:
+        self.tuner, self.operator, self.problem, self.device = tuner, operator, problem, device
+        self.env = capture_environment(device)
+        self.started = time.perf_counter()
+        self.reused: dict[KernelConfig, CandidateOutcome] = {}
+
+    def plan(self) -> None:
+        """The candidate list (generated, filtered, budgeted, dealt to this
+        worker) and, when resuming, the outcomes already on record."""
+        tuner = self.tuner
+        self.space = self.operator.search_space().generate(self.problem, device_caps(self.device),
+                                                           max_candidates=tuner.max_candidates)
+        keep = tuner.candidate_filter or (lambda index, config: True)
+        self.candidates = [c for i, c in enumerate(self.space.candidates) if keep(i, c)]
+        if tuner.resume:
+            for config in self.candidates:
+                row = tuner.db.latest_result(self.problem, config, device_key=self.env.device_key)
+                if row is not None:
+                    self.reused[config] = _outcome_from_row(config, row)
+            if self.reused:
+                tuner.log(f"Resuming: {len(self.reused)} of {len(self.candidates)} candidates already measured")
+        self.inputs = self.operator.make_inputs(self.problem, self.device, seed=tuner.seed)
+
+    def _run_checked(self, config: KernelConfig) -> torch.Tensor:
+        output = self.operator.run(config, *self.inputs)
+        _check_device_status(output.device)
+        return output
+
+    def gate(self) -> list[CandidateOutcome]:
+        """Launch and verify every new candidate before anything is timed."""
+        fresh = [c for c in self.candidates if c not in self.reused]
+        self.tuner.log(f"Verifying candidates... ({len(fresh)} to check)")
+        self.reference = self.operator.reference(*self.inputs)
+        gated = []
+        for config in fresh:
+            try:
+                output = self._run_checked(config)
+            except Exception as exc:  # noqa: BLE001 - one failing candidate must not end the sweep
+                status, message = _classify(exc)
+                gated.append(CandidateOutcome(config, status, error=message))
+                continue
+            check = verify(self.reference, output, dtype=self.problem.dtype)
+            gated.append(CandidateOutcome(config, STATUS_OK if check.passed else STATUS_INCORRECT, check,
+                                          error="" if check.passed else check.reason))
+        self.tuner.log(f"{sum(o.ok for o in gated)} / {len(fresh)} configurations passed correctness")
+        return gated
+
+    def time(self, gated: list[CandidateOutcome]) -> tuple[CandidateOutcome, ...]:
+        self.tuner.log("Benchmarking...")
+        measured = {o.config: _time_gated(self.tuner, self.operator, o, self.inputs, self.device) for o in gated}
+        return tuple(self.reused.get(c) or measured[c] for c in self.candidates)
+
+    def compare(self) -> dict[str, TimingResult]:
+        """Every comparison label, gated and timed like the candidates; a label
+        that disagrees with the reference or fails is logged and left out."""
+        tuner, found = self.tuner, {}
+        for label, call in self.operator.baselines(self.problem, self.inputs).items():
+            try:
+                check = verify(self.reference, call(), dtype=self.problem.dtype)
+                if check.passed:
+                    found[label] = benchmark(call, warmup=tuner.warmup, iterations=tuner.iterations,
+                                             device=self.device, flush_l2=tuner.flush_l2)
+                else:
+                    tuner.log(f"  baseline {label} disagrees with the reference: {check.reason}")
+            except Exception as exc:  # noqa: BLE001
+                tuner.log(f"  baseline {label} unavailable: {_classify(exc)[1]}")
+        return found
+
+    def result(self, outcomes: tuple[CandidateOutcome, ...], baselines: dict[str, TimingResult]) -> TuningResult:
+        op, problem = self.operator, self.problem
+        return TuningResult(problem, self.env, self.space.generated, self.space.feasible, outcomes, baselines,
+                            op.flops(problem), op.bytes_moved(problem), time.perf_counter() - self.started,
+                            op.is_memory_bound(), self.space.rejected)
 
 
 class Tuner:
@@ -165,23 +268,19 @@ class Tuner:
         candidate_filter: Callable[[int, KernelConfig], bool] | None = None,
         resume: bool = False,
     ) -> None:
-        self.warmup = warmup
-        self.iterations = iterations
-        self.flush_l2 = flush_l2
+        if resume and db is None:
+            raise ValueError("resume needs a results database")
+        self.warmup, self.iterations, self.flush_l2 = warmup, iterations, flush_l2
         self.max_candidates = max_candidates
         self.measure_baselines = measure_baselines
         self.seed = seed
-        self.db = db
-        self.cache = cache
+        self.db, self.cache = db, cache
         self._log = log
-        #: (index, config) -> keep? Used to shard one candidate list over workers.
+        #: (index, config) -> keep? Deals one candidate list over several workers.
         self.candidate_filter = candidate_filter
-        #: Reuse the outcome of every candidate the database already holds for
-        #: this problem and device, so an interrupted sweep continues where it
-        #: stopped (needs ``db``).
+        #: Reuse every outcome the database already holds for this problem on
+        #: this device, so an interrupted sweep continues where it stopped.
         self.resume = resume
-        if resume and db is None:
-            raise ValueError("resume needs a results database")
 
     def log(self, message: str) -> None:
         if self._log is not None:
@@ -190,147 +289,39 @@ class Tuner:
     def tune(
         self, operator: Operator, problem: Problem, *, device: torch.device | str | None = None
     ) -> TuningResult:
-        started = time.perf_counter()
         target = torch.device(device) if device is not None else require_cuda()
-        env = capture_environment(target)
-        caps = device_caps(target)
-        cset = operator.search_space().generate(problem, caps, max_candidates=self.max_candidates)
-        candidates = list(cset.candidates)
-        if self.candidate_filter is not None:
-            candidates = [c for i, c in enumerate(candidates) if self.candidate_filter(i, c)]
-        inputs = operator.make_inputs(problem, target, seed=self.seed)
-
-        reused: dict[KernelConfig, CandidateOutcome] = {}
-        if self.resume:
-            for c in candidates:
-                row = self.db.latest_result(problem, c, device_key=env.device_key)
-                if row is not None:
-                    reused[c] = _outcome_from_row(c, row)
-            if reused:
-                self.log(f"Resuming: {len(reused)} of {len(candidates)} candidates already measured")
-        fresh = [c for c in candidates if c not in reused]
-
+        sweep = _Sweep(self, operator, problem, target)
+        sweep.plan()
         with exact_fp32_matmul():
-            reference = operator.reference(*inputs)
-            self.log(f"Verifying candidates... ({len(fresh)} to check)")
-            verified = [self._verify_candidate(operator, c, inputs, reference, problem) for c in fresh]
-            self.log(f"{sum(o.ok for o in verified)} / {len(fresh)} configurations passed correctness")
-            self.log("Benchmarking...")
-            measured = {o.config: self._time_candidate(operator, o, inputs, target) for o in verified}
-            timed = [reused[c] if c in reused else measured[c] for c in candidates]
-            baselines = (
-                self._measure_baselines(operator, problem, inputs, reference, target)
-                if self.measure_baselines
-                else {}
-            )
-
-        result = TuningResult(
-            problem=problem,
-            environment=env,
-            generated=cset.generated,
-            feasible=cset.feasible,
-            outcomes=tuple(timed),
-            baselines=baselines,
-            flops=operator.flops(problem),
-            bytes_moved=operator.bytes_moved(problem),
-            elapsed_s=time.perf_counter() - started,
-            memory_bound=operator.is_memory_bound(),
-            rejections=cset.rejected,
-        )
-        self._persist(result, env, skip=set(reused))
+            gated = sweep.gate()
+            outcomes = sweep.time(gated)
+            baselines = sweep.compare() if self.measure_baselines else {}
+        result = sweep.result(outcomes, baselines)
+        self._persist(result, sweep.env, skip=set(sweep.reused))
         return result
 
-    # stages -------------------------------------------------------------------
-    def _verify_candidate(self, operator, config, inputs, reference, problem) -> CandidateOutcome:
-        try:
-            output = operator.run(config, *inputs)
-            _device_status_check(output.device)
-        except Exception as exc:  # one failing candidate must not end the sweep
-            status, message = _classify(exc)
-            return CandidateOutcome(config=config, status=status, error=message)
-        check = verify(reference, output, dtype=problem.dtype)
-        return CandidateOutcome(
-            config=config,
-            status=STATUS_OK if check.passed else STATUS_INCORRECT,
-            verification=check,
-            error="" if check.passed else check.reason,
-        )
-
     def _time_candidate(self, operator, outcome, inputs, device) -> CandidateOutcome:
-        if not outcome.ok:
-            return outcome
-        try:
-            timing = benchmark(
-                lambda: operator.run(outcome.config, *inputs),
-                warmup=self.warmup,
-                iterations=self.iterations,
-                device=device,
-                flush_l2=self.flush_l2,
-            )
-            _device_status_check(device)
-        except Exception as exc:
-            status, message = _classify(exc)
-            return CandidateOutcome(config=outcome.config, status=status,
-                                    verification=outcome.verification, error=message)
-        return CandidateOutcome(config=outcome.config, status=STATUS_OK,
-                                verification=outcome.verification, timing=timing)
-
-    def _measure_baselines(self, operator, problem, inputs, reference, device) -> dict[str, TimingResult]:
-        """Every comparison label, gated and timed exactly like the candidates."""
-        out: dict[str, TimingResult] = {}
-        for label, fn in operator.baselines(problem, inputs).items():
-            try:
-                check = verify(reference, fn(), dtype=problem.dtype)
-                if not check.passed:
-                    self.log(f"  baseline {label} disagrees with the reference: {check.reason}")
-                    continue
-                out[label] = benchmark(fn, warmup=self.warmup, iterations=self.iterations,
-                                       device=device, flush_l2=self.flush_l2)
-            except Exception as exc:
-                self.log(f"  baseline {label} unavailable: {_classify(exc)[1]}")
-        return out
+        """Time one gated candidate on ``inputs`` (used to re-time finalists)."""
+        return _time_gated(self, operator, outcome, inputs, torch.device(device))
 
     def _persist(self, result: TuningResult, env: Environment, *, skip: set[KernelConfig] = frozenset()) -> None:
+        """Winner to the cache; every new outcome and baseline to the database
+        (outcomes reused from an earlier run already have their rows)."""
         best = result.best
         if self.cache is not None and best is not None:
-            self.cache.put(
-                result.problem,
-                env.device_key,
-                best.config,
-                median_us=best.timing.median_us if best.timing else None,
-                timestamp=env.timestamp,
-                candidates_tested=result.tested,
-            )
+            self.cache.put(result.problem, env.device_key, best.config,
+                           median_us=best.timing.median_us if best.timing else None, timestamp=env.timestamp,
+                           candidates_tested=result.tested)
         if self.db is None:
             return
         from kernelo_b200 import __version__
 
+        def rates(ms: float | None) -> dict:
+            return {"tflops": result.tflops(ms), "gbps": result.gbps(ms)} if ms else {"tflops": None, "gbps": None}
+
+        rows = [Measurement("kernelforge", o.status, o.config, o.verification, o.timing,
+                            error=o.error, **rates(o.timing.median_ms if o.timing else None))
+                for o in result.outcomes if o.config not in skip]
+        rows += [Measurement(label, STATUS_OK, timing=t, **rates(t.median_ms)) for label, t in result.baselines.items()]
         run_id = self.db.start_run(env, notes="tune", version=__version__)
-        rows = []
-        for o in result.outcomes:
-            if o.config in skip:  # reused from an earlier run: its row is already there
-                continue
-            ms = o.timing.median_ms if o.timing else None
-            rows.append(
-                Measurement(
-                    label="kernelforge",
-                    status=o.status,
-                    config=o.config,
-                    verification=o.verification,
-                    timing=o.timing,
-                    tflops=result.tflops(ms) if ms else None,
-                    gbps=result.gbps(ms) if ms else None,
-                    error=o.error,
-                )
-            )
-        for label, timing in result.baselines.items():
-            rows.append(
-                Measurement(
-                    label=label,
-                    status=STATUS_OK,
-                    timing=timing,
-                    tflops=result.tflops(timing.median_ms),
-                    gbps=result.gbps(timing.median_ms),
-                )
-            )
         self.db.record_many(run_id, result.problem, rows)

@@ -251,6 +251,21 @@ def test_cache_round_trip_keys_and_atomic_write(tmp_path):
     assert cache.clear() == 1 and not path.exists()
 
 
+def test_cache_writers_merge_instead_of_overwriting(tmp_path):
+    """Two processes' caches on one file (a tuner per GPU): each put merges into
+    the file as it is on disk, so neither loses the other's entry."""
+    path = tmp_path / "configs.json"
+    first, second = ConfigCache(path), ConfigCache(path)
+    other = Problem.create("matmul", "bf16", M=2048, N=4096, K=4096)
+    first.put(PROBLEM, "NVIDIA_B200_sm100", CONFIG, median_us=1.0)
+    second.put(other, "NVIDIA_B200_sm100", CONFIG.replace(BLOCK_N=64), median_us=2.0)
+    merged = ConfigCache(path)
+    assert merged.get(PROBLEM, "NVIDIA_B200_sm100") == CONFIG
+    assert merged.get(other, "NVIDIA_B200_sm100") == CONFIG.replace(BLOCK_N=64)
+    doc = json.loads(path.read_text())
+    assert doc["version"] == CACHE_VERSION and set(doc["entries"]["NVIDIA_B200_sm100"]["matmul"]) == {"fp16", "bf16"}
+
+
 def test_cache_refuses_corrupt_or_foreign_versions(tmp_path):
     path = tmp_path / "c.json"
     path.write_text("{not json")
