@@ -1,40 +1,52 @@
-"""Candidate generation for sm_100a (``kernelforge/tuning/search.py:1-558``).
+"""Candidate generation for sm_100a.
 
-Same three stages as the reference -- enumerate a grid, reject points with a
-named reason, budget the survivors by a documented priority -- over the
-parameters that matter on Blackwell instead of Triton's:
+The reference's tuner takes its candidates from a hardware-derived grid,
+rejects points with a named reason, drops launches that would leave most SMs
+idle, and budgets the rest by a documented priority
+(``kernelforge/tuning/search.py:122-217``). That contract is kept; the grids
+and rules are Blackwell's, and every grid point is a configuration this
+library's kernels can actually run:
 
 GEMM (``matmul``, ``fused_linear``, ``fused_linear_erf``, ``gemv``)
-    tcgen05 grid: MMA tile ``BLOCK_M`` {64, 128, 256 (2-CTA pair)} x ``BLOCK_N``
-    {16, 64, 128, 192, 256} x ``BLOCK_K`` {32, 64, 128} x ``num_stages``
-    (shared-memory ring depth) {2, 4, 6} x thread-block cluster
-    {1x1, 2x1, 1x2, 2x2} = 540 points, plus the 3 SIMT tiles that serve fp32
-    and operands no TMA tensor map can describe. ``SWAP_AB`` is derived from
-    the shape (skinny M puts the weight on the 128-row side) and ``STREAM_K``
-    is left to the library (stream-K when whole tiles would leave SMs idle).
+    tcgen05 tiles: ``BLOCK_M`` {128 (one SM), 256 (an SM pair, cta_group::2,
+    on a 2x1 cluster)} x ``BLOCK_N`` {16, 64, 128, 192, 224, 256} x
+    ``BLOCK_K`` {64, 128} x ``num_stages`` (shared-memory ring depth)
+    {2, 3, 4, 6, 8} x ``STREAM_K`` (tile schedule: 1 stream-K, 2 whole
+    tiles, 3 whole tiles with the last partial wave split into half-width
+    tiles) = 360 points; ``SWAP_AB`` follows the shape (skinny M puts the
+    weight on the 128-row side) and ``GROUP_M`` (the L2 raster width) the
+    library's rule. Plus the 16-row tile GEMV's compiled shapes for
+    K-contiguous weights, and the CUDA-core tiles that serve fp32 and
+    operands no TMA tensor map can describe.
 
-    Hardware limits: 227 KiB shared memory per CTA, 512 TMEM columns per SM
-    (a double-buffered fp32 accumulator needs 2 x BLOCK_N), TMA's 16-byte
-    stride rule, whole 128-byte swizzle atoms (BLOCK_K >= 64 for 16-bit), an
-    MN-major B operand taking 64-column boxes. Implementation limits of this
-    build are rejected with "not implemented" so they stay visible.
+    Limits applied as named rules: 227 KiB of shared memory per CTA, 512
+    TMEM columns per SM (a double-buffered fp32 accumulator takes 2 x
+    BLOCK_N), TMA's 16-byte stride rule, an MN-major B in 64-column boxes, a
+    pair tile's BLOCK_N split in two 16-column-aligned halves, tile overshoot,
+    pipeline fill, and the schedules' own conditions.
 
 Row reductions (``softmax``, ``rmsnorm``)
-    ``num_warps`` {1..32} x ``ROWS_PER_PROGRAM`` {1, 2, 4} x ``CLUSTER``
-    {1, 2, 4, 8} (CTAs sharing one row through distributed shared memory).
+    The register kernel: ``num_warps`` {1..32} x ``ROWS_PER_PROGRAM``
+    {1, 2, 4} x ``CLUSTER`` {1, 2, 4, 8} (CTAs sharing one row through
+    distributed shared memory); the streaming kernel: warps per row group
+    {1..16} with as many or with two shared-memory slots per group.
     ``BLOCK_SIZE`` (next power of two of the row) is kept for the reference's
     "cannot hold a row" / "single-pass limit" checks; the single-pass limit
-    rises from 16384 to 131072 columns because a row may span a cluster.
+    is 131072 columns because a row may span a cluster.
 
-Filters read a :class:`DeviceCaps` value, never ``torch.cuda``, so they are
-unit-testable without the GPU they describe.
+Filters read a :class:`DeviceCaps` value, never ``torch.cuda``, so they can be
+tested against a GPU that is not attached. A :class:`CandidateSet` records
+how many configs survived each stage of the funnel.
 """
 
 from __future__ import annotations
 
 import math
+import re
 from abc import ABC, abstractmethod
+from collections import Counter
 from collections.abc import Iterator
+from dataclasses import dataclass
 from itertools import product
 
 from kernelo_b200.dtypes import itemsize
@@ -55,8 +67,35 @@ def ceil_div(a: int, b: int) -> int:
     return -(-a // b)
 
 
+@dataclass(frozen=True)
+class CandidateSet:
+    """The funnel's result: the budgeted candidates, what each stage left, and
+    every rejected config with its reason."""
+
+    problem: Problem
+    generated: int
+    feasible: int
+    after_prune: int
+    budget: int
+    candidates: list[KernelConfig]
+    rejected: tuple[tuple[KernelConfig, str], ...]
+
+    def __len__(self) -> int:
+        return len(self.candidates)
+
+    def __iter__(self) -> Iterator[KernelConfig]:
+        return iter(self.candidates)
+
+    def rule_counts(self) -> Counter:
+        """Rejections per rule: a reason's text before its first ':' or '('."""
+        return Counter(re.split(r"[:(]", reason, maxsplit=1)[0].strip() for _, reason in self.rejected)
+
+
 class SearchSpace(ABC):
-    """Configurations worth trying for one operation."""
+    """Configurations worth trying for one operation.
+
+    Subclasses give the grid, the rejection rules and (optionally) the launch
+    size and the budget priority; :meth:`generate` runs the funnel."""
 
     operation: str
 
@@ -73,6 +112,7 @@ class SearchSpace(ABC):
         """Why ``config`` is not worth trying, or None to keep it."""
 
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
+        """CTAs the launch would have; spaces that cannot say raise."""
         raise NotImplementedError
 
     def priority(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> tuple[float, ...]:
@@ -84,113 +124,83 @@ class SearchSpace(ABC):
     ) -> list[KernelConfig]:
         return self.generate(problem, caps, max_candidates=max_candidates).candidates
 
+    # ------------------------------------------------------------ the funnel
+    def _feasibility(self, problem: Problem, caps: DeviceCaps):
+        """Stage 1: every grid point, kept or rejected with its rule."""
+        kept, rejected, seen = [], [], 0
+        for config in self.grid(problem):
+            seen += 1
+            reason = self.reject_reason(config, problem, caps)
+            if reason is None:
+                kept.append(config)
+            else:
+                rejected.append((config, reason))
+        return seen, kept, rejected
+
+    def _occupancy(self, configs: list[KernelConfig], problem: Problem, caps: DeviceCaps):
+        """Stage 2: launches that fill under half the SMs go, unless no
+        feasible config fills them all (then nothing is dropped)."""
+        try:
+            sizes = [self.num_programs(c, problem) for c in configs]
+        except NotImplementedError:
+            return configs, []
+        if not sizes or max(sizes) < caps.sm_count:
+            return configs, []
+        floor = caps.sm_count // 2
+        keep = [c for c, n in zip(configs, sizes) if n >= floor]
+        drop = [(c, f"launch grid of {n} programs fills under half of {caps.sm_count} SMs")
+                for c, n in zip(configs, sizes) if n < floor]
+        return keep, drop
+
     def generate(
         self, problem: Problem, caps: DeviceCaps | None = None, *, max_candidates: int | None = None
     ) -> CandidateSet:
         if problem.operation != self.operation:
-            raise ValueError(
-                f"{type(self).__name__} handles {self.operation!r}, got {problem.operation!r}"
-            )
-        caps = caps if caps is not None else device_caps()
-        budget = max_candidates if max_candidates is not None else self.max_candidates
-        kept: list[KernelConfig] = []
-        rejected: list[tuple[KernelConfig, str]] = []
-        generated = 0
-        for config in self.grid(problem):
-            generated += 1
-            why = self.reject_reason(config, problem, caps)
-            if why is None:
-                kept.append(config)
-            else:
-                rejected.append((config, why))
-        feasible = len(kept)
-        kept, pruned = self._prune_underutilised(kept, problem, caps)
-        rejected.extend(pruned)
-        kept.sort(key=lambda c: (*self.priority(c, problem, caps), c.to_json()))
-        return CandidateSet(
-            problem=problem,
-            generated=generated,
-            feasible=feasible,
-            after_prune=len(kept),
-            budget=budget,
-            candidates=kept[:budget],
-            rejected=tuple(rejected),
-        )
-
-    def _prune_underutilised(
-        self, configs: list[KernelConfig], problem: Problem, caps: DeviceCaps
-    ) -> tuple[list[KernelConfig], list[tuple[KernelConfig, str]]]:
-        """Drop configs whose launch fills under half the SMs -- unless none can fill them all."""
-        try:
-            programs = {c: self.num_programs(c, problem) for c in configs}
-        except NotImplementedError:
-            return configs, []
-        if not programs or max(programs.values()) < caps.sm_count:
-            return configs, []
-        floor = caps.sm_count // 2
-        kept = [c for c in configs if programs[c] >= floor]
-        dropped = [
-            (c, f"launch grid of {programs[c]} programs fills under half of {caps.sm_count} SMs")
-            for c in configs
-            if programs[c] < floor
-        ]
-        return kept, dropped
+            raise ValueError(f"{type(self).__name__} handles {self.operation!r}, got {problem.operation!r}")
+        caps = caps or device_caps()
+        budget = self.max_candidates if max_candidates is None else max_candidates
+        generated, feasible, rejected = self._feasibility(problem, caps)
+        survivors, pruned = self._occupancy(feasible, problem, caps)
+        ranked = sorted(survivors, key=lambda c: (*self.priority(c, problem, caps), c.to_json()))
+        return CandidateSet(problem, generated, len(feasible), len(survivors), budget, ranked[:budget],
+                            tuple(rejected + pruned))
 
     def explain(self, problem: Problem, caps: DeviceCaps | None = None) -> str:
-        resolved = caps if caps is not None else device_caps()
-        result = self.generate(problem, resolved)
-        suffix = "" if resolved.measured else "  <- no device attached"
-        lines = [
+        caps = caps or device_caps()
+        funnel = self.generate(problem, caps)
+        note = "" if caps.measured else "  <- no device attached"
+        report = [
             problem.describe(),
-            f"  device           : {resolved.name}, {resolved.sm_count} SMs, "
-            f"{resolved.max_shared_memory_per_block // 1024} KiB shared/block{suffix}",
-            f"  grid points      : {result.generated}",
-            f"  feasible         : {result.feasible}",
-            f"  after prune      : {result.after_prune}",
-            f"  selected (budget): {len(result.candidates)} of {result.budget}",
+            f"  device           : {caps.name}, {caps.sm_count} SMs, "
+            f"{caps.max_shared_memory_per_block // 1024} KiB shared/block{note}",
+            f"  grid points      : {funnel.generated}",
+            f"  feasible         : {funnel.feasible}",
+            f"  after prune      : {funnel.after_prune}",
+            f"  selected (budget): {len(funnel.candidates)} of {funnel.budget}",
         ]
-        counts: dict[str, int] = {}
-        for _, reason in result.rejected:
-            rule = reason.split(":")[0].split("(")[0].strip()
-            counts[rule] = counts.get(rule, 0) + 1
-        if counts:
-            lines.append("  rejections by rule:")
-            lines.extend(f"    {n:>4}  {rule}" for rule, n in sorted(counts.items(), key=lambda kv: -kv[1]))
-        return "\n".join(lines)
-
-
-class CandidateSet:
-    """Candidates plus the count left after each stage."""
-
-    __slots__ = ("problem", "generated", "feasible", "after_prune", "budget", "candidates", "rejected")
-
-    def __init__(self, *, problem, generated, feasible, after_prune, budget, candidates, rejected):
-        self.problem = problem
-        self.generated = generated
-        self.feasible = feasible
-        self.after_prune = after_prune
-        self.budget = budget
-        self.candidates = candidates
-        self.rejected = rejected
-
-    def __len__(self) -> int:
-        return len(self.candidates)
-
-    def __iter__(self) -> Iterator[KernelConfig]:
-        return iter(self.candidates)
+        rules = funnel.rule_counts()
+        if rules:
+            report.append("  rejections by rule:")
+            report += [f"    {count:>4}  {rule}" for rule, count in rules.most_common()]
+        return "\n".join(report)
 
 
 # ------------------------------------------------------------------------ GEMM
 class _Sm100GemmSpace(SearchSpace):
     """tcgen05 tile grid plus the SIMT fallback tiles, shared by the GEMM operators."""
 
-    BLOCK_M = (64, 128, 256)
-    BLOCK_N = (16, 64, 128, 192, 256)
-    BLOCK_K = (32, 64, 128)
-    NUM_STAGES = (2, 3, 4, 6)
-    CLUSTERS = ((1, 1), (2, 1), (1, 2), (2, 2))
+    BLOCK_M = (128, 256)
+    BLOCK_N = (16, 64, 128, 192, 224, 256)
+    BLOCK_K = (64, 128)
+    NUM_STAGES = (2, 3, 4, 6, 8)
+    #: Tile schedules of the persistent kernel: 1 stream-K (the flattened
+    #: (tile, k-block) space split evenly over the SMs), 2 whole tiles,
+    #: 3 whole tiles with the last partial wave split into half-width tiles.
+    SCHEDULES = (1, 2, 3)
     #: L2 the A panels of one raster group may take (the library default's rule).
     GROUP_L2_BYTES = 48 << 20
+    #: Most output tiles stream-K keeps arrival counters for (gemm_tcgen05.cu).
+    STREAM_K_MAX_TILES = 16384
     #: (BLOCK_M, BLOCK_N, BLOCK_K) of the CUDA-core kernel's instantiations.
     SIMT_TILES = ((128, 128, 8), (64, 64, 16), (128, 64, 16))
     #: How B is laid out for this operator's canonical inputs.
@@ -217,43 +227,28 @@ class _Sm100GemmSpace(SearchSpace):
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
         default = self.library_default(problem)
         yield default
-        for config in self._grid(problem):
-            if config != default:
-                yield config
+        yield from (config for config in self._grid(problem) if config != default)
 
     def _grid(self, problem: Problem) -> Iterator[KernelConfig]:
         m, n, _ = self.dims(problem)
         if self.b_layout == "nk":
-            # decode shapes: 16-row weight tiles on mma.sync (BLOCK_M warps per tile,
-            # num_stages vector pairs in flight)
+            # decode shapes: 16-row weight tiles on mma.sync (BLOCK_M warps per
+            # tile, num_stages vector pairs in flight)
             for warps, pairs in gc.TILE_ROWS_SHAPES:
                 yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
         swap = 1 if gc.default_swap(m, n) else 2
-        for bm, bn, bk, stages, (cm, cn) in product(
-            self.BLOCK_M, self.BLOCK_N, self.BLOCK_K, self.NUM_STAGES, self.CLUSTERS
-        ):
-            yield KernelConfig(
-                self.operation,
-                KERNEL=gc.KERNEL_TCGEN05,
-                BLOCK_M=bm,
-                BLOCK_N=bn,
-                BLOCK_K=bk,
-                GROUP_M=self.group_m(bm, problem),
-                num_stages=stages,
-                STREAM_K=0,
-                SWAP_AB=swap,
-                CLUSTER_M=cm,
-                CLUSTER_N=cn,
-            )
+        for bm, bn, bk, stages, schedule in product(self.BLOCK_M, self.BLOCK_N, self.BLOCK_K, self.NUM_STAGES,
+                                                    self.SCHEDULES):
+            yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TCGEN05, BLOCK_M=bm, BLOCK_N=bn, BLOCK_K=bk,
+                               GROUP_M=self.group_m(bm, problem), num_stages=stages, STREAM_K=schedule,
+                               SWAP_AB=swap, CLUSTER_M=gc.cta_group(bm), CLUSTER_N=1)
         for bm, bn, bk in self.SIMT_TILES:
             yield KernelConfig(self.operation, KERNEL=gc.KERNEL_SIMT, BLOCK_M=bm, BLOCK_N=bn, BLOCK_K=bk)
 
     def kernel_view(self, config: KernelConfig, problem: Problem) -> tuple[int, int]:
         """(M', N') the kernel tiles, after an A/B swap."""
         m, n, _ = self.dims(problem)
-        if config.get("SWAP_AB", 2) == 1:
-            return n, m
-        return m, n
+        return (n, m) if config.get("SWAP_AB", 2) == 1 else (m, n)
 
     def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
@@ -264,13 +259,33 @@ class _Sm100GemmSpace(SearchSpace):
         return gc.tc_smem_bytes(config["BLOCK_N"], config["BLOCK_K"], config["num_stages"],
                                 itemsize(problem.dtype), gc.cta_group(config["BLOCK_M"]))
 
+    def output_tiles(self, config: KernelConfig, problem: Problem) -> int:
+        m_k, n_k = self.kernel_view(config, problem)
+        return ceil_div(m_k, config["BLOCK_M"]) * ceil_div(n_k, config["BLOCK_N"])
+
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
         """CTAs with work: tiles, times two for SM-pair tiles."""
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             return ceil_div(self.dims(problem)[1], 16)  # one CTA per 16 weight rows
-        m_k, n_k = self.kernel_view(config, problem)
-        tiles = ceil_div(m_k, config["BLOCK_M"]) * ceil_div(n_k, config["BLOCK_N"])
+        tiles = self.output_tiles(config, problem)
         return tiles * (gc.cta_group(config["BLOCK_M"]) if config["KERNEL"] == gc.KERNEL_TCGEN05 else 1)
+
+    def _schedule_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
+        """The tile schedules' own conditions."""
+        cg = gc.cta_group(config["BLOCK_M"])
+        tiles = self.output_tiles(config, problem)
+        schedule = config["STREAM_K"]
+        if schedule == 1 and tiles * cg > self.STREAM_K_MAX_TILES:
+            return f"stream-K: {tiles} tiles exceed the {self.STREAM_K_MAX_TILES // cg} it keeps counters for"
+        if schedule == 3:
+            bn = config["BLOCK_N"]
+            mn_major_b = self.b_layout == "kn" and config["SWAP_AB"] != 1
+            if (bn // 2) % (16 * cg) != 0 or (mn_major_b and (bn // cg // 2) % 64 != 0):
+                return f"split tail: half of BLOCK_N={bn} is not a tile the MMA and TMA boxes take"
+            units = caps.sm_count // cg
+            if tiles % units == 0 or tiles < units:
+                return f"split tail: {tiles} tiles leave no partial last wave on {units} units"
+        return None
 
     def reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
         m, n, k = self.dims(problem)
@@ -282,27 +297,15 @@ class _Sm100GemmSpace(SearchSpace):
         if why is not None:
             return why
         bm, bn, bk, stages = config["BLOCK_M"], config["BLOCK_N"], config["BLOCK_K"], config["num_stages"]
-        cluster = (config["CLUSTER_M"], config["CLUSTER_N"])
-        if bm == 64:
-            return "not implemented: BLOCK_M=64 (M=64 MMAs use a different TMEM layout)"
         cg = gc.cta_group(bm)
-        if cg == 2 and cluster != (2, 1):
-            if cluster == (1, 1):
-                return "SM pair: BLOCK_M=256 runs on a 2x1 cluster (CLUSTER_M=2)"
-            return f"not implemented: cluster {cluster[0]}x{cluster[1]} beyond the SM pair"
-        if cg == 1 and cluster != (1, 1):
-            return (f"not implemented: cluster {cluster[0]}x{cluster[1]} without the pair MMA "
-                    "(sharing tiles would need TMA multicast)")
         if bn % (16 * cg) != 0:
             return f"SM pair: BLOCK_N={bn} does not split into two 16-column halves"
         if bk * itemsize(problem.dtype) < 128:
             return f"swizzle atom: BLOCK_K={bk} is less than one 128-byte swizzle row"
         smem = self.shared_memory_bytes(config, problem)
         if smem > caps.max_shared_memory_per_block:
-            return (
-                f"shared memory: {smem // 1024} KiB of tiles exceeds the "
-                f"{caps.max_shared_memory_per_block // 1024} KiB per-block limit"
-            )
+            return (f"shared memory: {smem // 1024} KiB of tiles exceeds the "
+                    f"{caps.max_shared_memory_per_block // 1024} KiB per-block limit")
         tmem = gc.tc_tmem_columns(bn)
         if tmem > caps.tmem_columns_per_sm:
             return f"TMEM: {tmem} accumulator columns exceed {caps.tmem_columns_per_sm} per SM"
@@ -318,26 +321,30 @@ class _Sm100GemmSpace(SearchSpace):
         k_iters = ceil_div(k, bk)
         if stages > 2 and k_iters < stages:
             return f"pipeline cannot fill: {k_iters} K iterations for num_stages={stages}"
-        return None
+        return self._schedule_reason(config, problem, caps)
 
     def priority(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> tuple[float, ...]:
-        """The tile kernel first where it runs (its default shape first); then
-        tcgen05 before SIMT; then parallelism up to one wave; then reuse
-        BM*BN/(BM+BN) (operand bytes per MMA); then least padding; then the
-        deeper ring."""
+        """The library default first; the tile GEMV next where it runs (its
+        default shape first); then tcgen05 before SIMT; then parallelism up to
+        one wave; then operand reuse BM*BN/(BM+BN) (operand bytes per MMA);
+        then least padding; then the schedule the library would pick for that
+        tile before the other two; then the deeper ring."""
         if config == self.library_default(problem):
             return (-10,)
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             default = (config["BLOCK_M"], config["num_stages"]) == gc.tile_rows_default(self.dims(problem)[0])
             return (-3,) if default else (-2,)
-        kernel_rank = 0 if config["KERNEL"] == gc.KERNEL_TCGEN05 else 1
+        if config["KERNEL"] != gc.KERNEL_TCGEN05:
+            return (1,)
         m_k, n_k = self.kernel_view(config, problem)
         bm, bn = config["BLOCK_M"], config["BLOCK_N"]
         programs = min(self.num_programs(config, problem), caps.sm_count)
         reuse = bm * bn / (bm + bn)
-        padded = ceil_div(m_k, bm) * bm * ceil_div(n_k, bn) * bn
-        waste = padded / (m_k * n_k)
-        return (kernel_rank, -programs, -reuse, waste, -config.get("num_stages", 0))
+        waste = ceil_div(m_k, bm) * bm * ceil_div(n_k, bn) * bn / (m_k * n_k)
+        cg = gc.cta_group(bm)
+        tiles = self.output_tiles(config, problem)
+        natural = 1 if (cg == 1 and tiles < caps.sm_count) else 3
+        return (0, -programs, -reuse, waste, 0 if config["STREAM_K"] == natural else 1, -config["num_stages"])
 
 
 class MatmulSearchSpace(_Sm100GemmSpace):

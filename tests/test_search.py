@@ -28,9 +28,10 @@ FUSED = Problem.create("fused_linear_erf", "bf16", M=4096, N=11008, K=4096)
 
 
 def tc(op="matmul", **kw):
-    base = dict(KERNEL=1, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64, GROUP_M=8, num_stages=4, STREAM_K=0,
-                SWAP_AB=2, CLUSTER_M=1, CLUSTER_N=1)
+    base = dict(KERNEL=1, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64, GROUP_M=8, num_stages=4, STREAM_K=2,
+                SWAP_AB=2, CLUSTER_N=1)
     base.update(kw)
+    base.setdefault("CLUSTER_M", 2 if base["BLOCK_M"] == 256 else 1)
     return KernelConfig(op, **base)
 
 
@@ -41,7 +42,8 @@ def test_next_power_of_2(n, expected):
 
 def test_grid_size_and_budget(b200_caps):
     result = MatmulSearchSpace().generate(GEMM, b200_caps)
-    assert result.generated == 1 + 3 * 5 * 3 * 4 * 4 + 3  # library default + tcgen05 grid + SIMT tiles
+    # tcgen05 grid (2 x 6 x 2 x 5 x 3) + SIMT tiles; the library default is one of them here
+    assert result.generated == 2 * 6 * 2 * 5 * 3 + 3
     default = MatmulSearchSpace().library_default(GEMM)
     assert result.candidates[0] == default, "the library default is always measured, first"
     assert 0 < result.feasible < result.generated
@@ -71,18 +73,35 @@ def test_sm_pair_tiles_are_feasible_and_sized_per_cta(b200_caps):
     [
         (tc(BLOCK_N=256, BLOCK_K=64, num_stages=6), "shared memory"),
         (tc(BLOCK_K=32), "swizzle atom"),
-        (tc(BLOCK_M=256), "SM pair"),
-        (tc(BLOCK_M=64), "not implemented"),
-        (tc(CLUSTER_M=2), "not implemented"),
-        (tc(BLOCK_M=256, CLUSTER_M=2, CLUSTER_N=2), "not implemented"),
-        (tc(BLOCK_M=256, CLUSTER_M=2, BLOCK_N=192), "MN-major B"),
+        (tc(BLOCK_M=256, BLOCK_N=16), "SM pair"),
+        (tc(BLOCK_M=256, BLOCK_N=192), "MN-major B"),
         (tc(BLOCK_N=16), "MN-major B"),  # matmul's B is row-major (K, N)
         (tc(BLOCK_N=256, num_stages=6, BLOCK_K=128), "shared memory"),
+        (tc(BLOCK_M=256, BLOCK_N=128, STREAM_K=3), "split tail"),  # 64-column halves of a pair tile
     ],
 )
 def test_each_rule_rejects_its_config(config, rule, b200_caps):
     reason = MatmulSearchSpace().reject_reason(config, GEMM, b200_caps)
     assert reason is not None and reason.startswith(rule), reason
+
+
+def test_schedule_rules(b200_caps):
+    """Every point of the grid is a schedule the kernel runs: the split tail
+    only where the last wave is partial, stream-K only within its counters."""
+    space = FusedLinearErfSearchSpace()
+    whole_waves = Problem.create("fused_linear_erf", "bf16", M=128 * 148, N=256, K=1024)  # 148 one-SM tiles
+    reason = space.reject_reason(tc("fused_linear_erf", STREAM_K=3, BLOCK_N=256), whole_waves, b200_caps)
+    assert reason is not None and "no partial last wave" in reason
+    assert space.reject_reason(tc("fused_linear_erf", STREAM_K=2, BLOCK_N=256), whole_waves, b200_caps) is None
+    huge = Problem.create("fused_linear_erf", "bf16", M=65536, N=65536, K=1024)
+    reason = space.reject_reason(tc("fused_linear_erf", STREAM_K=1, BLOCK_N=128), huge, b200_caps)
+    assert reason is not None and reason.startswith("stream-K")
+    # no cluster shape, M=64 tile or other point the kernels cannot run is left in the grid
+    for config in space.grid(FUSED):
+        if config["KERNEL"] == gc.KERNEL_TCGEN05:
+            assert config["BLOCK_M"] in (128, 256) and config["CLUSTER_N"] == 1
+            assert config["CLUSTER_M"] == (2 if config["BLOCK_M"] == 256 else 1)
+            assert config["STREAM_K"] in (1, 2, 3)
 
 
 def test_tmem_budget_is_a_device_property(b200_caps, a100_caps):
