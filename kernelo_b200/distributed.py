@@ -5,13 +5,15 @@ Three shardings, each where the work splits naturally:
 * :class:`ShardedFusedLinear` -- the fused linear is column-sharded by N: rank r
   holds rows [r*chunk, (r+1)*chunk) of the [N, K] weight and of the bias and
   computes its [M, chunk] slice of ``gelu(x @ W^T + b)`` with the native
-  kernel. With ``gather="fused"`` (``"auto"``, the default, on CUDA) the kernel's epilogue
+  kernel. With ``gather="fused"`` the kernel's epilogue
   stores every output tile into all ranks' copies of Y over NVLink (peer
   pointers, mapped by CUDA IPC, into double-buffered copies) and a bounded cross-GPU
   barrier kernel publishes completion: no collective, no copy, and the
   transfer overlaps the math tile by tile. ``gather="nccl"`` (and ``"auto"``
   off CUDA) exchanges the slices with one ``all_gather_into_tensor`` of the
-  group's backend and permutes them into [M, N]. N is padded to ``world * chunk`` with zero weight rows (their
+  group's backend and permutes them into [M, N]. ``gather="auto"`` (the
+  default) on CUDA times both on the first call of each M and keeps the
+  faster, by the slowest rank's time, so every rank picks the same. N is padded to ``world * chunk`` with zero weight rows (their
   columns are dropped).
 * :class:`ShardedGemv` -- the decode GEMV ``x @ W^T`` sharded the same way:
   each rank streams 1/world of the weight (the HBM-bound part) through the
@@ -125,6 +127,9 @@ class ShardedFusedLinear:
                     b[: stop - start].copy_(bias[start:stop])
             self.w, self.b = w, b
         self._gather_buf: torch.Tensor | None = None
+        self._auto: dict[int, str] = {}  # M -> the gather "auto" chose
+        #: M -> {"fused": ms, "nccl": ms}, the measurements behind each choice
+        self.gather_timings: dict[int, dict[str, float]] = {}
 
     def _epilogue(self) -> int:
         from kernelo_b200.runtime import native
@@ -136,12 +141,51 @@ class ShardedFusedLinear:
         return fused_linear_gelu(x, self.w.t(), self.b, approximate=self.approximate,
                                  config=self.config, out=out)
 
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+    def gather_mode(self, x: torch.Tensor) -> str:
+        """"fused" or "nccl": fixed by ``gather``, or for ``"auto"`` on CUDA the
+        faster of the two for this M, measured once (collective: every rank
+        calls it with the same M)."""
+        if self.gather != "auto":
+            return self.gather
+        if not x.is_cuda:
+            return "nccl"
         m = x.shape[0]
+        if m not in self._auto:
+            self._auto[m] = self._measure_gathers(x)
+        return self._auto[m]
+
+    def _measure_gathers(self, x: torch.Tensor, calls: int = 3) -> str:
+        """Median-free and cheap: one untimed call of each mode, then ``calls``
+        timed back to back; each mode's time is the slowest rank's."""
+        stream = torch.cuda.current_stream(x.device)
+        spent = {}
+        for mode in ("fused", "nccl"):
+            run = self.fused_step if mode == "fused" else self.nccl_step
+            run(x)
+            torch.cuda.synchronize(x.device)
+            dist.barrier(group=self.group)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for _ in range(calls):
+                run(x)
+            end.record(stream)
+            end.synchronize()
+            t = torch.tensor([start.elapsed_time(end)], device=x.device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            spent[mode] = float(t.item())
+        self.gather_timings[x.shape[0]] = spent
+        return min(spent, key=spent.get)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return self.local(x)[:, : self.n]
-        if self.gather == "fused" or (self.gather == "auto" and x.is_cuda):
+        if self.gather_mode(x) == "fused":
             return self.fused_step(x)
+        return self.nccl_step(x)
+
+    def nccl_step(self, x: torch.Tensor) -> torch.Tensor:
+        """The local GEMM, then one all-gather of the group's backend and a permute into [M, N]."""
+        m = x.shape[0]
         if self._gather_buf is None or self._gather_buf.shape != (self.world, m, self.chunk):
             self._gather_buf = torch.empty(self.world, m, self.chunk, device=x.device, dtype=x.dtype)
         mine = self._gather_buf[self.rank]
@@ -309,10 +353,11 @@ class ShardedGemv(ShardedFusedLinear):
     HBM traffic that bounds the single-GPU GEMV -- through the 16-row tile
     kernel for up to 32 rows of x (the tcgen05 GEMM above that, up to the
     GEMV operator's 256 rows).
-    With ``gather="fused"`` (``"auto"`` on CUDA) that kernel's stores also
-    write every peer's copy of Y and the bounded barrier publishes it; at
-    M = 16, N = 11008 the whole gathered Y is 352 KB. ``gather="nccl"`` runs
-    :func:`kernelo_b200.kernels.gemv.gemv` locally and all-gathers the slices.
+    With ``gather="fused"`` that kernel's stores also write every peer's copy
+    of Y and the bounded barrier publishes it; at M = 16, N = 11008 the whole
+    gathered Y is 352 KB. ``gather="nccl"`` runs
+    :func:`kernelo_b200.kernels.gemv.gemv` locally and all-gathers the slices;
+    ``"auto"`` measures both on the first call of each M and keeps the faster.
     ``forward_host`` and ``close`` behave as for the fused linear.
 
     The reference has no dedicated GEMV and no multi-GPU code: single-GPU
