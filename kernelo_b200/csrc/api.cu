@@ -184,6 +184,70 @@ using namespace kf;
 
 namespace {
 
+// ---- packed tcgen05 path --------------------------------------------------
+// fp16/bf16 operands a TMA tensor map cannot describe (a row pitch or base off
+// the 16-byte grid: K = 4099, N = 2053, a view starting at an odd column; or
+// K < 8) are copied into the caller's workspace as pitched matrices and the
+// tcgen05 kernel runs on the copies (pack.cu). Workspace layout:
+//   [stream-K region, at least its 64 KiB of counters | packed A | packed B]
+// so the counters a later stream-K call relies on are never overwritten.
+struct PackPlan {
+  bool on = false;
+  bool pack_a = false, pack_b = false;
+  PackedOperand a, b;
+  GemmArgs view;  // the problem as the kernel sees it (packed operands' strides)
+};
+
+// Packing pays where the GEMM is compute-bound: both M and N above 64 (a
+// skinny problem keeps the CUDA-core kernel, which reads its operands in
+// place), or when tcgen05 is asked for explicitly.
+bool packing_applies(const GemmArgs& g, const kf_gemm_config* user) {
+  if (g.dtype == KF_FP32 || g.n_peers > 0 || g.K == 0) return false;
+  const int kernel = user ? user->kernel : KF_GEMM_AUTO;
+  if (kernel != KF_GEMM_AUTO && kernel != KF_GEMM_TCGEN05) return false;
+  if (tcgen05_operands_ok(g, nullptr)) return false;
+  return kernel == KF_GEMM_TCGEN05 || (g.M > 64 && g.N > 64);
+}
+
+PackPlan plan_packing(const GemmArgs& g) {
+  PackPlan plan;
+  plan.on = true;
+  plan.view = g;
+  // K below one 16-byte vector is padded with zeros to 8: then both operands
+  // need the padded extent, so both are copied.
+  const int64_t kp = g.K < 8 ? 8 : g.K;
+  plan.pack_a = kp != g.K || !tma_describable(g.a, g.sa_m, g.sa_k, g.M, g.K);
+  plan.pack_b = kp != g.K || !tma_describable(g.b, g.sb_n, g.sb_k, g.N, g.K);
+  // Stand-in aligned pointers until the workspace is known: only strides and
+  // sizes decide the config.
+  const void* stand_in = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  if (plan.pack_a) {
+    plan.a = plan_pack(g.a, g.sa_m, g.sa_k, g.M, g.K, kp);
+    plan.view.a = stand_in;
+    plan.view.sa_m = plan.a.k_inner ? plan.a.pitch : 1;
+    plan.view.sa_k = plan.a.k_inner ? 1 : plan.a.pitch;
+  }
+  if (plan.pack_b) {
+    plan.b = plan_pack(g.b, g.sb_n, g.sb_k, g.N, g.K, kp);
+    plan.view.b = stand_in;
+    plan.view.sb_n = plan.b.k_inner ? plan.b.pitch : 1;
+    plan.view.sb_k = plan.b.k_inner ? 1 : plan.b.pitch;
+  }
+  plan.view.K = kp;
+  return plan;
+}
+
+int64_t packed_bytes(const PackPlan& plan) {
+  return (plan.pack_a ? plan.a.bytes : 0) + (plan.pack_b ? plan.b.bytes : 0);
+}
+
+// Offset of the packed copies: after the stream-K region, never inside the
+// stream-K counters.
+int64_t pack_offset(int64_t stream_k_bytes) {
+  const int64_t sk = (stream_k_bytes + 255) / 256 * 256;
+  return sk > SK_COUNTER_BYTES ? sk : SK_COUNTER_BYTES;
+}
+
 int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
   if (!valid_dtype(g.dtype)) return set_error(KF_ERR_INVALID_ARGUMENT, "unknown dtype code");
   if (g.M < 0 || g.N < 0 || g.K < 0) return set_error(KF_ERR_INVALID_ARGUMENT, "negative size");
@@ -221,8 +285,43 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
   DeviceInfo* dev = nullptr;
   rc = device_info(device, &dev);
   if (rc != KF_OK) return rc;
-  kf_gemm_config cfg = resolve_gemm_config(g, user, dev->sm_count);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (packing_applies(g, user)) {
+    PackPlan plan = plan_packing(g);
+    GemmArgs& v = plan.view;
+    kf_gemm_config cfg = resolve_gemm_config(v, user, dev->sm_count);
+    int64_t sk = cfg.stream_k == 1 ? gemm_tcgen05_workspace_bytes(v, cfg, *dev) : 0;
+    const int64_t have = g.workspace != nullptr ? g.workspace_bytes : 0;
+    if (sk > 0 && pack_offset(sk) + packed_bytes(plan) > have && (user == nullptr || user->stream_k == 0)) {
+      cfg.stream_k = 2;  // the library's stream-K choice gives way to packing: whole tiles
+      sk = 0;
+    }
+    const int64_t need = pack_offset(sk) + packed_bytes(plan);
+    if (need <= have) {
+      char* base = static_cast<char*>(g.workspace);
+      char* dst = base + pack_offset(sk);
+      if (plan.pack_a) {
+        rc = launch_pack(plan.a, dst, s);
+        if (rc != KF_OK) return rc;
+        v.a = dst;
+        dst += plan.a.bytes;
+      }
+      if (plan.pack_b) {
+        rc = launch_pack(plan.b, dst, s);
+        if (rc != KF_OK) return rc;
+        v.b = dst;
+      }
+      v.workspace = sk > 0 ? g.workspace : nullptr;
+      v.workspace_bytes = sk;
+      return launch_gemm_tcgen05(v, cfg, *dev, s);
+    }
+    if (user != nullptr && user->kernel == KF_GEMM_TCGEN05)
+      return set_error(KF_ERR_WORKSPACE, "operands TMA cannot describe are packed first: this call needs " +
+                                             std::to_string(need) + " bytes of workspace, got " +
+                                             std::to_string(have));
+    // no room to pack: the CUDA-core kernel reads the operands in place
+  }
+  kf_gemm_config cfg = resolve_gemm_config(g, user, dev->sm_count);
   if (cfg.kernel == KF_GEMM_TCGEN05 && (user == nullptr || user->stream_k == 0)) {
     const int64_t need = gemm_tcgen05_workspace_bytes(g, cfg, *dev);
     if (need > 0 && (g.workspace == nullptr || g.workspace_bytes < need)) {
@@ -459,6 +558,14 @@ int64_t kf_gemm_workspace_bytes(int32_t device, int32_t dtype, int64_t sa_m, int
   g.sb_n = sb_n;
   // Any 16-byte-aligned stand-in: only strides and sizes decide the config.
   g.a = g.b = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  if (packing_applies(g, cfg)) {
+    // Packed copies after the stream-K region (see gemm_common).
+    const PackPlan plan = plan_packing(g);
+    const kf_gemm_config c = resolve_gemm_config(plan.view, cfg, dev->sm_count);
+    const int64_t sk = c.stream_k == 1 ? gemm_tcgen05_workspace_bytes(plan.view, c, *dev) : 0;
+    if (sk < 0) return sk;
+    return pack_offset(sk) + packed_bytes(plan);
+  }
   const kf_gemm_config c = resolve_gemm_config(g, cfg, dev->sm_count);
   if (c.kernel != KF_GEMM_TCGEN05) return 0;
   return gemm_tcgen05_workspace_bytes(g, c, *dev);

@@ -968,6 +968,10 @@ int validate_config(const kf_gemm_config& cfg, int b_mn, std::string* why) {
 
 }  // namespace
 
+bool tma_describable(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int64_t k) {
+  return operand_major(ptr, s_mn, s_k, mn, k) >= 0;
+}
+
 bool tcgen05_operands_ok(const GemmArgs& g, std::string* why) {
   if (g.dtype != KF_FP16 && g.dtype != KF_BF16) {
     if (why) *why = "tcgen05 kind::f16 path takes fp16/bf16 only";

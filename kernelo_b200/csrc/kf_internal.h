@@ -65,6 +65,27 @@ int query_tcgen05_config(int dtype, const kf_gemm_config& cfg, int64_t* smem_byt
                          int32_t* tmem_cols);
 // Whether the operands can take the tcgen05 path (TMA strides/alignment).
 bool tcgen05_operands_ok(const GemmArgs& args, std::string* why);
+// Whether one operand (element strides along its M/N and K extents) can be
+// described by a TMA tensor map: 16-byte base, unit stride along K or M/N,
+// the other stride a multiple of 8 elements, K >= 8.
+bool tma_describable(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int64_t k);
+
+// Operand packing (pack.cu): a 16-bit operand TMA cannot describe, copied
+// into the workspace as a pitched matrix the tcgen05 kernel can read.
+struct PackedOperand {
+  bool k_inner = true;      // K is the copy's inner (unit-stride) dimension
+  int64_t outer = 0;        // rows of the copy (the padded K when MN is inner)
+  int64_t src_outer = 0;    // rows that exist in the source
+  int64_t len = 0;          // elements per source row
+  int64_t pitch = 0;        // elements per row of the copy (a multiple of 8)
+  int64_t bytes = 0;        // size of the copy, 256-byte rounded
+  const void* src = nullptr;
+  int64_t s_outer = 0, s_inner = 0;
+};
+// The copy of an operand with element strides (s_mn, s_k) and extents
+// (mn, k); K is padded with zero rows/columns to k_padded (>= k).
+PackedOperand plan_pack(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int64_t k, int64_t k_padded);
+int launch_pack(const PackedOperand& p, void* dst, cudaStream_t stream);
 
 // CUDA-core path: any strides, fp16/bf16/fp32.
 int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream_t stream);

@@ -5,7 +5,8 @@ that configs can be stated explicitly (cached, ranked, filtered):
 
 * whether an operand can be described by a TMA tensor map (16-byte aligned
   base, unit stride along K or along M/N, the other stride a multiple of 16
-  bytes) -- otherwise only the SIMT kernel can take the problem;
+  bytes) -- otherwise a 16-bit problem that is not skinny is packed into the
+  workspace for tcgen05, and the rest go to the SIMT kernel;
 * the default tcgen05 tile for a shape: 256-row SM-pair tiles when they fill
   the machine (else 128-row), BLOCK_N up to 256, A/B swapped for skinny M (the
   weight becomes the 128-row operand), all stream-K when whole tiles would
@@ -111,14 +112,13 @@ def operand_major(t: torch.Tensor, mn_dim: int, k_dim: int) -> int:
     return -1
 
 
-def shape_allows_tcgen05(m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str) -> str | None:
-    """Why contiguous operands of this shape cannot take the tcgen05 path, or None.
+def tma_misfit(m: int, n: int, k: int, *, b_layout: str) -> str | None:
+    """Why contiguous operands of this shape cannot be TMA tensor maps as they
+    are (mirrors operand_major in gemm_tcgen05.cu), or None.
 
     ``b_layout`` is ``"kn"`` for a row-major (K, N) B (matmul) and ``"nk"`` for
     an nn.Linear-style [N, K] weight.
     """
-    if dtype not in (torch.float16, torch.bfloat16):
-        return "tcgen05 kind::f16 takes fp16/bf16 operands only"
     if k < 8:
         return f"TMA alignment: K={k} is below one 16-byte vector"
     if m > 1 and k % 8 != 0:
@@ -127,6 +127,23 @@ def shape_allows_tcgen05(m: int, n: int, k: int, dtype: torch.dtype, *, b_layout
         return f"TMA alignment: B row stride N={n} is not a multiple of 16 bytes"
     if b_layout == "nk" and n > 1 and k % 8 != 0:
         return f"TMA alignment: W row stride K={k} is not a multiple of 16 bytes"
+    return None
+
+
+def packs_by_default(m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str) -> bool:
+    """Whether the library packs this problem's operands for tcgen05 on its own
+    (mirrors packing_applies in api.cu): 16-bit operands TMA cannot describe,
+    in a problem that is not skinny (M and N above 64)."""
+    return (dtype in (torch.float16, torch.bfloat16) and k > 0 and m > 64 and n > 64
+            and tma_misfit(m, n, k, b_layout=b_layout) is not None)
+
+
+def shape_allows_tcgen05(m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str) -> str | None:
+    """Why operands of this shape cannot take the tcgen05 path, or None. Any
+    16-bit layout can: operands TMA cannot describe are first packed into the
+    workspace as pitched copies (csrc/pack.cu)."""
+    if dtype not in (torch.float16, torch.bfloat16):
+        return "tcgen05 kind::f16 takes fp16/bf16 operands only"
     return None
 
 
@@ -191,6 +208,10 @@ def default_gemm_config(
     if b_layout == "nk" and tile_rows_reject(m, k, dtype) is None:
         warps, pairs = tile_rows_default(m)
         return KernelConfig(operation, KERNEL=KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
-    if shape_allows_tcgen05(m, n, k, dtype, b_layout=b_layout) is None:
+    if dtype in (torch.float16, torch.bfloat16) and tma_misfit(m, n, k, b_layout=b_layout) is None:
         return default_tcgen05_config(operation, m, n, k, b_layout=b_layout, sm_count=sm_count)
+    if packs_by_default(m, n, k, dtype, b_layout=b_layout):
+        # the packed copies keep each operand's unit-stride dimension innermost,
+        # with K padded to at least 8
+        return default_tcgen05_config(operation, m, n, max(k, 8), b_layout=b_layout, sm_count=sm_count)
     return default_simt_config(operation, m, n, sm_count=sm_count)

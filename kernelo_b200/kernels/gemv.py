@@ -81,9 +81,10 @@ def default_config(m: int, n: int, k: int, dtype: torch.dtype, *, sm_count: int 
         return KernelConfig("gemv", KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
     if 1 <= m <= gc.WARP_ROWS_AUTO_MAX_M and gc.warp_rows_smem_bytes(m, k, itemsize(dtype)) <= gc.SM100_SMEM_PER_BLOCK:
         return KernelConfig("gemv", KERNEL=gc.KERNEL_WARP_ROWS)
-    if gc.shape_allows_tcgen05(m, n, k, dtype, b_layout="nk") is not None:
+    aligned = dtype in (torch.float16, torch.bfloat16) and gc.tma_misfit(m, n, k, b_layout="nk") is None
+    if not aligned and not gc.packs_by_default(m, n, k, dtype, b_layout="nk"):
         return gc.default_simt_config("gemv", m, n, sm_count=sm_count)
-    cfg = gc.default_tcgen05_config("gemv", m, n, k, b_layout="nk", sm_count=sm_count)
+    cfg = gc.default_tcgen05_config("gemv", m, n, max(k, 8), b_layout="nk", sm_count=sm_count)
     # Always swap and split K: the weight streams through every SM.
     return cfg.replace(SWAP_AB=1, STREAM_K=1)
 

@@ -142,9 +142,44 @@ def test_infeasible_config_raises_out_of_resources(device):
     a, b = operands(64, 72, 64, torch.float16, device)  # K=72 is fine, N=64 is fine
     with pytest.raises(native.OutOfResources):
         matmul(a, b, config=tc(BLOCK_N=256, BLOCK_K=64, num_stages=8))  # 384 KiB of smem
-    c, d = operands(64, 509, 64, torch.float16, device)  # K=509: no TMA description
+    c, d = operands(64, 512, 64, torch.float32, device)  # fp32 has no tcgen05 MMA
     with pytest.raises(native.OutOfResources):
         matmul(c, d, config=tc())
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+@pytest.mark.parametrize(
+    "case",
+    ["k509", "n2053", "k3", "odd_base", "transposed_odd", "gather"],
+)
+def test_unaligned_operands_are_packed_for_tcgen05(case, dtype, device):
+    """Operands a TMA tensor map cannot describe -- an odd row pitch along K or
+    N, K below one 16-byte vector, a view starting at an odd column, a
+    transposed view with an odd pitch, no unit stride at all -- are copied into
+    the workspace as pitched matrices and run on tcgen05, by default (M and N
+    above 64) and when tcgen05 is asked for at a skinny shape."""
+    gen = torch.Generator().manual_seed(7)
+
+    def rnd(*shape):
+        return torch.randn(*shape, generator=gen).to(dtype).to(device)
+
+    if case == "k509":
+        a, b = rnd(300, 509), rnd(509, 320)
+    elif case == "n2053":
+        a, b = rnd(257, 512), rnd(512, 2053)
+    elif case == "k3":
+        a, b = rnd(130, 3), rnd(3, 200)
+    elif case == "odd_base":
+        a, b = rnd(200, 513)[:, 1:], rnd(512, 264)[:, 3:259]
+    elif case == "transposed_odd":
+        a, b = rnd(509, 200).t(), rnd(330, 509).t()  # M-major A, K-major B, odd pitches
+    else:
+        a, b = rnd(400, 300)[::2, ::2], rnd(300, 260)[::2, ::2]  # no unit stride anywhere
+    expected = ref.matmul_ref(host(a), host(b))
+    out = matmul(a, b)
+    gate(expected, out, dtype, context=f"{case} default")
+    explicit = tc(BLOCK_N=128, num_stages=3, STREAM_K=2)  # (an N-contiguous B stays MN-major: 64-col boxes)
+    gate(expected[:16], matmul(a[:16], b, config=explicit), dtype, context=f"{case} explicit, skinny")
 
 
 # ------------------------------------------------------------------ fused linear

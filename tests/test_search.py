@@ -113,16 +113,23 @@ def test_tmem_budget_is_a_device_property(b200_caps, a100_caps):
     assert reason is not None and ("TMEM" in reason or "shared memory" in reason)
 
 
-def test_fp32_and_unaligned_shapes_fall_back_to_simt(b200_caps):
-    for problem in (
-        Problem.create("matmul", "fp32", M=4099, N=4099, K=4099),
-        Problem.create("matmul", "fp16", M=4099, N=4099, K=4099),
-        Problem.create("matmul", "bf16", M=1021, N=2053, K=509),
-    ):
+def test_fp32_falls_back_to_simt_and_unaligned_16bit_packs(b200_caps):
+    """fp32 has no tcgen05 path; 16-bit operands TMA cannot describe (the prime
+    sweep shapes) are packed for tcgen05, which becomes the library default."""
+    fp32 = Problem.create("matmul", "fp32", M=4099, N=4099, K=4099)
+    cands = MatmulSearchSpace().candidates(fp32, b200_caps)
+    assert cands and all(c["KERNEL"] == gc.KERNEL_SIMT for c in cands)
+    reasons = {r for _, r in MatmulSearchSpace().generate(fp32, b200_caps).rejected}
+    assert any(r.startswith("tcgen05 kind") for r in reasons)
+    for problem in (Problem.create("matmul", "fp16", M=4099, N=4099, K=4099),
+                    Problem.create("matmul", "bf16", M=1021, N=2053, K=509)):
         cands = MatmulSearchSpace().candidates(problem, b200_caps)
-        assert cands and all(c["KERNEL"] == gc.KERNEL_SIMT for c in cands)
-        reasons = {r for _, r in MatmulSearchSpace().generate(problem, b200_caps).rejected}
-        assert any(r.startswith(("tcgen05 kind", "TMA alignment")) for r in reasons)
+        assert cands[0]["KERNEL"] == gc.KERNEL_TCGEN05, "packed tcgen05 is the library default"
+        assert any(c["KERNEL"] == gc.KERNEL_SIMT for c in MatmulSearchSpace().grid(problem))
+    skinny = Problem.create("matmul", "fp16", M=16, N=2053, K=509)  # skinny: no copy by default
+    assert MatmulSearchSpace().library_default(skinny)["KERNEL"] == gc.KERNEL_SIMT
+    assert gc.packs_by_default(4099, 4099, 4099, torch.float16, b_layout="kn")
+    assert not gc.packs_by_default(4096, 4096, 4096, torch.float16, b_layout="kn")
 
 
 @pytest.mark.parametrize("m", [1, 4, 16])
