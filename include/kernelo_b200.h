@@ -75,13 +75,20 @@ enum kf_gemm_kernel {
   KF_GEMM_SIMT = 2,    /* CUDA-core FFMA, any strides, fp16/bf16/fp32        */
   KF_GEMM_WARP_ROWS = 3, /* kf_gemv only: a warp per K-contiguous weight row,
                            M <= 4, packed fp32x2 FMA; num_ctas = grid size   */
-  KF_GEMM_TILE_ROWS = 4  /* a CTA per 16 K-contiguous weight rows (B's columns),
+  KF_GEMM_TILE_ROWS = 4, /* a CTA per 16 K-contiguous weight rows (B's columns),
                            M <= 32, fp16/bf16, K % 8 == 0; the weight registers
                            feed mma.sync.m16n8k16 directly; block_m = warps
                            per tile (K slices), stages = 16-byte vector pairs
                            per lane in flight. kf_gemv, and kf_gemm /
                            kf_linear_bias_act (epilogue included); AUTO picks
                            it for such shapes                               */
+  KF_GEMM_COLUMNS = 5    /* a lane per 16-byte vector of an N-contiguous B's
+                           columns (the row-major (K, N) operand), M <= 8,
+                           any dtype; K split over CTAs, the last arrival per
+                           column strip adds the partials in a fixed order
+                           (workspace from kf_gemm_workspace_bytes; without
+                           it, one CTA per strip). AUTO picks it for such
+                           shapes; epilogue included                        */
 };
 
 /* Tunable GEMM parameters. Replaces KernelConfig's BLOCK_M/BLOCK_N/BLOCK_K/
@@ -207,10 +214,26 @@ KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t sx_m, int64
 
 /* Workspace bytes a kf_gemm / kf_linear_bias_act (resp. kf_gemv) call with
  * these strides, sizes and config needs on `device` (0 when none; negative
- * status on error). Operand pointers are assumed 16-byte aligned. */
+ * status on error). Operand pointers are assumed 16-byte aligned and C
+ * contiguous. The workspace holds the stream-K counters and partial tiles,
+ * the column GEMV's partial sums, the packed copies of fp16/bf16 operands
+ * that a TMA tensor map cannot describe (an odd row pitch or K < 8) and the
+ * staged copy of an output whose rows are off the 16-byte grid, these copies
+ * after the first 64 KiB. */
 KF_API int64_t kf_gemm_workspace_bytes(int32_t device, int32_t dtype, int64_t sa_m, int64_t sa_k,
                                 int64_t sb_k, int64_t sb_n, int64_t M, int64_t N, int64_t K,
                                 const kf_gemm_config* cfg);
+/* kf_gemm_workspace_bytes for these operands and output: an operand whose base
+ * is off the 16-byte grid (a view starting at an odd column) is packed too,
+ * and an output whose rows are off the 16-byte grid (an odd N) is written to
+ * a staged copy first; both are sized for. kf_gemm_workspace_bytes assumes
+ * aligned bases and a contiguous C. The ctypes layer behind kernelforge's
+ * matmul / fused_linear_gelu wrappers (kernels/matmul.py:132-155,
+ * fused_linear.py:112-157) sizes every workspace with it. */
+KF_API int64_t kf_gemm_workspace_bytes_for(int32_t device, int32_t dtype, const void* a, int64_t sa_m,
+                                           int64_t sa_k, const void* b, int64_t sb_k, int64_t sb_n, void* c,
+                                           int64_t sc_m, int64_t sc_n, int64_t M, int64_t N, int64_t K,
+                                           const kf_gemm_config* cfg);
 KF_API int64_t kf_gemv_workspace_bytes(int32_t device, int32_t dtype, int64_t sx_m, int64_t sx_k,
                                 int64_t sw_n, int64_t sw_k, int64_t M, int64_t N, int64_t K,
                                 const kf_gemm_config* cfg);

@@ -184,18 +184,29 @@ using namespace kf;
 
 namespace {
 
-// ---- packed tcgen05 path --------------------------------------------------
+// ---- the tcgen05 path's workspace plan ------------------------------------
 // fp16/bf16 operands a TMA tensor map cannot describe (a row pitch or base off
 // the 16-byte grid: K = 4099, N = 2053, a view starting at an odd column; or
 // K < 8) are copied into the caller's workspace as pitched matrices and the
-// tcgen05 kernel runs on the copies (pack.cu). Workspace layout:
-//   [stream-K region, at least its 64 KiB of counters | packed A | packed B]
+// tcgen05 kernel runs on the copies (pack.cu). An output whose rows are off
+// the 16-byte grid is written to a pitched copy with vector stores and moved
+// to C by one copy kernel. Workspace layout:
+//   [stream-K region, at least its 64 KiB of counters | packed A | packed B | staged C]
 // so the counters a later stream-K call relies on are never overwritten.
-struct PackPlan {
-  bool on = false;
-  bool pack_a = false, pack_b = false;
-  PackedOperand a, b;
+struct TcPlan {
+  bool pack_a = false, pack_b = false, stage_c = false;
+  PackedOperand a, b, c;
   GemmArgs view;  // the problem as the kernel sees it (packed operands' strides)
+  kf_gemm_config cfg{};
+  int64_t sk = 0;  // stream-K bytes
+  int64_t offset() const {
+    const int64_t r = (sk + 255) / 256 * 256;
+    return r > SK_COUNTER_BYTES ? r : SK_COUNTER_BYTES;
+  }
+  int64_t staging_bytes() const {
+    return (pack_a ? a.bytes : 0) + (pack_b ? b.bytes : 0) + (stage_c ? c.bytes : 0);
+  }
+  int64_t need() const { return staging_bytes() > 0 ? offset() + staging_bytes() : sk; }
 };
 
 // Packing pays where the GEMM is compute-bound: both M and N above 64 (a
@@ -209,43 +220,58 @@ bool packing_applies(const GemmArgs& g, const kf_gemm_config* user) {
   return kernel == KF_GEMM_TCGEN05 || (g.M > 64 && g.N > 64);
 }
 
-PackPlan plan_packing(const GemmArgs& g) {
-  PackPlan plan;
-  plan.on = true;
-  plan.view = g;
-  // K below one 16-byte vector is padded with zeros to 8: then both operands
-  // need the padded extent, so both are copied.
-  const int64_t kp = g.K < 8 ? 8 : g.K;
-  plan.pack_a = kp != g.K || !tma_describable(g.a, g.sa_m, g.sa_k, g.M, g.K);
-  plan.pack_b = kp != g.K || !tma_describable(g.b, g.sb_n, g.sb_k, g.N, g.K);
-  // Stand-in aligned pointers until the workspace is known: only strides and
-  // sizes decide the config.
-  const void* stand_in = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
-  if (plan.pack_a) {
-    plan.a = plan_pack(g.a, g.sa_m, g.sa_k, g.M, g.K, kp);
-    plan.view.a = stand_in;
-    plan.view.sa_m = plan.a.k_inner ? plan.a.pitch : 1;
-    plan.view.sa_k = plan.a.k_inner ? 1 : plan.a.pitch;
-  }
-  if (plan.pack_b) {
-    plan.b = plan_pack(g.b, g.sb_n, g.sb_k, g.N, g.K, kp);
-    plan.view.b = stand_in;
-    plan.view.sb_n = plan.b.k_inner ? plan.b.pitch : 1;
-    plan.view.sb_k = plan.b.k_inner ? 1 : plan.b.pitch;
-  }
-  plan.view.K = kp;
-  return plan;
+// Whether the epilogue's 16-byte stores cannot reach C: its rows are off the
+// 16-byte grid (an odd N, a view starting at an odd column). Swapped (skinny)
+// tiles write C's columns and keep their element stores.
+bool output_needs_stage(const GemmArgs& v, const kf_gemm_config& cfg) {
+  if (v.dtype == KF_FP32 || v.n_peers > 0 || cfg.swap_ab == 1 || v.M <= 64 || v.N < 16) return false;
+  return !(v.sc_n == 1 && (v.sc_m * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(v.c) & 15u) == 0);
 }
 
-int64_t packed_bytes(const PackPlan& plan) {
-  return (plan.pack_a ? plan.a.bytes : 0) + (plan.pack_b ? plan.b.bytes : 0);
-}
-
-// Offset of the packed copies: after the stream-K region, never inside the
-// stream-K counters.
-int64_t pack_offset(int64_t stream_k_bytes) {
-  const int64_t sk = (stream_k_bytes + 255) / 256 * 256;
-  return sk > SK_COUNTER_BYTES ? sk : SK_COUNTER_BYTES;
+// The plan of a tcgen05 call with `have` bytes of workspace (-1: as much as it
+// needs). Returns false when the call cannot take tcgen05 (operands to pack
+// and too little workspace); an explicit tcgen05 request then fails.
+bool plan_tc(const GemmArgs& g, const kf_gemm_config* user, const DeviceInfo& dev, int64_t have, TcPlan* out) {
+  TcPlan& p = *out;
+  p.view = g;
+  if (packing_applies(g, user)) {
+    // K below one 16-byte vector is padded with zeros to 8: then both operands
+    // need the padded extent, so both are copied.
+    const int64_t kp = g.K < 8 ? 8 : g.K;
+    p.pack_a = kp != g.K || !tma_describable(g.a, g.sa_m, g.sa_k, g.M, g.K);
+    p.pack_b = kp != g.K || !tma_describable(g.b, g.sb_n, g.sb_k, g.N, g.K);
+    // Stand-in aligned pointers until the workspace is known: only strides and
+    // sizes decide the config.
+    const void* stand_in = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+    if (p.pack_a) {
+      p.a = plan_pack(g.a, g.sa_m, g.sa_k, g.M, g.K, kp);
+      p.view.a = stand_in;
+      p.view.sa_m = p.a.k_inner ? p.a.pitch : 1;
+      p.view.sa_k = p.a.k_inner ? 1 : p.a.pitch;
+    }
+    if (p.pack_b) {
+      p.b = plan_pack(g.b, g.sb_n, g.sb_k, g.N, g.K, kp);
+      p.view.b = stand_in;
+      p.view.sb_n = p.b.k_inner ? p.b.pitch : 1;
+      p.view.sb_k = p.b.k_inner ? 1 : p.b.pitch;
+    }
+    p.view.K = kp;
+  }
+  p.cfg = resolve_gemm_config(p.view, user, dev.sm_count);
+  if (p.cfg.kernel != KF_GEMM_TCGEN05) return false;
+  p.stage_c = output_needs_stage(p.view, p.cfg);
+  if (p.stage_c) p.c = plan_output_stage(g.c, g.sc_m, g.sc_n, g.M, g.N);
+  p.sk = p.cfg.stream_k == 1 ? gemm_tcgen05_workspace_bytes(p.view, p.cfg, dev) : 0;
+  if (have < 0) return true;
+  const bool library_sk = user == nullptr || user->stream_k == 0;
+  // What gives way when the workspace is short: the library's own stream-K
+  // choice (whole tiles instead), then the output staging (element stores).
+  if (p.need() > have && p.sk > 0 && library_sk) {
+    p.cfg.stream_k = 2;
+    p.sk = 0;
+  }
+  if (p.need() > have && p.stage_c) p.stage_c = false;
+  return p.need() <= have;
 }
 
 int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
@@ -276,6 +302,26 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
                            tile_auto ? zero_config() : *user, static_cast<cudaStream_t>(stream), g.epilogue,
                            g.bias, g.peers, g.n_peers);
   }
+  // Up to 8 rows of x against an N-contiguous B (the reference's row-major
+  // (K, N) operand): lanes stream B's rows in 512-byte warp loads, K split
+  // over CTAs.
+  const bool cols_auto = (user == nullptr || user->kernel == KF_GEMM_AUTO) && g.n_peers == 0 &&
+                         gemv_cols_supported(g.dtype, g.a, g.b, g.sb_k, g.sb_n, g.M, g.N, g.K, nullptr);
+  if (cols_auto || (user != nullptr && user->kernel == KF_GEMM_COLUMNS)) {
+    if (g.n_peers > 0) return set_error(KF_ERR_UNSUPPORTED, "the column GEMV has no all-gather epilogue");
+    std::string why;
+    if (!gemv_cols_supported(g.dtype, g.a, g.b, g.sb_k, g.sb_n, g.M, g.N, g.K, &why))
+      return set_error(KF_ERR_UNALIGNED, why);
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc != KF_OK) return rc;
+    DeviceInfo* dev = nullptr;
+    rc = device_info(device, &dev);
+    if (rc != KF_OK) return rc;
+    return launch_gemv_cols(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_k, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K,
+                            g.epilogue, g.bias, g.workspace, g.workspace_bytes, dev->sm_count,
+                            static_cast<cudaStream_t>(stream));
+  }
   if (g.n_peers > 0 && !tcgen05_operands_ok(g, nullptr))
     return set_error(KF_ERR_UNALIGNED,
                      "the all-gather epilogue needs TMA-describable operands (or the tile GEMV's, M <= 32)");
@@ -286,50 +332,43 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
   rc = device_info(device, &dev);
   if (rc != KF_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (packing_applies(g, user)) {
-    PackPlan plan = plan_packing(g);
+  const int64_t have = g.workspace != nullptr ? g.workspace_bytes : 0;
+  TcPlan plan;
+  if (plan_tc(g, user, *dev, have, &plan)) {
     GemmArgs& v = plan.view;
-    kf_gemm_config cfg = resolve_gemm_config(v, user, dev->sm_count);
-    int64_t sk = cfg.stream_k == 1 ? gemm_tcgen05_workspace_bytes(v, cfg, *dev) : 0;
-    const int64_t have = g.workspace != nullptr ? g.workspace_bytes : 0;
-    if (sk > 0 && pack_offset(sk) + packed_bytes(plan) > have && (user == nullptr || user->stream_k == 0)) {
-      cfg.stream_k = 2;  // the library's stream-K choice gives way to packing: whole tiles
-      sk = 0;
+    char* dst = static_cast<char*>(g.workspace) + plan.offset();
+    if (plan.pack_a) {
+      rc = launch_pack(plan.a, dst, s);
+      if (rc != KF_OK) return rc;
+      v.a = dst;
+      dst += plan.a.bytes;
     }
-    const int64_t need = pack_offset(sk) + packed_bytes(plan);
-    if (need <= have) {
-      char* base = static_cast<char*>(g.workspace);
-      char* dst = base + pack_offset(sk);
-      if (plan.pack_a) {
-        rc = launch_pack(plan.a, dst, s);
-        if (rc != KF_OK) return rc;
-        v.a = dst;
-        dst += plan.a.bytes;
-      }
-      if (plan.pack_b) {
-        rc = launch_pack(plan.b, dst, s);
-        if (rc != KF_OK) return rc;
-        v.b = dst;
-      }
-      v.workspace = sk > 0 ? g.workspace : nullptr;
-      v.workspace_bytes = sk;
-      return launch_gemm_tcgen05(v, cfg, *dev, s);
+    if (plan.pack_b) {
+      rc = launch_pack(plan.b, dst, s);
+      if (rc != KF_OK) return rc;
+      v.b = dst;
+      dst += plan.b.bytes;
     }
+    if (plan.stage_c) {
+      v.c = dst;
+      v.sc_m = plan.c.pitch;
+      v.sc_n = 1;
+    }
+    v.workspace = plan.sk > 0 ? g.workspace : nullptr;
+    v.workspace_bytes = plan.sk;
+    rc = launch_gemm_tcgen05(v, plan.cfg, *dev, s);
+    if (rc != KF_OK || !plan.stage_c) return rc;
+    return launch_unpack(plan.c, dst, s);
+  }
+  if (plan.pack_a || plan.pack_b) {
     if (user != nullptr && user->kernel == KF_GEMM_TCGEN05)
       return set_error(KF_ERR_WORKSPACE, "operands TMA cannot describe are packed first: this call needs " +
-                                             std::to_string(need) + " bytes of workspace, got " +
+                                             std::to_string(plan.need()) + " bytes of workspace, got " +
                                              std::to_string(have));
     // no room to pack: the CUDA-core kernel reads the operands in place
   }
+  // (an explicit stream-K request without enough workspace is refused by the launch)
   kf_gemm_config cfg = resolve_gemm_config(g, user, dev->sm_count);
-  if (cfg.kernel == KF_GEMM_TCGEN05 && (user == nullptr || user->stream_k == 0)) {
-    const int64_t need = gemm_tcgen05_workspace_bytes(g, cfg, *dev);
-    if (need > 0 && (g.workspace == nullptr || g.workspace_bytes < need)) {
-      // The library's own stream-K choice never makes a call without (enough)
-      // workspace fail: it runs whole tiles instead. An explicit request errors.
-      cfg.stream_k = 2;
-    }
-  }
   if (cfg.kernel == KF_GEMM_TCGEN05) return launch_gemm_tcgen05(g, cfg, *dev, s);
   if (cfg.kernel == KF_GEMM_SIMT) {
     if (g.n_peers > 0)
@@ -544,6 +583,16 @@ int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const 
 int64_t kf_gemm_workspace_bytes(int32_t device, int32_t dtype, int64_t sa_m, int64_t sa_k,
                                 int64_t sb_k, int64_t sb_n, int64_t M, int64_t N, int64_t K,
                                 const kf_gemm_config* cfg) {
+  // Any 16-byte-aligned stand-in: only strides and sizes decide the config.
+  // (and C a contiguous [M, N] at a 16-byte-aligned address)
+  const void* stand_in = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  return kf_gemm_workspace_bytes_for(device, dtype, stand_in, sa_m, sa_k, stand_in, sb_k, sb_n,
+                                     const_cast<void*>(stand_in), N, 1, M, N, K, cfg);
+}
+
+int64_t kf_gemm_workspace_bytes_for(int32_t device, int32_t dtype, const void* a, int64_t sa_m, int64_t sa_k,
+                                    const void* b, int64_t sb_k, int64_t sb_n, void* c, int64_t sc_m, int64_t sc_n,
+                                    int64_t M, int64_t N, int64_t K, const kf_gemm_config* cfg) {
   DeviceInfo* dev = nullptr;
   const int rc = device_info(device, &dev);
   if (rc != KF_OK) return -rc;
@@ -556,19 +605,20 @@ int64_t kf_gemm_workspace_bytes(int32_t device, int32_t dtype, int64_t sa_m, int
   g.sa_k = sa_k;
   g.sb_k = sb_k;
   g.sb_n = sb_n;
-  // Any 16-byte-aligned stand-in: only strides and sizes decide the config.
-  g.a = g.b = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
-  if (packing_applies(g, cfg)) {
-    // Packed copies after the stream-K region (see gemm_common).
-    const PackPlan plan = plan_packing(g);
-    const kf_gemm_config c = resolve_gemm_config(plan.view, cfg, dev->sm_count);
-    const int64_t sk = c.stream_k == 1 ? gemm_tcgen05_workspace_bytes(plan.view, c, *dev) : 0;
-    if (sk < 0) return sk;
-    return pack_offset(sk) + packed_bytes(plan);
-  }
-  const kf_gemm_config c = resolve_gemm_config(g, cfg, dev->sm_count);
-  if (c.kernel != KF_GEMM_TCGEN05) return 0;
-  return gemm_tcgen05_workspace_bytes(g, c, *dev);
+  // A null pointer sizes for a 16-byte-aligned operand.
+  const void* stand_in = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  g.a = a != nullptr ? a : stand_in;
+  g.b = b != nullptr ? b : stand_in;
+  g.c = c != nullptr ? c : const_cast<void*>(stand_in);
+  g.sc_m = c != nullptr ? sc_m : N;
+  g.sc_n = c != nullptr ? sc_n : 1;
+  const int kernel = cfg ? cfg->kernel : KF_GEMM_AUTO;
+  if ((kernel == KF_GEMM_AUTO || kernel == KF_GEMM_COLUMNS) &&
+      gemv_cols_supported(dtype, g.a, g.b, sb_k, sb_n, M, N, K, nullptr))
+    return gemv_cols_workspace_bytes(dtype, M, N, K, dev->sm_count);
+  TcPlan plan;
+  if (!plan_tc(g, cfg, *dev, -1, &plan)) return 0;
+  return plan.need();
 }
 
 int64_t kf_gemv_workspace_bytes(int32_t device, int32_t dtype, int64_t sx_m, int64_t sx_k,

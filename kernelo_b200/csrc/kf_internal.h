@@ -86,6 +86,10 @@ struct PackedOperand {
 // (mn, k); K is padded with zero rows/columns to k_padded (>= k).
 PackedOperand plan_pack(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int64_t k, int64_t k_padded);
 int launch_pack(const PackedOperand& p, void* dst, cudaStream_t stream);
+// An output C [m, n] whose rows are off the 16-byte grid, staged as a pitched
+// copy: the GEMM writes the copy with vector stores, launch_unpack moves it to C.
+PackedOperand plan_output_stage(void* c, int64_t sc_m, int64_t sc_n, int64_t m, int64_t n);
+int launch_unpack(const PackedOperand& p, const void* staged, cudaStream_t stream);
 
 // CUDA-core path: any strides, fp16/bf16/fp32.
 int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream_t stream);
@@ -108,6 +112,18 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
                     int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
                     const kf_gemm_config& cfg, cudaStream_t stream, int epilogue = KF_EPI_NONE,
                     const void* bias = nullptr, void* const* peers = nullptr, int n_peers = 0);
+
+// Decode-shape GEMM against an N-contiguous B (gemv_cols.cu): M <= 8, any
+// dtype, K split over CTAs with a deterministic last-arrival sum.
+constexpr int GEMV_COLS_MAX_M = 8;
+bool gemv_cols_supported(int dtype, const void* x, const void* b, int64_t sb_k, int64_t sb_n, int64_t M,
+                         int64_t N, int64_t K, std::string* why);
+int gemv_cols_splits(int dtype, int64_t M, int64_t N, int64_t K, int sm_count);
+int64_t gemv_cols_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int sm_count);
+int launch_gemv_cols(int dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* b, int64_t sb_k,
+                     void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K, int epilogue,
+                     const void* bias, void* workspace, int64_t workspace_bytes, int sm_count,
+                     cudaStream_t stream);
 
 // Softmax kernel choice by row width in 16-byte vectors (rows.cu).
 constexpr long long SOFTMAX_STREAM_MAX_VECTORS = 128;     // up to 2 KB: streaming kernel

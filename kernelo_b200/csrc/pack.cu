@@ -47,6 +47,27 @@ __global__ void __launch_bounds__(256) pack16_kernel(const uint16_t* __restrict_
   }
 }
 
+// The inverse copy: dst[r * s_outer + c * s_inner] = src[r][c] for c < len;
+// each thread reads one 16-byte vector of the pitched source and writes its
+// elements with 2-byte stores (consecutive threads, consecutive columns).
+__global__ void __launch_bounds__(256) unpack16_kernel(const uint16_t* __restrict__ src, int pitch, long long outer,
+                                                       int len, uint16_t* __restrict__ dst, long long s_outer,
+                                                       long long s_inner) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  const int c0 = v * 8;
+  if (c0 >= len) return;
+  for (long long r = blockIdx.y; r < outer; r += gridDim.y) {
+    const uint4 q = *reinterpret_cast<const uint4*>(src + r * pitch + c0);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    uint16_t* row = dst + r * s_outer;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = c0 + j;
+      if (c < len) row[static_cast<long long>(c) * s_inner] = static_cast<uint16_t>(w[j / 2] >> (16 * (j & 1)));
+    }
+  }
+}
+
 }  // namespace
 
 PackedOperand plan_pack(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int64_t k, int64_t k_padded) {
@@ -83,6 +104,32 @@ int launch_pack(const PackedOperand& p, void* dst, cudaStream_t stream) {
                                           static_cast<int>(p.pitch));
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_error(err, "launch(pack16_kernel)");
+  return KF_OK;
+}
+
+PackedOperand plan_output_stage(void* c, int64_t sc_m, int64_t sc_n, int64_t m, int64_t n) {
+  PackedOperand p;
+  p.k_inner = true;
+  p.outer = p.src_outer = m;
+  p.len = n;
+  p.pitch = (n + 7) / 8 * 8;
+  p.bytes = (m * p.pitch * 2 + 255) / 256 * 256;
+  p.src = c;
+  p.s_outer = sc_m;
+  p.s_inner = sc_n;
+  return p;
+}
+
+int launch_unpack(const PackedOperand& p, const void* staged, cudaStream_t stream) {
+  if (p.outer == 0 || p.len == 0) return KF_OK;
+  const int vecs = static_cast<int>(p.pitch / 8);
+  dim3 grid(static_cast<unsigned>((vecs + 255) / 256), static_cast<unsigned>(p.outer < 65535 ? p.outer : 65535));
+  unpack16_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint16_t*>(staged), static_cast<int>(p.pitch),
+                                            p.outer, static_cast<int>(p.len),
+                                            static_cast<uint16_t*>(const_cast<void*>(p.src)), p.s_outer,
+                                            p.s_inner);
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_error(err, "launch(unpack16_kernel)");
   return KF_OK;
 }
 

@@ -28,6 +28,10 @@ KERNEL_WARP_ROWS = 3
 #: BLOCK_M = warps per tile (K slices), num_stages = vector pairs in flight.
 KERNEL_TILE_ROWS = 4
 TILE_ROWS_MAX_M = 32
+#: kf_gemm / kf_gemv: lanes streaming an N-contiguous B's rows (the row-major
+#: (K, N) operand), M <= 8, any dtype, K split over CTAs (csrc/gemv_cols.cu).
+KERNEL_COLUMNS = 5
+COLUMNS_MAX_M = 8
 #: (warps per tile, vector pairs in flight) compiled in gemv_mma.cu
 TILE_ROWS_SHAPES = ((8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8))
 
@@ -51,6 +55,28 @@ def tile_rows_reject(m: int, k: int, dtype: torch.dtype) -> str | None:
     if k % 8 != 0:
         return "the tile GEMV needs K % 8 == 0 (whole 16-byte vectors)"
     return None
+def columns_reject(m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str) -> str | None:
+    """Why the column GEMV cannot take this contiguous problem (None: it can;
+    mirrors gemv_cols_supported in gemv_cols.cu)."""
+    if b_layout != "kn":
+        return "the column GEMV streams an N-contiguous B (a row-major (K, N) operand)"
+    if not 1 <= m <= COLUMNS_MAX_M:
+        return f"the column GEMV takes 1..{COLUMNS_MAX_M} rows of x, got M={m}"
+    ve = 16 // torch.empty(0, dtype=dtype).element_size()
+    if n % ve != 0 or k < 1:
+        return f"the column GEMV needs N a multiple of {ve} (whole 16-byte vectors)"
+    return None
+
+
+def columns_programs(n: int, k: int, dtype: torch.dtype, sm_count: int = 148) -> int:
+    """CTAs of the column GEMV: 32-vector column strips times the K split
+    (mirrors gemv_cols_splits)."""
+    ve = 16 // torch.empty(0, dtype=dtype).element_size()
+    strips = -(-n // (32 * ve))
+    splits = max(1, min(-(-4 * sm_count // strips), max(1, k // 64), 256))
+    return strips * splits
+
+
 WARP_ROWS_MAX_M = 4
 #: The library default up to this M (measured on B200: at M=4 the tcgen05 GEMV is faster).
 WARP_ROWS_AUTO_MAX_M = 2
@@ -67,6 +93,7 @@ def warp_rows_smem_bytes(m: int, k: int, itemsize: int = 2) -> int:
     return warp_rows_rows(m) * (k // ve * ve + ve) * 4
 
 SM100_SMEM_PER_BLOCK = 232_448
+SM100_SMS = 148
 TC_BLOCK_M = 128
 #: Bytes the kernel adds to its operand ring: alignment slack and barriers.
 TC_SMEM_OVERHEAD = 1024 + 8 * 37 + 16
@@ -203,11 +230,14 @@ def default_gemm_config(
     operation: str, m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str, sm_count: int = 148
 ) -> KernelConfig:
     """The library's choice for contiguous operands (mirrors gemm_common in api.cu): the 16-row
-    tile kernel for up to 32 rows of x against a K-contiguous B, else tcgen05 tiles where TMA
-    can describe the operands, else the CUDA-core kernel."""
+    tile kernel for up to 32 rows of x against a K-contiguous B, the column GEMV for up to 8
+    rows against an N-contiguous B, else tcgen05 tiles (operands TMA cannot describe packed
+    first when the problem is not skinny), else the CUDA-core kernel."""
     if b_layout == "nk" and tile_rows_reject(m, k, dtype) is None:
         warps, pairs = tile_rows_default(m)
         return KernelConfig(operation, KERNEL=KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
+    if columns_reject(m, n, k, dtype, b_layout=b_layout) is None:
+        return KernelConfig(operation, KERNEL=KERNEL_COLUMNS)
     if dtype in (torch.float16, torch.bfloat16) and tma_misfit(m, n, k, b_layout=b_layout) is None:
         return default_tcgen05_config(operation, m, n, k, b_layout=b_layout, sm_count=sm_count)
     if packs_by_default(m, n, k, dtype, b_layout=b_layout):

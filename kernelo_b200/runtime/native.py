@@ -58,6 +58,7 @@ EXPORTED_SYMBOLS = (
     "kf_linear_bias_act",
     "kf_gemv",
     "kf_gemm_workspace_bytes",
+    "kf_gemm_workspace_bytes_for",
     "kf_gemv_workspace_bytes",
     "kf_query_gemm_config",
     "kf_softmax_rows",
@@ -153,6 +154,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kf_gemv": (_i32, [_i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
                        _GP, _vp, _i64, _vp]),
     "kf_gemm_workspace_bytes": (_i64, [_i32, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _GP]),
+    "kf_gemm_workspace_bytes_for": (_i64, [_i32, _i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64,
+                                           _i64, _i64, _GP]),
     "kf_gemv_workspace_bytes": (_i64, [_i32, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _GP]),
     "kf_query_gemm_config": (_i32, [_i32, _GP, ctypes.POINTER(_i64), ctypes.POINTER(_i32)]),
     "kf_softmax_rows": (_i32, [_i32, _vp, _i64, _vp, _i64, _i64, _i64, _RP, _vp]),
@@ -366,10 +369,11 @@ def gemm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, *, bias: torch.Tenso
     code = native_code(a.dtype)
     m, k = a.shape
     n = b.shape[1]
-    ws_bytes = lib.kf_gemm_workspace_bytes(dev.index or 0, code, a.stride(0), a.stride(1),
-                                           b.stride(0), b.stride(1), m, n, k, ctypes.byref(cfg))
+    ws_bytes = lib.kf_gemm_workspace_bytes_for(dev.index or 0, code, a.data_ptr(), a.stride(0), a.stride(1),
+                                               b.data_ptr(), b.stride(0), b.stride(1), c.data_ptr(), c.stride(0),
+                                               c.stride(1), m, n, k, ctypes.byref(cfg))
     if ws_bytes < 0:
-        check(int(-ws_bytes), "kf_gemm_workspace_bytes")
+        check(int(-ws_bytes), "kf_gemm_workspace_bytes_for")
     ws = workspaces.get(dev, stream, ws_bytes)
     ws_ptr = _ptr(ws)
     if epilogue == KF_EPI_NONE:

@@ -147,10 +147,14 @@ class SearchSpace(ABC):
         if not sizes or max(sizes) < caps.sm_count:
             return configs, []
         floor = caps.sm_count // 2
-        keep = [c for c, n in zip(configs, sizes) if n >= floor]
+        keep = [c for c, n in zip(configs, sizes) if n >= floor or self.protected(c, problem)]
         drop = [(c, f"launch grid of {n} programs fills under half of {caps.sm_count} SMs")
-                for c, n in zip(configs, sizes) if n < floor]
+                for c, n in zip(configs, sizes) if n < floor and not self.protected(c, problem)]
         return keep, drop
+
+    def protected(self, config: KernelConfig, problem: Problem) -> bool:
+        """Configs the funnel never prunes (the GEMM spaces: the library default)."""
+        return False
 
     def generate(
         self, problem: Problem, caps: DeviceCaps | None = None, *, max_candidates: int | None = None
@@ -224,6 +228,9 @@ class _Sm100GemmSpace(SearchSpace):
         m, n, k = self.dims(problem)
         return gc.default_gemm_config(self.operation, m, n, k, problem.dtype, b_layout=self.b_layout)
 
+    def protected(self, config: KernelConfig, problem: Problem) -> bool:
+        return config == self.library_default(problem)
+
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
         default = self.library_default(problem)
         yield default
@@ -236,6 +243,9 @@ class _Sm100GemmSpace(SearchSpace):
             # tile, num_stages vector pairs in flight)
             for warps, pairs in gc.TILE_ROWS_SHAPES:
                 yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
+        else:
+            # decode shapes against a row-major (K, N) B: the column GEMV
+            yield KernelConfig(self.operation, KERNEL=gc.KERNEL_COLUMNS)
         swap = 1 if gc.default_swap(m, n) else 2
         for bm, bn, bk, stages, schedule in product(self.BLOCK_M, self.BLOCK_N, self.BLOCK_K, self.NUM_STAGES,
                                                     self.SCHEDULES):
@@ -251,6 +261,8 @@ class _Sm100GemmSpace(SearchSpace):
         return (n, m) if config.get("SWAP_AB", 2) == 1 else (m, n)
 
     def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
+        if config["KERNEL"] == gc.KERNEL_COLUMNS:
+            return 0  # a few KB of reduction buffer and x slice
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             m = self.dims(problem)[0]
             return (config["BLOCK_M"] - 1) * 32 * gc.tile_rows_groups(m) * 16  # the K-slice partials
@@ -267,7 +279,14 @@ class _Sm100GemmSpace(SearchSpace):
         """CTAs with work: tiles, times two for SM-pair tiles."""
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             return ceil_div(self.dims(problem)[1], 16)  # one CTA per 16 weight rows
+        if config["KERNEL"] == gc.KERNEL_COLUMNS:
+            _, n, k = self.dims(problem)
+            return gc.columns_programs(n, k, problem.dtype)
         tiles = self.output_tiles(config, problem)
+        if config["KERNEL"] == gc.KERNEL_TCGEN05 and config.get("STREAM_K") == 1:
+            # stream-K deals the (tile, k-block) iterations over a persistent grid
+            iters = tiles * ceil_div(self.dims(problem)[2], config["BLOCK_K"]) * gc.cta_group(config["BLOCK_M"])
+            return min(gc.SM100_SMS, iters)
         return tiles * (gc.cta_group(config["BLOCK_M"]) if config["KERNEL"] == gc.KERNEL_TCGEN05 else 1)
 
     def _schedule_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
@@ -289,8 +308,12 @@ class _Sm100GemmSpace(SearchSpace):
 
     def reject_reason(self, config: KernelConfig, problem: Problem, caps: DeviceCaps) -> str | None:
         m, n, k = self.dims(problem)
+        if config == self.library_default(problem) and caps.is_blackwell_datacenter:
+            return None  # what the library runs anyway is always measured
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             return gc.tile_rows_reject(m, k, problem.dtype)
+        if config["KERNEL"] == gc.KERNEL_COLUMNS:
+            return gc.columns_reject(m, n, k, problem.dtype, b_layout=self.b_layout)
         if config["KERNEL"] == gc.KERNEL_SIMT:
             return None  # the fallback always runs
         why = gc.shape_allows_tcgen05(m, n, k, problem.dtype, b_layout=self.b_layout)
@@ -334,6 +357,8 @@ class _Sm100GemmSpace(SearchSpace):
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             default = (config["BLOCK_M"], config["num_stages"]) == gc.tile_rows_default(self.dims(problem)[0])
             return (-3,) if default else (-2,)
+        if config["KERNEL"] == gc.KERNEL_COLUMNS:
+            return (-3,)
         if config["KERNEL"] != gc.KERNEL_TCGEN05:
             return (1,)
         m_k, n_k = self.kernel_view(config, problem)

@@ -182,6 +182,63 @@ def test_unaligned_operands_are_packed_for_tcgen05(case, dtype, device):
     gate(expected[:16], matmul(a[:16], b, config=explicit), dtype, context=f"{case} explicit, skinny")
 
 
+@pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: str(d)[6:])
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+def test_column_gemv_row_major_b(m, dtype, device):
+    """Up to 8 rows of x against a row-major (K, N) B take the column GEMV (the
+    reference's decode layout), every dtype, K split over CTAs with a fixed
+    summation order: two calls agree bit for bit."""
+    gen = torch.Generator().manual_seed(m)
+    x = torch.randn(m, 4096, generator=gen).to(dtype).to(device)
+    b = (torch.randn(4096, 11008, generator=gen) * 4096 ** -0.5).to(dtype).to(device)
+    assert gc.default_gemm_config("matmul", m, 11008, 4096, dtype, b_layout="kn")["KERNEL"] == gc.KERNEL_COLUMNS
+    out = matmul(x, b)
+    gate(ref.matmul_ref(host(x), host(b)), out, dtype, context=f"M={m} {dtype}")
+    assert torch.equal(out, matmul(x, b)), "deterministic split-K sum"
+    # a ragged K (not a multiple of the split) and a strided x
+    xs = torch.randn(m, 2 * 1000, generator=gen).to(dtype).to(device)[:, ::2]
+    bs = (torch.randn(1000, 4096, generator=gen) * 0.03).to(dtype).to(device)
+    gate(ref.matmul_ref(host(xs), host(bs)), matmul(xs, bs), dtype, context=f"M={m} ragged K")
+
+
+def test_column_gemv_fused_epilogue_and_explicit_config(device):
+    """The reference's fused_linear_gelu takes W as (K, N): at decode shapes
+    that is the column GEMV with bias + GELU in its final sum."""
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(4, 2048, generator=gen).half().to(device)
+    w = (torch.randn(2048, 3072, generator=gen) * 2048 ** -0.5).half().to(device)  # (K, N) row-major
+    b = (torch.randn(3072, generator=gen) * 0.3).half().to(device)
+    for mode in ("tanh", "none"):
+        expected = ref.linear_gelu_ref(host(x), host(w), host(b), mode)
+        gate(expected, fused_linear_gelu(x, w, b, approximate=mode), torch.float16, context=mode)
+    cols = KernelConfig("matmul", KERNEL=gc.KERNEL_COLUMNS)
+    gate(ref.matmul_ref(host(x), host(w)), matmul(x, w, config=cols), torch.float16)
+    with pytest.raises(native.OutOfResources):
+        matmul(torch.randn(9, 64, device=device).half(), torch.randn(64, 64, device=device).half(), config=cols)
+
+
+@pytest.mark.parametrize("case", ["odd_n", "odd_column_view"])
+def test_output_rows_off_the_16_byte_grid_are_staged(case, device):
+    """An output whose rows are off the 16-byte grid (odd N, a view starting at
+    an odd column) is written to a pitched copy in the workspace with vector
+    stores and moved to C by one copy kernel; columns outside C stay untouched."""
+    gen = torch.Generator().manual_seed(5)
+    if case == "odd_n":
+        a = torch.randn(300, 512, generator=gen).half().to(device)
+        w = (torch.randn(1027, 512, generator=gen) * 0.05).half().to(device)  # [N, K], N odd
+        bias = torch.randn(1027, generator=gen).half().to(device)
+        expected = ref.linear_gelu_ref(host(a), host(w.t()), host(bias), "none")
+        gate(expected, fused_linear_gelu(a, w.t(), bias, approximate="none"), torch.float16, context=case)
+    else:
+        a = torch.randn(256, 512, generator=gen).half().to(device)
+        bmat = torch.randn(512, 640, generator=gen).half().to(device)
+        full = torch.full((256, 642), 7.0, device=device, dtype=torch.float16)
+        out = full[:, 1:641]
+        native.gemm(a, bmat, out)
+        gate(ref.matmul_ref(host(a), host(bmat)), out, torch.float16, context=case)
+        assert torch.all(full[:, 0] == 7.0) and torch.all(full[:, 641] == 7.0)
+
+
 # ------------------------------------------------------------------ fused linear
 def linear_inputs(m, k, n, dtype, device, seed=0, layout="nk"):
     gen = torch.Generator().manual_seed(seed)

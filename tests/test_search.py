@@ -15,6 +15,7 @@ from kernelo_b200.tuning.config import KernelConfig, Problem
 from kernelo_b200.tuning.search import (
     DEFAULT_MAX_CANDIDATES,
     FusedLinearErfSearchSpace,
+    FusedLinearSearchSpace,
     GemvSearchSpace,
     MatmulSearchSpace,
     RMSNormSearchSpace,
@@ -42,8 +43,8 @@ def test_next_power_of_2(n, expected):
 
 def test_grid_size_and_budget(b200_caps):
     result = MatmulSearchSpace().generate(GEMM, b200_caps)
-    # tcgen05 grid (2 x 6 x 2 x 5 x 3) + SIMT tiles; the library default is one of them here
-    assert result.generated == 2 * 6 * 2 * 5 * 3 + 3
+    # the column GEMV + tcgen05 grid (2 x 6 x 2 x 5 x 3) + SIMT tiles; the library default is one of them here
+    assert result.generated == 1 + 2 * 6 * 2 * 5 * 3 + 3
     default = MatmulSearchSpace().library_default(GEMM)
     assert result.candidates[0] == default, "the library default is always measured, first"
     assert 0 < result.feasible < result.generated
@@ -255,7 +256,27 @@ def test_fused_linear_decode_shapes_take_tile_rows(b200_caps):
     # a row-major (K, N) B is not K-contiguous: no tile candidates for matmul
     mm = Problem.create("matmul", "fp16", M=4, N=4096, K=4096)
     assert all(c["KERNEL"] != 4 for c in MatmulSearchSpace().candidates(mm, b200_caps))
-    assert gc.default_gemm_config("matmul", 4, 4096, 4096, torch.float16, b_layout="kn")["KERNEL"] == 1
+    # (up to 8 rows against a row-major B take the column GEMV; 16 rows take swapped tcgen05 tiles)
+    assert gc.default_gemm_config("matmul", 4, 4096, 4096, torch.float16, b_layout="kn")["KERNEL"] == 5
+    assert gc.default_gemm_config("matmul", 16, 4096, 4096, torch.float16, b_layout="kn")["KERNEL"] == 1
+
+
+def test_row_major_b_decode_shapes_take_the_column_gemv(b200_caps):
+    """M <= 8 against a row-major (K, N) B: the column GEMV, any dtype, leads;
+    wider M, N off the 16-byte grid or an [N, K] weight reject it."""
+    for dtype in ("fp16", "bf16", "fp32"):
+        p = Problem.create("matmul", dtype, M=1, N=11008, K=4096)
+        first = MatmulSearchSpace().candidates(p, b200_caps)[0]
+        assert first["KERNEL"] == gc.KERNEL_COLUMNS, (dtype, first)
+        assert MatmulSearchSpace().num_programs(first, p) >= b200_caps.sm_count
+    cols = KernelConfig("matmul", KERNEL=gc.KERNEL_COLUMNS)
+    space = MatmulSearchSpace()
+    assert "1..8 rows" in space.reject_reason(cols, Problem.create("matmul", "fp16", M=16, N=4096, K=64), b200_caps)
+    assert "multiple of 8" in space.reject_reason(cols, Problem.create("matmul", "fp16", M=2, N=2053, K=64),
+                                                  b200_caps)
+    assert "N-contiguous" in FusedLinearSearchSpace().reject_reason(
+        KernelConfig("fused_linear", KERNEL=gc.KERNEL_COLUMNS), Problem.create("fused_linear", "fp16", M=1, N=64,
+                                                                               K=64), b200_caps)
 
 
 def test_gemv_warp_rows_candidate(b200_caps):
