@@ -165,14 +165,31 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
     c.group_m = static_cast<int32_t>(gm);
   }
   if (c.stream_k == 0) {
-    // Fewer one-SM tiles than SMs: all stream-K. Otherwise the split tail:
-    // whole tiles for the full waves, the last partial wave as half-width
-    // tiles (at 4096x11008x4096: 688 pair tiles on 74 pairs leave 22 for the
-    // last wave; a stream-K tail measured slower there, its fix-up epilogues
-    // all falling at the end).
-    const int64_t tiles = ((m + 128LL * cg - 1) / (128LL * cg)) * ((n + c.block_n - 1) / c.block_n);
+    // Fewer one-SM tiles than SMs and a long K (decode shapes, the swapped
+    // GEMV): all stream-K. Fewer tiles than SMs and a short K: narrower
+    // tiles, whole (at 1021 x 2053 x 509 and 257^3 whole 64-column tiles
+    // measured 1.6-2x faster than stream-K, whose fix-up a few k-blocks
+    // cannot pay for). Otherwise the split tail: whole tiles for the full
+    // waves, the last partial wave as half-width tiles (at 4096x11008x4096:
+    // 688 pair tiles on 74 pairs leave 22 for the last wave; a stream-K tail
+    // measured slower there, its fix-up epilogues all falling at the end).
+    const int64_t tiles_m = (m + 128LL * cg - 1) / (128LL * cg);
+    int64_t tiles = tiles_m * ((n + c.block_n - 1) / c.block_n);
     const int64_t kb = (g.K + c.block_k - 1) / c.block_k;
-    c.stream_k = kb < 4 ? 2 : (cg == 1 && tiles < sm_count) ? 1 : 3;
+    if (kb < 4) {
+      c.stream_k = 2;
+    } else if (cg == 1 && tiles < sm_count && kb < 16) {
+      const int quantum = b_mn ? 64 : 16;
+      const bool user_bn = user != nullptr && user->block_n != 0;
+      for (const int bn : {128, 64}) {
+        if (user_bn || tiles >= sm_count || bn >= c.block_n || bn % quantum != 0) continue;
+        c.block_n = bn;
+        tiles = tiles_m * ((n + bn - 1) / bn);
+      }
+      c.stream_k = 2;
+    } else {
+      c.stream_k = (cg == 1 && tiles < sm_count) ? 1 : 3;
+    }
   }
   if (cg == 2 && c.cluster_m == 0) c.cluster_m = 2;
   return c;

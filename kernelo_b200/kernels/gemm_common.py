@@ -197,10 +197,23 @@ def default_tcgen05_config(
     block_k = 128 if (cg == 2 and k >= 512) else 64
     per_stage = (TC_BLOCK_M + block_n // cg) * block_k * 2
     stages = max(2, min(12, (SM100_SMEM_PER_BLOCK - 1024 - 256) // per_stage))
-    tiles = -(-m_k // (TC_BLOCK_M * cg)) * -(-n_k // block_n)
+    tiles_m = -(-m_k // (TC_BLOCK_M * cg))
+    tiles = tiles_m * -(-n_k // block_n)
     k_blocks = -(-k // block_k)
-    # all stream-K below one wave of one-SM tiles, else the split tail (mirrors api.cu)
-    stream_k = 2 if k_blocks < 4 else (1 if (cg == 1 and tiles < sm_count) else 3)
+    # (mirrors api.cu) short K: whole tiles; below one wave of one-SM tiles,
+    # stream-K for a long K and narrower whole tiles for a short one; else the split tail
+    if k_blocks < 4:
+        stream_k = 2
+    elif cg == 1 and tiles < sm_count and k_blocks < 16:
+        quantum = 64 if b_mn else 16
+        for bn in (128, 64):
+            if tiles >= sm_count or bn >= block_n or bn % quantum:
+                continue
+            block_n = bn
+            tiles = tiles_m * -(-n_k // bn)
+        stream_k = 2
+    else:
+        stream_k = 1 if (cg == 1 and tiles < sm_count) else 3
     # A panels of one raster group within ~48 MB of L2 (mirrors api.cu)
     tile_rows = TC_BLOCK_M * cg
     group_m = max(1, min(-(-m_k // tile_rows), (48 << 20) // max(1, tile_rows * k * 2)))
