@@ -127,7 +127,8 @@ typedef struct kf_rows_config {
                                row group (streaming kernel, 1..16)                   */
   int32_t rows_per_cta;     /* register kernel: rows one CTA (or cluster) handles     */
   int32_t cluster;          /* register kernel: CTAs sharing one row through DSMEM    */
-  int32_t kernel;           /* KF_ROWS_AUTO, KF_ROWS_REGISTER or KF_ROWS_STREAM       */
+  int32_t kernel;           /* KF_ROWS_AUTO, KF_ROWS_REGISTER, KF_ROWS_STREAM or
+                               KF_ROWS_WARP                                         */
   int32_t row_groups;       /* streaming kernel: row groups per CTA (0 = 16 / num_warps) */
   int32_t stages;           /* streaming kernel: shared-memory row slots per row group
                                (0 = as many as fit, at most 8)                        */
@@ -140,8 +141,11 @@ typedef struct kf_rows_config {
 /* Row kernels. REGISTER: one row per CTA (or per cluster of up to 8 CTAs for
  * wide rows), loaded straight into registers. STREAM: persistent CTAs (one or
  * two per SM) of row groups; each group keeps its next rows in flight as bulk
- * copies into shared-memory slots while it reduces and writes earlier ones. */
-enum kf_rows_kernel { KF_ROWS_AUTO = 0, KF_ROWS_REGISTER = 1, KF_ROWS_STREAM = 2 };
+ * copies into shared-memory slots while it reduces and writes earlier ones.
+ * WARP: persistent CTAs of 8 warps, a warp per row, the next row loaded into
+ * registers while the current one is reduced; rows of up to 2 KB that start on
+ * the 16-byte grid (the default for such softmax rows). */
+enum kf_rows_kernel { KF_ROWS_AUTO = 0, KF_ROWS_REGISTER = 1, KF_ROWS_STREAM = 2, KF_ROWS_WARP = 3 };
 
 /* ---- library information -------------------------------------------------- */
 KF_API int32_t kf_abi_version(void);

@@ -43,7 +43,9 @@
 // same; the mechanics are Blackwell's.
 #include <cudaTypedefs.h>
 
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "kf_common.cuh"
 #include "kf_internal.h"
@@ -1013,6 +1015,35 @@ int64_t gemm_tcgen05_workspace_bytes(const GemmArgs& g, const kf_gemm_config& cf
   return SK_COUNTER_BYTES + 2LL * grid * cfg.block_n * BM * 4;
 }
 
+namespace {
+
+// Per (kernel, dynamic shared memory, device): the attribute has been set, and
+// how many SM-pair clusters fit at once (-1 until asked).
+struct LaunchFacts {
+  int pair_clusters = -1;
+};
+
+cudaError_t launch_facts(void* fn, int64_t smem, const DeviceInfo& dev, LaunchFacts** out) {
+  static std::mutex mu;
+  static std::map<std::tuple<void*, int64_t, int>, LaunchFacts> facts;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  (void)dev;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(fn, smem, device);
+  auto it = facts.find(key);
+  if (it == facts.end()) {
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+    it = facts.emplace(key, LaunchFacts{}).first;
+  }
+  *out = &it->second;
+  return cudaSuccess;
+}
+
+}  // namespace
+
 int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const DeviceInfo& dev,
                         cudaStream_t stream) {
   std::string why;
@@ -1107,8 +1138,11 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   p.tmem_cols = tmem_cols_for(bn);
 
   void* fn = pick_kernel(g.dtype, g.epilogue, cg, g.n_peers > 0);
-  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_request));
+  // The attribute and the pair occupancy depend only on (kernel, shared memory,
+  // device): looked up once and kept, since the driver calls cost more host
+  // time per launch than a small GEMM takes on the GPU.
+  LaunchFacts* facts = nullptr;
+  cudaError_t err = launch_facts(fn, smem_request, dev, &facts);
   if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(tcgen05 gemm)");
 
   cudaLaunchConfig_t lc{};
@@ -1128,10 +1162,14 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
     lc.numAttrs = 1;
     if (cfg.num_ctas <= 0) {
       // Persistent pairs: as many as can be resident at once (pairs must share a GPC).
-      lc.gridDim = dim3(static_cast<unsigned>(2 * units));
-      int clusters = 0;
-      err = cudaOccupancyMaxActiveClusters(&clusters, fn, &lc);
-      if (err != cudaSuccess) return cuda_error(err, "cudaOccupancyMaxActiveClusters");
+      if (facts->pair_clusters < 0) {
+        lc.gridDim = dim3(static_cast<unsigned>(2 * units));
+        int clusters = 0;
+        err = cudaOccupancyMaxActiveClusters(&clusters, fn, &lc);
+        if (err != cudaSuccess) return cuda_error(err, "cudaOccupancyMaxActiveClusters");
+        facts->pair_clusters = clusters;
+      }
+      const int clusters = facts->pair_clusters;
       if (clusters > 0 && clusters < units) units = clusters;
     }
   }

@@ -166,6 +166,11 @@ int launch_rows(const RowsArgs& args, const kf_rows_config& cfg, const DeviceInf
                 cudaStream_t stream);
 // Streaming kernel (rows_stream.cu).
 bool rows_stream_supported(const RowsArgs& args, int max_smem_optin, std::string* why);
+// Warp-per-row persistent kernel for narrow rows (rows_warp.cu): rows of whole
+// 16-byte vectors, up to 128 of them, starting on the 16-byte grid.
+constexpr long long ROWS_WARP_MAX_VECTORS = 128;
+bool rows_warp_supported(const RowsArgs& args, std::string* why);
+int launch_rows_warp(const RowsArgs& args, const DeviceInfo& dev, cudaStream_t stream);
 int stream_default_warps(int64_t cols, int elem);
 int launch_rows_stream(const RowsArgs& args, const kf_rows_config& cfg, const DeviceInfo& dev,
                        cudaStream_t stream);

@@ -406,6 +406,7 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
     // over a cluster of SMs.
     const bool register_fields = c.rows_per_cta > 0 || c.cluster > 0 || c.num_warps > 16;
     const bool stream_fields = c.row_groups > 0 || c.stages > 0;
+    // (the warp-per-row kernel has no fields of its own: it is chosen by width)
     if (register_fields != stream_fields) {
       c.kernel = register_fields ? KF_ROWS_REGISTER : KF_ROWS_STREAM;
     } else {
@@ -425,6 +426,15 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
       const bool narrow = nvec_row <= SOFTMAX_STREAM_MAX_VECTORS;
       const bool in_registers = nvec_row <= SOFTMAX_REGISTER_MAX_VECTORS;
       c.kernel = stream_ok && (narrow || !in_registers) ? KF_ROWS_STREAM : KF_ROWS_REGISTER;
+      // Narrow rows on the 16-byte grid, either operation: a warp per row, no
+      // shared memory. The streaming kernel is issue-bound on its per-row
+      // machinery there (ncu: 67 % issue-active at 1000 fp16 columns), and
+      // one CTA per row leaves few loads in flight. Measured on B200
+      // (graph-timed, inputs beyond L2): softmax 32768 x 1000 fp16 1.05 of
+      // the copy bandwidth against 0.81 streamed; RMSNorm 16384 x 1024 fp16
+      // 1.09 against 0.87 in registers.
+      if (nvec_row <= ROWS_WARP_MAX_VECTORS && a.rows >= 2LL * dev.sm_count && rows_warp_supported(a, nullptr))
+        c.kernel = KF_ROWS_WARP;
       // Two slots per row group leave room for two CTAs per SM, which beats
       // deeper slots on narrow rows (25.8 against 27.6 us at 1000 columns).
       if (c.kernel == KF_ROWS_STREAM && narrow && c.stages <= 0) c.stages = 2;
@@ -432,6 +442,10 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
   }
   if (c.kernel == KF_ROWS_STREAM) {
     if (c.num_warps <= 0) c.num_warps = stream_default_warps(a.cols, elem);
+    return c;
+  }
+  if (c.kernel == KF_ROWS_WARP) {
+    c.num_warps = 1;  // warps per row
     return c;
   }
   const long long nvec = (a.cols * elem + 15) / 16;
@@ -475,8 +489,9 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
 int launch_rows(const RowsArgs& a, const kf_rows_config& cfg, const DeviceInfo& dev,
                 cudaStream_t stream) {
   if (cfg.kernel == KF_ROWS_STREAM) return launch_rows_stream(a, cfg, dev, stream);
+  if (cfg.kernel == KF_ROWS_WARP) return launch_rows_warp(a, dev, stream);
   if (cfg.kernel != KF_ROWS_REGISTER)
-    return set_error(KF_ERR_INVALID_CONFIG, "kernel must be KF_ROWS_AUTO, _REGISTER or _STREAM");
+    return set_error(KF_ERR_INVALID_CONFIG, "kernel must be KF_ROWS_AUTO, _REGISTER, _STREAM or _WARP");
   if (cfg.num_warps < 1 || cfg.num_warps > 32)
     return set_error(KF_ERR_INVALID_CONFIG, "num_warps must be in [1, 32]");
   if (cfg.cluster < 1 || cfg.cluster > 8 || (cfg.cluster & (cfg.cluster - 1)) != 0)

@@ -2,9 +2,14 @@
 
 ``default_rows_config`` mirrors ``resolve_rows_config`` in ``csrc/rows.cu``:
 
-* a softmax over many rows (at least two per SM) whose input and output rows
-  sit at the same 16-byte phase, with rows of up to 2 KB or beyond 32 KB, goes
-  to the persistent streaming kernel (``ROW_KERNEL=2``,
+* a softmax or RMSNorm over many rows (at least two per SM) of up to 2 KB that
+  hold whole 16-byte vectors and start on the 16-byte grid goes to the
+  warp-per-row kernel
+  (``ROW_KERNEL=3``, ``csrc/rows_warp.cu``): persistent CTAs of 8 warps, a warp
+  per row, the next row loaded into registers while the current one is reduced;
+* a softmax over many rows whose input and output rows sit at the same
+  16-byte phase, with rows of up to 2 KB (not taken by the warp kernel) or
+  beyond 32 KB, goes to the persistent streaming kernel (``ROW_KERNEL=2``,
   ``csrc/rows_stream.cu``): row groups of ``num_warps`` warps (the fewest, as a
   power of two, that hold a row at up to 16 vectors a thread) each keeping
   their next rows in flight as bulk copies into shared-memory slots (two slots
@@ -29,6 +34,9 @@ VECTORS_PER_CTA = 4096
 
 ROW_KERNEL_REGISTER = 1
 ROW_KERNEL_STREAM = 2
+ROW_KERNEL_WARP = 3
+#: Widest row of the warp-per-row kernel, in 16-byte vectors (mirrors kf_internal.h).
+WARP_MAX_VECTORS = 128
 #: Warps of one streaming CTA, shared by its row groups.
 STREAM_CONSUMER_WARPS = 16
 #: Shared memory of one sm_100 CTA, and what the streaming kernel keeps besides its slots.
@@ -64,6 +72,17 @@ def same_phase(x: torch.Tensor | None, cols: int) -> bool:
     return x.data_ptr() % 16 == 0 and (x.stride(0) * size) % 16 == (cols * size) % 16
 
 
+def warp_fits(cols: int, dtype: torch.dtype, x: torch.Tensor | None = None) -> bool:
+    """Rows the warp-per-row kernel takes (mirrors rows_warp_supported): whole
+    16-byte vectors, at most 2 KB, input rows on the 16-byte grid (the output
+    is a fresh contiguous tensor, on the grid whenever the rows are whole
+    vectors)."""
+    size = itemsize(dtype)
+    if (cols * size) % 16 != 0 or cols * size // 16 > WARP_MAX_VECTORS:
+        return False
+    return x is None or (x.data_ptr() % 16 == 0 and (x.stride(0) * size) % 16 == 0)
+
+
 #: Softmax kernel choice by row width in 16-byte vectors (mirrors kf_internal.h).
 SOFTMAX_STREAM_MAX_VECTORS = 128
 SOFTMAX_REGISTER_MAX_VECTORS = 2048
@@ -78,13 +97,16 @@ def default_rows_config(
     x: torch.Tensor | None = None,
     sm_count: int = 148,
 ) -> KernelConfig:
-    """The library's choice (mirrors resolve_rows_config in rows.cu): softmax
-    rows up to 2 KB stream, rows up to 32 KB sit in registers at about eight
-    16-byte vectors per thread, wider rows stream again (when there are enough
-    rows for every SM and the streaming kernel takes the layout); RMSNorm uses
-    the register kernel at about four vectors per thread."""
+    """The library's choice (mirrors resolve_rows_config in rows.cu): rows up
+    to 2 KB on the 16-byte grid go a warp per row (either operation); other
+    softmax rows up to 2 KB stream, rows up to 32 KB sit in registers at about
+    eight 16-byte vectors per thread, wider rows stream again (when there are
+    enough rows for every SM and the kernel takes the layout); RMSNorm uses the
+    register kernel at about four vectors per thread."""
     block = next_power_of_2(max(cols, 1))
     nvec = ceil_div(cols * itemsize(dtype), 16)
+    if rows is not None and rows >= 2 * sm_count and warp_fits(cols, dtype, x):
+        return KernelConfig(operation, BLOCK_SIZE=block, ROW_KERNEL=ROW_KERNEL_WARP, num_warps=1)
     if operation == "softmax":
         narrow = nvec <= SOFTMAX_STREAM_MAX_VECTORS
         in_registers = nvec <= SOFTMAX_REGISTER_MAX_VECTORS

@@ -440,7 +440,8 @@ class GemvSearchSpace(_Sm100GemmSpace):
 class _RowReductionSpace(SearchSpace):
     """Row kernels. The register kernel (``ROW_KERNEL=1``): threads per CTA, rows
     per CTA, CTAs per row. The persistent streaming kernel (``ROW_KERNEL=2``):
-    warps per row group, one CTA per SM with 16 consumer warps."""
+    warps per row group, one CTA per SM with 16 consumer warps. The
+    warp-per-row kernel (``ROW_KERNEL=3``): no fields, rows up to 2 KB."""
 
     NUM_WARPS = (1, 2, 4, 8, 16, 32)
     ROWS_PER_PROGRAM = (1, 2, 4)
@@ -461,6 +462,7 @@ class _RowReductionSpace(SearchSpace):
 
     def grid(self, problem: Problem) -> Iterator[KernelConfig]:
         block = next_power_of_2(problem.dims_dict["cols"])
+        yield KernelConfig(self.operation, BLOCK_SIZE=block, ROW_KERNEL=3, num_warps=1)
         for warps in self.STREAM_WARPS:
             yield KernelConfig(self.operation, BLOCK_SIZE=block, ROW_KERNEL=2, num_warps=warps)
             # two slots per row group: room for two CTAs per SM
@@ -475,14 +477,23 @@ class _RowReductionSpace(SearchSpace):
                 CLUSTER=cluster,
             )
 
+    #: Widest row of the warp-per-row kernel, in 16-byte vectors.
+    WARP_MAX_VECTORS = 128
+
     @staticmethod
     def is_stream(config: KernelConfig) -> bool:
         return config.get("ROW_KERNEL", 1) == 2
+
+    @staticmethod
+    def is_warp(config: KernelConfig) -> bool:
+        return config.get("ROW_KERNEL", 1) == 3
 
     def vectors_per_row(self, problem: Problem) -> int:
         return ceil_div(problem.dims_dict["cols"] * problem.itemsize, 16)
 
     def vectors_per_thread(self, config: KernelConfig, problem: Problem) -> int:
+        if self.is_warp(config):
+            return ceil_div(self.vectors_per_row(problem), 32)
         if self.is_stream(config):  # interior vectors only; head/tail are scalar
             whole = problem.dims_dict["cols"] * problem.itemsize // 16
             return max(1, ceil_div(whole, config["num_warps"] * 32))
@@ -490,6 +501,8 @@ class _RowReductionSpace(SearchSpace):
         return ceil_div(self.vectors_per_row(problem), threads)
 
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
+        if self.is_warp(config):
+            return ceil_div(problem.dims_dict["rows"], 8)
         if self.is_stream(config):
             return problem.dims_dict["rows"]
         return ceil_div(problem.dims_dict["rows"], config["ROWS_PER_PROGRAM"]) * config.get("CLUSTER", 1)
@@ -523,6 +536,12 @@ class _RowReductionSpace(SearchSpace):
             return f"row of {cols} exceeds the single-pass limit"
         if self.is_stream(config):
             return self.stream_reject_reason(config, problem, caps)
+        if self.is_warp(config):
+            if (cols * problem.itemsize) % 16 != 0:
+                return "warp-per-row kernel: rows must hold whole 16-byte vectors"
+            if self.vectors_per_row(problem) > self.WARP_MAX_VECTORS:
+                return f"warp-per-row kernel: a row of {cols * problem.itemsize} bytes exceeds 2 KB"
+            return None
         cluster = config.get("CLUSTER", 1)
         if cluster > caps.max_cluster_size:
             return f"cluster of {cluster} exceeds the portable limit of {caps.max_cluster_size}"
@@ -551,7 +570,7 @@ class _RowReductionSpace(SearchSpace):
                                       sm_count=caps.sm_count)
         is_default = dict(config) == dict(default)
         stream_first = self.is_stream(default)
-        kernel_rank = 0 if self.is_stream(config) == stream_first else 1
+        kernel_rank = 0 if config.get("ROW_KERNEL", 1) == default.get("ROW_KERNEL", 1) else 1
         programs = min(self.num_programs(config, problem), caps.sm_count)
         nv = self.vectors_per_thread(config, problem)
         target = 3 if (self.operation == "softmax" and not stream_first) else 2

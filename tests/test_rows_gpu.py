@@ -242,17 +242,22 @@ def test_stream_kernel_strided_rows(device):
 
 
 def test_softmax_default_kernel_by_row_width(device):
-    """Many rows: rows up to 2 KB stream (two slots per group), rows up to
-    64 KB sit in registers at ~8 vectors per thread, wider rows stream; few
-    rows, or x off the output's 16-byte phase, stay in registers. Each default
-    also runs and passes the gate."""
+    """Many rows: rows up to 2 KB go a warp per row (on the 16-byte grid) or
+    stream (two slots per group), rows up to 64 KB sit in registers at ~8
+    vectors per thread, wider rows stream; few rows, or x off the output's
+    16-byte phase, stay in registers. Each default also runs and passes the
+    gate."""
     from kernelo_b200.kernels.rows_common import default_rows_config
 
     x = rand(4096, 4096, torch.float16, device)
     narrow = rand(4096, 1000, torch.float16, device)
     cfg = default_rows_config("softmax", 1000, torch.float16, rows=4096, x=narrow)
-    assert (cfg["ROW_KERNEL"], cfg["num_warps"], cfg["num_stages"]) == (2, 1, 2)
+    assert (cfg["ROW_KERNEL"], cfg["num_warps"]) == (3, 1)
     gate(ref.softmax_ref(host(narrow)), softmax(narrow), torch.float16)
+    ragged = rand(4096, 1001, torch.float16, device)  # not whole vectors: streamed
+    cfg = default_rows_config("softmax", 1001, torch.float16, rows=4096, x=ragged)
+    assert (cfg["ROW_KERNEL"], cfg["num_warps"], cfg["num_stages"]) == (2, 1, 2)
+    gate(ref.softmax_ref(host(ragged)), softmax(ragged), torch.float16)
     cfg = default_rows_config("softmax", 4096, torch.float16, rows=4096, x=x)
     assert (cfg["ROW_KERNEL"], cfg["num_warps"]) == (1, 2)
     gate(ref.softmax_ref(host(x)), softmax(x), torch.float16)
@@ -260,6 +265,9 @@ def test_softmax_default_kernel_by_row_width(device):
     assert default_rows_config("softmax", 1000, torch.float16, rows=64, x=narrow[:64])["ROW_KERNEL"] == 1
     assert default_rows_config("softmax", 32000, torch.float32, rows=32768)["ROW_KERNEL"] == 2
     assert default_rows_config("rmsnorm", 4096, torch.float16, rows=16384, x=x)["ROW_KERNEL"] == 1
+    assert default_rows_config("rmsnorm", 1024, torch.float16, rows=16384)["ROW_KERNEL"] == 3
+    gamma = (rand(1, 1000, torch.float32, device, seed=1)[0] * 0.1 + 1).half()
+    gate(ref.rmsnorm_ref(host(narrow), host(gamma), 1e-6), rmsnorm(narrow, gamma, eps=1e-6), torch.float16)
 
 
 def test_stream_kernel_rejects_bad_configs(device):
@@ -274,8 +282,71 @@ def test_stream_kernel_rejects_bad_configs(device):
         softmax(x, config=stream_cfg("softmax", 4096, num_warps=8, num_stages=40))
 
 
+# ---------------------------------------------------------------- warp-per-row kernel
+def warp_cfg(op, cols):
+    return KernelConfig(op, BLOCK_SIZE=max(1, 1 << (cols - 1).bit_length()), ROW_KERNEL=3, num_warps=1)
+
+
+@pytest.mark.parametrize("cols", [8, 16, 64, 248, 256, 264, 512, 1000, 1024])
+@pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: str(d)[6:])
+@pytest.mark.parametrize("rows", [1, 7, 301, 5000])
+def test_warp_kernel_widths(cols, dtype, rows, device):
+    """One to four vectors per lane (the three instantiations), rows fewer
+    than one CTA's 8 warps, more rows than resident warps (each warp loops),
+    padding lanes of a partial last vector group; both operations."""
+    if cols * dtype.itemsize > 2048:
+        pytest.skip("rows beyond 2 KB are not the warp kernel's")
+    x = rand(rows, cols, dtype, device, scale=4.0, seed=cols)
+    y = torch.full_like(x, float("nan"))
+    from kernelo_b200.runtime import native
+
+    native.softmax_rows(x, y, warp_cfg("softmax", cols))
+    gate(ref.softmax_ref(host(x)), y, dtype, context=f"softmax {rows}x{cols}")
+    gamma = (rand(1, cols, torch.float32, device, seed=1)[0] * 0.1 + 1).to(dtype)
+    y = torch.full_like(x, float("nan"))
+    native.rmsnorm_rows(x, gamma, y, 1e-6, warp_cfg("rmsnorm", cols))
+    gate(ref.rmsnorm_ref(host(x), host(gamma), 1e-6), y, dtype, context=f"rmsnorm {rows}x{cols}")
+
+
+def test_warp_kernel_edge_rows(device):
+    """A -inf row mixed in (all but one element), a row of one value, huge
+    logits; a strided view whose rows stay on the 16-byte grid."""
+    x = rand(600, 1000, torch.float16, device, scale=4.0)
+    x[3] = float("-inf")
+    x[3, 17] = 1.0
+    x[5] = 7.0
+    x[9, 100] = 60000.0
+    out = softmax(x, config=warp_cfg("softmax", 1000))
+    assert out[3, 17].item() == 1.0 and float(out[3].float().sum()) == 1.0
+    assert torch.allclose(out[5].float(), torch.full((1000,), 1e-3, device=device), rtol=1e-3)
+    assert out[9, 100].item() == 1.0
+    gate(ref.softmax_ref(host(x)), out, torch.float16)
+    base = rand(700, 1536, torch.bfloat16, device, scale=4.0)
+    view = base[:, 64:1088]  # 1024 columns, row pitch 3 KB, start on the grid
+    gate(ref.softmax_ref(host(view)), softmax(view, config=warp_cfg("softmax", 1024)), torch.bfloat16)
+    gamma = torch.ones(1024, device=device, dtype=torch.bfloat16)
+    gate(ref.rmsnorm_ref(host(view), host(gamma)), rmsnorm(view, gamma, config=warp_cfg("rmsnorm", 1024)),
+         torch.bfloat16)
+
+
+def test_warp_kernel_refuses_layouts_it_cannot_take(device):
+    from kernelo_b200.runtime.native import OutOfResources
+
+    x = rand(400, 1001, torch.float16, device)
+    with pytest.raises(OutOfResources, match="whole 16-byte vectors"):
+        softmax(x, config=warp_cfg("softmax", 1001))
+    wide = rand(400, 2048, torch.float16, device)
+    with pytest.raises(OutOfResources, match="2 KB"):
+        softmax(wide, config=warp_cfg("softmax", 2048))
+    odd = rand(400, 1032, torch.float16, device)[:, 4:1028]  # start 8 bytes off the grid
+    with pytest.raises(OutOfResources, match="16-byte grid"):
+        softmax(odd, config=warp_cfg("softmax", 1024))
+    # the default routes the same view elsewhere and is still right
+    gate(ref.softmax_ref(host(odd)), softmax(odd), torch.float16)
+
+
 @pytest.mark.parametrize("cols", [1, 7, 1000, 4096, 4097, 32000])
-@pytest.mark.parametrize("kernel", [1, 2])
+@pytest.mark.parametrize("kernel", [1, 2, 3])
 def test_row_kernels_write_every_output(cols, kernel, device):
     """Outputs start as NaN, so a row or a tail the kernel skipped fails the
     finiteness check; both kernels, narrow to 128 KiB rows, unaligned widths."""
@@ -287,6 +358,8 @@ def test_row_kernels_write_every_output(cols, kernel, device):
     rows = 300 if kernel == 2 else 37
     if kernel == 2 and not stream_fits(cols, dtype):
         pytest.skip("row does not fit a streaming slot")
+    if kernel == 3 and (cols * dtype.itemsize % 16 or cols * dtype.itemsize > 2048):
+        pytest.skip("not a warp-kernel row")
     x = rand(rows, cols, dtype, device)
     gamma = rand(1, cols, dtype, device)[0]
     block = max(1, 1 << (cols - 1).bit_length())

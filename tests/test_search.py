@@ -172,13 +172,22 @@ def test_row_space_shape_and_rules(b200_caps):
     assert stream and {k for c in stream for k in c} == {"ROW_KERNEL", "BLOCK_SIZE", "num_warps", "num_stages"}
     assert sorted({c["num_warps"] for c in stream}) == [1, 2, 4, 8, 16]
     assert cands[0]["ROW_KERNEL"] == 1, "RMSNorm: the register kernel (library default) ranks first"
-    # softmax: 8 KB rows in registers at ~8 vectors per thread (2 warps), 2 KB rows streamed
+    # softmax: 8 KB rows in registers at ~8 vectors per thread (2 warps), 2 KB
+    # rows a warp per row, then the streaming kernel
     soft = Problem.create("softmax", "fp16", rows=16384, cols=4096)
     first = SoftmaxSearchSpace().candidates(soft, b200_caps)[0]
     assert (first["ROW_KERNEL"], first["num_warps"], first["CLUSTER"]) == (1, 2, 1)
     soft_narrow = Problem.create("softmax", "fp16", rows=32768, cols=1000)
-    first = SoftmaxSearchSpace().candidates(soft_narrow, b200_caps)[0]
-    assert (first["ROW_KERNEL"], first["num_warps"], first.get("num_stages")) == (2, 1, 2)
+    narrow_cands = SoftmaxSearchSpace().candidates(soft_narrow, b200_caps)
+    assert (narrow_cands[0]["ROW_KERNEL"], narrow_cands[0]["num_warps"]) == (3, 1)
+    assert any(c["ROW_KERNEL"] == 2 for c in narrow_cands)
+    # 8 KB rows exceed the warp kernel; odd rows of fp16 do not hold whole vectors
+    warp = KernelConfig("softmax", BLOCK_SIZE=4096, ROW_KERNEL=3, num_warps=1)
+    assert "exceeds 2 KB" in SoftmaxSearchSpace().reject_reason(warp, soft, b200_caps)
+    odd = Problem.create("softmax", "fp16", rows=32768, cols=999)
+    assert "whole 16-byte vectors" in SoftmaxSearchSpace().reject_reason(warp.replace(BLOCK_SIZE=1024), odd,
+                                                                          b200_caps)
+    assert SoftmaxSearchSpace().candidates(odd, b200_caps)[0]["ROW_KERNEL"] == 2
     assert {c["BLOCK_SIZE"] for c in cands} == {4096}
     wide = Problem.create("softmax", "fp32", rows=32768, cols=32000)
     space = SoftmaxSearchSpace()
