@@ -1017,28 +1017,30 @@ int64_t gemm_tcgen05_workspace_bytes(const GemmArgs& g, const kf_gemm_config& cf
 
 namespace {
 
-// Per (kernel, dynamic shared memory, device): the attribute has been set, and
-// how many SM-pair clusters fit at once (-1 until asked).
+// Per (kernel, dynamic shared memory, device): how many SM-pair clusters fit
+// at once (-1 until asked).
 struct LaunchFacts {
   int pair_clusters = -1;
 };
 
-cudaError_t launch_facts(void* fn, int64_t smem, const DeviceInfo& dev, LaunchFacts** out) {
+// The kernel's dynamic shared-memory limit only ever rises: a launch that asks
+// for more than the largest request so far raises it, a smaller one leaves it
+// (one kernel serves several stage counts and tile widths).
+cudaError_t launch_facts(void* fn, int64_t smem, LaunchFacts** out) {
   static std::mutex mu;
   static std::map<std::tuple<void*, int64_t, int>, LaunchFacts> facts;
+  static std::map<std::pair<void*, int>, int64_t> smem_limit;
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
-  (void)dev;
   std::lock_guard<std::mutex> lock(mu);
-  const auto key = std::make_tuple(fn, smem, device);
-  auto it = facts.find(key);
-  if (it == facts.end()) {
+  int64_t& limit = smem_limit[std::make_pair(fn, device)];
+  if (smem > limit) {
     err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    it = facts.emplace(key, LaunchFacts{}).first;
+    limit = smem;
   }
-  *out = &it->second;
+  *out = &facts[std::make_tuple(fn, smem, device)];
   return cudaSuccess;
 }
 
@@ -1142,7 +1144,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   // device): looked up once and kept, since the driver calls cost more host
   // time per launch than a small GEMM takes on the GPU.
   LaunchFacts* facts = nullptr;
-  cudaError_t err = launch_facts(fn, smem_request, dev, &facts);
+  cudaError_t err = launch_facts(fn, smem_request, &facts);
   if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(tcgen05 gemm)");
 
   cudaLaunchConfig_t lc{};

@@ -73,6 +73,25 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 // slices); U: vector pairs per lane in flight.
 // At least five CTAs per SM: a tile's CTA lasts about the whole kernel, so
 // all of them (688 for N = 11008) must be resident at once.
+// Weight vectors bypass L1 allocation (each is read once); x vectors are kept
+// in L1 ahead of other lines (every warp of every CTA on the SM re-reads them).
+// At M = 16 x is 128 KB per CTA, as much as the CTA's weights: without the
+// hints the weight stream evicts it (39 % L1 hits measured).
+__device__ __forceinline__ uint4 load_weight(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 load_x(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::evict_last.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 template <typename T, int NT, int S, int U, int EPI>
 __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams p) {
   __shared__ float4 part[S > 1 ? S - 1 : 1][32][NT];
@@ -102,28 +121,49 @@ __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams
     for (int i = 0; i < 4; ++i) acc[nt][i] = 0.0f;
 
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-  for (int q = q0; q < q1; q += U) {
-    // The weight loads of the batch go out first (HBM); x is read per vector
-    // just before its MMAs (L1 hits), which keeps its registers short-lived.
-    uint4 va[U], vb[U];
+  // A batch: U vector pairs (rows g and g + 8) at quads q .. q + U - 1.
+  auto load_batch = [&](int q, uint4 (&va)[U], uint4 (&vb)[U]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int v = 4 * (q + u) + t;
       const bool ok = q + u < q1 && v < nvec;
-      va[u] = ok ? __ldcs(wa + v) : zero;
-      vb[u] = ok ? __ldcs(wb + v) : zero;
+      va[u] = ok ? load_weight(wa + v) : zero;
+      vb[u] = ok ? load_weight(wb + v) : zero;
     }
+  };
+  // x is read per vector just before its MMAs (L1 hits), which keeps its
+  // registers short-lived.
+  auto mma_batch = [&](int q, const uint4 (&va)[U], const uint4 (&vb)[U]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int v = 4 * (q + u) + t;
       const bool ok = q + u < q1 && v < nvec;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint4 vx = (ok && xon[nt]) ? __ldg(xr[nt] + v) : zero;
+        const uint4 vx = (ok && xon[nt]) ? load_x(xr[nt] + v) : zero;
         // elements 0-3 of the vector, then 4-7: logical k {2t, 2t+1, 2t+8, 2t+9}
         mma16816<T>(acc[nt], va[u].x, vb[u].x, va[u].y, vb[u].y, vx.x, vx.y);
         mma16816<T>(acc[nt], va[u].z, vb[u].z, va[u].w, vb[u].w, vx.z, vx.w);
       }
+    }
+  };
+  if constexpr (U == 1) {
+    // One pair a batch, software-pipelined: the next pair's loads go out
+    // before this pair's MMAs, so a warp always has a load in flight.
+    uint4 ca[1], cb[1], na[1], nb[1];
+    load_batch(q0, ca, cb);
+    for (int q = q0; q < q1; ++q) {
+      load_batch(q + 1, na, nb);
+      mma_batch(q, ca, cb);
+      ca[0] = na[0];
+      cb[0] = nb[0];
+    }
+  } else {
+    // The weight loads of a batch go out together (HBM), then its MMAs.
+    for (int q = q0; q < q1; q += U) {
+      uint4 va[U], vb[U];
+      load_batch(q, va, vb);
+      mma_batch(q, va, vb);
     }
   }
 
@@ -188,16 +228,19 @@ int launch_shape(const GemvMmaParams& p, cudaStream_t stream) {
   return KF_OK;
 }
 
-// Launch shapes (S warps per tile, U vector pairs in flight per lane): config
-// block_m selects S and stages selects U; zero picks the default, measured
-// on B200 at N = 11008, K = 4096: (8, 2) up to 8 rows of x (17.0 us at M=1,
-// 17.9 at M=4), (6, 4) up to 16 (19.6 us at M=16; 8 warps of 4 pairs spill),
-// (4, 4) up to 32 (23.1 / 24.0 us at M = 24 / 32 against 27.1 / 27.4 for the
-// tcgen05 GEMV; 6 warps spill there).
+// Launch shapes (S warps per tile, U vector pairs per batch per lane; U = 1
+// is the software-pipelined single pair): config block_m selects S and stages
+// selects U; zero picks the default, measured on B200 at N = 11008, K = 4096
+// (graph-timed, weights beyond L2): (8, 1) up to 8 rows of x (15.5 / 15.7 /
+// 15.9 us at M = 1 / 4 / 8 against 16.4 / 16.8 / 17.1 for (8, 2)), (6, 4) up
+// to 16 (18.2 us at M = 16; 8 warps of 4 pairs spill, one pipelined pair
+// measured 23.7), (4, 4) up to 32 (23.1 / 24.0 us at M = 24 / 32 against
+// 27.1 / 27.4 for the tcgen05 GEMV; 6 warps spill there).
 template <typename T, int NT, int EPI>
 int launch_nt(const GemvMmaParams& p, const kf_gemm_config& cfg, cudaStream_t stream) {
   const int s = cfg.block_m != 0 ? cfg.block_m : (NT == 1 ? 8 : NT == 2 ? 6 : 4);
-  const int u = cfg.stages != 0 ? cfg.stages : (NT == 1 ? 2 : 4);
+  const int u = cfg.stages != 0 ? cfg.stages : (NT == 1 ? 1 : 4);
+  if (s == 8 && u == 1) return launch_shape<T, NT, 8, 1, EPI>(p, stream);
   if (s == 4 && u == 4) return launch_shape<T, NT, 4, 4, EPI>(p, stream);
   if (s == 4 && u == 2) return launch_shape<T, NT, 4, 2, EPI>(p, stream);
   if (s == 4 && u == 8) return launch_shape<T, NT, 4, 8, EPI>(p, stream);

@@ -32,8 +32,8 @@ TILE_ROWS_MAX_M = 32
 #: (K, N) operand), M <= 8, any dtype, K split over CTAs (csrc/gemv_cols.cu).
 KERNEL_COLUMNS = 5
 COLUMNS_MAX_M = 8
-#: (warps per tile, vector pairs in flight) compiled in gemv_mma.cu
-TILE_ROWS_SHAPES = ((8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8))
+#: (warps per tile, vector pairs per batch; 1 = one software-pipelined pair) compiled in gemv_mma.cu
+TILE_ROWS_SHAPES = ((8, 1), (8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8))
 
 
 def tile_rows_groups(m: int) -> int:
@@ -43,7 +43,7 @@ def tile_rows_groups(m: int) -> int:
 
 def tile_rows_default(m: int) -> tuple[int, int]:
     """The kernel's default shape (mirrors gemv_mma.cu)."""
-    return {1: (8, 2), 2: (6, 4), 4: (4, 4)}[tile_rows_groups(m)]
+    return {1: (8, 1), 2: (6, 4), 4: (4, 4)}[tile_rows_groups(m)]
 
 
 def tile_rows_reject(m: int, k: int, dtype: torch.dtype) -> str | None:

@@ -491,7 +491,7 @@ def test_gemv_tile_rows(m, dtype, device):
     gate(expected, gemv(x, w), dtype, context=f"M={m} library choice")
 
 
-@pytest.mark.parametrize("shape", [(8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8)])
+@pytest.mark.parametrize("shape", [(8, 1), (8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8)])
 @pytest.mark.parametrize("m", [4, 16, 32])
 def test_gemv_tile_rows_every_shape(shape, m, device):
     gen = torch.Generator().manual_seed(7 * shape[0] + shape[1])

@@ -238,7 +238,7 @@ def test_gemv_tile_rows_candidates(b200_caps):
     """The 16-row tile kernel leads for 16-bit x up to 16 rows, its default
     shape first; fp32, M > 16 and K % 8 != 0 reject it."""
     space = GemvSearchSpace()
-    for m, default in ((1, (8, 2)), (4, (8, 2)), (16, (6, 4))):
+    for m, default in ((1, (8, 1)), (4, (8, 1)), (16, (6, 4))):
         p = Problem.create("gemv", "bf16", M=m, N=11008, K=4096)
         cands = space.candidates(p, b200_caps)
         assert cands[0]["KERNEL"] == gc.KERNEL_TILE_ROWS
@@ -261,7 +261,7 @@ def test_fused_linear_decode_shapes_take_tile_rows(b200_caps):
         assert cfg["KERNEL"] == expected, (m, cfg)
     decode = Problem.create("fused_linear_erf", "bf16", M=4, N=11008, K=4096)
     first = FusedLinearErfSearchSpace().candidates(decode, b200_caps)[0]
-    assert (first["KERNEL"], first["BLOCK_M"], first["num_stages"]) == (4, 8, 2)
+    assert (first["KERNEL"], first["BLOCK_M"], first["num_stages"]) == (4, 8, 1)
     # a row-major (K, N) B is not K-contiguous: no tile candidates for matmul
     mm = Problem.create("matmul", "fp16", M=4, N=4096, K=4096)
     assert all(c["KERNEL"] != 4 for c in MatmulSearchSpace().candidates(mm, b200_caps))
