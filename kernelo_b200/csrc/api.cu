@@ -135,16 +135,21 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
   const int cg = c.block_m == 256 ? 2 : 1;
   if (c.block_n == 0) {
     const int quantum = (b_mn ? 64 : 16) * cg;
-    int64_t bn = n <= 256 ? ((n + quantum - 1) / quantum) * quantum : 256;
+    // TF32 tiles sum their accumulator chunks in registers: at most 128 wide.
+    const int64_t widest = g.dtype == KF_FP32 ? 128 : 256;
+    int64_t bn = n <= widest ? ((n + quantum - 1) / quantum) * quantum : widest;
     if (bn < quantum) bn = quantum;
     if (bn > 256) bn = 256;
     c.block_n = static_cast<int32_t>(bn);
   }
-  // Pair tiles: 128-deep k-blocks halve the barrier round trips per FLOP
-  // (measured faster than 64-deep blocks at equal bytes in flight).
-  if (c.block_k == 0) c.block_k = (cg == 2 && g.K >= 512) ? 128 : 64;
+  // Pair tiles: two 128-byte atoms of K per k-block halve the barrier round
+  // trips per FLOP (measured faster than one atom at equal bytes in flight).
+  // An atom is 64 16-bit or 32 fp32 (TF32) elements.
+  const int elem = g.dtype == KF_FP32 ? 4 : 2;
+  const int atom = 128 / elem;
+  if (c.block_k == 0) c.block_k = (cg == 2 && g.K >= 512) ? 2 * atom : atom;
   if (c.stages == 0) {
-    const int64_t per_stage = static_cast<int64_t>(128 + c.block_n / cg) * c.block_k * 2;
+    const int64_t per_stage = static_cast<int64_t>(128 + c.block_n / cg) * c.block_k * elem;
     // (the all-gather epilogue's output stage comes out of the same 227 KiB)
     int64_t s = (232448 - 1024 - 256 - (g.n_peers > 0 ? GEMM_PEER_STAGE_SMEM : 0)) / per_stage;
     if (s > 12) s = 12;
@@ -157,7 +162,7 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
     // stays resident across waves (measured on B200 at 4096x11008x4096: 16
     // groups-of-one-column read B once, 8 read it twice and ran 3 % slower).
     const int64_t tile_rows = 128LL * cg;
-    const int64_t panel = tile_rows * g.K * 2;
+    const int64_t panel = tile_rows * g.K * elem;
     int64_t gm = panel > 0 ? (48LL << 20) / panel : 8;
     const int64_t tiles_m = (m + tile_rows - 1) / tile_rows;
     if (gm > tiles_m) gm = tiles_m;
@@ -166,7 +171,9 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
   }
   if (c.stream_k == 0) {
     // Fewer one-SM tiles than SMs and a long K (decode shapes, the swapped
-    // GEMV): all stream-K. Fewer tiles than SMs and a short K: narrower
+    // GEMV): all stream-K. Fewer tiles than SMs and a short K (or too few
+    // k-blocks in all for 8 per SM, where stream-K's fix-up would gather a
+    // dozen partials per tile): narrower
     // tiles, whole (at 1021 x 2053 x 509 and 257^3 whole 64-column tiles
     // measured 1.6-2x faster than stream-K, whose fix-up a few k-blocks
     // cannot pay for). Otherwise the split tail: whole tiles for the full
@@ -178,7 +185,7 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
     const int64_t kb = (g.K + c.block_k - 1) / c.block_k;
     if (kb < 4) {
       c.stream_k = 2;
-    } else if (cg == 1 && tiles < sm_count && kb < 16) {
+    } else if (cg == 1 && tiles < sm_count && (kb < 16 || tiles * kb < 8LL * sm_count)) {
       const int quantum = b_mn ? 64 : 16;
       const bool user_bn = user != nullptr && user->block_n != 0;
       for (const int bn : {128, 64}) {
@@ -212,7 +219,9 @@ namespace {
 // so the counters a later stream-K call relies on are never overwritten.
 struct TcPlan {
   bool pack_a = false, pack_b = false, stage_c = false;
+  bool split = false;  // fp32: both operands split into TF32 parts (3xTF32)
   PackedOperand a, b, c;
+  SplitOperand sa, sb;
   GemmArgs view;  // the problem as the kernel sees it (packed operands' strides)
   kf_gemm_config cfg{};
   int64_t sk = 0;  // stream-K bytes
@@ -221,6 +230,7 @@ struct TcPlan {
     return r > SK_COUNTER_BYTES ? r : SK_COUNTER_BYTES;
   }
   int64_t staging_bytes() const {
+    if (split) return sa.bytes + sb.bytes;
     return (pack_a ? a.bytes : 0) + (pack_b ? b.bytes : 0) + (stage_c ? c.bytes : 0);
   }
   int64_t need() const { return staging_bytes() > 0 ? offset() + staging_bytes() : sk; }
@@ -237,6 +247,16 @@ bool packing_applies(const GemmArgs& g, const kf_gemm_config* user) {
   return kernel == KF_GEMM_TCGEN05 || (g.M > 64 && g.N > 64);
 }
 
+// fp32 on tensor cores (3xTF32, tf32_split.cu) where the GEMM is
+// compute-bound: both M and N above 64, or tcgen05 asked for explicitly.
+// Smaller fp32 problems keep the CUDA-core kernel (IEEE FMA in place).
+bool tf32_applies(const GemmArgs& g, const kf_gemm_config* user) {
+  if (g.dtype != KF_FP32 || g.n_peers > 0 || g.K == 0) return false;
+  const int kernel = user ? user->kernel : KF_GEMM_AUTO;
+  if (kernel == KF_GEMM_TCGEN05) return true;
+  return kernel == KF_GEMM_AUTO && g.M > 64 && g.N > 64;
+}
+
 // Whether the epilogue's 16-byte stores cannot reach C: its rows are off the
 // 16-byte grid (an odd N, a view starting at an odd column). Swapped (skinny)
 // tiles write C's columns and keep their element stores.
@@ -251,7 +271,21 @@ bool output_needs_stage(const GemmArgs& v, const kf_gemm_config& cfg) {
 bool plan_tc(const GemmArgs& g, const kf_gemm_config* user, const DeviceInfo& dev, int64_t have, TcPlan* out) {
   TcPlan& p = *out;
   p.view = g;
-  if (packing_applies(g, user)) {
+  const void* stand_in = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  if (tf32_applies(g, user)) {
+    // A'[M, 3Kp] and B'[N, 3Kp], both K-major: the kernel's K is 3 Kp.
+    p.split = true;
+    p.sa = plan_tf32_split(g.a, g.sa_m, g.sa_k, g.M, g.K, false);
+    p.sb = plan_tf32_split(g.b, g.sb_n, g.sb_k, g.N, g.K, true);
+    p.view.a = stand_in;
+    p.view.sa_m = p.sa.pitch;
+    p.view.sa_k = 1;
+    p.view.b = stand_in;
+    p.view.sb_n = p.sb.pitch;
+    p.view.sb_k = 1;
+    p.view.K = 3 * p.sa.kp;
+    p.view.tf32_split = true;
+  } else if (packing_applies(g, user)) {
     // K below one 16-byte vector is padded with zeros to 8: then both operands
     // need the padded extent, so both are copied.
     const int64_t kp = g.K < 8 ? 8 : g.K;
@@ -259,7 +293,6 @@ bool plan_tc(const GemmArgs& g, const kf_gemm_config* user, const DeviceInfo& de
     p.pack_b = kp != g.K || !tma_describable(g.b, g.sb_n, g.sb_k, g.N, g.K);
     // Stand-in aligned pointers until the workspace is known: only strides and
     // sizes decide the config.
-    const void* stand_in = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
     if (p.pack_a) {
       p.a = plan_pack(g.a, g.sa_m, g.sa_k, g.M, g.K, kp);
       p.view.a = stand_in;
@@ -354,6 +387,16 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
   if (plan_tc(g, user, *dev, have, &plan)) {
     GemmArgs& v = plan.view;
     char* dst = static_cast<char*>(g.workspace) + plan.offset();
+    if (plan.split) {
+      rc = launch_tf32_split(plan.sa, dst, s);
+      if (rc != KF_OK) return rc;
+      v.a = dst;
+      dst += plan.sa.bytes;
+      rc = launch_tf32_split(plan.sb, dst, s);
+      if (rc != KF_OK) return rc;
+      v.b = dst;
+      dst += plan.sb.bytes;
+    }
     if (plan.pack_a) {
       rc = launch_pack(plan.a, dst, s);
       if (rc != KF_OK) return rc;
@@ -377,12 +420,14 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
     if (rc != KF_OK || !plan.stage_c) return rc;
     return launch_unpack(plan.c, dst, s);
   }
-  if (plan.pack_a || plan.pack_b) {
+  if (plan.pack_a || plan.pack_b || plan.split) {
     if (user != nullptr && user->kernel == KF_GEMM_TCGEN05)
-      return set_error(KF_ERR_WORKSPACE, "operands TMA cannot describe are packed first: this call needs " +
-                                             std::to_string(plan.need()) + " bytes of workspace, got " +
-                                             std::to_string(have));
-    // no room to pack: the CUDA-core kernel reads the operands in place
+      return set_error(KF_ERR_WORKSPACE,
+                       std::string(plan.split ? "fp32 operands are split into TF32 parts first"
+                                              : "operands TMA cannot describe are packed first") +
+                           ": this call needs " + std::to_string(plan.need()) + " bytes of workspace, got " +
+                           std::to_string(have));
+    // no room to pack or split: the CUDA-core kernel reads the operands in place
   }
   // (an explicit stream-K request without enough workspace is refused by the launch)
   kf_gemm_config cfg = resolve_gemm_config(g, user, dev->sm_count);

@@ -2,6 +2,10 @@
 //
 //   C[M,N] = epilogue(A[M,K] . B[K,N])       fp16/bf16 in, fp32 accumulate
 //
+// and, with T = float, the same on TF32 operands (kind::tf32): the fp32 GEMM's
+// split operands (tf32_split.cu), K-major, whose extended K holds the three
+// partial products of the 3xTF32 scheme.
+//
 // One CTA per SM, 6 warps:
 //   warp 0      TMA producer: 2-D tiled bulk loads of A and B k-blocks into a
 //               `stages`-deep ring of 128-byte-swizzled shared-memory tiles,
@@ -62,6 +66,13 @@ constexpr int NUM_EPI_WARPS = 8;
 constexpr int NUM_EPI_THREADS = NUM_EPI_WARPS * 32;
 constexpr int NUM_THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
 constexpr int MAX_STAGES = 16;
+// TF32 tiles: columns of the accumulator one epilogue thread sums in registers
+// (half of BLOCK_N <= 128), and the K elements one TMEM chunk accumulates.
+constexpr int TF32_MAX_COLS = 64;
+#ifndef KF_TF32_PROMOTE_K
+#define KF_TF32_PROMOTE_K 256
+#endif
+constexpr int TF32_PROMOTE_K = KF_TF32_PROMOTE_K;
 constexpr int MIN_SMEM_PER_CTA = 120 * 1024;  // > half an SM: one CTA per SM
 constexpr uint64_t DRAIN_LIMIT_NS = 100000000ull;
 // Stream-K workspace layout: [tile arrival counters | 2 partial tiles per CTA];
@@ -82,6 +93,11 @@ struct TcParams {
   long long dp_tiles, sk_base, sk_iters;
   int tail_halves;  // half-width tiles after the whole ones (split tail)
   int stream_k;     // sk_iters > 0
+  // k-blocks per TMEM accumulation chunk (0: a segment is one chunk). The
+  // epilogue sums the chunks in fp32 registers: kind::tf32 accumulation over
+  // thousands of k loses bits (3xTF32 at K = 4096 measured 1.0e-5 relative
+  // error in one chunk, 5.7e-7 in chunks of 192).
+  int promote_kb;
   uint32_t idesc_half;
   void* c;
   long long sc_r, sc_c;
@@ -197,14 +213,14 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 template <typename T>
 __device__ __forceinline__ void load_bias16(const T* bias, int col0, int n, float (&b)[16]) {
   if (col0 + 16 <= n && (reinterpret_cast<uintptr_t>(bias + col0) & 15u) == 0) {
+    constexpr int PER_VEC = 16 / static_cast<int>(sizeof(T));
     const uint4* src = reinterpret_cast<const uint4*>(bias + col0);
-    const uint4 lo = __ldg(src), hi = __ldg(src + 1);
-    const T* e0 = reinterpret_cast<const T*>(&lo);
-    const T* e1 = reinterpret_cast<const T*>(&hi);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      b[j] = to_f32(e0[j]);
-      b[8 + j] = to_f32(e1[j]);
+    for (int v = 0; v < 16 / PER_VEC; ++v) {
+      const uint4 q = __ldg(src + v);
+      const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+      for (int j = 0; j < PER_VEC; ++j) b[v * PER_VEC + j] = to_f32(e[j]);
     }
   } else {
 #pragma unroll
@@ -246,8 +262,20 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col0
   epilogue16<T, EPI>(p, row, col0, acc, v);
   const long long off = static_cast<long long>(row) * p.sc_r + static_cast<long long>(col0) * p.sc_c;
   T* out = static_cast<T*>(p.c) + off;
-  const bool vec_ok = p.sc_c == 1 && col0 + 16 <= p.N &&
-                      (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && sizeof(T) == 2;
+  const bool vec_ok = p.sc_c == 1 && col0 + 16 <= p.N && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  if constexpr (sizeof(T) == 4) {
+    // fp32 output (no peers on this path): 64 bytes as four 16-byte stores
+    if (vec_ok) {
+      float4* dst = reinterpret_cast<float4*>(out);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (col0 + j < p.N) out[static_cast<long long>(j) * p.sc_c] = v[j];
+    }
+    return;
+  }
   if (vec_ok) {
     uint32_t packed[8];
 #pragma unroll
@@ -368,6 +396,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const __grid_constant__ CUtensorMap tm_b_half, const TcParams p,
                    const __grid_constant__ OutMaps<PEERS> out_maps) {
   extern __shared__ uint8_t smem_raw[];
+  // Elements in one 128-byte swizzle row (64 16-bit, 32 fp32), and per MMA K
+  // step (32 bytes: K = 16 for kind::f16, 8 for kind::tf32).
+  constexpr int ATOM = 128 / static_cast<int>(sizeof(T));
+  constexpr bool TF32 = sizeof(T) == 4;
+  static_assert(!(TF32 && PEERS), "the all-gather epilogue is compiled for 16-bit outputs");
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int S = p.stages;
@@ -452,7 +485,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int b_rows = seg_bn / CG;  // B rows this CTA stages
         const CUtensorMap* map_b = half ? &tm_b_half : &tm_b;
         const uint32_t tx_bytes =
-            (p.a_stage_bytes + static_cast<uint32_t>(b_rows * p.bk * 2)) * CG;
+            (p.a_stage_bytes + static_cast<uint32_t>(b_rows * p.bk * static_cast<int>(sizeof(T)))) * CG;
         const int m0 = m_blk * (BM * CG) + BM * static_cast<int>(crank);
         const int n0 = n_blk * p.bn + (half ? seg.half * seg_bn : 0) + b_rows * static_cast<int>(crank);
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
@@ -468,34 +501,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (leader) mbar_arrive_expect_tx(fb, tx_bytes);
             const uint32_t lb = mapa_shared(fb, 0);  // both CTAs count on the leader's barrier
             if (!p.a_mn) {
-              for (int j = 0; j < p.bk / 64; ++j)
-                tma_load_2d_pair(a_dst + j * (BM * 128), &tm_a, lb, k0 + 64 * j, m0);
+              for (int j = 0; j < p.bk / ATOM; ++j)
+                tma_load_2d_pair(a_dst + j * (BM * 128), &tm_a, lb, k0 + ATOM * j, m0);
             } else {
-              for (int i = 0; i < BM / 64; ++i)
-                tma_load_2d_pair(a_dst + i * (p.bk * 128), &tm_a, lb, m0 + 64 * i, k0);
+              for (int i = 0; i < BM / ATOM; ++i)
+                tma_load_2d_pair(a_dst + i * (p.bk * 128), &tm_a, lb, m0 + ATOM * i, k0);
             }
             if (!p.b_mn) {
-              for (int j = 0; j < p.bk / 64; ++j)
-                tma_load_2d_pair(b_dst + j * (b_rows * 128), map_b, lb, k0 + 64 * j, n0);
+              for (int j = 0; j < p.bk / ATOM; ++j)
+                tma_load_2d_pair(b_dst + j * (b_rows * 128), map_b, lb, k0 + ATOM * j, n0);
             } else {
-              for (int i = 0; i < b_rows / 64; ++i)
-                tma_load_2d_pair(b_dst + i * (p.bk * 128), map_b, lb, n0 + 64 * i, k0);
+              for (int i = 0; i < b_rows / ATOM; ++i)
+                tma_load_2d_pair(b_dst + i * (p.bk * 128), map_b, lb, n0 + ATOM * i, k0);
             }
           } else {
             mbar_arrive_expect_tx(fb, tx_bytes);
             if (!p.a_mn) {
-              for (int j = 0; j < p.bk / 64; ++j)
-                tma_load_2d(a_dst + j * (BM * 128), &tm_a, fb, k0 + 64 * j, m0);
+              for (int j = 0; j < p.bk / ATOM; ++j)
+                tma_load_2d(a_dst + j * (BM * 128), &tm_a, fb, k0 + ATOM * j, m0);
             } else {
-              for (int i = 0; i < BM / 64; ++i)
-                tma_load_2d(a_dst + i * (p.bk * 128), &tm_a, fb, m0 + 64 * i, k0);
+              for (int i = 0; i < BM / ATOM; ++i)
+                tma_load_2d(a_dst + i * (p.bk * 128), &tm_a, fb, m0 + ATOM * i, k0);
             }
             if (!p.b_mn) {
-              for (int j = 0; j < p.bk / 64; ++j)
-                tma_load_2d(b_dst + j * (b_rows * 128), map_b, fb, k0 + 64 * j, n0);
+              for (int j = 0; j < p.bk / ATOM; ++j)
+                tma_load_2d(b_dst + j * (b_rows * 128), map_b, fb, k0 + ATOM * j, n0);
             } else {
-              for (int i = 0; i < b_rows / 64; ++i)
-                tma_load_2d(b_dst + i * (p.bk * 128), map_b, fb, n0 + 64 * i, k0);
+              for (int i = 0; i < b_rows / ATOM; ++i)
+                tma_load_2d(b_dst + i * (p.bk * 128), map_b, fb, n0 + ATOM * i, k0);
             }
           }
           ++issued;
@@ -521,73 +554,89 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0 && leader) {
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
-      // Start-address steps in 16-byte units. K-major operands: a K=16 slice is
-      // 32 bytes inside a 128-byte swizzle row, and the next 64-element K atom
-      // starts `rows * 128` bytes on. MN-major operands: a K=16 slice is 16
-      // K-rows of 128 bytes, and one 64-deep atom is 4 slices.
+      // Start-address steps in 16-byte units. K-major operands: an MMA's K
+      // slice (16 16-bit or 8 fp32 elements) is 32 bytes inside a 128-byte
+      // swizzle row, and the next K atom starts `rows * 128` bytes on.
+      // MN-major operands (16-bit only): a K=16 slice is 16 K-rows of 128
+      // bytes, and one 64-deep atom is 4 slices.
       const uint32_t a_k_step = p.a_mn ? 2048 / 16 : 32 / 16;
       const uint32_t b_k_step = p.b_mn ? 2048 / 16 : 32 / 16;
       const uint32_t a_atom_step = p.a_mn ? 4 * 2048 / 16 : (BM * 128) / 16;
       const uint32_t a_lbo = p.a_mn ? static_cast<uint32_t>(p.bk * 128) : 16u;
       const uint32_t b_lbo = p.b_mn ? static_cast<uint32_t>(p.bk * 128) : 16u;
       while (ok && cursor_next(p, cur, seg, units)) {
-        if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, abort_flag, p.status,
-                       SITE_MMA_TMEM_EMPTY)) {
-          break;
-        }
-        tc_fence_after();
-        // A half-width tile: half the B rows per K atom and an N/2 instruction.
-        const int b_rows = (seg.half >= 0 ? p.bn / 2 : p.bn) / CG;
-        const uint32_t b_atom_step =
-            p.b_mn ? 4 * 2048 / 16 : static_cast<uint32_t>(b_rows * 128) / 16;
-        const uint32_t idesc = seg.half >= 0 ? p.idesc_half : p.idesc;
-        const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(p.bn);
-        for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
-          if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, p.status, SITE_MMA_FULL)) {
+        // A segment's k-blocks accumulate in TMEM as one chunk, or (promote_kb
+        // > 0) as chunks of promote_kb k-blocks, each into the next TMEM buffer,
+        // summed by the epilogue in fp32 registers.
+        for (int c0 = seg.kb0, c1; ok && c0 < seg.kb1; c0 = c1) {
+          c1 = p.promote_kb > 0 && seg.kb1 - c0 > p.promote_kb ? c0 + p.promote_kb : seg.kb1;
+          if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, abort_flag, p.status,
+                         SITE_MMA_TMEM_EMPTY)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(a_ring + static_cast<size_t>(stage) * p.a_stage_bytes);
-          const uint32_t b_base = smem_u32(b_ring + static_cast<size_t>(stage) * p.b_stage_bytes);
-          const uint64_t a_desc0 = smem_desc_sw128(a_base, a_lbo, 1024);
-          const uint64_t b_desc0 = smem_desc_sw128(b_base, b_lbo, 1024);
-          // The descriptors of one k-block differ only in their start address
-          // (bits 0-13, 16-byte units): step by constants, issue unrolled.
-          for (int atom = 0; atom < p.bk / 64; ++atom) {
+          // A half-width tile: half the B rows per K atom and an N/2 instruction.
+          const int b_rows = (seg.half >= 0 ? p.bn / 2 : p.bn) / CG;
+          const uint32_t b_atom_step =
+              p.b_mn ? 4 * 2048 / 16 : static_cast<uint32_t>(b_rows * 128) / 16;
+          const uint32_t idesc = seg.half >= 0 ? p.idesc_half : p.idesc;
+          const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(p.bn);
+          for (int kb = c0; kb < c1; ++kb) {
+            if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, p.status, SITE_MMA_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(a_ring + static_cast<size_t>(stage) * p.a_stage_bytes);
+            const uint32_t b_base = smem_u32(b_ring + static_cast<size_t>(stage) * p.b_stage_bytes);
+            const uint64_t a_desc0 = smem_desc_sw128(a_base, a_lbo, 1024);
+            const uint64_t b_desc0 = smem_desc_sw128(b_base, b_lbo, 1024);
+            // The descriptors of one k-block differ only in their start address
+            // (bits 0-13, 16-byte units): step by constants, issue unrolled.
+            for (int atom = 0; atom < p.bk / ATOM; ++atom) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(atom * a_atom_step + kk * a_k_step);
-              const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(atom * b_atom_step + kk * b_k_step);
-              const uint32_t accumulate = (kb > seg.kb0 || atom > 0 || kk > 0) ? 1u : 0u;
-              if constexpr (CG == 2) {
-                tc_mma_f16_pair(d_tmem, a_desc, b_desc, idesc, accumulate);
-              } else {
-                tc_mma_f16(d_tmem, a_desc, b_desc, idesc, accumulate);
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(atom * a_atom_step + kk * a_k_step);
+                const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(atom * b_atom_step + kk * b_k_step);
+                const uint32_t accumulate = (kb > c0 || atom > 0 || kk > 0) ? 1u : 0u;
+                if constexpr (CG == 2) {
+                  if constexpr (TF32) {
+                    tc_mma_tf32_pair(d_tmem, a_desc, b_desc, idesc, accumulate);
+                  } else {
+                    tc_mma_f16_pair(d_tmem, a_desc, b_desc, idesc, accumulate);
+                  }
+                } else {
+                  if constexpr (TF32) {
+                    tc_mma_tf32(d_tmem, a_desc, b_desc, idesc, accumulate);
+                  } else {
+                    tc_mma_f16(d_tmem, a_desc, b_desc, idesc, accumulate);
+                  }
+                }
               }
             }
+            // ring slot reusable (in every CTA of the group) once these MMAs finish
+            if constexpr (CG == 2) {
+              tc_commit_pair_to(empty0 + 8 * stage, 0x3);
+            } else {
+              tc_commit(empty0 + 8 * stage);
+            }
+            if (++stage == static_cast<uint32_t>(S)) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          // ring slot reusable (in every CTA of the group) once these MMAs finish
+          if (!ok) break;
+          // accumulator complete: wake the epilogue of every CTA of the group
           if constexpr (CG == 2) {
-            tc_commit_pair_to(empty0 + 8 * stage, 0x3);
+            tc_commit_pair_to(tfull0 + 8 * acc, 0x3);
           } else {
-            tc_commit(empty0 + 8 * stage);
+            tc_commit(tfull0 + 8 * acc);
           }
-          if (++stage == static_cast<uint32_t>(S)) {
-            stage = 0;
-            phase ^= 1u;
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
           }
-        }
-        if (!ok) break;
-        // accumulator complete: wake the epilogue of every CTA of the group
-        if constexpr (CG == 2) {
-          tc_commit_pair_to(tfull0 + 8 * acc, 0x3);
-        } else {
-          tc_commit(tfull0 + 8 * acc);
-        }
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
         }
       }
       // Every MMA issued must complete before TMEM is released.
@@ -610,6 +659,134 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t tempty_leader = CG == 2 ? mapa_shared(tempty0, 0) : tempty0;
     uint32_t acc = 0, acc_phase = 0;
     while (cursor_next(p, cur, seg, units)) {
+      if constexpr (TF32) {
+        // TF32 tiles (BLOCK_N <= 128: at most 64 columns per thread): the
+        // segment's TMEM chunks are summed into fp32 registers, then stored
+        // (a whole tile) or fixed up (stream-K) from the registers.
+        int m_blk, n_blk;
+        tile_coords(p, seg.tile, m_blk, n_blk);
+        const int seg_bn = seg.half >= 0 ? p.bn / 2 : p.bn;
+        const int chunk_split = (seg_bn / 16 + 1) / 2;
+        const int c_begin = half == 0 ? 0 : chunk_split * 16;
+        const int c_end = half == 0 ? chunk_split * 16 : seg_bn;
+        const int row = m_blk * (BM * CG) + BM * static_cast<int>(crank) + row_in_tile;
+        const int col_base = n_blk * p.bn + (seg.half >= 0 ? seg.half * seg_bn : 0);
+        float sums[TF32_MAX_COLS];
+#pragma unroll
+        for (int j = 0; j < TF32_MAX_COLS; ++j) sums[j] = 0.0f;
+        bool ok = true;
+        for (int c0 = seg.kb0, c1; c0 < seg.kb1; c0 = c1) {
+          c1 = p.promote_kb > 0 && seg.kb1 - c0 > p.promote_kb ? c0 + p.promote_kb : seg.kb1;
+          if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, p.status, SITE_EPI_TMEM_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t t_acc =
+              tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * static_cast<uint32_t>(p.bn);
+#pragma unroll
+          for (int g = 0; g < TF32_MAX_COLS / 16; g += 2) {
+            uint32_t r0[16], r1[16];
+            // warp-uniform: c_begin and c_end depend on the warp only
+            const bool on0 = c_begin + 16 * g < c_end, on1 = c_begin + 16 * (g + 1) < c_end;
+            __syncwarp();
+            if (on0) tmem_ld_16(t_acc + c_begin + 16 * g, r0);
+            if (on1) tmem_ld_16(t_acc + c_begin + 16 * (g + 1), r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (on0) sums[16 * g + j] += __uint_as_float(r0[j]);
+              if (on1) sums[16 * (g + 1) + j] += __uint_as_float(r1[j]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 2) {
+              mbar_arrive_cluster(tempty_leader + 8 * acc);
+            } else {
+              mbar_arrive(tempty0 + 8 * acc);
+            }
+          }
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if (seg.kb0 == 0 && seg.kb1 == p.kb_per_tile) {
+#pragma unroll
+          for (int g = 0; g < TF32_MAX_COLS / 16; ++g)
+            if (c_begin + 16 * g < c_end) store_chunk<T, EPI, false>(p, row, col_base + c_begin + 16 * g, sums + 16 * g);
+          continue;
+        }
+{
+          // Stream-K fix-up from the registers, as for the 16-bit tiles below:
+          // partials in [16-column chunk][row][16] slots, the last contributor
+          // sums them in contributor order.
+          const long long grid = units;
+          const long long t_start = static_cast<long long>(seg.tile) * p.kb_per_tile;
+          const long long rel = t_start - p.sk_base;
+          const long long c_first = owner_of(rel, p.sk_iters, grid);
+          const long long c_last = owner_of(rel + p.kb_per_tile - 1, p.sk_iters, grid);
+          const long long me = unit;
+          const size_t slot_elems = static_cast<size_t>(p.bn) * BM;
+          const long long my_slot = 2 * (me * CG + crank) + (cur.begin >= t_start ? 0 : 1);
+          float* mine = p.partials + static_cast<size_t>(my_slot) * slot_elems;
+          int* counter = p.counters + static_cast<size_t>(seg.tile) * CG + crank;
+#pragma unroll
+          for (int g = 0; g < TF32_MAX_COLS / 16; ++g) {
+            const int c = c_begin + 16 * g;
+            if (c >= c_end) continue;
+            float4* dst = reinterpret_cast<float4*>(mine + (static_cast<size_t>(c / 16) * BM + row_in_tile) * 16);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              __stcg(dst + q, make_float4(sums[16 * g + 4 * q], sums[16 * g + 4 * q + 1], sums[16 * g + 4 * q + 2],
+                                          sums[16 * g + 4 * q + 3]));
+          }
+          __threadfence();
+          epi_bar_sync();
+          if (ethread == 0) {
+            const int arrived = atomicAdd(counter, 1);
+            *last_flag = (arrived == static_cast<int>(c_last - c_first)) ? 1u : 0u;
+          }
+          epi_bar_sync();
+          if (*last_flag) {
+            __threadfence();
+#pragma unroll
+            for (int g = 0; g < TF32_MAX_COLS / 16; ++g) {
+              const int c = c_begin + 16 * g;
+              if (c >= c_end) continue;
+              float sum[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
+              for (long long cc = c_first; cc <= c_last; ++cc) {
+                if (cc == me) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) sum[j] += sums[16 * g + j];
+                  continue;
+                }
+                const long long cc_begin = sk_begin_of(p, cc, grid);
+                const long long slot = 2 * (cc * CG + crank) + (cc_begin >= t_start ? 0 : 1);
+                const float4* part = reinterpret_cast<const float4*>(
+                    p.partials + static_cast<size_t>(slot) * slot_elems + (static_cast<size_t>(c / 16) * BM + row_in_tile) * 16);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const float4 v = __ldcg(part + q);
+                  sum[4 * q] += v.x;
+                  sum[4 * q + 1] += v.y;
+                  sum[4 * q + 2] += v.z;
+                  sum[4 * q + 3] += v.w;
+                }
+              }
+              store_chunk<T, EPI, false>(p, row, col_base + c, sum);
+            }
+            if (ethread == 0) *counter = 0;  // leave the workspace clean
+          }
+          epi_bar_sync();
+        }
+        continue;
+      }
       if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, p.status, SITE_EPI_TMEM_FULL)) break;
       tc_fence_after();
       int m_blk, n_blk;
@@ -819,9 +996,11 @@ uint32_t tmem_cols_for(int bn) {
   return cols;
 }
 
+int elem_bytes(int dtype) { return dtype == KF_FP32 ? 4 : 2; }
+
 // Shared memory of one CTA: A rows (128) and this CTA's B rows per stage.
-int64_t smem_bytes_for(int bn, int bk, int stages, int cg, bool peer_stage = false) {
-  const int64_t ring = static_cast<int64_t>(stages) * (BM + bn / cg) * bk * 2;
+int64_t smem_bytes_for(int bn, int bk, int stages, int cg, int elem, bool peer_stage = false) {
+  const int64_t ring = static_cast<int64_t>(stages) * (BM + bn / cg) * bk * elem;
   return 1024 + ring + 8 * (2 * stages + 5) + 16 + (peer_stage ? GEMM_PEER_STAGE_SMEM : 0);
 }
 
@@ -840,19 +1019,23 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// A 2-D view [outer][inner] with `outer_stride` elements between rows.
+// A 2-D view [outer][inner] with `outer_stride` elements between rows; the box
+// is `box_inner` x `box_outer` elements (box_inner x element size = 128 bytes
+// for the swizzled operand tiles).
 int encode_map(CUtensorMap* map, int dtype, const void* ptr, uint64_t inner, uint64_t outer,
                int64_t outer_stride, uint32_t box_inner, uint32_t box_outer) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return set_error(KF_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
-  int64_t stride_bytes = outer_stride * 2;
-  if (outer <= 1) stride_bytes = ((static_cast<int64_t>(inner) * 2 + 15) / 16) * 16;
+  const int elem = elem_bytes(dtype);
+  int64_t stride_bytes = outer_stride * elem;
+  if (outer <= 1) stride_bytes = ((static_cast<int64_t>(inner) * elem + 15) / 16) * 16;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride_bytes)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t elem_strides[2] = {1, 1};
-  const CUtensorMapDataType t =
-      dtype == KF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType t = dtype == KF_FP32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                : dtype == KF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = enc(map, t, 2, const_cast<void*>(ptr), dims, strides, box, elem_strides,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -906,6 +1089,20 @@ void* kernel_ptr(int cg, bool peers) {
 }
 
 void* pick_kernel(int dtype, int epi, int cg, bool peers) {
+  if (dtype == KF_FP32) {  // TF32 split operands; never with peers (checked by the caller)
+    switch (epi) {
+      case KF_EPI_NONE: return cg == 2 ? reinterpret_cast<void*>(&tc_gemm_kernel<float, KF_EPI_NONE, 2, false>)
+                                       : reinterpret_cast<void*>(&tc_gemm_kernel<float, KF_EPI_NONE, 1, false>);
+      case KF_EPI_BIAS: return cg == 2 ? reinterpret_cast<void*>(&tc_gemm_kernel<float, KF_EPI_BIAS, 2, false>)
+                                       : reinterpret_cast<void*>(&tc_gemm_kernel<float, KF_EPI_BIAS, 1, false>);
+      case KF_EPI_BIAS_GELU_TANH:
+        return cg == 2 ? reinterpret_cast<void*>(&tc_gemm_kernel<float, KF_EPI_BIAS_GELU_TANH, 2, false>)
+                       : reinterpret_cast<void*>(&tc_gemm_kernel<float, KF_EPI_BIAS_GELU_TANH, 1, false>);
+      default:
+        return cg == 2 ? reinterpret_cast<void*>(&tc_gemm_kernel<float, KF_EPI_BIAS_GELU_ERF, 2, false>)
+                       : reinterpret_cast<void*>(&tc_gemm_kernel<float, KF_EPI_BIAS_GELU_ERF, 1, false>);
+    }
+  }
   if (dtype == KF_FP16) {
     switch (epi) {
       case KF_EPI_NONE: return kernel_ptr<__half, KF_EPI_NONE>(cg, peers);
@@ -924,7 +1121,7 @@ void* pick_kernel(int dtype, int epi, int cg, bool peers) {
 
 int cta_group_of(const kf_gemm_config& cfg) { return cfg.block_m == 2 * BM ? 2 : 1; }
 
-int validate_config(const kf_gemm_config& cfg, int b_mn, std::string* why) {
+int validate_config(const kf_gemm_config& cfg, int b_mn, int dtype, std::string* why) {
   if (cfg.block_m != BM && cfg.block_m != 2 * BM) {
     *why = "tcgen05 path supports BLOCK_M=128 (one SM) or 256 (an SM pair); got " +
            std::to_string(cfg.block_m);
@@ -940,9 +1137,17 @@ int validate_config(const kf_gemm_config& cfg, int b_mn, std::string* why) {
     *why = "an MN-major B operand needs each CTA's BLOCK_N share to be a multiple of 64";
     return KF_ERR_INVALID_CONFIG;
   }
-  if (cfg.block_k != 64 && cfg.block_k != 128) {
-    *why = "BLOCK_K must be 64 or 128 (whole 128-byte swizzle atoms); got " +
-           std::to_string(cfg.block_k);
+  if (dtype == KF_FP32 && cfg.block_n > 2 * TF32_MAX_COLS) {
+    *why = "TF32 tiles sum their accumulator chunks in registers: BLOCK_N must be at most " +
+           std::to_string(2 * TF32_MAX_COLS) + "; got " + std::to_string(cfg.block_n);
+    return KF_ERR_INVALID_CONFIG;
+  }
+  // One or two 128-byte swizzle atoms of K: 64 or 128 16-bit elements, 32 or
+  // 64 fp32 (TF32) elements.
+  const int atom = 128 / elem_bytes(dtype);
+  if (cfg.block_k != atom && cfg.block_k != 2 * atom) {
+    *why = "BLOCK_K must be " + std::to_string(atom) + " or " + std::to_string(2 * atom) +
+           " (whole 128-byte swizzle atoms); got " + std::to_string(cfg.block_k);
     return KF_ERR_INVALID_CONFIG;
   }
   if (cfg.stages < 2 || cfg.stages > MAX_STAGES) {
@@ -975,8 +1180,15 @@ bool tma_describable(const void* ptr, int64_t s_mn, int64_t s_k, int64_t mn, int
 }
 
 bool tcgen05_operands_ok(const GemmArgs& g, std::string* why) {
-  if (g.dtype != KF_FP16 && g.dtype != KF_BF16) {
-    if (why) *why = "tcgen05 kind::f16 path takes fp16/bf16 only";
+  if (g.dtype == KF_FP32) {
+    // fp32 runs as 3xTF32 on operands split into TF32 parts (tf32_split.cu),
+    // laid out K-major; plain fp32 operands never reach kind::tf32 directly.
+    if (!g.tf32_split || g.sa_k != 1 || g.sb_k != 1 || g.n_peers > 0) {
+      if (why) *why = "fp32 reaches tcgen05 only as TF32-split, K-major operands (no all-gather)";
+      return false;
+    }
+  } else if (g.dtype != KF_FP16 && g.dtype != KF_BF16) {
+    if (why) *why = "unknown dtype for tcgen05";
     return false;
   }
   if (operand_major(g.a, g.sa_m, g.sa_k, g.M, g.K) < 0 ||
@@ -993,11 +1205,12 @@ bool tcgen05_operands_ok(const GemmArgs& g, std::string* why) {
 int query_tcgen05_config(int dtype, const kf_gemm_config& cfg, int64_t* smem_bytes,
                          int32_t* tmem_cols) {
   std::string why;
-  if (dtype != KF_FP16 && dtype != KF_BF16)
-    return set_error(KF_ERR_INVALID_CONFIG, "tcgen05 path takes fp16/bf16 only");
-  int rc = validate_config(cfg, 0, &why);
+  if (dtype != KF_FP16 && dtype != KF_BF16 && dtype != KF_FP32)
+    return set_error(KF_ERR_INVALID_CONFIG, "unknown dtype for tcgen05");
+  int rc = validate_config(cfg, 0, dtype, &why);
   if (rc != KF_OK) return set_error(rc, why);
-  const int64_t smem = smem_bytes_for(cfg.block_n, cfg.block_k, cfg.stages, cta_group_of(cfg));
+  const int64_t smem =
+      smem_bytes_for(cfg.block_n, cfg.block_k, cfg.stages, cta_group_of(cfg), elem_bytes(dtype));
   if (smem_bytes) *smem_bytes = smem;
   if (tmem_cols) *tmem_cols = static_cast<int32_t>(tmem_cols_for(cfg.block_n));
   if (smem > 232448)
@@ -1055,21 +1268,25 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   const int a_major = operand_major(v.a, v.sa_r, v.sa_k, v.M, g.K);
   const int b_major = operand_major(v.b, v.sb_c, v.sb_k, v.N, g.K);
   if (a_major < 0 || b_major < 0) return set_error(KF_ERR_UNALIGNED, "operands not TMA-describable");
-  int rc = validate_config(cfg, b_major, &why);
+  int rc = validate_config(cfg, b_major, g.dtype, &why);
   if (rc != KF_OK) return set_error(rc, why);
+  if (g.dtype == KF_FP32 && (a_major != 0 || b_major != 0))
+    return set_error(KF_ERR_UNALIGNED, "TF32 operands must be K-major");
   if (v.M > INT32_MAX || v.N > INT32_MAX || g.K > INT32_MAX)
     return set_error(KF_ERR_UNSUPPORTED, "dimensions above 2^31 are not supported");
 
   const int cg = cta_group_of(cfg);
   const int bn = cfg.block_n, bk = cfg.block_k, S = cfg.stages;
   const int b_rows = bn / cg;
+  const int elem = elem_bytes(g.dtype);
+  const uint32_t atom = static_cast<uint32_t>(128 / elem);
   // The staged all-gather epilogue needs unit column stride and 16-byte
   // aligned rows in C and in every peer copy.
   bool peer_stage = g.n_peers > 0 && v.sc_c == 1 && (v.sc_r * 2) % 16 == 0 &&
                     (reinterpret_cast<uintptr_t>(g.c) & 15u) == 0;
   for (int i = 0; i < g.n_peers; ++i)
     peer_stage = peer_stage && (reinterpret_cast<uintptr_t>(g.peers[i]) & 15u) == 0;
-  const int64_t smem = smem_bytes_for(bn, bk, S, cg, peer_stage);
+  const int64_t smem = smem_bytes_for(bn, bk, S, cg, elem, peer_stage);
   if (smem > dev.max_smem_optin)
     return set_error(KF_ERR_INVALID_CONFIG, "shared memory " + std::to_string(smem) +
                                                 " B exceeds the device limit of " +
@@ -1077,11 +1294,11 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   const int64_t smem_request = smem < MIN_SMEM_PER_CTA ? MIN_SMEM_PER_CTA : smem;
 
   CUtensorMap tm_a, tm_b, tm_b_half;
-  rc = a_major == 0 ? encode_map(&tm_a, g.dtype, v.a, g.K, v.M, v.sa_r, 64, BM)
-                    : encode_map(&tm_a, g.dtype, v.a, v.M, g.K, v.sa_k, 64, bk);
+  rc = a_major == 0 ? encode_map(&tm_a, g.dtype, v.a, g.K, v.M, v.sa_r, atom, BM)
+                    : encode_map(&tm_a, g.dtype, v.a, v.M, g.K, v.sa_k, atom, bk);
   if (rc != KF_OK) return rc;
-  rc = b_major == 0 ? encode_map(&tm_b, g.dtype, v.b, g.K, v.N, v.sb_c, 64, b_rows)
-                    : encode_map(&tm_b, g.dtype, v.b, v.N, g.K, v.sb_k, 64, bk);
+  rc = b_major == 0 ? encode_map(&tm_b, g.dtype, v.b, g.K, v.N, v.sb_c, atom, b_rows)
+                    : encode_map(&tm_b, g.dtype, v.b, v.N, g.K, v.sb_k, atom, bk);
   if (rc != KF_OK) return rc;
   // Half-width tail tiles: an N/2 MMA needs N/2 a multiple of 16 per CTA pair
   // share, and MN-major B boxes stay 64 columns wide.
@@ -1089,7 +1306,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
                         (b_major == 0 || (b_rows / 2) % 64 == 0);
   tm_b_half = tm_b;
   if (split_ok && b_major == 0) {
-    rc = encode_map(&tm_b_half, g.dtype, v.b, g.K, v.N, v.sb_c, 64, b_rows / 2);
+    rc = encode_map(&tm_b_half, g.dtype, v.b, g.K, v.N, v.sb_c, atom, b_rows / 2);
     if (rc != KF_OK) return rc;
   }
 
@@ -1130,13 +1347,14 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
     }
   }
   p.status = dev.status;
-  p.idesc = instr_desc_f16(g.dtype == KF_BF16 ? 1u : 0u, static_cast<uint32_t>(a_major),
-                           static_cast<uint32_t>(b_major), BM * cg, static_cast<uint32_t>(bn));
-  p.idesc_half = instr_desc_f16(g.dtype == KF_BF16 ? 1u : 0u, static_cast<uint32_t>(a_major),
-                                static_cast<uint32_t>(b_major), BM * cg,
-                                static_cast<uint32_t>(bn / 2));
-  p.a_stage_bytes = static_cast<uint32_t>(BM * bk * 2);
-  p.b_stage_bytes = static_cast<uint32_t>(b_rows * bk * 2);
+  const uint32_t fmt = g.dtype == KF_FP32 ? 2u : g.dtype == KF_BF16 ? 1u : 0u;
+  p.idesc = instr_desc_f16(fmt, static_cast<uint32_t>(a_major), static_cast<uint32_t>(b_major), BM * cg,
+                           static_cast<uint32_t>(bn));
+  p.idesc_half = instr_desc_f16(fmt, static_cast<uint32_t>(a_major), static_cast<uint32_t>(b_major),
+                                BM * cg, static_cast<uint32_t>(bn / 2));
+  p.promote_kb = g.dtype == KF_FP32 ? TF32_PROMOTE_K / bk : 0;
+  p.a_stage_bytes = static_cast<uint32_t>(BM * bk * elem);
+  p.b_stage_bytes = static_cast<uint32_t>(b_rows * bk * elem);
   p.tmem_cols = tmem_cols_for(bn);
 
   void* fn = pick_kernel(g.dtype, g.epilogue, cg, g.n_peers > 0);

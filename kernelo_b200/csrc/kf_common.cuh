@@ -163,6 +163,18 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// The same with kind::tf32 (32-bit containers read as TF32, fp32 accumulate):
+// the fp32 GEMM's split operands, whose parts are already TF32 values.
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread completes.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile(
@@ -247,6 +259,15 @@ __device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ void tc_mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive on the barrier at this offset in every CTA of `cta_mask` when the
 // pair's MMAs issued so far complete.
 __device__ __forceinline__ void tc_commit_pair_to(uint32_t bar, uint16_t cta_mask) {
@@ -275,8 +296,9 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_
   return d;
 }
 
-// Instruction descriptor for kind::f16 with fp32 accumulation.
-// a_fmt/b_fmt: 0 = fp16, 1 = bf16. *_mn: operand is MN-major in shared memory.
+// Instruction descriptor with fp32 accumulation, for kind::f16 (fmt 0 = fp16,
+// 1 = bf16) and kind::tf32 (fmt 2 = tf32), which share the layout.
+// *_mn: operand is MN-major in shared memory.
 __host__ __device__ constexpr uint32_t instr_desc_f16(uint32_t fmt, uint32_t a_mn, uint32_t b_mn,
                                                       uint32_t m, uint32_t n) {
   return (1u << 4)            // D format: f32

@@ -44,6 +44,9 @@ struct GemmArgs {
   // into each of them as well (the all-gather of a column-sharded linear).
   void* peers[KF_MAX_PEERS] = {};
   int n_peers = 0;
+  // fp32 only: a and b are TF32-split operands (tf32_split.cu), K-major, K
+  // the extended length; the tcgen05 kernel runs them as kind::tf32.
+  bool tf32_split = false;
 };
 
 // Stream-K workspace layout (tcgen05 GEMM): one int32 arrival counter per
@@ -90,6 +93,20 @@ int launch_pack(const PackedOperand& p, void* dst, cudaStream_t stream);
 // copy: the GEMM writes the copy with vector stores, launch_unpack moves it to C.
 PackedOperand plan_output_stage(void* c, int64_t sc_m, int64_t sc_n, int64_t m, int64_t n);
 int launch_unpack(const PackedOperand& p, const void* staged, cudaStream_t stream);
+
+// fp32 operands split for 3xTF32 (tf32_split.cu): rows of [small|big|big]
+// (A, b_order false) or [big|small|big] (B, b_order true) TF32 parts, K
+// padded with zeros to kp (a multiple of 32), written K-major with `pitch`
+// = 3 kp elements. (s_r, s_k): the source's element strides of (row, k).
+struct SplitOperand {
+  const void* src = nullptr;
+  int64_t s_r = 0, s_k = 0;
+  int64_t rows = 0, K = 0, kp = 0, pitch = 0;
+  int64_t bytes = 0;  // 256-byte rounded
+  bool b_order = false;
+};
+SplitOperand plan_tf32_split(const void* src, int64_t s_r, int64_t s_k, int64_t rows, int64_t K, bool b_order);
+int launch_tf32_split(const SplitOperand& s, void* dst, cudaStream_t stream);
 
 // CUDA-core path: any strides, fp16/bf16/fp32.
 int launch_gemm_simt(const GemmArgs& args, const kf_gemm_config& cfg, cudaStream_t stream);

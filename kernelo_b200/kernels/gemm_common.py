@@ -168,9 +168,10 @@ def packs_by_default(m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: st
 def shape_allows_tcgen05(m: int, n: int, k: int, dtype: torch.dtype, *, b_layout: str) -> str | None:
     """Why operands of this shape cannot take the tcgen05 path, or None. Any
     16-bit layout can: operands TMA cannot describe are first packed into the
-    workspace as pitched copies (csrc/pack.cu)."""
-    if dtype not in (torch.float16, torch.bfloat16):
-        return "tcgen05 kind::f16 takes fp16/bf16 operands only"
+    workspace as pitched copies (csrc/pack.cu); fp32 operands are split into
+    K-major TF32 parts (csrc/tf32_split.cu) and run as 3xTF32 on kind::tf32."""
+    if dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        return "tcgen05 takes fp16/bf16 (kind::f16) or fp32 as 3xTF32 (kind::tf32)"
     return None
 
 
@@ -178,10 +179,23 @@ def default_swap(m: int, n: int) -> bool:
     return m <= 64 and n > m
 
 
+def tf32_split_k(k: int) -> int:
+    """The K the tcgen05 kernel sees for an fp32 problem: three TF32 segments of K
+    rounded up to a 32-element atom (mirrors tf32_split.cu)."""
+    return 3 * -(-k // 32) * 32
+
+
+def tf32_applies(m: int, n: int, k: int, dtype: torch.dtype) -> bool:
+    """fp32 runs as 3xTF32 on tensor cores by default when both M and N exceed 64
+    (mirrors tf32_applies in api.cu)."""
+    return dtype == torch.float32 and k > 0 and m > 64 and n > 64
+
+
 def default_tcgen05_config(
-    operation: str, m: int, n: int, k: int, *, b_layout: str, sm_count: int = 148
+    operation: str, m: int, n: int, k: int, *, b_layout: str, sm_count: int = 148, elem: int = 2
 ) -> KernelConfig:
-    """The tcgen05 config the library would choose for contiguous operands."""
+    """The tcgen05 config the library would choose for contiguous operands of
+    ``elem``-byte elements (4: the TF32-split fp32 operands, K the split K)."""
     swap = default_swap(m, n)
     m_k, n_k = (n, m) if swap else (m, n)
     # B' (the kernel's second operand) is MN-major for matmul's row-major B
@@ -190,12 +204,14 @@ def default_tcgen05_config(
     pair_tiles = -(-m_k // 256) * -(-n_k // 256)
     cg = 2 if (m_k >= 256 and n_k >= 128 and pair_tiles >= sm_count // 2) else 1
     quantum = (64 if b_mn else 16) * cg
-    if n_k <= 256:
+    widest = 128 if elem == 4 else 256  # TF32 tiles sum their chunks in registers
+    if n_k <= widest:
         block_n = max(quantum, -(-n_k // quantum) * quantum)
     else:
-        block_n = 256
-    block_k = 128 if (cg == 2 and k >= 512) else 64
-    per_stage = (TC_BLOCK_M + block_n // cg) * block_k * 2
+        block_n = widest
+    atom = 128 // elem  # elements per 128-byte swizzle row
+    block_k = 2 * atom if (cg == 2 and k >= 512) else atom
+    per_stage = (TC_BLOCK_M + block_n // cg) * block_k * elem
     stages = max(2, min(12, (SM100_SMEM_PER_BLOCK - 1024 - 256) // per_stage))
     tiles_m = -(-m_k // (TC_BLOCK_M * cg))
     tiles = tiles_m * -(-n_k // block_n)
@@ -204,7 +220,7 @@ def default_tcgen05_config(
     # stream-K for a long K and narrower whole tiles for a short one; else the split tail
     if k_blocks < 4:
         stream_k = 2
-    elif cg == 1 and tiles < sm_count and k_blocks < 16:
+    elif cg == 1 and tiles < sm_count and (k_blocks < 16 or tiles * k_blocks < 8 * sm_count):
         quantum = 64 if b_mn else 16
         for bn in (128, 64):
             if tiles >= sm_count or bn >= block_n or bn % quantum:
@@ -216,7 +232,7 @@ def default_tcgen05_config(
         stream_k = 1 if (cg == 1 and tiles < sm_count) else 3
     # A panels of one raster group within ~48 MB of L2 (mirrors api.cu)
     tile_rows = TC_BLOCK_M * cg
-    group_m = max(1, min(-(-m_k // tile_rows), (48 << 20) // max(1, tile_rows * k * 2)))
+    group_m = max(1, min(-(-m_k // tile_rows), (48 << 20) // max(1, tile_rows * k * elem)))
     return KernelConfig(
         operation,
         KERNEL=KERNEL_TCGEN05,
@@ -244,13 +260,17 @@ def default_gemm_config(
 ) -> KernelConfig:
     """The library's choice for contiguous operands (mirrors gemm_common in api.cu): the 16-row
     tile kernel for up to 32 rows of x against a K-contiguous B, the column GEMV for up to 8
-    rows against an N-contiguous B, else tcgen05 tiles (operands TMA cannot describe packed
-    first when the problem is not skinny), else the CUDA-core kernel."""
+    rows against an N-contiguous B, fp32 beyond 64 x 64 as 3xTF32 tcgen05 tiles, else tcgen05
+    tiles (operands TMA cannot describe packed first when the problem is not skinny), else the
+    CUDA-core kernel."""
     if b_layout == "nk" and tile_rows_reject(m, k, dtype) is None:
         warps, pairs = tile_rows_default(m)
         return KernelConfig(operation, KERNEL=KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
     if columns_reject(m, n, k, dtype, b_layout=b_layout) is None:
         return KernelConfig(operation, KERNEL=KERNEL_COLUMNS)
+    if tf32_applies(m, n, k, dtype):
+        # both operands split into K-major TF32 parts first
+        return default_tcgen05_config(operation, m, n, tf32_split_k(k), b_layout="nk", sm_count=sm_count, elem=4)
     if dtype in (torch.float16, torch.bfloat16) and tma_misfit(m, n, k, b_layout=b_layout) is None:
         return default_tcgen05_config(operation, m, n, k, b_layout=b_layout, sm_count=sm_count)
     if packs_by_default(m, n, k, dtype, b_layout=b_layout):

@@ -10,14 +10,16 @@ library's kernels can actually run:
 GEMM (``matmul``, ``fused_linear``, ``fused_linear_erf``, ``gemv``)
     tcgen05 tiles: ``BLOCK_M`` {128 (one SM), 256 (an SM pair, cta_group::2,
     on a 2x1 cluster)} x ``BLOCK_N`` {16, 64, 128, 192, 224, 256} x
-    ``BLOCK_K`` {64, 128} x ``num_stages`` (shared-memory ring depth)
+    ``BLOCK_K`` {one, two 128-byte swizzle atoms: 64, 128 16-bit or 32, 64
+    fp32 elements} x ``num_stages`` (shared-memory ring depth)
     {2, 3, 4, 6, 8} x ``STREAM_K`` (tile schedule: 1 stream-K, 2 whole
     tiles, 3 whole tiles with the last partial wave split into half-width
     tiles) = 360 points; ``SWAP_AB`` follows the shape (skinny M puts the
     weight on the 128-row side) and ``GROUP_M`` (the L2 raster width) the
-    library's rule. Plus the 16-row tile GEMV's compiled shapes for
-    K-contiguous weights, and the CUDA-core tiles that serve fp32 and
-    operands no TMA tensor map can describe.
+    library's rule. fp32 tiles run as 3xTF32 on split K-major operands (the
+    kernel's K is three TF32 segments). Plus the 16-row tile GEMV's compiled
+    shapes for K-contiguous weights, the column GEMV for an N-contiguous B,
+    and the CUDA-core tiles (IEEE fp32, any strides).
 
     Limits applied as named rules: 227 KiB of shared memory per CTA, 512
     TMEM columns per SM (a double-buffered fp32 accumulator takes 2 x
@@ -48,6 +50,8 @@ from collections import Counter
 from collections.abc import Iterator
 from dataclasses import dataclass
 from itertools import product
+
+import torch
 
 from kernelo_b200.dtypes import itemsize
 from kernelo_b200.kernels import gemm_common as gc
@@ -214,10 +218,30 @@ class _Sm100GemmSpace(SearchSpace):
         d = problem.dims_dict
         return d["M"], d["N"], d["K"]
 
+    @staticmethod
+    def tf32(problem: Problem) -> bool:
+        """fp32 tcgen05 tiles run on TF32-split operands (3xTF32)."""
+        return problem.dtype == torch.float32
+
+    def tc_k(self, problem: Problem) -> int:
+        """K as the tcgen05 kernel sees it: fp32's three TF32 segments."""
+        k = self.dims(problem)[2]
+        return gc.tf32_split_k(k) if self.tf32(problem) else k
+
+    def tc_b_layout(self, problem: Problem) -> str:
+        """B's layout as the tcgen05 kernel sees it: the split fp32 B is K-major."""
+        return "nk" if self.tf32(problem) else self.b_layout
+
+    def block_k_values(self, problem: Problem) -> tuple[int, ...]:
+        """One or two 128-byte swizzle atoms of K."""
+        atom = 128 // problem.itemsize
+        return (atom, 2 * atom)
+
     def group_m(self, block_m: int, problem: Problem) -> int:
         """Raster group width: as many M tiles as keep their A panels within
         GROUP_L2_BYTES of L2 (so each group streams B once)."""
-        m, n, k = self.dims(problem)
+        m, n, _ = self.dims(problem)
+        k = self.tc_k(problem)
         m_k = n if gc.default_swap(m, n) else m
         rows = max(block_m, gc.TC_BLOCK_M)
         return max(1, min(ceil_div(m_k, rows), self.GROUP_L2_BYTES // max(1, rows * k * problem.itemsize)))
@@ -247,8 +271,8 @@ class _Sm100GemmSpace(SearchSpace):
             # decode shapes against a row-major (K, N) B: the column GEMV
             yield KernelConfig(self.operation, KERNEL=gc.KERNEL_COLUMNS)
         swap = 1 if gc.default_swap(m, n) else 2
-        for bm, bn, bk, stages, schedule in product(self.BLOCK_M, self.BLOCK_N, self.BLOCK_K, self.NUM_STAGES,
-                                                    self.SCHEDULES):
+        for bm, bn, bk, stages, schedule in product(self.BLOCK_M, self.BLOCK_N, self.block_k_values(problem),
+                                                    self.NUM_STAGES, self.SCHEDULES):
             yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TCGEN05, BLOCK_M=bm, BLOCK_N=bn, BLOCK_K=bk,
                                GROUP_M=self.group_m(bm, problem), num_stages=stages, STREAM_K=schedule,
                                SWAP_AB=swap, CLUSTER_M=gc.cta_group(bm), CLUSTER_N=1)
@@ -285,7 +309,7 @@ class _Sm100GemmSpace(SearchSpace):
         tiles = self.output_tiles(config, problem)
         if config["KERNEL"] == gc.KERNEL_TCGEN05 and config.get("STREAM_K") == 1:
             # stream-K deals the (tile, k-block) iterations over a persistent grid
-            iters = tiles * ceil_div(self.dims(problem)[2], config["BLOCK_K"]) * gc.cta_group(config["BLOCK_M"])
+            iters = tiles * ceil_div(self.tc_k(problem), config["BLOCK_K"]) * gc.cta_group(config["BLOCK_M"])
             return min(gc.SM100_SMS, iters)
         return tiles * (gc.cta_group(config["BLOCK_M"]) if config["KERNEL"] == gc.KERNEL_TCGEN05 else 1)
 
@@ -298,7 +322,7 @@ class _Sm100GemmSpace(SearchSpace):
             return f"stream-K: {tiles} tiles exceed the {self.STREAM_K_MAX_TILES // cg} it keeps counters for"
         if schedule == 3:
             bn = config["BLOCK_N"]
-            mn_major_b = self.b_layout == "kn" and config["SWAP_AB"] != 1
+            mn_major_b = self.tc_b_layout(problem) == "kn" and config["SWAP_AB"] != 1
             if (bn // 2) % (16 * cg) != 0 or (mn_major_b and (bn // cg // 2) % 64 != 0):
                 return f"split tail: half of BLOCK_N={bn} is not a tile the MMA and TMA boxes take"
             units = caps.sm_count // cg
@@ -325,6 +349,10 @@ class _Sm100GemmSpace(SearchSpace):
             return f"SM pair: BLOCK_N={bn} does not split into two 16-column halves"
         if bk * itemsize(problem.dtype) < 128:
             return f"swizzle atom: BLOCK_K={bk} is less than one 128-byte swizzle row"
+        if bk * itemsize(problem.dtype) > 256:
+            return f"swizzle atom: BLOCK_K={bk} is more than two 128-byte swizzle rows"
+        if self.tf32(problem) and bn > 128:
+            return f"TF32 register sums: BLOCK_N={bn} exceeds 128"
         smem = self.shared_memory_bytes(config, problem)
         if smem > caps.max_shared_memory_per_block:
             return (f"shared memory: {smem // 1024} KiB of tiles exceeds the "
@@ -333,15 +361,16 @@ class _Sm100GemmSpace(SearchSpace):
         if tmem > caps.tmem_columns_per_sm:
             return f"TMEM: {tmem} accumulator columns exceed {caps.tmem_columns_per_sm} per SM"
         swapped = config["SWAP_AB"] == 1
-        if self.b_layout == "kn" and not swapped and (bn // cg) % 64 != 0:
+        b_layout = self.tc_b_layout(problem)
+        if b_layout == "kn" and not swapped and (bn // cg) % 64 != 0:
             return f"MN-major B: BLOCK_N={bn} gives each CTA a share that is not 64-column TMA boxes"
         m_k, n_k = self.kernel_view(config, problem)
-        smallest = min(v for v in self.BLOCK_N if self.b_layout != "kn" or swapped or v % 64 == 0)
+        smallest = min(v for v in self.BLOCK_N if b_layout != "kn" or swapped or v % 64 == 0)
         if bn > 2 * n_k and bn > smallest:
             return f"tile overshoot: BLOCK_N={bn} for N={n_k}"
         if cg == 2 and m_k <= gc.TC_BLOCK_M:
             return f"tile overshoot: BLOCK_M={bm} for M={m_k}"
-        k_iters = ceil_div(k, bk)
+        k_iters = ceil_div(self.tc_k(problem), bk)
         if stages > 2 and k_iters < stages:
             return f"pipeline cannot fill: {k_iters} K iterations for num_stages={stages}"
         return self._schedule_reason(config, problem, caps)

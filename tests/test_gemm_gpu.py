@@ -142,9 +142,9 @@ def test_infeasible_config_raises_out_of_resources(device):
     a, b = operands(64, 72, 64, torch.float16, device)  # K=72 is fine, N=64 is fine
     with pytest.raises(native.OutOfResources):
         matmul(a, b, config=tc(BLOCK_N=256, BLOCK_K=64, num_stages=8))  # 384 KiB of smem
-    c, d = operands(64, 512, 64, torch.float32, device)  # fp32 has no tcgen05 MMA
-    with pytest.raises(native.OutOfResources):
-        matmul(c, d, config=tc())
+    c, d = operands(64, 512, 64, torch.float32, device)  # fp32 tiles take 32- or 64-element K blocks
+    with pytest.raises(native.OutOfResources, match="BLOCK_K must be 32 or 64"):
+        matmul(c, d, config=tc(BLOCK_K=128))
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])

@@ -114,14 +114,27 @@ def test_tmem_budget_is_a_device_property(b200_caps, a100_caps):
     assert reason is not None and ("TMEM" in reason or "shared memory" in reason)
 
 
-def test_fp32_falls_back_to_simt_and_unaligned_16bit_packs(b200_caps):
-    """fp32 has no tcgen05 path; 16-bit operands TMA cannot describe (the prime
-    sweep shapes) are packed for tcgen05, which becomes the library default."""
+def test_fp32_runs_as_3xtf32_and_unaligned_16bit_packs(b200_caps):
+    """fp32 beyond 64 x 64 runs as 3xTF32 tcgen05 tiles on split operands (K is
+    three 32-aligned segments, BLOCK_K one or two 32-element atoms, B K-major
+    whatever its layout), the CUDA-core tiles staying candidates; 16-bit
+    operands TMA cannot describe (the prime sweep shapes) are packed for
+    tcgen05, which becomes the library default."""
     fp32 = Problem.create("matmul", "fp32", M=4099, N=4099, K=4099)
-    cands = MatmulSearchSpace().candidates(fp32, b200_caps)
-    assert cands and all(c["KERNEL"] == gc.KERNEL_SIMT for c in cands)
-    reasons = {r for _, r in MatmulSearchSpace().generate(fp32, b200_caps).rejected}
-    assert any(r.startswith("tcgen05 kind") for r in reasons)
+    space = MatmulSearchSpace()
+    cands = space.candidates(fp32, b200_caps)
+    assert cands[0]["KERNEL"] == gc.KERNEL_TCGEN05 and cands[0]["BLOCK_K"] in (32, 64)
+    assert space.tc_k(fp32) == gc.tf32_split_k(4099) == 3 * 4128
+    assert {c["BLOCK_K"] for c in cands if c["KERNEL"] == gc.KERNEL_TCGEN05} <= {32, 64}
+    assert any(c["KERNEL"] == gc.KERNEL_SIMT for c in space.grid(fp32))
+    # the split B is K-major: 16-column tiles are not refused as MN-major boxes
+    narrow = KernelConfig("matmul", KERNEL=1, BLOCK_M=128, BLOCK_N=16, BLOCK_K=32, GROUP_M=1, num_stages=4,
+                          STREAM_K=2, SWAP_AB=2, CLUSTER_M=1, CLUSTER_N=1)
+    assert "MN-major" not in (space.reject_reason(narrow, fp32, b200_caps) or "")
+    assert space.reject_reason(narrow.replace(BLOCK_K=16), fp32, b200_caps).startswith("swizzle atom")
+    assert space.reject_reason(narrow.replace(BLOCK_K=128), fp32, b200_caps).startswith("swizzle atom")
+    small = gc.default_gemm_config("matmul", 64, 4096, 4096, torch.float32, b_layout="kn")
+    assert small["KERNEL"] == gc.KERNEL_SIMT, "skinny fp32 keeps IEEE FMA in place"
     for problem in (Problem.create("matmul", "fp16", M=4099, N=4099, K=4099),
                     Problem.create("matmul", "bf16", M=1021, N=2053, K=509)):
         cands = MatmulSearchSpace().candidates(problem, b200_caps)
