@@ -32,8 +32,12 @@
 // Replaces the reference's matmul launch at decode shapes
 // (kernelforge/kernels/matmul.py:132-155 with M in {1, 4, 16}); fp32
 // accumulation and one output rounding as in the reference's matmul.
+#include <cooperative_groups.h>
+
 #include "kf_common.cuh"
 #include "kf_internal.h"
+
+namespace cg = cooperative_groups;
 
 namespace kf {
 namespace {
@@ -47,6 +51,10 @@ struct GemvMmaParams {
   long long sy_m, sy_n;
   const void* bias;  // [N], for the bias / GELU epilogues
   int M, N, K;
+  // CTAs per weight tile (a thread-block cluster along x): the tile's K extent
+  // is split over ks x S warps and the CTAs' sums meet in the leader's shared
+  // memory. 1 unless the tiles are too few to fill the GPU (a column shard).
+  int ks;
   // Peer copies of y (same strides; the element that corresponds to y[0, 0]):
   // every output element is stored there too -- the decode-shape all-gather.
   int n_peers;
@@ -97,12 +105,15 @@ __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams
   __shared__ float4 part[S > 1 ? S - 1 : 1][32][NT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int n0 = blockIdx.x * 16;
+  const int ks = p.ks;
+  const int part_rank = static_cast<int>(blockIdx.x) % ks;  // == the rank in the cluster
+  const int n0 = static_cast<int>(blockIdx.x) / ks * 16;
   const int nvec = p.K / 8;  // 16-byte vectors per row (K % 8 == 0)
   // This warp's K slice, in whole quads of vectors.
   const int quads = (nvec + 3) / 4;
-  const int q0 = static_cast<int>(static_cast<long long>(quads) * warp / S);
-  const int q1 = static_cast<int>(static_cast<long long>(quads) * (warp + 1) / S);
+  const int slice = part_rank * S + warp;  // of ks * S slices
+  const int q0 = static_cast<int>(static_cast<long long>(quads) * slice / (ks * S));
+  const int q1 = static_cast<int>(static_cast<long long>(quads) * (slice + 1) / (ks * S));
   const int ra = min(n0 + g, p.N - 1), rb = min(n0 + g + 8, p.N - 1);  // clamped rows are not stored
   const uint4* wa = reinterpret_cast<const uint4*>(static_cast<const T*>(p.w) + ra * p.sw_n);
   const uint4* wb = reinterpret_cast<const uint4*>(static_cast<const T*>(p.w) + rb * p.sw_n);
@@ -174,18 +185,47 @@ __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams
         part[warp - 1][lane][nt] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
     }
     __syncthreads();
-    if (warp > 0) return;
+    if (warp == 0) {
 #pragma unroll
-    for (int s = 0; s < S - 1; ++s)
+      for (int s = 0; s < S - 1; ++s)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const float4 o = part[s][lane][nt];
-        acc[nt][0] += o.x;
-        acc[nt][1] += o.y;
-        acc[nt][2] += o.z;
-        acc[nt][3] += o.w;
-      }
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 o = part[s][lane][nt];
+          acc[nt][0] += o.x;
+          acc[nt][1] += o.y;
+          acc[nt][2] += o.z;
+          acc[nt][3] += o.w;
+        }
+    }
   }
+  if (ks > 1) {
+    // Across the cluster: every CTA's warp 0 leaves its sum in its own shared
+    // memory; the leader adds the others' in rank order (deterministic) and
+    // runs the epilogue. No thread exits before both cluster barriers.
+    __shared__ float4 cta_sum[32][NT];
+    cg::cluster_group cluster = cg::this_cluster();
+    if (warp == 0 && part_rank != 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) cta_sum[lane][nt] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    }
+    cluster.sync();
+    if (warp == 0 && part_rank == 0) {
+      for (int r = 1; r < ks; ++r) {
+        const float4* other = cluster.map_shared_rank(&cta_sum[0][0], static_cast<unsigned>(r));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 o = other[lane * NT + nt];
+          acc[nt][0] += o.x;
+          acc[nt][1] += o.y;
+          acc[nt][2] += o.z;
+          acc[nt][3] += o.w;
+        }
+      }
+    }
+    cluster.sync();  // the others' shared memory stays until the leader has read it
+    if (part_rank != 0) return;
+  }
+  if (warp > 0) return;
   // D fragment: acc[nt][0..1] = rows n0+g, x rows 8nt+2t, +1; [2..3] = rows n0+g+8.
   // The fused linear's epilogue (bias[n], then GELU) runs here, before the
   // one rounding, as in the GEMM.
@@ -214,18 +254,49 @@ __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams
       }
     }
   }
-  // The peer barrier that follows on the stream publishes these stores with a
-  // system-scope release; this fence orders them before the kernel ends.
-  if (p.n_peers > 0) __threadfence_system();
+  // No fence here: the peer barrier that follows on the stream starts after
+  // this kernel has completed, and its system-scope fence before the release
+  // store is cumulative over these stores. (A fence.sc.sys at the end of
+  // every CTA measured +9 us on a 2-way shard of 11008 x 4096, 11 -> 20 us,
+  // with the "peer" copy in local memory as much as over NVLink.)
 }
 
 template <typename T, int NT, int S, int U, int EPI>
 int launch_shape(const GemvMmaParams& p, cudaStream_t stream) {
   const unsigned tiles = static_cast<unsigned>((p.N + 15) / 16);
-  gemv_mma_kernel<T, NT, S, U, EPI><<<tiles, 32 * S, 0, stream>>>(p);
-  const cudaError_t err = cudaGetLastError();
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(tiles * static_cast<unsigned>(p.ks));
+  lc.blockDim = dim3(32 * S);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (p.ks > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(p.ks);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+  }
+  const cudaError_t err = cudaLaunchKernelEx(&lc, gemv_mma_kernel<T, NT, S, U, EPI>, p);
   if (err != cudaSuccess) return cuda_error(err, "launch(gemv mma)");
   return KF_OK;
+}
+
+// CTAs per weight tile: the fewest (1, 2, 4, 8) that give at least four CTAs
+// per SM -- a tile's CTA streams its weights for about the whole kernel, so
+// fewer CTAs than that leave HBM idle (a 2-way column shard of 11008 rows:
+// 344 tiles measured 16.6 us, as long as the whole GEMV).
+int default_tile_split(long long tiles) {
+  static thread_local int cached_device = -1, sms = 148;
+  int device = 0;
+  if (cudaGetDevice(&device) == cudaSuccess && device != cached_device) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && v > 0) sms = v;
+    cached_device = device;
+  }
+  int ks = 1;
+  while (ks < 8 && tiles * ks < 4LL * sms) ks *= 2;
+  return ks;
 }
 
 // Launch shapes (S warps per tile, U vector pairs per batch per lane; U = 1
@@ -311,6 +382,9 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
   p.bias = bias;
+  p.ks = cfg.cluster_m > 0 ? cfg.cluster_m : default_tile_split((N + 15) / 16);
+  if (p.ks != 1 && p.ks != 2 && p.ks != 4 && p.ks != 8)
+    return set_error(KF_ERR_INVALID_CONFIG, "tile GEMV: CLUSTER_M (CTAs per weight tile) must be 1, 2, 4 or 8");
   p.n_peers = n_peers;
   for (int j = 0; j < n_peers; ++j) {
     if (peers[j] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer output pointer");

@@ -6,9 +6,11 @@
 // One warp: lane t < world - 1 owns peer t. It writes `epoch` into the slot
 // of this rank in that peer's signal array with a release store at system
 // scope, then polls this rank's own slot for that peer with acquire loads at
-// system scope until it reads `epoch` or a later one. The GEMM that precedes
-// this kernel on the stream ended with a system-scope fence, so a peer that
-// observes the signal also observes the data. Every wait is bounded by
+// system scope until it reads `epoch` or a later one. The GEMM or GEMV that
+// stored into the peers precedes this kernel on the stream and has completed
+// when it starts; the system-scope fence before the release store is
+// cumulative over those stores, so a peer that observes the signal also
+// observes the data. Every wait is bounded by
 // %globaltimer: on timeout the kernel records
 // KF_ERR_TIMEOUT | SITE_PEER_BARRIER << 8 in the device status word and
 // returns, leaving the context usable.

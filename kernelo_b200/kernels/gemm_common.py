@@ -46,6 +46,17 @@ def tile_rows_default(m: int) -> tuple[int, int]:
     return {1: (8, 1), 2: (6, 4), 4: (4, 4)}[tile_rows_groups(m)]
 
 
+def tile_rows_split(n: int, sm_count: int = 148) -> int:
+    """CTAs per 16-row weight tile the tile GEMV uses by default (mirrors
+    default_tile_split in gemv_mma.cu): the fewest of 1, 2, 4, 8 that give
+    at least four CTAs per SM, the tile's K split over a thread-block cluster."""
+    tiles = -(-n // 16)
+    ks = 1
+    while ks < 8 and tiles * ks < 4 * sm_count:
+        ks *= 2
+    return ks
+
+
 def tile_rows_reject(m: int, k: int, dtype: torch.dtype) -> str | None:
     """Why the tile GEMV cannot take this contiguous problem (None: it can)."""
     if dtype not in (torch.float16, torch.bfloat16):

@@ -501,6 +501,34 @@ def test_gemv_tile_rows_every_shape(shape, m, device):
          context=f"shape {shape} M={m}")
 
 
+@pytest.mark.parametrize("split", [1, 2, 4, 8])
+@pytest.mark.parametrize("m,n,k", [(1, 5504, 4096), (16, 1376, 4096), (4, 1000, 1032), (32, 17, 24), (2, 40, 8)])
+def test_gemv_tile_rows_split_over_a_cluster(split, m, n, k, device):
+    """A weight tile's K extent split over a cluster of 1-8 CTAs (summed in the
+    leader's shared memory in rank order): column shards with few tiles, K of
+    a single vector (most CTAs of the cluster get no K), ragged N; and the same
+    bits whatever the order the CTAs finish in (two runs agree exactly)."""
+    gen = torch.Generator().manual_seed(split * 100 + m)
+    x = torch.randn(m, k, generator=gen).half().to(device)
+    w = (torch.randn(n, k, generator=gen) * k ** -0.5).half().to(device)
+    cfg = KernelConfig("gemv", KERNEL=4, BLOCK_M=6 if m > 8 else 8, num_stages=4 if m > 8 else 1, CLUSTER_M=split)
+    out = gemv(x, w, config=cfg)
+    gate(ref.gemv_ref(host(x), host(w)), out, torch.float16, context=f"split {split} {m}x{n}x{k}")
+    assert torch.equal(out, gemv(x, w, config=cfg))
+
+
+def test_gemv_tile_rows_default_split_fills_the_gpu(device):
+    """Few tiles (a column shard) take a K split by default: the result matches
+    the unsplit kernel's within the gate and the launch is at least 4 CTAs per SM."""
+    from kernelo_b200.kernels import gemm_common as gc
+
+    assert gc.tile_rows_split(11008) == 1 and gc.tile_rows_split(5504) == 2 and gc.tile_rows_split(1376) == 8
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(4, 4096, generator=gen).half().to(device)
+    w = (torch.randn(2752, 4096, generator=gen) * 4096 ** -0.5).half().to(device)
+    gate(ref.gemv_ref(host(x), host(w)), gemv(x, w), torch.float16)
+
+
 def test_gemv_tile_rows_edges_and_strides(device):
     """K of one and two vectors, fewer weight rows than a tile, padded weight and
     x rows (16-byte aligned), y written transposed."""
