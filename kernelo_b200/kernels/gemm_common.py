@@ -198,8 +198,8 @@ def tf32_split_k(k: int) -> int:
 
 def tf32_applies(m: int, n: int, k: int, dtype: torch.dtype) -> bool:
     """fp32 runs as 3xTF32 on tensor cores by default when both M and N exceed 64
-    (mirrors tf32_applies in api.cu)."""
-    return dtype == torch.float32 and k > 0 and m > 64 and n > 64
+    and the problem has at least 2^27 multiply-adds (mirrors tf32_applies in api.cu)."""
+    return dtype == torch.float32 and k > 0 and m > 64 and n > 64 and m * n * k >= 1 << 27
 
 
 def default_tcgen05_config(

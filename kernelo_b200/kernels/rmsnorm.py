@@ -20,7 +20,7 @@ import torch
 
 from kernelo_b200.benchmark import metrics
 from kernelo_b200.kernels.base import Operator, seeded_generator
-from kernelo_b200.kernels.rows_common import check_block, check_row_input, default_rows_config
+from kernelo_b200.kernels.rows_common import MAX_BLOCK_SIZE, check_block, check_row_input, default_rows_config
 from kernelo_b200.runtime import native
 from kernelo_b200.tuning.config import KernelConfig, Problem
 from kernelo_b200.tuning.search import RMSNormSearchSpace
@@ -51,9 +51,12 @@ def rmsnorm(
         raise ValueError(f"dtype mismatch: {x.dtype} vs {gamma.dtype}")
     if gamma.device != x.device:
         raise ValueError("x and gamma must be on one device")
-    cfg = config or default_rows_config("rmsnorm", n_cols, x.dtype, rows=n_rows, x=x,
-                                        sm_count=native.sm_count(x.device.index))
-    check_block(cfg, n_cols, "hidden size")
+    if config is None and n_cols <= MAX_BLOCK_SIZE:
+        cfg = None  # the library resolves its default itself (default_rows_config mirrors it)
+    else:
+        cfg = config or default_rows_config("rmsnorm", n_cols, x.dtype, rows=n_rows, x=x,
+                                            sm_count=native.sm_count(x.device.index))
+        check_block(cfg, n_cols, "hidden size")
     out = torch.empty((n_rows, n_cols), device=x.device, dtype=x.dtype)
     if n_rows and n_cols:
         native.rmsnorm_rows(x, gamma, out, eps, cfg)

@@ -23,7 +23,7 @@ import torch
 
 from kernelo_b200.benchmark import metrics
 from kernelo_b200.kernels.base import Operator, seeded_generator
-from kernelo_b200.kernels.rows_common import check_block, check_row_input, default_rows_config
+from kernelo_b200.kernels.rows_common import MAX_BLOCK_SIZE, check_block, check_row_input, default_rows_config
 from kernelo_b200.runtime import native
 from kernelo_b200.tuning.config import KernelConfig, Problem
 from kernelo_b200.tuning.search import SoftmaxSearchSpace
@@ -37,9 +37,12 @@ def default_config(n_cols: int, dtype: torch.dtype = torch.float16, n_rows: int 
 def softmax(x: torch.Tensor, *, config: KernelConfig | None = None) -> torch.Tensor:
     check_row_input(x)
     n_rows, n_cols = x.shape
-    cfg = config or default_rows_config("softmax", n_cols, x.dtype, rows=n_rows, x=x,
-                                        sm_count=native.sm_count(x.device.index))
-    check_block(cfg, n_cols, "row width")
+    if config is None and n_cols <= MAX_BLOCK_SIZE:
+        cfg = None  # the library resolves its default itself (default_rows_config mirrors it)
+    else:
+        cfg = config or default_rows_config("softmax", n_cols, x.dtype, rows=n_rows, x=x,
+                                            sm_count=native.sm_count(x.device.index))
+        check_block(cfg, n_cols, "row width")
     out = torch.empty((n_rows, n_cols), device=x.device, dtype=x.dtype)
     if n_rows and n_cols:
         native.softmax_rows(x, out, cfg)

@@ -20,6 +20,7 @@ is missing or its recorded source hash no longer matches.
 from __future__ import annotations
 
 import ctypes
+import functools
 import os
 import threading
 from dataclasses import dataclass
@@ -233,7 +234,14 @@ def check(status: int, what: str) -> None:
     raise KernelLaunchError(message, status)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def current_stream_handle(device: torch.device) -> int:
+    """The current CUDA stream of ``device`` as a raw handle (the cheap accessor
+    torch's own extensions use, when this torch build has it)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -262,7 +270,7 @@ class GemmLaunch:
     @classmethod
     def from_config(cls, config) -> GemmLaunch:
         if config is None:
-            return cls()
+            return _DEFAULT_LAUNCH
         get = config.get
         return cls(
             kernel=get("KERNEL", 0),
@@ -280,6 +288,11 @@ class GemmLaunch:
         )
 
     def struct(self) -> KfGemmConfig:
+        """The C struct (built once per distinct launch and shared: the library
+        only reads it)."""
+        return _gemm_struct(self)
+
+    def _build(self) -> KfGemmConfig:
         s = KfGemmConfig()
         for name in (
             "kernel",
@@ -299,7 +312,23 @@ class GemmLaunch:
         return s
 
 
+_DEFAULT_LAUNCH = GemmLaunch()
+
+
+@functools.lru_cache(maxsize=1024)
+def _gemm_struct(launch: GemmLaunch) -> KfGemmConfig:
+    return launch._build()
+
+
+_AUTO_ROWS = None
+
+
 def rows_struct(config) -> KfRowsConfig:
+    global _AUTO_ROWS
+    if config is None:
+        if _AUTO_ROWS is None:
+            _AUTO_ROWS = KfRowsConfig()  # all zero: the library's own choice (only read)
+        return _AUTO_ROWS
     s = KfRowsConfig()
     if config is not None:
         s.num_warps = config.get("num_warps", 0)
@@ -355,6 +384,7 @@ class _WorkspacePool:
 
 
 workspaces = _WorkspacePool()
+_workspace_sizes: dict[tuple, int] = {}
 
 
 # ----------------------------------------------------------------------- calls
@@ -369,24 +399,33 @@ def gemm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, *, bias: torch.Tenso
     code = native_code(a.dtype)
     m, k = a.shape
     n = b.shape[1]
-    ws_bytes = lib.kf_gemm_workspace_bytes_for(dev.index or 0, code, a.data_ptr(), a.stride(0), a.stride(1),
-                                               b.data_ptr(), b.stride(0), b.stride(1), c.data_ptr(), c.stride(0),
-                                               c.stride(1), m, n, k, ctypes.byref(cfg))
-    if ws_bytes < 0:
-        check(int(-ws_bytes), "kf_gemm_workspace_bytes_for")
+    a_ptr, b_ptr, c_ptr = a.data_ptr(), b.data_ptr(), c.data_ptr()
+    sa, sb, sc = a.stride(), b.stride(), c.stride()
+    # The plan depends on sizes, strides, the pointers' 16-byte phase and the
+    # config only: sized once per distinct call shape.
+    key = (dev.index, code, m, n, k, sa, sb, sc, a_ptr & 15, b_ptr & 15, c_ptr & 15, launch)
+    ws_bytes = _workspace_sizes.get(key)
+    if ws_bytes is None:
+        ws_bytes = lib.kf_gemm_workspace_bytes_for(dev.index or 0, code, a_ptr, sa[0], sa[1], b_ptr, sb[0], sb[1],
+                                                   c_ptr, sc[0], sc[1], m, n, k, ctypes.byref(cfg))
+        if ws_bytes < 0:
+            check(int(-ws_bytes), "kf_gemm_workspace_bytes_for")
+        if len(_workspace_sizes) > 4096:
+            _workspace_sizes.clear()
+        _workspace_sizes[key] = ws_bytes
     ws = workspaces.get(dev, stream, ws_bytes)
     ws_ptr = _ptr(ws)
     if epilogue == KF_EPI_NONE:
-        status = lib.kf_gemm(code, a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0),
-                             b.stride(1), c.data_ptr(), c.stride(0), c.stride(1), m, n, k,
+        status = lib.kf_gemm(code, a_ptr, sa[0], sa[1], b_ptr, sb[0], sb[1], c_ptr, sc[0], sc[1], m, n, k,
                              ctypes.byref(cfg), ws_ptr, max(ws_bytes, 0), stream)
-        check(status, "kf_gemm")
+        if status:
+            check(status, "kf_gemm")
     else:
-        status = lib.kf_linear_bias_act(code, a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(),
-                                        b.stride(0), b.stride(1), _ptr(bias), c.data_ptr(),
-                                        c.stride(0), c.stride(1), m, n, k, epilogue,
-                                        ctypes.byref(cfg), ws_ptr, max(ws_bytes, 0), stream)
-        check(status, "kf_linear_bias_act")
+        status = lib.kf_linear_bias_act(code, a_ptr, sa[0], sa[1], b_ptr, sb[0], sb[1], _ptr(bias), c_ptr,
+                                        sc[0], sc[1], m, n, k, epilogue, ctypes.byref(cfg), ws_ptr,
+                                        max(ws_bytes, 0), stream)
+        if status:
+            check(status, "kf_linear_bias_act")
 
 
 def linear_bias_act_allgather(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, peers: list[int], *,
@@ -469,7 +508,8 @@ def gemv(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, *, w_layout: str = "
          launch: GemmLaunch | None = None) -> None:
     """Decode-shape ``y[M,N] = x[M,K] . W^T`` with W stored [N,K] (``"nk"``) or [K,N] (``"kn"``)."""
     lib = load()
-    cfg = (launch or GemmLaunch()).struct()
+    launch = launch or _DEFAULT_LAUNCH
+    cfg = launch.struct()
     dev = y.device
     stream = current_stream_handle(dev)
     code = native_code(x.dtype)
@@ -482,15 +522,23 @@ def gemv(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, *, w_layout: str = "
         sw_k, sw_n = w.stride(0), w.stride(1)
     else:
         raise ValueError(f"w_layout must be 'nk' or 'kn', got {w_layout!r}")
-    ws_bytes = lib.kf_gemv_workspace_bytes(dev.index or 0, code, x.stride(0), x.stride(1), sw_n,
-                                           sw_k, m, n, k, ctypes.byref(cfg))
-    if ws_bytes < 0:
-        check(int(-ws_bytes), "kf_gemv_workspace_bytes")
+    sx = x.stride()
+    key = ("gemv", dev.index, code, m, n, k, sx, sw_n, sw_k, launch)
+    ws_bytes = _workspace_sizes.get(key)
+    if ws_bytes is None:
+        ws_bytes = lib.kf_gemv_workspace_bytes(dev.index or 0, code, sx[0], sx[1], sw_n, sw_k, m, n, k,
+                                               ctypes.byref(cfg))
+        if ws_bytes < 0:
+            check(int(-ws_bytes), "kf_gemv_workspace_bytes")
+        if len(_workspace_sizes) > 4096:
+            _workspace_sizes.clear()
+        _workspace_sizes[key] = ws_bytes
     ws = workspaces.get(dev, stream, ws_bytes)
-    status = lib.kf_gemv(code, x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), sw_n, sw_k,
+    status = lib.kf_gemv(code, x.data_ptr(), sx[0], sx[1], w.data_ptr(), sw_n, sw_k,
                          y.data_ptr(), y.stride(0), y.stride(1), m, n, k, ctypes.byref(cfg),
                          _ptr(ws), max(ws_bytes, 0), stream)
-    check(status, "kf_gemv")
+    if status:
+        check(status, "kf_gemv")
 
 
 def softmax_rows(x: torch.Tensor, y: torch.Tensor, config=None) -> None:
@@ -500,7 +548,8 @@ def softmax_rows(x: torch.Tensor, y: torch.Tensor, config=None) -> None:
     status = lib.kf_softmax_rows(native_code(x.dtype), x.data_ptr(), x.stride(0), y.data_ptr(),
                                  y.stride(0), rows, cols, ctypes.byref(cfg),
                                  current_stream_handle(y.device))
-    check(status, "kf_softmax_rows")
+    if status:
+        check(status, "kf_softmax_rows")
 
 
 def rmsnorm_rows(x: torch.Tensor, gamma: torch.Tensor, y: torch.Tensor, eps: float,
@@ -511,7 +560,8 @@ def rmsnorm_rows(x: torch.Tensor, gamma: torch.Tensor, y: torch.Tensor, eps: flo
     status = lib.kf_rmsnorm_rows(native_code(x.dtype), x.data_ptr(), x.stride(0), gamma.data_ptr(),
                                  y.data_ptr(), y.stride(0), rows, cols, float(eps),
                                  ctypes.byref(cfg), current_stream_handle(y.device))
-    check(status, "kf_rmsnorm_rows")
+    if status:
+        check(status, "kf_rmsnorm_rows")
 
 
 def device_status(device: int | None = None) -> int:

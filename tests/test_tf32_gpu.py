@@ -50,7 +50,7 @@ def ran_on_tensor_cores(a, b, out) -> bool:
     return planned and not torch.equal(simt, out)
 
 
-@pytest.mark.parametrize("shape", [(512, 1024, 256), (257, 257, 257), (1021, 2053, 509), (2048, 4096, 4096)],
+@pytest.mark.parametrize("shape", [(512, 1024, 256), (640, 520, 1000), (1021, 2053, 509), (2048, 4096, 4096)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_default_fp32_runs_3xtf32_at_the_fp32_gate(shape, device):
     m, k, n = shape[0], shape[2], shape[1]
@@ -120,3 +120,13 @@ def test_tf32_accuracy_holds_over_long_k(device):
     a, b = operands(256, 16384, 256, device, seed=5)
     result = gate(ref.matmul_ref(host(a), host(b)), matmul(a, b), torch.float32)
     assert result.error < 2e-6
+
+
+def test_small_fp32_keeps_ieee_fma(device):
+    """Below 2^27 multiply-adds fp32 stays on the CUDA-core kernel: no split
+    planned, and the result is that kernel's bit for bit."""
+    a, b = operands(257, 257, 257, device)
+    out = matmul(a, b)
+    assert split_workspace_bytes(a, b, out) < 12 * (a.numel() + b.numel())
+    simt = matmul(a, b, config=KernelConfig("matmul", KERNEL=2, BLOCK_M=64, BLOCK_N=64, BLOCK_K=16))
+    assert torch.equal(simt, out)
