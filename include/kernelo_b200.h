@@ -162,9 +162,9 @@ KF_API int32_t kf_device_status(int32_t device, int32_t* out);
 /* ---- GEMM: C[M,N] = A[M,K] . B[K,N] --------------------------------------- *
  * Strides are in elements: A(m,k) = a[m*sa_m + k*sa_k], B(k,n) = b[k*sb_k + n*sb_n],
  * C(m,n) = c[m*sc_m + n*sc_n]. Accumulation is fp32; C has the operand dtype.
- * fp32 beyond 64 x 64 (or with KF_GEMM_TCGEN05) runs on tensor cores as
- * 3xTF32: A and B are split into TF32 parts in the workspace and one
- * kind::tf32 GEMM sums a_small b_big + a_big b_small + a_big b_big, which
+ * fp32 beyond 64 x 64 and 2^27 multiply-adds (or with KF_GEMM_TCGEN05) runs as
+ * 3xTF32 on tensor cores: A and B are split into TF32 parts in the workspace
+ * and a kind::tf32 GEMM sums a_small b_big + a_big b_small + a_big b_big, which
  * holds the fp32 gate (1e-5); smaller fp32 problems, and calls given too
  * little workspace, run IEEE FMA on CUDA cores.
  * `workspace` holds stream-K state and any operand copies;
@@ -228,7 +228,7 @@ KF_API int32_t kf_gemv_noalloc(int32_t dtype, const void* x, int64_t sx_m, int64
  * contiguous. The workspace holds the stream-K counters and partial tiles,
  * the column GEMV's partial sums, the packed copies of fp16/bf16 operands
  * that a TMA tensor map cannot describe (an odd row pitch or K < 8), the
- * TF32-split copies of fp32 operands (3 x 4 bytes per element, K rounded up
+ * TF32-split copies of fp32 operands (2 x 4 bytes per element, K rounded up
  * to 32) and the staged copy of an output whose rows are off the 16-byte
  * grid, these copies after the first 64 KiB. */
 KF_API int64_t kf_gemm_workspace_bytes(int32_t device, int32_t dtype, int64_t sa_m, int64_t sa_k,

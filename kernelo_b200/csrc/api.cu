@@ -147,9 +147,12 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
   // An atom is 64 16-bit or 32 fp32 (TF32) elements.
   const int elem = g.dtype == KF_FP32 ? 4 : 2;
   const int atom = 128 / elem;
-  if (c.block_k == 0) c.block_k = (cg == 2 && g.K >= 512) ? 2 * atom : atom;
+  // bytes per (row, k) in a ring stage and in an A panel: TF32 stages carry
+  // both split parts of each element
+  const int stage_elem = g.dtype == KF_FP32 ? 2 * elem : elem;
+  if (c.block_k == 0) c.block_k = (cg == 2 && g.K >= 512 && g.dtype != KF_FP32) ? 2 * atom : atom;
   if (c.stages == 0) {
-    const int64_t per_stage = static_cast<int64_t>(128 + c.block_n / cg) * c.block_k * elem;
+    const int64_t per_stage = static_cast<int64_t>(128 + c.block_n / cg) * c.block_k * stage_elem;
     // (the all-gather epilogue's output stage comes out of the same 227 KiB)
     int64_t s = (232448 - 1024 - 256 - (g.n_peers > 0 ? GEMM_PEER_STAGE_SMEM : 0)) / per_stage;
     if (s > 12) s = 12;
@@ -162,7 +165,7 @@ kf_gemm_config resolve_gemm_config(const GemmArgs& g, const kf_gemm_config* user
     // stays resident across waves (measured on B200 at 4096x11008x4096: 16
     // groups-of-one-column read B once, 8 read it twice and ran 3 % slower).
     const int64_t tile_rows = 128LL * cg;
-    const int64_t panel = tile_rows * g.K * elem;
+    const int64_t panel = tile_rows * g.K * stage_elem;
     int64_t gm = panel > 0 ? (48LL << 20) / panel : 8;
     const int64_t tiles_m = (m + tile_rows - 1) / tile_rows;
     if (gm > tiles_m) gm = tiles_m;
@@ -276,17 +279,18 @@ bool plan_tc(const GemmArgs& g, const kf_gemm_config* user, const DeviceInfo& de
   p.view = g;
   const void* stand_in = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
   if (tf32_applies(g, user)) {
-    // A'[M, 3Kp] and B'[N, 3Kp], both K-major: the kernel's K is 3 Kp.
+    // A'[M, 2Kp] and B'[N, 2Kp] ([small | big] rows), both K-major: the
+    // kernel's K is Kp and each k-block loads both segments.
     p.split = true;
-    p.sa = plan_tf32_split(g.a, g.sa_m, g.sa_k, g.M, g.K, false);
-    p.sb = plan_tf32_split(g.b, g.sb_n, g.sb_k, g.N, g.K, true);
+    p.sa = plan_tf32_split(g.a, g.sa_m, g.sa_k, g.M, g.K);
+    p.sb = plan_tf32_split(g.b, g.sb_n, g.sb_k, g.N, g.K);
     p.view.a = stand_in;
     p.view.sa_m = p.sa.pitch;
     p.view.sa_k = 1;
     p.view.b = stand_in;
     p.view.sb_n = p.sb.pitch;
     p.view.sb_k = 1;
-    p.view.K = 3 * p.sa.kp;
+    p.view.K = p.sa.kp;
     p.view.tf32_split = true;
   } else if (packing_applies(g, user)) {
     // K below one 16-byte vector is padded with zeros to 8: then both operands

@@ -70,7 +70,7 @@ constexpr int MAX_STAGES = 16;
 // (half of BLOCK_N <= 128), and the K elements one TMEM chunk accumulates.
 constexpr int TF32_MAX_COLS = 64;
 #ifndef KF_TF32_PROMOTE_K
-#define KF_TF32_PROMOTE_K 256
+#define KF_TF32_PROMOTE_K 128
 #endif
 constexpr int TF32_PROMOTE_K = KF_TF32_PROMOTE_K;
 constexpr int MIN_SMEM_PER_CTA = 120 * 1024;  // > half an SM: one CTA per SM
@@ -98,6 +98,7 @@ struct TcParams {
   // thousands of k loses bits (3xTF32 at K = 4096 measured 1.0e-5 relative
   // error in one chunk, 5.7e-7 in chunks of 192).
   int promote_kb;
+  int tf32_kp;  // TF32: elements between a split operand's small and big segments
   uint32_t idesc_half;
   void* c;
   long long sc_r, sc_c;
@@ -484,8 +485,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int seg_bn = half ? p.bn / 2 : p.bn;
         const int b_rows = seg_bn / CG;  // B rows this CTA stages
         const CUtensorMap* map_b = half ? &tm_b_half : &tm_b;
+        // TF32: a stage holds both parts of the k-block, small then big
+        // (segments 0 and 1 of the split operands, kp elements apart).
+        constexpr int PARTS = TF32 ? 2 : 1;
         const uint32_t tx_bytes =
-            (p.a_stage_bytes + static_cast<uint32_t>(b_rows * p.bk * static_cast<int>(sizeof(T)))) * CG;
+            (p.a_stage_bytes + static_cast<uint32_t>(PARTS * b_rows * p.bk * static_cast<int>(sizeof(T)))) * CG;
         const int m0 = m_blk * (BM * CG) + BM * static_cast<int>(crank);
         const int n0 = n_blk * p.bn + (half ? seg.half * seg_bn : 0) + b_rows * static_cast<int>(crank);
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
@@ -499,36 +503,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t b_dst = smem_u32(b_ring + static_cast<size_t>(stage) * p.b_stage_bytes);
           if constexpr (CG == 2) {
             if (leader) mbar_arrive_expect_tx(fb, tx_bytes);
-            const uint32_t lb = mapa_shared(fb, 0);  // both CTAs count on the leader's barrier
-            if (!p.a_mn) {
-              for (int j = 0; j < p.bk / ATOM; ++j)
-                tma_load_2d_pair(a_dst + j * (BM * 128), &tm_a, lb, k0 + ATOM * j, m0);
-            } else {
-              for (int i = 0; i < BM / ATOM; ++i)
-                tma_load_2d_pair(a_dst + i * (p.bk * 128), &tm_a, lb, m0 + ATOM * i, k0);
-            }
-            if (!p.b_mn) {
-              for (int j = 0; j < p.bk / ATOM; ++j)
-                tma_load_2d_pair(b_dst + j * (b_rows * 128), map_b, lb, k0 + ATOM * j, n0);
-            } else {
-              for (int i = 0; i < b_rows / ATOM; ++i)
-                tma_load_2d_pair(b_dst + i * (p.bk * 128), map_b, lb, n0 + ATOM * i, k0);
-            }
           } else {
             mbar_arrive_expect_tx(fb, tx_bytes);
-            if (!p.a_mn) {
-              for (int j = 0; j < p.bk / ATOM; ++j)
-                tma_load_2d(a_dst + j * (BM * 128), &tm_a, fb, k0 + ATOM * j, m0);
+          }
+          // both CTAs of a pair count on the leader's barrier
+          const uint32_t lb = CG == 2 ? mapa_shared(fb, 0) : fb;
+#pragma unroll
+          for (int part = 0; part < PARTS; ++part) {
+            const uint32_t a_p = a_dst + part * (p.a_stage_bytes / PARTS);
+            const uint32_t b_p = b_dst + part * (p.b_stage_bytes / PARTS);
+            const int kx = k0 + part * p.tf32_kp;
+            if constexpr (CG == 2) {
+              if (!p.a_mn) {
+                for (int j = 0; j < p.bk / ATOM; ++j)
+                  tma_load_2d_pair(a_p + j * (BM * 128), &tm_a, lb, kx + ATOM * j, m0);
+              } else {
+                for (int i = 0; i < BM / ATOM; ++i)
+                  tma_load_2d_pair(a_p + i * (p.bk * 128), &tm_a, lb, m0 + ATOM * i, kx);
+              }
+              if (!p.b_mn) {
+                for (int j = 0; j < p.bk / ATOM; ++j)
+                  tma_load_2d_pair(b_p + j * (b_rows * 128), map_b, lb, kx + ATOM * j, n0);
+              } else {
+                for (int i = 0; i < b_rows / ATOM; ++i)
+                  tma_load_2d_pair(b_p + i * (p.bk * 128), map_b, lb, n0 + ATOM * i, kx);
+              }
             } else {
-              for (int i = 0; i < BM / ATOM; ++i)
-                tma_load_2d(a_dst + i * (p.bk * 128), &tm_a, fb, m0 + ATOM * i, k0);
-            }
-            if (!p.b_mn) {
-              for (int j = 0; j < p.bk / ATOM; ++j)
-                tma_load_2d(b_dst + j * (b_rows * 128), map_b, fb, k0 + ATOM * j, n0);
-            } else {
-              for (int i = 0; i < b_rows / ATOM; ++i)
-                tma_load_2d(b_dst + i * (p.bk * 128), map_b, fb, n0 + ATOM * i, k0);
+              if (!p.a_mn) {
+                for (int j = 0; j < p.bk / ATOM; ++j)
+                  tma_load_2d(a_p + j * (BM * 128), &tm_a, lb, kx + ATOM * j, m0);
+              } else {
+                for (int i = 0; i < BM / ATOM; ++i)
+                  tma_load_2d(a_p + i * (p.bk * 128), &tm_a, lb, m0 + ATOM * i, kx);
+              }
+              if (!p.b_mn) {
+                for (int j = 0; j < p.bk / ATOM; ++j)
+                  tma_load_2d(b_p + j * (b_rows * 128), map_b, lb, kx + ATOM * j, n0);
+              } else {
+                for (int i = 0; i < b_rows / ATOM; ++i)
+                  tma_load_2d(b_p + i * (p.bk * 128), map_b, lb, n0 + ATOM * i, kx);
+              }
             }
           }
           ++issued;
@@ -600,18 +614,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(atom * a_atom_step + kk * a_k_step);
                 const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(atom * b_atom_step + kk * b_k_step);
                 const uint32_t accumulate = (kb > c0 || atom > 0 || kk > 0) ? 1u : 0u;
-                if constexpr (CG == 2) {
-                  if constexpr (TF32) {
-                    tc_mma_tf32_pair(d_tmem, a_desc, b_desc, idesc, accumulate);
+                if constexpr (TF32) {
+                  // 3xTF32 on the stage's two parts: small x big, big x small,
+                  // then big x big (the big halves sit half a stage on)
+                  const uint64_t a_big = a_desc + (p.a_stage_bytes / 2) / 16;
+                  const uint64_t b_big = b_desc + (p.b_stage_bytes / 2) / 16;
+                  if constexpr (CG == 2) {
+                    tc_mma_tf32_pair(d_tmem, a_desc, b_big, idesc, accumulate);
+                    tc_mma_tf32_pair(d_tmem, a_big, b_desc, idesc, 1u);
+                    tc_mma_tf32_pair(d_tmem, a_big, b_big, idesc, 1u);
                   } else {
-                    tc_mma_f16_pair(d_tmem, a_desc, b_desc, idesc, accumulate);
+                    tc_mma_tf32(d_tmem, a_desc, b_big, idesc, accumulate);
+                    tc_mma_tf32(d_tmem, a_big, b_desc, idesc, 1u);
+                    tc_mma_tf32(d_tmem, a_big, b_big, idesc, 1u);
                   }
+                } else if constexpr (CG == 2) {
+                  tc_mma_f16_pair(d_tmem, a_desc, b_desc, idesc, accumulate);
                 } else {
-                  if constexpr (TF32) {
-                    tc_mma_tf32(d_tmem, a_desc, b_desc, idesc, accumulate);
-                  } else {
-                    tc_mma_f16(d_tmem, a_desc, b_desc, idesc, accumulate);
-                  }
+                  tc_mma_f16(d_tmem, a_desc, b_desc, idesc, accumulate);
                 }
               }
             }
@@ -998,6 +1018,8 @@ uint32_t tmem_cols_for(int bn) {
 }
 
 int elem_bytes(int dtype) { return dtype == KF_FP32 ? 4 : 2; }
+// Bytes a ring stage holds per (row, k): TF32 stages carry both split parts.
+int stage_elem_bytes(int dtype) { return dtype == KF_FP32 ? 8 : 2; }
 
 // Shared memory of one CTA: A rows (128) and this CTA's B rows per stage.
 int64_t smem_bytes_for(int bn, int bk, int stages, int cg, int elem, bool peer_stage = false) {
@@ -1211,7 +1233,7 @@ int query_tcgen05_config(int dtype, const kf_gemm_config& cfg, int64_t* smem_byt
   int rc = validate_config(cfg, 0, dtype, &why);
   if (rc != KF_OK) return set_error(rc, why);
   const int64_t smem =
-      smem_bytes_for(cfg.block_n, cfg.block_k, cfg.stages, cta_group_of(cfg), elem_bytes(dtype));
+      smem_bytes_for(cfg.block_n, cfg.block_k, cfg.stages, cta_group_of(cfg), stage_elem_bytes(dtype));
   if (smem_bytes) *smem_bytes = smem;
   if (tmem_cols) *tmem_cols = static_cast<int32_t>(tmem_cols_for(cfg.block_n));
   if (smem > 232448)
@@ -1287,7 +1309,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
                     (reinterpret_cast<uintptr_t>(g.c) & 15u) == 0;
   for (int i = 0; i < g.n_peers; ++i)
     peer_stage = peer_stage && (reinterpret_cast<uintptr_t>(g.peers[i]) & 15u) == 0;
-  const int64_t smem = smem_bytes_for(bn, bk, S, cg, elem, peer_stage);
+  const int64_t smem = smem_bytes_for(bn, bk, S, cg, stage_elem_bytes(g.dtype), peer_stage);
   if (smem > dev.max_smem_optin)
     return set_error(KF_ERR_INVALID_CONFIG, "shared memory " + std::to_string(smem) +
                                                 " B exceeds the device limit of " +
@@ -1295,10 +1317,12 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
   const int64_t smem_request = smem < MIN_SMEM_PER_CTA ? MIN_SMEM_PER_CTA : smem;
 
   CUtensorMap tm_a, tm_b, tm_b_half;
-  rc = a_major == 0 ? encode_map(&tm_a, g.dtype, v.a, g.K, v.M, v.sa_r, atom, BM)
+  // TF32 split operands: rows of two K-segments (small, big), both mapped
+  const uint64_t k_extent = g.tf32_split ? 2 * static_cast<uint64_t>(g.K) : static_cast<uint64_t>(g.K);
+  rc = a_major == 0 ? encode_map(&tm_a, g.dtype, v.a, k_extent, v.M, v.sa_r, atom, BM)
                     : encode_map(&tm_a, g.dtype, v.a, v.M, g.K, v.sa_k, atom, bk);
   if (rc != KF_OK) return rc;
-  rc = b_major == 0 ? encode_map(&tm_b, g.dtype, v.b, g.K, v.N, v.sb_c, atom, b_rows)
+  rc = b_major == 0 ? encode_map(&tm_b, g.dtype, v.b, k_extent, v.N, v.sb_c, atom, b_rows)
                     : encode_map(&tm_b, g.dtype, v.b, v.N, g.K, v.sb_k, atom, bk);
   if (rc != KF_OK) return rc;
   // Half-width tail tiles: an N/2 MMA needs N/2 a multiple of 16 per CTA pair
@@ -1307,7 +1331,7 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
                         (b_major == 0 || (b_rows / 2) % 64 == 0);
   tm_b_half = tm_b;
   if (split_ok && b_major == 0) {
-    rc = encode_map(&tm_b_half, g.dtype, v.b, g.K, v.N, v.sb_c, atom, b_rows / 2);
+    rc = encode_map(&tm_b_half, g.dtype, v.b, k_extent, v.N, v.sb_c, atom, b_rows / 2);
     if (rc != KF_OK) return rc;
   }
 
@@ -1353,9 +1377,11 @@ int launch_gemm_tcgen05(const GemmArgs& g, const kf_gemm_config& cfg, const Devi
                            static_cast<uint32_t>(bn));
   p.idesc_half = instr_desc_f16(fmt, static_cast<uint32_t>(a_major), static_cast<uint32_t>(b_major),
                                 BM * cg, static_cast<uint32_t>(bn / 2));
-  p.promote_kb = g.dtype == KF_FP32 ? TF32_PROMOTE_K / bk : 0;
-  p.a_stage_bytes = static_cast<uint32_t>(BM * bk * elem);
-  p.b_stage_bytes = static_cast<uint32_t>(b_rows * bk * elem);
+  p.promote_kb = g.dtype == KF_FP32 ? (TF32_PROMOTE_K + bk - 1) / bk : 0;
+  p.tf32_kp = g.dtype == KF_FP32 ? static_cast<int>(g.K) : 0;
+  const int parts = g.dtype == KF_FP32 ? 2 : 1;
+  p.a_stage_bytes = static_cast<uint32_t>(BM * bk * elem * parts);
+  p.b_stage_bytes = static_cast<uint32_t>(b_rows * bk * elem * parts);
   p.tmem_cols = tmem_cols_for(bn);
 
   void* fn = pick_kernel(g.dtype, g.epilogue, cg, g.n_peers > 0);

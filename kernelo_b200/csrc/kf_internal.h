@@ -44,8 +44,9 @@ struct GemmArgs {
   // into each of them as well (the all-gather of a column-sharded linear).
   void* peers[KF_MAX_PEERS] = {};
   int n_peers = 0;
-  // fp32 only: a and b are TF32-split operands (tf32_split.cu), K-major, K
-  // the extended length; the tcgen05 kernel runs them as kind::tf32.
+  // fp32 only: a and b are TF32-split operands (tf32_split.cu), K-major rows
+  // of [small | big] with K (= kp) elements each; the tcgen05 kernel runs
+  // them as kind::tf32, three MMAs per k-block.
   bool tf32_split = false;
 };
 
@@ -94,18 +95,16 @@ int launch_pack(const PackedOperand& p, void* dst, cudaStream_t stream);
 PackedOperand plan_output_stage(void* c, int64_t sc_m, int64_t sc_n, int64_t m, int64_t n);
 int launch_unpack(const PackedOperand& p, const void* staged, cudaStream_t stream);
 
-// fp32 operands split for 3xTF32 (tf32_split.cu): rows of [small|big|big]
-// (A, b_order false) or [big|small|big] (B, b_order true) TF32 parts, K
-// padded with zeros to kp (a multiple of 32), written K-major with `pitch`
-// = 3 kp elements. (s_r, s_k): the source's element strides of (row, k).
+// fp32 operands split for 3xTF32 (tf32_split.cu): rows of [small|big] TF32
+// parts, K padded with zeros to kp (a multiple of 32), written K-major with
+// `pitch` = 2 kp elements. (s_r, s_k): the source's element strides of (row, k).
 struct SplitOperand {
   const void* src = nullptr;
   int64_t s_r = 0, s_k = 0;
   int64_t rows = 0, K = 0, kp = 0, pitch = 0;
   int64_t bytes = 0;  // 256-byte rounded
-  bool b_order = false;
 };
-SplitOperand plan_tf32_split(const void* src, int64_t s_r, int64_t s_k, int64_t rows, int64_t K, bool b_order);
+SplitOperand plan_tf32_split(const void* src, int64_t s_r, int64_t s_k, int64_t rows, int64_t K);
 int launch_tf32_split(const SplitOperand& s, void* dst, cudaStream_t stream);
 
 // CUDA-core path: any strides, fp16/bf16/fp32.

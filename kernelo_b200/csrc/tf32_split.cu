@@ -14,18 +14,17 @@
 // threshold for fp32 is 1e-5 (kernelforge/testing.py:31-35), which plain
 // TF32 misses by about 100x.
 //
-// The three products become one GEMM over an extended K: each operand is
-// copied into the workspace as rows of three K-segments,
+// Each operand is copied once into the workspace as rows of two K-segments,
 //
-//   A' [M, 3 Kp] = [ A_small | A_big   | A_big ]
-//   B' [N, 3 Kp] = [ B_big   | B_small | B_big ]
+//   A' [M, 2 Kp] = [ A_small | A_big ]      B' [N, 2 Kp] = [ B_small | B_big ]
 //
-// so A' . B'^T is the sum above (small products first, so they accumulate
-// before the large ones). Kp is K rounded up to a 128-byte TMA atom (32
-// elements) with zeros; rows are K-major whatever the source layout (a
-// row-major (K, N) B is transposed on the way through shared memory), which
-// is the layout kind::tf32 reads. Rounding is cvt.rna.tf32.f32 (to nearest,
-// ties away from zero).
+// K-major whatever the source layout (a row-major (K, N) B is transposed on
+// the way through shared memory), which is the layout kind::tf32 reads; Kp is
+// K rounded up to a 128-byte TMA atom (32 elements) with zeros. The tcgen05
+// kernel loads both segments of a k-block into one ring stage and issues the
+// three products' MMAs on them (small x big, big x small, big x big), so each
+// byte crosses L2 and shared memory once per k-block. Rounding is
+// cvt.rna.tf32.f32 (to nearest, ties away from zero).
 #include "kf_common.cuh"
 #include "kf_internal.h"
 
@@ -45,7 +44,7 @@ __device__ __forceinline__ float to_tf32(float x) {
 __global__ void __launch_bounds__(256) tf32_split_kernel(const float* __restrict__ src, long long s_r,
                                                          long long s_k, long long rows, long long K,
                                                          float* __restrict__ dst, long long pitch,
-                                                         long long kp, int b_order) {
+                                                         long long kp) {
   __shared__ float tile[SPLIT_TILE][SPLIT_TILE + 1];
   const int tx = threadIdx.x, ty = threadIdx.y;
   const long long k0 = static_cast<long long>(blockIdx.x) * SPLIT_TILE;
@@ -72,16 +71,14 @@ __global__ void __launch_bounds__(256) tf32_split_kernel(const float* __restrict
     const float big = to_tf32(x);
     const float small = to_tf32(x - big);
     float* row = dst + r * pitch + k0 + tx;
-    // A: [small | big | big]; B: [big | small | big]
-    row[0] = b_order ? big : small;
-    row[kp] = b_order ? small : big;
-    row[2 * kp] = big;
+    row[0] = small;
+    row[kp] = big;
   }
 }
 
 }  // namespace
 
-SplitOperand plan_tf32_split(const void* src, int64_t s_r, int64_t s_k, int64_t rows, int64_t K, bool b_order) {
+SplitOperand plan_tf32_split(const void* src, int64_t s_r, int64_t s_k, int64_t rows, int64_t K) {
   SplitOperand s;
   s.src = src;
   s.s_r = s_r;
@@ -89,9 +86,8 @@ SplitOperand plan_tf32_split(const void* src, int64_t s_r, int64_t s_k, int64_t 
   s.rows = rows;
   s.K = K;
   s.kp = (K + SPLIT_TILE - 1) / SPLIT_TILE * SPLIT_TILE;
-  s.pitch = 3 * s.kp;
+  s.pitch = 2 * s.kp;
   s.bytes = (rows * s.pitch * 4 + 255) / 256 * 256;
-  s.b_order = b_order;
   return s;
 }
 
@@ -104,7 +100,7 @@ int launch_tf32_split(const SplitOperand& s, void* dst, cudaStream_t stream) {
   if (rtiles > 65535) return set_error(KF_ERR_UNSUPPORTED, "TF32 split: more than 2^21 rows");
   tf32_split_kernel<<<dim3(static_cast<unsigned>(ktiles), static_cast<unsigned>(rtiles)), dim3(32, 8), 0,
                       stream>>>(static_cast<const float*>(s.src), s.s_r, s.s_k, s.rows, s.K,
-                                static_cast<float*>(dst), s.pitch, s.kp, s.b_order ? 1 : 0);
+                                static_cast<float*>(dst), s.pitch, s.kp);
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_error(err, "launch(tf32 split)");
   return KF_OK;

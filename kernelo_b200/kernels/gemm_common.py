@@ -116,7 +116,9 @@ def tc_smem_bytes(block_n: int, block_k: int, stages: int, itemsize: int = 2, ct
     Each CTA stages 128 rows of A and its share of B: all BLOCK_N rows for a
     one-SM tile, half of them for a 256-row SM-pair tile.
     """
-    ring = stages * (TC_BLOCK_M + block_n // cta_group) * block_k * itemsize
+    # fp32 (TF32-split) stages hold both parts of every element
+    stage_bytes = 2 * itemsize if itemsize == 4 else itemsize
+    ring = stages * (TC_BLOCK_M + block_n // cta_group) * block_k * stage_bytes
     return ring + 1024 + 8 * (2 * stages + 5) + 16
 
 
@@ -191,9 +193,9 @@ def default_swap(m: int, n: int) -> bool:
 
 
 def tf32_split_k(k: int) -> int:
-    """The K the tcgen05 kernel sees for an fp32 problem: three TF32 segments of K
-    rounded up to a 32-element atom (mirrors tf32_split.cu)."""
-    return 3 * -(-k // 32) * 32
+    """The K the tcgen05 kernel sees for an fp32 problem: K rounded up to a
+    32-element atom; each k-block carries both TF32 parts (mirrors tf32_split.cu)."""
+    return -(-k // 32) * 32
 
 
 def tf32_applies(m: int, n: int, k: int, dtype: torch.dtype) -> bool:
@@ -221,8 +223,9 @@ def default_tcgen05_config(
     else:
         block_n = widest
     atom = 128 // elem  # elements per 128-byte swizzle row
-    block_k = 2 * atom if (cg == 2 and k >= 512) else atom
-    per_stage = (TC_BLOCK_M + block_n // cg) * block_k * elem
+    stage_elem = 2 * elem if elem == 4 else elem  # TF32 stages carry both split parts
+    block_k = 2 * atom if (cg == 2 and k >= 512 and elem != 4) else atom
+    per_stage = (TC_BLOCK_M + block_n // cg) * block_k * stage_elem
     stages = max(2, min(12, (SM100_SMEM_PER_BLOCK - 1024 - 256) // per_stage))
     tiles_m = -(-m_k // (TC_BLOCK_M * cg))
     tiles = tiles_m * -(-n_k // block_n)
@@ -243,7 +246,7 @@ def default_tcgen05_config(
         stream_k = 1 if (cg == 1 and tiles < sm_count) else 3
     # A panels of one raster group within ~48 MB of L2 (mirrors api.cu)
     tile_rows = TC_BLOCK_M * cg
-    group_m = max(1, min(-(-m_k // tile_rows), (48 << 20) // max(1, tile_rows * k * elem)))
+    group_m = max(1, min(-(-m_k // tile_rows), (48 << 20) // max(1, tile_rows * k * stage_elem)))
     return KernelConfig(
         operation,
         KERNEL=KERNEL_TCGEN05,

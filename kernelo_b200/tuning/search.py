@@ -244,7 +244,8 @@ class _Sm100GemmSpace(SearchSpace):
         k = self.tc_k(problem)
         m_k = n if gc.default_swap(m, n) else m
         rows = max(block_m, gc.TC_BLOCK_M)
-        return max(1, min(ceil_div(m_k, rows), self.GROUP_L2_BYTES // max(1, rows * k * problem.itemsize)))
+        panel = rows * k * problem.itemsize * (2 if self.tf32(problem) else 1)  # TF32: both split parts
+        return max(1, min(ceil_div(m_k, rows), self.GROUP_L2_BYTES // max(1, panel)))
 
     def library_default(self, problem: Problem) -> KernelConfig:
         """The config the library picks on its own: always a candidate, so that

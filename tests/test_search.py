@@ -124,7 +124,7 @@ def test_fp32_runs_as_3xtf32_and_unaligned_16bit_packs(b200_caps):
     space = MatmulSearchSpace()
     cands = space.candidates(fp32, b200_caps)
     assert cands[0]["KERNEL"] == gc.KERNEL_TCGEN05 and cands[0]["BLOCK_K"] in (32, 64)
-    assert space.tc_k(fp32) == gc.tf32_split_k(4099) == 3 * 4128
+    assert space.tc_k(fp32) == gc.tf32_split_k(4099) == 4128
     assert {c["BLOCK_K"] for c in cands if c["KERNEL"] == gc.KERNEL_TCGEN05} <= {32, 64}
     assert any(c["KERNEL"] == gc.KERNEL_SIMT for c in space.grid(fp32))
     # the split B is K-major: 16-column tiles are not refused as MN-major boxes

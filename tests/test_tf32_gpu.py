@@ -26,14 +26,15 @@ def operands(m, k, n, device, seed=0):
 
 
 def tf32_cfg(op="matmul", **kw):
-    base = dict(KERNEL=1, BLOCK_M=128, BLOCK_N=128, BLOCK_K=32, GROUP_M=8, num_stages=4, STREAM_K=2, SWAP_AB=2)
+    # a TF32 stage holds both split parts: 8 bytes per (row, k)
+    base = dict(KERNEL=1, BLOCK_M=128, BLOCK_N=128, BLOCK_K=32, GROUP_M=8, num_stages=3, STREAM_K=2, SWAP_AB=2)
     base.update(kw)
     return KernelConfig(op, **base)
 
 
 def split_workspace_bytes(a, b, c) -> int:
     """Workspace the library plans for this call: the TF32 split copies make it
-    at least 12 bytes per operand element (0 or the stream-K state otherwise)."""
+    at least 8 bytes per operand element (0 or the stream-K state otherwise)."""
     lib = native.load()
     cfg = native.GemmLaunch().struct()
     return lib.kf_gemm_workspace_bytes_for(a.device.index or 0, native.native_code(a.dtype), a.data_ptr(),
@@ -45,7 +46,7 @@ def split_workspace_bytes(a, b, c) -> int:
 def ran_on_tensor_cores(a, b, out) -> bool:
     """The default path planned the split (workspace for both TF32 copies) and
     its result is not the CUDA-core kernel's bit for bit."""
-    planned = split_workspace_bytes(a, b, out) >= 12 * (a.numel() + b.numel())
+    planned = split_workspace_bytes(a, b, out) >= 8 * (a.numel() + b.numel())
     simt = matmul(a, b, config=KernelConfig("matmul", KERNEL=2, BLOCK_M=128, BLOCK_N=128, BLOCK_K=8))
     return planned and not torch.equal(simt, out)
 
@@ -63,9 +64,9 @@ def test_default_fp32_runs_3xtf32_at_the_fp32_gate(shape, device):
 
 
 @pytest.mark.parametrize("cfg", [
-    dict(BLOCK_K=32), dict(BLOCK_K=64, num_stages=3), dict(BLOCK_N=64, STREAM_K=1),
-    dict(BLOCK_M=256, BLOCK_N=128, BLOCK_K=64, num_stages=4, CLUSTER_M=2, STREAM_K=3),
-    dict(BLOCK_N=16, num_stages=8), dict(SWAP_AB=1, BLOCK_N=64),
+    dict(BLOCK_K=32), dict(BLOCK_N=64, BLOCK_K=64, num_stages=2), dict(BLOCK_N=64, STREAM_K=1),
+    dict(BLOCK_M=256, BLOCK_N=128, BLOCK_K=32, num_stages=4, CLUSTER_M=2, STREAM_K=3),
+    dict(BLOCK_N=16, num_stages=6), dict(SWAP_AB=1, BLOCK_N=64),
 ], ids=lambda c: "-".join(f"{k}{v}" for k, v in c.items()))
 @pytest.mark.parametrize("shape", [(300, 200, 100), (640, 520, 1000), (70, 4099, 33)],
                          ids=lambda s: "x".join(map(str, s)))
@@ -99,11 +100,11 @@ def test_tf32_layouts_and_views(device):
 @pytest.mark.parametrize("approximate", ["none", "tanh"])
 def test_fp32_fused_linear_on_tf32(approximate, device):
     gen = torch.Generator().manual_seed(7)
-    x = torch.randn(300, 512, generator=gen).to(device)
+    x = torch.randn(400, 512, generator=gen).to(device)  # 1.4e8 multiply-adds: past the 2^27 threshold
     w = (torch.randn(700, 512, generator=gen) * 512 ** -0.5).to(device)
     b = (torch.randn(700, generator=gen) * 0.3).to(device)
     out = fused_linear_gelu(x, w.t(), b, approximate=approximate)
-    assert split_workspace_bytes(x, w.t(), out) >= 12 * (x.numel() + w.numel())
+    assert split_workspace_bytes(x, w.t(), out) >= 8 * (x.numel() + w.numel())
     expect = ref.linear_gelu_ref(host(x), host(w.t()), host(b), approximate=approximate)
     gate(expect, out, torch.float32)
 
@@ -127,6 +128,6 @@ def test_small_fp32_keeps_ieee_fma(device):
     planned, and the result is that kernel's bit for bit."""
     a, b = operands(257, 257, 257, device)
     out = matmul(a, b)
-    assert split_workspace_bytes(a, b, out) < 12 * (a.numel() + b.numel())
+    assert split_workspace_bytes(a, b, out) < 8 * (a.numel() + b.numel())
     simt = matmul(a, b, config=KernelConfig("matmul", KERNEL=2, BLOCK_M=64, BLOCK_N=64, BLOCK_K=16))
     assert torch.equal(simt, out)
