@@ -35,8 +35,9 @@
 //
 // Work is a list of segments (tile, k-block range). Data-parallel mode gives
 // every CTA (pair) whole tiles in a grouped (GROUP_M) raster. Stream-K mode
-// (CG = 1 only) splits the flattened (tile, k-block) iteration space evenly
-// over the grid; a tile split between CTAs is finished by whichever
+// (the library picks it for one-SM tiles; pairs run it when asked) splits the
+// flattened (tile, k-block) iteration space evenly over the grid; a tile
+// split between units is finished by whichever
 // contributor arrives last, which sums the fp32 partials in a fixed order (so
 // results are deterministic) and runs the epilogue. Nobody waits for another
 // CTA, so the scheme cannot deadlock.
