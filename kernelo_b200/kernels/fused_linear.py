@@ -106,10 +106,13 @@ def fused_linear_gelu_host(
     """``gelu(x @ w + bias)`` for activations in pinned host memory, result in
     pinned host memory; ``w`` and ``bias`` are resident on the GPU.
 
-    The rows move in ``chunks`` pieces on two copy streams: chunk i+1 goes to
-    the device while chunk i runs through the fused kernel and chunk i-1
-    comes back, so a call costs about the larger of the two transfer
-    directions instead of their sum plus the kernel. Everything is ordered
+    The rows move in about ``chunks`` pieces on two copy streams: chunk i+1
+    goes to the device while chunk i runs through the fused kernel and chunk
+    i-1 comes back, so a call costs about the larger of the two transfer
+    directions instead of their sum plus the kernel. The first chunk is 256
+    rows, so that the device-to-host copies start early (4096 x 11008 x 4096
+    bf16 on B200: 1.84 ms a call against 1.90 with eight equal chunks; the
+    two copies alone, overlapped, take 1.66 ms). Everything is ordered
     after the work already queued on the current stream, and the current
     stream waits for the last copy, so synchronising it makes ``out`` valid.
     Each chunk is one launch of the same kernel as :func:`fused_linear_gelu`.
@@ -138,12 +141,20 @@ def fused_linear_gelu_host(
     s_in, s_out = _streams(dev)
     x_dev = torch.empty((m, x_host.shape[1]), device=dev, dtype=x_host.dtype)
     y_dev = torch.empty((m, n), device=dev, dtype=x_host.dtype)
-    rows = -(-m // chunks)
-    rows = -(-rows // 128) * 128  # whole 128-row MMA tiles per chunk
+    # Row boundaries: a short first chunk (256 rows) so that the device-to-host
+    # copies, the longer direction, start as early as possible; the rest in
+    # equal chunks of whole 128-row MMA tiles.
+    bounds = [0]
+    if chunks > 1 and m > 512:
+        bounds.append(256)
+    rest = m - bounds[-1]
+    parts = max(1, chunks - (len(bounds) - 1))
+    step = -(-(-(-rest // parts)) // 128) * 128
+    while bounds[-1] < m:
+        bounds.append(min(m, bounds[-1] + step))
     s_in.wait_stream(compute)
     s_out.wait_stream(compute)
-    for r0 in range(0, m, rows):
-        r1 = min(m, r0 + rows)
+    for r0, r1 in zip(bounds[:-1], bounds[1:]):
         with torch.cuda.stream(s_in):
             x_dev[r0:r1].copy_(x_host[r0:r1], non_blocking=True)
         loaded = s_in.record_event()
