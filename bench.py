@@ -275,9 +275,10 @@ def dist_setup(gpus: int):
         raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        # NCCL carries only the timing reductions and the gate here; without
-        # NVLS no buffer is ever bound to an NVLink multicast object, so a rank
-        # that fails cannot take its peers' GPUs down with it.
+        # NCCL carries the timing reductions, the gate and, where it measures
+        # faster than the fused gather at this N, the all-gather; without NVLS
+        # no buffer is ever bound to an NVLink multicast object, so a rank that
+        # fails cannot take its peers' GPUs down with it.
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
@@ -623,9 +624,10 @@ def run_native(args, world: int, rank: int, local: int) -> int:
     dev = torch.device("cuda", local)
     pk, pk_kind = peaks()
     x, w, b, chunk = make_inputs(dev, rank, world)
+    mode = "single"
     if world > 1:
         layer = ShardedFusedLinear(None, None, out_features=N, shard_weight=w, shard_bias=b, approximate="none",
-                                   gather="fused")
+                                   gather="auto")
         written: list[torch.Tensor] = []
 
         # layer(x) in two parts, so the timed loop can bracket the kernel alone:
@@ -668,6 +670,16 @@ def run_native(args, world: int, rank: int, local: int) -> int:
         del nccl
         if max_over_ranks(differs, world) > 0:  # every rank takes the same exit
             raise SystemExit("the fused all-gather differs from the NCCL all-gather before timing")
+        # The layer's own choice of gather at this N, by measurement (collective;
+        # every rank sees the slowest rank's times, so all choose alike).
+        mode = layer.gather_mode(x)
+        if mode == "nccl":
+            # the local GEMM is the bracketed kernel; NCCL's all-gather follows
+            def launch_kernel():
+                layer.nccl_kernel(x)
+
+            def finish_step():
+                return layer.nccl_publish(x)
     if max_over_ranks(float(native.device_status(local) != 0), world) > 0:
         raise SystemExit("device status word set before timing")
 
@@ -716,9 +728,17 @@ def run_native(args, world: int, rank: int, local: int) -> int:
                     "kernel": "tc_gemm_kernel<bf16,erf>", "kernel_ms": round(kernel_ms, 4)}
     else:
         link = measure_peer_copy_gbs(dev, world, rank)
-        roofline = allgather_roofline(flop_rank, M * chunk * 2 * (world - 1), kernel_ms, peak, peak_kind,
-                                      link["gbs"])
+        if mode == "fused":
+            roofline = allgather_roofline(flop_rank, M * chunk * 2 * (world - 1), kernel_ms, peak, peak_kind,
+                                          link["gbs"])
+        else:
+            # the bracketed kernel is the shard's GEMM alone; NCCL gathers after it
+            roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                        "kernel": "tc_gemm_kernel<bf16,erf> (shard; NCCL all-gather follows)",
+                        "kernel_ms": round(kernel_ms, 4), "step_ms": round(ms_step, 4)}
         roofline["nvlink_measurement"] = link
+        roofline["gather"] = {"chosen": mode, "ms_per_3_calls": layer.gather_timings.get(M)}
 
     # end to end through the public API: pinned host X in, Y back to pinned host
     e2e_steps = max(3, min(20, args.steps))
@@ -771,8 +791,11 @@ def run_native(args, world: int, rank: int, local: int) -> int:
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) X, N(0,1/4096) W, N(0,0.1) b; random init)",
             "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "gelu": "erf",
-                       "parallelism": (f"N-sharded columns x{world}, all-gather fused into the GEMM epilogue "
-                                       "(NVLink peer stores) + bounded peer barrier") if world > 1 else "single GPU",
+                       "parallelism": ("single GPU" if world == 1 else
+                                       f"N-sharded columns x{world}, all-gather fused into the GEMM epilogue "
+                                       "(NVLink peer stores) + bounded peer barrier" if mode == "fused" else
+                                       f"N-sharded columns x{world}, local GEMM + NCCL all_gather_into_tensor "
+                                       "(chosen over the fused gather by measurement at this N)"),
                        "l2": "inputs exceed L2 (X 32 MiB + W 86 MiB + Y 86 MiB > 126 MiB), no flush"},
             "roofline": roofline,
             "clocks": clock_summary,
@@ -781,12 +804,12 @@ def run_native(args, world: int, rank: int, local: int) -> int:
                     "bound": {"by": "host link (PCIe), pinned copies measured in this run on rank 0",
                               **pcie, "tflops_if_copies_alone": round(pcie_bound, 1),
                               "frac": round(e2e_value / pcie_bound, 3)},
-                    "api": ("fused_linear_gelu_host (pinned X in, pinned Y out, 8 row chunks overlapping "
+                    "api": ("fused_linear_gelu_host (pinned X in, pinned Y out, row chunks (a 256-row first one) overlapping "
                             "copies and kernel)" if world == 1 else
                             "ShardedFusedLinear.forward_host: each rank copies 1/N of X's rows in and 1/N of "
                             f"Y's rows out (bytes summed over ranks), X all-gathered over NVLink, "
                             f"{max(1, 8 // world)} row chunk(s) pipelined")},
-            "gpu_launches": args.steps * (2 if world > 1 else 1),
+            "gpu_launches": args.steps * (2 if mode == "fused" else 1),
             "cpu_baseline": baseline,
             "secondary": secondary,
         }

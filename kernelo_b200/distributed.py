@@ -185,11 +185,22 @@ class ShardedFusedLinear:
 
     def nccl_step(self, x: torch.Tensor) -> torch.Tensor:
         """The local GEMM, then one all-gather of the group's backend and a permute into [M, N]."""
+        self.nccl_kernel(x)
+        return self.nccl_publish(x)
+
+    def nccl_kernel(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's GEMM into its slot of the gather buffer (the first half of :meth:`nccl_step`)."""
         m = x.shape[0]
         if self._gather_buf is None or self._gather_buf.shape != (self.world, m, self.chunk):
             self._gather_buf = torch.empty(self.world, m, self.chunk, device=x.device, dtype=x.dtype)
         mine = self._gather_buf[self.rank]
         self.local(x, out=mine)
+        return mine
+
+    def nccl_publish(self, x: torch.Tensor) -> torch.Tensor:
+        """The all-gather and the permute into [M, N] (the second half of :meth:`nccl_step`)."""
+        m = x.shape[0]
+        mine = self._gather_buf[self.rank]
         dist.all_gather_into_tensor(self._gather_buf.view(-1), mine.reshape(-1), group=self.group)
         full = self._gather_buf.permute(1, 0, 2).reshape(m, self.world * self.chunk)
         return full[:, : self.n]
