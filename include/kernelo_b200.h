@@ -310,6 +310,35 @@ KF_API int32_t kf_peer_barrier_counted(uint32_t* local_signals, uint32_t* const*
                                        int32_t rank, int32_t world, uint32_t* epoch_counter,
                                        int32_t timeout_us, void* stream);
 
+/* The bounded cross-GPU barrier that completes an all-gather, as one struct
+ * (kf_peer_barrier_counted's arguments plus an arrival word): `arrivals` is a
+ * zeroed 4-byte device word of this rank, used and left at zero by the fused
+ * form below. */
+typedef struct kf_peer_sync {
+  uint32_t* local_signals;        /* this rank's signal array [world]            */
+  uint32_t* const* peer_signals;  /* the other ranks' arrays, rank order, this
+                                     rank skipped                               */
+  int32_t rank, world;
+  uint32_t* epoch_counter;        /* this rank's epoch word (device)             */
+  uint32_t* arrivals;             /* zeroed device word of this rank             */
+  int32_t timeout_us;
+  int32_t reserved;
+} kf_peer_sync;
+
+/* kf_linear_bias_act_allgather followed by kf_peer_barrier_counted, in one
+ * launch where the all-gather runs on the 16-row tile GEMV (M <= 32): the
+ * last CTA to finish (found by an atomic on `sync->arrivals`) runs the barrier
+ * itself, so no second kernel is launched. On the tcgen05 path the barrier
+ * kernel follows the GEMM on `stream`. Either way the peers' copies of Y hold
+ * every rank's block once this call's work on `stream` is done. */
+KF_API int32_t kf_linear_bias_act_allgather_sync(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
+                                                 const void* w, int64_t sw_k, int64_t sw_n, const void* bias,
+                                                 void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N,
+                                                 int64_t K, int32_t epilogue, void* const* y_peers,
+                                                 int32_t n_peers, const kf_peer_sync* sync,
+                                                 const kf_gemm_config* cfg, void* workspace,
+                                                 int64_t workspace_bytes, void* stream);
+
 /* Peer mapping for the all-gather buffers, by CUDA IPC (no multicast object).
  * kf_ipc_handle: the IPC handle (KF_IPC_HANDLE_BYTES bytes) of the allocation
  * holding `ptr`, and ptr's byte offset in it. kf_ipc_open: map a handle from

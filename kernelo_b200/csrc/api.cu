@@ -355,9 +355,21 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
       return set_error(KF_ERR_UNALIGNED, "tile GEMV: " + why);
     // The library's own choice ignores the other config fields (they describe
     // tcgen05 tiles when the kernel was left to the library).
-    return launch_gemv_mma(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K,
-                           tile_auto ? zero_config() : *user, static_cast<cudaStream_t>(stream), g.epilogue,
-                           g.bias, g.peers, g.n_peers);
+    int* status = nullptr;
+    if (g.sync != nullptr) {  // the barrier runs in the kernel's last CTA
+      int device = 0;
+      int rc = current_device(&device);
+      if (rc != KF_OK) return rc;
+      DeviceInfo* dev = nullptr;
+      rc = device_info(device, &dev);
+      if (rc != KF_OK) return rc;
+      status = dev->status;
+    }
+    const int rc = launch_gemv_mma(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K,
+                                   tile_auto ? zero_config() : *user, static_cast<cudaStream_t>(stream),
+                                   g.epilogue, g.bias, g.peers, g.n_peers, g.sync, status);
+    if (rc == KF_OK && g.sync != nullptr) g.sync_done = true;
+    return rc;
   }
   // Up to 8 rows of x against an N-contiguous B (the reference's row-major
   // (K, N) operand): lanes stream B's rows in 512-byte warp loads, K split
@@ -532,12 +544,13 @@ int32_t kf_linear_bias_act(int32_t dtype, const void* x, int64_t sx_m, int64_t s
   return gemm_common(g, cfg, stream);
 }
 
-int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
-                                     const void* w, int64_t sw_k, int64_t sw_n, const void* bias,
-                                     void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N,
-                                     int64_t K, int32_t epilogue, void* const* y_peers,
-                                     int32_t n_peers, const kf_gemm_config* cfg, void* workspace,
-                                     int64_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+static int allgather_impl(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w, int64_t sw_k,
+                          int64_t sw_n, const void* bias, void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N,
+                          int64_t K, int32_t epilogue, void* const* y_peers, int32_t n_peers,
+                          const kf_peer_sync* sync, const kf_gemm_config* cfg, void* workspace,
+                          int64_t workspace_bytes, void* stream) {
   if (n_peers < 0 || n_peers > KF_MAX_PEERS)
     return set_error(KF_ERR_INVALID_ARGUMENT,
                      "n_peers must be in [0, " + std::to_string(KF_MAX_PEERS) + "]");
@@ -567,7 +580,43 @@ int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_t sx_m,
     if (y_peers[i] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer output pointer");
     g.peers[i] = y_peers[i];
   }
-  return gemm_common(g, cfg, stream);
+  g.sync = sync;
+  int rc = gemm_common(g, cfg, stream);
+  if (rc != KF_OK || sync == nullptr || g.sync_done) return rc;
+  // the tcgen05 path (or an empty output): the barrier kernel follows
+  int device = 0;
+  rc = current_device(&device);
+  if (rc != KF_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = device_info(device, &dev);
+  if (rc != KF_OK) return rc;
+  return launch_peer_barrier(sync->local_signals, sync->peer_signals, sync->rank, sync->world, 0, sync->timeout_us,
+                             *dev, static_cast<cudaStream_t>(stream), sync->epoch_counter);
+}
+
+
+extern "C" {
+
+int32_t kf_linear_bias_act_allgather(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
+                                     const void* w, int64_t sw_k, int64_t sw_n, const void* bias,
+                                     void* y, int64_t sy_m, int64_t sy_n, int64_t M, int64_t N,
+                                     int64_t K, int32_t epilogue, void* const* y_peers,
+                                     int32_t n_peers, const kf_gemm_config* cfg, void* workspace,
+                                     int64_t workspace_bytes, void* stream) {
+  return allgather_impl(dtype, x, sx_m, sx_k, w, sw_k, sw_n, bias, y, sy_m, sy_n, M, N, K, epilogue, y_peers, n_peers,
+                        nullptr, cfg, workspace, workspace_bytes, stream);
+}
+
+int32_t kf_linear_bias_act_allgather_sync(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k,
+                                          const void* w, int64_t sw_k, int64_t sw_n, const void* bias, void* y,
+                                          int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
+                                          int32_t epilogue, void* const* y_peers, int32_t n_peers,
+                                          const kf_peer_sync* sync, const kf_gemm_config* cfg, void* workspace,
+                                          int64_t workspace_bytes, void* stream) {
+  if (sync == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer sync");
+  if (sync->epoch_counter == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null epoch counter");
+  return allgather_impl(dtype, x, sx_m, sx_k, w, sw_k, sw_n, bias, y, sy_m, sy_n, M, N, K, epilogue, y_peers, n_peers,
+                        sync, cfg, workspace, workspace_bytes, stream);
 }
 
 int32_t kf_peer_barrier(uint32_t* local_signals, uint32_t* const* peer_signals, int32_t rank,

@@ -36,6 +36,7 @@
 
 #include "kf_common.cuh"
 #include "kf_internal.h"
+#include "peer_sync.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -59,6 +60,14 @@ struct GemvMmaParams {
   // every output element is stored there too -- the decode-shape all-gather.
   int n_peers;
   void* peers[KF_MAX_PEERS];
+  // In-kernel peer barrier (sync = 1): every storing CTA counts itself on
+  // `arrivals`; the last one advances *epoch_counter and signals the peers.
+  int sync;
+  uint32_t* arrivals;
+  uint32_t* epoch_counter;
+  unsigned int storing_ctas;
+  PeerSignals sig;
+  int* status;
 };
 
 template <typename T>
@@ -254,11 +263,34 @@ __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams
       }
     }
   }
-  // No fence here: the peer barrier that follows on the stream starts after
-  // this kernel has completed, and its system-scope fence before the release
-  // store is cumulative over these stores. (A fence.sc.sys at the end of
-  // every CTA measured +9 us on a 2-way shard of 11008 x 4096, 11 -> 20 us,
-  // with the "peer" copy in local memory as much as over NVLink.)
+  // No fence per CTA: the barrier fences once at system scope, cumulatively
+  // over these stores. (A fence.sc.sys at the end of every CTA measured +9 us
+  // on a 2-way shard of 11008 x 4096, 11 -> 20 us, with the "peer" copy in
+  // local memory as much as over NVLink.) The barrier is either the kernel
+  // that follows on the stream, or (sync) this kernel's last CTA: each CTA's
+  // warp counts itself with an acq_rel atomic at GPU scope after its lanes'
+  // stores (ordered by __syncwarp), so the last one has observed every CTA's
+  // stores before it fences and signals.
+  if (p.sync) {
+    __syncwarp();
+    unsigned int last = 0;
+    if (lane == 0) {
+      unsigned int prev;
+      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.arrivals) : "memory");
+      last = prev + 1u == p.storing_ctas ? 1u : 0u;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      uint32_t epoch = 0;
+      if (lane == 0) {
+        *p.arrivals = 0u;  // for the next launch (kernel boundary)
+        epoch = *p.epoch_counter + 1u;
+        *p.epoch_counter = epoch;
+      }
+      epoch = __shfl_sync(0xffffffffu, epoch, 0);
+      peer_signal_and_wait(p.sig, epoch, lane, p.status);
+    }
+  }
 }
 
 template <typename T, int NT, int S, int U, int EPI>
@@ -365,7 +397,7 @@ bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, co
 int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
                     int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
                     const kf_gemm_config& cfg, cudaStream_t stream, int epilogue, const void* bias,
-                    void* const* peers, int n_peers) {
+                    void* const* peers, int n_peers, const kf_peer_sync* sync, int* status) {
   if (epilogue != KF_EPI_NONE && bias == nullptr)
     return set_error(KF_ERR_INVALID_ARGUMENT, "epilogue needs a bias pointer");
   if (n_peers < 0 || n_peers > KF_MAX_PEERS || (n_peers > 0 && peers == nullptr))
@@ -389,6 +421,23 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
   for (int j = 0; j < n_peers; ++j) {
     if (peers[j] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer output pointer");
     p.peers[j] = peers[j];
+  }
+  if (sync != nullptr) {
+    if (sync->arrivals == nullptr || sync->epoch_counter == nullptr || sync->local_signals == nullptr ||
+        sync->peer_signals == nullptr)
+      return set_error(KF_ERR_INVALID_ARGUMENT, "peer sync: null arrival, epoch or signal pointer");
+    if (sync->world < 2 || sync->world > KF_MAX_PEERS + 1 || sync->rank < 0 || sync->rank >= sync->world)
+      return set_error(KF_ERR_INVALID_ARGUMENT, "peer sync: rank / world out of range");
+    if (sync->timeout_us <= 0 || sync->timeout_us > 60000000)
+      return set_error(KF_ERR_INVALID_ARGUMENT, "peer sync: timeout_us must be in (0, 6e7]");
+    const int rc = fill_peer_signals(sync->local_signals, sync->peer_signals, sync->rank, sync->world,
+                                     sync->timeout_us, &p.sig);
+    if (rc != KF_OK) return rc;
+    p.sync = 1;
+    p.arrivals = sync->arrivals;
+    p.epoch_counter = sync->epoch_counter;
+    p.storing_ctas = static_cast<unsigned int>((N + 15) / 16);
+    p.status = status;
   }
   if (N == 0 || M == 0) return KF_OK;
   if (dtype == KF_BF16) return launch_typed<__nv_bfloat16>(p, cfg, epilogue, stream);

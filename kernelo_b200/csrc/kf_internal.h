@@ -48,6 +48,10 @@ struct GemmArgs {
   // of [small | big] with K (= kp) elements each; the tcgen05 kernel runs
   // them as kind::tf32, three MMAs per k-block.
   bool tf32_split = false;
+  // Peer barrier to run after the all-gather (kf_linear_bias_act_allgather_sync):
+  // the tile GEMV runs it in its last CTA and sets sync_done.
+  const kf_peer_sync* sync = nullptr;
+  bool sync_done = false;
 };
 
 // Stream-K workspace layout (tcgen05 GEMM): one int32 arrival counter per
@@ -127,7 +131,8 @@ bool gemv_mma_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, co
 int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
                     int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K,
                     const kf_gemm_config& cfg, cudaStream_t stream, int epilogue = KF_EPI_NONE,
-                    const void* bias = nullptr, void* const* peers = nullptr, int n_peers = 0);
+                    const void* bias = nullptr, void* const* peers = nullptr, int n_peers = 0,
+                    const kf_peer_sync* sync = nullptr, int* status = nullptr);
 
 // Decode-shape GEMM against an N-contiguous B (gemv_cols.cu): M <= 8, any
 // dtype, K split over CTAs with a deterministic last-arrival sum.

@@ -26,33 +26,17 @@
 
 #include "kf_common.cuh"
 #include "kf_internal.h"
+#include "peer_sync.cuh"
 
 namespace kf {
 namespace {
 
 struct PeerBarrierParams {
-  uint32_t* local;                    // this rank's signal array [world]
-  uint32_t* peers[KF_MAX_PEERS];      // the other ranks' arrays, in rank order
-  int peer_rank[KF_MAX_PEERS];        // their ranks
-  int rank, n_peers;
+  PeerSignals sig;
   uint32_t epoch;
   uint32_t* counter;  // counted form: the epoch is *counter + 1 (this rank's memory)
-  unsigned long long timeout_ns;
   int* status;
 };
-
-__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ bool reached(uint32_t v, uint32_t epoch) {
-  return static_cast<int32_t>(v - epoch) >= 0;
-}
 
 __global__ void peer_barrier_kernel(const PeerBarrierParams p) {
   const int t = threadIdx.x;
@@ -64,24 +48,27 @@ __global__ void peer_barrier_kernel(const PeerBarrierParams p) {
     __syncwarp();
     if (t == 0) *p.counter = epoch;
   }
-  if (t >= p.n_peers) return;
-  __threadfence_system();
-  st_release_sys(p.peers[t] + p.rank, epoch);
-  // A peer that saw this rank's signal may run ahead and write epoch + 1
-  // before this poll reads epoch, so "reached" is a wrap-safe v >= epoch.
-  const uint32_t* mine = p.local + p.peer_rank[t];
-  if (reached(ld_acquire_sys(mine), epoch)) return;
-  const unsigned long long start = global_timer_ns();
-  for (uint32_t spin = 1;; ++spin) {
-    if (reached(ld_acquire_sys(mine), epoch)) return;
-    if ((spin & 63u) == 0 && global_timer_ns() - start > p.timeout_ns) {
-      record_status(p.status, KF_ERR_TIMEOUT, SITE_PEER_BARRIER);
-      return;
-    }
-  }
+  peer_signal_and_wait(p.sig, epoch, t, p.status);
 }
 
 }  // namespace
+
+int fill_peer_signals(uint32_t* local, uint32_t* const* peers, int rank, int world, int timeout_us,
+                      PeerSignals* out) {
+  PeerSignals& s = *out;
+  s.local = local;
+  s.rank = rank;
+  s.n_peers = world - 1;
+  for (int i = 0, r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    if (peers[i] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer signal pointer");
+    s.peers[i] = peers[i];
+    s.peer_rank[i] = r;
+    ++i;
+  }
+  s.timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
+  return KF_OK;
+}
 
 int launch_peer_barrier(uint32_t* local, uint32_t* const* peers, int rank, int world,
                         uint32_t epoch, int timeout_us, const DeviceInfo& dev, cudaStream_t stream,
@@ -97,19 +84,10 @@ int launch_peer_barrier(uint32_t* local, uint32_t* const* peers, int rank, int w
   if (local == nullptr || peers == nullptr)
     return set_error(KF_ERR_INVALID_ARGUMENT, "null signal pointer");
   PeerBarrierParams p{};
-  p.local = local;
-  p.rank = rank;
-  p.n_peers = world - 1;
-  for (int i = 0, r = 0; r < world; ++r) {
-    if (r == rank) continue;
-    if (peers[i] == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null peer signal pointer");
-    p.peers[i] = peers[i];
-    p.peer_rank[i] = r;
-    ++i;
-  }
+  const int rc = fill_peer_signals(local, peers, rank, world, timeout_us, &p.sig);
+  if (rc != KF_OK) return rc;
   p.epoch = epoch;
   p.counter = counter;
-  p.timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
   p.status = dev.status;
   peer_barrier_kernel<<<1, 32, 0, stream>>>(p);
   const cudaError_t err = cudaGetLastError();

@@ -207,9 +207,11 @@ class ShardedFusedLinear:
 
 
     # ---------------------------------------------------------------- fused all-gather
-    def fused_kernel(self, x: torch.Tensor) -> torch.Tensor:
+    def fused_kernel(self, x: torch.Tensor, *, sync: bool = False) -> torch.Tensor:
         """Launch this rank's GEMM whose epilogue also writes every peer's Y;
-        returns the buffer it wrote (valid on all ranks after :meth:`fused_publish`)."""
+        returns the buffer it wrote (valid on all ranks after :meth:`fused_publish`,
+        or at once with ``sync``: the barrier follows in the same call, inside
+        the kernel on the tile GEMV path)."""
         from kernelo_b200.runtime import native
 
         m = x.shape[0]
@@ -220,7 +222,9 @@ class ShardedFusedLinear:
         buf, peers = sym.next_buffer(self.rank * self.chunk)
         mine = buf[:, self.rank * self.chunk:(self.rank + 1) * self.chunk]
         native.linear_bias_act_allgather(x, self.w.t(), mine, peers, bias=self.b, epilogue=self._epilogue(),
-                                         launch=native.GemmLaunch.from_config(self.config))
+                                         launch=native.GemmLaunch.from_config(self.config),
+                                         sync=sym.sync(self.rank, self.world, self.barrier_timeout_us) if sync
+                                         else None)
         return buf
 
     def fused_publish(self, x: torch.Tensor) -> None:
@@ -347,8 +351,7 @@ class ShardedFusedLinear:
         barrier and raises if the status word is set (a host round trip per
         call); otherwise read :func:`kernelo_b200.runtime.native.device_status`
         at a point of your choosing."""
-        buf = self.fused_kernel(x)
-        self.fused_publish(x)
+        buf = self.fused_kernel(x, sync=True)
         if check_status:
             from kernelo_b200.runtime import native
 
@@ -445,8 +448,11 @@ class _PeerOutput:
         check_peer_geometry(m, n_total, dtype, chunk, group)
         self.bufs = [torch.empty((m, n_total), dtype=dtype, device=device) for _ in range(2)]
         self.signals = torch.zeros((self.world,), dtype=torch.int32, device=device)
-        # this rank's barrier epoch, advanced on the device by each barrier
+        # this rank's barrier epoch, advanced on the device by each barrier,
+        # and the arrival word of the in-kernel barrier (left at zero)
         self.counter = torch.zeros((1,), dtype=torch.int32, device=device)
+        self.arrivals = torch.zeros((1,), dtype=torch.int32, device=device)
+        self._sync = None
         torch.cuda.synchronize(device)
         mine = [native.ipc_handle(t) for t in (*self.bufs, self.signals)]
         everyone: list = [None] * self.world
@@ -478,6 +484,16 @@ class _PeerOutput:
 
     def signal_ptrs(self) -> tuple[int, list[int]]:
         return self.signals.data_ptr(), [self.peer_ptrs[2][j] for j in range(self.world) if j != self.rank]
+
+    def sync(self, rank: int, world: int, timeout_us: int):
+        """The barrier's arguments as one kf_peer_sync struct (built once)."""
+        from kernelo_b200.runtime import native
+
+        if self._sync is None:
+            local, peers = self.signal_ptrs()
+            self._sync = native.peer_sync_struct(local, peers, rank, world, self.counter.data_ptr(),
+                                                 self.arrivals.data_ptr(), timeout_us)
+        return self._sync
 
     def barrier(self, rank: int, world: int, timeout_us: int) -> None:
         """Enqueue the bounded barrier; its epoch lives on the device, so a

@@ -67,6 +67,7 @@ EXPORTED_SYMBOLS = (
     "kf_selftest_bounded_wait",
     "kf_gemv_noalloc",
     "kf_linear_bias_act_allgather",
+    "kf_linear_bias_act_allgather_sync",
     "kf_peer_barrier",
     "kf_peer_barrier_counted",
     "kf_ipc_handle",
@@ -138,6 +139,19 @@ class KfRowsConfig(ctypes.Structure):
     ]
 
 
+class KfPeerSync(ctypes.Structure):
+    _fields_ = [
+        ("local_signals", ctypes.c_void_p),
+        ("peer_signals", ctypes.POINTER(ctypes.c_void_p)),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("epoch_counter", ctypes.c_void_p),
+        ("arrivals", ctypes.c_void_p),
+        ("timeout_us", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
 _i32, _i64, _vp, _f32 = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
 _GP = ctypes.POINTER(KfGemmConfig)
 _RP = ctypes.POINTER(KfRowsConfig)
@@ -167,6 +181,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kf_linear_bias_act_allgather": (_i32, [_i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64,
                                             _i64, _i64, _i64, _i32, ctypes.POINTER(_vp), _i32, _GP, _vp, _i64,
                                             _vp]),
+    "kf_linear_bias_act_allgather_sync": (_i32, [_i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64,
+                                                 _i64, _i64, _i64, _i32, ctypes.POINTER(_vp), _i32,
+                                                 ctypes.POINTER(KfPeerSync), _GP, _vp, _i64, _vp]),
     "kf_peer_barrier": (_i32, [_vp, ctypes.POINTER(_vp), _i32, _i32, ctypes.c_uint32, _i32, _vp]),
     "kf_peer_barrier_counted": (_i32, [_vp, ctypes.POINTER(_vp), _i32, _i32, _vp, _i32, _vp]),
     "kf_ipc_handle": (_i32, [_vp, _vp, ctypes.POINTER(_i64)]),
@@ -428,11 +445,24 @@ def gemm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, *, bias: torch.Tenso
             check(status, "kf_linear_bias_act")
 
 
+def peer_sync_struct(local_signals: int, peer_signals: list[int], rank: int, world: int, epoch_counter: int,
+                     arrivals: int, timeout_us: int = 2_000_000) -> KfPeerSync:
+    """The kf_peer_sync struct of one rank (keeps its peer-pointer array alive)."""
+    arr = (_vp * max(1, len(peer_signals)))(*[ctypes.c_void_p(int(p)) for p in peer_signals])
+    s = KfPeerSync(local_signals, ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)), rank, world, epoch_counter,
+                   arrivals, timeout_us, 0)
+    s._keep = arr
+    return s
+
+
 def linear_bias_act_allgather(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, peers: list[int], *,
-                              bias: torch.Tensor | None, epilogue: int, launch: GemmLaunch | None = None) -> None:
+                              bias: torch.Tensor | None, epilogue: int, launch: GemmLaunch | None = None,
+                              sync: KfPeerSync | None = None) -> None:
     """``c = epilogue(a @ b + bias)``, every output tile also stored at the same
     offsets from each address in ``peers`` (peer-mapped copies of c's buffer).
-    ``bias`` may be None with ``KF_EPI_NONE`` (the plain sharded GEMM/GEMV)."""
+    ``bias`` may be None with ``KF_EPI_NONE`` (the plain sharded GEMM/GEMV).
+    With ``sync`` the bounded peer barrier that completes the all-gather
+    follows in the same call (inside the kernel on the tile GEMV path)."""
     lib = load()
     launch = launch or GemmLaunch()
     cfg = launch.struct()
@@ -447,11 +477,19 @@ def linear_bias_act_allgather(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor,
         check(int(-ws_bytes), "kf_gemm_workspace_bytes")
     ws = workspaces.get(dev, stream, ws_bytes)
     arr = (_vp * max(1, len(peers)))(*[ctypes.c_void_p(int(p)) for p in peers])
-    status = lib.kf_linear_bias_act_allgather(code, a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(),
-                                              b.stride(0), b.stride(1), _ptr(bias), c.data_ptr(), c.stride(0),
-                                              c.stride(1), m, n, k, epilogue, arr, len(peers),
-                                              ctypes.byref(cfg), _ptr(ws), max(ws_bytes, 0), stream)
-    check(status, "kf_linear_bias_act_allgather")
+    if sync is None:
+        status = lib.kf_linear_bias_act_allgather(code, a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(),
+                                                  b.stride(0), b.stride(1), _ptr(bias), c.data_ptr(), c.stride(0),
+                                                  c.stride(1), m, n, k, epilogue, arr, len(peers),
+                                                  ctypes.byref(cfg), _ptr(ws), max(ws_bytes, 0), stream)
+        check(status, "kf_linear_bias_act_allgather")
+        return
+    status = lib.kf_linear_bias_act_allgather_sync(code, a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(),
+                                                   b.stride(0), b.stride(1), _ptr(bias), c.data_ptr(), c.stride(0),
+                                                   c.stride(1), m, n, k, epilogue, arr, len(peers),
+                                                   ctypes.byref(sync), ctypes.byref(cfg), _ptr(ws),
+                                                   max(ws_bytes, 0), stream)
+    check(status, "kf_linear_bias_act_allgather_sync")
 
 
 def peer_barrier(local_signals: int, peer_signals: list[int], rank: int, world: int, epoch: int,

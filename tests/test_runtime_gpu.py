@@ -151,3 +151,44 @@ def test_tuned_winner_is_no_slower_than_the_default(device):
     assert result.best is not None
     if default is not None:
         assert result.best.median_ms <= default.median_ms * 1.05
+
+
+def test_tile_gemv_runs_the_peer_barrier_in_its_last_cta(device):
+    """kf_linear_bias_act_allgather_sync on the tile GEMV (M <= 32) as rank 0
+    of 2, with the "peer" signal array and Y copy in local memory and rank 1's
+    arrival planted in advance: each call stores Y and the peer copy, its last
+    CTA advances the device epoch by one and signals the peer slot, and the
+    arrival word is back at zero; a peer that never reaches the epoch makes
+    the in-kernel wait give up after its limit with the barrier's site in the
+    status word, the context still usable."""
+    from kernelo_b200.kernels.gemv import gemv
+
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(4, 512, generator=gen).half().to(device)
+    w = (torch.randn(1000, 512, generator=gen) * 0.04).half().to(device)
+    y = torch.empty(4, 1000, device=device, dtype=torch.float16)
+    peer_y = torch.zeros_like(y)
+    local = torch.zeros(2, dtype=torch.int32, device=device)
+    peer_sig = torch.zeros(2, dtype=torch.int32, device=device)
+    counter = torch.zeros(1, dtype=torch.int32, device=device)
+    arrivals = torch.zeros(1, dtype=torch.int32, device=device)
+    local[1] = 100  # rank 1 "arrived" up to epoch 100
+    sync = native.peer_sync_struct(local.data_ptr(), [peer_sig.data_ptr()], 0, 2, counter.data_ptr(),
+                                   arrivals.data_ptr(), timeout_us=1_000_000)
+    for _ in range(3):
+        native.linear_bias_act_allgather(x, w.t(), y, [peer_y.data_ptr()], bias=None,
+                                         epilogue=native.KF_EPI_NONE, sync=sync)
+    torch.cuda.synchronize(device)
+    assert counter.item() == 3 and arrivals.item() == 0 and peer_sig.tolist() == [3, 0]
+    assert native.device_status(device.index) == 0
+    assert torch.equal(y, peer_y) and torch.equal(y, gemv(x, w))
+    counter.fill_(100)  # rank 1 stopped at epoch 100: epoch 101 times out
+    sync = native.peer_sync_struct(local.data_ptr(), [peer_sig.data_ptr()], 0, 2, counter.data_ptr(),
+                                   arrivals.data_ptr(), timeout_us=20_000)
+    native.linear_bias_act_allgather(x, w.t(), y, [peer_y.data_ptr()], bias=None, epilogue=native.KF_EPI_NONE,
+                                     sync=sync)
+    torch.cuda.synchronize(device)
+    value = native.device_status(device.index)
+    assert value & 0xFF == native.KF_ERR_TIMEOUT and value >> 8 == 7
+    assert counter.item() == 101 and arrivals.item() == 0
+    assert torch.equal(y, gemv(x, w))  # still usable
