@@ -2,10 +2,10 @@
 // shared by the stand-alone barrier kernel (peer_sync.cu) and the tile GEMV,
 // whose last CTA runs it in-kernel (gemv_mma.cu).
 //
-// Lane t < n_peers owns peer t. It fences at system scope (cumulative over
-// this GPU's stores into the peers' buffers that happen before it), writes
-// `epoch` into this rank's slot of that peer's signal array with a release
-// store at system scope, then polls this rank's own slot for that peer with
+// Lane t < n_peers owns peer t. It writes `epoch` into this rank's slot of
+// that peer's signal array with a release store at system scope (cumulative
+// over this GPU's stores into the peers' buffers that happen before it),
+// then polls this rank's own slot for that peer with
 // acquire loads at system scope until it reads `epoch` or a later one. The
 // wait is bounded by %globaltimer: on timeout it records KF_ERR_TIMEOUT |
 // SITE_PEER_BARRIER << 8 in the device status word and returns.
@@ -43,10 +43,12 @@ __device__ __forceinline__ bool epoch_reached(uint32_t v, uint32_t epoch) {
 int fill_peer_signals(uint32_t* local, uint32_t* const* peers, int rank, int world, int timeout_us,
                       PeerSignals* out);
 
-// Lane t < s.n_peers signals peer t and waits for it (see above).
+// Lane t < s.n_peers signals peer t and waits for it (see above). The
+// release store at system scope is the fence: it orders every write this
+// lane has observed (this GPU's stores into the peers' buffers, through the
+// kernel boundary or the arrival atomic) before the signal.
 __device__ __forceinline__ void peer_signal_and_wait(const PeerSignals& s, uint32_t epoch, int t, int* status) {
   if (t >= s.n_peers) return;
-  __threadfence_system();
   st_release_sys(s.peers[t] + s.rank, epoch);
   const uint32_t* mine = s.local + s.peer_rank[t];
   if (epoch_reached(ld_acquire_sys(mine), epoch)) return;
