@@ -224,7 +224,7 @@ def default_tcgen05_config(
         block_n = widest
     atom = 128 // elem  # elements per 128-byte swizzle row
     stage_elem = 2 * elem if elem == 4 else elem  # TF32 stages carry both split parts
-    block_k = 2 * atom if (cg == 2 and k >= 512 and elem != 4) else atom
+    block_k = 2 * atom if (cg == 2 and k >= 512) else atom
     per_stage = (TC_BLOCK_M + block_n // cg) * block_k * stage_elem
     stages = max(2, min(12, (SM100_SMEM_PER_BLOCK - 1024 - 256) // per_stage))
     tiles_m = -(-m_k // (TC_BLOCK_M * cg))
