@@ -109,12 +109,15 @@ __device__ __forceinline__ uint4 load_x(const uint4* p) {
   return v;
 }
 
-template <typename T, int NT, int S, int U, int EPI>
+// SPLIT: compiled for a K split over a cluster (p.ks > 1); without it the
+// split's index arithmetic folds away (it cost spills at 48 registers, and
+// 1.6 us at N = 11008).
+template <typename T, int NT, int S, int U, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams p) {
   __shared__ float4 part[S > 1 ? S - 1 : 1][32][NT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int ks = p.ks;
+  const int ks = SPLIT ? p.ks : 1;
   const int part_rank = static_cast<int>(blockIdx.x) % ks;  // == the rank in the cluster
   const int n0 = static_cast<int>(blockIdx.x) / ks * 16;
   const int nvec = p.K / 8;  // 16-byte vectors per row (K % 8 == 0)
@@ -207,7 +210,7 @@ __global__ void __launch_bounds__(32 * S, 5) gemv_mma_kernel(const GemvMmaParams
         }
     }
   }
-  if (ks > 1) {
+  if constexpr (SPLIT) {
     // Across the cluster: every CTA's warp 0 leaves its sum in its own shared
     // memory; the leader adds the others' in rank order (deterministic) and
     // runs the epilogue. No thread exits before both cluster barriers.
@@ -309,16 +312,20 @@ int launch_shape(const GemvMmaParams& p, cudaStream_t stream) {
     lc.attrs = attr;
     lc.numAttrs = 1;
   }
-  const cudaError_t err = cudaLaunchKernelEx(&lc, gemv_mma_kernel<T, NT, S, U, EPI>, p);
+  const cudaError_t err = p.ks > 1 ? cudaLaunchKernelEx(&lc, gemv_mma_kernel<T, NT, S, U, EPI, true>, p)
+                                   : cudaLaunchKernelEx(&lc, gemv_mma_kernel<T, NT, S, U, EPI, false>, p);
   if (err != cudaSuccess) return cuda_error(err, "launch(gemv mma)");
   return KF_OK;
 }
 
-// CTAs per weight tile: the fewest (1, 2, 4, 8) that give at least four CTAs
-// per SM -- a tile's CTA streams its weights for about the whole kernel, so
-// fewer CTAs than that leave HBM idle (a 2-way column shard of 11008 rows:
-// 344 tiles measured 16.6 us, as long as the whole GEMV).
-int default_tile_split(long long tiles) {
+// CTAs per weight tile: the fewest (1, 2, 4) that give at least two CTAs per
+// SM up to 8 rows of x, four beyond (a tile's CTA streams its weights for
+// about the whole kernel, so too few CTAs leave HBM idle; more x rows make
+// each CTA slower and want more of them). Measured on B200 at K = 4096
+// (graph-timed; M = 1 / M = 16, us): N = 5504 split 1 9.9 / 14.0, split 2
+// 10.9 / 13.3; N = 2752 split 2 8.1 / 10.3, split 4 7.6 / 10.1; N = 1376
+// split 4 6.1 / 7.8, split 8 6.3 / 8.4.
+int default_tile_split(long long tiles, int m) {
   static thread_local int cached_device = -1, sms = 148;
   int device = 0;
   if (cudaGetDevice(&device) == cudaSuccess && device != cached_device) {
@@ -326,8 +333,9 @@ int default_tile_split(long long tiles) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && v > 0) sms = v;
     cached_device = device;
   }
+  const long long target = static_cast<long long>(m <= 8 ? 2 : 4) * sms;
   int ks = 1;
-  while (ks < 8 && tiles * ks < 4LL * sms) ks *= 2;
+  while (ks < 4 && tiles * ks < target) ks *= 2;
   return ks;
 }
 
@@ -414,7 +422,7 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
   p.bias = bias;
-  p.ks = cfg.cluster_m > 0 ? cfg.cluster_m : default_tile_split((N + 15) / 16);
+  p.ks = cfg.cluster_m > 0 ? cfg.cluster_m : default_tile_split((N + 15) / 16, static_cast<int>(M));
   if (p.ks != 1 && p.ks != 2 && p.ks != 4 && p.ks != 8)
     return set_error(KF_ERR_INVALID_CONFIG, "tile GEMV: CLUSTER_M (CTAs per weight tile) must be 1, 2, 4 or 8");
   p.n_peers = n_peers;

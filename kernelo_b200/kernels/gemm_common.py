@@ -46,13 +46,15 @@ def tile_rows_default(m: int) -> tuple[int, int]:
     return {1: (8, 1), 2: (6, 4), 4: (4, 4)}[tile_rows_groups(m)]
 
 
-def tile_rows_split(n: int, sm_count: int = 148) -> int:
+def tile_rows_split(n: int, m: int = 1, sm_count: int = 148) -> int:
     """CTAs per 16-row weight tile the tile GEMV uses by default (mirrors
-    default_tile_split in gemv_mma.cu): the fewest of 1, 2, 4, 8 that give
-    at least four CTAs per SM, the tile's K split over a thread-block cluster."""
+    default_tile_split in gemv_mma.cu): the fewest of 1, 2, 4 that give at
+    least two CTAs per SM up to 8 rows of x, four beyond, the tile's K split
+    over a thread-block cluster."""
     tiles = -(-n // 16)
+    target = (2 if m <= 8 else 4) * sm_count
     ks = 1
-    while ks < 8 and tiles * ks < 4 * sm_count:
+    while ks < 4 and tiles * ks < target:
         ks *= 2
     return ks
 

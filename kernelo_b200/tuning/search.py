@@ -304,8 +304,8 @@ class _Sm100GemmSpace(SearchSpace):
         """CTAs with work: tiles, times two for SM-pair tiles."""
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             # a cluster of CTAs per 16 weight rows (CLUSTER_M, else the library's split)
-            n = self.dims(problem)[1]
-            return ceil_div(n, 16) * (config.get("CLUSTER_M", 0) or gc.tile_rows_split(n))
+            m, n, _ = self.dims(problem)
+            return ceil_div(n, 16) * (config.get("CLUSTER_M", 0) or gc.tile_rows_split(n, m))
         if config["KERNEL"] == gc.KERNEL_COLUMNS:
             _, n, k = self.dims(problem)
             return gc.columns_programs(n, k, problem.dtype)

@@ -518,11 +518,13 @@ def test_gemv_tile_rows_split_over_a_cluster(split, m, n, k, device):
 
 
 def test_gemv_tile_rows_default_split_fills_the_gpu(device):
-    """Few tiles (a column shard) take a K split by default: the result matches
-    the unsplit kernel's within the gate and the launch is at least 4 CTAs per SM."""
+    """Few tiles (a column shard) take a K split by default (at least two CTAs
+    per SM up to 8 rows of x, four beyond, at most 4 CTAs per tile), and the
+    result passes the gate."""
     from kernelo_b200.kernels import gemm_common as gc
 
-    assert gc.tile_rows_split(11008) == 1 and gc.tile_rows_split(5504) == 2 and gc.tile_rows_split(1376) == 8
+    assert gc.tile_rows_split(11008) == 1 and gc.tile_rows_split(5504) == 1 and gc.tile_rows_split(5504, 16) == 2
+    assert gc.tile_rows_split(2752) == 2 and gc.tile_rows_split(1376) == 4 and gc.tile_rows_split(1376, 16) == 4
     gen = torch.Generator().manual_seed(3)
     x = torch.randn(4, 4096, generator=gen).half().to(device)
     w = (torch.randn(2752, 4096, generator=gen) * 4096 ** -0.5).half().to(device)
