@@ -143,8 +143,9 @@ typedef struct kf_rows_config {
  * two per SM) of row groups; each group keeps its next rows in flight as bulk
  * copies into shared-memory slots while it reduces and writes earlier ones.
  * WARP: persistent CTAs of 8 warps, a warp per row, the next row loaded into
- * registers while the current one is reduced; rows of up to 2 KB that start on
- * the 16-byte grid (the default for such softmax rows). */
+ * registers while the current one is reduced; rows of up to 4 KB that start on
+ * the 16-byte grid (the default for such softmax rows up to 2 KB, RMSNorm rows
+ * up to 4 KB). */
 enum kf_rows_kernel { KF_ROWS_AUTO = 0, KF_ROWS_REGISTER = 1, KF_ROWS_STREAM = 2, KF_ROWS_WARP = 3 };
 
 /* ---- library information -------------------------------------------------- */

@@ -189,7 +189,11 @@ int launch_rows(const RowsArgs& args, const kf_rows_config& cfg, const DeviceInf
 bool rows_stream_supported(const RowsArgs& args, int max_smem_optin, std::string* why);
 // Warp-per-row persistent kernel for narrow rows (rows_warp.cu): rows of whole
 // 16-byte vectors, up to 128 of them, starting on the 16-byte grid.
+// Widest rows (16-byte vectors) of the warp-per-row kernel: its default for
+// softmax (2 KB) and for RMSNorm (4 KB), and what it takes at all (4 KB).
 constexpr long long ROWS_WARP_MAX_VECTORS = 128;
+constexpr long long ROWS_WARP_RMSNORM_MAX_VECTORS = 256;
+constexpr long long ROWS_WARP_EXPLICIT_MAX_VECTORS = 256;
 bool rows_warp_supported(const RowsArgs& args, std::string* why);
 int launch_rows_warp(const RowsArgs& args, const DeviceInfo& dev, cudaStream_t stream);
 int stream_default_warps(int64_t cols, int elem);

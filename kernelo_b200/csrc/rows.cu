@@ -432,8 +432,12 @@ kf_rows_config resolve_rows_config(const RowsArgs& a, const kf_rows_config* user
       // one CTA per row leaves few loads in flight. Measured on B200
       // (graph-timed, inputs beyond L2): softmax 32768 x 1000 fp16 1.05 of
       // the copy bandwidth against 0.81 streamed; RMSNorm 16384 x 1024 fp16
-      // 1.09 against 0.87 in registers.
-      if (nvec_row <= ROWS_WARP_MAX_VECTORS && a.rows >= 2LL * dev.sm_count && rows_warp_supported(a, nullptr))
+      // 1.09 against 0.87 in registers. RMSNorm keeps the gain up to 4 KB
+      // rows (16384 x 2048 fp16 1.09 against 0.96; 16384 x 1024 fp32 1.20
+      // against 0.91); softmax does not (32768 x 2048 fp16 0.85 against 0.96
+      // in registers), its exponentials being the heavier per-lane work.
+      const long long warp_max = a.op == 1 ? ROWS_WARP_RMSNORM_MAX_VECTORS : ROWS_WARP_MAX_VECTORS;
+      if (nvec_row <= warp_max && a.rows >= 2LL * dev.sm_count && rows_warp_supported(a, nullptr))
         c.kernel = KF_ROWS_WARP;
       // Two slots per row group leave room for two CTAs per SM, which beats
       // deeper slots on narrow rows (25.8 against 27.6 us at 1000 columns).

@@ -1,4 +1,5 @@
-// Row softmax and RMSNorm for narrow rows (up to 2 KB), one warp per row.
+// Row softmax and RMSNorm for narrow rows (up to 4 KB; the library's default
+// up to 2 KB for softmax, 4 KB for RMSNorm), one warp per row.
 //
 // At 1000 fp16 columns a row is 2 KB: 125 vectors of 16 bytes, four per lane.
 // The streaming kernel spends most of its issue slots on per-row machinery
@@ -123,7 +124,8 @@ int launch_nv(const WarpRowsParams& p, const DeviceInfo& dev, cudaStream_t strea
   const int nv = (p.nvec + 31) / 32;
   void* fn = nv <= 1   ? reinterpret_cast<void*>(&rows_warp_kernel<T, 1, OP>)
              : nv <= 2 ? reinterpret_cast<void*>(&rows_warp_kernel<T, 2, OP>)
-                       : reinterpret_cast<void*>(&rows_warp_kernel<T, 4, OP>);
+             : nv <= 4 ? reinterpret_cast<void*>(&rows_warp_kernel<T, 4, OP>)
+                       : reinterpret_cast<void*>(&rows_warp_kernel<T, 8, OP>);
   static thread_local std::pair<void*, int> cached{nullptr, 0};
   int per_sm = 0;
   if (cached.first == fn) {
@@ -153,7 +155,8 @@ bool rows_warp_supported(const RowsArgs& a, std::string* why) {
     return false;
   };
   if ((a.cols * elem) % 16 != 0) return no("the warp-per-row kernel needs rows of whole 16-byte vectors");
-  if ((a.cols * elem) / 16 > ROWS_WARP_MAX_VECTORS) return no("the warp-per-row kernel takes rows up to 2 KB");
+  if ((a.cols * elem) / 16 > ROWS_WARP_EXPLICIT_MAX_VECTORS)
+    return no("the warp-per-row kernel takes rows up to 4 KB");
   if ((reinterpret_cast<uintptr_t>(a.x) & 15u) != 0 || (reinterpret_cast<uintptr_t>(a.y) & 15u) != 0 ||
       (a.sx * elem) % 16 != 0 || (a.sy * elem) % 16 != 0)
     return no("the warp-per-row kernel needs rows that start on the 16-byte grid");

@@ -2,8 +2,8 @@
 
 ``default_rows_config`` mirrors ``resolve_rows_config`` in ``csrc/rows.cu``:
 
-* a softmax or RMSNorm over many rows (at least two per SM) of up to 2 KB that
-  hold whole 16-byte vectors and start on the 16-byte grid goes to the
+* a softmax (RMSNorm) over many rows (at least two per SM) of up to 2 KB (4 KB)
+  that hold whole 16-byte vectors and start on the 16-byte grid goes to the
   warp-per-row kernel
   (``ROW_KERNEL=3``, ``csrc/rows_warp.cu``): persistent CTAs of 8 warps, a warp
   per row, the next row loaded into registers while the current one is reduced;
@@ -35,8 +35,10 @@ VECTORS_PER_CTA = 4096
 ROW_KERNEL_REGISTER = 1
 ROW_KERNEL_STREAM = 2
 ROW_KERNEL_WARP = 3
-#: Widest row of the warp-per-row kernel, in 16-byte vectors (mirrors kf_internal.h).
+#: Widest rows of the warp-per-row kernel, in 16-byte vectors (mirrors kf_internal.h):
+#: the softmax default (2 KB), the RMSNorm default and the kernel's limit (4 KB).
 WARP_MAX_VECTORS = 128
+WARP_RMSNORM_MAX_VECTORS = 256
 #: Warps of one streaming CTA, shared by its row groups.
 STREAM_CONSUMER_WARPS = 16
 #: Shared memory of one sm_100 CTA, and what the streaming kernel keeps besides its slots.
@@ -72,13 +74,14 @@ def same_phase(x: torch.Tensor | None, cols: int) -> bool:
     return x.data_ptr() % 16 == 0 and (x.stride(0) * size) % 16 == (cols * size) % 16
 
 
-def warp_fits(cols: int, dtype: torch.dtype, x: torch.Tensor | None = None) -> bool:
-    """Rows the warp-per-row kernel takes (mirrors rows_warp_supported): whole
-    16-byte vectors, at most 2 KB, input rows on the 16-byte grid (the output
-    is a fresh contiguous tensor, on the grid whenever the rows are whole
-    vectors)."""
+def warp_fits(cols: int, dtype: torch.dtype, x: torch.Tensor | None = None, *,
+              max_vectors: int = WARP_MAX_VECTORS) -> bool:
+    """Rows the warp-per-row kernel takes by default (mirrors rows_warp_supported
+    and resolve_rows_config): whole 16-byte vectors, at most ``max_vectors``
+    of them, input rows on the 16-byte grid (the output is a fresh contiguous
+    tensor, on the grid whenever the rows are whole vectors)."""
     size = itemsize(dtype)
-    if (cols * size) % 16 != 0 or cols * size // 16 > WARP_MAX_VECTORS:
+    if (cols * size) % 16 != 0 or cols * size // 16 > max_vectors:
         return False
     return x is None or (x.data_ptr() % 16 == 0 and (x.stride(0) * size) % 16 == 0)
 
@@ -97,15 +100,16 @@ def default_rows_config(
     x: torch.Tensor | None = None,
     sm_count: int = 148,
 ) -> KernelConfig:
-    """The library's choice (mirrors resolve_rows_config in rows.cu): rows up
-    to 2 KB on the 16-byte grid go a warp per row (either operation); other
+    """The library's choice (mirrors resolve_rows_config in rows.cu): rows on
+    the 16-byte grid go a warp per row up to 2 KB (softmax) or 4 KB (RMSNorm); other
     softmax rows up to 2 KB stream, rows up to 32 KB sit in registers at about
     eight 16-byte vectors per thread, wider rows stream again (when there are
     enough rows for every SM and the kernel takes the layout); RMSNorm uses the
     register kernel at about four vectors per thread."""
     block = next_power_of_2(max(cols, 1))
     nvec = ceil_div(cols * itemsize(dtype), 16)
-    if rows is not None and rows >= 2 * sm_count and warp_fits(cols, dtype, x):
+    warp_max = WARP_RMSNORM_MAX_VECTORS if operation == "rmsnorm" else WARP_MAX_VECTORS
+    if rows is not None and rows >= 2 * sm_count and warp_fits(cols, dtype, x, max_vectors=warp_max):
         return KernelConfig(operation, BLOCK_SIZE=block, ROW_KERNEL=ROW_KERNEL_WARP, num_warps=1)
     if operation == "softmax":
         narrow = nvec <= SOFTMAX_STREAM_MAX_VECTORS

@@ -473,7 +473,7 @@ class _RowReductionSpace(SearchSpace):
     """Row kernels. The register kernel (``ROW_KERNEL=1``): threads per CTA, rows
     per CTA, CTAs per row. The persistent streaming kernel (``ROW_KERNEL=2``):
     warps per row group, one CTA per SM with 16 consumer warps. The
-    warp-per-row kernel (``ROW_KERNEL=3``): no fields, rows up to 2 KB."""
+    warp-per-row kernel (``ROW_KERNEL=3``): no fields, rows up to 4 KB."""
 
     NUM_WARPS = (1, 2, 4, 8, 16, 32)
     ROWS_PER_PROGRAM = (1, 2, 4)
@@ -509,8 +509,8 @@ class _RowReductionSpace(SearchSpace):
                 CLUSTER=cluster,
             )
 
-    #: Widest row of the warp-per-row kernel, in 16-byte vectors.
-    WARP_MAX_VECTORS = 128
+    #: Widest row of the warp-per-row kernel, in 16-byte vectors (4 KB).
+    WARP_MAX_VECTORS = 256
 
     @staticmethod
     def is_stream(config: KernelConfig) -> bool:
@@ -572,7 +572,7 @@ class _RowReductionSpace(SearchSpace):
             if (cols * problem.itemsize) % 16 != 0:
                 return "warp-per-row kernel: rows must hold whole 16-byte vectors"
             if self.vectors_per_row(problem) > self.WARP_MAX_VECTORS:
-                return f"warp-per-row kernel: a row of {cols * problem.itemsize} bytes exceeds 2 KB"
+                return f"warp-per-row kernel: a row of {cols * problem.itemsize} bytes exceeds 4 KB"
             return None
         cluster = config.get("CLUSTER", 1)
         if cluster > caps.max_cluster_size:

@@ -266,6 +266,9 @@ def test_softmax_default_kernel_by_row_width(device):
     assert default_rows_config("softmax", 32000, torch.float32, rows=32768)["ROW_KERNEL"] == 2
     assert default_rows_config("rmsnorm", 4096, torch.float16, rows=16384, x=x)["ROW_KERNEL"] == 1
     assert default_rows_config("rmsnorm", 1024, torch.float16, rows=16384)["ROW_KERNEL"] == 3
+    assert default_rows_config("rmsnorm", 2048, torch.float16, rows=16384)["ROW_KERNEL"] == 3
+    assert default_rows_config("rmsnorm", 4096, torch.float16, rows=16384)["ROW_KERNEL"] == 1
+    assert default_rows_config("softmax", 2048, torch.float16, rows=16384)["ROW_KERNEL"] == 1
     gamma = (rand(1, 1000, torch.float32, device, seed=1)[0] * 0.1 + 1).half()
     gate(ref.rmsnorm_ref(host(narrow), host(gamma), 1e-6), rmsnorm(narrow, gamma, eps=1e-6), torch.float16)
 
@@ -287,15 +290,15 @@ def warp_cfg(op, cols):
     return KernelConfig(op, BLOCK_SIZE=max(1, 1 << (cols - 1).bit_length()), ROW_KERNEL=3, num_warps=1)
 
 
-@pytest.mark.parametrize("cols", [8, 16, 64, 248, 256, 264, 512, 1000, 1024])
+@pytest.mark.parametrize("cols", [8, 16, 64, 248, 256, 264, 512, 1000, 1024, 1536, 2048])
 @pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: str(d)[6:])
 @pytest.mark.parametrize("rows", [1, 7, 301, 5000])
 def test_warp_kernel_widths(cols, dtype, rows, device):
     """One to four vectors per lane (the three instantiations), rows fewer
     than one CTA's 8 warps, more rows than resident warps (each warp loops),
     padding lanes of a partial last vector group; both operations."""
-    if cols * dtype.itemsize > 2048:
-        pytest.skip("rows beyond 2 KB are not the warp kernel's")
+    if cols * dtype.itemsize > 4096:
+        pytest.skip("rows beyond 4 KB are not the warp kernel's")
     x = rand(rows, cols, dtype, device, scale=4.0, seed=cols)
     y = torch.full_like(x, float("nan"))
     from kernelo_b200.runtime import native
@@ -335,9 +338,9 @@ def test_warp_kernel_refuses_layouts_it_cannot_take(device):
     x = rand(400, 1001, torch.float16, device)
     with pytest.raises(OutOfResources, match="whole 16-byte vectors"):
         softmax(x, config=warp_cfg("softmax", 1001))
-    wide = rand(400, 2048, torch.float16, device)
-    with pytest.raises(OutOfResources, match="2 KB"):
-        softmax(wide, config=warp_cfg("softmax", 2048))
+    wide = rand(400, 4096, torch.float16, device)
+    with pytest.raises(OutOfResources, match="4 KB"):
+        softmax(wide, config=warp_cfg("softmax", 4096))
     odd = rand(400, 1032, torch.float16, device)[:, 4:1028]  # start 8 bytes off the grid
     with pytest.raises(OutOfResources, match="16-byte grid"):
         softmax(odd, config=warp_cfg("softmax", 1024))

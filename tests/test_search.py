@@ -196,7 +196,7 @@ def test_row_space_shape_and_rules(b200_caps):
     assert any(c["ROW_KERNEL"] == 2 for c in narrow_cands)
     # 8 KB rows exceed the warp kernel; odd rows of fp16 do not hold whole vectors
     warp = KernelConfig("softmax", BLOCK_SIZE=4096, ROW_KERNEL=3, num_warps=1)
-    assert "exceeds 2 KB" in SoftmaxSearchSpace().reject_reason(warp, soft, b200_caps)
+    assert "exceeds 4 KB" in SoftmaxSearchSpace().reject_reason(warp, soft, b200_caps)
     odd = Problem.create("softmax", "fp16", rows=32768, cols=999)
     assert "whole 16-byte vectors" in SoftmaxSearchSpace().reject_reason(warp.replace(BLOCK_SIZE=1024), odd,
                                                                           b200_caps)
