@@ -562,13 +562,40 @@ def secondary_lines(pk: dict, flush, *, reference_kernels: bool = True) -> list[
     wbytes = N * K * 2
     sets = rotation_sets(wbytes, dev)
     ws = [(torch.randn(N, K, device=dev, generator=g) * K ** -0.5).half() for _ in range(sets)]
+    def with_overlap(entry, work, make_calls):
+        """The same launches with overlap=True (weights are not written by the
+        kernel before each call): programmatic dependent launch lets each GEMV
+        stream its weight while its predecessor's last tiles finish, as in a
+        decode loop of back-to-back layers."""
+        try:
+            ms = graph_time_per_launch(make_calls())
+            rate = work / ms / 1e6
+            entry["with_overlap"] = {"value": round(rate, 1), "frac": round(rate / pk["hbm_gbs"], 3),
+                                     "us_per_launch": round(ms * 1e3, 2)}
+        except Exception as exc:  # noqa: BLE001 - a variant never fails the bench
+            entry["with_overlap"] = {"unavailable": f"{type(exc).__name__}: {str(exc)[:160]}"}
+
     for m in (1, 4, 16):
         xx = torch.randn(m, K, device=dev, generator=g).half()
         calls = [lambda w=w: gemv(xx, w) for w in ws] * 4
-        line(f"gemv M={m} N={N} K={K} fp16", gemv_bytes(m, N, K, 2), calls, sets,
-             cublas=lambda: [lambda w=w: torch.mm(xx, w.t()) for w in ws] * 4,
-             reference=(lambda: [lambda w=w: ref.mm.matmul_triton_autotune(xx, w.t()) for w in ws] * 4)
-             if ok else None)
+        entry = line(f"gemv M={m} N={N} K={K} fp16", gemv_bytes(m, N, K, 2), calls, sets,
+                     cublas=lambda: [lambda w=w: torch.mm(xx, w.t()) for w in ws] * 4,
+                     reference=(lambda: [lambda w=w: ref.mm.matmul_triton_autotune(xx, w.t()) for w in ws] * 4)
+                     if ok else None)
+        with_overlap(entry, gemv_bytes(m, N, K, 2), lambda: [lambda w=w: gemv(xx, w, overlap=True) for w in ws] * 4)
+    del ws
+    # Not a BASELINE config: the MLP down-projection's decode shape (the
+    # transpose of config 2's weight, long K), where the library takes the
+    # streamed tile kernel beyond 8 rows of x.
+    n2, k2 = K, N
+    sets = rotation_sets(n2 * k2 * 2, dev)
+    ws = [(torch.randn(n2, k2, device=dev, generator=g) * k2 ** -0.5).half() for _ in range(sets)]
+    for m in (1, 16):
+        xx = torch.randn(m, k2, device=dev, generator=g).half()
+        entry = line(f"gemv M={m} N={n2} K={k2} fp16 (down-projection shape)", gemv_bytes(m, n2, k2, 2),
+                     [lambda w=w: gemv(xx, w) for w in ws] * 4, sets,
+                     cublas=lambda: [lambda w=w: torch.mm(xx, w.t()) for w in ws] * 4)
+        with_overlap(entry, gemv_bytes(m, n2, k2, 2), lambda: [lambda w=w: gemv(xx, w, overlap=True) for w in ws] * 4)
     del ws
     return out
 

@@ -82,13 +82,20 @@ enum kf_gemm_kernel {
                            per lane in flight. kf_gemv, and kf_gemm /
                            kf_linear_bias_act (epilogue included); AUTO picks
                            it for such shapes                               */
-  KF_GEMM_COLUMNS = 5    /* a lane per 16-byte vector of an N-contiguous B's
+  KF_GEMM_COLUMNS = 5,   /* a lane per 16-byte vector of an N-contiguous B's
                            columns (the row-major (K, N) operand), M <= 8,
                            any dtype; K split over CTAs, the last arrival per
                            column strip adds the partials in a fixed order
                            (workspace from kf_gemm_workspace_bytes; without
                            it, one CTA per strip). AUTO picks it for such
                            shapes; epilogue included                        */
+  KF_GEMM_TILE_STREAM = 6 /* the 16-row tile GEMV with the weight streamed
+                           through shared memory: one persistent CTA per SM
+                           keeps a ring of bulk copies (16 rows x 512
+                           elements per stage) in flight; M <= 16, the
+                           TILE_ROWS operand rules, no workspace; stages =
+                           ring depth (2..12), num_ctas = grid size. kf_gemv
+                           and kf_gemm / kf_linear_bias_act without peers   */
 };
 
 /* Tunable GEMM parameters. Replaces KernelConfig's BLOCK_M/BLOCK_N/BLOCK_K/
@@ -117,7 +124,14 @@ typedef struct kf_gemm_config {
   int32_t epi_store; /* all-gather epilogue (kf_linear_bias_act_allgather): 0 = library
                         choice, 1 = stores from the threads (rows staged through
                         shared memory), 2 = TMA tensor stores of the staged blocks    */
-  int32_t reserved[4];
+  int32_t overlap;   /* decode GEMV kernels (TILE_ROWS, TILE_STREAM) without peers:
+                        1 = the weight and bias are not written by the kernel that
+                        runs before this call on the stream, so this launch may
+                        start as that kernel's CTAs finish (programmatic dependent
+                        launch): it begins streaming the weight at once and waits
+                        for the earlier kernel to complete before it reads x or
+                        writes y. 0 = ordinary stream order. Other kernels ignore it */
+  int32_t reserved[3];
 } kf_gemm_config;
 
 /* Row-kernel parameters (softmax / RMSNorm). Replaces BLOCK_SIZE /

@@ -348,6 +348,40 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
   // peer stores included (the decode-shape fused linear and its all-gather).
   // It reads the weight at 0.8 of the copy bandwidth against ~0.55 for
   // 128-row TMA tiles.
+  if (user != nullptr && user->kernel == KF_GEMM_TILE_STREAM) {
+    if (g.n_peers != 0 || g.sync != nullptr)
+      return set_error(KF_ERR_UNSUPPORTED, "streamed tile GEMV: no peer stores (use the tile kernel)");
+    std::string why;
+    if (!gemv_stream_supported(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_n, g.sb_k, g.M, g.N, g.K, &why))
+      return set_error(g.M > GEMV_STREAM_MAX_M ? KF_ERR_UNSUPPORTED : KF_ERR_UNALIGNED, "streamed tile GEMV: " + why);
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc != KF_OK) return rc;
+    DeviceInfo* dev = nullptr;
+    rc = device_info(device, &dev);
+    if (rc != KF_OK) return rc;
+    return launch_gemv_stream(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K, *user, *dev,
+                              static_cast<cudaStream_t>(stream), g.epilogue, g.bias);
+  }
+  // The library's decode-shape choice between the two 16-row tile kernels.
+  if ((user == nullptr || user->kernel == KF_GEMM_AUTO) && g.n_peers == 0 && g.sync == nullptr &&
+      g.M <= GEMV_STREAM_MAX_M &&
+      gemv_stream_supported(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_n, g.sb_k, g.M, g.N, g.K, nullptr)) {
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc != KF_OK) return rc;
+    DeviceInfo* dev = nullptr;
+    rc = device_info(device, &dev);
+    if (rc != KF_OK) return rc;
+    const int overlap = user != nullptr ? user->overlap : 0;
+    if (gemv_stream_preferred(g.M, g.N, g.K, dev->sm_count, overlap != 0)) {
+      kf_gemm_config chosen = zero_config();
+      chosen.kernel = KF_GEMM_TILE_STREAM;
+      chosen.overlap = overlap;
+      return launch_gemv_stream(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K, chosen,
+                                *dev, static_cast<cudaStream_t>(stream), g.epilogue, g.bias);
+    }
+  }
   const bool tile_auto = (user == nullptr || user->kernel == KF_GEMM_AUTO) && g.M <= GEMV_MMA_MAX_M &&
                          gemv_mma_supported(g.dtype, g.a, g.sa_m, g.sa_k, g.b, g.sb_n, g.sb_k, g.M, g.N,
                                             g.K, nullptr);
@@ -367,8 +401,10 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
       if (rc != KF_OK) return rc;
       status = dev->status;
     }
+    kf_gemm_config chosen = zero_config();
+    if (tile_auto && user != nullptr) chosen.overlap = user->overlap;  // not a tile-shape field
     const int rc = launch_gemv_mma(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K,
-                                   tile_auto ? zero_config() : *user, static_cast<cudaStream_t>(stream),
+                                   tile_auto ? chosen : *user, static_cast<cudaStream_t>(stream),
                                    g.epilogue, g.bias, g.peers, g.n_peers, g.sync, status);
     if (rc == KF_OK && g.sync != nullptr) g.sync_done = true;
     return rc;
@@ -656,9 +692,37 @@ int32_t kf_gemv(int32_t dtype, const void* x, int64_t sx_m, int64_t sx_k, const 
   // tiles streamed by warps straight into mma.sync fragments (measured on
   // B200 at 11008 x 4096: 0.80 of the copy bandwidth at M = 1 and 4, 0.71 at
   // M = 16, against 0.53 for 128-row TMA tiles).
+  if (c.kernel == KF_GEMM_AUTO && M >= 1 && M <= GEMV_STREAM_MAX_M && N >= 1 && x != nullptr &&
+      w != nullptr && y != nullptr && gemv_stream_supported(dtype, x, sx_m, sx_k, w, sw_n, sw_k, M, N, K, nullptr)) {
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc != KF_OK) return rc;
+    DeviceInfo* dev = nullptr;
+    rc = device_info(device, &dev);
+    if (rc != KF_OK) return rc;
+    if (gemv_stream_preferred(M, N, K, dev->sm_count, c.overlap != 0)) c.kernel = KF_GEMM_TILE_STREAM;
+  }
   if (c.kernel == KF_GEMM_AUTO && M >= 1 && M <= GEMV_MMA_MAX_M && x != nullptr && w != nullptr &&
       y != nullptr && gemv_mma_supported(dtype, x, sx_m, sx_k, w, sw_n, sw_k, M, N, K, nullptr))
     c.kernel = KF_GEMM_TILE_ROWS;
+  if (c.kernel == KF_GEMM_TILE_STREAM) {
+    if (!valid_dtype(dtype)) return set_error(KF_ERR_INVALID_ARGUMENT, "unknown dtype code");
+    if (M < 0 || N < 0 || K < 0) return set_error(KF_ERR_INVALID_ARGUMENT, "negative size");
+    if (M == 0 || N == 0) return KF_OK;
+    if (x == nullptr || w == nullptr || y == nullptr)
+      return set_error(KF_ERR_INVALID_ARGUMENT, "null pointer");
+    std::string why;
+    if (!gemv_stream_supported(dtype, x, sx_m, sx_k, w, sw_n, sw_k, M, N, K, &why))
+      return set_error(M > GEMV_STREAM_MAX_M ? KF_ERR_UNSUPPORTED : KF_ERR_UNALIGNED, "streamed tile GEMV: " + why);
+    int device = 0;
+    int rc = current_device(&device);
+    if (rc != KF_OK) return rc;
+    DeviceInfo* dev = nullptr;
+    rc = device_info(device, &dev);
+    if (rc != KF_OK) return rc;
+    return launch_gemv_stream(dtype, x, sx_m, w, sw_n, y, sy_m, sy_n, M, N, K, c, *dev,
+                              static_cast<cudaStream_t>(stream));
+  }
   if (c.kernel == KF_GEMM_TILE_ROWS) {
     if (!valid_dtype(dtype)) return set_error(KF_ERR_INVALID_ARGUMENT, "unknown dtype code");
     if (M < 0 || N < 0 || K < 0) return set_error(KF_ERR_INVALID_ARGUMENT, "negative size");
@@ -733,6 +797,7 @@ int64_t kf_gemm_workspace_bytes_for(int32_t device, int32_t dtype, const void* a
   g.sc_m = c != nullptr ? sc_m : N;
   g.sc_n = c != nullptr ? sc_n : 1;
   const int kernel = cfg ? cfg->kernel : KF_GEMM_AUTO;
+  if (kernel == KF_GEMM_TILE_STREAM) return 0;
   if ((kernel == KF_GEMM_AUTO || kernel == KF_GEMM_COLUMNS) &&
       gemv_cols_supported(dtype, g.a, g.b, sb_k, sb_n, M, N, K, nullptr))
     return gemv_cols_workspace_bytes(dtype, M, N, K, dev->sm_count);
@@ -747,7 +812,7 @@ int64_t kf_gemv_workspace_bytes(int32_t device, int32_t dtype, int64_t sx_m, int
   kf_gemm_config c = cfg ? *cfg : zero_config();
   // The warp-per-row kernel needs none; AUTO reports the stream-K size, since
   // a weight pointer off the 16-byte grid sends the call there.
-  if (c.kernel == KF_GEMM_WARP_ROWS || c.kernel == KF_GEMM_TILE_ROWS) return 0;
+  if (c.kernel == KF_GEMM_WARP_ROWS || c.kernel == KF_GEMM_TILE_ROWS || c.kernel == KF_GEMM_TILE_STREAM) return 0;
   if (c.kernel == KF_GEMM_AUTO || c.kernel == KF_GEMM_TCGEN05) {
     if (c.swap_ab == 0) c.swap_ab = 1;
     if (c.stream_k == 0) c.stream_k = 1;
@@ -758,7 +823,8 @@ int64_t kf_gemv_workspace_bytes(int32_t device, int32_t dtype, int64_t sx_m, int
 int32_t kf_query_gemm_config(int32_t dtype, const kf_gemm_config* cfg, int64_t* smem_bytes,
                              int32_t* tmem_cols) {
   if (cfg == nullptr) return set_error(KF_ERR_INVALID_ARGUMENT, "null config");
-  if (cfg->kernel == KF_GEMM_WARP_ROWS || cfg->kernel == KF_GEMM_TILE_ROWS) {  // no TMEM; tiny or M/K-dependent smem
+  if (cfg->kernel == KF_GEMM_WARP_ROWS || cfg->kernel == KF_GEMM_TILE_ROWS ||
+      cfg->kernel == KF_GEMM_TILE_STREAM) {  // no TMEM; tiny or M/K-dependent smem
     if (smem_bytes) *smem_bytes = 0;
     if (tmem_cols) *tmem_cols = 0;
     return KF_OK;

@@ -70,40 +70,18 @@ struct GemvMmaParams {
   int* status;
 };
 
-template <typename T>
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  if constexpr (DType<T>::code == KF_BF16) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-        "{%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  } else {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-        "{%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  }
-}
-
 // NT: 8-row groups of x (1 for M <= 8, 2 for M <= 16, 4 for M <= 32); S: warps per CTA (K
 // slices); U: vector pairs per lane in flight.
 // At least five CTAs per SM: a tile's CTA lasts about the whole kernel, so
 // all of them (688 for N = 11008) must be resident at once.
 // Weight vectors bypass L1 allocation (each is read once); x vectors are kept
-// in L1 ahead of other lines (every warp of every CTA on the SM re-reads them).
+// in L1 ahead of other lines (every warp of every CTA on the SM re-reads them;
+// load_x in kf_common.cuh).
 // At M = 16 x is 128 KB per CTA, as much as the CTA's weights: without the
 // hints the weight stream evicts it (39 % L1 hits measured).
 __device__ __forceinline__ uint4 load_weight(const uint4* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint4 load_x(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::evict_last.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;

@@ -115,6 +115,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// ---------------------------------------------------------------- bulk copies
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory, completing as
+// transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy shared-memory accesses (and what
+// a barrier made visible to it) before its following bulk copies.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 // 2-D tiled bulk tensor load into this CTA's shared memory; completion is
 // signalled on `bar` as transaction bytes. x is the innermost coordinate.
@@ -468,6 +487,56 @@ __device__ __forceinline__ float apply_epilogue(float acc, float bias) {
   } else {
     return gelu_erf(acc + bias);
   }
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Lets the next grid on the stream (when launched with programmatic stream
+// serialization) be scheduled before this one finishes.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Waits until the grids this one depends on have completed and their memory
+// operations are visible (returns at once for an ordinary launch).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---------------------------------------------------------------- decode GEMV pieces
+// Warp-level m16n8k16 tensor-core product with fp32 accumulation (the decode
+// GEMVs' contraction: 16 weight rows against 8 rows of x).
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  if constexpr (DType<T>::code == KF_BF16) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+// A 16-byte vector of x (read-only for the kernel's lifetime, re-read by many
+// warps): kept in L1 ahead of streaming lines.
+__device__ __forceinline__ uint4 load_x(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::evict_last.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// The same from L2, bypassing L1: for a grid launched as a programmatic
+// dependent, whose x is written by the previous grid during this grid's
+// lifetime (the non-coherent path above may then return stale lines).
+__device__ __forceinline__ uint4 load_x_l2(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 
 }  // namespace kf

@@ -134,6 +134,33 @@ int launch_gemv_mma(int dtype, const void* x, int64_t sx_m, const void* w, int64
                     const void* bias = nullptr, void* const* peers = nullptr, int n_peers = 0,
                     const kf_peer_sync* sync = nullptr, int* status = nullptr);
 
+// Streamed 16-row tile decode GEMV (gemv_stream.cu): M <= 16, fp16/bf16, the
+// tile kernel's operand rules; one persistent CTA per SM streams its tiles
+// through a shared-memory ring of bulk copies. No peers, no workspace.
+constexpr int GEMV_STREAM_MAX_M = 16;
+constexpr int GEMV_STREAM_DEFAULT_CHUNK = 1024;  // weight elements per row per stage
+bool gemv_stream_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k, const void* w, int64_t sw_n,
+                           int64_t sw_k, int64_t M, int64_t N, int64_t K, std::string* why);
+// The library's choice of the streamed kernel over the register-fed one for a
+// supported decode shape (measured on B200, graph-timed back-to-back
+// launches). Without overlap: beyond 8 rows of x when K is long or the tiles
+// number at least eight per SM. With overlap (only the streamed kernel
+// prefetches its weight while the previous grid finishes) also up to 8 rows,
+// and for fewer than four tiles per SM; the register-fed kernel without
+// overlap keeps the rest (beyond 8 rows at 4-8 tiles per SM and short K, e.g.
+// 16 x 11008 x 4096: 18.1 us against 19.2 with overlap).
+inline bool gemv_stream_preferred(int64_t M, int64_t N, int64_t K, int sm_count, bool overlap) {
+  if (M < 1 || M > GEMV_STREAM_MAX_M) return false;
+  const int64_t tiles = (N + 15) / 16;
+  const bool long_or_many = K >= 8192 || tiles >= 8LL * sm_count;
+  if (overlap) return M <= 8 || long_or_many || tiles < 4LL * sm_count;
+  return M > 8 && long_or_many;
+}
+int launch_gemv_stream(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
+                       int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K, const kf_gemm_config& cfg,
+                       const DeviceInfo& dev, cudaStream_t stream, int epilogue = KF_EPI_NONE,
+                       const void* bias = nullptr);
+
 // Decode-shape GEMM against an N-contiguous B (gemv_cols.cu): M <= 8, any
 // dtype, K split over CTAs with a deterministic last-arrival sum.
 constexpr int GEMV_COLS_MAX_M = 8;

@@ -32,6 +32,13 @@ TILE_ROWS_MAX_M = 32
 #: (K, N) operand), M <= 8, any dtype, K split over CTAs (csrc/gemv_cols.cu).
 KERNEL_COLUMNS = 5
 COLUMNS_MAX_M = 8
+#: kf_gemv / kf_gemm: the 16-row tile GEMV with the weight streamed through a shared-memory
+#: ring of bulk copies, one persistent CTA per SM (fp16/bf16, M <= 16, K % 8 == 0; no peers);
+#: num_stages = ring depth (0: as deep as fits), NUM_CTAS = grid (csrc/gemv_stream.cu).
+KERNEL_TILE_STREAM = 6
+TILE_STREAM_MAX_M = 16
+#: weight elements per row per ring stage (BLOCK_K) compiled in gemv_stream.cu; the first is the default
+TILE_STREAM_CHUNKS = (1024, 512)
 #: (warps per tile, vector pairs per batch; 1 = one software-pipelined pair) compiled in gemv_mma.cu
 TILE_ROWS_SHAPES = ((8, 1), (8, 2), (8, 4), (6, 2), (6, 4), (4, 2), (4, 4), (4, 8))
 
@@ -57,6 +64,36 @@ def tile_rows_split(n: int, m: int = 1, sm_count: int = 148) -> int:
     while ks < 4 and tiles * ks < target:
         ks *= 2
     return ks
+
+
+def tile_stream_preferred(m: int, n: int, k: int, *, sm_count: int = 148, overlap: bool = False) -> bool:
+    """Whether the library runs a supported decode shape on the streamed tile
+    kernel rather than the register-fed one (mirrors gemv_stream_preferred in
+    kf_internal.h). Without overlap: beyond 8 rows of x when K is long or the
+    16-row tiles number at least eight per SM. With overlap also up to 8 rows
+    and below four tiles per SM."""
+    if not 1 <= m <= TILE_STREAM_MAX_M:
+        return False
+    tiles = -(-n // 16)
+    long_or_many = k >= 8192 or tiles >= 8 * sm_count
+    if overlap:
+        return m <= 8 or long_or_many or tiles < 4 * sm_count
+    return m > 8 and long_or_many
+
+
+def tile_stream_reject(m: int, k: int, dtype: torch.dtype) -> str | None:
+    """Why the streamed tile GEMV cannot take this contiguous problem (None: it can)."""
+    if not 1 <= m <= TILE_STREAM_MAX_M:
+        return f"the streamed tile GEMV takes 1..{TILE_STREAM_MAX_M} rows of x, got M={m}"
+    return tile_rows_reject(m, k, dtype)
+
+
+def tile_stream_smem_bytes(m: int, chunk: int, max_smem: int = 232448) -> int:
+    """Shared memory of the streamed tile GEMV at its default ring depth (mirrors launch_gemv_stream)."""
+    stage = 16 * chunk * 2
+    fixed = 128 + 8 * 32 * (1 if m <= 8 else 2) * 16 + 16
+    stages = min(12, (max_smem - fixed) // (stage + 16))
+    return fixed + stages * (stage + 16)
 
 
 def tile_rows_reject(m: int, k: int, dtype: torch.dtype) -> str | None:
@@ -279,6 +316,9 @@ def default_gemm_config(
     rows against an N-contiguous B, fp32 beyond 64 x 64 as 3xTF32 tcgen05 tiles, else tcgen05
     tiles (operands TMA cannot describe packed first when the problem is not skinny), else the
     CUDA-core kernel."""
+    if b_layout == "nk" and tile_stream_reject(m, k, dtype) is None and tile_stream_preferred(
+            m, n, k, sm_count=sm_count):
+        return KernelConfig(operation, KERNEL=KERNEL_TILE_STREAM, BLOCK_K=TILE_STREAM_CHUNKS[0])
     if b_layout == "nk" and tile_rows_reject(m, k, dtype) is None:
         warps, pairs = tile_rows_default(m)
         return KernelConfig(operation, KERNEL=KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)

@@ -26,6 +26,7 @@ W may be stored [N,K] (``w_layout="nk"``, nn.Linear, the baseline layout) or
 
 from __future__ import annotations
 
+import dataclasses
 from collections.abc import Callable
 
 import torch
@@ -49,8 +50,16 @@ def gemv(
     w_layout: str = "nk",
     config: KernelConfig | None = None,
     out: torch.Tensor | None = None,
+    overlap: bool = False,
 ) -> torch.Tensor:
-    """``x @ w.T`` (``"nk"``) or ``x @ w`` (``"kn"``) for a handful of rows."""
+    """``x @ w.T`` (``"nk"``) or ``x @ w`` (``"kn"``) for a handful of rows.
+
+    ``overlap=True`` promises that ``w`` is not written by the kernel queued
+    just before this call on the stream (a model weight): the decode kernels
+    then launch as that kernel's CTAs finish and stream the weight while it
+    completes, and wait for it before reading ``x`` or writing ``out``
+    (programmatic dependent launch; back-to-back GEMVs overlap their tails).
+    """
     if x.ndim != 2 or w.ndim != 2:
         raise ValueError(f"expected 2D x and w, got {tuple(x.shape)} and {tuple(w.shape)}")
     if w_layout not in ("nk", "kn"):
@@ -70,12 +79,17 @@ def gemv(
     if out is None:
         out = torch.empty((m, n), device=x.device, dtype=x.dtype)
     if m and n:
-        native.gemv(x, w, out, w_layout=w_layout, launch=native.GemmLaunch.from_config(config))
+        launch = native.GemmLaunch.from_config(config)
+        if overlap:
+            launch = dataclasses.replace(launch, overlap=1)
+        native.gemv(x, w, out, w_layout=w_layout, launch=launch)
     return out
 
 
 def default_config(m: int, n: int, k: int, dtype: torch.dtype, *, sm_count: int = 148) -> KernelConfig:
     """The library's choice for contiguous [M,K] x and [N,K] w (mirrors kf_gemv)."""
+    if gc.tile_stream_reject(m, k, dtype) is None and gc.tile_stream_preferred(m, n, k, sm_count=sm_count):
+        return KernelConfig("gemv", KERNEL=gc.KERNEL_TILE_STREAM, BLOCK_K=gc.TILE_STREAM_CHUNKS[0])
     if gc.tile_rows_reject(m, k, dtype) is None:
         warps, pairs = gc.tile_rows_default(m)
         return KernelConfig("gemv", KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)

@@ -123,7 +123,8 @@ class KfGemmConfig(ctypes.Structure):
         ("cluster_n", ctypes.c_int32),
         ("num_ctas", ctypes.c_int32),
         ("epi_store", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 4),
+        ("overlap", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 3),
     ]
 
 
@@ -283,6 +284,7 @@ class GemmLaunch:
     cluster_n: int = 0
     num_ctas: int = 0
     epi_store: int = 0
+    overlap: int = 0
 
     @classmethod
     def from_config(cls, config) -> GemmLaunch:
@@ -302,6 +304,7 @@ class GemmLaunch:
             cluster_n=get("CLUSTER_N", 0),
             num_ctas=get("NUM_CTAS", 0),
             epi_store=get("EPI_STORE", 0),
+            overlap=get("OVERLAP", 0),
         )
 
     def struct(self) -> KfGemmConfig:
@@ -324,6 +327,7 @@ class GemmLaunch:
             "cluster_n",
             "num_ctas",
             "epi_store",
+            "overlap",
         ):
             setattr(s, name, getattr(self, name))
         return s

@@ -268,6 +268,11 @@ class _Sm100GemmSpace(SearchSpace):
             # tile, num_stages vector pairs in flight)
             for warps, pairs in gc.TILE_ROWS_SHAPES:
                 yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TILE_ROWS, BLOCK_M=warps, num_stages=pairs)
+            # the same tiles with the weight streamed through a shared-memory
+            # ring (BLOCK_K weight elements per row per stage)
+            if m <= gc.TILE_STREAM_MAX_M:
+                for chunk in gc.TILE_STREAM_CHUNKS:
+                    yield KernelConfig(self.operation, KERNEL=gc.KERNEL_TILE_STREAM, BLOCK_K=chunk)
         else:
             # decode shapes against a row-major (K, N) B: the column GEMV
             yield KernelConfig(self.operation, KERNEL=gc.KERNEL_COLUMNS)
@@ -288,6 +293,8 @@ class _Sm100GemmSpace(SearchSpace):
     def shared_memory_bytes(self, config: KernelConfig, problem: Problem) -> int:
         if config["KERNEL"] == gc.KERNEL_COLUMNS:
             return 0  # a few KB of reduction buffer and x slice
+        if config["KERNEL"] == gc.KERNEL_TILE_STREAM:
+            return gc.tile_stream_smem_bytes(self.dims(problem)[0], config["BLOCK_K"])
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             m = self.dims(problem)[0]
             return (config["BLOCK_M"] - 1) * 32 * gc.tile_rows_groups(m) * 16  # the K-slice partials
@@ -302,6 +309,9 @@ class _Sm100GemmSpace(SearchSpace):
 
     def num_programs(self, config: KernelConfig, problem: Problem) -> int:
         """CTAs with work: tiles, times two for SM-pair tiles."""
+        if config["KERNEL"] == gc.KERNEL_TILE_STREAM:
+            # one persistent CTA per SM, never more than the 16-row tiles
+            return min(gc.SM100_SMS, ceil_div(self.dims(problem)[1], 16))
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             # a cluster of CTAs per 16 weight rows (CLUSTER_M, else the library's split)
             m, n, _ = self.dims(problem)
@@ -339,6 +349,8 @@ class _Sm100GemmSpace(SearchSpace):
             return None  # what the library runs anyway is always measured
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             return gc.tile_rows_reject(m, k, problem.dtype)
+        if config["KERNEL"] == gc.KERNEL_TILE_STREAM:
+            return gc.tile_stream_reject(m, k, problem.dtype)
         if config["KERNEL"] == gc.KERNEL_COLUMNS:
             return gc.columns_reject(m, n, k, problem.dtype, b_layout=self.b_layout)
         if config["KERNEL"] == gc.KERNEL_SIMT:
@@ -389,7 +401,7 @@ class _Sm100GemmSpace(SearchSpace):
         if config["KERNEL"] == gc.KERNEL_TILE_ROWS:
             default = (config["BLOCK_M"], config["num_stages"]) == gc.tile_rows_default(self.dims(problem)[0])
             return (-3,) if default else (-2,)
-        if config["KERNEL"] == gc.KERNEL_COLUMNS:
+        if config["KERNEL"] in (gc.KERNEL_COLUMNS, gc.KERNEL_TILE_STREAM):
             return (-3,)
         if config["KERNEL"] != gc.KERNEL_TCGEN05:
             return (1,)
