@@ -124,13 +124,15 @@ typedef struct kf_gemm_config {
   int32_t epi_store; /* all-gather epilogue (kf_linear_bias_act_allgather): 0 = library
                         choice, 1 = stores from the threads (rows staged through
                         shared memory), 2 = TMA tensor stores of the staged blocks    */
-  int32_t overlap;   /* decode GEMV kernels (TILE_ROWS, TILE_STREAM) without peers:
-                        1 = the weight and bias are not written by the kernel that
-                        runs before this call on the stream, so this launch may
-                        start as that kernel's CTAs finish (programmatic dependent
-                        launch): it begins streaming the weight at once and waits
-                        for the earlier kernel to complete before it reads x or
-                        writes y. 0 = ordinary stream order. Other kernels ignore it */
+  int32_t overlap;   /* decode GEMV (kf_gemv, and kf_gemm / kf_linear_bias_act at
+                        M <= 16 without peers): 1 = the weight and bias are not
+                        written by the kernel that runs before this call on the
+                        stream, so the launch may start as that kernel's CTAs
+                        finish (programmatic dependent launch): it streams the
+                        weight at once and waits for the earlier kernel to
+                        complete before it reads x or writes y. Runs on
+                        TILE_STREAM (AUTO picks it); other kernels ignore it.
+                        0 = ordinary stream order                                    */
   int32_t reserved[3];
 } kf_gemm_config;
 

@@ -401,10 +401,8 @@ int gemm_common(GemmArgs& g, const kf_gemm_config* user, void* stream) {
       if (rc != KF_OK) return rc;
       status = dev->status;
     }
-    kf_gemm_config chosen = zero_config();
-    if (tile_auto && user != nullptr) chosen.overlap = user->overlap;  // not a tile-shape field
     const int rc = launch_gemv_mma(g.dtype, g.a, g.sa_m, g.b, g.sb_n, g.c, g.sc_m, g.sc_n, g.M, g.N, g.K,
-                                   tile_auto ? chosen : *user, static_cast<cudaStream_t>(stream),
+                                   tile_auto ? zero_config() : *user, static_cast<cudaStream_t>(stream),
                                    g.epilogue, g.bias, g.peers, g.n_peers, g.sync, status);
     if (rc == KF_OK && g.sync != nullptr) g.sync_done = true;
     return rc;

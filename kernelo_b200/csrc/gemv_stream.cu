@@ -14,10 +14,14 @@
 //
 // Work order: a CTA owns a contiguous run of 16-row tiles (balanced to one
 // tile) and walks it in groups of TPG tiles, chunk-major inside a group: for
-// each CH-element K chunk, the TPG tiles' stages in turn. A lane's x
-// fragment for a chunk is loaded once and feeds all TPG tiles, so x is read
-// once per group instead of once per tile; each tile keeps its accumulators
-// in registers until the group ends. Then the warps' partial tiles meet in
+// each CH-element K chunk, the TPG tiles' stages in turn. Before a chunk's
+// weight stages the producer also copies the chunk of x ([16 rows][CH], zeros
+// past M and K) into a two-slot x ring; every lane reads its x fragment from
+// there once per chunk and it feeds all TPG tiles, so x is read once per group
+// and never waited on from global memory (at 16 x 11008 x 4096 loads of x
+// from L1/L2 in the consumers measured 19.1-21.1 us alone and 19.2 with
+// overlap; the x ring 20.0 and 18.2). Each tile keeps its
+// accumulators in registers until the group ends. Then the warps' partial tiles meet in
 // shared memory, are summed in warp order (deterministic) and rounded once
 // into y after the epilogue (bias, GELU). Consumer warp w reads vectors
 // 16w .. 16w + 15 of each row of a stage (its K slice) as mma.sync A
@@ -25,11 +29,11 @@
 //
 // With overlap (kf_gemm_config.overlap) the grid is launched as a
 // programmatic dependent of the kernel before it on the stream: it may start
-// as that kernel's CTAs leave their SMs, its producer streams the weight at
-// once (the caller promises the earlier kernel does not write it), and the
-// consumers wait for the earlier grid to complete before they read x or write
-// y; x then comes from L2, since the earlier grid writes it during this grid's
-// lifetime. Each CTA lets the next such launch start early in turn. Back to
+// as that kernel's CTAs leave their SMs, its producer issues the first ring of
+// weight stages at once (the caller promises the earlier kernel does not write
+// the weight) and waits for the earlier grid to complete before it copies any
+// x; the consumers wait for it too before they write y. Each CTA lets the
+// next such launch start early in turn. Back to
 // back, a launch's weight stream fills the SMs its predecessor's last tiles
 // leave idle.
 //
@@ -58,6 +62,7 @@ constexpr int ST_MAX_STAGES = 12;
 constexpr int ST_EPI_BAR = 1;  // named barrier of the consumer warps
 
 constexpr int ST_BOX_K = 256;  // elements per row of one TMA box (16 rows x 512 bytes)
+constexpr int ST_X_SLOTS = 2;  // chunks of x in flight (each [16 rows][CH], one stage's size)
 
 // A stage: CH / 256 boxes of [16 rows][256 elements], dense.
 template <int CH>
@@ -107,16 +112,21 @@ __device__ __forceinline__ bool consumer_bar_and(bool pred) {
 
 template <typename T, int NT, int CH, int EPI, bool OVERLAP>
 __global__ void __launch_bounds__(ST_THREADS, 1)
-    gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const GemvStreamParams p) {
+    gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                       const GemvStreamParams p) {
   constexpr int TPG = TilesPerGroup<NT>::value;
   constexpr int STAGE = StageShape<CH>::bytes;
   constexpr int QUADS = StageShape<CH>::quads;
+  constexpr int BOX_BYTES = 16 * ST_BOX_K * 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  float4* part = reinterpret_cast<float4*>(ring + static_cast<size_t>(p.stages) * STAGE);
+  uint8_t* xring = ring + static_cast<size_t>(p.stages) * STAGE;  // ST_X_SLOTS chunks of x, same shape
+  float4* part = reinterpret_cast<float4*>(xring + ST_X_SLOTS * STAGE);
   uint64_t* full = reinterpret_cast<uint64_t*>(part + ST_WARPS * 32 * NT);
   uint64_t* empty = full + p.stages;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + p.stages);
+  uint64_t* xfull = empty + p.stages;
+  uint64_t* xempty = xfull + ST_X_SLOTS;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(xempty + ST_X_SLOTS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long grid = gridDim.x;
@@ -128,6 +138,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       mbar_init(smem_u32(full + s), 1);
       mbar_init(smem_u32(empty + s), ST_WARPS);
     }
+    for (int s = 0; s < ST_X_SLOTS; ++s) {
+      mbar_init(smem_u32(xfull + s), 1);
+      mbar_init(smem_u32(xempty + s), ST_WARPS);
+    }
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -138,39 +152,69 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 
   if (warp == ST_WARPS) {
     // ---- producer: one thread walks the consumers' order (groups of TPG
-    // tiles, chunk-major inside a group) and fills each stage with CH / 256
-    // box loads. It does not wait for an earlier grid (overlap): the weight
-    // is not written by it.
+    // tiles, chunk-major inside a group): before a chunk's weight stages, the
+    // chunk of x ([16 rows][CH], rows past M are zeros) into the x ring; each
+    // stage as CH / 256 box loads.
     if (lane != 0) return;
     tma_prefetch_desc(&tm_w);
-    int slot = 0;
-    uint32_t phase = 0;
-    long long issued = 0;
+    tma_prefetch_desc(&tm_x);
+    int slot = 0, xslot = 0;
+    uint32_t phase = 0, xphase = 0;
+    long long issued = 0, xissued = 0;
     bool ok = true;
+    auto issue_w = [&](int tile, int c) {
+      if (issued >= p.stages) {  // the slot's previous unit has been read by every consumer warp
+        ok = mbar_wait(smem_u32(empty + slot), phase ^ 1u, abort_flag, p.status, SITE_TMA_EMPTY);
+        if (!ok) return;
+      }
+      const uint32_t bar = smem_u32(full + slot);
+      const uint32_t dst = smem_u32(ring + static_cast<size_t>(slot) * STAGE);
+      mbar_arrive_expect_tx(bar, STAGE);
+#pragma unroll
+      for (int b = 0; b < StageShape<CH>::boxes; ++b)
+        tma_load_2d(dst + b * BOX_BYTES, &tm_w, bar, c * CH + b * ST_BOX_K, tile * 16);
+      ++issued;
+      if (++slot == p.stages) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    };
+    // With overlap the first ring of weight stages goes out before the
+    // earlier grid has finished (it does not write the weight); x only after.
+    long long prefetched = 0;
+    if (OVERLAP) {
+      for (int tg0 = t_begin; tg0 < t_end && prefetched < p.stages; tg0 += TPG) {
+        const int in_group = min(TPG, t_end - tg0);
+        for (int c = 0; c < p.chunks && prefetched < p.stages; ++c)
+          for (int j = 0; j < in_group && prefetched < p.stages; ++j, ++prefetched) issue_w(tg0 + j, c);
+      }
+      griddep_wait();
+    }
+    long long u = 0;
     for (int tg0 = t_begin; tg0 < t_end && ok; tg0 += TPG) {
       const int in_group = min(TPG, t_end - tg0);
       for (int c = 0; c < p.chunks && ok; ++c) {
-        for (int j = 0; j < in_group; ++j) {
-          if (issued >= p.stages) {  // the slot's previous unit has been read by every consumer warp
-            ok = mbar_wait(smem_u32(empty + slot), phase ^ 1u, abort_flag, p.status, SITE_TMA_EMPTY);
-            if (!ok) break;
-          }
-          const uint32_t bar = smem_u32(full + slot);
-          const uint32_t dst = smem_u32(ring + static_cast<size_t>(slot) * STAGE);
-          mbar_arrive_expect_tx(bar, STAGE);
-#pragma unroll
-          for (int b = 0; b < StageShape<CH>::boxes; ++b)
-            tma_load_2d(dst + b * (16 * ST_BOX_K * 2), &tm_w, bar, c * CH + b * ST_BOX_K, (tg0 + j) * 16);
-          ++issued;
-          if (++slot == p.stages) {
-            slot = 0;
-            phase ^= 1u;
-          }
+        if (xissued >= ST_X_SLOTS) {  // every consumer warp has read the slot's previous chunk
+          ok = mbar_wait(smem_u32(xempty + xslot), xphase ^ 1u, abort_flag, p.status, SITE_TMA_EMPTY);
+          if (!ok) break;
         }
+        const uint32_t xbar = smem_u32(xfull + xslot);
+        const uint32_t xdst = smem_u32(xring + static_cast<size_t>(xslot) * STAGE);
+        mbar_arrive_expect_tx(xbar, STAGE);
+#pragma unroll
+        for (int b = 0; b < StageShape<CH>::boxes; ++b)
+          tma_load_2d(xdst + b * BOX_BYTES, &tm_x, xbar, c * CH + b * ST_BOX_K, 0);
+        ++xissued;
+        if (++xslot == ST_X_SLOTS) {
+          xslot = 0;
+          xphase ^= 1u;
+        }
+        for (int j = 0; j < in_group && ok; ++j, ++u)
+          if (u >= prefetched) issue_w(tg0 + j, c);
       }
     }
-    // Let every copy land before the CTA can leave: the last `stages` units
-    // (all consumed on the normal path, so these waits return at once).
+    // Let every copy land before the CTA can leave: the last units of both
+    // rings (all consumed on the normal path, so these waits return at once).
     const long long last = issued < p.stages ? issued : p.stages;
     for (long long v = 0; v < last; ++v) {
       if (slot == 0) {
@@ -180,26 +224,28 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       --slot;
       mbar_wait(smem_u32(full + slot), phase, nullptr, p.status, SITE_DRAIN, 100000000ull);
     }
+    const long long xlast = xissued < ST_X_SLOTS ? xissued : ST_X_SLOTS;
+    for (long long v = 0; v < xlast; ++v) {
+      if (xslot == 0) {
+        xslot = ST_X_SLOTS;
+        xphase ^= 1u;
+      }
+      --xslot;
+      mbar_wait(smem_u32(xfull + xslot), xphase, nullptr, p.status, SITE_DRAIN, 100000000ull);
+    }
     return;
   }
 
   // ---- consumers
   const int g = lane >> 2, t = lane & 3;
-  const uint4* xr[NT];
-  bool xon[NT];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int m = g + 8 * nt;
-    xon[nt] = m < p.M;
-    xr[nt] = reinterpret_cast<const uint4*>(static_cast<const T*>(p.x) + (xon[nt] ? m : 0) * p.sx_m);
-  }
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
   T* y = static_cast<T*>(p.y);
   const T* bias = static_cast<const T*>(p.bias);
-  // x may be the previous kernel's output, and y its input.
+  // y may be the earlier grid's input (x arrives only after it completed,
+  // through the producer's wait; this keeps the stores ordered on their own).
   if (OVERLAP) griddep_wait();
-  int slot = 0;
-  uint32_t phase = 0;
+  int slot = 0, xslot = 0;
+  uint32_t phase = 0, xphase = 0;
   bool ok = true;  // every wait so far succeeded (warp-uniform)
   for (int tg0 = t_begin; tg0 < t_end; tg0 += TPG) {
     const int in_group = min(TPG, t_end - tg0);
@@ -213,18 +259,27 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 
     for (int c = 0; c < p.chunks; ++c) {
       // This lane's x fragment for the chunk (vectors 4q + t of its warp's K
-      // slice), shared by the group's tiles. With overlap the previous grid
-      // writes x during this grid's lifetime, so x then comes from L2 (the
-      // non-coherent L1 path could return stale lines).
-      const int k0v = c * (CH / 8);               // chunk start, in vectors
-      const int nvc = min(CH, p.K - c * CH) / 8;  // valid vectors in the chunk
+      // slice, x rows g and g + 8), shared by the group's tiles; the x slot
+      // is released as soon as every warp holds its fragment.
       uint4 xv[QUADS][NT];
+      {
+        bool got = ok && mbar_wait(smem_u32(xfull + xslot), xphase, abort_flag, p.status, SITE_MMA_FULL);
+        ok = __all_sync(0xffffffffu, got);
+        const uint8_t* xp = xring + static_cast<size_t>(xslot) * STAGE;
 #pragma unroll
-      for (int q = 0; q < QUADS; ++q) {
-        const int v = warp * (4 * QUADS) + 4 * q + t;
+        for (int q = 0; q < QUADS; ++q) {
+          const int v = warp * (4 * QUADS) + 4 * q + t;
+          const uint8_t* vp = xp + (v >> 5) * BOX_BYTES + (v & 31) * 16;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-          xv[q][nt] = !(v < nvc && xon[nt]) ? zero : OVERLAP ? load_x_l2(xr[nt] + k0v + v) : load_x(xr[nt] + k0v + v);
+          for (int nt = 0; nt < NT; ++nt)
+            xv[q][nt] = ok ? *reinterpret_cast<const uint4*>(vp + (g + 8 * nt) * (ST_BOX_K * 2)) : zero;
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(smem_u32(xempty + xslot));
+        if (++xslot == ST_X_SLOTS) {
+          xslot = 0;
+          xphase ^= 1u;
+        }
       }
 #pragma unroll
       for (int j = 0; j < TPG; ++j) {
@@ -240,7 +295,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             // vector v of the chunk: box v / 32, vector v % 32 of its rows
             // (beyond K the box holds zeros)
             const int v = warp * (4 * QUADS) + 4 * q + t;
-            const uint8_t* vp = sp + (v >> 5) * (16 * ST_BOX_K * 2) + (v & 31) * 16;
+            const uint8_t* vp = sp + (v >> 5) * BOX_BYTES + (v & 31) * 16;
             va[q] = ok ? *reinterpret_cast<const uint4*>(vp + g * (ST_BOX_K * 2)) : zero;
             vb[q] = ok ? *reinterpret_cast<const uint4*>(vp + (g + 8) * (ST_BOX_K * 2)) : zero;
           }
@@ -295,8 +350,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
   }
 }
 
+// The weight's and x's tensor maps.
+struct StreamMaps {
+  CUtensorMap w, x;
+};
+
 template <typename T, int NT, int CH, int EPI>
-int launch_typed(const CUtensorMap& tm_w, const GemvStreamParams& p, size_t smem, int grid, cudaStream_t stream) {
+int launch_typed(const StreamMaps& maps, const GemvStreamParams& p, size_t smem, int grid, cudaStream_t stream) {
   void* fn = p.overlap ? reinterpret_cast<void*>(gemv_stream_kernel<T, NT, CH, EPI, true>)
                        : reinterpret_cast<void*>(gemv_stream_kernel<T, NT, CH, EPI, false>);
   // The attribute only ever grows: set it once per kernel (and device).
@@ -312,9 +372,9 @@ int launch_typed(const CUtensorMap& tm_w, const GemvStreamParams& p, size_t smem
     set_device[o] = device;
     set_bytes[o] = smem;
   }
-  CUtensorMap map = tm_w;
+  CUtensorMap mw = maps.w, mx = maps.x;
   GemvStreamParams q = p;
-  void* args[] = {&map, &q};
+  void* args[] = {&mw, &mx, &q};
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(static_cast<unsigned>(grid));
   lc.blockDim = dim3(ST_THREADS);
@@ -333,7 +393,7 @@ int launch_typed(const CUtensorMap& tm_w, const GemvStreamParams& p, size_t smem
 }
 
 template <typename T, int NT, int CH>
-int launch_epi(const CUtensorMap& tm, const GemvStreamParams& p, int epilogue, size_t smem, int grid,
+int launch_epi(const StreamMaps& tm, const GemvStreamParams& p, int epilogue, size_t smem, int grid,
                cudaStream_t stream) {
   switch (epilogue) {
     case KF_EPI_NONE: return launch_typed<T, NT, CH, KF_EPI_NONE>(tm, p, smem, grid, stream);
@@ -345,15 +405,15 @@ int launch_epi(const CUtensorMap& tm, const GemvStreamParams& p, int epilogue, s
 }
 
 template <typename T, int CH>
-int launch_nt(const CUtensorMap& tm, const GemvStreamParams& p, int nt, int epilogue, size_t smem, int grid,
+int launch_nt(const StreamMaps& tm, const GemvStreamParams& p, int nt, int epilogue, size_t smem, int grid,
               cudaStream_t stream) {
   return nt == 1 ? launch_epi<T, 1, CH>(tm, p, epilogue, smem, grid, stream)
                  : launch_epi<T, 2, CH>(tm, p, epilogue, smem, grid, stream);
 }
 
-// The weight as a 2-D tensor map [N rows][K elements], boxes of 16 rows x 256
-// elements, no swizzle, zeros outside the tensor.
-int encode_weight_map(CUtensorMap* map, int dtype, const void* w, int64_t N, int64_t K, int64_t sw_n) {
+// A K-contiguous operand (the weight [N][K], or x [M][K]) as a 2-D tensor
+// map, boxes of 16 rows x 256 elements, no swizzle, zeros outside the tensor.
+int encode_rows_map(CUtensorMap* map, int dtype, const void* w, int64_t N, int64_t K, int64_t sw_n) {
   static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -374,7 +434,7 @@ int encode_weight_map(CUtensorMap* map, int dtype, const void* w, int64_t N, int
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
-    return set_error(KF_ERR_UNALIGNED, "streamed tile GEMV: cuTensorMapEncodeTiled rejected the weight (error " +
+    return set_error(KF_ERR_UNALIGNED, "streamed tile GEMV: cuTensorMapEncodeTiled rejected an operand (error " +
                                            std::to_string(r) + ")");
   return KF_OK;
 }
@@ -421,7 +481,8 @@ int launch_gemv_stream(int dtype, const void* x, int64_t sx_m, const void* w, in
   p.overlap = cfg.overlap != 0 ? 1 : 0;
   const int nt = M <= 8 ? 1 : 2;
   const size_t stage = 16 * static_cast<size_t>(ch) * 2;
-  const size_t fixed = 128 + static_cast<size_t>(ST_WARPS) * 32 * nt * sizeof(float4) + 16;
+  // alignment slack, the x ring and its barriers, the warps' partial tiles, the abort flag
+  const size_t fixed = 128 + ST_X_SLOTS * (stage + 16) + static_cast<size_t>(ST_WARPS) * 32 * nt * sizeof(float4) + 16;
   // Ring depth: config stages if given, else as many as fit (two mbarriers per stage).
   const int fit = static_cast<int>((static_cast<size_t>(dev.max_smem_optin) - fixed) / (stage + 16));
   const int cap = fit < ST_MAX_STAGES ? fit : ST_MAX_STAGES;
@@ -433,8 +494,10 @@ int launch_gemv_stream(int dtype, const void* x, int64_t sx_m, const void* w, in
   // One CTA per SM (num_ctas overrides), never more CTAs than tiles.
   int grid = cfg.num_ctas > 0 ? cfg.num_ctas : dev.sm_count;
   if (grid > p.tiles) grid = p.tiles;
-  CUtensorMap tm;
-  const int rc = encode_weight_map(&tm, dtype, w, N, K, sw_n);
+  StreamMaps tm;
+  int rc = encode_rows_map(&tm.w, dtype, w, N, K, sw_n);
+  if (rc != KF_OK) return rc;
+  rc = encode_rows_map(&tm.x, dtype, x, M, K, sx_m);
   if (rc != KF_OK) return rc;
   if (dtype == KF_BF16)
     return ch == 512 ? launch_nt<__nv_bfloat16, 512>(tm, p, nt, epilogue, smem, grid, stream)

@@ -143,18 +143,16 @@ bool gemv_stream_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k,
                            int64_t sw_k, int64_t M, int64_t N, int64_t K, std::string* why);
 // The library's choice of the streamed kernel over the register-fed one for a
 // supported decode shape (measured on B200, graph-timed back-to-back
-// launches). Without overlap: beyond 8 rows of x when K is long or the tiles
-// number at least eight per SM. With overlap (only the streamed kernel
-// prefetches its weight while the previous grid finishes) also up to 8 rows,
-// and for fewer than four tiles per SM; the register-fed kernel without
-// overlap keeps the rest (beyond 8 rows at 4-8 tiles per SM and short K, e.g.
-// 16 x 11008 x 4096: 18.1 us against 19.2 with overlap).
+// launches). Without overlap: beyond 8 rows of x when K is long or the 16-row
+// tiles number at least eight per SM (16 x 4096 x 11008: 20.9 us against
+// 26.9; 16 x 44032 x 4096: 63.6 against 66.5). With overlap always: only the
+// streamed kernel prefetches its weight while the previous grid finishes
+// (1 / 4 / 16 x 11008 x 4096: 15.3 / 15.6 / 18.2 us, against 15.4 / 16.0 / 18.3
+// for the register-fed kernel in stream order).
 inline bool gemv_stream_preferred(int64_t M, int64_t N, int64_t K, int sm_count, bool overlap) {
   if (M < 1 || M > GEMV_STREAM_MAX_M) return false;
-  const int64_t tiles = (N + 15) / 16;
-  const bool long_or_many = K >= 8192 || tiles >= 8LL * sm_count;
-  if (overlap) return M <= 8 || long_or_many || tiles < 4LL * sm_count;
-  return M > 8 && long_or_many;
+  if (overlap) return true;
+  return M > 8 && (K >= 8192 || (N + 15) / 16 >= 8LL * sm_count);
 }
 int launch_gemv_stream(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
                        int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K, const kf_gemm_config& cfg,

@@ -130,17 +130,16 @@ def test_overlap_chain_matches_stream_order(cfg, m, device):
 
 
 def test_library_choice(device):
-    """The library takes the streamed kernel beyond 8 rows of x when K is long
-    or the tiles are many, and with overlap also up to 8 rows and for few
-    tiles; the register-fed kernel otherwise (the Python mirror agrees with
-    what runs)."""
+    """The library takes the streamed kernel whenever overlap is asked for, and
+    without it beyond 8 rows of x when K is long or the tiles are many; the
+    register-fed kernel otherwise (the Python mirror agrees with what runs)."""
     assert default_config(16, 4096, 11008, torch.float16)["KERNEL"] == gc.KERNEL_TILE_STREAM
     assert default_config(16, 44032, 4096, torch.bfloat16)["KERNEL"] == gc.KERNEL_TILE_STREAM
     assert default_config(16, 11008, 4096, torch.float16)["KERNEL"] == gc.KERNEL_TILE_ROWS
     assert default_config(8, 4096, 11008, torch.float16)["KERNEL"] == gc.KERNEL_TILE_ROWS
     assert gc.tile_stream_preferred(1, 11008, 4096, overlap=True)
-    assert gc.tile_stream_preferred(16, 4096, 4096, overlap=True)  # 256 tiles, under 4 per SM
-    assert not gc.tile_stream_preferred(16, 11008, 4096, overlap=True)  # the register-fed kernel's best shape
+    assert gc.tile_stream_preferred(16, 11008, 4096, overlap=True)
+    assert not gc.tile_stream_preferred(16, 11008, 4096)  # the register-fed kernel's best shape
     assert not gc.tile_stream_preferred(17, 11008, 4096, overlap=True)
     x, w = operands(16, 4096, 11008, torch.float16, device, seed=5)
     gate(ref.gemv_ref(host(x), host(w)), gemv(x, w), torch.float16, context="library choice, long K")
