@@ -131,7 +131,8 @@ typedef struct kf_gemm_config {
                         finish (programmatic dependent launch): it streams the
                         weight at once and waits for the earlier kernel to
                         complete before it reads x or writes y. Runs on
-                        TILE_STREAM (AUTO picks it); other kernels ignore it.
+                        TILE_STREAM (AUTO picks it where it is faster so);
+                        other kernels ignore it.
                         0 = ordinary stream order                                    */
   int32_t reserved[3];
 } kf_gemm_config;

@@ -145,14 +145,17 @@ bool gemv_stream_supported(int dtype, const void* x, int64_t sx_m, int64_t sx_k,
 // supported decode shape (measured on B200, graph-timed back-to-back
 // launches). Without overlap: beyond 8 rows of x when K is long or the 16-row
 // tiles number at least eight per SM (16 x 4096 x 11008: 20.9 us against
-// 26.9; 16 x 44032 x 4096: 63.6 against 66.5). With overlap always: only the
-// streamed kernel prefetches its weight while the previous grid finishes
-// (1 / 4 / 16 x 11008 x 4096: 15.3 / 15.6 / 18.2 us, against 15.4 / 16.0 / 18.3
-// for the register-fed kernel in stream order).
+// 26.9; 16 x 44032 x 4096: 63.6 against 66.5). With overlap (only the streamed
+// kernel prefetches its weight while the previous grid finishes) also beyond
+// 8 rows at any N (16 x 11008 x 4096: 17.8-18.2 us against 18.3), for long K
+// at any M (4 x 4096 x 11008: 17.6 against 20.2) and below four tiles per SM;
+// up to 8 rows on many tiles of short K the register-fed kernel in stream
+// order stays ahead (1 x 11008 x 4096: 15.1-15.4 us against 15.3-17.3).
 inline bool gemv_stream_preferred(int64_t M, int64_t N, int64_t K, int sm_count, bool overlap) {
   if (M < 1 || M > GEMV_STREAM_MAX_M) return false;
-  if (overlap) return true;
-  return M > 8 && (K >= 8192 || (N + 15) / 16 >= 8LL * sm_count);
+  const int64_t tiles = (N + 15) / 16;
+  if (overlap) return M > 8 || K >= 8192 || tiles < 4LL * sm_count;
+  return M > 8 && (K >= 8192 || tiles >= 8LL * sm_count);
 }
 int launch_gemv_stream(int dtype, const void* x, int64_t sx_m, const void* w, int64_t sw_n, void* y,
                        int64_t sy_m, int64_t sy_n, int64_t M, int64_t N, int64_t K, const kf_gemm_config& cfg,

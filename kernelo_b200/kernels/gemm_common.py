@@ -69,14 +69,15 @@ def tile_rows_split(n: int, m: int = 1, sm_count: int = 148) -> int:
 def tile_stream_preferred(m: int, n: int, k: int, *, sm_count: int = 148, overlap: bool = False) -> bool:
     """Whether the library runs a supported decode shape on the streamed tile
     kernel rather than the register-fed one (mirrors gemv_stream_preferred in
-    kf_internal.h): always with overlap (the kernel that prefetches its weight
-    while the previous grid finishes); otherwise beyond 8 rows of x when K is
-    long or the 16-row tiles number at least eight per SM."""
+    kf_internal.h). Without overlap: beyond 8 rows of x when K is long or the
+    16-row tiles number at least eight per SM. With overlap: beyond 8 rows,
+    for long K, or below four tiles per SM."""
     if not 1 <= m <= TILE_STREAM_MAX_M:
         return False
+    tiles = -(-n // 16)
     if overlap:
-        return True
-    return m > 8 and (k >= 8192 or -(-n // 16) >= 8 * sm_count)
+        return m > 8 or k >= 8192 or tiles < 4 * sm_count
+    return m > 8 and (k >= 8192 or tiles >= 8 * sm_count)
 
 
 def tile_stream_reject(m: int, k: int, dtype: torch.dtype) -> str | None:

@@ -105,7 +105,8 @@ def test_overlap_chain_matches_stream_order(cfg, m, device):
     may start before its predecessor finishes (programmatic dependent launch)
     and must still read the finished x: the chain's bits equal those of the
     same kernel in ordinary stream order (the library's choice with overlap
-    is the streamed kernel), eagerly and from a CUDA graph."""
+    at this shape, 128 tiles, is the streamed kernel), eagerly and from a
+    CUDA graph."""
     gen = torch.Generator().manual_seed(100 + m)
     ws = [(torch.randn(2048, 2048, generator=gen) * 2048 ** -0.5).half().to(device) for _ in range(6)]
     x0 = torch.randn(m, 2048, generator=gen).half().to(device)
@@ -130,20 +131,23 @@ def test_overlap_chain_matches_stream_order(cfg, m, device):
 
 
 def test_library_choice(device):
-    """The library takes the streamed kernel whenever overlap is asked for, and
-    without it beyond 8 rows of x when K is long or the tiles are many; the
-    register-fed kernel otherwise (the Python mirror agrees with what runs)."""
+    """The library takes the streamed kernel beyond 8 rows of x when K is long
+    or the tiles are many; with overlap also beyond 8 rows at any N, for long
+    K and for few tiles; the register-fed kernel otherwise (the Python mirror
+    agrees with what runs)."""
     assert default_config(16, 4096, 11008, torch.float16)["KERNEL"] == gc.KERNEL_TILE_STREAM
     assert default_config(16, 44032, 4096, torch.bfloat16)["KERNEL"] == gc.KERNEL_TILE_STREAM
     assert default_config(16, 11008, 4096, torch.float16)["KERNEL"] == gc.KERNEL_TILE_ROWS
     assert default_config(8, 4096, 11008, torch.float16)["KERNEL"] == gc.KERNEL_TILE_ROWS
-    assert gc.tile_stream_preferred(1, 11008, 4096, overlap=True)
     assert gc.tile_stream_preferred(16, 11008, 4096, overlap=True)
     assert not gc.tile_stream_preferred(16, 11008, 4096)  # the register-fed kernel's best shape
+    assert gc.tile_stream_preferred(1, 4096, 11008, overlap=True)  # long K
+    assert gc.tile_stream_preferred(1, 2048, 2048, overlap=True)  # 128 tiles, under 4 per SM
+    assert not gc.tile_stream_preferred(1, 11008, 4096, overlap=True)
     assert not gc.tile_stream_preferred(17, 11008, 4096, overlap=True)
     x, w = operands(16, 4096, 11008, torch.float16, device, seed=5)
     gate(ref.gemv_ref(host(x), host(w)), gemv(x, w), torch.float16, context="library choice, long K")
-    x, w = operands(4, 11008, 4096, torch.float16, device, seed=6)
+    x, w = operands(4, 4096, 11008, torch.float16, device, seed=6)
     gate(ref.gemv_ref(host(x), host(w)), gemv(x, w, overlap=True), torch.float16, context="library choice, overlap")
 
 

@@ -108,12 +108,15 @@ def test_harness_uses_cuda_events_and_the_flush_matters(device):
 
 
 def test_harness_agrees_with_torch_benchmark(device):
+    """Both timers over a similar span of back-to-back GEMMs (~10 ms each): a
+    loop of half a second reaches the 1 kW power cap and runs at lower clocks
+    (measured 0.101 against 0.119 ms), which is the GPU, not the harness."""
     from kernelo_b200.kernels.matmul import matmul
 
     a = torch.randn(4096, 4096, device=device, dtype=torch.bfloat16)
     b = torch.randn(4096, 4096, device=device, dtype=torch.bfloat16)
     ours = benchmark(lambda: matmul(a, b), warmup=10, iterations=100, device=device, flush_l2=False)
-    theirs = cross_check_median_ms(lambda: matmul(a, b), min_run_time=0.5)
+    theirs = cross_check_median_ms(lambda: matmul(a, b), min_run_time=0.01)
     assert ours.median_ms == pytest.approx(theirs, rel=0.15)
 
 
