@@ -19,9 +19,11 @@
 //    array's device address is looked up with cudaGetSymbolAddress once per
 //    device, by the first call made while that device is current; make that
 //    first call before any stream capture begins.
-//  - It accepts what kf_gemv accepts at M <= 16 and picks the same kernels.
-//    fp16/bf16 operands with K-contiguous rows (and K % 8 == 0) go to the
-//    16-row tile GEMV, which uses no scratch and never touches the array.
+//  - It accepts what kf_gemv accepts at M <= 16. fp16/bf16 operands with
+//    K-contiguous rows (and K % 8 == 0) go to the register-fed 16-row tile
+//    GEMV, which uses no scratch and never touches the array (kf_gemv's
+//    default there, except beyond 8 rows at long K or many tiles, where
+//    kf_gemv streams the tiles through shared memory instead).
 //    The rest may take the stream-K tcgen05 GEMV (the only kernel here that
 //    needs scratch) or a scratch-free CUDA-core kernel; a call whose
 //    stream-K scratch would exceed the array is rejected with
