@@ -208,7 +208,10 @@ KF_API int32_t kf_linear_bias_act(int32_t dtype, const void* x, int64_t sx_m, in
  * [N,K] (sw_n = row stride, sw_k = 1) or [K,N] (sw_k = row stride, sw_n = 1).
  * Memory-bound. The default config picks by layout: fp16/bf16 with
  * K-contiguous W and x rows and M <= 32 run the 16-row tile kernel (W streamed
- * by warps into mma.sync fragments, no workspace); fp32 at M <= 2 the
+ * by warps into mma.sync fragments, no workspace), or at 9..16 rows with
+ * K >= 8192 or at least eight 16-row tiles per SM, and with cfg->overlap
+ * beyond 8 rows, for K >= 8192 or below four tiles per SM, the streamed tile
+ * kernel (KF_GEMM_TILE_STREAM, no workspace); fp32 at M <= 2 the
  * warp-per-row kernel (no workspace); the rest the tcgen05 GEMV with A and B
  * swapped and K split over all SMs (stream-K), which uses
  * kf_gemv_workspace_bytes() of workspace when given one and whole tiles
