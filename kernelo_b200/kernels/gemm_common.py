@@ -90,7 +90,8 @@ def tile_stream_reject(m: int, k: int, dtype: torch.dtype) -> str | None:
 def tile_stream_smem_bytes(m: int, chunk: int, max_smem: int = 232448) -> int:
     """Shared memory of the streamed tile GEMV at its default ring depth (mirrors launch_gemv_stream)."""
     stage = 16 * chunk * 2
-    fixed = 128 + 8 * 32 * (1 if m <= 8 else 2) * 16 + 16
+    # alignment slack, the two-slot x ring and its barriers, the warps' partial tiles, two flags
+    fixed = 128 + 2 * (stage + 16) + 8 * 32 * (1 if m <= 8 else 2) * 16 + 16
     stages = min(12, (max_smem - fixed) // (stage + 16))
     return fixed + stages * (stage + 16)
 
